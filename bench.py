@@ -1,0 +1,402 @@
+#!/usr/bin/env python3
+"""MoE-layer forward throughput on B200 (tokens/s, max over ranks) + roofline fraction.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload qwen|switch] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...        (one rank per GPU, NCCL)
+
+Workload (default): one Qwen1.5-MoE-A2.7B MoE block — d_model 2048, 60 routed SwiGLU experts
+(I = 1408), top-4 softmax router, shared SwiGLU expert (I = 5632) with its sigmoid gate — on
+16 x 256 = 4096 tokens per GPU of N(0,1) bf16 hidden states, random-init bf16 weights, the
+router biased so top-1 expert loads follow Zipf s = 1.5.  Experts are placed contiguously
+(60 on 8 GPUs = 4 x 8 + 4 x 7) and the harmony plan (eq_tokens 150) rebalances hot experts.
+`--workload switch`: one Switch-base-64 MoE layer (d 768, 64 ReLU experts of 3072, top-1,
+Zipf s = 1.0 router).
+
+Timing: W untimed warm-up steps; then K steps, each bracketed by CUDA events on the launching
+stream, with a 256 MiB L2 flush (untimed) before each; barrier + synchronize before and after;
+the per-rank sum is reduced with MAX over ranks.  `value` = tokens of all ranks / that time.
+`e2e` repeats the measurement through the public API with the input in pinned host memory
+(H2D copy, forward, D2H copy of the output inside the timed region).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    "qwen": dict(name="qwen1.5-moe-a2.7b MoE block forward", d=2048, E=60, inter=1408, shared=5632, k=4,
+                 act="swiglu", zipf=1.5, T=4096),
+    "switch": dict(name="switch-base-64 MoE layer forward", d=768, E=64, inter=3072, shared=0, k=1,
+                   act="relu", zipf=1.0, T=4096),
+}
+FLUSH_BYTES = 256 << 20
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=list(WORKLOADS), default="qwen")
+    ap.add_argument("--tokens", type=int, default=None, help="tokens per GPU (default 4096 = 16 x 256)")
+    ap.add_argument("--eq-tokens", type=int, default=150)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    return ap.parse_args()
+
+
+def flops_and_bytes(w, T, rows_routed, E_touched):
+    """Algorithmic work of one block forward on one GPU (no padding)."""
+    d, I, Is, E = w["d"], w["inter"], w["shared"], w["E"]
+    glu = w["act"] == "swiglu"
+    m = 3 if glu else 2
+    router = 2.0 * T * d * E
+    g1 = 2.0 * rows_routed * d * (2 * I if glu else I) + (2.0 * T * d * 2 * Is if Is else 0.0)
+    g2 = 2.0 * rows_routed * I * d + (2.0 * T * Is * d if Is else 0.0)
+    hbm = (2.0 * T * d * 2                       # x read, out write (bf16)
+           + 2.0 * E * d                         # router weight
+           + 2.0 * E_touched * m * d * I         # experts touched at least once
+           + (2.0 * 3 * d * Is + 2.0 * d if Is else 0.0))
+    return router, g1, g2, hbm
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return dict(hbm=j["hbm_gbs"], tc=j["bf16_tflops"], tc_sus=j.get("bf16_tflops_sustained", j["bf16_tflops"]),
+                    src="measured")
+    return dict(hbm=6650.0, tc=1590.0, tc_sus=1400.0, src="fallback")
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    Q = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid=None):
+        self.uuid = uuid
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            out, _ = self.p.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+            out, _ = self.p.communicate()
+        rows = [r.split(", ") for r in out.strip().splitlines() if r.count(",") >= 9]
+        if self.uuid:
+            mine = [r for r in rows if self.uuid in r[1]]
+            rows = mine or rows
+        if not rows:
+            return None
+        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        pw = [float(r[4]) for r in rows if r[4].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[6 + i].strip() == "Active"})
+        loaded = [s for s, p in zip(sm, pw) if p > 300] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": float(rows[0][3]) if rows[0][3].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows), "power_w_max": max(pw) if pw else None}
+
+
+def build_block(w, T, rank, world, dev, eq_tokens, group=None):
+    import torch
+
+    from dsca_moe_b200 import _lib as L
+    from dsca_moe_b200 import synthetic as syn
+    from dsca_moe_b200.engine import MoEEngine, pack_relu, pack_swiglu
+
+    d, E, I, Is = w["d"], w["E"], w["inter"], w["shared"]
+    Wr, info = syn.router_weight(E, d, 1234, zipf_s=w["zipf"], dtype="bf16")
+    g = torch.Generator(device=dev)
+    g.manual_seed(4321)  # identical experts on every rank (every GPU holds the whole layer)
+
+    def n(*shape):
+        return (torch.randn(*shape, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+
+    raw = {}
+    if w["act"] == "swiglu":
+        raw = dict(gate=n(E, I, d), up=n(E, I, d), down=n(E, d, I), s_gate=n(Is, d), s_up=n(Is, d), s_down=n(d, Is))
+        sgw = syn.bf16_round(syn.rng(99).standard_normal((1, d)).astype(np.float32) / np.sqrt(d))
+        pe = pack_swiglu(raw["gate"], raw["up"], raw["down"], shared=(raw["s_gate"], raw["s_up"], raw["s_down"]),
+                         device=dev)
+        raw["s_gate_w"] = sgw
+        eng = MoEEngine(torch.from_numpy(Wr).to(dev, torch.bfloat16), pe, top_k=w["k"],
+                        route_mode=L.ROUTE_SOFTMAX_TOPK,
+                        shared_gate_weight=torch.from_numpy(sgw).to(dev, torch.bfloat16),
+                        rank=rank, world=world, group=group, eq_tokens=eq_tokens)
+    else:
+        raw = dict(wi=n(E, I, d), wo=n(E, d, I))
+        pe = pack_relu(raw["wi"], raw["wo"], device=dev)
+        eng = MoEEngine(torch.from_numpy(Wr).to(dev, torch.bfloat16), pe, top_k=1, route_mode=L.ROUTE_SWITCH_TOP1,
+                        rank=rank, world=world, group=group, eq_tokens=eq_tokens)
+    x = torch.from_numpy(syn.hidden_states(T, d, 5000 + rank, "bf16")).to(dev, torch.bfloat16)
+    return eng, x, Wr, raw, info
+
+
+def cpu_oracle_rate(w, Wr, raw_host, seconds, sample_tokens=256):
+    """Oracle port (routing in C, FFN in numpy fp32 BLAS) on a sample of the workload's tokens;
+    returns (tokens/s, threads, description)."""
+    from dsca_moe_b200 import synthetic as syn
+    from oracle import oracle as O
+
+    x = syn.hidden_states(sample_tokens, w["d"], 777, "bf16")
+    run = (lambda: O.qwen_forward(x, Wr, raw_host, w["k"], False, "bf16", compute=np.float32)) \
+        if w["act"] == "swiglu" else (lambda: O.switch_forward(x, Wr, raw_host["wi"], raw_host["wo"], "bf16",
+                                                               compute=np.float32))
+    run()  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        run()
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or n >= 200:
+            break
+    threads = os.cpu_count()
+    return sample_tokens * n / el, threads, f"{n} x {sample_tokens} tokens of the workload ({el:.1f} s)"
+
+
+def host_weights(raw):
+    import torch
+
+    out = {}
+    for k, v in raw.items():
+        out[k] = v.float().cpu().numpy() if isinstance(v, torch.Tensor) else v
+    return out
+
+
+def run_reference(args, w, T):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+
+    from dsca_moe_b200 import synthetic as syn
+
+    E, d, I, Is = w["E"], w["d"], w["inter"], w["shared"]
+    Wr, _ = syn.router_weight(E, d, 1234, zipf_s=w["zipf"], dtype="bf16")
+    g = torch.Generator()
+    g.manual_seed(4321)
+
+    def n(*shape):
+        return (torch.randn(*shape, generator=g) * 0.02).to(torch.bfloat16).float().numpy()
+
+    if w["act"] == "swiglu":
+        raw = dict(gate=n(E, I, d), up=n(E, I, d), down=n(E, d, I), s_gate=n(Is, d), s_up=n(Is, d),
+                   s_down=n(d, Is), s_gate_w=syn.bf16_round(syn.rng(99).standard_normal((1, d)).astype(np.float32)
+                                                            / np.sqrt(d)))
+    else:
+        raw = dict(wi=n(E, I, d), wo=n(E, d, I))
+    sample = 256
+    per_step = max(args.cpu_seconds / max(args.steps, 1), 0.5)
+    for _ in range(args.warmup):
+        cpu_oracle_rate(w, Wr, raw, 0.0, sample)
+    rates = []
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        r, threads, desc = cpu_oracle_rate(w, Wr, raw, per_step, sample)
+        rates.append(r)
+    el = time.perf_counter() - t0
+    value = statistics.mean(rates)
+    line = {"impl": "reference", "metric": "MoE-layer tokens/sec (max over ranks)", "value": value,
+            "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * T / value, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": w["name"], "tokens_per_gpu": T, "router": f"zipf{w['zipf']}",
+                       "path": "oracle port of the reference path (routing C, FFN numpy fp32 BLAS) on host cores"},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                             "sample": f"{args.steps} steps x {sample}-token samples ({el:.1f} s)"},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    w = dict(WORKLOADS[args.workload])
+    T = args.tokens or w["T"]
+    if args.impl == "reference":
+        run_reference(args, w, T)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    group = None
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+        group = dist.group.WORLD
+    eng, x, Wr, raw, info = build_block(w, T, rank, world, dev, args.eq_tokens, group)
+    peaks = load_peaks()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    for _ in range(args.warmup):
+        eng.forward(x)
+    barrier()
+    uuid = None
+    try:
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:  # noqa: BLE001
+        pass
+    clocks = ClockSampler(uuid)
+    if local == 0:
+        clocks.start()
+        time.sleep(0.3)
+    # ---- timed region (device, inputs resident)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    torch.cuda._sleep(20_000_000)  # let the host queue ahead of the first timed step
+    for i in range(args.steps):
+        flush.zero_()
+        evs[i][0].record()
+        eng.forward(x)
+        evs[i][1].record()
+    barrier()
+    step_ms = [a.elapsed_time(b) for a, b in evs]
+    tot = torch.tensor([sum(step_ms)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(tot, op=dist.ReduceOp.MAX)
+    ms_per_step = float(tot.item()) / args.steps
+    value = T * world / (ms_per_step / 1e3)
+    clk = clocks.stop() if local == 0 else None
+
+    # ---- per-kernel phases (separate profiled steps with event markers between launches)
+    eng.markers = []
+    phase_ms = {}
+    prof_steps = 10
+    for _ in range(prof_steps):
+        flush.zero_()
+        eng.forward(x)
+    torch.cuda.synchronize()
+    marks = eng.markers
+    eng.markers = None
+    seq = []
+    for i in range(1, len(marks)):
+        if marks[i][0] == "start":
+            continue
+        seq.append((marks[i][0], marks[i - 1][1].elapsed_time(marks[i][1])))
+    for name, ms in seq:
+        phase_ms.setdefault(name, []).append(ms)
+    phase_ms = {k: statistics.mean(v) for k, v in phase_ms.items()}
+
+    # ---- end to end through the public API with host buffers
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty(T, w["d"], dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty_like(x)
+    for _ in range(2):
+        x_dev.copy_(x_host, non_blocking=True)
+        out_host.copy_(eng.forward(x_dev)["out"], non_blocking=True)
+    barrier()
+    e_evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush.zero_()
+        e_evs[i][0].record()
+        x_dev.copy_(x_host, non_blocking=True)
+        r = eng.forward(x_dev)
+        out_host.copy_(r["out"], non_blocking=True)
+        e_evs[i][1].record()
+    barrier()
+    e_tot = torch.tensor([sum(a.elapsed_time(b) for a, b in e_evs)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e_tot, op=dist.ReduceOp.MAX)
+    e2e_value = T * world / (float(e_tot.item()) / args.steps / 1e3)
+
+    # ---- roofline of the dominant kernel (grouped GEMM: GEMM1 + GEMM2 launches)
+    if world == 1:
+        rows = T * w["k"]
+        counts = eng.forward(x)["counts"].cpu().numpy()
+    else:
+        lay = eng.last_layout
+        rows = int(lay.group_offsets[-1]) if lay.num_groups else 0
+        counts = np.zeros(w["E"])
+        counts[lay.group_expert] = np.diff(lay.group_offsets)
+    e_touched = int((counts > 0).sum())
+    f_router, f_g1, f_g2, hbm = flops_and_bytes(w, T, rows, e_touched)
+    t_g1, t_g2 = phase_ms.get("gemm1", float("nan")), phase_ms.get("gemm2", float("nan"))
+    achieved = (f_g1 + f_g2) / ((t_g1 + t_g2) / 1e3) / 1e12
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            tj = json.load(f).get(args.workload)
+        if tj:
+            traffic = tj.get("gemm_bytes_per_launch")
+    roof = {"bound": "tensor", "kernel": "dsca grouped_gemm_kernel (tcgen05, GEMM1+GEMM2 launches)",
+            "achieved": achieved, "peak": peaks["tc_sus"], "unit": "TFLOP/s",
+            "frac": achieved / peaks["tc_sus"], "traffic": traffic,
+            "peak_kind": f"bf16_tflops_sustained ({peaks['src']})",
+            "algorithmic_flops_per_step": f_g1 + f_g2, "gemm1_ms": t_g1, "gemm2_ms": t_g2}
+    total_flops = f_router + f_g1 + f_g2
+    t_roof = max(total_flops / (peaks["tc_sus"] * 1e12), hbm / (peaks["hbm"] * 1e9))
+    layer_roof = {"flops": total_flops, "hbm_bytes": hbm, "t_roof_ms": t_roof * 1e3,
+                  "frac": t_roof * 1e3 / ms_per_step, "peaks": f"tensor {peaks['tc_sus']} TFLOP/s sustained, "
+                                                             f"HBM {peaks['hbm']} GB/s ({peaks['src']})"}
+
+    # ---- CPU baseline (rank 0, one GPU only)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, threads, desc = cpu_oracle_rate(w, Wr, host_weights(raw), args.cpu_seconds)
+        cpu = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": desc}
+
+    if rank == 0:
+        line = {
+            "metric": "MoE-layer tokens/sec (max over ranks)", "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": w["name"], "tokens_per_gpu": T, "batch_x_seq": "16x256" if T == 4096 else str(T),
+                       "d_model": w["d"], "experts": w["E"], "expert_inter": w["inter"], "shared_inter": w["shared"],
+                       "top_k": w["k"], "router": f"zipf{w['zipf']} (calibrated top-1)",
+                       "placement": "contiguous (60 on 8 = 4x8 + 4x7)" if w["E"] % max(world, 1) else "contiguous",
+                       "plan": f"harmony eq_tokens={args.eq_tokens}" if world > 1 else "local",
+                       "l2": "flushed (256 MiB write, untimed) before every timed step",
+                       "parallelism": f"ep{world}"},
+            "roofline": roof, "layer_roofline": layer_roof, "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * w["d"] * 2,
+                    "d2h_bytes_per_step": T * w["d"] * 2},
+            "gpu_launches": 6 * args.steps, "clocks": clk,
+            "phases_ms": phase_ms,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

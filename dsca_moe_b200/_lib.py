@@ -1,0 +1,120 @@
+"""ctypes binding of libdsca_b200.so (include/dsca_b200.h).
+
+The library is the only compute path: if it is missing or the device is not an sm_100 part,
+every call raises; there is no CPU or eager-PyTorch fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "lib", "libdsca_b200.so")
+
+# status codes / enums (include/dsca_b200.h)
+OK, ERR_BAD_ARG, ERR_CAPACITY, ERR_WAIT_TIMEOUT, ERR_CUDA, ERR_DEVICE_INDEX, ERR_UNSUPPORTED = range(7)
+F32, BF16, F8E4M3 = 0, 1, 2
+ROUTE_SWITCH_TOP1, ROUTE_SOFTMAX_TOPK = 0, 1
+ACT_RELU, ACT_SWIGLU = 0, 1
+ROUTER_TOKENS = 32
+MAX_EXPERTS = 64
+MAX_TOPK = 8
+
+_vp = ctypes.c_void_p
+_i = ctypes.c_int
+
+
+class RouterArgs(ctypes.Structure):
+    _fields_ = [("x", _vp), ("w_router", _vp), ("w_shared_gate", _vp),
+                ("T", _i), ("d", _i), ("E", _i), ("top_k", _i), ("dtype", _i), ("mode", _i),
+                ("norm_topk", _i), ("weight_round_bf16", _i),
+                ("logits", _vp), ("topk_ids", _vp), ("topk_w", _vp), ("expert_index", _vp),
+                ("shared_gate", _vp), ("block_hist", _vp), ("local_rank", _vp)]
+
+
+class ScanArgs(ctypes.Structure):
+    _fields_ = [("block_hist", _vp), ("nblocks", _i), ("E", _i), ("counts", _vp), ("offsets", _vp),
+                ("block_base", _vp)]
+
+
+class PermuteArgs(ctypes.Structure):
+    _fields_ = [("x", _vp), ("T", _i), ("d", _i), ("E", _i), ("top_k", _i), ("dtype", _i),
+                ("topk_ids", _vp), ("local_rank", _vp), ("block_base", _vp), ("offsets", _vp),
+                ("G", _i), ("cum_split", _vp), ("dest_base", _vp), ("capacity", _i), ("out", _vp),
+                ("token_row", _vp), ("err", _vp)]
+
+
+class FfnArgs(ctypes.Structure):
+    _fields_ = [("dtype", _i), ("act", _i), ("d", _i), ("n1p", _i), ("ip", _i), ("dp", _i),
+                ("num_groups", _i), ("group_offsets", _vp), ("group_weight", _vp),
+                ("num_experts_w", _i), ("capacity", _i), ("a", _vp), ("w1", _vp), ("w2", _vp),
+                ("h", _vp), ("y", _vp), ("shared_rows", _i), ("shared_n1p", _i), ("shared_ip", _i),
+                ("xs", _vp), ("ws1", _vp), ("ws2", _vp), ("hs", _vp), ("ys", _vp), ("err", _vp),
+                ("num_ctas", _i), ("phases", _i)]
+
+
+class CombineArgs(ctypes.Structure):
+    _fields_ = [("T", _i), ("d", _i), ("top_k", _i), ("dtype", _i), ("y", _vp), ("token_row", _vp),
+                ("topk_w", _vp), ("ys", _vp), ("shared_gate", _vp), ("rows", _i), ("out", _vp),
+                ("err", _vp)]
+
+
+# every symbol include/dsca_b200.h declares
+EXPORTED = ["dsca_version", "dsca_status_string", "dsca_device_info", "dsca_router_topk",
+            "dsca_dispatch_scan", "dsca_permute", "dsca_grouped_ffn", "dsca_combine",
+            "dsca_plan_harmony", "dsca_plan_layout", "dsca_check_error", "dsca_exp_neg_eval"]
+
+_LIB = None
+
+
+class DscaError(RuntimeError):
+    def __init__(self, code: int, where: str):
+        self.code = code
+        super().__init__(f"{where}: dsca status {code} ({status_string(code)})")
+
+
+def load():
+    """Load the library (raises if it has not been built)."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(f"libdsca_b200.so not found at {LIB_PATH}: run `python -m dsca_moe_b200.build` "
+                           "(there is no fallback path)")
+    lib = ctypes.CDLL(LIB_PATH)
+    p = ctypes.POINTER
+    lib.dsca_version.restype = ctypes.c_char_p
+    lib.dsca_status_string.restype = ctypes.c_char_p
+    lib.dsca_status_string.argtypes = [_i]
+    lib.dsca_device_info.argtypes = [p(_i), p(_i)]
+    lib.dsca_router_topk.argtypes = [p(RouterArgs), _vp]
+    lib.dsca_dispatch_scan.argtypes = [p(ScanArgs), _vp]
+    lib.dsca_permute.argtypes = [p(PermuteArgs), _vp]
+    lib.dsca_grouped_ffn.argtypes = [p(FfnArgs), _vp]
+    lib.dsca_combine.argtypes = [p(CombineArgs), _vp]
+    lib.dsca_plan_harmony.argtypes = [_vp, _i, _i, _vp, _i, _vp]
+    lib.dsca_plan_layout.argtypes = [_vp, _i, _i, _i, p(_i), _vp, _vp, _vp, _vp, _vp, _vp, _vp]
+    lib.dsca_check_error.argtypes = [_vp, _vp]
+    lib.dsca_exp_neg_eval.argtypes = [_vp, _vp, _i, _vp]
+    for name in EXPORTED:
+        getattr(lib, name).restype = getattr(lib, name).restype or _i
+    lib.dsca_version.restype = ctypes.c_char_p
+    lib.dsca_status_string.restype = ctypes.c_char_p
+    _LIB = lib
+    return lib
+
+
+def status_string(code: int) -> str:
+    try:
+        return load().dsca_status_string(code).decode()
+    except Exception:  # noqa: BLE001 - only used to format an error message
+        return "?"
+
+
+def check(code: int, where: str):
+    if code != OK:
+        raise DscaError(code, where)
+
+
+def call(name: str, *args):
+    check(getattr(load(), name)(*args), name)

@@ -1,0 +1,189 @@
+// extern "C" entry points: argument validation, then the kernel launches in router.cu,
+// dispatch.cu, gemm_sm100.cu and gemm_simt.cu.  No entry point allocates device memory.
+#include <stdio.h>
+
+#include "common.cuh"
+
+namespace dsca {
+int launch_router(const dsca_router_args* p, cudaStream_t stream);
+int launch_exp_eval(const float* x, float* y, int n, cudaStream_t stream);
+int launch_scan(const dsca_scan_args* a, cudaStream_t stream);
+int launch_permute(const dsca_permute_args* a, cudaStream_t stream);
+int launch_combine(const dsca_combine_args* a, cudaStream_t stream);
+int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t stream);
+int launch_grouped_ffn_f32(const dsca_ffn_args* f, int num_sms, cudaStream_t stream);
+}  // namespace dsca
+
+namespace {
+
+struct DevInfo {
+  int device = -1;
+  int num_sms = 0;
+  int major = 0;
+};
+
+// per-device cache of the SM count (queried once per device)
+DevInfo g_dev[64];
+
+int device_info(int* num_sms, int* major) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return DSCA_ERR_CUDA;
+  DevInfo& d = g_dev[dev];
+  if (d.device != dev) {
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return DSCA_ERR_CUDA;
+    d.num_sms = prop.multiProcessorCount;
+    d.major = prop.major;
+    d.device = dev;
+  }
+  *num_sms = d.num_sms;
+  *major = d.major;
+  return DSCA_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+const char* dsca_version(void) { return "dsca_b200 0.1 (sm_100a)"; }
+
+const char* dsca_status_string(int s) {
+  switch (s) {
+    case DSCA_OK: return "ok";
+    case DSCA_ERR_BAD_ARG: return "bad argument";
+    case DSCA_ERR_CAPACITY: return "capacity exceeded";
+    case DSCA_ERR_WAIT_TIMEOUT: return "device wait timed out";
+    case DSCA_ERR_CUDA: return "CUDA error";
+    case DSCA_ERR_DEVICE_INDEX: return "device bounds check failed";
+    case DSCA_ERR_UNSUPPORTED: return "unsupported device (needs sm_100)";
+    default: return "unknown status";
+  }
+}
+
+int dsca_device_info(int* num_sms, int* is_sm100) {
+  if (num_sms == nullptr || is_sm100 == nullptr) return DSCA_ERR_BAD_ARG;
+  int major = 0;
+  int rc = device_info(num_sms, &major);
+  if (rc) return rc;
+  *is_sm100 = major == 10 ? 1 : 0;
+  return DSCA_OK;
+}
+
+int dsca_router_topk(const dsca_router_args* a, dsca_stream_t stream) {
+  if (a == nullptr || a->x == nullptr || a->w_router == nullptr || a->logits == nullptr ||
+      a->topk_ids == nullptr || a->topk_w == nullptr || a->block_hist == nullptr ||
+      a->local_rank == nullptr)
+    return DSCA_ERR_BAD_ARG;
+  if (a->T < 0 || a->d <= 0 || a->E <= 0) return DSCA_ERR_BAD_ARG;
+  if (a->dtype != DSCA_BF16 && a->dtype != DSCA_F32) return DSCA_ERR_BAD_ARG;
+  if (a->mode != DSCA_ROUTE_SWITCH_TOP1 && a->mode != DSCA_ROUTE_SOFTMAX_TOPK) return DSCA_ERR_BAD_ARG;
+  const int k = a->mode == DSCA_ROUTE_SWITCH_TOP1 ? 1 : a->top_k;
+  if (k <= 0 || k > DSCA_MAX_TOPK || k > a->E) return DSCA_ERR_BAD_ARG;
+  if (a->E + (a->w_shared_gate ? 1 : 0) > DSCA_MAX_EXPERTS) return DSCA_ERR_CAPACITY;
+  // 16-byte vector loads of x / W rows
+  const int vec = a->dtype == DSCA_BF16 ? 8 : 4;
+  if (a->d % vec != 0 || !aligned16(a->x) || !aligned16(a->w_router) ||
+      (a->w_shared_gate && !aligned16(a->w_shared_gate)))
+    return DSCA_ERR_BAD_ARG;
+  if (a->T == 0) return DSCA_OK;
+  return dsca::launch_router(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int dsca_dispatch_scan(const dsca_scan_args* a, dsca_stream_t stream) {
+  if (a == nullptr || a->block_hist == nullptr || a->counts == nullptr || a->offsets == nullptr ||
+      a->block_base == nullptr || a->nblocks < 0 || a->E <= 0)
+    return DSCA_ERR_BAD_ARG;
+  if (a->E > 4 * DSCA_MAX_EXPERTS) return DSCA_ERR_CAPACITY;
+  return dsca::launch_scan(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int dsca_permute(const dsca_permute_args* a, dsca_stream_t stream) {
+  if (a == nullptr || a->x == nullptr || a->topk_ids == nullptr || a->local_rank == nullptr ||
+      a->block_base == nullptr || a->out == nullptr || a->token_row == nullptr || a->T < 0 ||
+      a->d <= 0 || a->E <= 0 || a->top_k <= 0 || a->top_k > DSCA_MAX_TOPK || a->capacity < 0)
+    return DSCA_ERR_BAD_ARG;
+  if (a->dtype != DSCA_BF16 && a->dtype != DSCA_F32) return DSCA_ERR_BAD_ARG;
+  const int esz = a->dtype == DSCA_BF16 ? 2 : 4;
+  if (((size_t)a->d * esz) % 16 != 0 || !aligned16(a->x) || !aligned16(a->out)) return DSCA_ERR_BAD_ARG;
+  if (a->cum_split == nullptr) {
+    if (a->offsets == nullptr) return DSCA_ERR_BAD_ARG;
+  } else {
+    if (a->dest_base == nullptr || a->G <= 0 || a->G > DSCA_MAX_GPUS) return DSCA_ERR_BAD_ARG;
+  }
+  return dsca::launch_permute(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int dsca_grouped_ffn(const dsca_ffn_args* f, dsca_stream_t stream) {
+  if (f == nullptr || f->a == nullptr || f->w1 == nullptr || f->w2 == nullptr || f->h == nullptr ||
+      f->y == nullptr || f->group_offsets == nullptr)
+    return DSCA_ERR_BAD_ARG;
+  if (f->num_groups <= 0 || f->num_groups > 256 || f->capacity < 0 || f->d <= 0 || f->num_experts_w <= 0)
+    return f->num_groups > 256 ? DSCA_ERR_CAPACITY : DSCA_ERR_BAD_ARG;
+  if (f->act != DSCA_ACT_RELU && f->act != DSCA_ACT_SWIGLU) return DSCA_ERR_BAD_ARG;
+  const bool glu = f->act == DSCA_ACT_SWIGLU;
+  // packing contract (see dsca_b200.h)
+  if (f->n1p <= 0 || f->n1p % 256 != 0 || f->dp < f->d || f->dp % 256 != 0) return DSCA_ERR_BAD_ARG;
+  if (f->ip != (glu ? f->n1p / 2 : f->n1p)) return DSCA_ERR_BAD_ARG;
+  if (f->d % 8 != 0) return DSCA_ERR_BAD_ARG;
+  if (f->shared_rows > 0) {
+    if (f->xs == nullptr || f->ws1 == nullptr || f->ws2 == nullptr || f->hs == nullptr || f->ys == nullptr)
+      return DSCA_ERR_BAD_ARG;
+    if (f->shared_n1p <= 0 || f->shared_n1p % 256 != 0 ||
+        f->shared_ip != (glu ? f->shared_n1p / 2 : f->shared_n1p))
+      return DSCA_ERR_BAD_ARG;
+  }
+  int num_sms = 0, major = 0;
+  int rc = device_info(&num_sms, &major);
+  if (rc) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (f->dtype == DSCA_BF16) {
+    if (major != 10) return DSCA_ERR_UNSUPPORTED;
+    if (f->d < 64) return DSCA_ERR_BAD_ARG;  // one 64-wide K box at least
+    const void* ptrs[] = {f->a, f->w1, f->w2, f->h, f->y};
+    for (const void* p : ptrs)
+      if (!aligned16(p)) return DSCA_ERR_BAD_ARG;
+    return dsca::launch_grouped_ffn_bf16(f, num_sms, st);
+  }
+  if (f->dtype == DSCA_F32) return dsca::launch_grouped_ffn_f32(f, num_sms, st);
+  return DSCA_ERR_BAD_ARG;
+}
+
+int dsca_combine(const dsca_combine_args* a, dsca_stream_t stream) {
+  if (a == nullptr || a->y == nullptr || a->token_row == nullptr || a->topk_w == nullptr ||
+      a->out == nullptr || a->T < 0 || a->d <= 0 || a->top_k <= 0 || a->top_k > DSCA_MAX_TOPK)
+    return DSCA_ERR_BAD_ARG;
+  if (a->dtype != DSCA_BF16 && a->dtype != DSCA_F32) return DSCA_ERR_BAD_ARG;
+  if (a->d % 8 != 0 || !aligned16(a->y) || !aligned16(a->out) || (a->ys && !aligned16(a->ys)))
+    return DSCA_ERR_BAD_ARG;
+  if ((a->ys == nullptr) != (a->shared_gate == nullptr)) return DSCA_ERR_BAD_ARG;
+  return dsca::launch_combine(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int dsca_check_error(int32_t* err_dev, dsca_stream_t stream) {
+  if (err_dev == nullptr) return DSCA_ERR_BAD_ARG;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int32_t h = 0;
+  if (cudaMemcpyAsync(&h, err_dev, sizeof(int32_t), cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return DSCA_ERR_CUDA;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return DSCA_ERR_CUDA;
+  if (h != 0) {
+    if (cudaMemsetAsync(err_dev, 0, sizeof(int32_t), st) != cudaSuccess) return DSCA_ERR_CUDA;
+    if (cudaStreamSynchronize(st) != cudaSuccess) return DSCA_ERR_CUDA;
+  }
+  switch (h) {
+    case dsca::kErrNone: return DSCA_OK;
+    case dsca::kErrWaitTimeout: return DSCA_ERR_WAIT_TIMEOUT;
+    case dsca::kErrIndex: return DSCA_ERR_DEVICE_INDEX;
+    case dsca::kErrCapacity: return DSCA_ERR_CAPACITY;
+    default: return DSCA_ERR_DEVICE_INDEX;
+  }
+}
+
+int dsca_exp_neg_eval(const float* x, float* y, int n, dsca_stream_t stream) {
+  if ((x == nullptr || y == nullptr) && n > 0) return DSCA_ERR_BAD_ARG;
+  return dsca::launch_exp_eval(x, y, n, reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,210 @@
+// K3 dispatch scan + permute, and K6 combine.
+//
+// Scan: counts, expert-major offsets and per-block base ranks from the router's per-block
+// histograms (replaces bincount / sort / nonzero at src/qosmoe/moe_layer.py:206-215,300-304
+// and qwen_ep_adapter/qwen_ep.py:62,69,80).
+// Permute: stable expert-major (or plan-ordered send-buffer) row copy, one warp per routed
+// (token, slot), 16-byte vector loads / stores (replaces the gathers of
+// src/qosmoe/moe_layer.py:214-215 and Scheduler.distribute_tokens,
+// src/harmonymoe/scheduler.py:101-124).
+// Combine: deterministic gather-reduce (replaces router_probs * h at moe_layer.py:255-258 and
+// index_add_ + shared add at qwen_ep.py:92-94).
+#include "common.cuh"
+
+namespace dsca {
+
+// ------------------------------------------------------------------ scan
+// One CTA of 1024 threads: thread (e, c) with c in [0, 16) sums a contiguous run of blocks of
+// expert e, the 16 partials are scanned in shared memory, then each thread writes the base
+// ranks of its run.
+constexpr int kScanChunks = 16;
+
+__global__ void __launch_bounds__(1024) scan_kernel(const int32_t* __restrict__ hist, int nb, int E,
+                                                    int32_t* counts, int32_t* offsets,
+                                                    int32_t* block_base) {
+  __shared__ int part[DSCA_MAX_EXPERTS * 4][kScanChunks + 1];
+  __shared__ int cnt_s[DSCA_MAX_EXPERTS * 4];
+  const int per = (nb + kScanChunks - 1) / kScanChunks;
+  for (int base_e = 0; base_e < E; base_e += 1024 / kScanChunks) {
+    int e = base_e + threadIdx.x / kScanChunks;
+    int c = threadIdx.x % kScanChunks;
+    int b0 = c * per, b1 = min(nb, b0 + per);
+    int s = 0;
+    if (e < E)
+      for (int b = b0; b < b1; ++b) s += hist[(size_t)b * E + e];
+    if (e < E) part[e][c] = s;
+    __syncthreads();
+    if (e < E && c == 0) {
+      int run = 0;
+      for (int i = 0; i < kScanChunks; ++i) {
+        int v = part[e][i];
+        part[e][i] = run;
+        run += v;
+      }
+      cnt_s[e] = run;
+      counts[e] = run;
+    }
+    __syncthreads();
+    if (e < E) {
+      int run = part[e][c];
+      for (int b = b0; b < b1; ++b) {
+        int v = hist[(size_t)b * E + e];
+        block_base[(size_t)b * E + e] = run;
+        run += v;
+      }
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    int run = 0;
+    for (int e = 0; e < E; ++e) {
+      offsets[e] = run;
+      run += cnt_s[e];
+    }
+    offsets[E] = run;
+  }
+}
+
+int launch_scan(const dsca_scan_args* a, cudaStream_t stream) {
+  scan_kernel<<<1, 1024, 0, stream>>>(a->block_hist, a->nblocks, a->E, a->counts, a->offsets,
+                                      a->block_base);
+  return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
+}
+
+// ------------------------------------------------------------------ permute
+template <int ESZ>
+__global__ void __launch_bounds__(256) permute_kernel(dsca_permute_args a) {
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = lane_id();
+  const int total = a.T * a.top_k;
+  if (w >= total) return;
+  const int t = w / a.top_k;
+  const int e = a.topk_ids[w];
+  if (e < 0 || e >= a.E) {
+    if (lane == 0) record_error(a.err, kErrIndex);
+    return;
+  }
+  const int b = t / DSCA_ROUTER_TOKENS;
+  const int q = a.block_base[(size_t)b * a.E + e] + a.local_rank[w];
+  int row;
+  if (a.cum_split == nullptr) {
+    row = a.offsets[e] + q;
+  } else {
+    int dst = 0;
+    int before = 0;
+    const int32_t* cs = a.cum_split + (size_t)e * a.G;
+    while (dst < a.G && q >= cs[dst]) ++dst;
+    if (dst >= a.G) {
+      if (lane == 0) record_error(a.err, kErrIndex);
+      return;
+    }
+    before = dst > 0 ? cs[dst - 1] : 0;
+    row = a.dest_base[(size_t)e * a.G + dst] + (q - before);
+  }
+  if (row < 0 || row >= a.capacity) {
+    if (lane == 0) record_error(a.err, kErrCapacity);
+    return;
+  }
+  if (lane == 0) a.token_row[w] = row;
+  const size_t row_bytes = (size_t)a.d * ESZ;
+  const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(a.x) + (size_t)t * row_bytes);
+  uint4* dstp = reinterpret_cast<uint4*>(reinterpret_cast<char*>(a.out) + (size_t)row * row_bytes);
+  const int nvec = (int)(row_bytes / 16);
+  for (int v = lane; v < nvec; v += 32) dstp[v] = src[v];
+}
+
+int launch_permute(const dsca_permute_args* a, cudaStream_t stream) {
+  const long long warps = (long long)a->T * a->top_k;
+  if (warps == 0) return DSCA_OK;
+  const int blocks = (int)((warps * 32 + 255) / 256);
+  if (a->dtype == DSCA_BF16)
+    permute_kernel<2><<<blocks, 256, 0, stream>>>(*a);
+  else
+    permute_kernel<4><<<blocks, 256, 0, stream>>>(*a);
+  return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
+}
+
+// ------------------------------------------------------------------ combine
+// One warp per token; lane owns 8 consecutive columns per step (one 16-byte bf16 vector or
+// two 16-byte f32 vectors).  Sum order: slot 0..k-1, then the shared expert.
+template <typename T>
+struct Vec8;
+template <>
+struct Vec8<__nv_bfloat16> {
+  static __device__ void load(const void* p, float (&v)[8]) {
+    uint4 u = *reinterpret_cast<const uint4*>(p);
+    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __bfloat162float(h[i]);
+  }
+  static __device__ void store(void* p, const float (&v)[8]) {
+    uint4 u;
+    u.x = pack_bf16x2(v[0], v[1]);
+    u.y = pack_bf16x2(v[2], v[3]);
+    u.z = pack_bf16x2(v[4], v[5]);
+    u.w = pack_bf16x2(v[6], v[7]);
+    *reinterpret_cast<uint4*>(p) = u;
+  }
+};
+template <>
+struct Vec8<float> {
+  static __device__ void load(const void* p, float (&v)[8]) {
+    float4 a = reinterpret_cast<const float4*>(p)[0];
+    float4 b = reinterpret_cast<const float4*>(p)[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+  static __device__ void store(void* p, const float (&v)[8]) {
+    reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+  }
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256) combine_kernel(dsca_combine_args a) {
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = lane_id();
+  if (t >= a.T) return;
+  int rows[DSCA_MAX_TOPK];
+  float w[DSCA_MAX_TOPK];
+  for (int j = 0; j < a.top_k; ++j) {
+    rows[j] = a.token_row[(size_t)t * a.top_k + j];
+    w[j] = a.topk_w[(size_t)t * a.top_k + j];
+    if (rows[j] < 0 || rows[j] >= a.rows) {
+      if (lane == 0) record_error(a.err, kErrIndex);
+      return;
+    }
+  }
+  const float sg = (a.ys != nullptr && a.shared_gate != nullptr) ? a.shared_gate[t] : 0.0f;
+  const T* Y = reinterpret_cast<const T*>(a.y);
+  const T* YS = reinterpret_cast<const T*>(a.ys);
+  T* O = reinterpret_cast<T*>(a.out);
+  for (int c = lane * 8; c < a.d; c += 256) {
+    float acc[8], v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+    for (int j = 0; j < a.top_k; ++j) {
+      Vec8<T>::load(Y + (size_t)rows[j] * a.d + c, v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = __fmaf_rn(w[j], v[i], acc[i]);
+    }
+    if (YS != nullptr) {
+      Vec8<T>::load(YS + (size_t)t * a.d + c, v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = __fmaf_rn(sg, v[i], acc[i]);
+    }
+    Vec8<T>::store(O + (size_t)t * a.d + c, acc);
+  }
+}
+
+int launch_combine(const dsca_combine_args* a, cudaStream_t stream) {
+  if (a->T == 0) return DSCA_OK;
+  const int blocks = (int)(((long long)a->T * 32 + 255) / 256);
+  if (a->dtype == DSCA_BF16)
+    combine_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>(*a);
+  else
+    combine_kernel<float><<<blocks, 256, 0, stream>>>(*a);
+  return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
+}
+
+}  // namespace dsca

@@ -1,0 +1,264 @@
+// K5 (fp32 parity mode) — grouped expert FFN on the CUDA cores in fp32.
+//
+// tf32 tensor-core math (10-bit mantissa) cannot meet the 1e-4 relative bar of the fp32 Switch
+// layer, so this mode accumulates true fp32 FMAs.  Same packed weight layout, same row groups
+// and same epilogues as the tcgen05 path (gemm_sm100.cu); it is a correctness mode, not the
+// throughput path.  Tile 64 x 64 (x 2 for SwiGLU: gate and up halves), K step 16,
+// 256 threads x (4 x 4) outputs, persistent over (segment, group, M tile, N tile).
+#include "common.cuh"
+
+namespace dsca {
+namespace simt {
+
+constexpr int TM = 64, TN = 64, TK = 16;
+constexpr int kThreads = 256;
+constexpr int kMaxGroups = 256;
+
+enum Epi { kEpiSwiGLU = 0, kEpiReLU = 1, kEpiStore = 2 };
+
+struct Segment {
+  const int32_t* group_offsets;
+  const int32_t* group_weight;
+  int ngroups, rows;
+  const float* a;       // [*, K]
+  int lda;
+  const float* b;       // [groups_w * b_rows_per_group, K]
+  int b_rows_per_group;
+  int K;
+  int n_tiles;          // output column tiles of TN
+  float* c;
+  int ldc, n_store, capacity;
+};
+
+struct Params {
+  Segment seg[2];
+  int nseg, epi;
+  int32_t* err;
+};
+
+__global__ void __launch_bounds__(kThreads) grouped_gemm_f32(const Params p) {
+  __shared__ float As[TK][TM + 4];
+  __shared__ float Bs[2][TK][TN + 4];
+  __shared__ int tile_start[kMaxGroups + 1];
+  __shared__ int goff[kMaxGroups + 1];
+  __shared__ int gw[kMaxGroups];
+  __shared__ int tot[2];
+
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    const Segment& sg = p.seg[0];
+    int run = 0;
+    for (int g = 0; g <= sg.ngroups; ++g)
+      goff[g] = sg.group_offsets ? sg.group_offsets[g] : (g == 0 ? 0 : sg.rows);
+    for (int g = 0; g < sg.ngroups; ++g) {
+      gw[g] = sg.group_weight ? sg.group_weight[g] : g;
+      tile_start[g] = run;
+      int rows_g = goff[g + 1] - goff[g];
+      if (rows_g < 0 || goff[g + 1] > sg.capacity) {
+        record_error(p.err, kErrCapacity);
+        rows_g = 0;
+      }
+      run += ((rows_g + TM - 1) / TM) * sg.n_tiles;
+    }
+    tile_start[sg.ngroups] = run;
+    tot[0] = run;
+    tot[1] = p.nseg > 1 ? ((p.seg[1].rows + TM - 1) / TM) * p.seg[1].n_tiles : 0;
+  }
+  __syncthreads();
+  const int total = tot[0] + tot[1];
+  const bool glu = p.epi == kEpiSwiGLU;
+  const int ty = tid / 16, tx = tid % 16;  // 16 x 16 threads, 4 x 4 outputs each
+
+  for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
+    int segi, row0, rows_valid, brow0, n_blk;
+    if (tile < tot[0]) {
+      const Segment& sg = p.seg[0];
+      int lo = 0, hi = sg.ngroups;
+      while (hi - lo > 1) {
+        int mid = (lo + hi) >> 1;
+        if (tile_start[mid] <= tile) lo = mid; else hi = mid;
+      }
+      int local = tile - tile_start[lo];
+      int m_blk = local / sg.n_tiles;
+      n_blk = local - m_blk * sg.n_tiles;
+      segi = 0;
+      row0 = goff[lo] + m_blk * TM;
+      rows_valid = min(TM, goff[lo + 1] - goff[lo] - m_blk * TM);
+      brow0 = gw[lo] * sg.b_rows_per_group;
+    } else {
+      const Segment& sg = p.seg[1];
+      int local = tile - tot[0];
+      int m_blk = local / sg.n_tiles;
+      n_blk = local - m_blk * sg.n_tiles;
+      segi = 1;
+      row0 = m_blk * TM;
+      rows_valid = min(TM, sg.rows - row0);
+      brow0 = 0;
+    }
+    const Segment& sg = p.seg[segi];
+    // B rows of this tile: SwiGLU takes 64 gate rows at (n_blk/2)*256 + (n_blk%2)*64 and the
+    // matching up rows 128 further; other epilogues take 64 consecutive rows.
+    int bcol_gate, bcol_up;
+    if (glu) {
+      bcol_gate = brow0 + (n_blk / 2) * 256 + (n_blk % 2) * 64;
+      bcol_up = bcol_gate + 128;
+    } else {
+      bcol_gate = brow0 + n_blk * TN;
+      bcol_up = bcol_gate;
+    }
+    float acc[2][4][4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[h][i][j] = 0.0f;
+
+    for (int k0 = 0; k0 < sg.K; k0 += TK) {
+      __syncthreads();
+      // A tile: TM x TK -> As[k][m]; 1024 values / 256 threads
+      for (int idx = tid; idx < TM * TK; idx += kThreads) {
+        int m = idx / TK, k = idx % TK;
+        float v = 0.0f;
+        if (m < rows_valid && k0 + k < sg.K) v = sg.a[(size_t)(row0 + m) * sg.lda + k0 + k];
+        As[k][m] = v;
+      }
+      for (int h = 0; h < (glu ? 2 : 1); ++h) {
+        int bc = h == 0 ? bcol_gate : bcol_up;
+        for (int idx = tid; idx < TN * TK; idx += kThreads) {
+          int n = idx / TK, k = idx % TK;
+          float v = 0.0f;
+          if (k0 + k < sg.K) v = sg.b[(size_t)(bc + n) * sg.K + k0 + k];
+          Bs[h][k][n] = v;
+        }
+      }
+      __syncthreads();
+#pragma unroll
+      for (int k = 0; k < TK; ++k) {
+        float av[4], bv[4], uv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) av[i] = As[k][ty * 4 + i];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) bv[j] = Bs[0][k][tx * 4 + j];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[0][i][j] = __fmaf_rn(av[i], bv[j], acc[0][i][j]);
+        if (glu) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) uv[j] = Bs[1][k][tx * 4 + j];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[1][i][j] = __fmaf_rn(av[i], uv[j], acc[1][i][j]);
+        }
+      }
+    }
+    // epilogue
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      int m = ty * 4 + i;
+      if (m >= rows_valid) continue;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        int col = n_blk * TN + tx * 4 + j;
+        if (col >= sg.n_store) continue;
+        float v = acc[0][i][j];
+        if (glu) {
+          v = (v / (1.0f + expf(-v))) * acc[1][i][j];
+        } else if (p.epi == kEpiReLU) {
+          v = fmaxf(v, 0.0f);
+        }
+        sg.c[(size_t)(row0 + m) * sg.ldc + col] = v;
+      }
+    }
+  }
+}
+
+}  // namespace simt
+
+int launch_grouped_ffn_f32(const dsca_ffn_args* f, int num_sms, cudaStream_t stream) {
+  const bool shared = f->shared_rows > 0;
+  const int grid = (f->num_ctas > 0 ? f->num_ctas : num_sms) * 4;
+  const bool glu = f->act == DSCA_ACT_SWIGLU;
+  const int phases = f->phases == 0 ? 3 : f->phases;
+  // GEMM1
+  if (phases & 1) {
+    simt::Params p{};
+    p.epi = glu ? simt::kEpiSwiGLU : simt::kEpiReLU;
+    p.err = f->err;
+    p.nseg = shared ? 2 : 1;
+    simt::Segment& s0 = p.seg[0];
+    s0.group_offsets = f->group_offsets;
+    s0.group_weight = f->group_weight;
+    s0.ngroups = f->num_groups;
+    s0.a = reinterpret_cast<const float*>(f->a);
+    s0.lda = f->d;
+    s0.b = reinterpret_cast<const float*>(f->w1);
+    s0.b_rows_per_group = f->n1p;
+    s0.K = f->d;
+    s0.n_tiles = f->ip / simt::TN;
+    s0.c = reinterpret_cast<float*>(f->h);
+    s0.ldc = f->ip;
+    s0.n_store = f->ip;
+    s0.capacity = f->capacity;
+    if (shared) {
+      simt::Segment& s1 = p.seg[1];
+      s1.ngroups = 1;
+      s1.rows = f->shared_rows;
+      s1.a = reinterpret_cast<const float*>(f->xs);
+      s1.lda = f->d;
+      s1.b = reinterpret_cast<const float*>(f->ws1);
+      s1.b_rows_per_group = f->shared_n1p;
+      s1.K = f->d;
+      s1.n_tiles = f->shared_ip / simt::TN;
+      s1.c = reinterpret_cast<float*>(f->hs);
+      s1.ldc = f->shared_ip;
+      s1.n_store = f->shared_ip;
+      s1.capacity = f->shared_rows;
+    }
+    simt::grouped_gemm_f32<<<grid, simt::kThreads, 0, stream>>>(p);
+    if (cudaGetLastError() != cudaSuccess) return DSCA_ERR_CUDA;
+  }
+  // GEMM2
+  if (phases & 2) {
+    simt::Params p{};
+    p.epi = simt::kEpiStore;
+    p.err = f->err;
+    p.nseg = shared ? 2 : 1;
+    simt::Segment& s0 = p.seg[0];
+    s0.group_offsets = f->group_offsets;
+    s0.group_weight = f->group_weight;
+    s0.ngroups = f->num_groups;
+    s0.a = reinterpret_cast<const float*>(f->h);
+    s0.lda = f->ip;
+    s0.b = reinterpret_cast<const float*>(f->w2);
+    s0.b_rows_per_group = f->dp;
+    s0.K = f->ip;
+    s0.n_tiles = (f->d + simt::TN - 1) / simt::TN;
+    s0.c = reinterpret_cast<float*>(f->y);
+    s0.ldc = f->d;
+    s0.n_store = f->d;
+    s0.capacity = f->capacity;
+    if (shared) {
+      simt::Segment& s1 = p.seg[1];
+      s1.ngroups = 1;
+      s1.rows = f->shared_rows;
+      s1.a = reinterpret_cast<const float*>(f->hs);
+      s1.lda = f->shared_ip;
+      s1.b = reinterpret_cast<const float*>(f->ws2);
+      s1.b_rows_per_group = f->dp;
+      s1.K = f->shared_ip;
+      s1.n_tiles = (f->d + simt::TN - 1) / simt::TN;
+      s1.c = reinterpret_cast<float*>(f->ys);
+      s1.ldc = f->d;
+      s1.n_store = f->d;
+      s1.capacity = f->shared_rows;
+    }
+    simt::grouped_gemm_f32<<<grid, simt::kThreads, 0, stream>>>(p);
+    if (cudaGetLastError() != cudaSuccess) return DSCA_ERR_CUDA;
+  }
+  return DSCA_OK;
+}
+
+}  // namespace dsca

@@ -1,0 +1,528 @@
+// K5 — grouped expert GEMM on the 5th-generation tensor cores (sm_100a).
+//
+// One persistent kernel computes C[g] = epilogue(A[rows of group g] . B[weight(g)]^T) for every
+// row group g of up to two segments (segment 0: routed experts with device-side row offsets;
+// segment 1: the shared expert over all tokens).  It replaces the per-expert loop
+// tokens[idx] = expert(tokens[idx]) (src/qosmoe/async_cpu.py:137-173,
+// src/qosmoe/moe_layer.py:226-253, qwen_ep_adapter/qwen_ep.py:85-89) and the shared expert
+// (qwen_ep.py:94).
+//
+// Tile: 128 (rows) x 256 (cols) x 64 (K) per stage, bf16 in, fp32 accumulate in TMEM.
+//   warp 0      TMA producer (one thread): A 128x64 and B 256x64 tiles, 128-byte swizzle,
+//               4-stage ring guarded by full/empty mbarriers.  No multicast.
+//   warp 1      TMEM allocator (512 columns = two 128x256 fp32 accumulators) and MMA issuer
+//               (one thread): 4 x tcgen05.mma (M128 N256 K16) per stage, tcgen05.commit frees
+//               the stage and, after the last K block, signals the accumulator full.
+//   warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns, activation, bf16 pack, masked
+//               16-byte stores; the accumulator is released as soon as it has been read, so
+//               the next tile's MMAs overlap this tile's stores.
+// Tiles are enumerated (segment, group, M tile, N tile) with N fastest; CTA i takes tiles
+// i, i + grid, ...  Group row offsets are read on the device, so no host sync is needed.
+// Every wait is bounded (2 s): on a timeout the kernel records DSCA_ERR_WAIT_TIMEOUT in the
+// error word, drains its own outstanding copies and MMAs, frees TMEM and returns.
+#include "common.cuh"
+
+namespace dsca {
+namespace gemm {
+
+constexpr int BM = 128, BN = 256, BK = 64;
+constexpr int kStages = 4;
+constexpr int kABytes = BM * BK * 2;
+constexpr int kBBytes = BN * BK * 2;
+constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kThreads = 192;
+constexpr int kTmemCols = 512;
+constexpr int kMaxGroups = 256;
+constexpr int kSmemBytes = kStages * kStageBytes + 1024;  // + alignment slack
+
+enum Epi { kEpiSwiGLU = 0, kEpiReLU = 1, kEpiStore = 2 };
+
+struct Segment {
+  const int32_t* group_offsets;  // device [ngroups + 1], or null = one group of `rows`
+  const int32_t* group_weight;   // device [ngroups], or null = identity
+  int ngroups;
+  int rows;
+  int n_tiles;
+  int b_rows_per_group;
+  int k_blocks;
+  __nv_bfloat16* c;
+  int ldc;
+  int n_store;
+  int capacity;
+};
+
+struct Params {
+  Segment seg[2];
+  int nseg;
+  int epi;
+  int32_t* err;
+};
+
+struct TileInfo {
+  int seg, row0, rows_valid, b_row0, n_blk;
+};
+
+struct SmemCtl {
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t tmem_full[2];
+  uint64_t tmem_empty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort_flag;
+  int total_tiles;
+  int seg0_tiles;
+  int tile_start[kMaxGroups + 1];
+  int goff[kMaxGroups + 1];
+  int gw[kMaxGroups];
+};
+
+__device__ __forceinline__ TileInfo decode(const Params& p, const SmemCtl& s, int tile) {
+  TileInfo ti;
+  if (tile < s.seg0_tiles) {
+    const Segment& sg = p.seg[0];
+    // upper_bound over tile_start[0..ngroups]
+    int lo = 0, hi = sg.ngroups;  // find g with tile_start[g] <= tile < tile_start[g+1]
+    while (hi - lo > 1) {
+      int mid = (lo + hi) >> 1;
+      if (s.tile_start[mid] <= tile) lo = mid; else hi = mid;
+    }
+    int g = lo;
+    int local = tile - s.tile_start[g];
+    int m_blk = local / sg.n_tiles;
+    ti.n_blk = local - m_blk * sg.n_tiles;
+    int rows_g = s.goff[g + 1] - s.goff[g];
+    ti.seg = 0;
+    ti.row0 = s.goff[g] + m_blk * BM;
+    ti.rows_valid = min(BM, rows_g - m_blk * BM);
+    ti.b_row0 = s.gw[g] * sg.b_rows_per_group + ti.n_blk * BN;
+  } else {
+    const Segment& sg = p.seg[1];
+    int local = tile - s.seg0_tiles;
+    int m_blk = local / sg.n_tiles;
+    ti.n_blk = local - m_blk * sg.n_tiles;
+    ti.seg = 1;
+    ti.row0 = m_blk * BM;
+    ti.rows_valid = min(BM, sg.rows - ti.row0);
+    ti.b_row0 = ti.n_blk * BN;
+  }
+  return ti;
+}
+
+// Bounded wait that ignores the abort flag (used to drain in-flight work before exit).
+__device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) return;
+  }
+}
+
+__device__ __forceinline__ float silu(float g) { return g / (1.0f + __expf(-g)); }
+
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmB0,
+                        const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmB1,
+                        const Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  __shared__ SmemCtl ctl;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t smem_a = smem_u32(smem);
+  const uint32_t smem_b = smem_a + kStages * kABytes;
+
+  const int warp = warp_id(), lane = lane_id();
+  volatile int* abort_flag = &ctl.abort_flag;
+
+  // ---- prologue: barriers, TMEM, group tile table
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(&ctl.full[s]), 1);
+      mbar_init(smem_u32(&ctl.empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&ctl.tmem_full[a]), 1);
+      mbar_init(smem_u32(&ctl.tmem_empty[a]), 128);
+    }
+    mbar_init(smem_u32(&ctl.mma_done), 1);
+    ctl.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA0);
+    prefetch_tmap(&tmB0);
+    if (p.nseg > 1) {
+      prefetch_tmap(&tmA1);
+      prefetch_tmap(&tmB1);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&ctl.tmem_base), kTmemCols);
+    tmem_relinquish();
+  }
+  // group table of segment 0 (device offsets -> tile prefix), computed by warp 2
+  if (warp == 2) {
+    const Segment& sg = p.seg[0];
+    const int ng = sg.ngroups;
+    for (int g = lane; g <= ng; g += 32)
+      ctl.goff[g] = sg.group_offsets ? sg.group_offsets[g] : (g == 0 ? 0 : sg.rows);
+    for (int g = lane; g < ng; g += 32) ctl.gw[g] = sg.group_weight ? sg.group_weight[g] : g;
+    __syncwarp();
+    // each lane scans a contiguous run of groups, then a warp scan stitches the runs
+    const int per = (ng + 31) / 32;
+    const int g0 = min(ng, lane * per), g1 = min(ng, g0 + per);
+    int run = 0;
+    for (int g = g0; g < g1; ++g) {
+      int rows_g = ctl.goff[g + 1] - ctl.goff[g];
+      if (rows_g < 0 || ctl.goff[g + 1] > sg.capacity) {
+        record_error(p.err, kErrCapacity);
+        rows_g = 0;
+      }
+      run += ((rows_g + BM - 1) / BM) * sg.n_tiles;
+    }
+    int incl = run;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      int v = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += v;
+    }
+    int excl = incl - run;
+    for (int g = g0; g < g1; ++g) {
+      ctl.tile_start[g] = excl;
+      int rows_g = max(0, ctl.goff[g + 1] - ctl.goff[g]);
+      if (ctl.goff[g + 1] > sg.capacity) rows_g = 0;
+      excl += ((rows_g + BM - 1) / BM) * sg.n_tiles;
+    }
+    int total0 = __shfl_sync(0xffffffffu, incl, 31);
+    if (lane == 0) {
+      ctl.tile_start[ng] = total0;
+      ctl.seg0_tiles = total0;
+      int total1 = 0;
+      if (p.nseg > 1) total1 = ((p.seg[1].rows + BM - 1) / BM) * p.seg[1].n_tiles;
+      ctl.total_tiles = total0 + total1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = ctl.tmem_base;
+  const int total = ctl.total_tiles;
+
+  if (warp == 0) {
+    // ---------------- TMA producer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      int pending_phase[kStages];
+      for (int i = 0; i < kStages; ++i) pending_phase[i] = -1;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+        const TileInfo ti = decode(p, ctl, tile);
+        const CUtensorMap* ma = ti.seg == 0 ? &tmA0 : &tmA1;
+        const CUtensorMap* mb = ti.seg == 0 ? &tmB0 : &tmB1;
+        const int kb_n = p.seg[ti.seg].k_blocks;
+        for (int kb = 0; kb < kb_n; ++kb) {
+          if (!mbar_wait(smem_u32(&ctl.empty[s]), ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
+          const uint32_t fb = smem_u32(&ctl.full[s]);
+          mbar_arrive_expect_tx(fb, kStageBytes);
+          tma_load_2d(smem_a + s * kABytes, ma, fb, kb * BK, ti.row0);
+          tma_load_2d(smem_b + s * kBBytes, mb, fb, kb * BK, ti.b_row0);
+          pending_phase[s] = (int)ph;
+          if (++s == kStages) { s = 0; ph ^= 1u; }
+        }
+      }
+      if (!ok) {
+        // drain: the last issued load of every stage must land before the CTA exits
+        for (int i = 0; i < kStages; ++i)
+          if (pending_phase[i] >= 0) mbar_drain(smem_u32(&ctl.full[i]), (uint32_t)pending_phase[i]);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+      int s = 0;
+      uint32_t ph = 0;
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++it) {
+        const TileInfo ti = decode(p, ctl, tile);
+        const int acc = it & 1;
+        const uint32_t acc_ph = (uint32_t)((it >> 1) & 1);
+        if (!mbar_wait(smem_u32(&ctl.tmem_empty[acc]), acc_ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        const int kb_n = p.seg[ti.seg].k_blocks;
+        for (int kb = 0; kb < kb_n; ++kb) {
+          if (!mbar_wait(smem_u32(&ctl.full[s]), ph, abort_flag, p.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t adesc = sw128_kmajor_desc(smem_a + s * kABytes);
+          const uint64_t bdesc = sw128_kmajor_desc(smem_b + s * kBBytes);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_f16(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), idesc,
+                     (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit(smem_u32(&ctl.empty[s]));
+          if (++s == kStages) { s = 0; ph ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit(smem_u32(&ctl.tmem_full[acc]));
+      }
+      if (!ok) {
+        // aborting: wait until every MMA this thread issued has completed before TMEM is freed
+        umma_commit(smem_u32(&ctl.mma_done));
+        mbar_drain(smem_u32(&ctl.mma_done), 0);
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5 -> TMEM lane quarters 2, 3, 0, 1)
+    const int q = warp & 3;
+    const int r_in_tile = q * 32 + lane;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
+      const TileInfo ti = decode(p, ctl, tile);
+      const Segment& sg = p.seg[ti.seg];
+      const int acc = it & 1;
+      const uint32_t acc_ph = (uint32_t)((it >> 1) & 1);
+      // one lane polls, the warp follows its verdict (tcgen05.ld below must not diverge)
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait(smem_u32(&ctl.tmem_full[acc]), acc_ph, abort_flag, p.err) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      const bool valid = r_in_tile < ti.rows_valid;
+      const size_t row = (size_t)(ti.row0 + r_in_tile);
+      __nv_bfloat16* crow = sg.c + row * (size_t)sg.ldc;
+      if constexpr (EPI == kEpiSwiGLU) {
+        const int col0 = ti.n_blk * (BN / 2);
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 32) {
+          uint32_t g[32], u[32];
+          tmem_ld32(taddr + c, g);
+          tmem_ld32(taddr + BN / 2 + c, u);
+          tmem_wait_ld();
+          uint32_t packed[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float g0 = __uint_as_float(g[2 * i]), g1 = __uint_as_float(g[2 * i + 1]);
+            float u0 = __uint_as_float(u[2 * i]), u1 = __uint_as_float(u[2 * i + 1]);
+            packed[i] = pack_bf16x2(silu(g0) * u0, silu(g1) * u1);
+          }
+          const int col = col0 + c;
+          if (valid && col < sg.n_store) {
+            uint4* dst = reinterpret_cast<uint4*>(crow + col);
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              if (col + v * 8 < sg.n_store)
+                dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+          }
+        }
+      } else {
+        const int col0 = ti.n_blk * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t v32[32];
+          tmem_ld32(taddr + c, v32);
+          tmem_wait_ld();
+          uint32_t packed[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float a0 = __uint_as_float(v32[2 * i]), a1 = __uint_as_float(v32[2 * i + 1]);
+            if constexpr (EPI == kEpiReLU) {
+              a0 = fmaxf(a0, 0.0f);
+              a1 = fmaxf(a1, 0.0f);
+            }
+            packed[i] = pack_bf16x2(a0, a1);
+          }
+          const int col = col0 + c;
+          if (valid && col < sg.n_store) {
+            uint4* dst = reinterpret_cast<uint4*>(crow + col);
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              if (col + v * 8 < sg.n_store)
+                dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(smem_u32(&ctl.tmem_empty[acc]));
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace gemm
+
+// ------------------------------------------------------------------ host side
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static PFN_encodeTiled get_encode_fn() {
+  static PFN_encodeTiled fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    fn = reinterpret_cast<PFN_encodeTiled>(ptr);
+  }
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix, box = box_rows x 64, 128B swizzle.
+static int make_map_bf16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  PFN_encodeTiled enc = get_encode_fn();
+  if (enc == nullptr) return DSCA_ERR_CUDA;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (cols * 2) % 16 != 0) return DSCA_ERR_BAD_ARG;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? DSCA_OK : DSCA_ERR_CUDA;
+}
+
+static int launch_one(int epi, const CUtensorMap& a0, const CUtensorMap& b0, const CUtensorMap& a1,
+                      const CUtensorMap& b1, const gemm::Params& p, int grid, cudaStream_t stream) {
+  static bool attr_set[3] = {false, false, false};
+  cudaError_t e = cudaSuccess;
+  switch (epi) {
+    case gemm::kEpiSwiGLU:
+      if (!attr_set[0]) {
+        e = cudaFuncSetAttribute(gemm::grouped_gemm_kernel<gemm::kEpiSwiGLU>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::kSmemBytes);
+        attr_set[0] = e == cudaSuccess;
+      }
+      if (e == cudaSuccess)
+        gemm::grouped_gemm_kernel<gemm::kEpiSwiGLU><<<grid, gemm::kThreads, gemm::kSmemBytes, stream>>>(a0, b0, a1, b1, p);
+      break;
+    case gemm::kEpiReLU:
+      if (!attr_set[1]) {
+        e = cudaFuncSetAttribute(gemm::grouped_gemm_kernel<gemm::kEpiReLU>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::kSmemBytes);
+        attr_set[1] = e == cudaSuccess;
+      }
+      if (e == cudaSuccess)
+        gemm::grouped_gemm_kernel<gemm::kEpiReLU><<<grid, gemm::kThreads, gemm::kSmemBytes, stream>>>(a0, b0, a1, b1, p);
+      break;
+    default:
+      if (!attr_set[2]) {
+        e = cudaFuncSetAttribute(gemm::grouped_gemm_kernel<gemm::kEpiStore>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::kSmemBytes);
+        attr_set[2] = e == cudaSuccess;
+      }
+      if (e == cudaSuccess)
+        gemm::grouped_gemm_kernel<gemm::kEpiStore><<<grid, gemm::kThreads, gemm::kSmemBytes, stream>>>(a0, b0, a1, b1, p);
+      break;
+  }
+  if (e != cudaSuccess) return DSCA_ERR_CUDA;
+  return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
+}
+
+int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t stream) {
+  const int grid = f->num_ctas > 0 ? f->num_ctas : num_sms;
+  const bool shared = f->shared_rows > 0;
+  const int phases = f->phases == 0 ? 3 : f->phases;
+  int rc;
+  // ---- GEMM1: h = act(a . w1^T)   (+ hs = act(xs . ws1^T))
+  if (phases & 1) {
+    CUtensorMap a0, b0, a1, b1;
+    if ((rc = make_map_bf16(&a0, f->a, (uint64_t)f->capacity, (uint64_t)f->d, gemm::BM))) return rc;
+    if ((rc = make_map_bf16(&b0, f->w1, (uint64_t)f->num_experts_w * f->n1p, (uint64_t)f->d, gemm::BN))) return rc;
+    if (shared) {
+      if ((rc = make_map_bf16(&a1, f->xs, (uint64_t)f->shared_rows, (uint64_t)f->d, gemm::BM))) return rc;
+      if ((rc = make_map_bf16(&b1, f->ws1, (uint64_t)f->shared_n1p, (uint64_t)f->d, gemm::BN))) return rc;
+    } else {
+      a1 = a0;
+      b1 = b0;
+    }
+    gemm::Params p{};
+    const int epi = f->act == DSCA_ACT_SWIGLU ? gemm::kEpiSwiGLU : gemm::kEpiReLU;
+    p.epi = epi;
+    p.err = f->err;
+    p.nseg = shared ? 2 : 1;
+    gemm::Segment& s0 = p.seg[0];
+    s0.group_offsets = f->group_offsets;
+    s0.group_weight = f->group_weight;
+    s0.ngroups = f->num_groups;
+    s0.rows = 0;
+    s0.n_tiles = f->n1p / gemm::BN;
+    s0.b_rows_per_group = f->n1p;
+    s0.k_blocks = (f->d + gemm::BK - 1) / gemm::BK;
+    s0.c = reinterpret_cast<__nv_bfloat16*>(f->h);
+    s0.ldc = f->ip;
+    s0.n_store = f->ip;
+    s0.capacity = f->capacity;
+    if (shared) {
+      gemm::Segment& s1 = p.seg[1];
+      s1.group_offsets = nullptr;
+      s1.group_weight = nullptr;
+      s1.ngroups = 1;
+      s1.rows = f->shared_rows;
+      s1.n_tiles = f->shared_n1p / gemm::BN;
+      s1.b_rows_per_group = f->shared_n1p;
+      s1.k_blocks = (f->d + gemm::BK - 1) / gemm::BK;
+      s1.c = reinterpret_cast<__nv_bfloat16*>(f->hs);
+      s1.ldc = f->shared_ip;
+      s1.n_store = f->shared_ip;
+      s1.capacity = f->shared_rows;
+    }
+    if ((rc = launch_one(epi, a0, b0, a1, b1, p, grid, stream))) return rc;
+  }
+  // ---- GEMM2: y = h . w2^T   (+ ys = hs . ws2^T)
+  if (phases & 2) {
+    CUtensorMap a0, b0, a1, b1;
+    if ((rc = make_map_bf16(&a0, f->h, (uint64_t)f->capacity, (uint64_t)f->ip, gemm::BM))) return rc;
+    if ((rc = make_map_bf16(&b0, f->w2, (uint64_t)f->num_experts_w * f->dp, (uint64_t)f->ip, gemm::BN))) return rc;
+    if (shared) {
+      if ((rc = make_map_bf16(&a1, f->hs, (uint64_t)f->shared_rows, (uint64_t)f->shared_ip, gemm::BM))) return rc;
+      if ((rc = make_map_bf16(&b1, f->ws2, (uint64_t)f->dp, (uint64_t)f->shared_ip, gemm::BN))) return rc;
+    } else {
+      a1 = a0;
+      b1 = b0;
+    }
+    gemm::Params p{};
+    p.epi = gemm::kEpiStore;
+    p.err = f->err;
+    p.nseg = shared ? 2 : 1;
+    gemm::Segment& s0 = p.seg[0];
+    s0.group_offsets = f->group_offsets;
+    s0.group_weight = f->group_weight;
+    s0.ngroups = f->num_groups;
+    s0.rows = 0;
+    s0.n_tiles = f->dp / gemm::BN;
+    s0.b_rows_per_group = f->dp;
+    s0.k_blocks = (f->ip + gemm::BK - 1) / gemm::BK;
+    s0.c = reinterpret_cast<__nv_bfloat16*>(f->y);
+    s0.ldc = f->d;
+    s0.n_store = f->d;
+    s0.capacity = f->capacity;
+    if (shared) {
+      gemm::Segment& s1 = p.seg[1];
+      s1.group_offsets = nullptr;
+      s1.group_weight = nullptr;
+      s1.ngroups = 1;
+      s1.rows = f->shared_rows;
+      s1.n_tiles = f->dp / gemm::BN;
+      s1.b_rows_per_group = f->dp;
+      s1.k_blocks = (f->shared_ip + gemm::BK - 1) / gemm::BK;
+      s1.c = reinterpret_cast<__nv_bfloat16*>(f->ys);
+      s1.ldc = f->d;
+      s1.n_store = f->d;
+      s1.capacity = f->shared_rows;
+    }
+    if ((rc = launch_one(gemm::kEpiStore, a0, b0, a1, b1, p, grid, stream))) return rc;
+  }
+  return DSCA_OK;
+}
+
+}  // namespace dsca

@@ -1,0 +1,431 @@
+"""MoE-block forward engine: packed expert weights, workspace, and the kernel sequence.
+
+One GPU:   router -> scan -> permute -> grouped FFN (routed + shared) -> combine, all on the
+           caller's current stream with device-side counts (no host sync).
+G GPUs:    router -> scan -> counts all-gather -> harmony plan (host C++, identical on every
+           rank) -> permute into the plan's send layout -> chunk exchange (NCCL grouped
+           send/recv, landing expert-major) -> grouped FFN on the received rows (+ the shared
+           expert on local tokens) -> return exchange -> combine.
+
+Reference hot path: QoSMoELayer.forward (src/qosmoe/moe_layer.py:271-459) and
+ShardedQwenMoE.forward (qwen_ep_adapter/qwen_ep.py:44-97).  Every expert's weights are
+resident on every GPU (B200 HBM holds a whole layer), so tokens that the harmony plan migrates
+to a GPU that does not own their expert are served from local HBM: replication needs no copy
+on the critical path.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib as L
+
+__all__ = ["PackedExperts", "pack_swiglu", "pack_relu", "MoEEngine", "plan_harmony", "plan_layout"]
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _ceil(a, b):
+    return (a + b - 1) // b
+
+
+def _dt(dtype: torch.dtype) -> int:
+    if dtype == torch.bfloat16:
+        return L.BF16
+    if dtype == torch.float32:
+        return L.F32
+    raise ValueError(f"unsupported dtype {dtype}")
+
+
+# ----------------------------------------------------------------------------- packing
+@dataclass
+class PackedExperts:
+    """Expert weights in the kernel layout (include/dsca_b200.h, dsca_ffn_args)."""
+    act: int
+    d: int
+    inter: int
+    E: int
+    w1: torch.Tensor      # [E, n1p, d]
+    w2: torch.Tensor      # [E, dp, ip]
+    n1p: int
+    ip: int
+    dp: int
+    # shared expert (SwiGLU, E = 1) or None
+    ws1: torch.Tensor | None = None
+    ws2: torch.Tensor | None = None
+    s_inter: int = 0
+    s_n1p: int = 0
+    s_ip: int = 0
+
+    @property
+    def dtype(self):
+        return self.w1.dtype
+
+
+def _pack_glu_w1(gate: torch.Tensor, up: torch.Tensor) -> tuple[torch.Tensor, int]:
+    """[E, I, d] gate / up -> [E, 2*Ip, d]: 256-row blocks of 128 gate rows then 128 up rows."""
+    E, I, d = gate.shape
+    ip = _ceil(I, 128) * 128
+    w = torch.zeros(E, ip // 128, 2, 128, d, dtype=gate.dtype, device=gate.device)
+    g = torch.zeros(E, ip, d, dtype=gate.dtype, device=gate.device)
+    u = torch.zeros(E, ip, d, dtype=gate.dtype, device=gate.device)
+    g[:, :I] = gate
+    u[:, :I] = up
+    w[:, :, 0] = g.view(E, ip // 128, 128, d)
+    w[:, :, 1] = u.view(E, ip // 128, 128, d)
+    return w.view(E, 2 * ip, d).contiguous(), ip
+
+
+def _pack_w2(down: torch.Tensor, ip: int) -> tuple[torch.Tensor, int]:
+    """[E, d, I] -> [E, dp, ip] zero padded (dp = ceil(d/256)*256)."""
+    E, d, I = down.shape
+    dp = _ceil(d, 256) * 256
+    w = torch.zeros(E, dp, ip, dtype=down.dtype, device=down.device)
+    w[:, :d, :I] = down
+    return w.contiguous(), dp
+
+
+def pack_swiglu(gate, up, down, shared=None, dtype=torch.bfloat16, device="cuda") -> PackedExperts:
+    """Qwen2MoeMLP experts: gate/up [E, I, d], down [E, d, I]; shared = (gate, up, down) of the
+    shared expert ([Is, d], [Is, d], [d, Is]) or None."""
+    gate = torch.as_tensor(gate).to(device=device, dtype=dtype)
+    up = torch.as_tensor(up).to(device=device, dtype=dtype)
+    down = torch.as_tensor(down).to(device=device, dtype=dtype)
+    E, I, d = gate.shape
+    w1, ip = _pack_glu_w1(gate, up)
+    w2, dp = _pack_w2(down, ip)
+    pe = PackedExperts(act=L.ACT_SWIGLU, d=d, inter=I, E=E, w1=w1, w2=w2, n1p=2 * ip, ip=ip, dp=dp)
+    if shared is not None:
+        sg, su, sd = (torch.as_tensor(t).to(device=device, dtype=dtype) for t in shared)
+        ws1, sip = _pack_glu_w1(sg[None], su[None])
+        ws2, _ = _pack_w2(sd[None], sip)
+        pe.ws1, pe.ws2 = ws1[0].contiguous(), ws2[0].contiguous()
+        pe.s_inter, pe.s_n1p, pe.s_ip = sg.shape[0], 2 * sip, sip
+    return pe
+
+
+def pack_relu(wi, wo, dtype=torch.bfloat16, device="cuda") -> PackedExperts:
+    """Switch DenseActDense experts: wi [E, F, d], wo [E, d, F]."""
+    wi = torch.as_tensor(wi).to(device=device, dtype=dtype)
+    wo = torch.as_tensor(wo).to(device=device, dtype=dtype)
+    E, F, d = wi.shape
+    fp = _ceil(F, 256) * 256
+    w1 = torch.zeros(E, fp, d, dtype=dtype, device=device)
+    w1[:, :F] = wi
+    w2, dp = _pack_w2(wo, fp)
+    return PackedExperts(act=L.ACT_RELU, d=d, inter=F, E=E, w1=w1.contiguous(), w2=w2, n1p=fp, ip=fp, dp=dp)
+
+
+# ----------------------------------------------------------------------------- plan (host C++)
+def plan_harmony(meta: np.ndarray, expert_to_gpu, eq_tokens: int) -> np.ndarray:
+    """S[G, E, G] from all-gathered counts meta[G, E] (dsca_plan_harmony)."""
+    meta = np.ascontiguousarray(meta, dtype=np.int32)
+    G, E = meta.shape
+    e2g = np.ascontiguousarray(expert_to_gpu, dtype=np.int32)
+    S = np.zeros((G, E, G), np.int32)
+    L.call("dsca_plan_harmony", meta.ctypes.data, G, E, e2g.ctypes.data, int(eq_tokens), S.ctypes.data)
+    return S
+
+
+@dataclass
+class Layout:
+    num_groups: int
+    group_expert: np.ndarray   # [ng]
+    group_offsets: np.ndarray  # [ng + 1]
+    recv_off: np.ndarray       # [G, E]
+    send_base: np.ndarray      # [E, G]
+    cum_split: np.ndarray      # [E, G]
+    send_splits: np.ndarray    # [G]
+    recv_splits: np.ndarray    # [G]
+
+
+def plan_layout(S: np.ndarray, rank: int) -> Layout:
+    S = np.ascontiguousarray(S, dtype=np.int32)
+    G, E, _ = S.shape
+    ng = ctypes.c_int(0)
+    ge = np.zeros(E, np.int32)
+    go = np.zeros(E + 1, np.int32)
+    ro = np.zeros((G, E), np.int32)
+    sb = np.zeros((E, G), np.int32)
+    cs = np.zeros((E, G), np.int32)
+    ss = np.zeros(G, np.int32)
+    rs = np.zeros(G, np.int32)
+    L.call("dsca_plan_layout", S.ctypes.data, G, E, rank, ctypes.byref(ng), ge.ctypes.data, go.ctypes.data,
+           ro.ctypes.data, sb.ctypes.data, cs.ctypes.data, ss.ctypes.data, rs.ctypes.data)
+    n = ng.value
+    return Layout(n, ge[:n].copy(), go[:n + 1].copy(), ro, sb, cs, ss, rs)
+
+
+def exchange_chunks(S: np.ndarray, lay: Layout, rank: int, send_buf, recv_buf, group=None, reverse=False):
+    """Move the plan's (src, e, dst) chunks.  Forward: send_buf (sender layout) -> recv_buf
+    (expert-major receive layout).  reverse=True moves expert outputs back: recv_buf (receive
+    layout) -> send_buf (sender layout).  Chunks between one pair of ranks are posted in expert
+    order on both sides, so NCCL pairs them in order.  Self chunks are device copies."""
+    import torch.distributed as dist
+
+    G, E, _ = S.shape
+    ops = []
+    for peer in range(G):
+        for e in range(E):
+            n_out = int(S[rank, e, peer])   # my tokens of e processed on peer
+            n_in = int(S[peer, e, rank])    # peer's tokens of e processed here
+            if peer == rank:
+                if n_out:
+                    a = int(lay.send_base[e, rank])
+                    b = int(lay.recv_off[rank, e])
+                    if not reverse:
+                        recv_buf[b:b + n_out].copy_(send_buf[a:a + n_out])
+                    else:
+                        send_buf[a:a + n_out].copy_(recv_buf[b:b + n_out])
+                continue
+            if n_out:
+                a = int(lay.send_base[e, peer])
+                t = send_buf[a:a + n_out]
+                ops.append(dist.P2POp(dist.irecv if reverse else dist.isend, t, peer, group))
+            if n_in:
+                b = int(lay.recv_off[peer, e])
+                t = recv_buf[b:b + n_in]
+                ops.append(dist.P2POp(dist.isend if reverse else dist.irecv, t, peer, group))
+    if ops:
+        for r in dist.batch_isend_irecv(ops):
+            r.wait()
+
+
+# ----------------------------------------------------------------------------- engine
+class MoEEngine:
+    """Runs one MoE block through libdsca_b200.
+
+    router_weight [E, d] (router dtype == activation dtype, as the reference's nn.Linear
+    requires); experts: PackedExperts; route_mode L.ROUTE_SWITCH_TOP1 or L.ROUTE_SOFTMAX_TOPK;
+    shared_gate_weight [d] or None.  Multi-GPU: pass world > 1, a torch.distributed group and
+    expert_to_gpu [E] (the placement), eq_tokens as in the reference scheduler.
+    """
+
+    def __init__(self, router_weight: torch.Tensor, experts: PackedExperts, top_k: int, route_mode: int,
+                 norm_topk: bool = False, shared_gate_weight: torch.Tensor | None = None,
+                 rank: int = 0, world: int = 1, group=None, expert_to_gpu=None, eq_tokens: int = 150,
+                 num_ctas: int = 0):
+        lib = L.load()
+        n_sms, is_sm100 = ctypes.c_int(0), ctypes.c_int(0)
+        L.check(lib.dsca_device_info(ctypes.byref(n_sms), ctypes.byref(is_sm100)), "dsca_device_info")
+        if experts.dtype == torch.bfloat16 and not is_sm100.value:
+            raise RuntimeError("the bf16 expert path needs an sm_100 (B200) GPU")
+        self.num_sms = n_sms.value
+        self.experts = experts
+        self.dtype = experts.dtype
+        self.device = experts.w1.device
+        self.router_weight = router_weight.to(device=self.device, dtype=self.dtype).contiguous()
+        self.E, self.d = self.router_weight.shape
+        if self.E != experts.E or self.d != experts.d:
+            raise ValueError("router and experts disagree on E / d")
+        self.route_mode = route_mode
+        self.top_k = 1 if route_mode == L.ROUTE_SWITCH_TOP1 else int(top_k)
+        self.norm_topk = bool(norm_topk)
+        self.shared_gate_weight = (None if shared_gate_weight is None else
+                                   shared_gate_weight.reshape(-1).to(device=self.device, dtype=self.dtype).contiguous())
+        if (self.shared_gate_weight is None) != (experts.ws1 is None):
+            raise ValueError("shared expert and shared gate must be given together")
+        self.rank, self.world, self.group = rank, world, group
+        if expert_to_gpu is None:
+            expert_to_gpu = default_expert_to_gpu(self.E, world)
+        self.expert_to_gpu = np.asarray(expert_to_gpu, dtype=np.int32)
+        self.eq_tokens = int(eq_tokens)
+        self.num_ctas = num_ctas
+        self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._ws = {}
+        self.last_plan = None
+        self.last_layout = None
+        # when a list, forward() appends (name, cuda.Event) markers between its kernel launches
+        self.markers = None
+
+    def _mark(self, name: str):
+        if self.markers is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self.markers.append((name, ev))
+
+    # -------------------------------------------------------------- workspace
+    def _workspace(self, T: int) -> dict:
+        ws = self._ws.get(T)
+        if ws is not None:
+            return ws
+        dev, dt, k, E, d = self.device, self.dtype, self.top_k, self.E, self.d
+        nb = _ceil(T, L.ROUTER_TOKENS)
+        pe = self.experts
+        cap = max(T * k, 1)
+        ws = dict(
+            topk_w=torch.empty(T, k, dtype=torch.float32, device=dev),
+            shared_gate=torch.empty(T, dtype=torch.float32, device=dev) if pe.ws1 is not None else None,
+            block_hist=torch.empty(max(nb, 1), E, dtype=torch.int32, device=dev),
+            local_rank=torch.empty(T, k, dtype=torch.int32, device=dev),
+            counts=torch.empty(E, dtype=torch.int32, device=dev),
+            offsets=torch.empty(E + 1, dtype=torch.int32, device=dev),
+            block_base=torch.empty(max(nb, 1), E, dtype=torch.int32, device=dev),
+            token_row=torch.empty(T, k, dtype=torch.int32, device=dev),
+            hs=torch.empty(T, pe.s_ip, dtype=dt, device=dev) if pe.ws1 is not None else None,
+            ys=torch.empty(T, d, dtype=dt, device=dev) if pe.ws1 is not None else None,
+        )
+        if self.world == 1:
+            ws.update(a=torch.empty(cap, d, dtype=dt, device=dev),
+                      h=torch.empty(cap, pe.ip, dtype=dt, device=dev),
+                      y=torch.empty(cap, d, dtype=dt, device=dev))
+        self._ws = {T: ws}  # keep one shape resident
+        return ws
+
+    # -------------------------------------------------------------- kernel steps
+    def _route(self, x: torch.Tensor, ws: dict):
+        T = x.shape[0]
+        a = L.RouterArgs()
+        a.x, a.w_router = _ptr(x), _ptr(self.router_weight)
+        a.w_shared_gate = _ptr(self.shared_gate_weight)
+        a.T, a.d, a.E, a.top_k = T, self.d, self.E, self.top_k
+        a.dtype = _dt(self.dtype)
+        a.mode = self.route_mode
+        a.norm_topk = int(self.norm_topk)
+        a.weight_round_bf16 = int(self.dtype == torch.bfloat16)
+        a.logits, a.topk_ids, a.topk_w = _ptr(ws["logits"]), _ptr(ws["topk_ids"]), _ptr(ws["topk_w"])
+        a.expert_index = _ptr(ws["expert_index"])
+        a.shared_gate = _ptr(ws["shared_gate"])
+        a.block_hist, a.local_rank = _ptr(ws["block_hist"]), _ptr(ws["local_rank"])
+        L.call("dsca_router_topk", ctypes.byref(a), _stream())
+        self._mark("router")
+        s = L.ScanArgs()
+        s.block_hist, s.nblocks, s.E = _ptr(ws["block_hist"]), _ceil(T, L.ROUTER_TOKENS), self.E
+        s.counts, s.offsets, s.block_base = _ptr(ws["counts"]), _ptr(ws["offsets"]), _ptr(ws["block_base"])
+        L.call("dsca_dispatch_scan", ctypes.byref(s), _stream())
+
+    def _permute(self, x, ws, out, capacity, G=1, cum_split=None, dest_base=None):
+        p = L.PermuteArgs()
+        p.x, p.T, p.d, p.E, p.top_k, p.dtype = _ptr(x), x.shape[0], self.d, self.E, self.top_k, _dt(self.dtype)
+        p.topk_ids, p.local_rank, p.block_base = _ptr(ws["topk_ids"]), _ptr(ws["local_rank"]), _ptr(ws["block_base"])
+        p.offsets = _ptr(ws["offsets"])
+        p.G, p.cum_split, p.dest_base = G, _ptr(cum_split), _ptr(dest_base)
+        p.capacity, p.out, p.token_row, p.err = capacity, _ptr(out), _ptr(ws["token_row"]), _ptr(self.err)
+        L.call("dsca_permute", ctypes.byref(p), _stream())
+
+    def _ffn(self, x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight):
+        if self.markers is not None:
+            # time GEMM1 and GEMM2 as separate launches
+            self._ffn_call(x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, 1)
+            self._mark("gemm1")
+            self._ffn_call(x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, 2)
+            self._mark("gemm2")
+        else:
+            self._ffn_call(x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, 3)
+
+    def _ffn_call(self, x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, phases):
+        pe = self.experts
+        f = L.FfnArgs()
+        f.dtype, f.act, f.d = _dt(self.dtype), pe.act, self.d
+        f.n1p, f.ip, f.dp = pe.n1p, pe.ip, pe.dp
+        f.num_groups, f.group_offsets, f.group_weight = num_groups, _ptr(group_offsets), _ptr(group_weight)
+        f.num_experts_w, f.capacity = pe.E, capacity
+        f.a, f.w1, f.w2, f.h, f.y = _ptr(a), _ptr(pe.w1), _ptr(pe.w2), _ptr(h), _ptr(y)
+        if pe.ws1 is not None:
+            f.shared_rows, f.shared_n1p, f.shared_ip = x.shape[0], pe.s_n1p, pe.s_ip
+            f.xs, f.ws1, f.ws2, f.hs, f.ys = _ptr(x), _ptr(pe.ws1), _ptr(pe.ws2), _ptr(ws["hs"]), _ptr(ws["ys"])
+        f.err, f.num_ctas, f.phases = _ptr(self.err), self.num_ctas, phases
+        L.call("dsca_grouped_ffn", ctypes.byref(f), _stream())
+
+    def _combine(self, ws, y, rows):
+        c = L.CombineArgs()
+        c.T, c.d, c.top_k, c.dtype = ws["out"].shape[0], self.d, self.top_k, _dt(self.dtype)
+        c.y, c.token_row, c.topk_w = _ptr(y), _ptr(ws["token_row"]), _ptr(ws["topk_w"])
+        c.ys, c.shared_gate = _ptr(ws["ys"]), _ptr(ws["shared_gate"])
+        c.rows, c.out, c.err = rows, _ptr(ws["out"]), _ptr(self.err)
+        L.call("dsca_combine", ctypes.byref(c), _stream())
+
+    # -------------------------------------------------------------- forward
+    def forward(self, x: torch.Tensor) -> dict:
+        """x [T, d] (activation dtype, on this engine's device).  Returns a dict with the fresh
+        results out [T, d], logits [T, E], topk_ids [T, k] and expert_index [T] (int64), plus
+        views of the reused scratch (topk_w, counts, token_row, ...) valid until the next call."""
+        if x.dim() != 2 or x.shape[1] != self.d:
+            raise ValueError(f"expected [T, {self.d}] input, got {tuple(x.shape)}")
+        x = x.to(dtype=self.dtype).contiguous()
+        T = x.shape[0]
+        ws = dict(self._workspace(T))
+        dev, k = self.device, self.top_k
+        # results are fresh tensors (the caller keeps them); scratch above is reused
+        ws.update(out=torch.empty(T, self.d, dtype=self.dtype, device=dev),
+                  logits=torch.empty(T, self.E, dtype=self.dtype, device=dev),
+                  topk_ids=torch.empty(T, k, dtype=torch.int32, device=dev),
+                  expert_index=torch.empty(T, dtype=torch.int64, device=dev))
+        if T == 0:
+            return ws
+        self._mark("start")
+        self._route(x, ws)
+        self._mark("scan")
+        if self.world == 1:
+            cap = ws["a"].shape[0]
+            self._permute(x, ws, ws["a"], cap)
+            self._mark("permute")
+            self._ffn(x, ws, ws["a"], ws["h"], ws["y"], cap, self.E, ws["offsets"], None)
+            self._combine(ws, ws["y"], cap)
+            self._mark("combine")
+            return ws
+        return self._forward_ep(x, ws)
+
+    def _forward_ep(self, x, ws):
+        import torch.distributed as dist
+
+        G, rank, E, d, dt, dev = self.world, self.rank, self.E, self.d, self.dtype, self.device
+        meta = torch.empty(G, E, dtype=torch.int32, device=dev)
+        dist.all_gather_into_tensor(meta, ws["counts"], group=self.group)
+        meta_h = meta.cpu().numpy()
+        S = plan_harmony(meta_h, self.expert_to_gpu, self.eq_tokens)
+        lay = plan_layout(S, rank)
+        self.last_plan, self.last_layout = S, lay
+        send_total = int(lay.send_splits.sum())
+        recv_total = int(lay.recv_splits.sum())
+        small = torch.from_numpy(np.concatenate([lay.cum_split.reshape(-1), lay.send_base.reshape(-1),
+                                                 lay.group_offsets, lay.group_expert])).to(dev, non_blocking=True)
+        n = E * G
+        cum_split, send_base = small[:n], small[n:2 * n]
+        ng = lay.num_groups
+        group_offsets = small[2 * n:2 * n + ng + 1]
+        group_expert = small[2 * n + ng + 1:]
+        send_buf = torch.empty(max(send_total, 1), d, dtype=dt, device=dev)
+        self._permute(x, ws, send_buf, send_buf.shape[0], G=G, cum_split=cum_split, dest_base=send_base)
+        recv_buf = torch.empty(max(recv_total, 1), d, dtype=dt, device=dev)
+        exchange_chunks(S, lay, rank, send_buf, recv_buf, self.group)
+        cap = recv_buf.shape[0]
+        h = torch.empty(cap, self.experts.ip, dtype=dt, device=dev)
+        y = torch.empty(cap, d, dtype=dt, device=dev)
+        if ng == 0:
+            # no routed rows here: one empty group keeps the launch uniform (shared expert still runs)
+            group_offsets = torch.zeros(2, dtype=torch.int32, device=dev)
+            group_expert = torch.zeros(1, dtype=torch.int32, device=dev)
+            ng = 1
+        self._ffn(x, ws, recv_buf, h, y, cap, ng, group_offsets, group_expert)
+        ret_buf = torch.empty(max(send_total, 1), d, dtype=dt, device=dev)
+        exchange_chunks(S, lay, rank, ret_buf, y, self.group, reverse=True)
+        self._combine(ws, ret_buf, ret_buf.shape[0])
+        return ws
+
+    def check(self):
+        """Synchronise and raise if a kernel recorded an error."""
+        L.check(L.load().dsca_check_error(_ptr(self.err), _stream()), "device error word")
+
+
+def default_expert_to_gpu(E: int, G: int) -> np.ndarray:
+    """Contiguous blocks, the first E % G GPUs one expert more (60 on 8 -> 4 x 8 + 4 x 7).
+    Equals the reference's naive arange(E) // (E // G) when G divides E
+    (src/harmonymoe/scheduler.py:215-222)."""
+    base, extra = divmod(E, G)
+    e2g = np.zeros(E, np.int32)
+    e = 0
+    for g in range(G):
+        n = base + (1 if g < extra else 0)
+        e2g[e:e + n] = g
+        e += n
+    return e2g

@@ -1,0 +1,239 @@
+/*
+ * dsca_b200 — C ABI of the B200 (sm_100a) MoE-block forward for DSCA-MoE.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream, launches its kernels
+ * on that stream and returns an int status (DSCA_OK = 0).  Nothing here allocates device
+ * memory: buffers and scratch space come from the caller, with the shapes documented beside
+ * each argument struct.  Kernels that detect a problem (a wait past its
+ * time limit, an out-of-range index, more rows than the workspace holds) write a code into the
+ * caller's device error word instead of trapping; dsca_check_error reads it back.
+ *
+ * References are to the acbling/DSCA-MoE source tree.
+ */
+#ifndef DSCA_B200_H_
+#define DSCA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define DSCA_API __attribute__((visibility("default")))
+#else
+#define DSCA_API
+#endif
+
+typedef struct CUstream_st* dsca_stream_t;
+
+/* status codes */
+enum {
+  DSCA_OK = 0,
+  DSCA_ERR_BAD_ARG = 1,       /* a null pointer, a bad size or an unsupported combination */
+  DSCA_ERR_CAPACITY = 2,      /* more rows / experts / tokens than the kernel or buffer allows */
+  DSCA_ERR_WAIT_TIMEOUT = 3,  /* a device-side wait passed its time limit (kernel returned) */
+  DSCA_ERR_CUDA = 4,          /* a CUDA runtime or driver call failed */
+  DSCA_ERR_DEVICE_INDEX = 5,  /* a kernel's bounds check rejected an index */
+  DSCA_ERR_UNSUPPORTED = 6    /* not available on this device (needs sm_100) */
+};
+
+/* element types */
+enum { DSCA_F32 = 0, DSCA_BF16 = 1, DSCA_F8E4M3 = 2 };
+
+/* routing modes */
+enum {
+  DSCA_ROUTE_SWITCH_TOP1 = 0, /* softmax in the router dtype, argmax (first index on ties) */
+  DSCA_ROUTE_SOFTMAX_TOPK = 1 /* softmax in fp32, top-k by (prob desc, expert id asc) */
+};
+
+/* expert activation */
+enum {
+  DSCA_ACT_RELU = 0,   /* Switch DenseActDense: wo(ReLU(wi x)) */
+  DSCA_ACT_SWIGLU = 1  /* Qwen2MoeMLP: down(SiLU(gate x) * up x) */
+};
+
+/* Tokens routed by one router CTA; per-block histograms are [ceil(T / DSCA_ROUTER_TOKENS), E]. */
+#define DSCA_ROUTER_TOKENS 32
+/* Largest expert count the router handles in one warp (2 experts per lane). */
+#define DSCA_MAX_EXPERTS 64
+#define DSCA_MAX_TOPK 8
+#define DSCA_MAX_GPUS 8
+
+DSCA_API const char* dsca_version(void);
+DSCA_API const char* dsca_status_string(int status);
+
+/* Number of SMs of the current device and whether it is an sm_100 part (1) or not (0). */
+DSCA_API int dsca_device_info(int* num_sms, int* is_sm100);
+
+/*
+ * Router: logits, softmax, top-k, per-block histogram and in-block stable ranks, fused.
+ * Replaces Router.standard_forward (src/harmonymoe/router.py:52-63) with the argmax at
+ * src/qosmoe/moe_layer.py:286-287, and the gate / softmax / topk of ShardedQwenMoE.forward
+ * (qwen_ep_adapter/qwen_ep.py:48-53), plus the shared-expert gate sigmoid(x . g)
+ * (qwen_ep_adapter/qwen_ep.py:94).
+ * Arithmetic order is fixed: logit = round_dtype(fp32 fma over i = 0..d-1), softmax with a
+ * deterministic exp (bit-identical to the C oracle).
+ */
+typedef struct {
+  const void* x;              /* [T, d], dtype */
+  const void* w_router;       /* [E, d], dtype (the reference router runs in its weight dtype) */
+  const void* w_shared_gate;  /* [d] dtype, or NULL (no shared expert) */
+  int T, d, E, top_k;
+  int dtype;                  /* DSCA_F32 or DSCA_BF16, for x and the router weight */
+  int mode;                   /* DSCA_ROUTE_* */
+  int norm_topk;              /* divide the k weights by their sum (Qwen norm_topk_prob) */
+  int weight_round_bf16;      /* round routing weights to bf16 (activation dtype bf16) */
+  void* logits;               /* [T, E] dtype */
+  int32_t* topk_ids;          /* [T, top_k] */
+  float* topk_w;              /* [T, top_k] */
+  int64_t* expert_index;      /* [T] top-1 id as int64, or NULL */
+  float* shared_gate;         /* [T] sigmoid(round_dtype(x . g)), or NULL */
+  int32_t* block_hist;        /* [ceil(T/32), E] tokens per expert in each 32-token block */
+  int32_t* local_rank;        /* [T, top_k] rank of (t, j) among its block's tokens of that expert */
+} dsca_router_args;
+DSCA_API int dsca_router_topk(const dsca_router_args* a, dsca_stream_t stream);
+
+/*
+ * Dispatch scan: per-expert counts, expert-major row offsets and each block's base rank inside
+ * every expert.  Replaces the bincount / sort / nonzero lists of
+ * src/qosmoe/moe_layer.py:206-215,300-304 and qwen_ep_adapter/qwen_ep.py:62,69,80.
+ */
+typedef struct {
+  const int32_t* block_hist;  /* [nblocks, E] */
+  int nblocks, E;
+  int32_t* counts;            /* [E] */
+  int32_t* offsets;           /* [E + 1] exclusive prefix of counts */
+  int32_t* block_base;        /* [nblocks, E] tokens of expert e in blocks before b */
+} dsca_scan_args;
+DSCA_API int dsca_dispatch_scan(const dsca_scan_args* a, dsca_stream_t stream);
+
+/*
+ * Permute: copy each routed (token, slot) row of x into the send / expert-major buffer.
+ * Row of (t, j) with expert e and per-expert rank q = block_base[b][e] + local_rank[t][j]:
+ * the destination dst is the first with q < cum_split[e][dst] (cumulative plan S[rank, e, :]),
+ * and the row is dest_base[e][dst] + q - cum_split[e][dst-1].  With one GPU, pass
+ * cum_split = NULL: the row is offsets[e] + q.  This is the a8 order of
+ * Scheduler.distribute_tokens (src/harmonymoe/scheduler.py:101-124): destination ascending,
+ * expert ascending, token ascending inside the expert, earliest tokens to the lowest dst.
+ */
+typedef struct {
+  const void* x;              /* [T, d] */
+  int T, d, E, top_k, dtype;
+  const int32_t* topk_ids;    /* [T, k] */
+  const int32_t* local_rank;  /* [T, k] */
+  const int32_t* block_base;  /* [nblocks, E] */
+  const int32_t* offsets;     /* [E + 1] (one-GPU layout) */
+  int G;                      /* GPUs in the plan (1 = local layout) */
+  const int32_t* cum_split;   /* [E, G] inclusive prefix over dst of S[rank, e, :], or NULL */
+  const int32_t* dest_base;   /* [E, G] first send row of (e, dst), or NULL */
+  int capacity;               /* rows of `out` */
+  void* out;                  /* [capacity, d] */
+  int32_t* token_row;         /* [T, k] row written for (t, j) */
+  int32_t* err;               /* device error word */
+} dsca_permute_args;
+DSCA_API int dsca_permute(const dsca_permute_args* a, dsca_stream_t stream);
+
+/*
+ * Grouped expert FFN.  Replaces the per-expert loop tokens[idx] = expert(tokens[idx])
+ * (src/qosmoe/async_cpu.py:137-173, src/qosmoe/moe_layer.py:226-253,
+ * qwen_ep_adapter/qwen_ep.py:85-89) and the shared expert (qwen_ep.py:94).
+ * bf16: tcgen05 grouped GEMM (TMEM accumulators, TMA-fed 128B-swizzled tiles, persistent
+ * tile scheduler over (group, M tile, N tile) read from device-side offsets).
+ * f32: CUDA-core grouped GEMM (fp32 parity mode).
+ * Weights are packed once (dsca_moe_b200 python: pack_*):
+ *   SwiGLU w1: [E, N1p, d] with N1p = 2 * ceil(I/128) * 128; each 256-row block holds 128 gate
+ *              rows then the 128 matching up rows (zero rows past I).
+ *   ReLU   w1: [E, N1p, d] with N1p = ceil(F/256) * 256 (zero rows past F).
+ *   w2:        [E, dp, Ip] with dp = ceil(d/256) * 256, Ip = N1p/2 (SwiGLU) or N1p (ReLU),
+ *              zero past d rows / I columns.
+ * h holds the activated intermediate [rows, Ip]; y the expert outputs [rows, d].
+ */
+typedef struct {
+  int dtype;                  /* DSCA_BF16 (tcgen05) or DSCA_F32 (CUDA cores) */
+  int act;                    /* DSCA_ACT_* */
+  int d;                      /* model width: GEMM1 K, GEMM2 N */
+  int n1p;                    /* packed GEMM1 N per expert */
+  int ip;                     /* packed intermediate width (GEMM2 K) */
+  int dp;                     /* packed GEMM2 N per expert */
+  int num_groups;             /* row groups in `a` */
+  const int32_t* group_offsets; /* device [num_groups + 1] row offsets into a / h / y */
+  const int32_t* group_weight;  /* device [num_groups] expert index into w1 / w2, NULL = identity */
+  int num_experts_w;          /* experts in w1 / w2 */
+  int capacity;               /* rows of a / h / y */
+  const void* a;              /* [capacity, d] */
+  const void* w1;             /* [num_experts_w, n1p, d] */
+  const void* w2;             /* [num_experts_w, dp, ip] */
+  void* h;                    /* [capacity, ip] */
+  void* y;                    /* [capacity, d] */
+  /* optional shared expert on all T tokens (Qwen): same packing with E = 1 */
+  int shared_rows;            /* 0 = none */
+  int shared_n1p, shared_ip;
+  const void* xs;             /* [shared_rows, d] */
+  const void* ws1;            /* [shared_n1p, d] */
+  const void* ws2;            /* [dp, shared_ip] */
+  void* hs;                   /* [shared_rows, shared_ip] */
+  void* ys;                   /* [shared_rows, d] */
+  int32_t* err;               /* device error word */
+  int num_ctas;               /* persistent CTAs (0 = one per SM) */
+  int phases;                 /* 0 or 3 = both GEMMs; 1 = GEMM1 only; 2 = GEMM2 only */
+} dsca_ffn_args;
+DSCA_API int dsca_grouped_ffn(const dsca_ffn_args* a, dsca_stream_t stream);
+
+/*
+ * Combine: out[t] = sum_j w[t,j] * y[token_row[t,j]] (+ shared_gate[t] * ys[t]), summed in
+ * fp32 in slot order and rounded once.  Replaces router_probs * h (src/qosmoe/moe_layer.py:
+ * 255-258) and the index_add_ + shared-expert add of qwen_ep_adapter/qwen_ep.py:92-94 with a
+ * deterministic gather (no atomics).
+ */
+typedef struct {
+  int T, d, top_k, dtype;
+  const void* y;              /* [rows, d] expert outputs */
+  const int32_t* token_row;   /* [T, k] */
+  const float* topk_w;        /* [T, k] */
+  const void* ys;             /* [T, d] shared expert output, or NULL */
+  const float* shared_gate;   /* [T] or NULL */
+  int rows;                   /* rows of y (bounds check) */
+  void* out;                  /* [T, d] */
+  int32_t* err;
+} dsca_combine_args;
+DSCA_API int dsca_combine(const dsca_combine_args* a, dsca_stream_t stream);
+
+/*
+ * Harmony plan on the host (integer, deterministic, identical on every rank).
+ * Restates Scheduler.schedule_harmony (src/harmonymoe/scheduler.py:324-372) over an arbitrary
+ * expert -> GPU placement (the exflow [layer][gpu] -> experts format,
+ * src/harmonymoe/scheduler.py:51-64,230-237, converted to expert_to_gpu).  eq_tokens < 0 gives
+ * schedule_fixed (:268-279).  One guard is added: an outer pass that moves nothing ends the
+ * loop (the reference would spin there).  meta: [G, E] counts; S: [G, E, G] out.
+ */
+DSCA_API int dsca_plan_harmony(const int32_t* meta, int G, int E, const int32_t* expert_to_gpu,
+                      int eq_tokens, int32_t* S);
+
+/*
+ * Receive layout for rank `rank` from plan S [G, E, G] (host arrays): the groups are the
+ * experts with tokens for this rank in ascending id; inside a group, chunks of src ascending
+ * (the stable form of Scheduler.generate_expert_mask, src/harmonymoe/scheduler.py:185-213).
+ * Outputs: num_groups, group_expert[E], group_offsets[E + 1], recv_off[G, E] (row of chunk
+ * (src, e) in the expert-major receive buffer, -1 if empty), and for the sender side
+ * send_base[E, G] (first send row of (e, dst) on `rank`), cum_split[E, G], send_splits[G],
+ * recv_splits[G].
+ */
+DSCA_API int dsca_plan_layout(const int32_t* S, int G, int E, int rank, int* num_groups,
+                     int32_t* group_expert, int32_t* group_offsets, int32_t* recv_off,
+                     int32_t* send_base, int32_t* cum_split, int32_t* send_splits,
+                     int32_t* recv_splits);
+
+/* Read (and clear) the device error word; returns the matching DSCA_ERR_* or DSCA_OK.
+ * Synchronises `stream`. */
+DSCA_API int dsca_check_error(int32_t* err_dev, dsca_stream_t stream);
+
+/* Device-side exp used by routing, evaluated on n inputs (test hook for the oracle pin). */
+DSCA_API int dsca_exp_neg_eval(const float* x, float* y, int n, dsca_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSCA_B200_H_ */

@@ -1,0 +1,119 @@
+"""C-ABI library: loads, exports every symbol include/dsca_b200.h declares, and its host-side
+planner (no GPU needed) matches the oracle and the reference's plans."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from golden_io import json_fixture
+from oracle import oracle as O
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared_symbols():
+    src = open(os.path.join(ROOT, "include", "dsca_b200.h")).read()
+    return sorted(set(re.findall(r"\b(dsca_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_symbols_exported(lib):
+    from dsca_moe_b200 import _lib
+
+    declared = _declared_symbols()
+    assert set(declared) == set(_lib.EXPORTED)
+    for name in declared:
+        assert hasattr(lib, name), name
+    assert b"sm_100a" in lib.dsca_version()
+    assert lib.dsca_status_string(3) == b"device wait timed out"
+
+
+def test_struct_layouts_match_header(lib):
+    """ctypes mirrors of the argument structs have the C sizes (checked against offsets that
+    the C compiler computes for the same declarations)."""
+    from dsca_moe_b200 import _lib
+
+    # every struct is pointers and ints; recompute the C layout rule independently
+    def c_size(fields):
+        off = 0
+        for f in fields:
+            sz = 8 if f[1] is ctypes.c_void_p else 4
+            off = (off + sz - 1) // sz * sz + sz
+        return (off + 7) // 8 * 8
+
+    for s in (_lib.RouterArgs, _lib.ScanArgs, _lib.PermuteArgs, _lib.FfnArgs, _lib.CombineArgs):
+        assert ctypes.sizeof(s) == c_size(s._fields_), s.__name__
+
+
+def test_bad_args_rejected_without_gpu(lib):
+    from dsca_moe_b200 import _lib
+
+    assert lib.dsca_router_topk(None, None) == _lib.ERR_BAD_ARG
+    a = _lib.RouterArgs()
+    assert lib.dsca_router_topk(ctypes.byref(a), None) == _lib.ERR_BAD_ARG
+    assert lib.dsca_grouped_ffn(None, None) == _lib.ERR_BAD_ARG
+    assert lib.dsca_plan_harmony(None, 2, 8, None, 150, None) == _lib.ERR_BAD_ARG
+
+
+def test_plan_harmony_matches_reference_plans(lib):
+    from dsca_moe_b200.engine import plan_harmony
+
+    for c in json_fixture("harmony_plans.json")["cases"]:
+        meta = np.array(c["meta"], np.int32)
+        S = plan_harmony(meta, c["expert_to_gpu"], c["eq_tokens"])
+        assert np.array_equal(S, np.array(c["harmony"])), (c["E"], c["G"], c["counts"])
+        F = plan_harmony(meta, c["expert_to_gpu"], -1)
+        assert np.array_equal(F, np.array(c["fixed"]))
+
+
+def test_plan_harmony_random_vs_oracle(lib):
+    from dsca_moe_b200.engine import default_expert_to_gpu, plan_harmony
+
+    g = np.random.default_rng(5)
+    for trial in range(300):
+        G = int(g.choice([2, 3, 4, 8]))
+        E = int(g.choice([6, 8, 16, 60, 64]))
+        eq = int(g.choice([0, 1, 50, 150, 10**6]))
+        meta = g.integers(0, int(g.choice([1, 5, 300])), size=(G, E)).astype(np.int32)
+        if trial % 3 == 0:
+            meta[:, 0] += g.integers(0, 3000, size=G).astype(np.int32)
+        e2g = default_expert_to_gpu(E, G)
+        assert np.array_equal(plan_harmony(meta, e2g, eq), O.harmony_schedule(meta, e2g, eq))
+
+
+def test_plan_layout_matches_reference_order(lib):
+    """Sender rows (dst, expert, token) and receiver groups (expert, src) as in
+    distribute_tokens / generate_expert_mask."""
+    from dsca_moe_b200.engine import plan_layout
+
+    for c in json_fixture("dispatch_order.json"):
+        S = np.array(c["schedule"], np.int32)
+        G, E = c["G"], c["E"]
+        for r in range(G):
+            lay = plan_layout(S, r)
+            assert lay.send_splits.tolist() == c["ranks"][r]["send_splits"]
+            assert lay.recv_splits.tolist() == c["ranks"][r]["recv_splits"]
+            # sender: row of the q-th token of expert e is send_base[e, dst] + q - cum_before
+            lists = O.expert_token_lists(np.array(c["expert_ids"][r]), E)
+            send_rows = np.full(int(S[r].sum()), -1)
+            for e in range(E):
+                for q, tok in enumerate(lists[e]):
+                    dst = int(np.searchsorted(lay.cum_split[e], q, side="right"))
+                    before = lay.cum_split[e, dst - 1] if dst > 0 else 0
+                    send_rows[lay.send_base[e, dst] + q - before] = tok
+            assert send_rows.tolist() == c["ranks"][r]["send_tokens"]
+            # receiver: expert-major groups; group g rows = recv positions of expert_mask[e]
+            recv = O.recv_expert_lists(S, r)
+            src_start = np.concatenate([[0], np.cumsum(lay.recv_splits)])
+            for gi, e in enumerate(lay.group_expert):
+                rows = []
+                for src in range(G):
+                    n = int(S[src, e, r])
+                    if n:
+                        # position in the reference's src-major receive buffer of chunk (src, e)
+                        pos0 = src_start[src] + int(S[src, :e, r].sum())
+                        rows.extend(range(pos0, pos0 + n))
+                        assert lay.recv_off[src, e] == lay.group_offsets[gi] + len(rows) - n
+                assert rows == recv[e].tolist()
+                assert lay.group_offsets[gi + 1] - lay.group_offsets[gi] == len(rows)
