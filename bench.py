@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--eq-tokens", type=int, default=150)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--once", action="store_true",
+                    help="one untimed forward of the workload and exit (the case profiled under ncu)")
     return ap.parse_args()
 
 
@@ -258,6 +260,13 @@ def main():
         group = dist.group.WORLD
     eng, x, Wr, raw, info = build_block(w, T, rank, world, dev, args.eq_tokens, group)
     peaks = load_peaks()
+    if args.once:
+        eng.forward(x)
+        torch.cuda.synchronize()
+        eng.check()
+        if world > 1:
+            dist.destroy_process_group()
+        return
 
     def barrier():
         if world > 1:
