@@ -62,7 +62,9 @@ class CombineArgs(ctypes.Structure):
 # every symbol include/dsca_b200.h declares
 EXPORTED = ["dsca_version", "dsca_status_string", "dsca_device_info", "dsca_router_topk",
             "dsca_dispatch_scan", "dsca_permute", "dsca_grouped_ffn", "dsca_combine",
-            "dsca_plan_harmony", "dsca_plan_layout", "dsca_check_error", "dsca_exp_neg_eval"]
+            "dsca_plan_harmony", "dsca_plan_layout", "dsca_check_error", "dsca_exp_neg_eval",
+            "dsca_grouped_ffn_static_scratch"]
+STATIC_SCRATCH_BYTES = 16 << 20
 
 _LIB = None
 
@@ -91,6 +93,7 @@ def load():
     lib.dsca_dispatch_scan.argtypes = [p(ScanArgs), _vp]
     lib.dsca_permute.argtypes = [p(PermuteArgs), _vp]
     lib.dsca_grouped_ffn.argtypes = [p(FfnArgs), _vp]
+    lib.dsca_grouped_ffn_static_scratch.argtypes = [p(FfnArgs), _vp]
     lib.dsca_combine.argtypes = [p(CombineArgs), _vp]
     lib.dsca_plan_harmony.argtypes = [_vp, _i, _i, _vp, _i, _vp]
     lib.dsca_plan_layout.argtypes = [_vp, _i, _i, _i, p(_i), _vp, _vp, _vp, _vp, _vp, _vp, _vp]
