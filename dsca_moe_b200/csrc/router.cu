@@ -6,122 +6,34 @@
 // topk / renorm / cast of ShardedQwenMoE.forward (qwen_ep_adapter/qwen_ep.py:48-53) and the
 // shared-expert gate sigmoid (qwen_ep.py:94) for the Qwen block.
 //
-// Layout: one CTA = 8 warps = 32 tokens (DSCA_ROUTER_TOKENS).  Warp w owns tokens 4w..4w+3;
-// lane L owns router rows L and L+32 (E + shared gate <= 64).  x and W stream through shared
-// memory in 64-wide slices of d (converted to fp32, W rows padded to 68 floats so the float4
-// reads of 8 consecutive lanes hit distinct banks); the next slice is fetched into registers
-// while the current one is consumed.  Each logit is one thread's sequential fma chain over
-// i = 0..d-1, so the value is fixed by the data alone.  Softmax and selection then run inside
-// the warp that already holds the token's logits (no shared-memory round trip).
+// Fixed arithmetic order of a logit (the C oracle follows it bit for bit):
+//   C = 32 * ceil(d / 128); chunk q covers i in [qC, min(d, (q+1)C)) (at most 4 chunks);
+//   S_q = fma chain over the chunk in increasing i from 0.0f; logit = ((S_0 + S_1) + S_2) + S_3,
+//   rounded to the router dtype.
+//
+// Layout: one CTA = 32 tokens (DSCA_ROUTER_TOKENS) x 64 router rows (E experts, then the shared
+// gate row, then zeros), 512 threads = 4 chunk groups of 128.  In group q, thread g owns tokens
+// 4*(g/16)..+3 and rows 4*(g%16)..+3: a 4 x 4 register tile fed by two 16-byte shared-memory
+// loads per k (x and W staged k-major in fp32).  Each group streams its chunk in 32-wide k
+// slices, fetching the next slice into registers while it computes the current one, and syncs
+// on its own named barrier.  The chunk partials meet in shared memory; softmax and selection
+// then run one warp per token.
 #include "common.cuh"
 
 namespace dsca {
 namespace router {
 
 constexpr int kTokens = DSCA_ROUTER_TOKENS;  // 32
-constexpr int kThreads = 256;
-constexpr int kRows = 64;                   // router rows per CTA (E experts + shared gate)
-constexpr int kDK = 64;                     // d slice
-constexpr int kXPitch = kDK + 4;
-constexpr int kWPitch = kDK + 4;
-
-template <typename T>
-struct Loader;
-
-template <>
-struct Loader<__nv_bfloat16> {
-  // x slice: 32 tokens x 64 values = 256 x 8 bf16 (one uint4 per thread)
-  // W slice: 64 rows x 64 values = 512 x 8 bf16 (two uint4 per thread)
-  static constexpr int kXVec = 1, kWVec = 2;
-  uint4 xr[kXVec], wr[kWVec];
-  __device__ void fetch(const __nv_bfloat16* x, const __nv_bfloat16* W, int T, int d, int rows,
-                        int tok0, int k0) {
-    for (int v = 0; v < kXVec; ++v) {
-      int idx = threadIdx.x + v * kThreads;  // 0..255
-      int t = idx >> 3, c = (idx & 7) * 8;
-      int tok = tok0 + t, col = k0 + c;
-      xr[v] = make_uint4(0, 0, 0, 0);
-      if (tok < T && col < d) xr[v] = *reinterpret_cast<const uint4*>(x + (size_t)tok * d + col);
-    }
-    for (int v = 0; v < kWVec; ++v) {
-      int idx = threadIdx.x + v * kThreads;  // 0..511
-      int r = idx >> 3, c = (idx & 7) * 8;
-      int col = k0 + c;
-      wr[v] = make_uint4(0, 0, 0, 0);
-      if (r < rows && col < d) wr[v] = *reinterpret_cast<const uint4*>(W + (size_t)r * d + col);
-    }
-  }
-  __device__ void store(float* xs, float* ws) {
-    for (int v = 0; v < kXVec; ++v) {
-      int idx = threadIdx.x + v * kThreads;
-      int t = idx >> 3, c = (idx & 7) * 8;
-      const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&xr[v]);
-      float4 a = make_float4(__bfloat162float(h[0]), __bfloat162float(h[1]), __bfloat162float(h[2]),
-                             __bfloat162float(h[3]));
-      float4 b = make_float4(__bfloat162float(h[4]), __bfloat162float(h[5]), __bfloat162float(h[6]),
-                             __bfloat162float(h[7]));
-      *reinterpret_cast<float4*>(xs + t * kXPitch + c) = a;
-      *reinterpret_cast<float4*>(xs + t * kXPitch + c + 4) = b;
-    }
-    for (int v = 0; v < kWVec; ++v) {
-      int idx = threadIdx.x + v * kThreads;
-      int r = idx >> 3, c = (idx & 7) * 8;
-      const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&wr[v]);
-      float4 a = make_float4(__bfloat162float(h[0]), __bfloat162float(h[1]), __bfloat162float(h[2]),
-                             __bfloat162float(h[3]));
-      float4 b = make_float4(__bfloat162float(h[4]), __bfloat162float(h[5]), __bfloat162float(h[6]),
-                             __bfloat162float(h[7]));
-      *reinterpret_cast<float4*>(ws + r * kWPitch + c) = a;
-      *reinterpret_cast<float4*>(ws + r * kWPitch + c + 4) = b;
-    }
-  }
-};
-
-template <>
-struct Loader<float> {
-  // x slice: 32 x 64 floats = 512 float4 (two per thread); W: 64 x 64 = 1024 float4 (four)
-  static constexpr int kXVec = 2, kWVec = 4;
-  float4 xr[kXVec], wr[kWVec];
-  __device__ void fetch(const float* x, const float* W, int T, int d, int rows, int tok0, int k0) {
-    for (int v = 0; v < kXVec; ++v) {
-      int idx = threadIdx.x + v * kThreads;  // 0..511
-      int t = idx >> 4, c = (idx & 15) * 4;
-      int tok = tok0 + t, col = k0 + c;
-      xr[v] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (tok < T && col < d) xr[v] = *reinterpret_cast<const float4*>(x + (size_t)tok * d + col);
-    }
-    for (int v = 0; v < kWVec; ++v) {
-      int idx = threadIdx.x + v * kThreads;  // 0..1023
-      int r = idx >> 4, c = (idx & 15) * 4;
-      int col = k0 + c;
-      wr[v] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (r < rows && col < d) wr[v] = *reinterpret_cast<const float4*>(W + (size_t)r * d + col);
-    }
-  }
-  __device__ void store(float* xs, float* ws) {
-    for (int v = 0; v < kXVec; ++v) {
-      int idx = threadIdx.x + v * kThreads;
-      int t = idx >> 4, c = (idx & 15) * 4;
-      *reinterpret_cast<float4*>(xs + t * kXPitch + c) = xr[v];
-    }
-    for (int v = 0; v < kWVec; ++v) {
-      int idx = threadIdx.x + v * kThreads;
-      int r = idx >> 4, c = (idx & 15) * 4;
-      *reinterpret_cast<float4*>(ws + r * kWPitch + c) = wr[v];
-    }
-  }
-};
-
-template <typename T>
-__device__ __forceinline__ void store_logit(void* logits, size_t i, float v);
-template <>
-__device__ __forceinline__ void store_logit<__nv_bfloat16>(void* logits, size_t i, float v) {
-  reinterpret_cast<__nv_bfloat16*>(logits)[i] = __float2bfloat16_rn(v);
-}
-template <>
-__device__ __forceinline__ void store_logit<float>(void* logits, size_t i, float v) {
-  reinterpret_cast<float*>(logits)[i] = v;
-}
+constexpr int kRows = 64;                    // router rows (E + shared gate <= 64)
+constexpr int kGroups = 4;
+constexpr int kGroupThreads = 128;
+constexpr int kThreads = kGroups * kGroupThreads;  // 512
+constexpr int kKS = 32;                      // k slice
+constexpr int kXP = kTokens + 4;             // x_s row pitch (floats): [k][token]
+constexpr int kWP = kRows + 4;               // w_s row pitch (floats): [k][row]
+constexpr int kStageFloats = kKS * kXP + kKS * kWP;
+constexpr int kLP = kRows + 1;               // logit tile pitch
+constexpr size_t kSmemBytes = sizeof(float) * (size_t)(kGroups * kStageFloats);
 
 struct Args {
   const void* x;
@@ -137,113 +49,207 @@ struct Args {
   int32_t* local_rank;
 };
 
+__device__ __forceinline__ void group_sync(int q) {
+  asm volatile("bar.sync %0, %1;" ::"r"(q + 1), "r"(kGroupThreads) : "memory");
+}
+
+// Row pointer of router row r (router weight, shared-gate row, or nothing).
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 2) router_kernel(Args a) {
-  __shared__ __align__(16) float xs[kTokens * kXPitch];
-  __shared__ __align__(16) float ws[kRows * kWPitch];
+__device__ __forceinline__ const T* wrow(const Args& a, int r) {
+  if (r < a.E) return reinterpret_cast<const T*>(a.w_router) + (size_t)r * a.d;
+  if (r == a.E && a.w_shared_gate != nullptr) return reinterpret_cast<const T*>(a.w_shared_gate);
+  return nullptr;
+}
+
+// Per-thread staging registers for one 32-wide k slice of the group's chunk.
+template <typename T>
+struct Slice;
+
+template <>
+struct Slice<__nv_bfloat16> {
+  // x: 32 tokens x 32 k = 128 x uint4 (1 per thread); W: 64 rows x 32 k = 256 x uint4 (2)
+  uint4 xv, wv[2];
+  __device__ void fetch(const Args& a, int g, int tok0, int k0, int kend) {
+    const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(a.x);
+    {
+      int t = g >> 2, c = (g & 3) * 8;
+      xv = make_uint4(0, 0, 0, 0);
+      if (tok0 + t < a.T && k0 + c < kend) xv = *reinterpret_cast<const uint4*>(x + (size_t)(tok0 + t) * a.d + k0 + c);
+    }
+#pragma unroll
+    for (int v = 0; v < 2; ++v) {
+      int idx = g + v * kGroupThreads;
+      int r = idx >> 2, c = (idx & 3) * 8;
+      const __nv_bfloat16* w = wrow<__nv_bfloat16>(a, r);
+      wv[v] = make_uint4(0, 0, 0, 0);
+      if (w != nullptr && k0 + c < kend) wv[v] = *reinterpret_cast<const uint4*>(w + k0 + c);
+    }
+  }
+  __device__ void store(float* xs, float* ws, int g) const {
+    {
+      int t = g >> 2, c = (g & 3) * 8;
+      const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&xv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) xs[(c + j) * kXP + t] = __bfloat162float(h[j]);
+    }
+#pragma unroll
+    for (int v = 0; v < 2; ++v) {
+      int idx = g + v * kGroupThreads;
+      int r = idx >> 2, c = (idx & 3) * 8;
+      const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&wv[v]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ws[(c + j) * kWP + r] = __bfloat162float(h[j]);
+    }
+  }
+};
+
+template <>
+struct Slice<float> {
+  // x: 32 x 32 floats = 256 float4 (2 per thread); W: 64 x 32 = 512 float4 (4)
+  float4 xv[2], wv[4];
+  __device__ void fetch(const Args& a, int g, int tok0, int k0, int kend) {
+    const float* x = reinterpret_cast<const float*>(a.x);
+#pragma unroll
+    for (int v = 0; v < 2; ++v) {
+      int idx = g + v * kGroupThreads;
+      int t = idx >> 3, c = (idx & 7) * 4;
+      xv[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (tok0 + t < a.T && k0 + c < kend) xv[v] = *reinterpret_cast<const float4*>(x + (size_t)(tok0 + t) * a.d + k0 + c);
+    }
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      int idx = g + v * kGroupThreads;
+      int r = idx >> 3, c = (idx & 7) * 4;
+      const float* w = wrow<float>(a, r);
+      wv[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (w != nullptr && k0 + c < kend) wv[v] = *reinterpret_cast<const float4*>(w + k0 + c);
+    }
+  }
+  __device__ void store(float* xs, float* ws, int g) const {
+#pragma unroll
+    for (int v = 0; v < 2; ++v) {
+      int idx = g + v * kGroupThreads;
+      int t = idx >> 3, c = (idx & 7) * 4;
+      xs[(c + 0) * kXP + t] = xv[v].x;
+      xs[(c + 1) * kXP + t] = xv[v].y;
+      xs[(c + 2) * kXP + t] = xv[v].z;
+      xs[(c + 3) * kXP + t] = xv[v].w;
+    }
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      int idx = g + v * kGroupThreads;
+      int r = idx >> 3, c = (idx & 7) * 4;
+      ws[(c + 0) * kWP + r] = wv[v].x;
+      ws[(c + 1) * kWP + r] = wv[v].y;
+      ws[(c + 2) * kWP + r] = wv[v].z;
+      ws[(c + 3) * kWP + r] = wv[v].w;
+    }
+  }
+};
+
+template <typename T>
+__device__ __forceinline__ void store_logit(void* logits, size_t i, float v);
+template <>
+__device__ __forceinline__ void store_logit<__nv_bfloat16>(void* logits, size_t i, float v) {
+  reinterpret_cast<__nv_bfloat16*>(logits)[i] = __float2bfloat16_rn(v);
+}
+template <>
+__device__ __forceinline__ void store_logit<float>(void* logits, size_t i, float v) {
+  reinterpret_cast<float*>(logits)[i] = v;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1) router_kernel(Args a) {
+  extern __shared__ __align__(16) float smem[];
+  __shared__ float lg_s[kTokens * kLP];
   __shared__ int ids_s[kTokens][DSCA_MAX_TOPK];
 
-  const int warp = warp_id(), lane = lane_id();
+  const int tid = threadIdx.x;
+  const int q = tid / kGroupThreads;  // chunk group
+  const int g = tid % kGroupThreads;
   const int tok0 = blockIdx.x * kTokens;
   const int E = a.E;
   const bool has_sg = a.w_shared_gate != nullptr;
-  const T* x = reinterpret_cast<const T*>(a.x);
-  const T* Wr = reinterpret_cast<const T*>(a.w_router);
-  const T* Wg = reinterpret_cast<const T*>(a.w_shared_gate);
+  const bool tau_bf16 = sizeof(T) == 2;
 
-  // rows 0..E-1 = router, row E = shared gate.  Build a virtual [rows, d] view: the loader
-  // reads row r < E from Wr and row E from Wg.
-  float acc[4][2];
+  // ---------------- chunk partial sums: 4 x 4 tile per thread
+  const int C = 32 * ((a.d + 127) / 128);
+  const int nq = (a.d + C - 1) / C;
+  const int kbeg = q * C, kend = min(a.d, kbeg + C);
+  const int tq = g >> 4, rq = g & 15;
+  float acc[4][4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = 0.0f;
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
 
-  Loader<T> ld;
-  auto fetch = [&](int k0) {
-    ld.fetch(x, Wr, a.T, a.d, E, tok0, k0);
-    if (has_sg) {
-      // the shared-gate row replaces row E of the W slice (loader zero-filled it)
-      constexpr int per_row = kDK / (16 / (int)sizeof(T));  // vectors per 64-wide row
-      for (int v = 0; v < Loader<T>::kWVec; ++v) {
-        int idx = threadIdx.x + v * kThreads;
-        int r = idx / per_row, c = (idx % per_row) * (16 / (int)sizeof(T));
-        if (r == E && k0 + c < a.d) {
-          if constexpr (sizeof(T) == 2)
-            ld.wr[v] = *reinterpret_cast<const uint4*>(Wg + k0 + c);
-          else
-            ld.wr[v] = *reinterpret_cast<const float4*>(Wg + k0 + c);
-        }
-      }
-    }
-  };
-
-  const int nslices = (a.d + kDK - 1) / kDK;
-  fetch(0);
-  for (int s = 0; s < nslices; ++s) {
-    __syncthreads();  // previous slice fully consumed
-    ld.store(xs, ws);
-    __syncthreads();
-    if (s + 1 < nslices) fetch((s + 1) * kDK);
-    const int kmax = min(kDK, a.d - s * kDK);
-    const float* w0 = ws + lane * kWPitch;
-    const float* w1 = ws + (lane + 32) * kWPitch;
-    const float* xw = xs + (warp * 4) * kXPitch;
-    int k = 0;
-    for (; k + 4 <= kmax; k += 4) {
-      float4 wa = *reinterpret_cast<const float4*>(w0 + k);
-      float4 wb = *reinterpret_cast<const float4*>(w1 + k);
+  float* xs = smem + q * kStageFloats;
+  float* ws = xs + kKS * kXP;
+  if (q < nq) {
+    Slice<T> sl;
+    sl.fetch(a, g, tok0, kbeg, kend);
+    for (int k0 = kbeg; k0 < kend; k0 += kKS) {
+      group_sync(q);  // the previous slice is consumed
+      sl.store(xs, ws, g);
+      group_sync(q);
+      if (k0 + kKS < kend) sl.fetch(a, g, tok0, k0 + kKS, kend);
+      const int kmax = min(kKS, kend - k0);
+      for (int k = 0; k < kmax; ++k) {
+        const float4 xv = *reinterpret_cast<const float4*>(xs + k * kXP + 4 * tq);
+        const float4 wv = *reinterpret_cast<const float4*>(ws + k * kWP + 4 * rq);
+        const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
+        const float wa[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float4 xv = *reinterpret_cast<const float4*>(xw + i * kXPitch + k);
-        acc[i][0] = __fmaf_rn(xv.x, wa.x, acc[i][0]);
-        acc[i][0] = __fmaf_rn(xv.y, wa.y, acc[i][0]);
-        acc[i][0] = __fmaf_rn(xv.z, wa.z, acc[i][0]);
-        acc[i][0] = __fmaf_rn(xv.w, wa.w, acc[i][0]);
-        acc[i][1] = __fmaf_rn(xv.x, wb.x, acc[i][1]);
-        acc[i][1] = __fmaf_rn(xv.y, wb.y, acc[i][1]);
-        acc[i][1] = __fmaf_rn(xv.z, wb.z, acc[i][1]);
-        acc[i][1] = __fmaf_rn(xv.w, wb.w, acc[i][1]);
-      }
-    }
-    for (; k < kmax; ++k) {
+        for (int i = 0; i < 4; ++i)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        acc[i][0] = __fmaf_rn(xw[i * kXPitch + k], w0[k], acc[i][0]);
-        acc[i][1] = __fmaf_rn(xw[i * kXPitch + k], w1[k], acc[i][1]);
+          for (int j = 0; j < 4; ++j) acc[i][j] = __fmaf_rn(xa[i], wa[j], acc[i][j]);
       }
     }
   }
-
-  const bool tau_bf16 = sizeof(T) == 2;
-  const int e0 = lane, e1 = lane + 32;
+  __syncthreads();  // staging buffers are reused for the partials below
+  float* part = smem;  // [nq][32 tokens][64 rows]
+  if (q < nq) {
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int tl = warp * 4 + i;
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) part[(q * kTokens + 4 * tq + i) * kRows + 4 * rq + j] = acc[i][j];
+  }
+  __syncthreads();
+  for (int idx = tid; idx < kTokens * kRows; idx += kThreads) {
+    const int t = idx / kRows, r = idx % kRows;
+    float tot = part[t * kRows + r];
+    for (int qq = 1; qq < nq; ++qq) tot = __fadd_rn(tot, part[(qq * kTokens + t) * kRows + r]);
+    lg_s[t * kLP + r] = tau_bf16 ? round_bf16(tot) : tot;
+  }
+  __syncthreads();
+
+  // ---------------- softmax and selection: one warp per token
+  const int warp = tid >> 5, lane = tid & 31;
+  const int e0 = lane, e1 = lane + 32;
+  for (int tl = warp; tl < kTokens; tl += kThreads / 32) {
     const int t = tok0 + tl;
-    float l0 = tau_bf16 ? round_bf16(acc[i][0]) : acc[i][0];
-    float l1 = tau_bf16 ? round_bf16(acc[i][1]) : acc[i][1];
     const bool valid = t < a.T;
+    const float l0 = lg_s[tl * kLP + e0];
+    const float l1 = lg_s[tl * kLP + e1];
     if (valid) {
       if (e0 < E) store_logit<T>(a.logits, (size_t)t * E + e0, l0);
       if (e1 < E) store_logit<T>(a.logits, (size_t)t * E + e1, l1);
-      if (has_sg && a.shared_gate != nullptr) {
-        float z = (e0 == E) ? l0 : l1;
-        if (e0 == E || e1 == E) a.shared_gate[t] = 1.0f / (1.0f + expf(-z));
+      if (has_sg && a.shared_gate != nullptr && (e0 == E || e1 == E)) {
+        const float z = (e0 == E) ? l0 : l1;
+        a.shared_gate[t] = 1.0f / (1.0f + expf(-z));
       }
     }
-    // softmax over the E router logits of this token
-    float v0 = (e0 < E) ? l0 : -INFINITY;
-    float v1 = (e1 < E) ? l1 : -INFINITY;
-    float m = fmaxf(v0, v1);
+    float m = fmaxf((e0 < E) ? l0 : -INFINITY, (e1 < E) ? l1 : -INFINITY);
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-    float x0 = (e0 < E) ? exp_neg(__fsub_rn(l0, m)) : 0.0f;
-    float x1 = (e1 < E) ? exp_neg(__fsub_rn(l1, m)) : 0.0f;
-    float part = (e0 < E) ? __fadd_rn(0.0f, x0) : 0.0f;
-    if (e1 < E) part = __fadd_rn(part, x1);
+    const float x0 = (e0 < E) ? exp_neg(__fsub_rn(l0, m)) : 0.0f;
+    const float x1 = (e1 < E) ? exp_neg(__fsub_rn(l1, m)) : 0.0f;
+    float ps = (e0 < E) ? __fadd_rn(0.0f, x0) : 0.0f;
+    if (e1 < E) ps = __fadd_rn(ps, x1);
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, off));
-    float p0 = (e0 < E) ? __fdiv_rn(x0, part) : -INFINITY;
-    float p1 = (e1 < E) ? __fdiv_rn(x1, part) : -INFINITY;
+    for (int off = 16; off >= 1; off >>= 1) ps = __fadd_rn(ps, __shfl_xor_sync(0xffffffffu, ps, off));
+    float p0 = (e0 < E) ? __fdiv_rn(x0, ps) : -INFINITY;
+    float p1 = (e1 < E) ? __fdiv_rn(x1, ps) : -INFINITY;
 
     if (a.mode == DSCA_ROUTE_SWITCH_TOP1) {
       if (tau_bf16) {
@@ -255,15 +261,15 @@ __global__ void __launch_bounds__(kThreads, 2) router_kernel(Args a) {
       if (p1 > bv) { bv = p1; bi = e1; }
 #pragma unroll
       for (int off = 16; off >= 1; off >>= 1) {
-        float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-        int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
         if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
       }
       if (lane == 0) {
         ids_s[tl][0] = valid ? bi : -1;
         if (valid) {
           a.topk_ids[t] = bi;
-          a.topk_w[t] = (a.weight_round_bf16 && !tau_bf16) ? round_bf16(bv) : bv;
+          a.topk_w[t] = bv;
           if (a.expert_index != nullptr) a.expert_index[t] = bi;
         }
       }
@@ -278,8 +284,8 @@ __global__ void __launch_bounds__(kThreads, 2) router_kernel(Args a) {
         if (!taken1 && (p1 > bv || bi == (1 << 30))) { bv = p1; bi = e1; }
 #pragma unroll
         for (int off = 16; off >= 1; off >>= 1) {
-          float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-          int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+          const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
           if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
         }
         if (bi == e0) taken0 = true;
@@ -306,18 +312,18 @@ __global__ void __launch_bounds__(kThreads, 2) router_kernel(Args a) {
   }
   __syncthreads();
 
-  // per-block histogram and stable in-block ranks (token order, slot order)
+  // ---------------- per-block histogram and stable in-block ranks (token, then slot order)
   const int k = (a.mode == DSCA_ROUTE_SWITCH_TOP1) ? 1 : a.top_k;
-  for (int e = threadIdx.x; e < E; e += kThreads) {
+  for (int e = tid; e < E; e += kThreads) {
     int c = 0;
     for (int tl = 0; tl < kTokens; ++tl)
       for (int j = 0; j < k; ++j) c += (ids_s[tl][j] == e);
     a.block_hist[(size_t)blockIdx.x * E + e] = c;
   }
-  for (int idx = threadIdx.x; idx < kTokens * k; idx += kThreads) {
-    int tl = idx / k, j = idx % k;
-    int t = tok0 + tl;
-    int e = ids_s[tl][j];
+  for (int idx = tid; idx < kTokens * k; idx += kThreads) {
+    const int tl = idx / k, j = idx % k;
+    const int t = tok0 + tl;
+    const int e = ids_s[tl][j];
     if (t >= a.T || e < 0) continue;
     int r = 0;
     for (int u = 0; u < tl; ++u)
@@ -329,6 +335,7 @@ __global__ void __launch_bounds__(kThreads, 2) router_kernel(Args a) {
 }  // namespace router
 
 int launch_router(const dsca_router_args* p, cudaStream_t stream) {
+  static bool attr_done[2] = {false, false};
   router::Args a;
   a.x = p->x;
   a.w_router = p->w_router;
@@ -348,10 +355,24 @@ int launch_router(const dsca_router_args* p, cudaStream_t stream) {
   a.block_hist = p->block_hist;
   a.local_rank = p->local_rank;
   const int nblocks = (p->T + router::kTokens - 1) / router::kTokens;
-  if (p->dtype == DSCA_BF16)
-    router::router_kernel<__nv_bfloat16><<<nblocks, router::kThreads, 0, stream>>>(a);
-  else
-    router::router_kernel<float><<<nblocks, router::kThreads, 0, stream>>>(a);
+  cudaError_t e = cudaSuccess;
+  if (p->dtype == DSCA_BF16) {
+    if (!attr_done[0]) {
+      e = cudaFuncSetAttribute(router::router_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)router::kSmemBytes);
+      attr_done[0] = e == cudaSuccess;
+    }
+    if (e == cudaSuccess)
+      router::router_kernel<__nv_bfloat16><<<nblocks, router::kThreads, router::kSmemBytes, stream>>>(a);
+  } else {
+    if (!attr_done[1]) {
+      e = cudaFuncSetAttribute(router::router_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)router::kSmemBytes);
+      attr_done[1] = e == cudaSuccess;
+    }
+    if (e == cudaSuccess) router::router_kernel<float><<<nblocks, router::kThreads, router::kSmemBytes, stream>>>(a);
+  }
+  if (e != cudaSuccess) return DSCA_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
 }
 

@@ -20,7 +20,9 @@
  *     w      = w.to(activation dtype)
  *
  * Fixed order used here and in the kernel (the reference leaves it to cuBLAS/ATen):
- *   logit[t,e] = round_tau( fma-accumulate over i = 0..d-1 of x[t,i] * W[e,i], from 0.0f )
+ *   C          = 32 * ceil(d / 128)   (d splits into at most 4 chunks of C)
+ *   S_q        = fma-accumulate over i in [qC, min(d, (q+1)C)) of x[t,i] * W[e,i], from 0.0f
+ *   logit[t,e] = round_tau( ((S_0 + S_1) + S_2) + S_3 )
  *   m          = max_e logit[t,e]
  *   ex[e]      = dsca_exp(logit[t,e] - m)
  *   s          = 32 lane partials (lane L sums e = L, L+32, L+64 ... in that order) combined by
@@ -75,15 +77,28 @@ float oracle_exp_neg(float x) {
     return p * scale;
 }
 
-/* logits[T,E] = round_tau(x[T,d] . W[E,d]^T); round_bf16 selects tau = bf16, else fp32 */
+/* Chunk length of the logit sum: C = 32 * ceil(d / 128), so d splits into at most 4 chunks. */
+int oracle_router_chunk(int d) { return 32 * ((d + 127) / 128); }
+
+/*
+ * logits[T,E] = round_tau(x[T,d] . W[E,d]^T); round_bf16 selects tau = bf16, else fp32.
+ * Order: chunk q covers i in [qC, min(d, (q+1)C)); its partial S_q is the fma chain over i in
+ * increasing order from 0.0f; the logit is ((S_0 + S_1) + S_2) + S_3.
+ */
 void oracle_router_logits(const float* x, const float* W, int T, int d, int E, int round_bf16,
                           float* logits) {
+    const int C = oracle_router_chunk(d);
     for (int t = 0; t < T; ++t) {
         const float* xr = x + (size_t)t * d;
         for (int e = 0; e < E; ++e) {
             const float* wr = W + (size_t)e * d;
             float acc = 0.0f;
-            for (int i = 0; i < d; ++i) acc = fmaf(xr[i], wr[i], acc);
+            for (int q = 0; q * C < d; ++q) {
+                const int i1 = (q + 1) * C < d ? (q + 1) * C : d;
+                float s = 0.0f;
+                for (int i = q * C; i < i1; ++i) s = fmaf(xr[i], wr[i], s);
+                acc = (q == 0) ? s : acc + s;
+            }
             logits[(size_t)t * E + e] = round_bf16 ? oracle_round_bf16(acc) : acc;
         }
     }

@@ -31,3 +31,26 @@ def qwen_weights(z, m):
 def json_fixture(name):
     with open(os.path.join(GOLDEN, name)) as f:
         return json.load(f)
+
+
+def assert_logits_close(ours, ref, tau):
+    """Logits from the fixed chunked order vs the reference's own accumulation order: f32 within
+    a few ulps; bf16 equal or one bf16 ulp apart on under 1 % of the entries."""
+    ours = np.asarray(ours, np.float32)
+    ref = np.asarray(ref, np.float32)
+    if tau == "f32":
+        assert np.all(np.abs(ours - ref) <= 4e-6 * np.maximum(np.abs(ref), 1.0))
+    else:
+        a = ours.view(np.int32).astype(np.int64)
+        b = ref.view(np.int32).astype(np.int64)
+        diff = np.abs(a - b) >> 16
+        assert diff.max() <= 1
+        assert (diff > 0).mean() < 0.01
+
+
+def routing_near_ties(logits, k, tau="bf16"):
+    """Tokens whose k-th and (k+1)-th probabilities are within 2^-7 (bf16 logits: one logit ulp)
+    or 1e-5 (f32 logits: a few ulps) of each other: another valid summation order can swap them."""
+    from oracle import oracle as O
+
+    return O.near_tie_tokens(logits, k, tau, rel=2.0 ** -7 if tau == "bf16" else 1e-5)
