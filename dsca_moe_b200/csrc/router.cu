@@ -29,11 +29,11 @@ constexpr int kGroups = 4;
 constexpr int kGroupThreads = 128;
 constexpr int kThreads = kGroups * kGroupThreads;  // 512
 constexpr int kKS = 32;                      // k slice
-constexpr int kXP = kTokens + 4;             // x_s row pitch (floats): [k][token]
-constexpr int kWP = kRows + 4;               // w_s row pitch (floats): [k][row]
-constexpr int kStageFloats = kKS * kXP + kKS * kWP;
+constexpr int kP = kKS + 4;                  // staging row pitch (floats): x_s[token][k], w_s[row][k]
+constexpr int kStageFloats = kTokens * kP + kRows * kP;
 constexpr int kLP = kRows + 1;               // logit tile pitch
-constexpr size_t kSmemBytes = sizeof(float) * (size_t)(kGroups * kStageFloats);
+// two staging buffers per chunk group
+constexpr size_t kSmemBytes = sizeof(float) * (size_t)(kGroups * 2 * kStageFloats);
 
 struct Args {
   const void* x;
@@ -85,20 +85,19 @@ struct Slice<__nv_bfloat16> {
       if (w != nullptr && k0 + c < kend) wv[v] = *reinterpret_cast<const uint4*>(w + k0 + c);
     }
   }
+  static __device__ void put8(float* dst, const uint4& u) {
+    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
+    *reinterpret_cast<float4*>(dst) = make_float4(__bfloat162float(h[0]), __bfloat162float(h[1]),
+                                                  __bfloat162float(h[2]), __bfloat162float(h[3]));
+    *reinterpret_cast<float4*>(dst + 4) = make_float4(__bfloat162float(h[4]), __bfloat162float(h[5]),
+                                                      __bfloat162float(h[6]), __bfloat162float(h[7]));
+  }
   __device__ void store(float* xs, float* ws, int g) const {
-    {
-      int t = g >> 2, c = (g & 3) * 8;
-      const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&xv);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) xs[(c + j) * kXP + t] = __bfloat162float(h[j]);
-    }
+    put8(xs + (g >> 2) * kP + (g & 3) * 8, xv);
 #pragma unroll
     for (int v = 0; v < 2; ++v) {
       int idx = g + v * kGroupThreads;
-      int r = idx >> 2, c = (idx & 3) * 8;
-      const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&wv[v]);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) ws[(c + j) * kWP + r] = __bfloat162float(h[j]);
+      put8(ws + (idx >> 2) * kP + (idx & 3) * 8, wv[v]);
     }
   }
 };
@@ -129,20 +128,12 @@ struct Slice<float> {
 #pragma unroll
     for (int v = 0; v < 2; ++v) {
       int idx = g + v * kGroupThreads;
-      int t = idx >> 3, c = (idx & 7) * 4;
-      xs[(c + 0) * kXP + t] = xv[v].x;
-      xs[(c + 1) * kXP + t] = xv[v].y;
-      xs[(c + 2) * kXP + t] = xv[v].z;
-      xs[(c + 3) * kXP + t] = xv[v].w;
+      *reinterpret_cast<float4*>(xs + (idx >> 3) * kP + (idx & 7) * 4) = xv[v];
     }
 #pragma unroll
     for (int v = 0; v < 4; ++v) {
       int idx = g + v * kGroupThreads;
-      int r = idx >> 3, c = (idx & 7) * 4;
-      ws[(c + 0) * kWP + r] = wv[v].x;
-      ws[(c + 1) * kWP + r] = wv[v].y;
-      ws[(c + 2) * kWP + r] = wv[v].z;
-      ws[(c + 3) * kWP + r] = wv[v].w;
+      *reinterpret_cast<float4*>(ws + (idx >> 3) * kP + (idx & 7) * 4) = wv[v];
     }
   }
 };
@@ -183,27 +174,44 @@ __global__ void __launch_bounds__(kThreads, 1) router_kernel(Args a) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
 
-  float* xs = smem + q * kStageFloats;
-  float* ws = xs + kKS * kXP;
+  // thread tile: tokens 4*tq + i, rows rq + 16*j (strided rows keep the float4 reads of the 16
+  // row lanes of a warp on distinct banks)
+  float* stage0 = smem + q * 2 * kStageFloats;
   if (q < nq) {
     Slice<T> sl;
     sl.fetch(a, g, tok0, kbeg, kend);
-    for (int k0 = kbeg; k0 < kend; k0 += kKS) {
-      group_sync(q);  // the previous slice is consumed
-      sl.store(xs, ws, g);
-      group_sync(q);
-      if (k0 + kKS < kend) sl.fetch(a, g, tok0, k0 + kKS, kend);
-      const int kmax = min(kKS, kend - k0);
-      for (int k = 0; k < kmax; ++k) {
-        const float4 xv = *reinterpret_cast<const float4*>(xs + k * kXP + 4 * tq);
-        const float4 wv = *reinterpret_cast<const float4*>(ws + k * kWP + 4 * rq);
-        const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
-        const float wa[4] = {wv.x, wv.y, wv.z, wv.w};
+    sl.store(stage0, stage0 + kTokens * kP, g);
+    group_sync(q);
+    int s = 0;
+    for (int k0 = kbeg; k0 < kend; k0 += kKS, s ^= 1) {
+      const bool more = k0 + kKS < kend;
+      if (more) sl.fetch(a, g, tok0, k0 + kKS, kend);  // in flight during the compute below
+      const float* xs = stage0 + s * kStageFloats;
+      const float* ws = xs + kTokens * kP;
+      const float* xb = xs + (4 * tq) * kP;
+      const float* wb = ws + rq * kP;
+      const int kmax = min(kKS, kend - k0);  // a multiple of 8
+      for (int k = 0; k < kmax; k += 4) {
+        float4 xv[4], wv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) xv[i] = *reinterpret_cast<const float4*>(xb + i * kP + k);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) wv[j] = *reinterpret_cast<const float4*>(wb + 16 * j * kP + k);
 #pragma unroll
         for (int i = 0; i < 4; ++i)
 #pragma unroll
-          for (int j = 0; j < 4; ++j) acc[i][j] = __fmaf_rn(xa[i], wa[j], acc[i][j]);
+          for (int j = 0; j < 4; ++j) {
+            acc[i][j] = __fmaf_rn(xv[i].x, wv[j].x, acc[i][j]);
+            acc[i][j] = __fmaf_rn(xv[i].y, wv[j].y, acc[i][j]);
+            acc[i][j] = __fmaf_rn(xv[i].z, wv[j].z, acc[i][j]);
+            acc[i][j] = __fmaf_rn(xv[i].w, wv[j].w, acc[i][j]);
+          }
       }
+      if (more) {
+        float* nx = stage0 + (s ^ 1) * kStageFloats;  // last read two slices ago
+        sl.store(nx, nx + kTokens * kP, g);
+      }
+      group_sync(q);
     }
   }
   __syncthreads();  // staging buffers are reused for the partials below
@@ -212,7 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1) router_kernel(Args a) {
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) part[(q * kTokens + 4 * tq + i) * kRows + 4 * rq + j] = acc[i][j];
+      for (int j = 0; j < 4; ++j) part[(q * kTokens + 4 * tq + i) * kRows + rq + 16 * j] = acc[i][j];
   }
   __syncthreads();
   for (int idx = tid; idx < kTokens * kRows; idx += kThreads) {

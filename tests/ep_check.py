@@ -1,0 +1,113 @@
+"""Expert-parallel parity check, one rank per GPU (run by tests/test_gpu_ep.py through torchrun):
+
+    torchrun --nproc-per-node G --master-addr 127.0.0.1 --master-port P tests/ep_check.py
+
+Each rank routes its own tokens, the harmony plan moves hot-expert tokens between GPUs, and the
+block's output on every rank must equal the single-GPU result of the same tokens: routing
+bit-exact, outputs within 2e-2 (they come out bit-identical when the plan does not matter to the
+row arithmetic, and the check reports that).  Covers the Qwen top-4 + shared block (even and
+uneven placements, harmony on and off) and the Switch top-1 block (whose multi-GPU output the
+reference leaves uncombined, src/harmonymoe/scheduler.py:158-175)."""
+import json
+import os
+import sys
+from datetime import timedelta
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+from dsca_moe_b200 import _lib as L  # noqa: E402
+from dsca_moe_b200 import synthetic as syn  # noqa: E402
+from dsca_moe_b200.engine import MoEEngine, pack_relu, pack_swiglu  # noqa: E402
+
+
+def rel(a, b):
+    a, b = a.float(), b.float()
+    return float((a - b).abs().max() / b.abs().max().clamp_min(1e-30))
+
+
+def case_qwen(rank, world, dev, group, e2g, eq_tokens, T=512):
+    d, E, I, Is = 1024, 60, 256, 512
+    Wg, _ = syn.router_weight(E, d, 71, zipf_s=1.5, dtype="bf16")
+    g = torch.Generator(device=dev)
+    g.manual_seed(72)
+
+    def n(*s):
+        return (torch.randn(*s, generator=g, device=dev) * 0.03).to(torch.bfloat16)
+
+    w = dict(gate=n(E, I, d), up=n(E, I, d), down=n(E, d, I), sg=n(Is, d), su=n(Is, d), sd=n(d, Is), g=n(d))
+    pe = pack_swiglu(w["gate"], w["up"], w["down"], shared=(w["sg"], w["su"], w["sd"]), device=dev)
+    Wt = torch.from_numpy(Wg).to(dev, torch.bfloat16)
+    ep = MoEEngine(Wt, pe, top_k=4, route_mode=L.ROUTE_SOFTMAX_TOPK, shared_gate_weight=w["g"], rank=rank,
+                   world=world, group=group, expert_to_gpu=e2g, eq_tokens=eq_tokens)
+    one = MoEEngine(Wt, pe, top_k=4, route_mode=L.ROUTE_SOFTMAX_TOPK, shared_gate_weight=w["g"])
+    x = torch.from_numpy(syn.hidden_states(T, d, 700 + rank, "bf16")).to(dev, torch.bfloat16)
+    return ep, one, x
+
+
+def case_switch(rank, world, dev, group, e2g, eq_tokens, T=640):
+    d, E, F = 768, 64, 1024
+    Wr, _ = syn.router_weight(E, d, 81, zipf_s=1.0, dtype="bf16")
+    g = torch.Generator(device=dev)
+    g.manual_seed(82)
+    wi = (torch.randn(E, F, d, generator=g, device=dev) * 0.03).to(torch.bfloat16)
+    wo = (torch.randn(E, d, F, generator=g, device=dev) * 0.03).to(torch.bfloat16)
+    pe = pack_relu(wi, wo, device=dev)
+    Wt = torch.from_numpy(Wr).to(dev, torch.bfloat16)
+    ep = MoEEngine(Wt, pe, top_k=1, route_mode=L.ROUTE_SWITCH_TOP1, rank=rank, world=world, group=group,
+                   expert_to_gpu=e2g, eq_tokens=eq_tokens)
+    one = MoEEngine(Wt, pe, top_k=1, route_mode=L.ROUTE_SWITCH_TOP1)
+    x = torch.from_numpy(syn.hidden_states(T, d, 800 + rank, "bf16")).to(dev, torch.bfloat16)
+    return ep, one, x
+
+
+def main():
+    world = int(os.environ["WORLD_SIZE"])
+    rank = int(os.environ["RANK"])
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", rank)))
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    group = dist.group.WORLD
+    results = []
+    uneven60 = np.array([min(world - 1, (e * world * world) // (60 * (world + 1))) for e in range(60)], np.int32)
+    cases = [
+        ("qwen contiguous, harmony", case_qwen, None, 150),
+        ("qwen contiguous, fixed", case_qwen, None, -1),
+        ("qwen uneven placement, harmony", case_qwen, uneven60, 150),
+        ("switch top-1, harmony", case_switch, None, 150),
+    ]
+    ok = True
+    for name, fn, e2g, eq in cases:
+        ep, one, x = fn(rank, world, dev, group, e2g, eq)
+        for it in range(2):
+            r_ep = ep.forward(x)
+            r_one = one.forward(x)
+            torch.cuda.synchronize()
+            ep.check()
+            one.check()
+            same_route = torch.equal(r_ep["topk_ids"], r_one["topk_ids"]) and torch.equal(r_ep["logits"], r_one["logits"])
+            err = rel(r_ep["out"], r_one["out"])
+            exact = torch.equal(r_ep["out"], r_one["out"])
+            S = ep.last_plan
+            migrated = int(S.sum() - sum(S[:, e, ep.expert_to_gpu[e]].sum() for e in range(S.shape[1])))
+            good = same_route and err < 2e-2 and torch.isfinite(r_ep["out"].float()).all().item()
+            ok &= bool(good)
+            results.append({"case": name, "iter": it, "rank": rank, "routing_equal": bool(same_route),
+                            "max_rel_err": err, "bit_identical": bool(exact), "tokens_migrated": migrated})
+    flag = torch.tensor([1 if ok else 0], device=dev)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    gathered = [None] * world
+    dist.all_gather_object(gathered, results)
+    if rank == 0:
+        print(json.dumps({"world": world, "ok": bool(flag.item()), "results": sum(gathered, [])}))
+    dist.barrier()
+    dist.destroy_process_group()
+    sys.exit(0 if flag.item() == 1 else 1)
+
+
+if __name__ == "__main__":
+    main()
