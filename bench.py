@@ -406,10 +406,8 @@ def main():
         rows = T * w["k"]
         counts = eng.forward(x)["counts"].cpu().numpy()
     else:
-        lay = eng.last_layout
-        rows = int(lay.group_offsets[-1]) if lay.num_groups else 0
-        counts = np.zeros(w["E"])
-        counts[lay.group_expert] = np.diff(lay.group_offsets)
+        S, rows = eng.read_plan()
+        counts = S[:, :, rank].sum(axis=0)
     e_touched = int((counts > 0).sum())
     f_router, f_g1, f_g2, hbm = flops_and_bytes(w, T, rows, e_touched)
     t_g1, t_g2 = phase_ms.get("gemm1", float("nan")), phase_ms.get("gemm2", float("nan"))
@@ -465,6 +463,7 @@ def main():
         }
         print(json.dumps(line), flush=True)
     if world > 1:
+        eng.close()
         dist.barrier()
         dist.destroy_process_group()
 

@@ -50,7 +50,22 @@ class FfnArgs(ctypes.Structure):
                 ("num_experts_w", _i), ("capacity", _i), ("a", _vp), ("w1", _vp), ("w2", _vp),
                 ("h", _vp), ("y", _vp), ("shared_rows", _i), ("shared_n1p", _i), ("shared_ip", _i),
                 ("xs", _vp), ("ws1", _vp), ("ws2", _vp), ("hs", _vp), ("ys", _vp), ("err", _vp),
-                ("num_ctas", _i), ("phases", _i)]
+                ("num_ctas", _i), ("phases", _i), ("ep_ctx", _vp)]
+
+
+MAX_GPUS = 8
+
+
+class EpSetup(ctypes.Structure):
+    _fields_ = [("G", _i), ("E", _i), ("me", _i), ("d", _i), ("elem_bytes", _i),
+                ("recv_capacity", _i), ("ret_capacity", _i), ("eq_tokens", _i), ("start_epoch", ctypes.c_uint),
+                ("expert_to_gpu", _vp), ("flags", _vp * MAX_GPUS), ("meta", _vp * MAX_GPUS),
+                ("recv", _vp * MAX_GPUS), ("ret", _vp * MAX_GPUS)]
+
+
+class EpDispatchArgs(ctypes.Structure):
+    _fields_ = [("x", _vp), ("T", _i), ("d", _i), ("top_k", _i), ("dtype", _i), ("topk_ids", _vp),
+                ("local_rank", _vp), ("block_base", _vp), ("ctx", _vp), ("token_row", _vp), ("err", _vp)]
 
 
 class CombineArgs(ctypes.Structure):
@@ -63,7 +78,10 @@ class CombineArgs(ctypes.Structure):
 EXPORTED = ["dsca_version", "dsca_status_string", "dsca_device_info", "dsca_router_topk",
             "dsca_dispatch_scan", "dsca_permute", "dsca_grouped_ffn", "dsca_combine",
             "dsca_plan_harmony", "dsca_plan_layout", "dsca_check_error", "dsca_exp_neg_eval",
-            "dsca_grouped_ffn_static_scratch"]
+            "dsca_grouped_ffn_static_scratch", "dsca_ep_ctx_bytes", "dsca_ep_init", "dsca_ep_group_offsets",
+            "dsca_ep_plan", "dsca_ep_dispatch", "dsca_ep_wait", "dsca_ep_plan_eval", "dsca_ipc_export",
+            "dsca_ipc_import", "dsca_ipc_close", "dsca_ep_read_plan", "dsca_ep_region_alloc",
+            "dsca_ep_region_free"]
 STATIC_SCRATCH_BYTES = 16 << 20
 
 _LIB = None
@@ -94,6 +112,22 @@ def load():
     lib.dsca_permute.argtypes = [p(PermuteArgs), _vp]
     lib.dsca_grouped_ffn.argtypes = [p(FfnArgs), _vp]
     lib.dsca_grouped_ffn_static_scratch.argtypes = [p(FfnArgs), _vp]
+    u64 = ctypes.c_uint64
+    lib.dsca_ep_ctx_bytes.restype = ctypes.c_size_t
+    lib.dsca_ep_ctx_bytes.argtypes = []
+    lib.dsca_ep_init.argtypes = [_vp, p(EpSetup), _vp]
+    lib.dsca_ep_group_offsets.restype = _vp
+    lib.dsca_ep_group_offsets.argtypes = [_vp]
+    lib.dsca_ep_plan.argtypes = [_vp, _vp, u64, _vp, _vp]
+    lib.dsca_ep_dispatch.argtypes = [p(EpDispatchArgs), _vp]
+    lib.dsca_ep_wait.argtypes = [_vp, _i, u64, _vp, _vp]
+    lib.dsca_ep_plan_eval.argtypes = [_vp, _i, _i, _vp, _i, _vp, _vp]
+    lib.dsca_ipc_export.argtypes = [_vp, _vp, p(ctypes.c_size_t)]
+    lib.dsca_ipc_import.argtypes = [_vp, ctypes.c_size_t, p(_vp)]
+    lib.dsca_ipc_close.argtypes = [_vp, ctypes.c_size_t]
+    lib.dsca_ep_read_plan.argtypes = [_vp, _vp, _vp, _vp]
+    lib.dsca_ep_region_alloc.argtypes = [ctypes.c_size_t, p(_vp)]
+    lib.dsca_ep_region_free.argtypes = [_vp]
     lib.dsca_combine.argtypes = [p(CombineArgs), _vp]
     lib.dsca_plan_harmony.argtypes = [_vp, _i, _i, _vp, _i, _vp]
     lib.dsca_plan_layout.argtypes = [_vp, _i, _i, _i, p(_i), _vp, _vp, _vp, _vp, _vp, _vp, _vp]

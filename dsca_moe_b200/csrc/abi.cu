@@ -146,7 +146,10 @@ int dsca_grouped_ffn(const dsca_ffn_args* f, dsca_stream_t stream) {
       if (!aligned16(p)) return DSCA_ERR_BAD_ARG;
     return dsca::launch_grouped_ffn_bf16(f, num_sms, st);
   }
-  if (f->dtype == DSCA_F32) return dsca::launch_grouped_ffn_f32(f, num_sms, st);
+  if (f->dtype == DSCA_F32) {
+    if (f->ep_ctx != nullptr) return DSCA_ERR_UNSUPPORTED;  // the fused return path is bf16 only
+    return dsca::launch_grouped_ffn_f32(f, num_sms, st);
+  }
   return DSCA_ERR_BAD_ARG;
 }
 

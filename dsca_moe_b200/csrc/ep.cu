@@ -1,0 +1,421 @@
+// Fused expert-parallel exchange over NVLink peer memory (one process per GPU, CUDA IPC).
+//
+//   plan kernel     counts of this rank -> every peer's meta table (P2P stores), epoch flag,
+//                   bounded wait for every peer's counts, then the harmony plan and the send /
+//                   receive tables computed on the device by one warp (the same integer algorithm
+//                   as dsca_plan_harmony, src/harmonymoe/scheduler.py:324-372, and
+//                   dsca_plan_layout, :101-124 / :185-213) — no host sync anywhere.
+//   dispatch kernel every routed (token, slot) row stored straight into the destination rank's
+//                   expert-major receive buffer (16-byte stores over NVLink); the last CTA sets
+//                   the dispatch flag at every peer.
+//   wait kernel     bounded wait for one flag kind from every peer.
+// The grouped GEMM's return epilogue (gemm_sm100.cu) stores expert outputs straight into the
+// source rank's return buffer and sets the return flag.  Peer memory is only ever the target of
+// plain stores or the source of plain loads: no TMA and no multicast touches it.
+#include <string.h>
+
+#include "ep.cuh"
+
+namespace dsca {
+namespace ep {
+
+// ------------------------------------------------------------------ harmony plan, one warp
+// S (shared) [G][E][G]; meta [G][E]; all lanes call it, control flow is warp-uniform.
+__device__ void harmony_warp(const int32_t* meta, int G, int E, const int32_t* e2g, int eq_tokens, int32_t* S,
+                             long long* amt) {
+  const int lane = threadIdx.x & 31;
+  for (int i = lane; i < G * E * G; i += 32) S[i] = 0;
+  __syncwarp();
+  long long part = 0;
+  for (int i = lane; i < G * E; i += 32) {
+    const int src = i / E, e = i % E;
+    S[(src * E + e) * G + e2g[e]] = meta[i];
+    part += meta[i];
+  }
+  for (int off = 16; off; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+  const long long total = part;
+  __syncwarp();
+  if (eq_tokens < 0) return;
+  const long long avg = total / G;
+  if (lane < G) {
+    long long a = 0;
+    for (int src = 0; src < G; ++src)
+      for (int e = 0; e < E; ++e) a += S[(src * E + e) * G + lane];
+    amt[lane] = a;
+  }
+  __syncwarp();
+  for (int guard = 0; guard < (1 << 20); ++guard) {
+    // most / least loaded GPU (first index on ties)
+    long long mv = lane < G ? amt[lane] : LLONG_MIN, lv = lane < G ? amt[lane] : LLONG_MAX;
+    int mi = lane < G ? lane : 1 << 30, li = mi;
+    bool over_any = lane < G && amt[lane] > avg;
+    over_any = __any_sync(0xffffffffu, over_any);
+    if (!over_any) break;
+    for (int off = 16; off; off >>= 1) {
+      long long ov = __shfl_xor_sync(0xffffffffu, mv, off);
+      int oi = __shfl_xor_sync(0xffffffffu, mi, off);
+      if (ov > mv || (ov == mv && oi < mi)) { mv = ov; mi = oi; }
+      long long lv2 = __shfl_xor_sync(0xffffffffu, lv, off);
+      int li2 = __shfl_xor_sync(0xffffffffu, li, off);
+      if (lv2 < lv || (lv2 == lv && li2 < li)) { lv = lv2; li = li2; }
+    }
+    const int over = mi, least = li;
+    if (least == over || amt[least] + eq_tokens > avg) break;
+    // the expert with most tokens on the overloaded GPU
+    long long sv = LLONG_MIN;
+    int si = 1 << 30;
+    for (int e = lane; e < E; e += 32) {
+      long long s = 0;
+      for (int src = 0; src < G; ++src) s += S[(src * E + e) * G + over];
+      if (s > sv) { sv = s; si = e; }
+    }
+    for (int off = 16; off; off >>= 1) {
+      long long ov = __shfl_xor_sync(0xffffffffu, sv, off);
+      int oi = __shfl_xor_sync(0xffffffffu, si, off);
+      if (ov > sv || (ov == sv && oi < si)) { sv = ov; si = oi; }
+    }
+    const int e = si;
+    if (sv < eq_tokens) break;
+    long long amount_over = amt[over] - avg;
+    long long moved = 0;
+    while (amount_over > 0 && avg - amt[least] > 0) {
+      long long tv = lane < G ? (long long)S[(lane * E + e) * G + over] : LLONG_MIN;
+      int ti = lane < G ? lane : 1 << 30;
+      for (int off = 16; off; off >>= 1) {
+        long long ov = __shfl_xor_sync(0xffffffffu, tv, off);
+        int oi = __shfl_xor_sync(0xffffffffu, ti, off);
+        if (ov > tv || (ov == tv && oi < ti)) { tv = ov; ti = oi; }
+      }
+      if (tv <= 0) break;
+      const long long room = avg - amt[least];
+      const long long n = tv < room ? tv : room;
+      __syncwarp();
+      if (lane == 0) {
+        S[(ti * E + e) * G + over] -= (int32_t)n;
+        S[(ti * E + e) * G + least] += (int32_t)n;
+        amt[over] -= n;
+        amt[least] += n;
+      }
+      __syncwarp();
+      amount_over -= n;
+      moved += n;
+    }
+    if (moved == 0) break;
+  }
+  __syncwarp();
+}
+
+// ------------------------------------------------------------------ plan kernel
+__global__ void __launch_bounds__(256) plan_kernel(Ctx* c, const int32_t* counts, uint64_t limit_ns, int32_t* err) {
+  __shared__ int32_t meta_s[kMaxG * kMaxE];
+  __shared__ int32_t S_s[kMaxG * kMaxE * kMaxG];
+  __shared__ long long amt_s[kMaxG];
+  __shared__ int32_t e2g_s[kMaxE];
+  const int G = c->G, E = c->E, me = c->me, tid = threadIdx.x;
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(&c->epoch) + 1u;
+  // 1. my counts into every rank's meta[me][*]
+  for (int i = tid; i < G * E; i += blockDim.x) {
+    const int p = i / E, e = i % E;
+    c->meta[p][me * kMaxE + e] = counts[e];
+  }
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence_system();
+    for (int p = 0; p < G; ++p) st_release_sys(c->flags[p] + kCounts * kMaxG + me, epoch);
+  }
+  // 2. every rank's counts
+  if (tid < G) {
+    if (!wait_flag(c->flags[me] + kCounts * kMaxG + tid, epoch, limit_ns)) record_error(err, kErrWaitTimeout);
+  }
+  __syncthreads();
+  const volatile int32_t* ml = c->meta[me];
+  for (int i = tid; i < G * E; i += blockDim.x) meta_s[i] = ml[(i / E) * kMaxE + i % E];
+  for (int e = tid; e < E; e += blockDim.x) e2g_s[e] = c->expert_to_gpu[e];
+  __syncthreads();
+  // 3. the plan
+  if (tid < 32) harmony_warp(meta_s, G, E, e2g_s, c->eq_tokens, S_s, amt_s);
+  __syncthreads();
+  auto Sv = [&](int src, int e, int dst) { return S_s[(src * E + e) * G + dst]; };
+  for (int i = tid; i < G * E * G; i += blockDim.x) {
+    const int src = i / (E * G), e = (i / G) % E, dst = i % G;
+    c->S[src][e][dst] = S_s[i];
+  }
+  // 4. tables.  rows_to(dst, e) = sum_src S[src][e][dst]; group offsets of rank r =
+  //    prefix over e of rows_to(r, e); chunk (src, e) sits after the chunks of lower src.
+  for (int i = tid; i < E * G; i += blockDim.x) {
+    const int e = i / G, dst = i % G;
+    // cum_split and send_base (this rank as sender)
+    int cs = 0;
+    for (int d2 = 0; d2 <= dst; ++d2) cs += Sv(me, e, d2);
+    c->cum_split[e][dst] = cs;
+    int sb = 0;
+    for (int d2 = 0; d2 < dst; ++d2)
+      for (int e2 = 0; e2 < E; ++e2) sb += Sv(me, e2, d2);
+    for (int e2 = 0; e2 < e; ++e2) sb += Sv(me, e2, dst);
+    c->send_base[e][dst] = sb;
+    // remote_base: first row of chunk (me, e) in dst's receive buffer
+    int rb = 0;
+    for (int e2 = 0; e2 < e; ++e2)
+      for (int s2 = 0; s2 < G; ++s2) rb += Sv(s2, e2, dst);
+    for (int s2 = 0; s2 < me; ++s2) rb += Sv(s2, e, dst);
+    c->remote_base[e][dst] = rb;
+    // receive side (this rank as dst), chunk of src = dst-index here
+    const int src = dst;
+    int cst = 0;
+    for (int e2 = 0; e2 < e; ++e2)
+      for (int s2 = 0; s2 < G; ++s2) cst += Sv(s2, e2, me);
+    for (int s2 = 0; s2 < src; ++s2) cst += Sv(s2, e, me);
+    c->chunk_start[e][src] = cst;
+    c->chunk_len[e][src] = Sv(src, e, me);
+    // where that chunk goes back: src's send layout, position of (e, me)
+    int rs = 0;
+    for (int d2 = 0; d2 < me; ++d2)
+      for (int e2 = 0; e2 < E; ++e2) rs += Sv(src, e2, d2);
+    for (int e2 = 0; e2 < e; ++e2) rs += Sv(src, e2, me);
+    c->ret_start[e][src] = rs;
+  }
+  if (tid == 0) {
+    int r = 0;
+    for (int e = 0; e < E; ++e) {
+      c->group_offsets[e] = r;
+      for (int s2 = 0; s2 < G; ++s2) r += Sv(s2, e, me);
+    }
+    c->group_offsets[E] = r;
+    c->recv_total = r;
+    if (r > c->recv_capacity) record_error(err, kErrCapacity);
+    int snd = 0;
+    for (int e = 0; e < E; ++e)
+      for (int d2 = 0; d2 < G; ++d2) snd += Sv(me, e, d2);
+    if (snd > c->ret_capacity) record_error(err, kErrCapacity);
+    __threadfence();
+    *reinterpret_cast<volatile uint32_t*>(&c->epoch) = epoch;
+  }
+}
+
+// ------------------------------------------------------------------ dispatch kernel
+template <int ESZ>
+__global__ void __launch_bounds__(256) dispatch_kernel(dsca_ep_dispatch_args a, Ctx* c) {
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int total = a.T * a.top_k;
+  if (w < total) {
+    const int t = w / a.top_k;
+    const int e = a.topk_ids[w];
+    const int G = c->G;
+    bool ok = e >= 0 && e < c->E;
+    int dst = 0, q = 0, before = 0;
+    if (ok) {
+      q = a.block_base[(size_t)(t / DSCA_ROUTER_TOKENS) * c->E + e] + a.local_rank[w];
+      while (dst < G && q >= c->cum_split[e][dst]) ++dst;
+      ok = dst < G;
+    }
+    if (!ok) {
+      if (lane == 0) record_error(a.err, kErrIndex);
+    } else {
+      before = dst > 0 ? c->cum_split[e][dst - 1] : 0;
+      const int rrow = c->remote_base[e][dst] + (q - before);
+      const int srow = c->send_base[e][dst] + (q - before);
+      if (rrow < 0 || rrow >= c->recv_capacity || srow < 0 || srow >= c->ret_capacity) {
+        if (lane == 0) record_error(a.err, kErrCapacity);
+      } else {
+        if (lane == 0) a.token_row[w] = srow;
+        const size_t row_bytes = (size_t)a.d * ESZ;
+        const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(a.x) + (size_t)t * row_bytes);
+        uint4* dp = reinterpret_cast<uint4*>(c->recv[dst] + (size_t)rrow * row_bytes);
+        const int nvec = (int)(row_bytes / 16);
+        for (int v = lane; v < nvec; v += 32) dp[v] = src[v];
+      }
+    }
+  }
+  signal_when_grid_done(c, &c->dispatch_done, kDispatch);
+}
+
+// ------------------------------------------------------------------ wait kernel
+__global__ void wait_kernel(Ctx* c, int kind, uint64_t limit_ns, int32_t* err) {
+  const int src = threadIdx.x;
+  if (src < c->G) {
+    const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(&c->epoch);
+    if (!wait_flag(c->flags[c->me] + kind * kMaxG + src, epoch, limit_ns)) record_error(err, kErrWaitTimeout);
+  }
+}
+
+// ------------------------------------------------------------------ test hook: device plan
+__global__ void plan_eval_kernel(const int32_t* meta, int G, int E, const int32_t* e2g, int eq, int32_t* S) {
+  __shared__ int32_t meta_s[kMaxG * kMaxE];
+  __shared__ int32_t S_s[kMaxG * kMaxE * kMaxG];
+  __shared__ long long amt_s[kMaxG];
+  __shared__ int32_t e2g_s[kMaxE];
+  for (int i = threadIdx.x; i < G * E; i += 32) meta_s[i] = meta[i];
+  for (int i = threadIdx.x; i < E; i += 32) e2g_s[i] = e2g[i];
+  __syncwarp();
+  harmony_warp(meta_s, G, E, e2g_s, eq, S_s, amt_s);
+  for (int i = threadIdx.x; i < G * E * G; i += 32) S[i] = S_s[i];
+}
+
+}  // namespace ep
+}  // namespace dsca
+
+// ------------------------------------------------------------------ C ABI
+using dsca::ep::Ctx;
+using dsca::ep::kMaxE;
+using dsca::ep::kMaxG;
+
+extern "C" {
+
+size_t dsca_ep_ctx_bytes(void) { return sizeof(Ctx); }
+
+int32_t* dsca_ep_group_offsets(void* ctx_dev) {
+  return ctx_dev == nullptr ? nullptr : static_cast<Ctx*>(ctx_dev)->group_offsets;
+}
+
+int dsca_ep_read_plan(void* ctx_dev, int32_t* S_host, int32_t* recv_total_host, dsca_stream_t stream) {
+  if (ctx_dev == nullptr || S_host == nullptr || recv_total_host == nullptr) return DSCA_ERR_BAD_ARG;
+  Ctx* c = static_cast<Ctx*>(ctx_dev);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(S_host, c->S, sizeof(c->S), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaMemcpyAsync(recv_total_host, &c->recv_total, sizeof(int32_t), cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return DSCA_ERR_CUDA;
+  return cudaStreamSynchronize(st) == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
+}
+
+int dsca_ep_init(void* ctx_dev, const dsca_ep_setup* s, dsca_stream_t stream) {
+  if (ctx_dev == nullptr || s == nullptr || s->G <= 0 || s->G > kMaxG || s->E <= 0 || s->E > kMaxE || s->me < 0 ||
+      s->me >= s->G || s->d <= 0 || s->expert_to_gpu == nullptr || s->recv_capacity <= 0 || s->ret_capacity <= 0)
+    return DSCA_ERR_BAD_ARG;
+  if (s->elem_bytes != 2 && s->elem_bytes != 4) return DSCA_ERR_BAD_ARG;
+  static thread_local Ctx host;  // staging copy (stream-ordered H2D below is synchronised before return)
+  memset(&host, 0, sizeof(Ctx));
+  host.G = s->G;
+  host.E = s->E;
+  host.me = s->me;
+  host.d = s->d;
+  host.recv_capacity = s->recv_capacity;
+  host.ret_capacity = s->ret_capacity;
+  host.eq_tokens = s->eq_tokens;
+  host.elem_bytes = s->elem_bytes;
+  host.epoch = s->start_epoch;
+  for (int e = 0; e < s->E; ++e) {
+    if (s->expert_to_gpu[e] < 0 || s->expert_to_gpu[e] >= s->G) return DSCA_ERR_BAD_ARG;
+    host.expert_to_gpu[e] = s->expert_to_gpu[e];
+  }
+  for (int p = 0; p < s->G; ++p) {
+    if (s->flags[p] == nullptr || s->meta[p] == nullptr || s->recv[p] == nullptr || s->ret[p] == nullptr)
+      return DSCA_ERR_BAD_ARG;
+    host.flags[p] = static_cast<uint32_t*>(s->flags[p]);
+    host.meta[p] = static_cast<int32_t*>(s->meta[p]);
+    host.recv[p] = static_cast<char*>(s->recv[p]);
+    host.ret[p] = static_cast<char*>(s->ret[p]);
+  }
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(ctx_dev, &host, sizeof(Ctx), cudaMemcpyHostToDevice, st) != cudaSuccess) return DSCA_ERR_CUDA;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return DSCA_ERR_CUDA;
+  return DSCA_OK;
+}
+
+int dsca_ep_plan(void* ctx_dev, const int32_t* counts, uint64_t limit_ns, int32_t* err, dsca_stream_t stream) {
+  if (ctx_dev == nullptr || counts == nullptr) return DSCA_ERR_BAD_ARG;
+  dsca::ep::plan_kernel<<<1, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(static_cast<Ctx*>(ctx_dev), counts,
+                                                                            limit_ns, err);
+  return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
+}
+
+int dsca_ep_dispatch(const dsca_ep_dispatch_args* a, dsca_stream_t stream) {
+  if (a == nullptr || a->ctx == nullptr || a->x == nullptr || a->topk_ids == nullptr || a->local_rank == nullptr ||
+      a->block_base == nullptr || a->token_row == nullptr || a->top_k <= 0 || a->top_k > DSCA_MAX_TOPK || a->T < 0)
+    return DSCA_ERR_BAD_ARG;
+  if (a->dtype != DSCA_BF16 && a->dtype != DSCA_F32) return DSCA_ERR_BAD_ARG;
+  const int esz = a->dtype == DSCA_BF16 ? 2 : 4;
+  if (((size_t)a->d * esz) % 16 != 0 || (reinterpret_cast<uintptr_t>(a->x) & 15u)) return DSCA_ERR_BAD_ARG;
+  const long long warps = (long long)a->T * a->top_k;
+  const int blocks = (int)(warps > 0 ? (warps * 32 + 255) / 256 : 1);  // >= 1 CTA so the flag is still set
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (esz == 2)
+    dsca::ep::dispatch_kernel<2><<<blocks, 256, 0, st>>>(*a, static_cast<Ctx*>(a->ctx));
+  else
+    dsca::ep::dispatch_kernel<4><<<blocks, 256, 0, st>>>(*a, static_cast<Ctx*>(a->ctx));
+  return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
+}
+
+int dsca_ep_wait(void* ctx_dev, int kind, uint64_t limit_ns, int32_t* err, dsca_stream_t stream) {
+  if (ctx_dev == nullptr || kind < 0 || kind > 2) return DSCA_ERR_BAD_ARG;
+  dsca::ep::wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(static_cast<Ctx*>(ctx_dev), kind,
+                                                                            limit_ns, err);
+  return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
+}
+
+int dsca_ep_plan_eval(const int32_t* meta, int G, int E, const int32_t* expert_to_gpu, int eq_tokens, int32_t* S,
+                      dsca_stream_t stream) {
+  if (meta == nullptr || expert_to_gpu == nullptr || S == nullptr || G <= 0 || G > kMaxG || E <= 0 || E > kMaxE)
+    return DSCA_ERR_BAD_ARG;
+  dsca::ep::plan_eval_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(meta, G, E, expert_to_gpu,
+                                                                                 eq_tokens, S);
+  return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
+}
+
+// ------------------------------------------------------------------ the symmetric region itself
+// Its own cudaMalloc allocation (set-up time, once per engine), zeroed, so that CUDA IPC maps
+// exactly this region into the peers.
+int dsca_ep_region_alloc(size_t bytes, void** ptr) {
+  if (ptr == nullptr || bytes == 0) return DSCA_ERR_BAD_ARG;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return DSCA_ERR_CUDA;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+    cudaFree(p);
+    return DSCA_ERR_CUDA;
+  }
+  *ptr = p;
+  return DSCA_OK;
+}
+
+int dsca_ep_region_free(void* ptr) {
+  if (ptr == nullptr) return DSCA_ERR_BAD_ARG;
+  return cudaFree(ptr) == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
+}
+
+// ------------------------------------------------------------------ CUDA IPC of the symmetric region
+typedef CUresult (*PFN_getAddressRange)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+static PFN_getAddressRange get_range_fn() {
+  static PFN_getAddressRange fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    fn = reinterpret_cast<PFN_getAddressRange>(p);
+  }
+  return fn;
+}
+
+int dsca_ipc_export(const void* ptr, void* handle64, size_t* offset) {
+  if (ptr == nullptr || handle64 == nullptr || offset == nullptr) return DSCA_ERR_BAD_ARG;
+  PFN_getAddressRange range = get_range_fn();
+  if (range == nullptr) return DSCA_ERR_CUDA;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) return DSCA_ERR_CUDA;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)) != cudaSuccess) return DSCA_ERR_CUDA;
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  memcpy(handle64, &h, 64);
+  *offset = static_cast<size_t>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return DSCA_OK;
+}
+
+int dsca_ipc_import(const void* handle64, size_t offset, void** ptr) {
+  if (handle64 == nullptr || ptr == nullptr) return DSCA_ERR_BAD_ARG;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle64, 64);
+  void* base = nullptr;
+  if (cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return DSCA_ERR_CUDA;
+  *ptr = static_cast<char*>(base) + offset;
+  return DSCA_OK;
+}
+
+int dsca_ipc_close(void* ptr, size_t offset) {
+  if (ptr == nullptr) return DSCA_ERR_BAD_ARG;
+  return cudaIpcCloseMemHandle(static_cast<char*>(ptr) - offset) == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
+}
+
+}  // extern "C"

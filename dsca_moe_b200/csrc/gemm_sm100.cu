@@ -21,6 +21,7 @@
 // Every wait is bounded (2 s): on a timeout the kernel records DSCA_ERR_WAIT_TIMEOUT in the
 // error word, drains its own outstanding copies and MMAs, frees TMEM and returns.
 #include "common.cuh"
+#include "ep.cuh"
 
 namespace dsca {
 namespace gemm {
@@ -49,6 +50,9 @@ struct Segment {
   int ldc;
   int n_store;
   int capacity;
+  // expert parallel: when set, output row r of group e belongs to chunk (src, e) of the
+  // receive buffer and is stored straight into rank src's return buffer (peer memory)
+  const ep::Ctx* ep;
 };
 
 struct Params {
@@ -56,11 +60,22 @@ struct Params {
   int nseg;
   int epi;
   int32_t* err;
+  ep::Ctx* ep_signal;  // set: signal the return flag at every peer once the grid is done
 };
 
 struct TileInfo {
-  int seg, row0, rows_valid, b_row0, n_blk;
+  int seg, group, row0, rows_valid, b_row0, n_blk;
 };
+
+// Destination row pointer of a routed output row in the expert-parallel return path.
+__device__ __forceinline__ __nv_bfloat16* ep_return_row(const ep::Ctx* c, int e, int r, int ldc) {
+  for (int src = 0; src < c->G; ++src) {
+    const int cs = c->chunk_start[e][src];
+    if (r >= cs && r < cs + c->chunk_len[e][src])
+      return reinterpret_cast<__nv_bfloat16*>(c->ret[src]) + (size_t)(c->ret_start[e][src] + r - cs) * ldc;
+  }
+  return nullptr;
+}
 
 struct SmemCtl {
   uint64_t full[kStages];
@@ -93,6 +108,7 @@ __device__ __forceinline__ TileInfo decode(const Params& p, const SmemCtl& s, in
     ti.n_blk = local - m_blk * sg.n_tiles;
     int rows_g = s.goff[g + 1] - s.goff[g];
     ti.seg = 0;
+    ti.group = g;
     ti.row0 = s.goff[g] + m_blk * BM;
     ti.rows_valid = min(BM, rows_g - m_blk * BM);
     ti.b_row0 = s.gw[g] * sg.b_rows_per_group + ti.n_blk * BN;
@@ -102,6 +118,7 @@ __device__ __forceinline__ TileInfo decode(const Params& p, const SmemCtl& s, in
     int m_blk = local / sg.n_tiles;
     ti.n_blk = local - m_blk * sg.n_tiles;
     ti.seg = 1;
+    ti.group = 0;
     ti.row0 = m_blk * BM;
     ti.rows_valid = min(BM, sg.rows - ti.row0);
     ti.b_row0 = ti.n_blk * BN;
@@ -290,9 +307,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-      const bool valid = r_in_tile < ti.rows_valid;
+      bool valid = r_in_tile < ti.rows_valid;
       const size_t row = (size_t)(ti.row0 + r_in_tile);
       __nv_bfloat16* crow = sg.c + row * (size_t)sg.ldc;
+      if (EPI == kEpiStore && sg.ep != nullptr && valid) {
+        // expert parallel: this row goes back to the rank that sent it (NVLink store)
+        crow = ep_return_row(sg.ep, ti.group, (int)row, sg.ldc);
+        if (crow == nullptr) {
+          record_error(p.err, kErrIndex);
+          valid = false;
+        }
+      }
       if constexpr (EPI == kEpiSwiGLU) {
         const int col0 = ti.n_blk * (BN / 2);
 #pragma unroll 1
@@ -354,6 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
+  if (p.ep_signal != nullptr) ep::signal_when_grid_done(p.ep_signal, &p.ep_signal->return_done, ep::kReturn);
 }
 
 }  // namespace gemm
@@ -494,7 +520,9 @@ int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t st
     p.epi = gemm::kEpiStore;
     p.err = f->err;
     p.nseg = shared ? 2 : 1;
+    p.ep_signal = static_cast<ep::Ctx*>(f->ep_ctx);
     gemm::Segment& s0 = p.seg[0];
+    s0.ep = static_cast<const ep::Ctx*>(f->ep_ctx);
     s0.group_offsets = f->group_offsets;
     s0.group_weight = f->group_weight;
     s0.ngroups = f->num_groups;

@@ -27,7 +27,27 @@ __all__ = ["PackedExperts", "pack_swiglu", "pack_relu", "MoEEngine", "plan_harmo
 
 
 def _ptr(t):
-    return None if t is None else ctypes.c_void_p(t.data_ptr())
+    if t is None:
+        return None
+    if isinstance(t, int):
+        return ctypes.c_void_p(t)
+    return ctypes.c_void_p(t.data_ptr())
+
+
+class _DevPtr:
+    """A raw device pointer seen as a torch tensor (zero copy, through __cuda_array_interface__)."""
+
+    _TYPESTR = {torch.bfloat16: "<f2", torch.float32: "<f4", torch.int32: "<i4", torch.uint8: "|u1"}
+
+    def __init__(self, ptr: int, shape, dtype):
+        # bf16 has no numpy type string: expose it as 2-byte float and reinterpret below
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": self._TYPESTR[dtype],
+                                         "data": (ptr, False), "version": 3}
+
+    @staticmethod
+    def tensor(ptr: int, shape, dtype, device):
+        t = torch.as_tensor(_DevPtr(ptr, shape, dtype), device=device)
+        return t.view(dtype) if dtype == torch.bfloat16 else t
 
 
 def _stream():
@@ -208,12 +228,17 @@ class MoEEngine:
     requires); experts: PackedExperts; route_mode L.ROUTE_SWITCH_TOP1 or L.ROUTE_SOFTMAX_TOPK;
     shared_gate_weight [d] or None.  Multi-GPU: pass world > 1, a torch.distributed group and
     expert_to_gpu [E] (the placement), eq_tokens as in the reference scheduler.
+
+    exchange = "p2p" (default): the fused NVLink path — counts, plan, dispatch and return all on
+    the device over CUDA-IPC peer memory, no host synchronisation.  exchange = "nccl": the
+    NCCL baseline (host plan, grouped send/recv).  p2p capacity is fixed by the first forward
+    (max tokens over the ranks) or by reserve(tokens); wait_limit_ns bounds every device wait.
     """
 
     def __init__(self, router_weight: torch.Tensor, experts: PackedExperts, top_k: int, route_mode: int,
                  norm_topk: bool = False, shared_gate_weight: torch.Tensor | None = None,
                  rank: int = 0, world: int = 1, group=None, expert_to_gpu=None, eq_tokens: int = 150,
-                 num_ctas: int = 0):
+                 num_ctas: int = 0, exchange: str = "p2p", wait_limit_ns: int = 2_000_000_000):
         lib = L.load()
         n_sms, is_sm100 = ctypes.c_int(0), ctypes.c_int(0)
         L.check(lib.dsca_device_info(ctypes.byref(n_sms), ctypes.byref(is_sm100)), "dsca_device_info")
@@ -240,6 +265,14 @@ class MoEEngine:
         self.expert_to_gpu = np.asarray(expert_to_gpu, dtype=np.int32)
         self.eq_tokens = int(eq_tokens)
         self.num_ctas = num_ctas
+        if exchange not in ("p2p", "nccl"):
+            raise ValueError("exchange must be 'p2p' or 'nccl'")
+        self.exchange = exchange
+        self.wait_limit_ns = int(wait_limit_ns)
+        self._ep = None
+        # one GPU through the fused exchange path (the rank is its own only peer): exercises the
+        # plan / dispatch / return kernels without a second GPU
+        self.ep_loopback = False
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._ws = {}
         self.last_plan = None
@@ -312,17 +345,17 @@ class MoEEngine:
         p.capacity, p.out, p.token_row, p.err = capacity, _ptr(out), _ptr(ws["token_row"]), _ptr(self.err)
         L.call("dsca_permute", ctypes.byref(p), _stream())
 
-    def _ffn(self, x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight):
+    def _ffn(self, x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, ep_ctx=None):
         if self.markers is not None:
             # time GEMM1 and GEMM2 as separate launches
-            self._ffn_call(x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, 1)
+            self._ffn_call(x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, 1, ep_ctx)
             self._mark("gemm1")
-            self._ffn_call(x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, 2)
+            self._ffn_call(x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, 2, ep_ctx)
             self._mark("gemm2")
         else:
-            self._ffn_call(x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, 3)
+            self._ffn_call(x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, 3, ep_ctx)
 
-    def _ffn_call(self, x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, phases):
+    def _ffn_call(self, x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, phases, ep_ctx=None):
         pe = self.experts
         f = L.FfnArgs()
         f.dtype, f.act, f.d = _dt(self.dtype), pe.act, self.d
@@ -334,6 +367,7 @@ class MoEEngine:
             f.shared_rows, f.shared_n1p, f.shared_ip = x.shape[0], pe.s_n1p, pe.s_ip
             f.xs, f.ws1, f.ws2, f.hs, f.ys = _ptr(x), _ptr(pe.ws1), _ptr(pe.ws2), _ptr(ws["hs"]), _ptr(ws["ys"])
         f.err, f.num_ctas, f.phases = _ptr(self.err), self.num_ctas, phases
+        f.ep_ctx = _ptr(ep_ctx)
         L.call("dsca_grouped_ffn", ctypes.byref(f), _stream())
 
     def _combine(self, ws, y, rows):
@@ -365,7 +399,7 @@ class MoEEngine:
         self._mark("start")
         self._route(x, ws)
         self._mark("scan")
-        if self.world == 1:
+        if self.world == 1 and not self.ep_loopback:
             cap = ws["a"].shape[0]
             self._permute(x, ws, ws["a"], cap)
             self._mark("permute")
@@ -376,6 +410,133 @@ class MoEEngine:
         return self._forward_ep(x, ws)
 
     def _forward_ep(self, x, ws):
+        if self.exchange == "p2p":
+            return self._forward_p2p(x, ws)
+        return self._forward_nccl(x, ws)
+
+    # -------------------------------------------------------------- fused NVLink path
+    def reserve(self, tokens: int):
+        """Collective (every rank calls it): size the symmetric region for `tokens` tokens per
+        rank (max over the ranks is used) and map every peer's region."""
+        self._p2p_setup(tokens)
+
+    def _p2p_setup(self, T: int):
+        import torch.distributed as dist
+
+        lib = L.load()
+        G, me, k, d, dev = self.world, self.rank, self.top_k, self.d, self.device
+        if G > L.MAX_GPUS or self.E > L.MAX_EXPERTS:
+            raise ValueError("the p2p exchange supports up to 8 GPUs and 64 experts")
+        if G > 1:
+            t = torch.tensor([T], dtype=torch.int64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+            T = int(t.item())
+        T_cap = max(T, 1)
+        esz = 2 if self.dtype == torch.bfloat16 else 4
+        recv_cap, ret_cap = G * T_cap * k, T_cap * k
+        off_flags, off_meta = 0, 256
+        off_recv = 256 + 4 * L.MAX_GPUS * L.MAX_EXPERTS
+        off_recv = _ceil(off_recv, 256) * 256
+        off_ret = _ceil(off_recv + recv_cap * d * esz, 256) * 256
+        total = off_ret + ret_cap * d * esz
+        region = ctypes.c_void_p()
+        L.call("dsca_ep_region_alloc", ctypes.c_size_t(total), ctypes.byref(region))
+        handle = (ctypes.c_char * 64)()
+        off = ctypes.c_size_t(0)
+        L.call("dsca_ipc_export", region, handle, ctypes.byref(off))
+        allh = [(bytes(handle), int(off.value))]
+        if G > 1:
+            allh = [None] * G
+            dist.all_gather_object(allh, (bytes(handle), int(off.value)), group=self.group)
+        bases, imported = [], []
+        for p in range(G):
+            if p == me:
+                bases.append(region.value)
+                continue
+            h = (ctypes.c_char * 64).from_buffer_copy(allh[p][0])
+            ptr = ctypes.c_void_p()
+            L.call("dsca_ipc_import", h, ctypes.c_size_t(allh[p][1]), ctypes.byref(ptr))
+            bases.append(ptr.value)
+            imported.append((ptr.value, allh[p][1]))
+        s = L.EpSetup()
+        s.G, s.E, s.me, s.d, s.elem_bytes = G, self.E, me, d, esz
+        s.recv_capacity, s.ret_capacity, s.eq_tokens, s.start_epoch = recv_cap, ret_cap, self.eq_tokens, 0
+        e2g = np.ascontiguousarray(self.expert_to_gpu, dtype=np.int32)
+        s.expert_to_gpu = e2g.ctypes.data
+        for p in range(G):
+            s.flags[p] = bases[p] + off_flags
+            s.meta[p] = bases[p] + off_meta
+            s.recv[p] = bases[p] + off_recv
+            s.ret[p] = bases[p] + off_ret
+        ctx = torch.empty(int(lib.dsca_ep_ctx_bytes()), dtype=torch.uint8, device=dev)
+        L.call("dsca_ep_init", _ptr(ctx), ctypes.byref(s), _stream())
+        torch.cuda.synchronize(dev)
+        if G > 1:
+            dist.barrier(group=self.group)  # every region is zeroed and mapped before anyone stores
+        dt = self.dtype
+        self._ep = dict(
+            region=region.value, imported=imported, ctx=ctx, T_cap=T_cap, recv_cap=recv_cap, ret_cap=ret_cap,
+            recv=_DevPtr.tensor(region.value + off_recv, (recv_cap, d), dt, dev),
+            ret=_DevPtr.tensor(region.value + off_ret, (ret_cap, d), dt, dev),
+            h=torch.empty(recv_cap, self.experts.ip, dtype=dt, device=dev),
+            group_offsets=int(lib.dsca_ep_group_offsets(_ptr(ctx)) or 0),
+            bytes=total)
+
+    def _forward_p2p(self, x, ws):
+        T = x.shape[0]
+        if self._ep is None:
+            self._p2p_setup(T)
+        ep = self._ep
+        if T > ep["T_cap"]:
+            raise RuntimeError(f"{T} tokens exceed the reserved {ep['T_cap']} per rank (call reserve())")
+        lib, st, ctx = L.load(), _stream(), _ptr(ep["ctx"])
+        L.check(lib.dsca_ep_plan(ctx, _ptr(ws["counts"]), self.wait_limit_ns, _ptr(self.err), st), "dsca_ep_plan")
+        self._mark("plan")
+        a = L.EpDispatchArgs()
+        a.x, a.T, a.d, a.top_k, a.dtype = _ptr(x), T, self.d, self.top_k, _dt(self.dtype)
+        a.topk_ids, a.local_rank, a.block_base = _ptr(ws["topk_ids"]), _ptr(ws["local_rank"]), _ptr(ws["block_base"])
+        a.ctx, a.token_row, a.err = ctx, _ptr(ws["token_row"]), _ptr(self.err)
+        L.call("dsca_ep_dispatch", ctypes.byref(a), st)
+        self._mark("dispatch")
+        L.check(lib.dsca_ep_wait(ctx, 1, self.wait_limit_ns, _ptr(self.err), st), "dsca_ep_wait")
+        self._mark("wait_dispatch")
+        self._ffn(x, ws, ep["recv"], ep["h"], ep["recv"], ep["recv_cap"], self.E, ep["group_offsets"], None,
+                  ep_ctx=ep["ctx"])
+        L.check(lib.dsca_ep_wait(ctx, 2, self.wait_limit_ns, _ptr(self.err), st), "dsca_ep_wait")
+        self._mark("wait_return")
+        self._combine(ws, ep["ret"], ep["ret_cap"])
+        self._mark("combine")
+        return ws
+
+    def read_plan(self):
+        """(S [G, E, G], rows received here) of the last forward (host copy; synchronises)."""
+        if self.exchange == "nccl" or self._ep is None:
+            S = self.last_plan
+            return S, (int(self.last_layout.group_offsets[-1]) if self.last_layout is not None else 0)
+        S = np.zeros((L.MAX_GPUS, L.MAX_EXPERTS, L.MAX_GPUS), np.int32)
+        rt = np.zeros(1, np.int32)
+        L.call("dsca_ep_read_plan", _ptr(self._ep["ctx"]), S.ctypes.data, rt.ctypes.data, _stream())
+        return S[:self.world, :self.E, :self.world].copy(), int(rt[0])
+
+    def close(self):
+        """Unmap the peers' regions and free this rank's (collective: every rank calls it, after
+        its last forward)."""
+        if self._ep is None:
+            return
+        import torch.distributed as dist
+
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)  # no peer stores into our region any more
+        for ptr, off in self._ep["imported"]:
+            L.load().dsca_ipc_close(ctypes.c_void_p(ptr), ctypes.c_size_t(off))
+        if self.world > 1:
+            dist.barrier(group=self.group)  # every peer has unmapped ours
+        L.load().dsca_ep_region_free(ctypes.c_void_p(self._ep["region"]))
+        self._ep = None
+
+    # -------------------------------------------------------------- NCCL baseline path
+    def _forward_nccl(self, x, ws):
         import torch.distributed as dist
 
         G, rank, E, d, dt, dev = self.world, self.rank, self.E, self.d, self.dtype, self.device

@@ -2,7 +2,8 @@
  * dsca_b200 — C ABI of the B200 (sm_100a) MoE-block forward for DSCA-MoE.
  *
  * Every entry point takes plain device pointers, sizes and a CUDA stream, launches its kernels
- * on that stream and returns an int status (DSCA_OK = 0).  Nothing here allocates device
+ * on that stream and returns an int status (DSCA_OK = 0).  Apart from the expert-parallel
+ * symmetric region (dsca_ep_region_alloc, set-up time), nothing here allocates device
  * memory: buffers and scratch space come from the caller, with the shapes documented beside
  * each argument struct.  Kernels that detect a problem (a wait past its
  * time limit, an out-of-range index, more rows than the workspace holds) write a code into the
@@ -178,6 +179,9 @@ typedef struct {
   int32_t* err;               /* device error word */
   int num_ctas;               /* persistent CTAs (0 = one per SM) */
   int phases;                 /* 0 or 3 = both GEMMs; 1 = GEMM1 only; 2 = GEMM2 only */
+  void* ep_ctx;               /* expert-parallel context (dsca_ep_init), or NULL: when set, GEMM2
+                                 stores each routed output row straight into the return buffer of
+                                 the rank that sent it and sets that rank's return flag */
 } dsca_ffn_args;
 DSCA_API int dsca_grouped_ffn(const dsca_ffn_args* a, dsca_stream_t stream);
 
@@ -239,6 +243,70 @@ DSCA_API int dsca_plan_layout(const int32_t* S, int G, int E, int rank, int* num
                      int32_t* group_expert, int32_t* group_offsets, int32_t* recv_off,
                      int32_t* send_base, int32_t* cum_split, int32_t* send_splits,
                      int32_t* recv_splits);
+
+/*
+ * Fused expert-parallel exchange over NVLink (one process per GPU).  Each rank owns a symmetric
+ * region: flags [3][DSCA_MAX_GPUS] u32, meta [DSCA_MAX_GPUS][DSCA_MAX_EXPERTS] i32, a receive
+ * buffer [recv_capacity, d] and a return buffer [ret_capacity, d]; every rank maps every peer's
+ * region (dsca_ipc_export / dsca_ipc_import) and passes the G pointers of each part.
+ * Per forward, on one stream, with no host synchronisation:
+ *   dsca_ep_plan      counts -> every peer, bounded wait for all counts, harmony plan and send /
+ *                     receive tables on the device (replaces the metadata all_to_all and
+ *                     Scheduler.schedule_harmony, src/qosmoe/moe_layer.py:367-385);
+ *   dsca_ep_dispatch  rows stored straight into the destination ranks' expert-major receive
+ *                     buffers, then the dispatch flag (replaces distribute_tokens + the dispatch
+ *                     all_to_all_single, moe_layer.py:393-408);
+ *   dsca_ep_wait      bounded wait for a flag kind from every peer (kind 0 counts, 1 dispatch,
+ *                     2 return);
+ *   dsca_grouped_ffn  with ep_ctx set (the return all_to_all fused into GEMM2's epilogue,
+ *                     moe_layer.py:435-440);
+ *   dsca_combine      over the local return buffer.
+ * Every wait gives up after limit_ns and records DSCA_ERR_WAIT_TIMEOUT in the error word.
+ */
+typedef struct {
+  int G, E, me, d, elem_bytes;
+  int recv_capacity, ret_capacity;
+  int eq_tokens;                  /* harmony threshold; < 0 = fixed placement */
+  unsigned int start_epoch;       /* the same on every rank (0 on a freshly zeroed region) */
+  const int32_t* expert_to_gpu;   /* host [E] */
+  void* flags[DSCA_MAX_GPUS];     /* per rank p: p's flag array (this process's mapping) */
+  void* meta[DSCA_MAX_GPUS];
+  void* recv[DSCA_MAX_GPUS];
+  void* ret[DSCA_MAX_GPUS];
+} dsca_ep_setup;
+DSCA_API size_t dsca_ep_ctx_bytes(void);
+DSCA_API int dsca_ep_init(void* ctx_dev, const dsca_ep_setup* s, dsca_stream_t stream);
+/* Device pointer of the plan's receive-side group offsets [E + 1] inside ctx_dev. */
+DSCA_API int32_t* dsca_ep_group_offsets(void* ctx_dev);
+/* Copy the last plan S [DSCA_MAX_GPUS][DSCA_MAX_EXPERTS][DSCA_MAX_GPUS] and the rows this rank
+ * received to the host (synchronises `stream`; for statistics, not the hot path). */
+DSCA_API int dsca_ep_read_plan(void* ctx_dev, int32_t* S_host, int32_t* recv_total_host, dsca_stream_t stream);
+DSCA_API int dsca_ep_plan(void* ctx_dev, const int32_t* counts, uint64_t limit_ns, int32_t* err,
+                          dsca_stream_t stream);
+typedef struct {
+  const void* x;
+  int T, d, top_k, dtype;
+  const int32_t* topk_ids;
+  const int32_t* local_rank;
+  const int32_t* block_base;
+  void* ctx;                  /* device context */
+  int32_t* token_row;         /* [T, k] out: row of (t, j) in this rank's return buffer */
+  int32_t* err;
+} dsca_ep_dispatch_args;
+DSCA_API int dsca_ep_dispatch(const dsca_ep_dispatch_args* a, dsca_stream_t stream);
+DSCA_API int dsca_ep_wait(void* ctx_dev, int kind, uint64_t limit_ns, int32_t* err, dsca_stream_t stream);
+/* The device harmony plan on its own (test hook): meta, e2g, S are device arrays. */
+DSCA_API int dsca_ep_plan_eval(const int32_t* meta, int G, int E, const int32_t* expert_to_gpu,
+                               int eq_tokens, int32_t* S, dsca_stream_t stream);
+/* The one set-up-time allocation of this library: a rank's symmetric region, its own cudaMalloc
+ * block (zeroed) so that CUDA IPC maps exactly that block into the peers.  Freed by
+ * dsca_ep_region_free after every peer closed its mapping. */
+DSCA_API int dsca_ep_region_alloc(size_t bytes, void** ptr);
+DSCA_API int dsca_ep_region_free(void* ptr);
+/* CUDA IPC of a device allocation (any pointer inside it): 64-byte handle + offset. */
+DSCA_API int dsca_ipc_export(const void* ptr, void* handle64, size_t* offset);
+DSCA_API int dsca_ipc_import(const void* handle64, size_t offset, void** ptr);
+DSCA_API int dsca_ipc_close(void* ptr, size_t offset);
 
 /* Read (and clear) the device error word; returns the matching DSCA_ERR_* or DSCA_OK.
  * Synchronises `stream`. */

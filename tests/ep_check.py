@@ -30,7 +30,7 @@ def rel(a, b):
     return float((a - b).abs().max() / b.abs().max().clamp_min(1e-30))
 
 
-def case_qwen(rank, world, dev, group, e2g, eq_tokens, T=512):
+def case_qwen(rank, world, dev, group, e2g, eq_tokens, exchange, T=512):
     d, E, I, Is = 1024, 60, 256, 512
     Wg, _ = syn.router_weight(E, d, 71, zipf_s=1.5, dtype="bf16")
     g = torch.Generator(device=dev)
@@ -43,13 +43,13 @@ def case_qwen(rank, world, dev, group, e2g, eq_tokens, T=512):
     pe = pack_swiglu(w["gate"], w["up"], w["down"], shared=(w["sg"], w["su"], w["sd"]), device=dev)
     Wt = torch.from_numpy(Wg).to(dev, torch.bfloat16)
     ep = MoEEngine(Wt, pe, top_k=4, route_mode=L.ROUTE_SOFTMAX_TOPK, shared_gate_weight=w["g"], rank=rank,
-                   world=world, group=group, expert_to_gpu=e2g, eq_tokens=eq_tokens)
+                   world=world, group=group, expert_to_gpu=e2g, eq_tokens=eq_tokens, exchange=exchange)
     one = MoEEngine(Wt, pe, top_k=4, route_mode=L.ROUTE_SOFTMAX_TOPK, shared_gate_weight=w["g"])
     x = torch.from_numpy(syn.hidden_states(T, d, 700 + rank, "bf16")).to(dev, torch.bfloat16)
     return ep, one, x
 
 
-def case_switch(rank, world, dev, group, e2g, eq_tokens, T=640):
+def case_switch(rank, world, dev, group, e2g, eq_tokens, exchange, T=640):
     d, E, F = 768, 64, 1024
     Wr, _ = syn.router_weight(E, d, 81, zipf_s=1.0, dtype="bf16")
     g = torch.Generator(device=dev)
@@ -59,7 +59,7 @@ def case_switch(rank, world, dev, group, e2g, eq_tokens, T=640):
     pe = pack_relu(wi, wo, device=dev)
     Wt = torch.from_numpy(Wr).to(dev, torch.bfloat16)
     ep = MoEEngine(Wt, pe, top_k=1, route_mode=L.ROUTE_SWITCH_TOP1, rank=rank, world=world, group=group,
-                   expert_to_gpu=e2g, eq_tokens=eq_tokens)
+                   expert_to_gpu=e2g, eq_tokens=eq_tokens, exchange=exchange)
     one = MoEEngine(Wt, pe, top_k=1, route_mode=L.ROUTE_SWITCH_TOP1)
     x = torch.from_numpy(syn.hidden_states(T, d, 800 + rank, "bf16")).to(dev, torch.bfloat16)
     return ep, one, x
@@ -74,16 +74,18 @@ def main():
     group = dist.group.WORLD
     results = []
     uneven60 = np.array([min(world - 1, (e * world * world) // (60 * (world + 1))) for e in range(60)], np.int32)
-    cases = [
-        ("qwen contiguous, harmony", case_qwen, None, 150),
-        ("qwen contiguous, fixed", case_qwen, None, -1),
-        ("qwen uneven placement, harmony", case_qwen, uneven60, 150),
-        ("switch top-1, harmony", case_switch, None, 150),
-    ]
+    cases = []
+    for exchange in ("p2p", "nccl"):
+        cases += [
+            (f"qwen contiguous, harmony, {exchange}", case_qwen, None, 150, exchange),
+            (f"qwen contiguous, fixed, {exchange}", case_qwen, None, -1, exchange),
+            (f"qwen uneven placement, harmony, {exchange}", case_qwen, uneven60, 150, exchange),
+            (f"switch top-1, harmony, {exchange}", case_switch, None, 150, exchange),
+        ]
     ok = True
-    for name, fn, e2g, eq in cases:
-        ep, one, x = fn(rank, world, dev, group, e2g, eq)
-        for it in range(2):
+    for name, fn, e2g, eq, exchange in cases:
+        ep, one, x = fn(rank, world, dev, group, e2g, eq, exchange)
+        for it in range(3):
             r_ep = ep.forward(x)
             r_one = one.forward(x)
             torch.cuda.synchronize()
@@ -92,12 +94,13 @@ def main():
             same_route = torch.equal(r_ep["topk_ids"], r_one["topk_ids"]) and torch.equal(r_ep["logits"], r_one["logits"])
             err = rel(r_ep["out"], r_one["out"])
             exact = torch.equal(r_ep["out"], r_one["out"])
-            S = ep.last_plan
+            S, _ = ep.read_plan()
             migrated = int(S.sum() - sum(S[:, e, ep.expert_to_gpu[e]].sum() for e in range(S.shape[1])))
             good = same_route and err < 2e-2 and torch.isfinite(r_ep["out"].float()).all().item()
             ok &= bool(good)
             results.append({"case": name, "iter": it, "rank": rank, "routing_equal": bool(same_route),
                             "max_rel_err": err, "bit_identical": bool(exact), "tokens_migrated": migrated})
+        ep.close()
     flag = torch.tensor([1 if ok else 0], device=dev)
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)
     gathered = [None] * world
