@@ -410,7 +410,10 @@ def main():
         counts = S[:, :, rank].sum(axis=0)
     e_touched = int((counts > 0).sum())
     f_router, f_g1, f_g2, hbm = flops_and_bytes(w, T, rows, e_touched)
-    t_g1, t_g2 = phase_ms.get("gemm1", float("nan")), phase_ms.get("gemm2", float("nan"))
+    # GEMM launches per step: gemm1 / gemm2 (one GPU) or their routed / shared halves (expert
+    # parallel; the fused variant names its GEMM2 gemm2_fused)
+    t_g1 = sum(v for k, v in phase_ms.items() if k.startswith("gemm1")) or float("nan")
+    t_g2 = sum(v for k, v in phase_ms.items() if k.startswith("gemm2")) or float("nan")
     achieved = (f_g1 + f_g2) / ((t_g1 + t_g2) / 1e3) / 1e12
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "traffic.json")

@@ -50,7 +50,7 @@ class FfnArgs(ctypes.Structure):
                 ("num_experts_w", _i), ("capacity", _i), ("a", _vp), ("w1", _vp), ("w2", _vp),
                 ("h", _vp), ("y", _vp), ("shared_rows", _i), ("shared_n1p", _i), ("shared_ip", _i),
                 ("xs", _vp), ("ws1", _vp), ("ws2", _vp), ("hs", _vp), ("ys", _vp), ("err", _vp),
-                ("num_ctas", _i), ("phases", _i), ("ep_ctx", _vp)]
+                ("num_ctas", _i), ("phases", _i), ("ep_ctx", _vp), ("segments", _i)]
 
 
 MAX_GPUS = 8
@@ -81,7 +81,7 @@ EXPORTED = ["dsca_version", "dsca_status_string", "dsca_device_info", "dsca_rout
             "dsca_grouped_ffn_static_scratch", "dsca_ep_ctx_bytes", "dsca_ep_init", "dsca_ep_group_offsets",
             "dsca_ep_plan", "dsca_ep_dispatch", "dsca_ep_wait", "dsca_ep_plan_eval", "dsca_ipc_export",
             "dsca_ipc_import", "dsca_ipc_close", "dsca_ep_read_plan", "dsca_ep_region_alloc",
-            "dsca_ep_region_free"]
+            "dsca_ep_region_free", "dsca_ep_return"]
 STATIC_SCRATCH_BYTES = 16 << 20
 
 _LIB = None
@@ -128,6 +128,7 @@ def load():
     lib.dsca_ep_read_plan.argtypes = [_vp, _vp, _vp, _vp]
     lib.dsca_ep_region_alloc.argtypes = [ctypes.c_size_t, p(_vp)]
     lib.dsca_ep_region_free.argtypes = [_vp]
+    lib.dsca_ep_return.argtypes = [_vp, _vp, _i, _i, _i, _vp, _vp]
     lib.dsca_combine.argtypes = [p(CombineArgs), _vp]
     lib.dsca_plan_harmony.argtypes = [_vp, _i, _i, _vp, _i, _vp]
     lib.dsca_plan_layout.argtypes = [_vp, _i, _i, _i, p(_i), _vp, _vp, _vp, _vp, _vp, _vp, _vp]

@@ -140,53 +140,65 @@ __global__ void __launch_bounds__(256) plan_kernel(Ctx* c, const int32_t* counts
     const int src = i / (E * G), e = (i / G) % E, dst = i % G;
     c->S[src][e][dst] = S_s[i];
   }
-  // 4. tables.  rows_to(dst, e) = sum_src S[src][e][dst]; group offsets of rank r =
-  //    prefix over e of rows_to(r, e); chunk (src, e) sits after the chunks of lower src.
+  // 4. tables from three prefix arrays (reusing meta_s, which is no longer needed):
+  //    rin[dst][e]  = rows of expert e arriving at dst before expert e (exclusive prefix over e of
+  //                   sum_src S[src][e][dst]) -> receive-buffer group starts of every rank;
+  //    sout[src][dst] = rows src sends to destinations before dst (exclusive prefix over dst of
+  //                   sum_e S[src][e][dst]) -> send-layout start of dst on src.
+  __shared__ int32_t rin_s[kMaxG][kMaxE + 1];
+  __shared__ int32_t sout_s[kMaxG][kMaxG];
+  __syncthreads();
+  if (tid < G) {  // one thread per destination rank: prefix over experts
+    const int dst = tid;
+    int r = 0;
+    for (int e = 0; e < E; ++e) {
+      rin_s[dst][e] = r;
+      for (int s2 = 0; s2 < G; ++s2) r += Sv(s2, e, dst);
+    }
+    rin_s[dst][E] = r;
+  } else if (tid >= 32 && tid < 32 + G) {  // one thread per source rank: prefix over destinations
+    const int src = tid - 32;
+    int r = 0;
+    for (int d2 = 0; d2 < G; ++d2) {
+      sout_s[src][d2] = r;
+      for (int e2 = 0; e2 < E; ++e2) r += Sv(src, e2, d2);
+    }
+  }
+  __syncthreads();
   for (int i = tid; i < E * G; i += blockDim.x) {
     const int e = i / G, dst = i % G;
-    // cum_split and send_base (this rank as sender)
+    // sender side (this rank)
     int cs = 0;
     for (int d2 = 0; d2 <= dst; ++d2) cs += Sv(me, e, d2);
     c->cum_split[e][dst] = cs;
-    int sb = 0;
-    for (int d2 = 0; d2 < dst; ++d2)
-      for (int e2 = 0; e2 < E; ++e2) sb += Sv(me, e2, d2);
+    int sb = sout_s[me][dst];
     for (int e2 = 0; e2 < e; ++e2) sb += Sv(me, e2, dst);
     c->send_base[e][dst] = sb;
-    // remote_base: first row of chunk (me, e) in dst's receive buffer
-    int rb = 0;
-    for (int e2 = 0; e2 < e; ++e2)
-      for (int s2 = 0; s2 < G; ++s2) rb += Sv(s2, e2, dst);
+    int rb = rin_s[dst][e];  // chunk (me, e) in dst's receive buffer: after lower sources
     for (int s2 = 0; s2 < me; ++s2) rb += Sv(s2, e, dst);
     c->remote_base[e][dst] = rb;
-    // receive side (this rank as dst), chunk of src = dst-index here
+    // receiver side (this rank), chunk of source `src`
     const int src = dst;
-    int cst = 0;
-    for (int e2 = 0; e2 < e; ++e2)
-      for (int s2 = 0; s2 < G; ++s2) cst += Sv(s2, e2, me);
+    int cst = rin_s[me][e];
     for (int s2 = 0; s2 < src; ++s2) cst += Sv(s2, e, me);
     c->chunk_start[e][src] = cst;
     c->chunk_len[e][src] = Sv(src, e, me);
-    // where that chunk goes back: src's send layout, position of (e, me)
-    int rs = 0;
-    for (int d2 = 0; d2 < me; ++d2)
-      for (int e2 = 0; e2 < E; ++e2) rs += Sv(src, e2, d2);
+    int rs = sout_s[src][me];  // where that chunk goes back in src's send layout
     for (int e2 = 0; e2 < e; ++e2) rs += Sv(src, e2, me);
     c->ret_start[e][src] = rs;
   }
+  for (int e = tid; e <= E; e += blockDim.x) c->group_offsets[e] = rin_s[me][e];
   if (tid == 0) {
-    int r = 0;
-    for (int e = 0; e < E; ++e) {
-      c->group_offsets[e] = r;
-      for (int s2 = 0; s2 < G; ++s2) r += Sv(s2, e, me);
-    }
-    c->group_offsets[E] = r;
+    const int r = rin_s[me][E];
     c->recv_total = r;
     if (r > c->recv_capacity) record_error(err, kErrCapacity);
     int snd = 0;
-    for (int e = 0; e < E; ++e)
-      for (int d2 = 0; d2 < G; ++d2) snd += Sv(me, e, d2);
+    for (int e2 = 0; e2 < E; ++e2)
+      for (int d2 = 0; d2 < G; ++d2) snd += Sv(me, e2, d2);
     if (snd > c->ret_capacity) record_error(err, kErrCapacity);
+  }
+  __syncthreads();
+  if (tid == 0) {
     __threadfence();
     *reinterpret_cast<volatile uint32_t*>(&c->epoch) = epoch;
   }
@@ -228,6 +240,43 @@ __global__ void __launch_bounds__(256) dispatch_kernel(dsca_ep_dispatch_args a, 
     }
   }
   signal_when_grid_done(c, &c->dispatch_done, kDispatch);
+}
+
+// ------------------------------------------------------------------ return kernel
+// Row r of this rank's receive layout (expert e, chunk of source src) goes to row
+// ret_start[e][src] + (r - chunk_start[e][src]) of src's return buffer; one warp per row, so each
+// NVLink store instruction writes 512 contiguous bytes.  The last CTA sets the return flags.
+template <int ESZ>
+__global__ void __launch_bounds__(256) return_kernel(Ctx* c, const char* y, int d, int32_t* err) {
+  const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int total = c->recv_total;
+  if (r < total) {
+    // expert: upper bound over group_offsets
+    int lo = 0, hi = c->E;
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (c->group_offsets[mid] <= r) lo = mid; else hi = mid;
+    }
+    const int e = lo;
+    char* dst = nullptr;
+    for (int src = 0; src < c->G; ++src) {
+      const int cs = c->chunk_start[e][src];
+      if (r >= cs && r < cs + c->chunk_len[e][src]) {
+        dst = c->ret[src] + (size_t)(c->ret_start[e][src] + r - cs) * d * ESZ;
+        break;
+      }
+    }
+    if (dst == nullptr) {
+      if (lane == 0) record_error(err, kErrIndex);
+    } else {
+      const uint4* s = reinterpret_cast<const uint4*>(y + (size_t)r * d * ESZ);
+      uint4* t = reinterpret_cast<uint4*>(dst);
+      const int nvec = d * ESZ / 16;
+      for (int v = lane; v < nvec; v += 32) t[v] = s[v];
+    }
+  }
+  signal_when_grid_done(c, &c->return_done, kReturn);
 }
 
 // ------------------------------------------------------------------ wait kernel
@@ -333,6 +382,21 @@ int dsca_ep_dispatch(const dsca_ep_dispatch_args* a, dsca_stream_t stream) {
     dsca::ep::dispatch_kernel<2><<<blocks, 256, 0, st>>>(*a, static_cast<Ctx*>(a->ctx));
   else
     dsca::ep::dispatch_kernel<4><<<blocks, 256, 0, st>>>(*a, static_cast<Ctx*>(a->ctx));
+  return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
+}
+
+int dsca_ep_return(void* ctx_dev, const void* y, int d, int dtype, int max_rows, int32_t* err, dsca_stream_t stream) {
+  if (ctx_dev == nullptr || y == nullptr || d <= 0 || max_rows < 0) return DSCA_ERR_BAD_ARG;
+  if (dtype != DSCA_BF16 && dtype != DSCA_F32) return DSCA_ERR_BAD_ARG;
+  const int esz = dtype == DSCA_BF16 ? 2 : 4;
+  if (((size_t)d * esz) % 16 != 0 || (reinterpret_cast<uintptr_t>(y) & 15u)) return DSCA_ERR_BAD_ARG;
+  // one warp per possible row (the actual count is on the device); >= 1 CTA so the flag is set
+  const int blocks = max(1, (int)(((long long)max_rows * 32 + 255) / 256));
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (esz == 2)
+    dsca::ep::return_kernel<2><<<blocks, 256, 0, st>>>(static_cast<Ctx*>(ctx_dev), static_cast<const char*>(y), d, err);
+  else
+    dsca::ep::return_kernel<4><<<blocks, 256, 0, st>>>(static_cast<Ctx*>(ctx_dev), static_cast<const char*>(y), d, err);
   return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
 }
 

@@ -178,7 +178,9 @@ __global__ void __launch_bounds__(kThreads) grouped_gemm_f32(const Params p) {
 }  // namespace simt
 
 int launch_grouped_ffn_f32(const dsca_ffn_args* f, int num_sms, cudaStream_t stream) {
-  const bool shared = f->shared_rows > 0;
+  const int segs = f->segments == 0 ? 3 : f->segments;
+  const bool shared = f->shared_rows > 0 && (segs & 2);
+  const bool routed = (segs & 1) != 0;
   const int grid = (f->num_ctas > 0 ? f->num_ctas : num_sms) * 4;
   const bool glu = f->act == DSCA_ACT_SWIGLU;
   const int phases = f->phases == 0 ? 3 : f->phases;
@@ -191,7 +193,7 @@ int launch_grouped_ffn_f32(const dsca_ffn_args* f, int num_sms, cudaStream_t str
     simt::Segment& s0 = p.seg[0];
     s0.group_offsets = f->group_offsets;
     s0.group_weight = f->group_weight;
-    s0.ngroups = f->num_groups;
+    s0.ngroups = routed ? f->num_groups : 0;
     s0.a = reinterpret_cast<const float*>(f->a);
     s0.lda = f->d;
     s0.b = reinterpret_cast<const float*>(f->w1);
@@ -229,7 +231,7 @@ int launch_grouped_ffn_f32(const dsca_ffn_args* f, int num_sms, cudaStream_t str
     simt::Segment& s0 = p.seg[0];
     s0.group_offsets = f->group_offsets;
     s0.group_weight = f->group_weight;
-    s0.ngroups = f->num_groups;
+    s0.ngroups = routed ? f->num_groups : 0;
     s0.a = reinterpret_cast<const float*>(f->h);
     s0.lda = f->ip;
     s0.b = reinterpret_cast<const float*>(f->w2);

@@ -456,8 +456,11 @@ static int launch_one(int epi, const CUtensorMap& a0, const CUtensorMap& b0, con
 
 int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t stream) {
   const int grid = f->num_ctas > 0 ? f->num_ctas : num_sms;
-  const bool shared = f->shared_rows > 0;
+  const int segs = f->segments == 0 ? 3 : f->segments;
+  const bool shared = f->shared_rows > 0 && (segs & 2);
+  const bool routed = (segs & 1) != 0;
   const int phases = f->phases == 0 ? 3 : f->phases;
+  if (!routed && !shared) return DSCA_OK;
   int rc;
   // ---- GEMM1: h = act(a . w1^T)   (+ hs = act(xs . ws1^T))
   if (phases & 1) {
@@ -479,7 +482,7 @@ int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t st
     gemm::Segment& s0 = p.seg[0];
     s0.group_offsets = f->group_offsets;
     s0.group_weight = f->group_weight;
-    s0.ngroups = f->num_groups;
+    s0.ngroups = routed ? f->num_groups : 0;
     s0.rows = 0;
     s0.n_tiles = f->n1p / gemm::BN;
     s0.b_rows_per_group = f->n1p;
@@ -520,12 +523,12 @@ int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t st
     p.epi = gemm::kEpiStore;
     p.err = f->err;
     p.nseg = shared ? 2 : 1;
-    p.ep_signal = static_cast<ep::Ctx*>(f->ep_ctx);
+    p.ep_signal = routed ? static_cast<ep::Ctx*>(f->ep_ctx) : nullptr;
     gemm::Segment& s0 = p.seg[0];
     s0.ep = static_cast<const ep::Ctx*>(f->ep_ctx);
     s0.group_offsets = f->group_offsets;
     s0.group_weight = f->group_weight;
-    s0.ngroups = f->num_groups;
+    s0.ngroups = routed ? f->num_groups : 0;
     s0.rows = 0;
     s0.n_tiles = f->dp / gemm::BN;
     s0.b_rows_per_group = f->dp;

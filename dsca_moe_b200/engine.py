@@ -273,6 +273,9 @@ class MoEEngine:
         # one GPU through the fused exchange path (the rank is its own only peer): exercises the
         # plan / dispatch / return kernels without a second GPU
         self.ep_loopback = False
+        # "overlap": routed GEMM2 stores locally and a return kernel sends the rows on a side
+        # stream beside the shared-expert GEMM2; "fused": GEMM2's epilogue stores them remotely
+        self.ep_return = "overlap"
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._ws = {}
         self.last_plan = None
@@ -355,7 +358,8 @@ class MoEEngine:
         else:
             self._ffn_call(x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, 3, ep_ctx)
 
-    def _ffn_call(self, x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, phases, ep_ctx=None):
+    def _ffn_call(self, x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, phases, ep_ctx=None,
+                  segments=3):
         pe = self.experts
         f = L.FfnArgs()
         f.dtype, f.act, f.d = _dt(self.dtype), pe.act, self.d
@@ -368,6 +372,7 @@ class MoEEngine:
             f.xs, f.ws1, f.ws2, f.hs, f.ys = _ptr(x), _ptr(pe.ws1), _ptr(pe.ws2), _ptr(ws["hs"]), _ptr(ws["ys"])
         f.err, f.num_ctas, f.phases = _ptr(self.err), self.num_ctas, phases
         f.ep_ctx = _ptr(ep_ctx)
+        f.segments = segments
         L.call("dsca_grouped_ffn", ctypes.byref(f), _stream())
 
     def _combine(self, ws, y, rows):
@@ -479,30 +484,66 @@ class MoEEngine:
             recv=_DevPtr.tensor(region.value + off_recv, (recv_cap, d), dt, dev),
             ret=_DevPtr.tensor(region.value + off_ret, (ret_cap, d), dt, dev),
             h=torch.empty(recv_cap, self.experts.ip, dtype=dt, device=dev),
+            y=torch.empty(recv_cap, d, dtype=dt, device=dev),
+            side=torch.cuda.Stream(device=dev),
             group_offsets=int(lib.dsca_ep_group_offsets(_ptr(ctx)) or 0),
             bytes=total)
 
     def _forward_p2p(self, x, ws):
+        """Main stream: plan -> shared GEMM1 -> [dispatch done] routed GEMM1 -> routed GEMM2 ->
+        shared GEMM2 -> [return done] combine.  Side stream: dispatch (beside the shared GEMM1)
+        and the return kernel (beside the shared GEMM2).  ep_return = "fused" instead stores
+        GEMM2's routed rows straight into the source ranks from its epilogue."""
         T = x.shape[0]
         if self._ep is None:
             self._p2p_setup(T)
         ep = self._ep
         if T > ep["T_cap"]:
             raise RuntimeError(f"{T} tokens exceed the reserved {ep['T_cap']} per rank (call reserve())")
-        lib, st, ctx = L.load(), _stream(), _ptr(ep["ctx"])
-        L.check(lib.dsca_ep_plan(ctx, _ptr(ws["counts"]), self.wait_limit_ns, _ptr(self.err), st), "dsca_ep_plan")
+        lib, ctx, err = L.load(), _ptr(ep["ctx"]), _ptr(self.err)
+        main, side = torch.cuda.current_stream(), ep["side"]
+        L.check(lib.dsca_ep_plan(ctx, _ptr(ws["counts"]), self.wait_limit_ns, err, _stream()), "dsca_ep_plan")
         self._mark("plan")
-        a = L.EpDispatchArgs()
-        a.x, a.T, a.d, a.top_k, a.dtype = _ptr(x), T, self.d, self.top_k, _dt(self.dtype)
-        a.topk_ids, a.local_rank, a.block_base = _ptr(ws["topk_ids"]), _ptr(ws["local_rank"]), _ptr(ws["block_base"])
-        a.ctx, a.token_row, a.err = ctx, _ptr(ws["token_row"]), _ptr(self.err)
-        L.call("dsca_ep_dispatch", ctypes.byref(a), st)
-        self._mark("dispatch")
-        L.check(lib.dsca_ep_wait(ctx, 1, self.wait_limit_ns, _ptr(self.err), st), "dsca_ep_wait")
+        planned = torch.cuda.Event()
+        planned.record(main)
+        side.wait_event(planned)
+        with torch.cuda.stream(side):
+            a = L.EpDispatchArgs()
+            a.x, a.T, a.d, a.top_k, a.dtype = _ptr(x), T, self.d, self.top_k, _dt(self.dtype)
+            a.topk_ids, a.local_rank = _ptr(ws["topk_ids"]), _ptr(ws["local_rank"])
+            a.block_base, a.ctx, a.token_row, a.err = _ptr(ws["block_base"]), ctx, _ptr(ws["token_row"]), err
+            L.call("dsca_ep_dispatch", ctypes.byref(a), _stream())
+            dispatched = torch.cuda.Event()
+            dispatched.record(side)
+        args = (x, ws, ep["recv"], ep["h"], ep["y"], ep["recv_cap"], self.E, ep["group_offsets"], None)
+        has_shared = self.experts.ws1 is not None
+        if has_shared:
+            self._ffn_call(*args, 1, segments=2)
+            self._mark("gemm1_shared")
+        main.wait_event(dispatched)
+        L.check(lib.dsca_ep_wait(ctx, 1, self.wait_limit_ns, err, _stream()), "dsca_ep_wait")
         self._mark("wait_dispatch")
-        self._ffn(x, ws, ep["recv"], ep["h"], ep["recv"], ep["recv_cap"], self.E, ep["group_offsets"], None,
-                  ep_ctx=ep["ctx"])
-        L.check(lib.dsca_ep_wait(ctx, 2, self.wait_limit_ns, _ptr(self.err), st), "dsca_ep_wait")
+        self._ffn_call(*args, 1, segments=1)
+        self._mark("gemm1_routed")
+        if self.ep_return == "fused":
+            self._ffn_call(*args, 2, ep_ctx=ep["ctx"], segments=3)
+            self._mark("gemm2_fused")
+        else:
+            self._ffn_call(*args, 2, segments=1)
+            self._mark("gemm2_routed")
+            computed = torch.cuda.Event()
+            computed.record(main)
+            side.wait_event(computed)
+            with torch.cuda.stream(side):
+                L.check(lib.dsca_ep_return(ctx, _ptr(ep["y"]), self.d, _dt(self.dtype), ep["recv_cap"], err,
+                                           _stream()), "dsca_ep_return")
+                returned = torch.cuda.Event()
+                returned.record(side)
+            if has_shared:
+                self._ffn_call(*args, 2, segments=2)
+                self._mark("gemm2_shared")
+            main.wait_event(returned)
+        L.check(lib.dsca_ep_wait(ctx, 2, self.wait_limit_ns, err, _stream()), "dsca_ep_wait")
         self._mark("wait_return")
         self._combine(ws, ep["ret"], ep["ret_cap"])
         self._mark("combine")

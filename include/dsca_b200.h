@@ -182,6 +182,7 @@ typedef struct {
   void* ep_ctx;               /* expert-parallel context (dsca_ep_init), or NULL: when set, GEMM2
                                  stores each routed output row straight into the return buffer of
                                  the rank that sent it and sets that rank's return flag */
+  int segments;               /* 0 or 3 = routed and shared; 1 = routed only; 2 = shared only */
 } dsca_ffn_args;
 DSCA_API int dsca_grouped_ffn(const dsca_ffn_args* a, dsca_stream_t stream);
 
@@ -295,6 +296,12 @@ typedef struct {
 } dsca_ep_dispatch_args;
 DSCA_API int dsca_ep_dispatch(const dsca_ep_dispatch_args* a, dsca_stream_t stream);
 DSCA_API int dsca_ep_wait(void* ctx_dev, int kind, uint64_t limit_ns, int32_t* err, dsca_stream_t stream);
+/* Return path as its own kernel (when GEMM2 stored routed rows locally into y [rows, d]): row r
+ * of this rank's receive layout is stored into its source rank's return buffer, one warp per row
+ * (contiguous 512-byte NVLink stores), then the return flag is set at every peer.  max_rows
+ * bounds the launch (the receive capacity); the row count itself is read on the device. */
+DSCA_API int dsca_ep_return(void* ctx_dev, const void* y, int d, int dtype, int max_rows, int32_t* err,
+                            dsca_stream_t stream);
 /* The device harmony plan on its own (test hook): meta, e2g, S are device arrays. */
 DSCA_API int dsca_ep_plan_eval(const int32_t* meta, int G, int E, const int32_t* expert_to_gpu,
                                int eq_tokens, int32_t* S, dsca_stream_t stream);

@@ -75,7 +75,7 @@ def main():
     results = []
     uneven60 = np.array([min(world - 1, (e * world * world) // (60 * (world + 1))) for e in range(60)], np.int32)
     cases = []
-    for exchange in ("p2p", "nccl"):
+    for exchange in ("p2p", "p2p-fused", "nccl"):
         cases += [
             (f"qwen contiguous, harmony, {exchange}", case_qwen, None, 150, exchange),
             (f"qwen contiguous, fixed, {exchange}", case_qwen, None, -1, exchange),
@@ -84,7 +84,8 @@ def main():
         ]
     ok = True
     for name, fn, e2g, eq, exchange in cases:
-        ep, one, x = fn(rank, world, dev, group, e2g, eq, exchange)
+        ep, one, x = fn(rank, world, dev, group, e2g, eq, "nccl" if exchange == "nccl" else "p2p")
+        ep.ep_return = "fused" if exchange == "p2p-fused" else "overlap"
         for it in range(3):
             r_ep = ep.forward(x)
             r_one = one.forward(x)

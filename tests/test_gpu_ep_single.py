@@ -68,8 +68,10 @@ def _qwen_pair(dev, T=384, d=512, E=60, I=128, Is=256):
     return loop, local, x
 
 
-def test_p2p_loopback_equals_local_path(lib, cuda):
+@pytest.mark.parametrize("ret_mode", ["overlap", "fused"])
+def test_p2p_loopback_equals_local_path(lib, cuda, ret_mode):
     loop, local, x = _qwen_pair(cuda)
+    loop.ep_return = ret_mode
     try:
         for it in range(3):  # successive epochs reuse the region
             a = loop.forward(x)
