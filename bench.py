@@ -53,6 +53,9 @@ def parse():
     ap.add_argument("--eq-tokens", type=int, default=150)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="expert-parallel exchange: fused NVLink kernels (default) or the NCCL baseline")
+    ap.add_argument("--ep-return", choices=["overlap", "fused"], default="overlap")
     ap.add_argument("--once", action="store_true",
                     help="one untimed forward of the workload and exit (the case profiled under ncu)")
     return ap.parse_args()
@@ -312,6 +315,8 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
         group = dist.group.WORLD
     eng, x, Wr, raw, info = build_block(w, T, rank, world, dev, args.eq_tokens, group)
+    eng.exchange = args.exchange
+    eng.ep_return = args.ep_return
     peaks = load_peaks()
     if args.once:
         eng.forward(x)
@@ -457,7 +462,8 @@ def main():
                        "placement": "contiguous (60 on 8 = 4x8 + 4x7)" if w["E"] % max(world, 1) else "contiguous",
                        "plan": f"harmony eq_tokens={args.eq_tokens}" if world > 1 else "local",
                        "l2": "flushed (256 MiB write, untimed) before every timed step",
-                       "parallelism": f"ep{world}"},
+                       "parallelism": f"ep{world}",
+                       "exchange": (f"{args.exchange} (return {args.ep_return})" if world > 1 else "none")},
             "roofline": roof, "layer_roofline": layer_roof, "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * w["d"] * 2,
                     "d2h_bytes_per_step": T * w["d"] * 2},
