@@ -367,6 +367,7 @@ def main():
 
     # ---- per-kernel phases (separate profiled steps with event markers between launches)
     eng.markers = []
+    eng.side_markers = []
     phase_ms = {}
     prof_steps = 10
     for _ in range(prof_steps):
@@ -382,6 +383,9 @@ def main():
         seq.append((marks[i][0], marks[i - 1][1].elapsed_time(marks[i][1])))
     for name, ms in seq:
         phase_ms.setdefault(name, []).append(ms)
+    # side-stream kernels (expert parallel: dispatch, return) overlap the main-stream phases
+    for name, a, b in eng.side_markers:
+        phase_ms.setdefault("side_" + name, []).append(a.elapsed_time(b))
     phase_ms = {k: statistics.mean(v) for k, v in phase_ms.items()}
 
     # ---- end to end through the public API with host buffers

@@ -234,8 +234,7 @@ __global__ void __launch_bounds__(256) dispatch_kernel(dsca_ep_dispatch_args a, 
         const size_t row_bytes = (size_t)a.d * ESZ;
         const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(a.x) + (size_t)t * row_bytes);
         uint4* dp = reinterpret_cast<uint4*>(c->recv[dst] + (size_t)rrow * row_bytes);
-        const int nvec = (int)(row_bytes / 16);
-        for (int v = lane; v < nvec; v += 32) dp[v] = src[v];
+        warp_copy_row(dp, src, (int)(row_bytes / 16), lane);
       }
     }
   }
@@ -272,8 +271,7 @@ __global__ void __launch_bounds__(256) return_kernel(Ctx* c, const char* y, int 
     } else {
       const uint4* s = reinterpret_cast<const uint4*>(y + (size_t)r * d * ESZ);
       uint4* t = reinterpret_cast<uint4*>(dst);
-      const int nvec = d * ESZ / 16;
-      for (int v = lane; v < nvec; v += 32) t[v] = s[v];
+      warp_copy_row(t, s, d * ESZ / 16, lane);
     }
   }
   signal_when_grid_done(c, &c->return_done, kReturn);

@@ -61,6 +61,21 @@ __device__ __forceinline__ bool wait_flag(const uint32_t* p, uint32_t v, uint64_
   }
 }
 
+// Copy one row of nvec 16-byte vectors with a warp (lane-strided, so each store instruction
+// covers 512 contiguous bytes), eight loads in flight per lane before the stores go out.
+__device__ __forceinline__ void warp_copy_row(uint4* __restrict__ dst, const uint4* __restrict__ src, int nvec,
+                                              int lane) {
+  int v = lane;
+  for (; v + 7 * 32 < nvec; v += 8 * 32) {
+    uint4 r[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) r[i] = src[v + 32 * i];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dst[v + 32 * i] = r[i];
+  }
+  for (; v < nvec; v += 32) dst[v] = src[v];
+}
+
 // Last-CTA-done signal: every thread fences its own stores (system scope), the CTA counts
 // itself in; the last CTA tells every peer (flag kind `kind`, value = epoch) and resets the
 // counter for the next forward.  Called by every thread of the CTA.

@@ -281,13 +281,26 @@ class MoEEngine:
         self.last_plan = None
         self.last_layout = None
         # when a list, forward() appends (name, cuda.Event) markers between its kernel launches
+        # (and (name, start, end) of side-stream kernels to side_markers)
         self.markers = None
+        self.side_markers = []
 
     def _mark(self, name: str):
         if self.markers is not None:
             ev = torch.cuda.Event(enable_timing=True)
             ev.record()
             self.markers.append((name, ev))
+
+    def _side_mark(self, name: str | None = None, start=None):
+        """Timing of a side-stream kernel: call once before (returns the start event) and once
+        after with its name; pairs land in side_markers when profiling is on."""
+        if self.markers is None:
+            return None
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        if name is not None and start is not None:
+            self.side_markers.append((name, start, ev))
+        return ev
 
     # -------------------------------------------------------------- workspace
     def _workspace(self, T: int) -> dict:
@@ -508,11 +521,13 @@ class MoEEngine:
         planned.record(main)
         side.wait_event(planned)
         with torch.cuda.stream(side):
+            t0 = self._side_mark()
             a = L.EpDispatchArgs()
             a.x, a.T, a.d, a.top_k, a.dtype = _ptr(x), T, self.d, self.top_k, _dt(self.dtype)
             a.topk_ids, a.local_rank = _ptr(ws["topk_ids"]), _ptr(ws["local_rank"])
             a.block_base, a.ctx, a.token_row, a.err = _ptr(ws["block_base"]), ctx, _ptr(ws["token_row"]), err
             L.call("dsca_ep_dispatch", ctypes.byref(a), _stream())
+            self._side_mark("dispatch", t0)
             dispatched = torch.cuda.Event()
             dispatched.record(side)
         args = (x, ws, ep["recv"], ep["h"], ep["y"], ep["recv_cap"], self.E, ep["group_offsets"], None)
@@ -535,8 +550,10 @@ class MoEEngine:
             computed.record(main)
             side.wait_event(computed)
             with torch.cuda.stream(side):
+                t0 = self._side_mark()
                 L.check(lib.dsca_ep_return(ctx, _ptr(ep["y"]), self.d, _dt(self.dtype), ep["recv_cap"], err,
                                            _stream()), "dsca_ep_return")
+                self._side_mark("return", t0)
                 returned = torch.cuda.Event()
                 returned.record(side)
             if has_shared:
