@@ -56,6 +56,10 @@ def parse():
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="expert-parallel exchange: fused NVLink kernels (default) or the NCCL baseline")
     ap.add_argument("--ep-return", choices=["overlap", "fused"], default="overlap")
+    ap.add_argument("--fp8", action="store_true",
+                    help="fp8-e4m3 expert weights with per-output-channel scales (bf16 activations)")
+    ap.add_argument("--router", choices=["zipf", "uniform"], default="zipf",
+                    help="zipf: rows scaled for the workload's Zipf top-1 loads; uniform: unscaled N(0,1/d) router")
     ap.add_argument("--once", action="store_true",
                     help="one untimed forward of the workload and exit (the case profiled under ncu)")
     return ap.parse_args()
@@ -181,12 +185,12 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows), "power_w_max": max(pw) if pw else None}
 
 
-def build_block(w, T, rank, world, dev, eq_tokens, group=None):
+def build_block(w, T, rank, world, dev, eq_tokens, group=None, fp8=False):
     import torch
 
     from dsca_moe_b200 import _lib as L
     from dsca_moe_b200 import synthetic as syn
-    from dsca_moe_b200.engine import MoEEngine, pack_relu, pack_swiglu
+    from dsca_moe_b200.engine import MoEEngine, pack_relu, pack_swiglu, quantize_fp8
 
     d, E, I, Is = w["d"], w["E"], w["inter"], w["shared"]
     Wr, info = syn.router_weight(E, d, 1234, zipf_s=w["zipf"], dtype="bf16")
@@ -202,6 +206,8 @@ def build_block(w, T, rank, world, dev, eq_tokens, group=None):
         sgw = syn.bf16_round(syn.rng(99).standard_normal((1, d)).astype(np.float32) / np.sqrt(d))
         pe = pack_swiglu(raw["gate"], raw["up"], raw["down"], shared=(raw["s_gate"], raw["s_up"], raw["s_down"]),
                          device=dev)
+        if fp8:
+            pe = quantize_fp8(pe)
         raw["s_gate_w"] = sgw
         eng = MoEEngine(torch.from_numpy(Wr).to(dev, torch.bfloat16), pe, top_k=w["k"],
                         route_mode=L.ROUTE_SOFTMAX_TOPK,
@@ -210,6 +216,8 @@ def build_block(w, T, rank, world, dev, eq_tokens, group=None):
     else:
         raw = dict(wi=n(E, I, d), wo=n(E, d, I))
         pe = pack_relu(raw["wi"], raw["wo"], device=dev)
+        if fp8:
+            pe = quantize_fp8(pe)
         eng = MoEEngine(torch.from_numpy(Wr).to(dev, torch.bfloat16), pe, top_k=1, route_mode=L.ROUTE_SWITCH_TOP1,
                         rank=rank, world=world, group=group, eq_tokens=eq_tokens)
     x = torch.from_numpy(syn.hidden_states(T, d, 5000 + rank, "bf16")).to(dev, torch.bfloat16)
@@ -314,7 +322,9 @@ def main():
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
         group = dist.group.WORLD
-    eng, x, Wr, raw, info = build_block(w, T, rank, world, dev, args.eq_tokens, group)
+    if args.router == "uniform":
+        w["zipf"] = None
+    eng, x, Wr, raw, info = build_block(w, T, rank, world, dev, args.eq_tokens, group, fp8=args.fp8)
     eng.exchange = args.exchange
     eng.ep_return = args.ep_return
     peaks = load_peaks()
@@ -462,7 +472,9 @@ def main():
             "data": "synthetic",
             "config": {"workload": w["name"], "tokens_per_gpu": T, "batch_x_seq": "16x256" if T == 4096 else str(T),
                        "d_model": w["d"], "experts": w["E"], "expert_inter": w["inter"], "shared_inter": w["shared"],
-                       "top_k": w["k"], "router": f"zipf{w['zipf']} (calibrated top-1)",
+                       "top_k": w["k"],
+                       "router": (f"zipf{w['zipf']} (calibrated top-1)" if w["zipf"] else "uniform (unscaled)"),
+                       "expert_weights": "fp8-e4m3 + per-channel fp32 scales (f16 MMA operands)" if args.fp8 else "bf16",
                        "placement": "contiguous (60 on 8 = 4x8 + 4x7)" if w["E"] % max(world, 1) else "contiguous",
                        "plan": f"harmony eq_tokens={args.eq_tokens}" if world > 1 else "local",
                        "l2": "flushed (256 MiB write, untimed) before every timed step",

@@ -41,7 +41,7 @@ class PermuteArgs(ctypes.Structure):
     _fields_ = [("x", _vp), ("T", _i), ("d", _i), ("E", _i), ("top_k", _i), ("dtype", _i),
                 ("topk_ids", _vp), ("local_rank", _vp), ("block_base", _vp), ("offsets", _vp),
                 ("G", _i), ("cum_split", _vp), ("dest_base", _vp), ("capacity", _i), ("out", _vp),
-                ("token_row", _vp), ("err", _vp)]
+                ("token_row", _vp), ("err", _vp), ("out_f16", _i), ("x_f16", _vp)]
 
 
 class FfnArgs(ctypes.Structure):
@@ -50,7 +50,8 @@ class FfnArgs(ctypes.Structure):
                 ("num_experts_w", _i), ("capacity", _i), ("a", _vp), ("w1", _vp), ("w2", _vp),
                 ("h", _vp), ("y", _vp), ("shared_rows", _i), ("shared_n1p", _i), ("shared_ip", _i),
                 ("xs", _vp), ("ws1", _vp), ("ws2", _vp), ("hs", _vp), ("ys", _vp), ("err", _vp),
-                ("num_ctas", _i), ("phases", _i), ("ep_ctx", _vp), ("segments", _i)]
+                ("num_ctas", _i), ("phases", _i), ("ep_ctx", _vp), ("segments", _i),
+                ("w1_scale", _vp), ("w2_scale", _vp), ("ws1_scale", _vp), ("ws2_scale", _vp)]
 
 
 MAX_GPUS = 8

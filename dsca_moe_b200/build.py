@@ -25,8 +25,8 @@ NVCC = shutil.which("nvcc") or os.path.join(CUDA_HOME, "bin", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
               "--expt-relaxed-constexpr", "-I" + INCLUDE] + ARCH
-CU_SOURCES = ["router.cu", "dispatch.cu", "gemm_sm100.cu", "gemm_simt.cu", "abi.cu", "ffn_static_scratch.cu",
-              "ep.cu"]
+CU_SOURCES = ["router.cu", "dispatch.cu", "gemm_sm100.cu", "gemm_sm100_fp8.cu", "gemm_simt.cu", "abi.cu",
+              "ffn_static_scratch.cu", "ep.cu"]
 CXX_SOURCES = ["plan.cpp"]
 
 

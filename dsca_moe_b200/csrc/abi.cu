@@ -12,6 +12,7 @@ int launch_permute(const dsca_permute_args* a, cudaStream_t stream);
 int launch_combine(const dsca_combine_args* a, cudaStream_t stream);
 int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t stream);
 int launch_grouped_ffn_f32(const dsca_ffn_args* f, int num_sms, cudaStream_t stream);
+int launch_grouped_ffn_fp8(const dsca_ffn_args* f, int num_sms, cudaStream_t stream);
 }  // namespace dsca
 
 namespace {
@@ -145,6 +146,16 @@ int dsca_grouped_ffn(const dsca_ffn_args* f, dsca_stream_t stream) {
     for (const void* p : ptrs)
       if (!aligned16(p)) return DSCA_ERR_BAD_ARG;
     return dsca::launch_grouped_ffn_bf16(f, num_sms, st);
+  }
+  if (f->dtype == DSCA_F8E4M3) {
+    if (major != 10) return DSCA_ERR_UNSUPPORTED;
+    if (f->ep_ctx != nullptr) return DSCA_ERR_UNSUPPORTED;  // fused return epilogue: bf16 path only
+    if (f->d < 64 || f->w1_scale == nullptr || f->w2_scale == nullptr) return DSCA_ERR_BAD_ARG;
+    if (f->shared_rows > 0 && (f->ws1_scale == nullptr || f->ws2_scale == nullptr)) return DSCA_ERR_BAD_ARG;
+    const void* ptrs[] = {f->a, f->w1, f->w2, f->h, f->y};
+    for (const void* p : ptrs)
+      if (!aligned16(p)) return DSCA_ERR_BAD_ARG;
+    return dsca::launch_grouped_ffn_fp8(f, num_sms, st);
   }
   if (f->dtype == DSCA_F32) {
     if (f->ep_ctx != nullptr) return DSCA_ERR_UNSUPPORTED;  // the fused return path is bf16 only

@@ -110,7 +110,29 @@ __global__ void __launch_bounds__(256) permute_kernel(dsca_permute_args a) {
   const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(a.x) + (size_t)t * row_bytes);
   uint4* dstp = reinterpret_cast<uint4*>(reinterpret_cast<char*>(a.out) + (size_t)row * row_bytes);
   const int nvec = (int)(row_bytes / 16);
-  for (int v = lane; v < nvec; v += 32) dstp[v] = src[v];
+  if (ESZ == 2 && a.out_f16) {
+    // bf16 -> f16 on the way (operand of the fp8-weight FFN); the f16 copy of x for the shared
+    // expert is written once per token, by its slot-0 warp
+    uint4* xh = (a.x_f16 != nullptr && (w % a.top_k) == 0)
+                    ? reinterpret_cast<uint4*>(reinterpret_cast<char*>(a.x_f16) + (size_t)t * row_bytes)
+                    : nullptr;
+    for (int v = lane; v < nvec; v += 32) {
+      const uint4 u = src[v];
+      const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);
+      uint4 o;
+      uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(b[i]);
+        __half2 h = __floats2half2_rn(f.x, f.y);
+        op[i] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      dstp[v] = o;
+      if (xh != nullptr) xh[v] = o;
+    }
+  } else {
+    for (int v = lane; v < nvec; v += 32) dstp[v] = src[v];
+  }
 }
 
 int launch_permute(const dsca_permute_args* a, cudaStream_t stream) {

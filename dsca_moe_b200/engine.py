@@ -85,10 +85,67 @@ class PackedExperts:
     s_inter: int = 0
     s_n1p: int = 0
     s_ip: int = 0
+    # fp8-e4m3 weights: per packed-row (output channel) fp32 scales, weights = q * scale
+    w1_scale: torch.Tensor | None = None
+    w2_scale: torch.Tensor | None = None
+    ws1_scale: torch.Tensor | None = None
+    ws2_scale: torch.Tensor | None = None
+
+    @property
+    def fp8(self) -> bool:
+        return self.w1.dtype == torch.float8_e4m3fn
 
     @property
     def dtype(self):
-        return self.w1.dtype
+        """Activation dtype of the block (bf16 for fp8 weights)."""
+        return torch.bfloat16 if self.fp8 else self.w1.dtype
+
+
+def _quant_rows(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-row (output channel) e4m3 quantisation: scale = amax / 448, q = rne_e4m3(w / scale)."""
+    wf = w.float()
+    amax = wf.abs().amax(dim=-1, keepdim=True)
+    scale = torch.where(amax > 0, amax / 448.0, torch.ones_like(amax))
+    q = (wf / scale).to(torch.float8_e4m3fn)
+    return q.contiguous(), scale.squeeze(-1).contiguous()
+
+
+def quantize_fp8(pe: PackedExperts) -> PackedExperts:
+    """fp8-e4m3 copy of packed expert weights with per-output-channel fp32 scales."""
+    w1, s1 = _quant_rows(pe.w1)
+    w2, s2 = _quant_rows(pe.w2)
+    out = PackedExperts(act=pe.act, d=pe.d, inter=pe.inter, E=pe.E, w1=w1, w2=w2, n1p=pe.n1p, ip=pe.ip, dp=pe.dp,
+                        s_inter=pe.s_inter, s_n1p=pe.s_n1p, s_ip=pe.s_ip, w1_scale=s1, w2_scale=s2)
+    if pe.ws1 is not None:
+        out.ws1, out.ws1_scale = _quant_rows(pe.ws1)
+        out.ws2, out.ws2_scale = _quant_rows(pe.ws2)
+    return out
+
+
+def dequantize_fp8(pe: PackedExperts) -> PackedExperts:
+    """The weights an fp8 block computes with (q * scale), as a float32 PackedExperts."""
+    f = PackedExperts(act=pe.act, d=pe.d, inter=pe.inter, E=pe.E,
+                      w1=pe.w1.float() * pe.w1_scale[..., None], w2=pe.w2.float() * pe.w2_scale[..., None],
+                      n1p=pe.n1p, ip=pe.ip, dp=pe.dp, s_inter=pe.s_inter, s_n1p=pe.s_n1p, s_ip=pe.s_ip)
+    if pe.ws1 is not None:
+        f.ws1 = pe.ws1.float() * pe.ws1_scale[..., None]
+        f.ws2 = pe.ws2.float() * pe.ws2_scale[..., None]
+    return f
+
+
+def unpack_swiglu(pe: PackedExperts):
+    """Inverse of pack_swiglu on float weights: (gate [E,I,d], up [E,I,d], down [E,d,I], shared)."""
+    E, I, d, ip = pe.E, pe.inter, pe.d, pe.ip
+    w = pe.w1.float().view(E, ip // 128, 2, 128, d)
+    gate = w[:, :, 0].reshape(E, ip, d)[:, :I]
+    up = w[:, :, 1].reshape(E, ip, d)[:, :I]
+    down = pe.w2.float()[:, :d, :I]
+    shared = None
+    if pe.ws1 is not None:
+        sip, Is = pe.s_ip, pe.s_inter
+        s = pe.ws1.float().view(sip // 128, 2, 128, d)
+        shared = (s[:, 0].reshape(sip, d)[:Is], s[:, 1].reshape(sip, d)[:Is], pe.ws2.float()[:d, :Is])
+    return gate, up, down, shared
 
 
 def _pack_glu_w1(gate: torch.Tensor, up: torch.Tensor) -> tuple[torch.Tensor, int]:
@@ -246,7 +303,10 @@ class MoEEngine:
             raise RuntimeError("the bf16 expert path needs an sm_100 (B200) GPU")
         self.num_sms = n_sms.value
         self.experts = experts
-        self.dtype = experts.dtype
+        self.dtype = experts.dtype  # activation dtype (bf16 for fp8 weights)
+        self.op_dtype = torch.float16 if experts.fp8 else self.dtype  # FFN operand dtype
+        if experts.fp8 and world > 1:
+            raise NotImplementedError("fp8 expert weights run on one GPU in this build")
         self.device = experts.w1.device
         self.router_weight = router_weight.to(device=self.device, dtype=self.dtype).contiguous()
         self.E, self.d = self.router_weight.shape
@@ -320,12 +380,14 @@ class MoEEngine:
             offsets=torch.empty(E + 1, dtype=torch.int32, device=dev),
             block_base=torch.empty(max(nb, 1), E, dtype=torch.int32, device=dev),
             token_row=torch.empty(T, k, dtype=torch.int32, device=dev),
-            hs=torch.empty(T, pe.s_ip, dtype=dt, device=dev) if pe.ws1 is not None else None,
+            # fp8 weights: the FFN operands (rows, shared input, intermediates) are f16
+            hs=torch.empty(T, pe.s_ip, dtype=self.op_dtype, device=dev) if pe.ws1 is not None else None,
             ys=torch.empty(T, d, dtype=dt, device=dev) if pe.ws1 is not None else None,
+            x_f16=torch.empty(T, d, dtype=torch.float16, device=dev) if (pe.fp8 and pe.ws1 is not None) else None,
         )
         if self.world == 1:
-            ws.update(a=torch.empty(cap, d, dtype=dt, device=dev),
-                      h=torch.empty(cap, pe.ip, dtype=dt, device=dev),
+            ws.update(a=torch.empty(cap, d, dtype=self.op_dtype, device=dev),
+                      h=torch.empty(cap, pe.ip, dtype=self.op_dtype, device=dev),
                       y=torch.empty(cap, d, dtype=dt, device=dev))
         self._ws = {T: ws}  # keep one shape resident
         return ws
@@ -359,6 +421,8 @@ class MoEEngine:
         p.offsets = _ptr(ws["offsets"])
         p.G, p.cum_split, p.dest_base = G, _ptr(cum_split), _ptr(dest_base)
         p.capacity, p.out, p.token_row, p.err = capacity, _ptr(out), _ptr(ws["token_row"]), _ptr(self.err)
+        p.out_f16 = int(self.experts.fp8)
+        p.x_f16 = _ptr(ws.get("x_f16"))
         L.call("dsca_permute", ctypes.byref(p), _stream())
 
     def _ffn(self, x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, ep_ctx=None):
@@ -375,14 +439,18 @@ class MoEEngine:
                   segments=3):
         pe = self.experts
         f = L.FfnArgs()
-        f.dtype, f.act, f.d = _dt(self.dtype), pe.act, self.d
+        f.dtype, f.act, f.d = (L.F8E4M3 if pe.fp8 else _dt(self.dtype)), pe.act, self.d
         f.n1p, f.ip, f.dp = pe.n1p, pe.ip, pe.dp
         f.num_groups, f.group_offsets, f.group_weight = num_groups, _ptr(group_offsets), _ptr(group_weight)
         f.num_experts_w, f.capacity = pe.E, capacity
         f.a, f.w1, f.w2, f.h, f.y = _ptr(a), _ptr(pe.w1), _ptr(pe.w2), _ptr(h), _ptr(y)
         if pe.ws1 is not None:
+            xs = ws["x_f16"] if pe.fp8 else x
             f.shared_rows, f.shared_n1p, f.shared_ip = x.shape[0], pe.s_n1p, pe.s_ip
-            f.xs, f.ws1, f.ws2, f.hs, f.ys = _ptr(x), _ptr(pe.ws1), _ptr(pe.ws2), _ptr(ws["hs"]), _ptr(ws["ys"])
+            f.xs, f.ws1, f.ws2, f.hs, f.ys = _ptr(xs), _ptr(pe.ws1), _ptr(pe.ws2), _ptr(ws["hs"]), _ptr(ws["ys"])
+        if pe.fp8:
+            f.w1_scale, f.w2_scale = _ptr(pe.w1_scale), _ptr(pe.w2_scale)
+            f.ws1_scale, f.ws2_scale = _ptr(pe.ws1_scale), _ptr(pe.ws2_scale)
         f.err, f.num_ctas, f.phases = _ptr(self.err), self.num_ctas, phases
         f.ep_ctx = _ptr(ep_ctx)
         f.segments = segments

@@ -133,6 +133,8 @@ typedef struct {
   void* out;                  /* [capacity, d] */
   int32_t* token_row;         /* [T, k] row written for (t, j) */
   int32_t* err;               /* device error word */
+  int out_f16;                /* bf16 input: write the rows as f16 (fp8-weight FFN operand) */
+  void* x_f16;                /* [T, d] f16 copy of x (shared-expert operand), or NULL */
 } dsca_permute_args;
 DSCA_API int dsca_permute(const dsca_permute_args* a, dsca_stream_t stream);
 
@@ -183,6 +185,13 @@ typedef struct {
                                  stores each routed output row straight into the return buffer of
                                  the rank that sent it and sets that rank's return flag */
   int segments;               /* 0 or 3 = routed and shared; 1 = routed only; 2 = shared only */
+  /* dtype = DSCA_F8E4M3: w1 / w2 / ws1 / ws2 hold e4m3 bytes and these per-output-channel fp32
+     scales (one per packed weight row: [E * n1p], [E * dp], [shared_n1p], [dp]); a, xs, h and hs
+     are f16 (e4m3 converts exactly to f16 for the kind::f16 MMA), y and ys bf16. */
+  const float* w1_scale;
+  const float* w2_scale;
+  const float* ws1_scale;
+  const float* ws2_scale;
 } dsca_ffn_args;
 DSCA_API int dsca_grouped_ffn(const dsca_ffn_args* a, dsca_stream_t stream);
 

@@ -1,0 +1,86 @@
+"""fp8-e4m3 expert weights with per-output-channel fp32 scales: the block (f16 operands, fp32
+accumulation, scales in the epilogue) against the fp32 oracle run on the dequantised weights
+(q * scale) and the same inputs — 2e-2 max relative error.  Routing is unchanged by the weight
+format and stays bit-exact."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from dsca_moe_b200 import synthetic as syn
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+
+
+def _qwen(dev, T, d, E, I, Is, seed):
+    from dsca_moe_b200 import _lib as L
+    from dsca_moe_b200.engine import MoEEngine, dequantize_fp8, pack_swiglu, quantize_fp8, unpack_swiglu
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+
+    def n(*s):
+        return (torch.randn(*s, generator=g, device=dev) * 0.03).to(torch.bfloat16)
+
+    pe = pack_swiglu(n(E, I, d), n(E, I, d), n(E, d, I), shared=(n(Is, d), n(Is, d), n(d, Is)), device=dev)
+    q = quantize_fp8(pe)
+    Wg, _ = syn.router_weight(E, d, seed + 1, zipf_s=1.5, dtype="bf16")
+    sgw = syn.bf16_round(syn.rng(seed + 2).standard_normal((1, d)).astype(np.float32) / np.sqrt(d))
+    eng = MoEEngine(torch.from_numpy(Wg).to(dev, torch.bfloat16), q, top_k=4, route_mode=L.ROUTE_SOFTMAX_TOPK,
+                    shared_gate_weight=torch.from_numpy(sgw).to(dev, torch.bfloat16))
+    gate, up, down, shared = unpack_swiglu(dequantize_fp8(q))
+    p = {"gate": gate.cpu().numpy(), "up": up.cpu().numpy(), "down": down.cpu().numpy(),
+         "s_gate": shared[0].cpu().numpy(), "s_up": shared[1].cpu().numpy(), "s_down": shared[2].cpu().numpy(),
+         "s_gate_w": sgw}
+    return eng, Wg, p
+
+
+@pytest.mark.parametrize("T,d,E,I,Is", [(200, 256, 60, 128, 256), (77, 128, 8, 64, 128), (1, 64, 8, 32, 64)])
+def test_qwen_fp8_vs_oracle(cuda, T, d, E, I, Is):
+    eng, Wg, p = _qwen(cuda, T, d, E, I, Is, 41)
+    x = syn.hidden_states(T, d, 42, "bf16")
+    r = eng.forward(torch.from_numpy(x).to(cuda, torch.bfloat16))
+    torch.cuda.synchronize()
+    eng.check()
+    y, lg, ids, w, sg = O.qwen_forward(x, Wg, p, 4, False, "bf16")
+    assert np.array_equal(r["topk_ids"].cpu().numpy(), ids)
+    assert O.max_rel_err(r["out"].float().cpu().numpy(), y) < TOL
+
+
+def test_switch_fp8_vs_oracle(cuda):
+    from dsca_moe_b200 import _lib as L
+    from dsca_moe_b200.engine import MoEEngine, dequantize_fp8, pack_relu, quantize_fp8
+
+    T, d, E, F = 300, 256, 16, 512
+    g = torch.Generator(device=cuda)
+    g.manual_seed(51)
+    wi = (torch.randn(E, F, d, generator=g, device=cuda) * 0.03).to(torch.bfloat16)
+    wo = (torch.randn(E, d, F, generator=g, device=cuda) * 0.03).to(torch.bfloat16)
+    q = quantize_fp8(pack_relu(wi, wo, device=cuda))
+    Wr, _ = syn.router_weight(E, d, 52, zipf_s=1.0, dtype="bf16")
+    eng = MoEEngine(torch.from_numpy(Wr).to(cuda, torch.bfloat16), q, top_k=1, route_mode=L.ROUTE_SWITCH_TOP1)
+    x = syn.hidden_states(T, d, 53, "bf16")
+    r = eng.forward(torch.from_numpy(x).to(cuda, torch.bfloat16))
+    torch.cuda.synchronize()
+    eng.check()
+    dq = dequantize_fp8(q)
+    wi_d = dq.w1[:, :F].cpu().numpy()
+    wo_d = dq.w2[:, :d, :F].cpu().numpy()
+    y, lg, idx, gate = O.switch_forward(x, Wr, wi_d, wo_d, "bf16")
+    assert np.array_equal(r["expert_index"].cpu().numpy(), idx)
+    assert O.max_rel_err(r["out"].float().cpu().numpy(), y) < TOL
+
+
+def test_qwen_fp8_full_size(cuda):
+    """Qwen1.5-MoE-A2.7B shape, 4096 tokens: fp8 output vs the oracle on a token sample, and its
+    distance from the unquantised bf16 block (the quantisation error itself)."""
+    T, d, E, I, Is = 4096, 2048, 60, 1408, 5632
+    eng, Wg, p = _qwen(cuda, T, d, E, I, Is, 61)
+    x = syn.hidden_states(T, d, 62, "bf16")
+    r = eng.forward(torch.from_numpy(x).to(cuda, torch.bfloat16))
+    torch.cuda.synchronize()
+    eng.check()
+    sample = syn.rng(63).choice(T, 48, replace=False)
+    y, *_ = O.qwen_forward(x[sample], Wg, p, 4, False, "bf16")
+    assert O.max_rel_err(r["out"].float().cpu().numpy()[sample], y) < TOL
