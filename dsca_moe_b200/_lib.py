@@ -29,7 +29,8 @@ class RouterArgs(ctypes.Structure):
                 ("T", _i), ("d", _i), ("E", _i), ("top_k", _i), ("dtype", _i), ("mode", _i),
                 ("norm_topk", _i), ("weight_round_bf16", _i),
                 ("logits", _vp), ("topk_ids", _vp), ("topk_w", _vp), ("expert_index", _vp),
-                ("shared_gate", _vp), ("block_hist", _vp), ("local_rank", _vp)]
+                ("shared_gate", _vp), ("block_hist", _vp), ("local_rank", _vp),
+                ("counts", _vp), ("offsets", _vp), ("block_base", _vp), ("done_counter", _vp)]
 
 
 class ScanArgs(ctypes.Structure):

@@ -88,6 +88,10 @@ int dsca_router_topk(const dsca_router_args* a, dsca_stream_t stream) {
   if (a->d % vec != 0 || !aligned16(a->x) || !aligned16(a->w_router) ||
       (a->w_shared_gate && !aligned16(a->w_shared_gate)))
     return DSCA_ERR_BAD_ARG;
+  // the fused scan takes all four outputs or none
+  const int nscan = (a->counts != nullptr) + (a->offsets != nullptr) + (a->block_base != nullptr) +
+                    (a->done_counter != nullptr);
+  if (nscan != 0 && nscan != 4) return DSCA_ERR_BAD_ARG;
   if (a->T == 0) return DSCA_OK;
   return dsca::launch_router(a, reinterpret_cast<cudaStream_t>(stream));
 }

@@ -1,5 +1,5 @@
-// K1 — router: logits, softmax, top-1 / top-k, shared-expert gate, per-block histogram and
-// in-block stable ranks, fused in one launch.
+// K1 — router: logits, softmax, top-1 / top-k, shared-expert gate, per-block histogram,
+// in-block stable ranks and (optionally) the per-expert scan, fused in one launch.
 //
 // Reference semantics: Router.standard_forward (src/harmonymoe/router.py:52-63) and the
 // argmax at src/qosmoe/moe_layer.py:287 for the Switch top-1 block; gate / softmax(fp32) /
@@ -7,17 +7,19 @@
 // shared-expert gate sigmoid (qwen_ep.py:94) for the Qwen block.
 //
 // Fixed arithmetic order of a logit (the C oracle follows it bit for bit):
-//   C = 32 * ceil(d / 128); chunk q covers i in [qC, min(d, (q+1)C)) (at most 4 chunks);
-//   S_q = fma chain over the chunk in increasing i from 0.0f; logit = ((S_0 + S_1) + S_2) + S_3,
-//   rounded to the router dtype.
+//   C = 32 * ceil(d / 256); chunk q covers i in [qC, min(d, (q+1)C)) (at most 8 chunks);
+//   S_q = fma chain over the chunk in increasing i from 0.0f; logit = partials summed left to
+//   right, rounded to the router dtype.
 //
 // Layout: one CTA = 32 tokens (DSCA_ROUTER_TOKENS) x 64 router rows (E experts, then the shared
-// gate row, then zeros), 512 threads = 4 chunk groups of 128.  In group q, thread g owns tokens
-// 4*(g/16)..+3 and rows 4*(g%16)..+3: a 4 x 4 register tile fed by two 16-byte shared-memory
-// loads per k (x and W staged k-major in fp32).  Each group streams its chunk in 32-wide k
-// slices, fetching the next slice into registers while it computes the current one, and syncs
-// on its own named barrier.  The chunk partials meet in shared memory; softmax and selection
-// then run one warp per token.
+// gate row, then zeros), 1024 threads = 8 chunk groups of 128.  In group q, thread g owns tokens
+// 4*(g/16)..+3 and rows g%16 + 16j (j < 4): a 4 x 4 register tile fed by 16-byte shared-memory
+// reads (x and W staged row-major in fp32, pitch 20 floats so the 16 row lanes of a warp hit
+// distinct banks).  Each group streams its chunk in 16-wide k slices through two buffers,
+// fetching the next slice into registers while computing the current one, and syncs on its own
+// named barrier.  The chunk partials meet in shared memory; softmax and selection then run one
+// warp per token.  With the fused scan, the last CTA to finish turns every block's histogram into
+// the per-expert counts, offsets and block bases (stable: block order, then token order).
 #include "common.cuh"
 
 namespace dsca {
@@ -25,14 +27,13 @@ namespace router {
 
 constexpr int kTokens = DSCA_ROUTER_TOKENS;  // 32
 constexpr int kRows = 64;                    // router rows (E + shared gate <= 64)
-constexpr int kGroups = 4;
+constexpr int kGroups = 8;
 constexpr int kGroupThreads = 128;
-constexpr int kThreads = kGroups * kGroupThreads;  // 512
-constexpr int kKS = 32;                      // k slice
-constexpr int kP = kKS + 4;                  // staging row pitch (floats): x_s[token][k], w_s[row][k]
+constexpr int kThreads = kGroups * kGroupThreads;  // 1024
+constexpr int kKS = 16;                      // k slice
+constexpr int kP = kKS + 4;                  // staging row pitch (floats)
 constexpr int kStageFloats = kTokens * kP + kRows * kP;
 constexpr int kLP = kRows + 1;               // logit tile pitch
-// two staging buffers per chunk group
 constexpr size_t kSmemBytes = sizeof(float) * (size_t)(kGroups * 2 * kStageFloats);
 
 struct Args {
@@ -47,6 +48,10 @@ struct Args {
   float* shared_gate;
   int32_t* block_hist;
   int32_t* local_rank;
+  int32_t* counts;
+  int32_t* offsets;
+  int32_t* block_base;
+  uint32_t* done_counter;
 };
 
 __device__ __forceinline__ void group_sync(int q) {
@@ -61,29 +66,25 @@ __device__ __forceinline__ const T* wrow(const Args& a, int r) {
   return nullptr;
 }
 
-// Per-thread staging registers for one 32-wide k slice of the group's chunk.
+// Per-thread staging registers for one 16-wide k slice of the group's chunk.
 template <typename T>
 struct Slice;
 
 template <>
 struct Slice<__nv_bfloat16> {
-  // x: 32 tokens x 32 k = 128 x uint4 (1 per thread); W: 64 rows x 32 k = 256 x uint4 (2)
-  uint4 xv, wv[2];
+  // x: 32 tokens x 16 k = 64 x uint4 (threads 0..63); W: 64 rows x 16 k = 128 x uint4 (one each)
+  uint4 xv, wv;
   __device__ void fetch(const Args& a, int g, int tok0, int k0, int kend) {
     const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(a.x);
-    {
-      int t = g >> 2, c = (g & 3) * 8;
-      xv = make_uint4(0, 0, 0, 0);
+    xv = make_uint4(0, 0, 0, 0);
+    if (g < 64) {
+      const int t = g >> 1, c = (g & 1) * 8;
       if (tok0 + t < a.T && k0 + c < kend) xv = *reinterpret_cast<const uint4*>(x + (size_t)(tok0 + t) * a.d + k0 + c);
     }
-#pragma unroll
-    for (int v = 0; v < 2; ++v) {
-      int idx = g + v * kGroupThreads;
-      int r = idx >> 2, c = (idx & 3) * 8;
-      const __nv_bfloat16* w = wrow<__nv_bfloat16>(a, r);
-      wv[v] = make_uint4(0, 0, 0, 0);
-      if (w != nullptr && k0 + c < kend) wv[v] = *reinterpret_cast<const uint4*>(w + k0 + c);
-    }
+    const int r = g >> 1, c = (g & 1) * 8;
+    const __nv_bfloat16* w = wrow<__nv_bfloat16>(a, r);
+    wv = make_uint4(0, 0, 0, 0);
+    if (w != nullptr && k0 + c < kend) wv = *reinterpret_cast<const uint4*>(w + k0 + c);
   }
   static __device__ void put8(float* dst, const uint4& u) {
     const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
@@ -93,47 +94,37 @@ struct Slice<__nv_bfloat16> {
                                                       __bfloat162float(h[6]), __bfloat162float(h[7]));
   }
   __device__ void store(float* xs, float* ws, int g) const {
-    put8(xs + (g >> 2) * kP + (g & 3) * 8, xv);
-#pragma unroll
-    for (int v = 0; v < 2; ++v) {
-      int idx = g + v * kGroupThreads;
-      put8(ws + (idx >> 2) * kP + (idx & 3) * 8, wv[v]);
-    }
+    if (g < 64) put8(xs + (g >> 1) * kP + (g & 1) * 8, xv);
+    put8(ws + (g >> 1) * kP + (g & 1) * 8, wv);
   }
 };
 
 template <>
 struct Slice<float> {
-  // x: 32 x 32 floats = 256 float4 (2 per thread); W: 64 x 32 = 512 float4 (4)
-  float4 xv[2], wv[4];
+  // x: 32 x 16 floats = 128 float4 (one each); W: 64 x 16 = 256 float4 (two each)
+  float4 xv, wv[2];
   __device__ void fetch(const Args& a, int g, int tok0, int k0, int kend) {
     const float* x = reinterpret_cast<const float*>(a.x);
-#pragma unroll
-    for (int v = 0; v < 2; ++v) {
-      int idx = g + v * kGroupThreads;
-      int t = idx >> 3, c = (idx & 7) * 4;
-      xv[v] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (tok0 + t < a.T && k0 + c < kend) xv[v] = *reinterpret_cast<const float4*>(x + (size_t)(tok0 + t) * a.d + k0 + c);
+    {
+      const int t = g >> 2, c = (g & 3) * 4;
+      xv = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (tok0 + t < a.T && k0 + c < kend) xv = *reinterpret_cast<const float4*>(x + (size_t)(tok0 + t) * a.d + k0 + c);
     }
 #pragma unroll
-    for (int v = 0; v < 4; ++v) {
-      int idx = g + v * kGroupThreads;
-      int r = idx >> 3, c = (idx & 7) * 4;
+    for (int v = 0; v < 2; ++v) {
+      const int idx = g + v * kGroupThreads;
+      const int r = idx >> 2, c = (idx & 3) * 4;
       const float* w = wrow<float>(a, r);
       wv[v] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (w != nullptr && k0 + c < kend) wv[v] = *reinterpret_cast<const float4*>(w + k0 + c);
     }
   }
   __device__ void store(float* xs, float* ws, int g) const {
+    *reinterpret_cast<float4*>(xs + (g >> 2) * kP + (g & 3) * 4) = xv;
 #pragma unroll
     for (int v = 0; v < 2; ++v) {
-      int idx = g + v * kGroupThreads;
-      *reinterpret_cast<float4*>(xs + (idx >> 3) * kP + (idx & 7) * 4) = xv[v];
-    }
-#pragma unroll
-    for (int v = 0; v < 4; ++v) {
-      int idx = g + v * kGroupThreads;
-      *reinterpret_cast<float4*>(ws + (idx >> 3) * kP + (idx & 7) * 4) = wv[v];
+      const int idx = g + v * kGroupThreads;
+      *reinterpret_cast<float4*>(ws + (idx >> 2) * kP + (idx & 3) * 4) = wv[v];
     }
   }
 };
@@ -149,11 +140,60 @@ __device__ __forceinline__ void store_logit<float>(void* logits, size_t i, float
   reinterpret_cast<float*>(logits)[i] = v;
 }
 
+// Per-expert counts, offsets and block bases from all blocks' histograms (one CTA).
+__device__ void scan_blocks(const Args& a, int nb, int* cnt_s) {
+  const int E = a.E;
+  const volatile int32_t* hist = a.block_hist;
+  // thread (e, c): a contiguous run of blocks of expert e; 16 runs per expert
+  constexpr int kRuns = 16;
+  __shared__ int part[kRows][kRuns + 1];
+  const int per = (nb + kRuns - 1) / kRuns;
+  for (int base_e = 0; base_e < E; base_e += kThreads / kRuns) {
+    const int e = base_e + threadIdx.x / kRuns, c = threadIdx.x % kRuns;
+    const int b0 = c * per, b1 = min(nb, b0 + per);
+    int s = 0;
+    if (e < E)
+      for (int b = b0; b < b1; ++b) s += hist[(size_t)b * E + e];
+    if (e < E) part[e][c] = s;
+    __syncthreads();
+    if (e < E && c == 0) {
+      int run = 0;
+      for (int i = 0; i < kRuns; ++i) {
+        const int v = part[e][i];
+        part[e][i] = run;
+        run += v;
+      }
+      cnt_s[e] = run;
+      a.counts[e] = run;
+    }
+    __syncthreads();
+    if (e < E) {
+      int run = part[e][c];
+      for (int b = b0; b < b1; ++b) {
+        const int v = hist[(size_t)b * E + e];
+        a.block_base[(size_t)b * E + e] = run;
+        run += v;
+      }
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    int run = 0;
+    for (int e = 0; e < E; ++e) {
+      a.offsets[e] = run;
+      run += cnt_s[e];
+    }
+    a.offsets[E] = run;
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) router_kernel(Args a) {
   extern __shared__ __align__(16) float smem[];
   __shared__ float lg_s[kTokens * kLP];
   __shared__ int ids_s[kTokens][DSCA_MAX_TOPK];
+  __shared__ int cnt_s[kRows];
+  __shared__ int is_last;
 
   const int tid = threadIdx.x;
   const int q = tid / kGroupThreads;  // chunk group
@@ -164,7 +204,7 @@ __global__ void __launch_bounds__(kThreads, 1) router_kernel(Args a) {
   const bool tau_bf16 = sizeof(T) == 2;
 
   // ---------------- chunk partial sums: 4 x 4 tile per thread
-  const int C = 32 * ((a.d + 127) / 128);
+  const int C = 32 * ((a.d + 255) / 256);
   const int nq = (a.d + C - 1) / C;
   const int kbeg = q * C, kend = min(a.d, kbeg + C);
   const int tq = g >> 4, rq = g & 15;
@@ -174,8 +214,6 @@ __global__ void __launch_bounds__(kThreads, 1) router_kernel(Args a) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
 
-  // thread tile: tokens 4*tq + i, rows rq + 16*j (strided rows keep the float4 reads of the 16
-  // row lanes of a warp on distinct banks)
   float* stage0 = smem + q * 2 * kStageFloats;
   if (q < nq) {
     Slice<T> sl;
@@ -187,10 +225,9 @@ __global__ void __launch_bounds__(kThreads, 1) router_kernel(Args a) {
       const bool more = k0 + kKS < kend;
       if (more) sl.fetch(a, g, tok0, k0 + kKS, kend);  // in flight during the compute below
       const float* xs = stage0 + s * kStageFloats;
-      const float* ws = xs + kTokens * kP;
       const float* xb = xs + (4 * tq) * kP;
-      const float* wb = ws + rq * kP;
-      const int kmax = min(kKS, kend - k0);  // a multiple of 8
+      const float* wb = xs + kTokens * kP + rq * kP;
+      const int kmax = min(kKS, kend - k0);  // a multiple of 8 (bf16) or 4 (fp32)
       for (int k = 0; k < kmax; k += 4) {
         float4 xv[4], wv[4];
 #pragma unroll
@@ -338,6 +375,22 @@ __global__ void __launch_bounds__(kThreads, 1) router_kernel(Args a) {
       for (int jj = 0; jj < k; ++jj) r += (ids_s[u][jj] == e);
     a.local_rank[(size_t)t * k + j] = r;
   }
+
+  // ---------------- fused scan: the last CTA to finish
+  if (a.done_counter != nullptr) {
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+      const uint32_t prev = atomicAdd(a.done_counter, 1u);
+      is_last = prev == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (is_last) {
+      __threadfence();
+      scan_blocks(a, gridDim.x, cnt_s);
+      if (tid == 0) *a.done_counter = 0u;  // ready for the next launch (stream ordered)
+    }
+  }
 }
 
 }  // namespace router
@@ -362,6 +415,12 @@ int launch_router(const dsca_router_args* p, cudaStream_t stream) {
   a.shared_gate = p->shared_gate;
   a.block_hist = p->block_hist;
   a.local_rank = p->local_rank;
+  const bool fused = p->done_counter != nullptr && p->counts != nullptr && p->offsets != nullptr &&
+                     p->block_base != nullptr;
+  a.counts = fused ? p->counts : nullptr;
+  a.offsets = fused ? p->offsets : nullptr;
+  a.block_base = fused ? p->block_base : nullptr;
+  a.done_counter = fused ? p->done_counter : nullptr;
   const int nblocks = (p->T + router::kTokens - 1) / router::kTokens;
   cudaError_t e = cudaSuccess;
   if (p->dtype == DSCA_BF16) {

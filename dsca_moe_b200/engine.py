@@ -336,7 +336,11 @@ class MoEEngine:
         # "overlap": routed GEMM2 stores locally and a return kernel sends the rows on a side
         # stream beside the shared-expert GEMM2; "fused": GEMM2's epilogue stores them remotely
         self.ep_return = "overlap"
+        # True: the router's last CTA computes counts / offsets / block bases (one launch);
+        # False: the separate dsca_dispatch_scan launch does
+        self.fuse_scan = True
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._done_counter = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._ws = {}
         self.last_plan = None
         self.last_layout = None
@@ -407,8 +411,13 @@ class MoEEngine:
         a.expert_index = _ptr(ws["expert_index"])
         a.shared_gate = _ptr(ws["shared_gate"])
         a.block_hist, a.local_rank = _ptr(ws["block_hist"]), _ptr(ws["local_rank"])
+        if self.fuse_scan:
+            a.counts, a.offsets, a.block_base = _ptr(ws["counts"]), _ptr(ws["offsets"]), _ptr(ws["block_base"])
+            a.done_counter = _ptr(self._done_counter)
         L.call("dsca_router_topk", ctypes.byref(a), _stream())
         self._mark("router")
+        if self.fuse_scan:
+            return
         s = L.ScanArgs()
         s.block_hist, s.nblocks, s.E = _ptr(ws["block_hist"]), _ceil(T, L.ROUTER_TOKENS), self.E
         s.counts, s.offsets, s.block_base = _ptr(ws["counts"]), _ptr(ws["offsets"]), _ptr(ws["block_base"])

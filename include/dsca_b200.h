@@ -93,6 +93,12 @@ typedef struct {
   float* shared_gate;         /* [T] sigmoid(round_dtype(x . g)), or NULL */
   int32_t* block_hist;        /* [ceil(T/32), E] tokens per expert in each 32-token block */
   int32_t* local_rank;        /* [T, top_k] rank of (t, j) among its block's tokens of that expert */
+  /* optional fused scan (the dsca_dispatch_scan outputs, computed by the last CTA to finish):
+     set all four, done_counter pointing at a zeroed uint32 that the kernel leaves at zero */
+  int32_t* counts;            /* [E] */
+  int32_t* offsets;           /* [E + 1] */
+  int32_t* block_base;        /* [ceil(T/32), E] */
+  uint32_t* done_counter;
 } dsca_router_args;
 DSCA_API int dsca_router_topk(const dsca_router_args* a, dsca_stream_t stream);
 

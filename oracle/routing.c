@@ -20,9 +20,9 @@
  *     w      = w.to(activation dtype)
  *
  * Fixed order used here and in the kernel (the reference leaves it to cuBLAS/ATen):
- *   C          = 32 * ceil(d / 128)   (d splits into at most 4 chunks of C)
+ *   C          = 32 * ceil(d / 256)   (d splits into at most 8 chunks of C)
  *   S_q        = fma-accumulate over i in [qC, min(d, (q+1)C)) of x[t,i] * W[e,i], from 0.0f
- *   logit[t,e] = round_tau( ((S_0 + S_1) + S_2) + S_3 )
+ *   logit[t,e] = round_tau( partials summed left to right: ((S_0 + S_1) + S_2) + ... )
  *   m          = max_e logit[t,e]
  *   ex[e]      = dsca_exp(logit[t,e] - m)
  *   s          = 32 lane partials (lane L sums e = L, L+32, L+64 ... in that order) combined by
@@ -77,13 +77,13 @@ float oracle_exp_neg(float x) {
     return p * scale;
 }
 
-/* Chunk length of the logit sum: C = 32 * ceil(d / 128), so d splits into at most 4 chunks. */
-int oracle_router_chunk(int d) { return 32 * ((d + 127) / 128); }
+/* Chunk length of the logit sum: C = 32 * ceil(d / 256), so d splits into at most 8 chunks. */
+int oracle_router_chunk(int d) { return 32 * ((d + 255) / 256); }
 
 /*
  * logits[T,E] = round_tau(x[T,d] . W[E,d]^T); round_bf16 selects tau = bf16, else fp32.
  * Order: chunk q covers i in [qC, min(d, (q+1)C)); its partial S_q is the fma chain over i in
- * increasing order from 0.0f; the logit is ((S_0 + S_1) + S_2) + S_3.
+ * increasing order from 0.0f; the logit is (((S_0 + S_1) + S_2) + ...) + S_7, left to right.
  */
 void oracle_router_logits(const float* x, const float* W, int T, int d, int E, int round_bf16,
                           float* logits) {

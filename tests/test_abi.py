@@ -52,6 +52,15 @@ def test_bad_args_rejected_without_gpu(lib):
     assert lib.dsca_router_topk(None, None) == _lib.ERR_BAD_ARG
     a = _lib.RouterArgs()
     assert lib.dsca_router_topk(ctypes.byref(a), None) == _lib.ERR_BAD_ARG
+    # the fused scan needs all four of counts / offsets / block_base / done_counter (checked
+    # before any device call; the pointers are never dereferenced)
+    a.x = a.w_router = a.logits = a.topk_ids = a.topk_w = a.block_hist = a.local_rank = 4096
+    a.T, a.d, a.E, a.top_k, a.dtype, a.mode = 32, 64, 8, 2, _lib.BF16, _lib.ROUTE_SOFTMAX_TOPK
+    a.counts = a.offsets = 4096
+    assert lib.dsca_router_topk(ctypes.byref(a), None) == _lib.ERR_BAD_ARG
+    a.T = 0  # a valid empty call with all four set returns OK without launching
+    a.block_base = a.done_counter = 4096
+    assert lib.dsca_router_topk(ctypes.byref(a), None) == _lib.OK
     assert lib.dsca_grouped_ffn(None, None) == _lib.ERR_BAD_ARG
     assert lib.dsca_plan_harmony(None, 2, 8, None, 150, None) == _lib.ERR_BAD_ARG
 

@@ -357,3 +357,27 @@ def test_repeat_calls_are_deterministic(cuda):
     b = eng.forward(x)["out"].clone()
     torch.cuda.synchronize()
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("T,k,E", [(4096, 4, 60), (33, 1, 8), (20000, 8, 64)])
+def test_fused_scan_matches_separate_scan(cuda, T, k, E):
+    """The router's last-CTA scan gives the same counts, offsets and block bases as the separate
+    scan launch, and leaves its completion counter at zero (two fused calls in a row agree)."""
+    d = 128
+    x = _t(syn.hidden_states(T, d, 1101, "bf16"), torch.bfloat16, cuda)
+    Wg, _ = syn.router_weight(E, d, 1102, zipf_s=1.2, dtype="bf16")
+    eng = qwen_engine(Wg, syn.qwen_expert_weights(E, d, 64, 128, 1103, dtype="bf16"), k, False,
+                      torch.bfloat16, cuda)
+    keys = ("counts", "offsets", "block_base", "token_row", "out")
+    ws = eng._workspace(T)
+    got = []
+    for fused in (True, True, False):
+        eng.fuse_scan = fused
+        r = eng.forward(x)
+        torch.cuda.synchronize()
+        eng.check()
+        got.append({kk: (ws[kk] if kk in ws else r[kk]).clone() for kk in keys})
+        assert int(eng._done_counter.item()) == 0
+    for kk in keys:
+        assert torch.equal(got[0][kk], got[2][kk]), kk
+        assert torch.equal(got[1][kk], got[2][kk]), kk
