@@ -12,14 +12,24 @@
 //   right, rounded to the router dtype.
 //
 // Layout: one CTA = 32 tokens (DSCA_ROUTER_TOKENS) x 64 router rows (E experts, then the shared
-// gate row, then zeros), 1024 threads = 8 chunk groups of 128.  In group q, thread g owns tokens
-// 4*(g/16)..+3 and rows g%16 + 16j (j < 4): a 4 x 4 register tile fed by 16-byte shared-memory
-// reads (x and W staged row-major in fp32, pitch 20 floats so the 16 row lanes of a warp hit
-// distinct banks).  Each group streams its chunk in 16-wide k slices through two buffers,
-// fetching the next slice into registers while computing the current one, and syncs on its own
-// named barrier.  The chunk partials meet in shared memory; softmax and selection then run one
-// warp per token.  With the fused scan, the last CTA to finish turns every block's histogram into
-// the per-expert counts, offsets and block bases (stable: block order, then token order).
+// gate row, then zeros), 512 threads = 4 groups of 128.  Group j runs the chunks 2j and 2j+1
+// side by side: every accumulator is a packed fp32x2 pair {S_2j, S_2j+1} of one (token, row),
+// updated by __ffma2_rn, which rounds each element exactly like fmaf, so each element is its own
+// chunk's fma chain.  A 16-wide k slice of both chunks is staged in shared memory interleaved
+// ([t][k] -> {x[2jC + k], x[(2j+1)C + k]}, the same for W rows), so one 16-byte read gives two k
+// of a pair.  Thread g owns tokens tq + 8i and rows rq + 16j (i, j < 4), a 4 x 4 tile of pairs;
+// a warp spans 4 tq x 8 rq, arranged so that each group of 4 consecutive lanes covers 2 tq x 2 rq:
+// a 16-byte shared-memory read then costs the minimum of two wavefronts (a lane quad receives
+// one distinct 16-byte word per wavefront; the row pitch of 36 floats puts consecutive rows in
+// distinct bank groups).  A shorter
+// (or missing) second chunk reads zeros past its end: fma(0, 0, s) == s for every s such a chain
+// can hold (it starts at +0.0f and never becomes -0.0f).  Each group streams its chunks through
+// two buffers, fetching the next slice into registers while computing the current one, and
+// syncs on its own named barrier.  The chunk partials meet in shared memory; softmax and
+// selection then run one warp per token.  Per-block histograms and in-block ranks come from
+// 32-bit token masks per expert.  With the fused scan, the last CTA to finish turns every
+// block's histogram into the per-expert counts, offsets and block bases (stable: block order,
+// then token order).
 #include "common.cuh"
 
 namespace dsca {
@@ -27,14 +37,16 @@ namespace router {
 
 constexpr int kTokens = DSCA_ROUTER_TOKENS;  // 32
 constexpr int kRows = 64;                    // router rows (E + shared gate <= 64)
-constexpr int kGroups = 8;
+constexpr int kGroups = 4;                   // chunk pairs
 constexpr int kGroupThreads = 128;
-constexpr int kThreads = kGroups * kGroupThreads;  // 1024
-constexpr int kKS = 16;                      // k slice
-constexpr int kP = kKS + 4;                  // staging row pitch (floats)
-constexpr int kStageFloats = kTokens * kP + kRows * kP;
+constexpr int kThreads = kGroups * kGroupThreads;  // 512
+constexpr int kKS = 16;                      // k slice (per chunk)
+constexpr int kXP = 2 * kKS + 4;             // floats per token row of the interleaved x slice
+constexpr int kWP = 2 * kKS + 4;             // floats per router row of the interleaved W slice
+constexpr int kStageFloats = kTokens * kXP + kRows * kWP;
 constexpr int kLP = kRows + 1;               // logit tile pitch
 constexpr size_t kSmemBytes = sizeof(float) * (size_t)(kGroups * 2 * kStageFloats);
+static_assert(kSmemBytes >= sizeof(float) * 8 * kTokens * kRows, "partials fit the staging area");
 
 struct Args {
   const void* x;
@@ -66,68 +78,73 @@ __device__ __forceinline__ const T* wrow(const Args& a, int r) {
   return nullptr;
 }
 
-// Per-thread staging registers for one 16-wide k slice of the group's chunk.
+__device__ __forceinline__ void st4(float* p, float a, float b, float c, float d) {
+  *reinterpret_cast<float4*>(p) = make_float4(a, b, c, d);
+}
+
+// Staging of one slice: 96 rows (32 tokens, then 64 router rows) x kKS/4 k-quads, kTasks per
+// thread (task = g + 128 u).  A task reads 4 k of its row from each chunk of the pair and
+// writes them interleaved.
+constexpr int kQuads = kKS / 4;
+constexpr int kTasks = (kTokens + kRows) * kQuads / kGroupThreads;
+static_assert((kTokens + kRows) * kQuads % kGroupThreads == 0 && kGroupThreads % kQuads == 0, "task split");
+
 template <typename T>
-struct Slice;
-
+struct Vec4;  // 4 elements of T
 template <>
-struct Slice<__nv_bfloat16> {
-  // x: 32 tokens x 16 k = 64 x uint4 (threads 0..63); W: 64 rows x 16 k = 128 x uint4 (one each)
-  uint4 xv, wv;
-  __device__ void fetch(const Args& a, int g, int tok0, int k0, int kend) {
-    const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(a.x);
-    xv = make_uint4(0, 0, 0, 0);
-    if (g < 64) {
-      const int t = g >> 1, c = (g & 1) * 8;
-      if (tok0 + t < a.T && k0 + c < kend) xv = *reinterpret_cast<const uint4*>(x + (size_t)(tok0 + t) * a.d + k0 + c);
-    }
-    const int r = g >> 1, c = (g & 1) * 8;
-    const __nv_bfloat16* w = wrow<__nv_bfloat16>(a, r);
-    wv = make_uint4(0, 0, 0, 0);
-    if (w != nullptr && k0 + c < kend) wv = *reinterpret_cast<const uint4*>(w + k0 + c);
-  }
-  static __device__ void put8(float* dst, const uint4& u) {
-    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
-    *reinterpret_cast<float4*>(dst) = make_float4(__bfloat162float(h[0]), __bfloat162float(h[1]),
-                                                  __bfloat162float(h[2]), __bfloat162float(h[3]));
-    *reinterpret_cast<float4*>(dst + 4) = make_float4(__bfloat162float(h[4]), __bfloat162float(h[5]),
-                                                      __bfloat162float(h[6]), __bfloat162float(h[7]));
-  }
-  __device__ void store(float* xs, float* ws, int g) const {
-    if (g < 64) put8(xs + (g >> 1) * kP + (g & 1) * 8, xv);
-    put8(ws + (g >> 1) * kP + (g & 1) * 8, wv);
-  }
+struct Vec4<__nv_bfloat16> {
+  using type = uint2;
+  static __device__ type zero() { return make_uint2(0, 0); }
+  static __device__ float lo(uint32_t u) { return __uint_as_float(u << 16); }
+  static __device__ float hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
+  static __device__ float4 f32(type v) { return make_float4(lo(v.x), hi(v.x), lo(v.y), hi(v.y)); }
+};
+template <>
+struct Vec4<float> {
+  using type = float4;
+  static __device__ type zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
+  static __device__ float4 f32(type v) { return v; }
 };
 
-template <>
-struct Slice<float> {
-  // x: 32 x 16 floats = 128 float4 (one each); W: 64 x 16 = 256 float4 (two each)
-  float4 xv, wv[2];
-  __device__ void fetch(const Args& a, int g, int tok0, int k0, int kend) {
-    const float* x = reinterpret_cast<const float*>(a.x);
-    {
-      const int t = g >> 2, c = (g & 3) * 4;
-      xv = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (tok0 + t < a.T && k0 + c < kend) xv = *reinterpret_cast<const float4*>(x + (size_t)(tok0 + t) * a.d + k0 + c);
-    }
+template <typename T>
+struct Slice {
+  using V = Vec4<T>;
+  typename V::type va[kTasks], vb[kTasks];
+  const T* row[kTasks];
+  __device__ void init(const Args& a, int g, int tok0) {
 #pragma unroll
-    for (int v = 0; v < 2; ++v) {
-      const int idx = g + v * kGroupThreads;
-      const int r = idx >> 2, c = (idx & 3) * 4;
-      const float* w = wrow<float>(a, r);
-      wv[v] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (w != nullptr && k0 + c < kend) wv[v] = *reinterpret_cast<const float4*>(w + k0 + c);
+    for (int u = 0; u < kTasks; ++u) {
+      const int r = (g + kGroupThreads * u) / kQuads;
+      if (r < kTokens) {
+        const int t = tok0 + r;
+        row[u] = t < a.T ? reinterpret_cast<const T*>(a.x) + (size_t)t * a.d : nullptr;
+      } else {
+        row[u] = wrow<T>(a, r - kTokens);
+      }
     }
   }
-  __device__ void store(float* xs, float* ws, int g) const {
-    *reinterpret_cast<float4*>(xs + (g >> 2) * kP + (g & 3) * 4) = xv;
+  // ka / kb: the slice's first k in chunk A / B; la / lb: k past the end of each chunk
+  __device__ void fetch(int g, int ka, int la, int kb, int lb) {
+    const int kq = 4 * (g % kQuads);
 #pragma unroll
-    for (int v = 0; v < 2; ++v) {
-      const int idx = g + v * kGroupThreads;
-      *reinterpret_cast<float4*>(ws + (idx >> 2) * kP + (idx & 3) * 4) = wv[v];
+    for (int u = 0; u < kTasks; ++u) {
+      const T* r = row[u];
+      va[u] = (r && ka + kq < la) ? *reinterpret_cast<const typename V::type*>(r + ka + kq) : V::zero();
+      vb[u] = (r && kb + kq < lb) ? *reinterpret_cast<const typename V::type*>(r + kb + kq) : V::zero();
+    }
+  }
+  __device__ void store(float* st, int g) const {
+#pragma unroll
+    for (int u = 0; u < kTasks; ++u) {
+      const int r = (g + kGroupThreads * u) / kQuads;  // x rows then W rows: one pitch
+      float* dst = st + r * kXP + 8 * (g % kQuads);
+      const float4 A = V::f32(va[u]), B = V::f32(vb[u]);
+      st4(dst, A.x, B.x, A.y, B.y);
+      st4(dst + 4, A.z, B.z, A.w, B.w);
     }
   }
 };
+static_assert(kXP == kWP, "one pitch for the x and W rows of a slice");
 
 template <typename T>
 __device__ __forceinline__ void store_logit(void* logits, size_t i, float v);
@@ -140,50 +157,104 @@ __device__ __forceinline__ void store_logit<float>(void* logits, size_t i, float
   reinterpret_cast<float*>(logits)[i] = v;
 }
 
-// Per-expert counts, offsets and block bases from all blocks' histograms (one CTA).
-__device__ void scan_blocks(const Args& a, int nb, int* cnt_s) {
-  const int E = a.E;
-  const volatile int32_t* hist = a.block_hist;
-  // thread (e, c): a contiguous run of blocks of expert e; 16 runs per expert
-  constexpr int kRuns = 16;
-  __shared__ int part[kRows][kRuns + 1];
-  const int per = (nb + kRuns - 1) / kRuns;
-  for (int base_e = 0; base_e < E; base_e += kThreads / kRuns) {
-    const int e = base_e + threadIdx.x / kRuns, c = threadIdx.x % kRuns;
-    const int b0 = c * per, b1 = min(nb, b0 + per);
-    int s = 0;
-    if (e < E)
-      for (int b = b0; b < b1; ++b) s += hist[(size_t)b * E + e];
-    if (e < E) part[e][c] = s;
-    __syncthreads();
-    if (e < E && c == 0) {
-      int run = 0;
-      for (int i = 0; i < kRuns; ++i) {
-        const int v = part[e][i];
-        part[e][i] = run;
-        run += v;
+// Order-preserving map of a (non-NaN) float onto uint32, and back.
+__device__ __forceinline__ uint32_t ord_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float ord_val(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+// Two k of the slice for both chunks of the pair: 4 tokens x 4 rows of packed pairs.
+__device__ __forceinline__ void mma_k2(float2 (&acc)[4][4], const float* xb, const float* wb, int kk) {
+  float4 xv[4], wv[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) xv[i] = *reinterpret_cast<const float4*>(xb + 8 * i * kXP + 4 * kk);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) wv[j] = *reinterpret_cast<const float4*>(wb + 16 * j * kWP + 4 * kk);
+  // first k of the two for all 16 pairs, then the second: dependent updates sit 16 apart
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      acc[i][j] = __ffma2_rn(make_float2(xv[i].x, xv[i].y), make_float2(wv[j].x, wv[j].y), acc[i][j]);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      acc[i][j] = __ffma2_rn(make_float2(xv[i].z, xv[i].w), make_float2(wv[j].z, wv[j].w), acc[i][j]);
+}
+
+// Per-expert counts, offsets and block bases from all blocks' histograms (the last CTA).
+// The histograms pass through shared memory in chunks of rows.  Thread (c, e) (e = tid % 64,
+// c = tid / 64) sums a contiguous run of rows of column e (a warp reads 32 consecutive columns
+// of one row: no bank conflicts), the 8 run sums of a column give each run its base, and the
+// bases go back through shared memory to coalesced stores.
+__device__ void scan_blocks(const Args& a, int nb, int* sbuf, int cap_ints, int* run_s, int (*seg)[kRows]) {
+  constexpr int kSegs = kThreads / kRows;  // 8
+  const int E = a.E, tid = threadIdx.x;
+  const int e = tid % kRows, c = tid / kRows;
+  const int rows = max(1, min(nb, cap_ints / E));
+  if (tid < kRows) run_s[tid] = 0;
+  for (int b0 = 0; b0 < nb; b0 += rows) {
+    const int nr = min(rows, nb - b0), n = nr * E;
+    const int32_t* src = a.block_hist + (size_t)b0 * E;
+    constexpr int kBatch = 8;  // loads in flight per thread
+    for (int i0 = 0; i0 < n; i0 += kBatch * kThreads) {
+      int v[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int i = i0 + u * kThreads + tid;
+        v[u] = i < n ? __ldcg(src + i) : 0;
       }
-      cnt_s[e] = run;
-      a.counts[e] = run;
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int i = i0 + u * kThreads + tid;
+        if (i < n) sbuf[i] = v[u];
+      }
     }
+    __syncthreads();
+    const int per = (nr + kSegs - 1) / kSegs;
+    const int r0 = min(nr, c * per), r1 = min(nr, r0 + per);
+    int sum = 0;
+    if (e < E)
+      for (int r = r0; r < r1; ++r) sum += sbuf[r * E + e];
+    seg[c][e] = sum;
     __syncthreads();
     if (e < E) {
-      int run = part[e][c];
-      for (int b = b0; b < b1; ++b) {
-        const int v = hist[(size_t)b * E + e];
-        a.block_base[(size_t)b * E + e] = run;
-        run += v;
+      int base = run_s[e];
+      for (int cc = 0; cc < c; ++cc) base += seg[cc][e];
+      for (int r = r0; r < r1; ++r) {
+        const int v = sbuf[r * E + e];
+        sbuf[r * E + e] = base;
+        base += v;
       }
     }
     __syncthreads();
-  }
-  if (threadIdx.x == 0) {
-    int run = 0;
-    for (int e = 0; e < E; ++e) {
-      a.offsets[e] = run;
-      run += cnt_s[e];
+    if (c == 0 && e < E) {
+      int tot = run_s[e];
+      for (int cc = 0; cc < kSegs; ++cc) tot += seg[cc][e];
+      run_s[e] = tot;
     }
-    a.offsets[E] = run;
+    int32_t* dst = a.block_base + (size_t)b0 * E;
+    for (int i = tid; i < n; i += kThreads) dst[i] = sbuf[i];
+    __syncthreads();
+  }
+  // counts, and offsets by a warp-wide scan (lane L holds experts L and L + 32)
+  if (tid < 32) {
+    const int L = tid;
+    const int v0 = L < E ? run_s[L] : 0, v1 = L + 32 < E ? run_s[L + 32] : 0;
+    int i0 = v0, i1 = v1;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int u0 = __shfl_up_sync(0xffffffffu, i0, off), u1 = __shfl_up_sync(0xffffffffu, i1, off);
+      if (L >= off) { i0 += u0; i1 += u1; }
+    }
+    const int tot0 = __shfl_sync(0xffffffffu, i0, 31), tot1 = __shfl_sync(0xffffffffu, i1, 31);
+    if (L < E) { a.counts[L] = v0; a.offsets[L] = i0 - v0; }
+    if (L + 32 < E) { a.counts[L + 32] = v1; a.offsets[L + 32] = tot0 + i1 - v1; }
+    if (L == 0) a.offsets[E] = tot0 + tot1;
   }
 }
 
@@ -192,7 +263,9 @@ __global__ void __launch_bounds__(kThreads, 1) router_kernel(Args a) {
   extern __shared__ __align__(16) float smem[];
   __shared__ float lg_s[kTokens * kLP];
   __shared__ int ids_s[kTokens][DSCA_MAX_TOPK];
-  __shared__ int cnt_s[kRows];
+  __shared__ uint32_t emask[kRows];
+  __shared__ int run_s[kRows];
+  __shared__ int seg_s[kThreads / kRows][kRows];
   __shared__ int is_last;
 
   const int tid = threadIdx.x;
@@ -202,62 +275,61 @@ __global__ void __launch_bounds__(kThreads, 1) router_kernel(Args a) {
   const int E = a.E;
   const bool has_sg = a.w_shared_gate != nullptr;
   const bool tau_bf16 = sizeof(T) == 2;
+  if (tid < kRows) emask[tid] = 0u;
 
-  // ---------------- chunk partial sums: 4 x 4 tile per thread
+  // ---------------- chunk partial sums, two chunks per group
   const int C = 32 * ((a.d + 255) / 256);
   const int nq = (a.d + C - 1) / C;
-  const int kbeg = q * C, kend = min(a.d, kbeg + C);
-  const int tq = g >> 4, rq = g & 15;
-  float acc[4][4];
+  const int qa = 2 * q, qb = 2 * q + 1;
+  const int ka0 = qa * C, la = min(a.d, ka0 + C);
+  const int kb0 = qb * C, lb = min(a.d, kb0 + C);  // lb <= kb0: no chunk B
+  // warp w of the group, lane l, quad u = l / 4: tq = 4 (w & 1) + 2 (u & 1) + (l & 1),
+  // rq = 8 (w >> 1) + 2 (u >> 1) + ((l >> 1) & 1)
+  const int lq = g & 31, u4 = lq >> 2, wg = g >> 5;
+  const int tq = ((wg & 1) << 2) | ((u4 & 1) << 1) | (lq & 1);
+  const int rq = ((wg >> 1) << 3) | ((u4 >> 1) << 1) | ((lq >> 1) & 1);
+  float2 acc[4][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+    for (int j = 0; j < 4; ++j) acc[i][j] = make_float2(0.0f, 0.0f);
 
   float* stage0 = smem + q * 2 * kStageFloats;
-  if (q < nq) {
+  if (qa < nq) {
     Slice<T> sl;
-    sl.fetch(a, g, tok0, kbeg, kend);
-    sl.store(stage0, stage0 + kTokens * kP, g);
+    sl.init(a, g, tok0);
+    sl.fetch(g, ka0, la, kb0, lb);
+    sl.store(stage0, g);
     group_sync(q);
     int s = 0;
-    for (int k0 = kbeg; k0 < kend; k0 += kKS, s ^= 1) {
-      const bool more = k0 + kKS < kend;
-      if (more) sl.fetch(a, g, tok0, k0 + kKS, kend);  // in flight during the compute below
-      const float* xs = stage0 + s * kStageFloats;
-      const float* xb = xs + (4 * tq) * kP;
-      const float* wb = xs + kTokens * kP + rq * kP;
-      const int kmax = min(kKS, kend - k0);  // a multiple of 8 (bf16) or 4 (fp32)
-      for (int k = 0; k < kmax; k += 4) {
-        float4 xv[4], wv[4];
+    for (int o = 0; ka0 + o < la; o += kKS, s ^= 1) {
+      const bool more = ka0 + o + kKS < la;
+      if (more) sl.fetch(g, ka0 + o + kKS, la, kb0 + o + kKS, lb);  // in flight during the compute
+      const float* st = stage0 + s * kStageFloats;
+      const float* xb = st + tq * kXP;
+      const float* wb = st + (kTokens + rq) * kWP;
+      const int kmax = min(kKS, la - ka0 - o);  // a multiple of 8 (bf16) or 4 (fp32)
+      if (kmax == kKS) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) xv[i] = *reinterpret_cast<const float4*>(xb + i * kP + k);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) wv[j] = *reinterpret_cast<const float4*>(wb + 16 * j * kP + k);
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            acc[i][j] = __fmaf_rn(xv[i].x, wv[j].x, acc[i][j]);
-            acc[i][j] = __fmaf_rn(xv[i].y, wv[j].y, acc[i][j]);
-            acc[i][j] = __fmaf_rn(xv[i].z, wv[j].z, acc[i][j]);
-            acc[i][j] = __fmaf_rn(xv[i].w, wv[j].w, acc[i][j]);
-          }
+        for (int kk = 0; kk < kKS / 2; ++kk) mma_k2(acc, xb, wb, kk);
+      } else {
+        for (int kk = 0; kk < kmax / 2; ++kk) mma_k2(acc, xb, wb, kk);
       }
-      if (more) {
-        float* nx = stage0 + (s ^ 1) * kStageFloats;  // last read two slices ago
-        sl.store(nx, nx + kTokens * kP, g);
-      }
+      if (more) sl.store(stage0 + (s ^ 1) * kStageFloats, g);  // last read two slices ago
       group_sync(q);
     }
   }
   __syncthreads();  // staging buffers are reused for the partials below
-  float* part = smem;  // [nq][32 tokens][64 rows]
-  if (q < nq) {
+  float* part = smem;  // [chunk][32 tokens][64 rows]
+  if (qa < nq) {
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) part[(q * kTokens + 4 * tq + i) * kRows + rq + 16 * j] = acc[i][j];
+      for (int j = 0; j < 4; ++j) {
+        const int t = tq + 8 * i, r = rq + 16 * j;
+        part[(qa * kTokens + t) * kRows + r] = acc[i][j].x;
+        if (qb < nq) part[(qb * kTokens + t) * kRows + r] = acc[i][j].y;
+      }
   }
   __syncthreads();
   for (int idx = tid; idx < kTokens * kRows; idx += kThreads) {
@@ -271,6 +343,7 @@ __global__ void __launch_bounds__(kThreads, 1) router_kernel(Args a) {
   // ---------------- softmax and selection: one warp per token
   const int warp = tid >> 5, lane = tid & 31;
   const int e0 = lane, e1 = lane + 32;
+  const int k = (a.mode == DSCA_ROUTE_SWITCH_TOP1) ? 1 : a.top_k;
   for (int tl = warp; tl < kTokens; tl += kThreads / 32) {
     const int t = tok0 + tl;
     const bool valid = t < a.T;
@@ -284,110 +357,83 @@ __global__ void __launch_bounds__(kThreads, 1) router_kernel(Args a) {
         a.shared_gate[t] = 1.0f / (1.0f + expf(-z));
       }
     }
-    float m = fmaxf((e0 < E) ? l0 : -INFINITY, (e1 < E) ? l1 : -INFINITY);
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    // row max through an order-preserving integer key (one warp reduction)
+    const uint32_t mkey = __reduce_max_sync(0xffffffffu, max((e0 < E) ? ord_key(l0) : 0u, (e1 < E) ? ord_key(l1) : 0u));
+    const float m = ord_val(mkey);
     const float x0 = (e0 < E) ? exp_neg(__fsub_rn(l0, m)) : 0.0f;
     const float x1 = (e1 < E) ? exp_neg(__fsub_rn(l1, m)) : 0.0f;
     float ps = (e0 < E) ? __fadd_rn(0.0f, x0) : 0.0f;
     if (e1 < E) ps = __fadd_rn(ps, x1);
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) ps = __fadd_rn(ps, __shfl_xor_sync(0xffffffffu, ps, off));
-    float p0 = (e0 < E) ? __fdiv_rn(x0, ps) : -INFINITY;
-    float p1 = (e1 < E) ? __fdiv_rn(x1, ps) : -INFINITY;
+    float p0 = (e0 < E) ? __fdiv_rn(x0, ps) : 0.0f;
+    float p1 = (e1 < E) ? __fdiv_rn(x1, ps) : 0.0f;
+    if (a.mode == DSCA_ROUTE_SWITCH_TOP1 && tau_bf16) {
+      p0 = round_bf16(p0);
+      p1 = round_bf16(p1);
+    }
 
-    if (a.mode == DSCA_ROUTE_SWITCH_TOP1) {
-      if (tau_bf16) {
-        p0 = (e0 < E) ? round_bf16(p0) : -INFINITY;
-        p1 = (e1 < E) ? round_bf16(p1) : -INFINITY;
-      }
-      float bv = p0;
-      int bi = e0;
-      if (p1 > bv) { bv = p1; bi = e1; }
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-      }
-      if (lane == 0) {
-        ids_s[tl][0] = valid ? bi : -1;
-        if (valid) {
-          a.topk_ids[t] = bi;
-          a.topk_w[t] = bv;
-          if (a.expert_index != nullptr) a.expert_index[t] = bi;
+    // k rounds of (probability desc, expert id asc): probabilities are >= +0, so their bits
+    // order like the values; key = bits + 1, 0 = no candidate.  Lane j keeps the j-th choice;
+    // every lane sums the choices in rank order.
+    float my_p = 0.0f, sum = 0.0f;
+    int my_id = -1;
+    bool taken0 = !(e0 < E), taken1 = !(e1 < E);
+    for (int j = 0; j < k; ++j) {
+      const uint32_t k0 = taken0 ? 0u : __float_as_uint(p0) + 1u;
+      const uint32_t k1 = taken1 ? 0u : __float_as_uint(p1) + 1u;
+      const uint32_t best = __reduce_max_sync(0xffffffffu, max(k0, k1));
+      const uint32_t cand = (k0 == best) ? (uint32_t)e0 : ((k1 == best) ? (uint32_t)e1 : 0xffffffffu);
+      const int bi = (int)__reduce_min_sync(0xffffffffu, cand);
+      const float bv = __uint_as_float(best - 1u);
+      if (bi == e0) taken0 = true;
+      if (bi == e1) taken1 = true;
+      if (lane == j) { my_p = bv; my_id = bi; }
+      sum = __fadd_rn(sum, bv);
+    }
+    if (lane < k) {
+      ids_s[tl][lane] = valid ? my_id : -1;
+      if (valid) {
+        float w = my_p;
+        if (a.mode != DSCA_ROUTE_SWITCH_TOP1) {
+          if (a.norm_topk) w = __fdiv_rn(my_p, sum);
+          if (a.weight_round_bf16) w = round_bf16(w);
         }
-      }
-    } else {
-      bool taken0 = !(e0 < E), taken1 = !(e1 < E);
-      float sel[DSCA_MAX_TOPK];
-      int seli[DSCA_MAX_TOPK];
-      for (int j = 0; j < a.top_k; ++j) {
-        float bv = -INFINITY;
-        int bi = 1 << 30;
-        if (!taken0) { bv = p0; bi = e0; }
-        if (!taken1 && (p1 > bv || bi == (1 << 30))) { bv = p1; bi = e1; }
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) {
-          const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-          const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-          if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-        }
-        if (bi == e0) taken0 = true;
-        if (bi == e1) taken1 = true;
-        sel[j] = bv;
-        seli[j] = bi;
-      }
-      if (lane == 0) {
-        float sum = 0.0f;
-        if (a.norm_topk)
-          for (int j = 0; j < a.top_k; ++j) sum = __fadd_rn(sum, sel[j]);
-        for (int j = 0; j < a.top_k; ++j) {
-          ids_s[tl][j] = valid ? seli[j] : -1;
-          if (valid) {
-            float w = a.norm_topk ? __fdiv_rn(sel[j], sum) : sel[j];
-            if (a.weight_round_bf16) w = round_bf16(w);
-            a.topk_ids[(size_t)t * a.top_k + j] = seli[j];
-            a.topk_w[(size_t)t * a.top_k + j] = w;
-          }
-        }
-        if (valid && a.expert_index != nullptr) a.expert_index[t] = seli[0];
+        a.topk_ids[(size_t)t * k + lane] = my_id;
+        a.topk_w[(size_t)t * k + lane] = w;
+        if (lane == 0 && a.expert_index != nullptr) a.expert_index[t] = my_id;
+        atomicOr(&emask[my_id], 1u << tl);
       }
     }
   }
   __syncthreads();
 
-  // ---------------- per-block histogram and stable in-block ranks (token, then slot order)
-  const int k = (a.mode == DSCA_ROUTE_SWITCH_TOP1) ? 1 : a.top_k;
+  // ---------------- per-block histogram and stable in-block ranks (token, then slot order):
+  // an expert appears at most once per token, so the rank of (t, j) is the number of earlier
+  // tokens of the block routed to the same expert
   for (int e = tid; e < E; e += kThreads) {
-    int c = 0;
-    for (int tl = 0; tl < kTokens; ++tl)
-      for (int j = 0; j < k; ++j) c += (ids_s[tl][j] == e);
-    a.block_hist[(size_t)blockIdx.x * E + e] = c;
+    a.block_hist[(size_t)blockIdx.x * E + e] = __popc(emask[e]);
+    if (a.done_counter != nullptr) __threadfence();  // the histogram before this CTA's arrival
   }
   for (int idx = tid; idx < kTokens * k; idx += kThreads) {
     const int tl = idx / k, j = idx % k;
     const int t = tok0 + tl;
     const int e = ids_s[tl][j];
     if (t >= a.T || e < 0) continue;
-    int r = 0;
-    for (int u = 0; u < tl; ++u)
-      for (int jj = 0; jj < k; ++jj) r += (ids_s[u][jj] == e);
-    a.local_rank[(size_t)t * k + j] = r;
+    a.local_rank[(size_t)t * k + j] = __popc(emask[e] & ((1u << tl) - 1u));
   }
 
   // ---------------- fused scan: the last CTA to finish
   if (a.done_counter != nullptr) {
-    __threadfence();
     __syncthreads();
     if (tid == 0) {
       const uint32_t prev = atomicAdd(a.done_counter, 1u);
       is_last = prev == gridDim.x - 1;
+      __threadfence();
     }
     __syncthreads();
     if (is_last) {
-      __threadfence();
-      scan_blocks(a, gridDim.x, cnt_s);
+      scan_blocks(a, gridDim.x, reinterpret_cast<int*>(smem), (int)(kSmemBytes / sizeof(int)), run_s, seg_s);
       if (tid == 0) *a.done_counter = 0u;  // ready for the next launch (stream ordered)
     }
   }

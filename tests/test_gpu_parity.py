@@ -359,7 +359,7 @@ def test_repeat_calls_are_deterministic(cuda):
     assert torch.equal(a, b)
 
 
-@pytest.mark.parametrize("T,k,E", [(4096, 4, 60), (33, 1, 8), (20000, 8, 64)])
+@pytest.mark.parametrize("T,k,E", [(4096, 4, 60), (33, 1, 8), (20000, 8, 63)])
 def test_fused_scan_matches_separate_scan(cuda, T, k, E):
     """The router's last-CTA scan gives the same counts, offsets and block bases as the separate
     scan launch, and leaves its completion counter at zero (two fused calls in a row agree)."""
