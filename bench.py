@@ -56,6 +56,9 @@ def parse():
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="expert-parallel exchange: fused NVLink kernels (default) or the NCCL baseline")
     ap.add_argument("--ep-return", choices=["overlap", "fused"], default="overlap")
+    ap.add_argument("--tile-rows", type=int, choices=[0, 128, 256], default=0,
+                    help="bf16 expert GEMM tiles: 0 = default per GEMM, 256 = CTA pairs (cta_group::2, "
+                         "weights as M), 128 = one CTA per 128-token tile")
     ap.add_argument("--fp8", action="store_true",
                     help="fp8-e4m3 expert weights with per-output-channel scales (bf16 activations)")
     ap.add_argument("--router", choices=["zipf", "uniform"], default="zipf",
@@ -78,6 +81,19 @@ def flops_and_bytes(w, T, rows_routed, E_touched):
            + 2.0 * E_touched * m * d * I         # experts touched at least once
            + (2.0 * 3 * d * Is + 2.0 * d if Is else 0.0))
     return router, g1, g2, hbm
+
+
+def launches_per_step(world, exchange, eng):
+    """This library's kernel launches in one forward (the timed step)."""
+    if world == 1:
+        # router (+ fused scan), permute, GEMM1, GEMM2, combine
+        return 5 + (0 if eng.fuse_scan else 1)
+    if exchange == "p2p":
+        # router, plan, dispatch, shared GEMM1, wait, routed GEMM1, routed GEMM2 (+ return kernel),
+        # shared GEMM2, wait, combine
+        return 10 + (1 if eng.ep_return == "overlap" else 0) + (0 if eng.fuse_scan else 1)
+    # router, permute into the send buffer, GEMM1, GEMM2, combine (NCCL does the exchange)
+    return 5 + (0 if eng.fuse_scan else 1)
 
 
 def load_peaks():
@@ -327,6 +343,7 @@ def main():
     eng, x, Wr, raw, info = build_block(w, T, rank, world, dev, args.eq_tokens, group, fp8=args.fp8)
     eng.exchange = args.exchange
     eng.ep_return = args.ep_return
+    eng.tile_rows = args.tile_rows
     peaks = load_peaks()
     if args.once:
         eng.forward(x)
@@ -479,11 +496,14 @@ def main():
                        "plan": f"harmony eq_tokens={args.eq_tokens}" if world > 1 else "local",
                        "l2": "flushed (256 MiB write, untimed) before every timed step",
                        "parallelism": f"ep{world}",
-                       "exchange": (f"{args.exchange} (return {args.ep_return})" if world > 1 else "none")},
+                       "exchange": (f"{args.exchange} (return {args.ep_return})" if world > 1 else "none"),
+                       "gemm_tiles": {0: "GEMM1 128-token single-CTA tiles, GEMM2 CTA-pair swap-AB tiles",
+                                      128: "128-token single-CTA tiles",
+                                      256: "CTA-pair swap-AB tiles (256 channels x <=256 tokens)"}[args.tile_rows]},
             "roofline": roof, "layer_roofline": layer_roof, "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * w["d"] * 2,
                     "d2h_bytes_per_step": T * w["d"] * 2},
-            "gpu_launches": 6 * args.steps, "clocks": clk,
+            "gpu_launches": launches_per_step(world, args.exchange, eng) * args.steps, "clocks": clk,
             "phases_ms": phase_ms,
         }
         print(json.dumps(line), flush=True)

@@ -52,7 +52,8 @@ class FfnArgs(ctypes.Structure):
                 ("h", _vp), ("y", _vp), ("shared_rows", _i), ("shared_n1p", _i), ("shared_ip", _i),
                 ("xs", _vp), ("ws1", _vp), ("ws2", _vp), ("hs", _vp), ("ys", _vp), ("err", _vp),
                 ("num_ctas", _i), ("phases", _i), ("ep_ctx", _vp), ("segments", _i),
-                ("w1_scale", _vp), ("w2_scale", _vp), ("ws1_scale", _vp), ("ws2_scale", _vp)]
+                ("w1_scale", _vp), ("w2_scale", _vp), ("ws1_scale", _vp), ("ws2_scale", _vp),
+                ("tile_rows", _i)]
 
 
 MAX_GPUS = 8

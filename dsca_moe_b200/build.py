@@ -25,7 +25,7 @@ NVCC = shutil.which("nvcc") or os.path.join(CUDA_HOME, "bin", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
               "--expt-relaxed-constexpr", "-I" + INCLUDE] + ARCH
-CU_SOURCES = ["router.cu", "dispatch.cu", "gemm_sm100.cu", "gemm_sm100_fp8.cu", "gemm_simt.cu", "abi.cu",
+CU_SOURCES = ["router.cu", "dispatch.cu", "gemm_sm100.cu", "gemm_sm100_pair.cu", "gemm_sm100_fp8.cu", "gemm_simt.cu", "abi.cu",
               "ffn_static_scratch.cu", "ep.cu"]
 CXX_SOURCES = ["plan.cpp"]
 
@@ -40,7 +40,7 @@ def _newer(src_list, target):
 def build(verbose: bool = False, ptxas_verbose: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
     os.makedirs(LIBDIR, exist_ok=True)
-    headers = [os.path.join(CSRC, "common.cuh"), os.path.join(CSRC, "ep.cuh"), os.path.join(INCLUDE, "dsca_b200.h")]
+    headers = [os.path.join(CSRC, "common.cuh"), os.path.join(CSRC, "ep.cuh"), os.path.join(CSRC, "gemm_sm100.cuh"), os.path.join(INCLUDE, "dsca_b200.h")]
     objs = []
     for src in CU_SOURCES:
         s = os.path.join(CSRC, src)

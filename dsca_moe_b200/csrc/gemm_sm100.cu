@@ -1,13 +1,14 @@
-// K5 — grouped expert GEMM on the 5th-generation tensor cores (sm_100a).
+// K5 — grouped expert GEMM on the 5th-generation tensor cores (sm_100a), single-CTA tiles.
 //
 // One persistent kernel computes C[g] = epilogue(A[rows of group g] . B[weight(g)]^T) for every
 // row group g of up to two segments (segment 0: routed experts with device-side row offsets;
 // segment 1: the shared expert over all tokens).  It replaces the per-expert loop
 // tokens[idx] = expert(tokens[idx]) (src/qosmoe/async_cpu.py:137-173,
 // src/qosmoe/moe_layer.py:226-253, qwen_ep_adapter/qwen_ep.py:85-89) and the shared expert
-// (qwen_ep.py:94).
+// (qwen_ep.py:94).  This file holds the 128-row tile form (tile_rows = 128); the default
+// 256-row CTA-pair form is in gemm_sm100_pair.cu.
 //
-// Tile: 128 (rows) x 256 (cols) x 64 (K) per stage, bf16 in, fp32 accumulate in TMEM.
+// Tile: 128 (token rows) x 256 (weight rows) x 64 (K) per stage, bf16 in, fp32 accumulate in TMEM.
 //   warp 0      TMA producer (one thread): A 128x64 and B 256x64 tiles, 128-byte swizzle,
 //               4-stage ring guarded by full/empty mbarriers.  No multicast.
 //   warp 1      TMEM allocator (512 columns = two 128x256 fp32 accumulators) and MMA issuer
@@ -16,125 +17,26 @@
 //   warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns, activation, bf16 pack, masked
 //               16-byte stores; the accumulator is released as soon as it has been read, so
 //               the next tile's MMAs overlap this tile's stores.
-// Tiles are enumerated (segment, group, M tile, N tile) with N fastest; CTA i takes tiles
-// i, i + grid, ...  Group row offsets are read on the device, so no host sync is needed.
+// SwiGLU weights are packed in 128-row blocks of 64 gate rows then the 64 matching up rows, so a
+// 256-column accumulator holds two (gate, up) blocks.
+// Tiles follow the cost-ordered boustrophedon schedule of gemm_sm100.cuh (full tiles of the
+// longer-K segment first, partial tiles last).  Group row offsets are read on the device, so no
+// host sync is needed.
 // Every wait is bounded (2 s): on a timeout the kernel records DSCA_ERR_WAIT_TIMEOUT in the
 // error word, drains its own outstanding copies and MMAs, frees TMEM and returns.
-#include "common.cuh"
-#include "ep.cuh"
+#include <algorithm>
+
+#include "gemm_sm100.cuh"
 
 namespace dsca {
 namespace gemm {
 
-constexpr int BM = 128, BN = 256, BK = 64;
+constexpr int BM = 128;
 constexpr int kStages = 4;
 constexpr int kABytes = BM * BK * 2;
 constexpr int kBBytes = BN * BK * 2;
 constexpr int kStageBytes = kABytes + kBBytes;
-constexpr int kThreads = 192;
-constexpr int kTmemCols = 512;
-constexpr int kMaxGroups = 256;
 constexpr int kSmemBytes = kStages * kStageBytes + 1024;  // + alignment slack
-
-enum Epi { kEpiSwiGLU = 0, kEpiReLU = 1, kEpiStore = 2 };
-
-struct Segment {
-  const int32_t* group_offsets;  // device [ngroups + 1], or null = one group of `rows`
-  const int32_t* group_weight;   // device [ngroups], or null = identity
-  int ngroups;
-  int rows;
-  int n_tiles;
-  int b_rows_per_group;
-  int k_blocks;
-  __nv_bfloat16* c;
-  int ldc;
-  int n_store;
-  int capacity;
-  // expert parallel: when set, output row r of group e belongs to chunk (src, e) of the
-  // receive buffer and is stored straight into rank src's return buffer (peer memory)
-  const ep::Ctx* ep;
-};
-
-struct Params {
-  Segment seg[2];
-  int nseg;
-  int epi;
-  int32_t* err;
-  ep::Ctx* ep_signal;  // set: signal the return flag at every peer once the grid is done
-};
-
-struct TileInfo {
-  int seg, group, row0, rows_valid, b_row0, n_blk;
-};
-
-// Destination row pointer of a routed output row in the expert-parallel return path.
-__device__ __forceinline__ __nv_bfloat16* ep_return_row(const ep::Ctx* c, int e, int r, int ldc) {
-  for (int src = 0; src < c->G; ++src) {
-    const int cs = c->chunk_start[e][src];
-    if (r >= cs && r < cs + c->chunk_len[e][src])
-      return reinterpret_cast<__nv_bfloat16*>(c->ret[src]) + (size_t)(c->ret_start[e][src] + r - cs) * ldc;
-  }
-  return nullptr;
-}
-
-struct SmemCtl {
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
-  uint64_t tmem_full[2];
-  uint64_t tmem_empty[2];
-  uint64_t mma_done;
-  uint32_t tmem_base;
-  int abort_flag;
-  int total_tiles;
-  int seg0_tiles;
-  int tile_start[kMaxGroups + 1];
-  int goff[kMaxGroups + 1];
-  int gw[kMaxGroups];
-};
-
-__device__ __forceinline__ TileInfo decode(const Params& p, const SmemCtl& s, int tile) {
-  TileInfo ti;
-  if (tile < s.seg0_tiles) {
-    const Segment& sg = p.seg[0];
-    // upper_bound over tile_start[0..ngroups]
-    int lo = 0, hi = sg.ngroups;  // find g with tile_start[g] <= tile < tile_start[g+1]
-    while (hi - lo > 1) {
-      int mid = (lo + hi) >> 1;
-      if (s.tile_start[mid] <= tile) lo = mid; else hi = mid;
-    }
-    int g = lo;
-    int local = tile - s.tile_start[g];
-    int m_blk = local / sg.n_tiles;
-    ti.n_blk = local - m_blk * sg.n_tiles;
-    int rows_g = s.goff[g + 1] - s.goff[g];
-    ti.seg = 0;
-    ti.group = g;
-    ti.row0 = s.goff[g] + m_blk * BM;
-    ti.rows_valid = min(BM, rows_g - m_blk * BM);
-    ti.b_row0 = s.gw[g] * sg.b_rows_per_group + ti.n_blk * BN;
-  } else {
-    const Segment& sg = p.seg[1];
-    int local = tile - s.seg0_tiles;
-    int m_blk = local / sg.n_tiles;
-    ti.n_blk = local - m_blk * sg.n_tiles;
-    ti.seg = 1;
-    ti.group = 0;
-    ti.row0 = m_blk * BM;
-    ti.rows_valid = min(BM, sg.rows - ti.row0);
-    ti.b_row0 = ti.n_blk * BN;
-  }
-  return ti;
-}
-
-// Bounded wait that ignores the abort flag (used to drain in-flight work before exit).
-__device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
-  const uint64_t t0 = globaltimer_ns();
-  while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer_ns() - t0 > kWaitLimitNs) return;
-  }
-}
-
-__device__ __forceinline__ float silu(float g) { return g / (1.0f + __expf(-g)); }
 
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -176,48 +78,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc(smem_u32(&ctl.tmem_base), kTmemCols);
     tmem_relinquish();
   }
-  // group table of segment 0 (device offsets -> tile prefix), computed by warp 2
-  if (warp == 2) {
-    const Segment& sg = p.seg[0];
-    const int ng = sg.ngroups;
-    for (int g = lane; g <= ng; g += 32)
-      ctl.goff[g] = sg.group_offsets ? sg.group_offsets[g] : (g == 0 ? 0 : sg.rows);
-    for (int g = lane; g < ng; g += 32) ctl.gw[g] = sg.group_weight ? sg.group_weight[g] : g;
-    __syncwarp();
-    // each lane scans a contiguous run of groups, then a warp scan stitches the runs
-    const int per = (ng + 31) / 32;
-    const int g0 = min(ng, lane * per), g1 = min(ng, g0 + per);
-    int run = 0;
-    for (int g = g0; g < g1; ++g) {
-      int rows_g = ctl.goff[g + 1] - ctl.goff[g];
-      if (rows_g < 0 || ctl.goff[g + 1] > sg.capacity) {
-        record_error(p.err, kErrCapacity);
-        rows_g = 0;
-      }
-      run += ((rows_g + BM - 1) / BM) * sg.n_tiles;
-    }
-    int incl = run;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      int v = __shfl_up_sync(0xffffffffu, incl, off);
-      if (lane >= off) incl += v;
-    }
-    int excl = incl - run;
-    for (int g = g0; g < g1; ++g) {
-      ctl.tile_start[g] = excl;
-      int rows_g = max(0, ctl.goff[g + 1] - ctl.goff[g]);
-      if (ctl.goff[g + 1] > sg.capacity) rows_g = 0;
-      excl += ((rows_g + BM - 1) / BM) * sg.n_tiles;
-    }
-    int total0 = __shfl_sync(0xffffffffu, incl, 31);
-    if (lane == 0) {
-      ctl.tile_start[ng] = total0;
-      ctl.seg0_tiles = total0;
-      int total1 = 0;
-      if (p.nseg > 1) total1 = ((p.seg[1].rows + BM - 1) / BM) * p.seg[1].n_tiles;
-      ctl.total_tiles = total0 + total1;
-    }
-  }
+  if (warp == 2) build_group_table<BM>(p, ctl, lane);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -232,8 +93,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       int pending_phase[kStages];
       for (int i = 0; i < kStages; ++i) pending_phase[i] = -1;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
-        const TileInfo ti = decode(p, ctl, tile);
+      for (int r = 0; ok; ++r) {
+        const int tile = sched_tile(r, (int)blockIdx.x, (int)gridDim.x);
+        if (tile >= total) break;
+        const TileInfo ti = decode<BM>(p, ctl, tile);
         const CUtensorMap* ma = ti.seg == 0 ? &tmA0 : &tmA1;
         const CUtensorMap* mb = ti.seg == 0 ? &tmB0 : &tmB1;
         const int kb_n = p.seg[ti.seg].k_blocks;
@@ -261,8 +124,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t ph = 0;
       int it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++it) {
-        const TileInfo ti = decode(p, ctl, tile);
+      for (int r = 0; ok; ++r, ++it) {
+        const int tile = sched_tile(r, (int)blockIdx.x, (int)gridDim.x);
+        if (tile >= total) break;
+        const TileInfo ti = decode<BM>(p, ctl, tile);
         const int acc = it & 1;
         const uint32_t acc_ph = (uint32_t)((it >> 1) & 1);
         if (!mbar_wait(smem_u32(&ctl.tmem_empty[acc]), acc_ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
@@ -295,8 +160,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     const int r_in_tile = q * 32 + lane;
     int it = 0;
-    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
-      const TileInfo ti = decode(p, ctl, tile);
+    for (int r = 0;; ++r, ++it) {
+      const int tile = sched_tile(r, (int)blockIdx.x, (int)gridDim.x);
+      if (tile >= total) break;
+      const TileInfo ti = decode<BM>(p, ctl, tile);
       const Segment& sg = p.seg[ti.seg];
       const int acc = it & 1;
       const uint32_t acc_ph = (uint32_t)((it >> 1) & 1);
@@ -322,9 +189,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int col0 = ti.n_blk * (BN / 2);
 #pragma unroll 1
         for (int c = 0; c < BN / 2; c += 32) {
+          // accumulator columns: 128-column blocks of 64 gate then the 64 matching up channels
+          const int gc = (c >> 6) * 128 + (c & 63);
           uint32_t g[32], u[32];
-          tmem_ld32(taddr + c, g);
-          tmem_ld32(taddr + BN / 2 + c, u);
+          tmem_ld32(taddr + gc, g);
+          tmem_ld32(taddr + gc + 64, u);
           tmem_wait_ld();
           uint32_t packed[16];
 #pragma unroll
@@ -403,7 +272,7 @@ static PFN_encodeTiled get_encode_fn() {
 }
 
 // 2-D bf16 tensor map over a row-major [rows, cols] matrix, box = box_rows x 64, 128B swizzle.
-static int make_map_bf16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+int make_map_bf16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
   PFN_encodeTiled enc = get_encode_fn();
   if (enc == nullptr) return DSCA_ERR_CUDA;
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (cols * 2) % 16 != 0) return DSCA_ERR_BAD_ARG;
@@ -417,49 +286,55 @@ static int make_map_bf16(CUtensorMap* m, const void* base, uint64_t rows, uint64
   return r == CUDA_SUCCESS ? DSCA_OK : DSCA_ERR_CUDA;
 }
 
-static int launch_one(int epi, const CUtensorMap& a0, const CUtensorMap& b0, const CUtensorMap& a1,
-                      const CUtensorMap& b1, const gemm::Params& p, int grid, cudaStream_t stream) {
-  static bool attr_set[3] = {false, false, false};
-  cudaError_t e = cudaSuccess;
-  switch (epi) {
-    case gemm::kEpiSwiGLU:
-      if (!attr_set[0]) {
-        e = cudaFuncSetAttribute(gemm::grouped_gemm_kernel<gemm::kEpiSwiGLU>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::kSmemBytes);
-        attr_set[0] = e == cudaSuccess;
-      }
-      if (e == cudaSuccess)
-        gemm::grouped_gemm_kernel<gemm::kEpiSwiGLU><<<grid, gemm::kThreads, gemm::kSmemBytes, stream>>>(a0, b0, a1, b1, p);
-      break;
-    case gemm::kEpiReLU:
-      if (!attr_set[1]) {
-        e = cudaFuncSetAttribute(gemm::grouped_gemm_kernel<gemm::kEpiReLU>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::kSmemBytes);
-        attr_set[1] = e == cudaSuccess;
-      }
-      if (e == cudaSuccess)
-        gemm::grouped_gemm_kernel<gemm::kEpiReLU><<<grid, gemm::kThreads, gemm::kSmemBytes, stream>>>(a0, b0, a1, b1, p);
-      break;
-    default:
-      if (!attr_set[2]) {
-        e = cudaFuncSetAttribute(gemm::grouped_gemm_kernel<gemm::kEpiStore>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::kSmemBytes);
-        attr_set[2] = e == cudaSuccess;
-      }
-      if (e == cudaSuccess)
-        gemm::grouped_gemm_kernel<gemm::kEpiStore><<<grid, gemm::kThreads, gemm::kSmemBytes, stream>>>(a0, b0, a1, b1, p);
-      break;
+template <int EPI>
+static int launch_kernel(const CUtensorMap& a0, const CUtensorMap& b0, const CUtensorMap& a1, const CUtensorMap& b1,
+                         const gemm::Params& p, int grid, cudaStream_t stream) {
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(gemm::grouped_gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             gemm::kSmemBytes) != cudaSuccess)
+      return DSCA_ERR_CUDA;
+    attr_set = true;
   }
-  if (e != cudaSuccess) return DSCA_ERR_CUDA;
+  gemm::grouped_gemm_kernel<EPI><<<grid, gemm::kThreads, gemm::kSmemBytes, stream>>>(a0, b0, a1, b1, p);
   return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
 }
 
+static int launch_one(int epi, const CUtensorMap& a0, const CUtensorMap& b0, const CUtensorMap& a1,
+                      const CUtensorMap& b1, const gemm::Params& p, int grid, cudaStream_t stream) {
+  switch (epi) {
+    case gemm::kEpiSwiGLU: return launch_kernel<gemm::kEpiSwiGLU>(a0, b0, a1, b1, p, grid, stream);
+    case gemm::kEpiReLU: return launch_kernel<gemm::kEpiReLU>(a0, b0, a1, b1, p, grid, stream);
+    default: return launch_kernel<gemm::kEpiStore>(a0, b0, a1, b1, p, grid, stream);
+  }
+}
+
 int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t stream) {
+  const int phases_all = f->phases == 0 ? 3 : f->phases;
+  if (f->tile_rows == 256) return launch_grouped_ffn_bf16_pair(f, num_sms, stream);
+  if (f->tile_rows == 0) {
+    // default: the CTA-pair swap-AB kernel for GEMM2 (and a ReLU GEMM1); single-CTA tiles for
+    // the SwiGLU GEMM1, whose gate and up halves then sit in the same accumulator row
+    const bool glu = f->act == DSCA_ACT_SWIGLU;
+    dsca_ffn_args g = *f;
+    int rc;
+    if (phases_all & 1) {
+      g.phases = 1;
+      g.tile_rows = glu ? 128 : 256;
+      if ((rc = launch_grouped_ffn_bf16(&g, num_sms, stream))) return rc;
+    }
+    if (phases_all & 2) {
+      g.phases = 2;
+      g.tile_rows = 256;
+      if ((rc = launch_grouped_ffn_bf16(&g, num_sms, stream))) return rc;
+    }
+    return DSCA_OK;
+  }
   const int grid = f->num_ctas > 0 ? f->num_ctas : num_sms;
   const int segs = f->segments == 0 ? 3 : f->segments;
   const bool shared = f->shared_rows > 0 && (segs & 2);
   const bool routed = (segs & 1) != 0;
-  const int phases = f->phases == 0 ? 3 : f->phases;
+  const int phases = phases_all;
   if (!routed && !shared) return DSCA_OK;
   int rc;
   // ---- GEMM1: h = act(a . w1^T)   (+ hs = act(xs . ws1^T))
@@ -479,6 +354,7 @@ int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t st
     p.epi = epi;
     p.err = f->err;
     p.nseg = shared ? 2 : 1;
+    p.seg_first = 0;  // equal K (the model width) in both segments
     gemm::Segment& s0 = p.seg[0];
     s0.group_offsets = f->group_offsets;
     s0.group_weight = f->group_weight;
@@ -523,6 +399,7 @@ int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t st
     p.epi = gemm::kEpiStore;
     p.err = f->err;
     p.nseg = shared ? 2 : 1;
+    p.seg_first = (shared && f->shared_ip > f->ip) ? 1 : 0;  // the longer K first
     p.ep_signal = routed ? static_cast<ep::Ctx*>(f->ep_ctx) : nullptr;
     gemm::Segment& s0 = p.seg[0];
     s0.ep = static_cast<const ep::Ctx*>(f->ep_ctx);

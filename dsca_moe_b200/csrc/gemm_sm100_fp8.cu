@@ -337,17 +337,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int col0 = ti.n_blk * (BN / 2);
 #pragma unroll 1
         for (int c = 0; c < BN / 2; c += 32) {
+          // packed columns: 128-column blocks of 64 gate then the 64 matching up channels
+          const int gc = (c >> 6) * 128 + (c & 63), uc = gc + 64;
           uint32_t g[32], u[32];
-          tmem_ld32(taddr + c, g);
-          tmem_ld32(taddr + BN / 2 + c, u);
+          tmem_ld32(taddr + gc, g);
+          tmem_ld32(taddr + uc, u);
           tmem_wait_ld();
           uint32_t packed[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const float g0 = __uint_as_float(g[2 * i]) * __ldg(sc + c + 2 * i);
-            const float g1 = __uint_as_float(g[2 * i + 1]) * __ldg(sc + c + 2 * i + 1);
-            const float u0 = __uint_as_float(u[2 * i]) * __ldg(sc + BN / 2 + c + 2 * i);
-            const float u1 = __uint_as_float(u[2 * i + 1]) * __ldg(sc + BN / 2 + c + 2 * i + 1);
+            const float g0 = __uint_as_float(g[2 * i]) * __ldg(sc + gc + 2 * i);
+            const float g1 = __uint_as_float(g[2 * i + 1]) * __ldg(sc + gc + 2 * i + 1);
+            const float u0 = __uint_as_float(u[2 * i]) * __ldg(sc + uc + 2 * i);
+            const float u1 = __uint_as_float(u[2 * i + 1]) * __ldg(sc + uc + 2 * i + 1);
             packed[i] = pack_f16x2(silu(g0) * u0, silu(g1) * u1);
           }
           const int col = col0 + c;

@@ -1,0 +1,501 @@
+// K5 — grouped expert GEMM on CTA pairs (tcgen05 cta_group::2), weights as the M operand.
+//
+// Same contract as gemm_sm100.cu (routed experts with device-side row offsets + the shared
+// expert, SwiGLU / ReLU / store epilogues, expert-parallel remote store), computed as
+// C^T = W . X^T: a tile is 256 weight rows (M) x up to 256 token rows (N) x K.
+//   * A cluster of two CTAs on neighbouring SMs runs tcgen05.mma.cta_group::2 (M256 N<=256 K16)
+//     issued by the even CTA.  Each CTA loads its own 128 weight rows and its half of the token
+//     rows, so an SM streams at most 32 KB per 64-wide K step (48 KB for a 128 x 256 single-CTA
+//     tile of the same tensor work).
+//   * The token count of a tile is rounded up to 16 only (the MMA N granularity), not to a tile
+//     height: an expert with 300 routed rows costs 256 + 48 token columns instead of 2 x 256
+//     rows.  Token rows are loaded in 32-row boxes, only as many as the tile needs.
+//   * Accumulator (per CTA): TMEM lane = weight row, column = token.  The epilogue writes each
+//     token's outputs as 64-byte row pieces (32 consecutive channels).  SwiGLU weights are
+//     packed in 128-row blocks of 64 gate rows then the 64 matching up rows, so one CTA holds
+//     both halves of its 64 channels: the warp reading gate lanes and the warp reading the
+//     matching up lanes swap half a chunk through shared memory and each finishes 16 tokens.
+//     Outputs are staged per warp in shared memory and written as 16-byte pieces of token rows.
+//   warp 0      TMA producer (one thread), 128-byte swizzle, 6-stage ring.  No multicast.
+//   warp 1      TMEM allocator (512 columns, two accumulators); in the even CTA the MMA issuer.
+//   warps 2-5   epilogue.
+// Both CTAs' loads complete on the even CTA's full barrier; the even CTA's commits arrive on the
+// empty / accumulator-full barriers of both CTAs; each epilogue warp arrives on the even CTA's
+// accumulator-empty barrier.  Every wait is bounded (2 s); on a timeout the kernel records
+// DSCA_ERR_WAIT_TIMEOUT, drains what it can observe, waits a bounded grace period for copies
+// completing on the peer's barriers, frees TMEM and returns.
+#include <algorithm>
+
+#include "gemm_sm100.cuh"
+
+namespace dsca {
+namespace gemm {
+namespace pair {
+
+constexpr int S = 6;                        // stages
+constexpr int TBN = 256;                    // token rows per tile (MMA N <= 256)
+constexpr int kWRows = 128;                 // weight rows per CTA
+constexpr int kBox = 32;                    // token rows per TMA box
+constexpr int kWBytes = kWRows * BK * 2;    // 16 KB
+constexpr int kTBytes = 128 * BK * 2;       // token slot per stage: up to 128 rows, 16 KB
+constexpr int kBoxBytes = kBox * BK * 2;    // 4 KB
+constexpr int kXchFloats = 2 * 2 * 32 * 32; // SwiGLU hand-off: 2 warp pairs x 2 buffers x 32 x 32
+constexpr int kStageElems = 32 * 32;         // per epilogue warp: 32 tokens x 32 channels, bf16
+constexpr int kSmemBytes = S * (kWBytes + kTBytes) + kXchFloats * 4 + 4 * kStageElems * 2 + 1024;
+
+// MMA N for a tile of `ntok` token rows: a multiple of 16 (each CTA holds N / 2 rows, a whole
+// number of 8-row swizzle atoms).
+__device__ __forceinline__ int tile_n(int ntok) { return max(16, (ntok + 15) & ~15); }
+
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    pair_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__ CUtensorMap tmT0,
+                     const __grid_constant__ CUtensorMap tmW1, const __grid_constant__ CUtensorMap tmT1,
+                     const Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  __shared__ SmemCtl ctl;
+  __shared__ uint64_t xbar[2][2][2];  // SwiGLU hand-off: [warp pair][buffer][sent, done]
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t smem_w = smem_u32(smem);
+  const uint32_t smem_t = smem_w + S * kWBytes;
+  float* xch = reinterpret_cast<float*>(smem + S * (kWBytes + kTBytes));
+  __nv_bfloat16* stage_all = reinterpret_cast<__nv_bfloat16*>(xch + kXchFloats);
+
+  const int warp = warp_id(), lane = lane_id();
+  volatile int* abort_flag = &ctl.abort_flag;
+  const uint32_t rank = cluster_ctarank();  // 0 = the CTA that issues the MMAs
+  const int unit = (int)(blockIdx.x >> 1), units = (int)(gridDim.x >> 1);
+
+  // ---- prologue: barriers, TMEM, group tile table
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(smem_u32(&ctl.full[s]), 1);
+      mbar_init(smem_u32(&ctl.empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&ctl.tmem_full[a]), 1);
+      mbar_init(smem_u32(&ctl.tmem_empty[a]), 8);  // 4 epilogue warps x 2 CTAs
+    }
+    mbar_init(smem_u32(&ctl.mma_done), 1);
+    for (int a = 0; a < 2; ++a)
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(smem_u32(&xbar[a][b][0]), 2);  // both warps of the pair sent their half
+        mbar_init(smem_u32(&xbar[a][b][1]), 2);  // both warps read the other's half
+      }
+    ctl.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmW0);
+    prefetch_tmap(&tmT0);
+    if (p.nseg > 1) {
+      prefetch_tmap(&tmW1);
+      prefetch_tmap(&tmT1);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(&ctl.tmem_base), kTmemCols);
+    tmem_relinquish_pair();
+  }
+  if (warp == 2) build_group_table<TBN>(p, ctl, lane);
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers exist before any cross-CTA signal
+  tc_fence_after();
+  const uint32_t tmem_base = ctl.tmem_base;
+  const int total = ctl.total_tiles;
+
+  if (warp == 0) {
+    // ---------------- TMA producer: this CTA's 128 weight rows and its half of the token rows
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      int pending_phase[S];
+      for (int i = 0; i < S; ++i) pending_phase[i] = -1;
+      bool ok = true;
+      for (int r = 0; ok; ++r) {
+        const int tile = sched_tile(r, unit, units);
+        if (tile >= total) break;
+        const TileInfo ti = decode<TBN>(p, ctl, tile);
+        const CUtensorMap* mw = ti.seg == 0 ? &tmW0 : &tmW1;
+        const CUtensorMap* mt = ti.seg == 0 ? &tmT0 : &tmT1;
+        const int half = tile_n(ti.rows_valid) / 2;
+        const int nbox = (half + kBox - 1) / kBox;
+        const uint32_t tx = 2u * (uint32_t)(kWBytes + nbox * kBoxBytes);
+        const int w_row = ti.b_row0 + kWRows * (int)rank;
+        const int t_row = ti.row0 + half * (int)rank;
+        const int kb_n = p.seg[ti.seg].k_blocks;
+        for (int kb = 0; kb < kb_n; ++kb) {
+          if (!mbar_wait(smem_u32(&ctl.empty[s]), ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
+          const uint32_t fb = smem_u32(&ctl.full[s]);
+          const uint32_t fb0 = mapa_shared(fb, 0);  // the even CTA's full barrier
+          if (rank == 0) mbar_arrive_expect_tx(fb, tx);
+          tma_load_2d_pair(smem_w + s * kWBytes, mw, fb0, kb * BK, w_row);
+          for (int b = 0; b < nbox; ++b)
+            tma_load_2d_pair(smem_t + s * kTBytes + b * kBoxBytes, mt, fb0, kb * BK, t_row + b * kBox);
+          pending_phase[s] = (int)ph;
+          if (++s == S) { s = 0; ph ^= 1u; }
+        }
+      }
+      if (!ok && rank == 0) {
+        // drain: the last armed phase of every stage must complete before the CTA exits (this
+        // also covers the odd CTA's loads, which complete on these barriers)
+        for (int i = 0; i < S; ++i)
+          if (pending_phase[i] >= 0) mbar_drain(smem_u32(&ctl.full[i]), (uint32_t)pending_phase[i]);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (even CTA)
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc_m = idesc_bf16_f32(256, 0);
+      int s = 0;
+      uint32_t ph = 0;
+      int it = 0;
+      bool ok = true;
+      for (int r = 0; ok; ++r, ++it) {
+        const int tile = sched_tile(r, unit, units);
+        if (tile >= total) break;
+        const TileInfo ti = decode<TBN>(p, ctl, tile);
+        const uint32_t idesc = idesc_m | ((uint32_t)(tile_n(ti.rows_valid) >> 3) << 17);
+        const int acc = it & 1;
+        const uint32_t acc_ph = (uint32_t)((it >> 1) & 1);
+        if (!mbar_wait(smem_u32(&ctl.tmem_empty[acc]), acc_ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * 256);
+        const int kb_n = p.seg[ti.seg].k_blocks;
+        for (int kb = 0; kb < kb_n; ++kb) {
+          if (!mbar_wait(smem_u32(&ctl.full[s]), ph, abort_flag, p.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t wdesc = sw128_kmajor_desc(smem_w + s * kWBytes);
+          const uint64_t tdesc = sw128_kmajor_desc(smem_t + s * kTBytes);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_f16_pair(d_tmem, wdesc + (uint64_t)(2 * k), tdesc + (uint64_t)(2 * k), idesc,
+                          (kb > 0 || k > 0) ? 1u : 0u);
+          const uint32_t eb = smem_u32(&ctl.empty[s]);
+          umma_commit_pair(mapa_shared(eb, 0));
+          umma_commit_pair(mapa_shared(eb, 1));
+          if (++s == S) { s = 0; ph ^= 1u; }
+        }
+        if (!ok) break;
+        const uint32_t fb = smem_u32(&ctl.tmem_full[acc]);
+        umma_commit_pair(mapa_shared(fb, 0));
+        umma_commit_pair(mapa_shared(fb, 1));
+      }
+      if (!ok) {
+        // aborting: wait until every MMA this thread issued has completed before TMEM is freed
+        umma_commit_pair(mapa_shared(smem_u32(&ctl.mma_done), 0));
+        mbar_drain(smem_u32(&ctl.mma_done), 0);
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5 -> TMEM lane quarters 2, 3, 0, 1)
+    const int q = warp & 3;
+    const uint32_t empty_bar[2] = {mapa_shared(smem_u32(&ctl.tmem_empty[0]), 0),
+                                   mapa_shared(smem_u32(&ctl.tmem_empty[1]), 0)};
+    // SwiGLU: lane quarters 0, 1 hold gate channels, 2, 3 the matching up channels; the warps of
+    // pair (q, q + 2) exchange halves through a double buffer guarded by mbarriers (bounded
+    // waits, so an abort on either side cannot leave the other stuck)
+    const int pr = q & 1;
+    const bool gate_warp = q < 2;
+    float* xp = xch + pr * (2 * 32 * 32);
+    __nv_bfloat16* stg = stage_all + (warp - 2) * kStageElems;
+    int chunk = 0;  // running chunk count of this warp pair: buffer chunk & 1, parity chunk >> 1
+    int it = 0;
+    bool ok = true;
+    for (int r = 0; ok; ++r, ++it) {
+      const int tile = sched_tile(r, unit, units);
+      if (tile >= total) break;
+      const TileInfo ti = decode<TBN>(p, ctl, tile);
+      const Segment& sg = p.seg[ti.seg];
+      const int acc = it & 1;
+      const uint32_t acc_ph = (uint32_t)((it >> 1) & 1);
+      // one lane polls, the warp follows its verdict (tcgen05.ld below must not diverge)
+      int w_ok = 1;
+      if (lane == 0) w_ok = mbar_wait(smem_u32(&ctl.tmem_full[acc]), acc_ph, abort_flag, p.err) ? 1 : 0;
+      w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
+      if (!w_ok) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * 256);
+      const int ntok = ti.rows_valid;
+      const int ncol = tile_n(ntok);
+      // staged output: each lane writes its channel for `rows` tokens from t0, then the warp
+      // stores whole 64-byte token rows with 16-byte stores
+      auto flush = [&](int t0, int rows, int ch0) {
+        __syncwarp();
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const int jj = r * 8 + (lane >> 2), piece = lane & 3;
+          const int t = t0 + jj, col = ch0 + piece * 8;
+          if (jj < rows && t < ntok && col < sg.n_store) {
+            const uint4 val = *reinterpret_cast<const uint4*>(stg + jj * 32 + piece * 8);
+            const int row = ti.row0 + t;
+            __nv_bfloat16* crow = sg.c + (size_t)row * sg.ldc;
+            if (EPI == kEpiStore && sg.ep != nullptr) {
+              // expert parallel: this row goes back to the rank that sent it (NVLink store)
+              crow = ep_return_row(sg.ep, ti.group, row, sg.ldc);
+              if (crow == nullptr) {
+                record_error(p.err, kErrIndex);
+                continue;
+              }
+            }
+            *reinterpret_cast<uint4*>(crow + col) = val;
+          }
+        }
+        __syncwarp();
+      };
+      if constexpr (EPI == kEpiSwiGLU) {
+        // channels of this warp pair: 128-row packed block (2 * n_blk + rank), 64 channels each.
+        // Per 32-token chunk the gate warp finishes tokens 0-15 and the up warp tokens 16-31:
+        // each hands the other the half it needs through a double buffer.
+        const int ch0 = 64 * (2 * ti.n_blk + (int)rank) + 32 * pr;
+#pragma unroll 1
+        for (int c = 0; c < ncol && ok; c += 32, ++chunk) {
+          uint32_t v[32];
+          tmem_ld32(taddr + c, v);
+          tmem_wait_ld();
+          const int b = chunk & 1;
+          const uint32_t par = (uint32_t)((chunk >> 1) & 1);
+          float* buf = xp + b * (32 * 32);  // [0, 512): gate -> up, [512, 1024): up -> gate
+          float* mine = buf + (gate_warp ? 0 : 512);
+          const float* theirs = buf + (gate_warp ? 512 : 0);
+          const uint32_t sent = smem_u32(&xbar[pr][b][0]), done = smem_u32(&xbar[pr][b][1]);
+          int h_ok = 1;
+          if (lane == 0) h_ok = mbar_wait(done, par ^ 1u, abort_flag, p.err) ? 1 : 0;  // buffer free
+          h_ok = __shfl_sync(0xffffffffu, h_ok, 0);
+          if (h_ok) {
+            // the gate warp sends gate values of tokens 16-31, the up warp up values of 0-15
+#pragma unroll
+            for (int j = 0; j < 16; ++j) mine[j * 32 + lane] = __uint_as_float(v[gate_warp ? 16 + j : j]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(sent);
+            if (lane == 0) h_ok = mbar_wait(sent, par, abort_flag, p.err) ? 1 : 0;
+            h_ok = __shfl_sync(0xffffffffu, h_ok, 0);
+          }
+          if (h_ok) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float other = theirs[j * 32 + lane];
+              const float g = gate_warp ? __uint_as_float(v[j]) : other;
+              const float u = gate_warp ? other : __uint_as_float(v[16 + j]);
+              stg[j * 32 + lane] = __float2bfloat16_rn(silu(g) * u);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(done);
+            flush(c + (gate_warp ? 0 : 16), 16, ch0);
+          }
+          if (!h_ok) ok = false;
+        }
+      } else {
+        // output channels of this warp: weight rows of the 256-row block
+        const int ch0 = ti.n_blk * 256 + 128 * (int)rank + 32 * q;
+#pragma unroll 1
+        for (int c = 0; c < ncol; c += 32) {
+          uint32_t v[32];
+          tmem_ld32(taddr + c, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float a = __uint_as_float(v[j]);
+            if constexpr (EPI == kEpiReLU) a = fmaxf(a, 0.0f);
+            stg[j * 32 + lane] = __float2bfloat16_rn(a);
+          }
+          flush(c, 32, ch0);
+        }
+      }
+      // every lane's TMEM reads are complete: the warp releases the accumulator once
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(empty_bar[acc]);
+    }
+  }
+
+  __syncthreads();
+  if (*abort_flag) {
+    // the odd CTA's loads complete on the even CTA's barriers, which this CTA cannot observe:
+    // give copies still in flight a bounded grace period before the pair frees its memory
+    const uint64_t t0 = globaltimer_ns();
+    while (globaltimer_ns() - t0 < 200000ull) __nanosleep(1000);
+  }
+  cluster_sync_all();  // the pair's MMAs into this CTA's TMEM and remote arrivals are finished
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+  if (p.ep_signal != nullptr) ep::signal_when_grid_done(p.ep_signal, &p.ep_signal->return_done, ep::kReturn);
+}
+
+}  // namespace pair
+}  // namespace gemm
+
+template <int EPI>
+static int launch_pair(const CUtensorMap& w0, const CUtensorMap& t0, const CUtensorMap& w1, const CUtensorMap& t1,
+                       const gemm::Params& p, int grid, cudaStream_t stream) {
+  static bool attr_set = false;
+  auto kern = gemm::pair::pair_gemm_kernel<EPI>;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::pair::kSmemBytes) !=
+        cudaSuccess)
+      return DSCA_ERR_CUDA;
+    attr_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(gemm::kThreads);
+  cfg.dynamicSmemBytes = gemm::pair::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, w0, t0, w1, t1, p) != cudaSuccess) return DSCA_ERR_CUDA;
+  return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
+}
+
+// CTA pairs that can be resident at once (a cluster of two needs two free SMs of one GPC).
+static int max_resident_pairs(int num_sms) {
+  static int cached = -1;
+  if (cached < 0) {
+    auto kern = gemm::pair::pair_gemm_kernel<gemm::kEpiStore>;
+    int n = 0;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::pair::kSmemBytes) ==
+        cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3((unsigned)(num_sms & ~1));
+      cfg.blockDim = dim3(gemm::kThreads);
+      cfg.dynamicSmemBytes = gemm::pair::kSmemBytes;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
+    }
+    cudaGetLastError();
+    cached = n > 0 ? std::min(n, num_sms / 2) : num_sms / 2;
+  }
+  return cached;
+}
+
+static int launch_pair_one(int epi, const CUtensorMap& w0, const CUtensorMap& t0, const CUtensorMap& w1,
+                           const CUtensorMap& t1, const gemm::Params& p, int grid, cudaStream_t stream) {
+  switch (epi) {
+    case gemm::kEpiSwiGLU: return launch_pair<gemm::kEpiSwiGLU>(w0, t0, w1, t1, p, grid, stream);
+    case gemm::kEpiReLU: return launch_pair<gemm::kEpiReLU>(w0, t0, w1, t1, p, grid, stream);
+    default: return launch_pair<gemm::kEpiStore>(w0, t0, w1, t1, p, grid, stream);
+  }
+}
+
+int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream_t stream) {
+  const int want = f->num_ctas > 0 ? f->num_ctas : num_sms;
+  const int grid = 2 * std::max(1, std::min(want / 2, max_resident_pairs(num_sms)));
+  const int segs = f->segments == 0 ? 3 : f->segments;
+  const bool shared = f->shared_rows > 0 && (segs & 2);
+  const bool routed = (segs & 1) != 0;
+  const int phases = f->phases == 0 ? 3 : f->phases;
+  if (!routed && !shared) return DSCA_OK;
+  if (f->n1p % 256 != 0 || f->dp % 256 != 0 || (shared && f->shared_n1p % 256 != 0)) return DSCA_ERR_BAD_ARG;
+  constexpr uint32_t wbox = gemm::pair::kWRows, tbox = gemm::pair::kBox;
+  int rc;
+  // ---- GEMM1: h = act(a . w1^T)   (+ hs = act(xs . ws1^T))
+  if (phases & 1) {
+    CUtensorMap w0, t0, w1, t1;
+    if ((rc = make_map_bf16(&w0, f->w1, (uint64_t)f->num_experts_w * f->n1p, (uint64_t)f->d, wbox))) return rc;
+    if ((rc = make_map_bf16(&t0, f->a, (uint64_t)f->capacity, (uint64_t)f->d, tbox))) return rc;
+    if (shared) {
+      if ((rc = make_map_bf16(&w1, f->ws1, (uint64_t)f->shared_n1p, (uint64_t)f->d, wbox))) return rc;
+      if ((rc = make_map_bf16(&t1, f->xs, (uint64_t)f->shared_rows, (uint64_t)f->d, tbox))) return rc;
+    } else {
+      w1 = w0;
+      t1 = t0;
+    }
+    gemm::Params p{};
+    const int epi = f->act == DSCA_ACT_SWIGLU ? gemm::kEpiSwiGLU : gemm::kEpiReLU;
+    p.epi = epi;
+    p.err = f->err;
+    p.nseg = shared ? 2 : 1;
+    p.seg_first = 0;  // equal K (the model width) in both segments
+    gemm::Segment& s0 = p.seg[0];
+    s0.group_offsets = f->group_offsets;
+    s0.group_weight = f->group_weight;
+    s0.ngroups = routed ? f->num_groups : 0;
+    s0.rows = 0;
+    s0.n_tiles = f->n1p / gemm::BN;
+    s0.b_rows_per_group = f->n1p;
+    s0.k_blocks = (f->d + gemm::BK - 1) / gemm::BK;
+    s0.c = reinterpret_cast<__nv_bfloat16*>(f->h);
+    s0.ldc = f->ip;
+    s0.n_store = f->ip;
+    s0.capacity = f->capacity;
+    if (shared) {
+      gemm::Segment& s1 = p.seg[1];
+      s1.group_offsets = nullptr;
+      s1.group_weight = nullptr;
+      s1.ngroups = 1;
+      s1.rows = f->shared_rows;
+      s1.n_tiles = f->shared_n1p / gemm::BN;
+      s1.b_rows_per_group = f->shared_n1p;
+      s1.k_blocks = (f->d + gemm::BK - 1) / gemm::BK;
+      s1.c = reinterpret_cast<__nv_bfloat16*>(f->hs);
+      s1.ldc = f->shared_ip;
+      s1.n_store = f->shared_ip;
+      s1.capacity = f->shared_rows;
+    }
+    if ((rc = launch_pair_one(epi, w0, t0, w1, t1, p, grid, stream))) return rc;
+  }
+  // ---- GEMM2: y = h . w2^T   (+ ys = hs . ws2^T)
+  if (phases & 2) {
+    CUtensorMap w0, t0, w1, t1;
+    if ((rc = make_map_bf16(&w0, f->w2, (uint64_t)f->num_experts_w * f->dp, (uint64_t)f->ip, wbox))) return rc;
+    if ((rc = make_map_bf16(&t0, f->h, (uint64_t)f->capacity, (uint64_t)f->ip, tbox))) return rc;
+    if (shared) {
+      if ((rc = make_map_bf16(&w1, f->ws2, (uint64_t)f->dp, (uint64_t)f->shared_ip, wbox))) return rc;
+      if ((rc = make_map_bf16(&t1, f->hs, (uint64_t)f->shared_rows, (uint64_t)f->shared_ip, tbox))) return rc;
+    } else {
+      w1 = w0;
+      t1 = t0;
+    }
+    gemm::Params p{};
+    p.epi = gemm::kEpiStore;
+    p.err = f->err;
+    p.nseg = shared ? 2 : 1;
+    p.seg_first = (shared && f->shared_ip > f->ip) ? 1 : 0;  // the longer K first
+    p.ep_signal = routed ? static_cast<ep::Ctx*>(f->ep_ctx) : nullptr;
+    gemm::Segment& s0 = p.seg[0];
+    s0.ep = static_cast<const ep::Ctx*>(f->ep_ctx);
+    s0.group_offsets = f->group_offsets;
+    s0.group_weight = f->group_weight;
+    s0.ngroups = routed ? f->num_groups : 0;
+    s0.rows = 0;
+    s0.n_tiles = f->dp / gemm::BN;
+    s0.b_rows_per_group = f->dp;
+    s0.k_blocks = (f->ip + gemm::BK - 1) / gemm::BK;
+    s0.c = reinterpret_cast<__nv_bfloat16*>(f->y);
+    s0.ldc = f->d;
+    s0.n_store = f->d;
+    s0.capacity = f->capacity;
+    if (shared) {
+      gemm::Segment& s1 = p.seg[1];
+      s1.group_offsets = nullptr;
+      s1.group_weight = nullptr;
+      s1.ngroups = 1;
+      s1.rows = f->shared_rows;
+      s1.n_tiles = f->dp / gemm::BN;
+      s1.b_rows_per_group = f->dp;
+      s1.k_blocks = (f->shared_ip + gemm::BK - 1) / gemm::BK;
+      s1.c = reinterpret_cast<__nv_bfloat16*>(f->ys);
+      s1.ldc = f->d;
+      s1.n_store = f->d;
+      s1.capacity = f->shared_rows;
+    }
+    if ((rc = launch_pair_one(gemm::kEpiStore, w0, t0, w1, t1, p, grid, stream))) return rc;
+  }
+  return DSCA_OK;
+}
+
+}  // namespace dsca

@@ -198,6 +198,10 @@ typedef struct {
   const float* w2_scale;
   const float* ws1_scale;
   const float* ws2_scale;
+  int tile_rows;              /* bf16 path tile form: 128 = one CTA per 128-token x 256-channel
+                                 tile; 256 = a CTA pair (tcgen05 cta_group::2) per 256-channel x
+                                 <=256-token tile, tokens rounded up to 16 only; 0 = default
+                                 (pair for GEMM2 and ReLU GEMM1, single CTA for SwiGLU GEMM1) */
 } dsca_ffn_args;
 DSCA_API int dsca_grouped_ffn(const dsca_ffn_args* a, dsca_stream_t stream);
 

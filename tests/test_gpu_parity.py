@@ -381,3 +381,26 @@ def test_fused_scan_matches_separate_scan(cuda, T, k, E):
     for kk in keys:
         assert torch.equal(got[0][kk], got[2][kk]), kk
         assert torch.equal(got[1][kk], got[2][kk]), kk
+
+
+@pytest.mark.parametrize("T,d,E,I,Is,k", [(600, 256, 60, 128, 512, 4), (257, 128, 8, 64, 256, 2)])
+def test_single_cta_and_pair_tiles_agree(cuda, T, d, E, I, Is, k):
+    """The 128-row single-CTA tiles and the 256-row CTA-pair tiles give the same block output
+    (both accumulate each output element over K in the same order, so bf16 results match),
+    and both stay within the bf16 tolerance of the fp32 oracle."""
+    x = syn.hidden_states(T, d, 1201, "bf16")
+    Wg, _ = syn.router_weight(E, d, 1202, zipf_s=1.5, dtype="bf16")
+    p = syn.qwen_expert_weights(E, d, I, Is, 1203, dtype="bf16")
+    eng = qwen_engine(Wg, p, k, False, torch.bfloat16, cuda)
+    xd = _t(x, torch.bfloat16, cuda)
+    outs = []
+    for rows in (128, 256):
+        eng.tile_rows = rows
+        r = eng.forward(xd)
+        torch.cuda.synchronize()
+        eng.check()
+        outs.append(r["out"].float().cpu().numpy())
+    y, *_ = O.qwen_forward(x, Wg, p, k, False, "bf16")
+    for o in outs:
+        assert O.max_rel_err(o, y) < BF16_TOL
+    assert np.abs(outs[0] - outs[1]).max() <= 1e-2 * max(1.0, np.abs(outs[1]).max())
