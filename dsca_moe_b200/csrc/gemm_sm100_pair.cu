@@ -32,16 +32,24 @@ namespace dsca {
 namespace gemm {
 namespace pair {
 
-constexpr int S = 6;                        // stages
-constexpr int TBN = 256;                    // token rows per tile (MMA N <= 256)
-constexpr int kWRows = 128;                 // weight rows per CTA
-constexpr int kBox = 32;                    // token rows per TMA box
-constexpr int kWBytes = kWRows * BK * 2;    // 16 KB
-constexpr int kTBytes = 128 * BK * 2;       // token slot per stage: up to 128 rows, 16 KB
-constexpr int kBoxBytes = kBox * BK * 2;    // 4 KB
-constexpr int kXchFloats = 2 * 2 * 32 * 32; // SwiGLU hand-off: 2 warp pairs x 2 buffers x 32 x 32
-constexpr int kStageElems = 32 * 32;         // per epilogue warp: 32 tokens x 32 channels, bf16
-constexpr int kSmemBytes = S * (kWBytes + kTBytes) + kXchFloats * 4 + 4 * kStageElems * 2 + 1024;
+// Per-epilogue configuration.  SwiGLU: a CTA's 128 channels need 128 gate rows (slot A) and the
+// 128 matching up rows (slot A2), two MMAs per K step into a gate and an up accumulator of N <=
+// 128 columns each.  Others: 128 weight rows (slot A), N <= 256.
+template <int EPI>
+struct Cfg {
+  static constexpr bool kGlu = EPI == kEpiSwiGLU;
+  static constexpr int S = kGlu ? 5 : 6;                  // stages
+  static constexpr int TBN = kGlu ? 128 : 256;            // token rows per tile (MMA N)
+  static constexpr int kWBox = kGlu ? 64 : 128;           // weight rows per TMA box
+  static constexpr int kABytes = 128 * BK * 2;            // 16 KB
+  static constexpr int kA2Bytes = kGlu ? 128 * BK * 2 : 0;
+  static constexpr int kTBytes = (TBN / 2) * BK * 2;      // this CTA's token rows
+  static constexpr int kStageBytes = kABytes + kA2Bytes + kTBytes;
+  static constexpr int kStageElems = 32 * 32;             // epilogue staging per warp, bf16
+  static constexpr int kSmemBytes = S * kStageBytes + 4 * kStageElems * 2 + 1024;
+};
+constexpr int kBox = 32;                  // token rows per TMA box
+constexpr int kBoxBytes = kBox * BK * 2;  // 4 KB
 
 // MMA N for a tile of `ntok` token rows: a multiple of 16 (each CTA holds N / 2 rows, a whole
 // number of 8-row swizzle atoms).
@@ -52,21 +60,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     pair_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__ CUtensorMap tmT0,
                      const __grid_constant__ CUtensorMap tmW1, const __grid_constant__ CUtensorMap tmT1,
                      const Params p) {
+  using C = Cfg<EPI>;
+  constexpr int S = C::S;
+  constexpr int TBN = C::TBN;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ SmemCtl ctl;
-  __shared__ uint64_t xbar[2][2][2];  // SwiGLU hand-off: [warp pair][buffer][sent, done]
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const uint32_t smem_w = smem_u32(smem);
-  const uint32_t smem_t = smem_w + S * kWBytes;
-  float* xch = reinterpret_cast<float*>(smem + S * (kWBytes + kTBytes));
-  __nv_bfloat16* stage_all = reinterpret_cast<__nv_bfloat16*>(xch + kXchFloats);
+  const uint32_t smem_a = smem_u32(smem);
+  const uint32_t smem_a2 = smem_a + S * C::kABytes;
+  const uint32_t smem_t = smem_a2 + S * C::kA2Bytes;
+  __nv_bfloat16* stage_all = reinterpret_cast<__nv_bfloat16*>(smem + S * C::kStageBytes);
 
   const int warp = warp_id(), lane = lane_id();
   volatile int* abort_flag = &ctl.abort_flag;
   const uint32_t rank = cluster_ctarank();  // 0 = the CTA that issues the MMAs
   const int unit = (int)(blockIdx.x >> 1), units = (int)(gridDim.x >> 1);
 
-  // ---- prologue: barriers, TMEM, group tile table
+  // ---- prologue: barriers, TMEM, tile schedule
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(smem_u32(&ctl.full[s]), 1);
@@ -77,11 +87,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(smem_u32(&ctl.tmem_empty[a]), 8);  // 4 epilogue warps x 2 CTAs
     }
     mbar_init(smem_u32(&ctl.mma_done), 1);
-    for (int a = 0; a < 2; ++a)
-      for (int b = 0; b < 2; ++b) {
-        mbar_init(smem_u32(&xbar[a][b][0]), 2);  // both warps of the pair sent their half
-        mbar_init(smem_u32(&xbar[a][b][1]), 2);  // both warps read the other's half
-      }
     ctl.abort_flag = 0;
     fence_mbar_init();
   }
@@ -106,7 +111,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int total = ctl.total_tiles;
 
   if (warp == 0) {
-    // ---------------- TMA producer: this CTA's 128 weight rows and its half of the token rows
+    // ---------------- TMA producer: this CTA's weight rows and its half of the token rows
     if (lane == 0) {
       int s = 0;
       uint32_t ph = 0;
@@ -121,8 +126,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const CUtensorMap* mt = ti.seg == 0 ? &tmT0 : &tmT1;
         const int half = tile_n(ti.rows_valid) / 2;
         const int nbox = (half + kBox - 1) / kBox;
-        const uint32_t tx = 2u * (uint32_t)(kWBytes + nbox * kBoxBytes);
-        const int w_row = ti.b_row0 + kWRows * (int)rank;
+        const uint32_t tx = 2u * (uint32_t)(C::kABytes + C::kA2Bytes + nbox * kBoxBytes);
+        // weight rows: SwiGLU packs 128-row blocks [64 gate | 64 up]; this CTA's 128 channels
+        // are the 64-channel blocks 4 n_blk + 2 rank and + 1 (packed rows 512 n_blk + 256 rank)
+        const int w_row = C::kGlu ? ti.b_row0 - ti.n_blk * BN + 512 * ti.n_blk + 256 * (int)rank
+                                  : ti.b_row0 + 128 * (int)rank;
         const int t_row = ti.row0 + half * (int)rank;
         const int kb_n = p.seg[ti.seg].k_blocks;
         for (int kb = 0; kb < kb_n; ++kb) {
@@ -130,9 +138,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t fb = smem_u32(&ctl.full[s]);
           const uint32_t fb0 = mapa_shared(fb, 0);  // the even CTA's full barrier
           if (rank == 0) mbar_arrive_expect_tx(fb, tx);
-          tma_load_2d_pair(smem_w + s * kWBytes, mw, fb0, kb * BK, w_row);
+          if constexpr (C::kGlu) {
+            const uint32_t ga = smem_a + s * C::kABytes, ua = smem_a2 + s * C::kA2Bytes;
+            tma_load_2d_pair(ga, mw, fb0, kb * BK, w_row);
+            tma_load_2d_pair(ga + 64 * 128, mw, fb0, kb * BK, w_row + 128);
+            tma_load_2d_pair(ua, mw, fb0, kb * BK, w_row + 64);
+            tma_load_2d_pair(ua + 64 * 128, mw, fb0, kb * BK, w_row + 192);
+          } else {
+            tma_load_2d_pair(smem_a + s * C::kABytes, mw, fb0, kb * BK, w_row);
+          }
           for (int b = 0; b < nbox; ++b)
-            tma_load_2d_pair(smem_t + s * kTBytes + b * kBoxBytes, mt, fb0, kb * BK, t_row + b * kBox);
+            tma_load_2d_pair(smem_t + s * C::kTBytes + b * kBoxBytes, mt, fb0, kb * BK, t_row + b * kBox);
           pending_phase[s] = (int)ph;
           if (++s == S) { s = 0; ph ^= 1u; }
         }
@@ -166,12 +182,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kb = 0; kb < kb_n; ++kb) {
           if (!mbar_wait(smem_u32(&ctl.full[s]), ph, abort_flag, p.err)) { ok = false; break; }
           tc_fence_after();
-          const uint64_t wdesc = sw128_kmajor_desc(smem_w + s * kWBytes);
-          const uint64_t tdesc = sw128_kmajor_desc(smem_t + s * kTBytes);
+          const uint64_t adesc = sw128_kmajor_desc(smem_a + s * C::kABytes);
+          const uint64_t tdesc = sw128_kmajor_desc(smem_t + s * C::kTBytes);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            umma_f16_pair(d_tmem, wdesc + (uint64_t)(2 * k), tdesc + (uint64_t)(2 * k), idesc,
-                          (kb > 0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+            umma_f16_pair(d_tmem, adesc + (uint64_t)(2 * k), tdesc + (uint64_t)(2 * k), idesc, accum);
+            if constexpr (C::kGlu) {
+              const uint64_t udesc = sw128_kmajor_desc(smem_a2 + s * C::kA2Bytes);
+              umma_f16_pair(d_tmem + 128, udesc + (uint64_t)(2 * k), tdesc + (uint64_t)(2 * k), idesc, accum);
+            }
+          }
           const uint32_t eb = smem_u32(&ctl.empty[s]);
           umma_commit_pair(mapa_shared(eb, 0));
           umma_commit_pair(mapa_shared(eb, 1));
@@ -193,17 +214,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     const uint32_t empty_bar[2] = {mapa_shared(smem_u32(&ctl.tmem_empty[0]), 0),
                                    mapa_shared(smem_u32(&ctl.tmem_empty[1]), 0)};
-    // SwiGLU: lane quarters 0, 1 hold gate channels, 2, 3 the matching up channels; the warps of
-    // pair (q, q + 2) exchange halves through a double buffer guarded by mbarriers (bounded
-    // waits, so an abort on either side cannot leave the other stuck)
-    const int pr = q & 1;
-    const bool gate_warp = q < 2;
-    float* xp = xch + pr * (2 * 32 * 32);
-    __nv_bfloat16* stg = stage_all + (warp - 2) * kStageElems;
-    int chunk = 0;  // running chunk count of this warp pair: buffer chunk & 1, parity chunk >> 1
+    __nv_bfloat16* stg = stage_all + (warp - 2) * C::kStageElems;
     int it = 0;
-    bool ok = true;
-    for (int r = 0; ok; ++r, ++it) {
+    for (int r = 0;; ++r, ++it) {
       const int tile = sched_tile(r, unit, units);
       if (tile >= total) break;
       const TileInfo ti = decode<TBN>(p, ctl, tile);
@@ -219,15 +232,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * 256);
       const int ntok = ti.rows_valid;
       const int ncol = tile_n(ntok);
-      // staged output: each lane writes its channel for `rows` tokens from t0, then the warp
-      // stores whole 64-byte token rows with 16-byte stores
-      auto flush = [&](int t0, int rows, int ch0) {
+      // this warp's 32 output channels: SwiGLU channel block n_blk (256 channels per pair);
+      // otherwise weight rows of the 256-row block
+      const int ch0 = ti.n_blk * 256 + 128 * (int)rank + 32 * q;
+      // staged output: each lane writes its channel for 32 tokens, then the warp stores whole
+      // 64-byte token-row pieces with 16-byte stores
+#pragma unroll 1
+      for (int c = 0; c < ncol; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(taddr + c, v);
+        if constexpr (C::kGlu) {
+          uint32_t u[32];
+          tmem_ld32(taddr + 128 + c, u);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            stg[j * 32 + lane] = __float2bfloat16_rn(silu(__uint_as_float(v[j])) * __uint_as_float(u[j]));
+        } else {
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float a = __uint_as_float(v[j]);
+            if constexpr (EPI == kEpiReLU) a = fmaxf(a, 0.0f);
+            stg[j * 32 + lane] = __float2bfloat16_rn(a);
+          }
+        }
         __syncwarp();
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          const int jj = r * 8 + (lane >> 2), piece = lane & 3;
-          const int t = t0 + jj, col = ch0 + piece * 8;
-          if (jj < rows && t < ntok && col < sg.n_store) {
+        for (int rr = 0; rr < 4; ++rr) {
+          const int jj = rr * 8 + (lane >> 2), piece = lane & 3;
+          const int t = c + jj, col = ch0 + piece * 8;
+          if (t < ntok && col < sg.n_store) {
             const uint4 val = *reinterpret_cast<const uint4*>(stg + jj * 32 + piece * 8);
             const int row = ti.row0 + t;
             __nv_bfloat16* crow = sg.c + (size_t)row * sg.ldc;
@@ -243,65 +278,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         __syncwarp();
-      };
-      if constexpr (EPI == kEpiSwiGLU) {
-        // channels of this warp pair: 128-row packed block (2 * n_blk + rank), 64 channels each.
-        // Per 32-token chunk the gate warp finishes tokens 0-15 and the up warp tokens 16-31:
-        // each hands the other the half it needs through a double buffer.
-        const int ch0 = 64 * (2 * ti.n_blk + (int)rank) + 32 * pr;
-#pragma unroll 1
-        for (int c = 0; c < ncol && ok; c += 32, ++chunk) {
-          uint32_t v[32];
-          tmem_ld32(taddr + c, v);
-          tmem_wait_ld();
-          const int b = chunk & 1;
-          const uint32_t par = (uint32_t)((chunk >> 1) & 1);
-          float* buf = xp + b * (32 * 32);  // [0, 512): gate -> up, [512, 1024): up -> gate
-          float* mine = buf + (gate_warp ? 0 : 512);
-          const float* theirs = buf + (gate_warp ? 512 : 0);
-          const uint32_t sent = smem_u32(&xbar[pr][b][0]), done = smem_u32(&xbar[pr][b][1]);
-          int h_ok = 1;
-          if (lane == 0) h_ok = mbar_wait(done, par ^ 1u, abort_flag, p.err) ? 1 : 0;  // buffer free
-          h_ok = __shfl_sync(0xffffffffu, h_ok, 0);
-          if (h_ok) {
-            // the gate warp sends gate values of tokens 16-31, the up warp up values of 0-15
-#pragma unroll
-            for (int j = 0; j < 16; ++j) mine[j * 32 + lane] = __uint_as_float(v[gate_warp ? 16 + j : j]);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(sent);
-            if (lane == 0) h_ok = mbar_wait(sent, par, abort_flag, p.err) ? 1 : 0;
-            h_ok = __shfl_sync(0xffffffffu, h_ok, 0);
-          }
-          if (h_ok) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const float other = theirs[j * 32 + lane];
-              const float g = gate_warp ? __uint_as_float(v[j]) : other;
-              const float u = gate_warp ? other : __uint_as_float(v[16 + j]);
-              stg[j * 32 + lane] = __float2bfloat16_rn(silu(g) * u);
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(done);
-            flush(c + (gate_warp ? 0 : 16), 16, ch0);
-          }
-          if (!h_ok) ok = false;
-        }
-      } else {
-        // output channels of this warp: weight rows of the 256-row block
-        const int ch0 = ti.n_blk * 256 + 128 * (int)rank + 32 * q;
-#pragma unroll 1
-        for (int c = 0; c < ncol; c += 32) {
-          uint32_t v[32];
-          tmem_ld32(taddr + c, v);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float a = __uint_as_float(v[j]);
-            if constexpr (EPI == kEpiReLU) a = fmaxf(a, 0.0f);
-            stg[j * 32 + lane] = __float2bfloat16_rn(a);
-          }
-          flush(c, 32, ch0);
-        }
       }
       // every lane's TMEM reads are complete: the warp releases the accumulator once
       tc_fence_before();
@@ -332,17 +308,17 @@ template <int EPI>
 static int launch_pair(const CUtensorMap& w0, const CUtensorMap& t0, const CUtensorMap& w1, const CUtensorMap& t1,
                        const gemm::Params& p, int grid, cudaStream_t stream) {
   static bool attr_set = false;
+  constexpr int smem_bytes = gemm::pair::Cfg<EPI>::kSmemBytes;
   auto kern = gemm::pair::pair_gemm_kernel<EPI>;
   if (!attr_set) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::pair::kSmemBytes) !=
-        cudaSuccess)
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) != cudaSuccess)
       return DSCA_ERR_CUDA;
     attr_set = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3(gemm::kThreads);
-  cfg.dynamicSmemBytes = gemm::pair::kSmemBytes;
+  cfg.dynamicSmemBytes = smem_bytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -359,14 +335,14 @@ static int launch_pair(const CUtensorMap& w0, const CUtensorMap& t0, const CUten
 static int max_resident_pairs(int num_sms) {
   static int cached = -1;
   if (cached < 0) {
-    auto kern = gemm::pair::pair_gemm_kernel<gemm::kEpiStore>;
+    auto kern = gemm::pair::pair_gemm_kernel<gemm::kEpiSwiGLU>;
+    constexpr int smem_bytes = gemm::pair::Cfg<gemm::kEpiSwiGLU>::kSmemBytes;
     int n = 0;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::pair::kSmemBytes) ==
-        cudaSuccess) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) == cudaSuccess) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3((unsigned)(num_sms & ~1));
       cfg.blockDim = dim3(gemm::kThreads);
-      cfg.dynamicSmemBytes = gemm::pair::kSmemBytes;
+      cfg.dynamicSmemBytes = smem_bytes;
       cudaLaunchAttribute attr[1];
       attr[0].id = cudaLaunchAttributeClusterDimension;
       attr[0].val.clusterDim.x = 2;
@@ -400,11 +376,13 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
   const int phases = f->phases == 0 ? 3 : f->phases;
   if (!routed && !shared) return DSCA_OK;
   if (f->n1p % 256 != 0 || f->dp % 256 != 0 || (shared && f->shared_n1p % 256 != 0)) return DSCA_ERR_BAD_ARG;
-  constexpr uint32_t wbox = gemm::pair::kWRows, tbox = gemm::pair::kBox;
+  constexpr uint32_t tbox = gemm::pair::kBox;
   int rc;
   // ---- GEMM1: h = act(a . w1^T)   (+ hs = act(xs . ws1^T))
   if (phases & 1) {
     CUtensorMap w0, t0, w1, t1;
+    const bool glu = f->act == DSCA_ACT_SWIGLU;
+    const uint32_t wbox = glu ? gemm::pair::Cfg<gemm::kEpiSwiGLU>::kWBox : gemm::pair::Cfg<gemm::kEpiReLU>::kWBox;
     if ((rc = make_map_bf16(&w0, f->w1, (uint64_t)f->num_experts_w * f->n1p, (uint64_t)f->d, wbox))) return rc;
     if ((rc = make_map_bf16(&t0, f->a, (uint64_t)f->capacity, (uint64_t)f->d, tbox))) return rc;
     if (shared) {
@@ -425,7 +403,8 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
     s0.group_weight = f->group_weight;
     s0.ngroups = routed ? f->num_groups : 0;
     s0.rows = 0;
-    s0.n_tiles = f->n1p / gemm::BN;
+    // SwiGLU: a tile covers 256 output channels (gate and up rows of them); others 256 rows
+    s0.n_tiles = glu ? (f->ip + gemm::BN - 1) / gemm::BN : f->n1p / gemm::BN;
     s0.b_rows_per_group = f->n1p;
     s0.k_blocks = (f->d + gemm::BK - 1) / gemm::BK;
     s0.c = reinterpret_cast<__nv_bfloat16*>(f->h);
@@ -438,7 +417,7 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
       s1.group_weight = nullptr;
       s1.ngroups = 1;
       s1.rows = f->shared_rows;
-      s1.n_tiles = f->shared_n1p / gemm::BN;
+      s1.n_tiles = glu ? (f->shared_ip + gemm::BN - 1) / gemm::BN : f->shared_n1p / gemm::BN;
       s1.b_rows_per_group = f->shared_n1p;
       s1.k_blocks = (f->d + gemm::BK - 1) / gemm::BK;
       s1.c = reinterpret_cast<__nv_bfloat16*>(f->hs);
@@ -451,6 +430,7 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
   // ---- GEMM2: y = h . w2^T   (+ ys = hs . ws2^T)
   if (phases & 2) {
     CUtensorMap w0, t0, w1, t1;
+    constexpr uint32_t wbox = gemm::pair::Cfg<gemm::kEpiStore>::kWBox;
     if ((rc = make_map_bf16(&w0, f->w2, (uint64_t)f->num_experts_w * f->dp, (uint64_t)f->ip, wbox))) return rc;
     if ((rc = make_map_bf16(&t0, f->h, (uint64_t)f->capacity, (uint64_t)f->ip, tbox))) return rc;
     if (shared) {

@@ -718,6 +718,60 @@ class MoEEngine:
         L.check(L.load().dsca_check_error(_ptr(self.err), _stream()), "device error word")
 
 
+class HostPipeline:
+    """MoEEngine.forward over batches that live in pinned host memory, with the PCIe copies
+    overlapped: while batch i computes on the current stream, batch i + 1 is copied in on one copy
+    stream and batch i - 1's output is copied out on another.  Every batch still crosses PCIe both
+    ways; only the waiting overlaps (two device input buffers, event-ordered reuse)."""
+
+    def __init__(self, engine: "MoEEngine", tokens: int):
+        self.eng = engine
+        dev = engine.device
+        self.x_dev = [torch.empty(tokens, engine.d, dtype=engine.dtype, device=dev) for _ in range(2)]
+        self.h2d = torch.cuda.Stream(device=dev)
+        self.d2h = torch.cuda.Stream(device=dev)
+        self._copied = [torch.cuda.Event() for _ in range(2)]
+        self._consumed = [torch.cuda.Event() for _ in range(2)]
+        self._used = [False, False]
+
+    def _copy_in(self, i, x_host):
+        b = i & 1
+        with torch.cuda.stream(self.h2d):
+            if self._used[b]:
+                self.h2d.wait_event(self._consumed[b])  # the forward that read this buffer is done
+            self.x_dev[b].copy_(x_host, non_blocking=True)
+            self._copied[b].record(self.h2d)
+
+    def run(self, xs_host, outs_host):
+        """Forward every xs_host[i] ([T, d], pinned) into outs_host[i] (pinned).  Asynchronous:
+        returns once everything is enqueued; synchronize (or wait on .d2h) before reading."""
+        main = torch.cuda.current_stream(self.eng.device)
+        n = len(xs_host)
+        start = torch.cuda.Event()
+        start.record(main)
+        self.h2d.wait_event(start)
+        self.d2h.wait_event(start)
+        if n:
+            self._copy_in(0, xs_host[0])
+        for i in range(n):
+            b = i & 1
+            if i + 1 < n:
+                self._copy_in(i + 1, xs_host[i + 1])
+            main.wait_event(self._copied[b])
+            out = self.eng.forward(self.x_dev[b])["out"]
+            self._consumed[b].record(main)
+            self._used[b] = True
+            done = torch.cuda.Event()
+            done.record(main)
+            self.d2h.wait_event(done)
+            with torch.cuda.stream(self.d2h):
+                outs_host[i].copy_(out, non_blocking=True)
+            out.record_stream(self.d2h)
+        end = torch.cuda.Event()
+        end.record(self.d2h)
+        main.wait_event(end)
+
+
 def default_expert_to_gpu(E: int, G: int) -> np.ndarray:
     """Contiguous blocks, the first E % G GPUs one expert more (60 on 8 -> 4 x 8 + 4 x 7).
     Equals the reference's naive arange(E) // (E // G) when G divides E

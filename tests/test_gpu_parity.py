@@ -404,3 +404,20 @@ def test_single_cta_and_pair_tiles_agree(cuda, T, d, E, I, Is, k):
     for o in outs:
         assert O.max_rel_err(o, y) < BF16_TOL
     assert np.abs(outs[0] - outs[1]).max() <= 1e-2 * max(1.0, np.abs(outs[1]).max())
+
+
+def test_host_pipeline_matches_forward(cuda):
+    """HostPipeline (overlapped H2D / forward / D2H over pinned host batches) returns, for every
+    batch, exactly what forward() returns for it."""
+    from dsca_moe_b200.engine import HostPipeline
+    T, d, E, I, Is, k = 300, 128, 16, 64, 128, 4
+    Wg, _ = syn.router_weight(E, d, 1302, zipf_s=1.2, dtype="bf16")
+    eng = qwen_engine(Wg, syn.qwen_expert_weights(E, d, I, Is, 1303, dtype="bf16"), k, False, torch.bfloat16, cuda)
+    xs = [torch.from_numpy(syn.hidden_states(T, d, 1310 + i, "bf16")).to(torch.bfloat16).pin_memory() for i in range(5)]
+    outs = [torch.empty(T, d, dtype=torch.bfloat16).pin_memory() for _ in range(5)]
+    HostPipeline(eng, T).run(xs, outs)
+    torch.cuda.synchronize()
+    eng.check()
+    for xh, oh in zip(xs, outs):
+        ref = eng.forward(xh.to(cuda))["out"].cpu()
+        assert torch.equal(oh, ref)
