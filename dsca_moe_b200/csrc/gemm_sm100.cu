@@ -19,9 +19,9 @@
 //               the next tile's MMAs overlap this tile's stores.
 // SwiGLU weights are packed in 128-row blocks of 64 gate rows then the 64 matching up rows, so a
 // 256-column accumulator holds two (gate, up) blocks.
-// Tiles follow the cost-ordered boustrophedon schedule of gemm_sm100.cuh (full tiles of the
-// longer-K segment first, partial tiles last).  Group row offsets are read on the device, so no
-// host sync is needed.
+// Tiles follow the boustrophedon schedule of gemm_sm100.cuh (the longer-K segment first,
+// group-major inside a segment).  Group row offsets are read on the device, so no host sync is
+// needed.
 // Every wait is bounded (2 s): on a timeout the kernel records DSCA_ERR_WAIT_TIMEOUT in the
 // error word, drains its own outstanding copies and MMAs, frees TMEM and returns.
 #include <algorithm>

@@ -70,20 +70,19 @@ struct SmemCtl {
   uint32_t tmem_base;
   int abort_flag;
   int total_tiles;
-  int cls_start[5];              // tile classes in schedule order (see build_group_table)
-  int cls_kind[4];               // 0 / 1: full tiles of segment 0 / 1; 2 / 3: tail tiles
-  int full_start[kMaxGroups + 1];  // segment 0: prefix of full-height tiles per group
-  int tail_start[kMaxGroups + 1];  // segment 0: prefix of the partial tile per group
+  int seg0_tiles;
+  int seg1_tiles;
+  int tile_start[kMaxGroups + 1];  // segment 0: prefix of tiles per group
   int goff[kMaxGroups + 1];
   int gw[kMaxGroups];
 };
 
-// Tile schedule.  Tiles fall in four classes: full-height tiles (TBM token rows) of each
-// segment and the partial last tile of each group.  They are laid out cost first: full tiles of
-// the segment with the longer K (p.seg_first), full tiles of the other, then the partial tiles in
-// the same segment order; unit u of U takes tiles in boustrophedon order (round r: r U + u for
-// even r, r U + U - 1 - u for odd r), which evens out the per-unit work.  Built by one warp from
-// the device-side group offsets (no host sync).
+// Tile schedule.  The segment with the longer K (p.seg_first) comes first, then the other; inside
+// segment 0 tiles are group-major (a group's M tiles, then its N blocks), so the tiles that
+// read one expert's weights run close together and hit L2.  Unit u of U takes tiles in
+// boustrophedon order (round r: r U + u for even r, r U + U - 1 - u for odd r), which evens out
+// the per-unit work when one segment's tiles are longer.  Built by one warp from the device-side
+// group offsets (no host sync).
 template <int TBM>
 __device__ __forceinline__ void build_group_table(const Params& p, SmemCtl& ctl, int lane) {
   const Segment& sg = p.seg[0];
@@ -92,61 +91,39 @@ __device__ __forceinline__ void build_group_table(const Params& p, SmemCtl& ctl,
     ctl.goff[g] = sg.group_offsets ? sg.group_offsets[g] : (g == 0 ? 0 : sg.rows);
   for (int g = lane; g < ng; g += 32) ctl.gw[g] = sg.group_weight ? sg.group_weight[g] : g;
   __syncwarp();
-  // each lane scans a contiguous run of groups, then warp scans stitch the runs
+  // each lane scans a contiguous run of groups, then a warp scan stitches the runs
   const int per = (ng + 31) / 32;
   const int g0 = min(ng, lane * per), g1 = min(ng, g0 + per);
-  auto rows_of = [&](int g) {
-    int r = ctl.goff[g + 1] - ctl.goff[g];
-    if (r < 0 || ctl.goff[g + 1] > sg.capacity) r = -1;
-    return r;
-  };
-  int run_f = 0, run_t = 0;
+  int run = 0;
   for (int g = g0; g < g1; ++g) {
-    int r = rows_of(g);
-    if (r < 0) {
+    int rows_g = ctl.goff[g + 1] - ctl.goff[g];
+    if (rows_g < 0 || ctl.goff[g + 1] > sg.capacity) {
       record_error(p.err, kErrCapacity);
-      r = 0;
+      rows_g = 0;
     }
-    run_f += (r / TBM) * sg.n_tiles;
-    run_t += (r % TBM ? 1 : 0) * sg.n_tiles;
+    run += ((rows_g + TBM - 1) / TBM) * sg.n_tiles;
   }
-  int inc_f = run_f, inc_t = run_t;
+  int incl = run;
 #pragma unroll
   for (int off = 1; off < 32; off <<= 1) {
-    const int vf = __shfl_up_sync(0xffffffffu, inc_f, off), vt = __shfl_up_sync(0xffffffffu, inc_t, off);
-    if (lane >= off) {
-      inc_f += vf;
-      inc_t += vt;
-    }
+    int v = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += v;
   }
-  int ex_f = inc_f - run_f, ex_t = inc_t - run_t;
+  int excl = incl - run;
   for (int g = g0; g < g1; ++g) {
-    ctl.full_start[g] = ex_f;
-    ctl.tail_start[g] = ex_t;
-    const int r = max(0, rows_of(g));
-    ex_f += (r / TBM) * sg.n_tiles;
-    ex_t += (r % TBM ? 1 : 0) * sg.n_tiles;
+    ctl.tile_start[g] = excl;
+    int rows_g = max(0, ctl.goff[g + 1] - ctl.goff[g]);
+    if (ctl.goff[g + 1] > sg.capacity) rows_g = 0;
+    excl += ((rows_g + TBM - 1) / TBM) * sg.n_tiles;
   }
-  const int tot_f = __shfl_sync(0xffffffffu, inc_f, 31), tot_t = __shfl_sync(0xffffffffu, inc_t, 31);
+  int total0 = __shfl_sync(0xffffffffu, incl, 31);
   if (lane == 0) {
-    ctl.full_start[ng] = tot_f;
-    ctl.tail_start[ng] = tot_t;
-    int cnt[4] = {tot_f, 0, tot_t, 0};  // by kind
-    if (p.nseg > 1) {
-      const Segment& s1 = p.seg[1];
-      cnt[1] = (s1.rows / TBM) * s1.n_tiles;
-      cnt[3] = (s1.rows % TBM ? 1 : 0) * s1.n_tiles;
-    }
-    const int L = p.seg_first;
-    const int kinds[4] = {L, 1 - L, 2 + L, 3 - L};
-    int acc = 0;
-    for (int c = 0; c < 4; ++c) {
-      ctl.cls_kind[c] = kinds[c];
-      ctl.cls_start[c] = acc;
-      acc += cnt[kinds[c]];
-    }
-    ctl.cls_start[4] = acc;
-    ctl.total_tiles = acc;
+    ctl.tile_start[ng] = total0;
+    ctl.seg0_tiles = total0;
+    int total1 = 0;
+    if (p.nseg > 1) total1 = ((p.seg[1].rows + TBM - 1) / TBM) * p.seg[1].n_tiles;
+    ctl.seg1_tiles = total1;
+    ctl.total_tiles = total0 + total1;
   }
 }
 
@@ -156,36 +133,40 @@ __device__ __forceinline__ int sched_tile(int r, int u, int U) { return r * U + 
 template <int TBM>
 __device__ __forceinline__ TileInfo decode(const Params& p, const SmemCtl& s, int tile) {
   TileInfo ti;
-  int c = 0;
-  while (c < 3 && tile >= s.cls_start[c + 1]) ++c;
-  const int kind = s.cls_kind[c];
-  const int local = tile - s.cls_start[c];
-  const bool tail = kind >= 2;
-  const int seg = kind & 1;
-  const Segment& sg = p.seg[seg];
-  ti.seg = seg;
+  const int n_first = p.seg_first == 0 ? s.seg0_tiles : s.seg1_tiles;
+  int seg, local;
+  if (tile < n_first) {
+    seg = p.seg_first;
+    local = tile;
+  } else {
+    seg = 1 - p.seg_first;
+    local = tile - n_first;
+  }
   if (seg == 0) {
-    const int* start = tail ? s.tail_start : s.full_start;
-    int lo = 0, hi = sg.ngroups;  // g with start[g] <= local < start[g + 1]
+    const Segment& sg = p.seg[0];
+    int lo = 0, hi = sg.ngroups;  // g with tile_start[g] <= local < tile_start[g + 1]
     while (hi - lo > 1) {
       const int mid = (lo + hi) >> 1;
-      if (start[mid] <= local) lo = mid; else hi = mid;
+      if (s.tile_start[mid] <= local) lo = mid; else hi = mid;
     }
     const int g = lo;
-    const int l = local - start[g];
+    const int l = local - s.tile_start[g];
+    const int m_blk = l / sg.n_tiles;
+    ti.n_blk = l - m_blk * sg.n_tiles;
     const int rows_g = s.goff[g + 1] - s.goff[g];
-    const int m_blk = tail ? rows_g / TBM : l / sg.n_tiles;
-    ti.n_blk = tail ? l : l - m_blk * sg.n_tiles;
+    ti.seg = 0;
     ti.group = g;
     ti.row0 = s.goff[g] + m_blk * TBM;
-    ti.rows_valid = tail ? rows_g - m_blk * TBM : TBM;
+    ti.rows_valid = min(TBM, rows_g - m_blk * TBM);
     ti.b_row0 = s.gw[g] * sg.b_rows_per_group + ti.n_blk * BN;
   } else {
-    const int m_blk = tail ? sg.rows / TBM : local / sg.n_tiles;
-    ti.n_blk = tail ? local : local - m_blk * sg.n_tiles;
+    const Segment& sg = p.seg[1];
+    const int m_blk = local / sg.n_tiles;
+    ti.n_blk = local - m_blk * sg.n_tiles;
+    ti.seg = 1;
     ti.group = 0;
     ti.row0 = m_blk * TBM;
-    ti.rows_valid = tail ? sg.rows - m_blk * TBM : TBM;
+    ti.rows_valid = min(TBM, sg.rows - ti.row0);
     ti.b_row0 = ti.n_blk * BN;
   }
   return ti;
