@@ -96,12 +96,13 @@ __global__ void __launch_bounds__(kThreads) grouped_gemm_f32(const Params p) {
       brow0 = 0;
     }
     const Segment& sg = p.seg[segi];
-    // B rows of this tile: SwiGLU takes the 64 gate rows of packed block n_blk (128 rows: 64
-    // gate, then the 64 matching up rows); other epilogues take 64 consecutive rows.
+    // B rows of this tile: SwiGLU takes 64 gate rows at (n_blk/2)*256 + (n_blk%2)*64 (packed
+    // 256-row blocks: 128 gate rows, then the 128 matching up rows) and the up rows 128 further;
+    // other epilogues take 64 consecutive rows.
     int bcol_gate, bcol_up;
     if (glu) {
-      bcol_gate = brow0 + n_blk * 128;
-      bcol_up = bcol_gate + 64;
+      bcol_gate = brow0 + (n_blk / 2) * 256 + (n_blk % 2) * 64;
+      bcol_up = bcol_gate + 128;
     } else {
       bcol_gate = brow0 + n_blk * TN;
       bcol_up = bcol_gate;

@@ -17,8 +17,8 @@
 //   warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns, activation, bf16 pack, masked
 //               16-byte stores; the accumulator is released as soon as it has been read, so
 //               the next tile's MMAs overlap this tile's stores.
-// SwiGLU weights are packed in 128-row blocks of 64 gate rows then the 64 matching up rows, so a
-// 256-column accumulator holds two (gate, up) blocks.
+// SwiGLU weights are packed in 256-row blocks of 128 gate rows then the 128 matching up rows, so
+// one 256-column accumulator row yields 128 finished SiLU(g) * u channels.
 // Tiles follow the boustrophedon schedule of gemm_sm100.cuh (the longer-K segment first,
 // group-major inside a segment).  Group row offsets are read on the device, so no host sync is
 // needed.
@@ -189,11 +189,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int col0 = ti.n_blk * (BN / 2);
 #pragma unroll 1
         for (int c = 0; c < BN / 2; c += 32) {
-          // accumulator columns: 128-column blocks of 64 gate then the 64 matching up channels
-          const int gc = (c >> 6) * 128 + (c & 63);
+          // accumulator columns: 128 gate channels, then the 128 matching up channels
           uint32_t g[32], u[32];
-          tmem_ld32(taddr + gc, g);
-          tmem_ld32(taddr + gc + 64, u);
+          tmem_ld32(taddr + c, g);
+          tmem_ld32(taddr + BN / 2 + c, u);
           tmem_wait_ld();
           uint32_t packed[16];
 #pragma unroll

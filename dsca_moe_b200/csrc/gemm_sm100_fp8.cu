@@ -337,8 +337,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int col0 = ti.n_blk * (BN / 2);
 #pragma unroll 1
         for (int c = 0; c < BN / 2; c += 32) {
-          // packed columns: 128-column blocks of 64 gate then the 64 matching up channels
-          const int gc = (c >> 6) * 128 + (c & 63), uc = gc + 64;
+          // packed columns: 128 gate channels, then the 128 matching up channels
+          const int gc = c, uc = c + BN / 2;
           uint32_t g[32], u[32];
           tmem_ld32(taddr + gc, g);
           tmem_ld32(taddr + uc, u);

@@ -9,13 +9,13 @@
 //     tile of the same tensor work).
 //   * The token count of a tile is rounded up to 16 only (the MMA N granularity), not to a tile
 //     height: an expert with 300 routed rows costs 256 + 48 token columns instead of 2 x 256
-//     rows.  Token rows are loaded in 32-row boxes, only as many as the tile needs.
+//     rows.
 //   * Accumulator (per CTA): TMEM lane = weight row, column = token.  The epilogue writes each
-//     token's outputs as 64-byte row pieces (32 consecutive channels).  SwiGLU weights are
-//     packed in 128-row blocks of 64 gate rows then the 64 matching up rows, so one CTA holds
-//     both halves of its 64 channels: the warp reading gate lanes and the warp reading the
-//     matching up lanes swap half a chunk through shared memory and each finishes 16 tokens.
-//     Outputs are staged per warp in shared memory and written as 16-byte pieces of token rows.
+//     token's outputs as 64-byte row pieces (32 consecutive channels), staged per warp in
+//     shared memory and written as 16-byte pieces.  SwiGLU: weights are packed in 256-row
+//     blocks [128 gate | 128 up]; a CTA loads the gate and the up rows of its 128 channels and
+//     runs two MMAs per K step into a gate and an up accumulator (N <= 128), so SiLU(g) * u is
+//     formed in registers.
 //   warp 0      TMA producer (one thread), 128-byte swizzle, 6-stage ring.  No multicast.
 //   warp 1      TMEM allocator (512 columns, two accumulators); in the even CTA the MMA issuer.
 //   warps 2-5   epilogue.
@@ -40,7 +40,8 @@ struct Cfg {
   static constexpr bool kGlu = EPI == kEpiSwiGLU;
   static constexpr int S = kGlu ? 5 : 6;                  // stages
   static constexpr int TBN = kGlu ? 128 : 256;            // token rows per tile (MMA N)
-  static constexpr int kWBox = kGlu ? 64 : 128;           // weight rows per TMA box
+  static constexpr int kWBox = 128;                       // weight rows per TMA box
+  static constexpr int kTBox = TBN / 2;                   // token rows per TMA box (one per stage)
   static constexpr int kABytes = 128 * BK * 2;            // 16 KB
   static constexpr int kA2Bytes = kGlu ? 128 * BK * 2 : 0;
   static constexpr int kTBytes = (TBN / 2) * BK * 2;      // this CTA's token rows
@@ -48,8 +49,6 @@ struct Cfg {
   static constexpr int kStageElems = 32 * 32;             // epilogue staging per warp, bf16
   static constexpr int kSmemBytes = S * kStageBytes + 4 * kStageElems * 2 + 1024;
 };
-constexpr int kBox = 32;                  // token rows per TMA box
-constexpr int kBoxBytes = kBox * BK * 2;  // 4 KB
 
 // MMA N for a tile of `ntok` token rows: a multiple of 16 (each CTA holds N / 2 rows, a whole
 // number of 8-row swizzle atoms).
@@ -125,12 +124,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const CUtensorMap* mw = ti.seg == 0 ? &tmW0 : &tmW1;
         const CUtensorMap* mt = ti.seg == 0 ? &tmT0 : &tmT1;
         const int half = tile_n(ti.rows_valid) / 2;
-        const int nbox = (half + kBox - 1) / kBox;
-        const uint32_t tx = 2u * (uint32_t)(C::kABytes + C::kA2Bytes + nbox * kBoxBytes);
-        // weight rows: SwiGLU packs 128-row blocks [64 gate | 64 up]; this CTA's 128 channels
-        // are the 64-channel blocks 4 n_blk + 2 rank and + 1 (packed rows 512 n_blk + 256 rank)
-        const int w_row = C::kGlu ? ti.b_row0 - ti.n_blk * BN + 512 * ti.n_blk + 256 * (int)rank
-                                  : ti.b_row0 + 128 * (int)rank;
+        // the whole token box lands every stage (rows past the tile's tokens are loaded and not
+        // used by the MMA)
+        constexpr uint32_t tx = 2u * (uint32_t)C::kStageBytes;
+        // weight rows: SwiGLU packs 256-row blocks [128 gate | 128 up]; this CTA's 128 channels
+        // are packed block 2 n_blk + rank
+        const int w_row = C::kGlu ? ti.b_row0 + ti.n_blk * BN + 256 * (int)rank : ti.b_row0 + 128 * (int)rank;
         const int t_row = ti.row0 + half * (int)rank;
         const int kb_n = p.seg[ti.seg].k_blocks;
         for (int kb = 0; kb < kb_n; ++kb) {
@@ -138,17 +137,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t fb = smem_u32(&ctl.full[s]);
           const uint32_t fb0 = mapa_shared(fb, 0);  // the even CTA's full barrier
           if (rank == 0) mbar_arrive_expect_tx(fb, tx);
-          if constexpr (C::kGlu) {
-            const uint32_t ga = smem_a + s * C::kABytes, ua = smem_a2 + s * C::kA2Bytes;
-            tma_load_2d_pair(ga, mw, fb0, kb * BK, w_row);
-            tma_load_2d_pair(ga + 64 * 128, mw, fb0, kb * BK, w_row + 128);
-            tma_load_2d_pair(ua, mw, fb0, kb * BK, w_row + 64);
-            tma_load_2d_pair(ua + 64 * 128, mw, fb0, kb * BK, w_row + 192);
-          } else {
-            tma_load_2d_pair(smem_a + s * C::kABytes, mw, fb0, kb * BK, w_row);
-          }
-          for (int b = 0; b < nbox; ++b)
-            tma_load_2d_pair(smem_t + s * C::kTBytes + b * kBoxBytes, mt, fb0, kb * BK, t_row + b * kBox);
+          tma_load_2d_pair(smem_a + s * C::kABytes, mw, fb0, kb * BK, w_row);
+          if constexpr (C::kGlu) tma_load_2d_pair(smem_a2 + s * C::kA2Bytes, mw, fb0, kb * BK, w_row + 128);
+          tma_load_2d_pair(smem_t + s * C::kTBytes, mt, fb0, kb * BK, t_row);
           pending_phase[s] = (int)ph;
           if (++s == S) { s = 0; ph ^= 1u; }
         }
@@ -376,13 +367,14 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
   const int phases = f->phases == 0 ? 3 : f->phases;
   if (!routed && !shared) return DSCA_OK;
   if (f->n1p % 256 != 0 || f->dp % 256 != 0 || (shared && f->shared_n1p % 256 != 0)) return DSCA_ERR_BAD_ARG;
-  constexpr uint32_t tbox = gemm::pair::kBox;
+
   int rc;
   // ---- GEMM1: h = act(a . w1^T)   (+ hs = act(xs . ws1^T))
   if (phases & 1) {
     CUtensorMap w0, t0, w1, t1;
     const bool glu = f->act == DSCA_ACT_SWIGLU;
-    const uint32_t wbox = glu ? gemm::pair::Cfg<gemm::kEpiSwiGLU>::kWBox : gemm::pair::Cfg<gemm::kEpiReLU>::kWBox;
+    const uint32_t wbox = gemm::pair::Cfg<gemm::kEpiSwiGLU>::kWBox;
+    const uint32_t tbox = glu ? gemm::pair::Cfg<gemm::kEpiSwiGLU>::kTBox : gemm::pair::Cfg<gemm::kEpiReLU>::kTBox;
     if ((rc = make_map_bf16(&w0, f->w1, (uint64_t)f->num_experts_w * f->n1p, (uint64_t)f->d, wbox))) return rc;
     if ((rc = make_map_bf16(&t0, f->a, (uint64_t)f->capacity, (uint64_t)f->d, tbox))) return rc;
     if (shared) {
@@ -431,6 +423,7 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
   if (phases & 2) {
     CUtensorMap w0, t0, w1, t1;
     constexpr uint32_t wbox = gemm::pair::Cfg<gemm::kEpiStore>::kWBox;
+    constexpr uint32_t tbox = gemm::pair::Cfg<gemm::kEpiStore>::kTBox;
     if ((rc = make_map_bf16(&w0, f->w2, (uint64_t)f->num_experts_w * f->dp, (uint64_t)f->ip, wbox))) return rc;
     if ((rc = make_map_bf16(&t0, f->h, (uint64_t)f->capacity, (uint64_t)f->ip, tbox))) return rc;
     if (shared) {

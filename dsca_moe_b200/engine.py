@@ -136,30 +136,30 @@ def dequantize_fp8(pe: PackedExperts) -> PackedExperts:
 def unpack_swiglu(pe: PackedExperts):
     """Inverse of pack_swiglu on float weights: (gate [E,I,d], up [E,I,d], down [E,d,I], shared)."""
     E, I, d, ip = pe.E, pe.inter, pe.d, pe.ip
-    w = pe.w1.float().view(E, ip // 64, 2, 64, d)
+    w = pe.w1.float().view(E, ip // 128, 2, 128, d)
     gate = w[:, :, 0].reshape(E, ip, d)[:, :I]
     up = w[:, :, 1].reshape(E, ip, d)[:, :I]
     down = pe.w2.float()[:, :d, :I]
     shared = None
     if pe.ws1 is not None:
         sip, Is = pe.s_ip, pe.s_inter
-        s = pe.ws1.float().view(sip // 64, 2, 64, d)
+        s = pe.ws1.float().view(sip // 128, 2, 128, d)
         shared = (s[:, 0].reshape(sip, d)[:Is], s[:, 1].reshape(sip, d)[:Is], pe.ws2.float()[:d, :Is])
     return gate, up, down, shared
 
 
 def _pack_glu_w1(gate: torch.Tensor, up: torch.Tensor) -> tuple[torch.Tensor, int]:
-    """[E, I, d] gate / up -> [E, 2*Ip, d]: 128-row blocks of 64 gate rows, then the 64 up rows of
-    the same intermediate channels (Ip = I rounded up to 128, so 2*Ip is a multiple of 256)."""
+    """[E, I, d] gate / up -> [E, 2*Ip, d]: 256-row blocks of 128 gate rows, then the 128 up rows
+    of the same intermediate channels (Ip = I rounded up to 128)."""
     E, I, d = gate.shape
     ip = _ceil(I, 128) * 128
-    w = torch.zeros(E, ip // 64, 2, 64, d, dtype=gate.dtype, device=gate.device)
+    w = torch.zeros(E, ip // 128, 2, 128, d, dtype=gate.dtype, device=gate.device)
     g = torch.zeros(E, ip, d, dtype=gate.dtype, device=gate.device)
     u = torch.zeros(E, ip, d, dtype=gate.dtype, device=gate.device)
     g[:, :I] = gate
     u[:, :I] = up
-    w[:, :, 0] = g.view(E, ip // 64, 64, d)
-    w[:, :, 1] = u.view(E, ip // 64, 64, d)
+    w[:, :, 0] = g.view(E, ip // 128, 128, d)
+    w[:, :, 1] = u.view(E, ip // 128, 128, d)
     return w.view(E, 2 * ip, d).contiguous(), ip
 
 

@@ -13,12 +13,12 @@ def test_swiglu_packing_blocks_and_round_trip():
     # intermediate width rounded up to 128, so the gate+up rows are a multiple of 256
     assert pe.ip == 256 and pe.n1p == 512 and pe.n1p % 256 == 0 and pe.dp == 256
     assert pe.s_ip == 256 and pe.s_n1p == 512
-    # 128-row blocks: 64 gate rows, then the 64 up rows of the same channels
-    for blk in range(pe.n1p // 128):
+    # 256-row blocks: 128 gate rows, then the 128 up rows of the same channels
+    for blk in range(pe.n1p // 256):
         for half, src in ((0, gate), (1, up)):
-            rows = pe.w1[:, blk * 128 + half * 64: blk * 128 + half * 64 + 64]
-            ch0 = blk * 64
-            n = max(0, min(64, I - ch0))
+            rows = pe.w1[:, blk * 256 + half * 128: blk * 256 + half * 128 + 128]
+            ch0 = blk * 128
+            n = max(0, min(128, I - ch0))
             assert torch.equal(rows[:, :n], src[:, ch0:ch0 + n])
             assert torch.count_nonzero(rows[:, n:]) == 0
     g2, u2, d2, (sg2, su2, sd2) = unpack_swiglu(pe)
