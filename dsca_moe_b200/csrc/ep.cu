@@ -21,8 +21,10 @@ namespace ep {
 
 // ------------------------------------------------------------------ harmony plan, one warp
 // S (shared) [G][E][G]; meta [G][E]; all lanes call it, control flow is warp-uniform.
-__device__ void harmony_warp(const int32_t* meta, int G, int E, const int32_t* e2g, int eq_tokens, int32_t* S,
-                             long long* amt) {
+// Reference form with 64-bit sums and shuffle reductions (used when the token total does not fit
+// the packed keys of harmony_warp_fast below).
+__device__ void harmony_warp_wide(const int32_t* meta, int G, int E, const int32_t* e2g, int eq_tokens, int32_t* S,
+                                  long long* amt) {
   const int lane = threadIdx.x & 31;
   for (int i = lane; i < G * E * G; i += 32) S[i] = 0;
   __syncwarp();
@@ -105,11 +107,91 @@ __device__ void harmony_warp(const int32_t* meta, int G, int E, const int32_t* e
   __syncwarp();
 }
 
+// The same plan with every arg-max / arg-min as one warp reduction over a packed (value, index)
+// key (value << bits | index or its complement, so ties go to the lowest index exactly as in the
+// reference's first-index scans) and the per-expert load of each GPU kept in Le[e][g] instead
+// of being re-summed over the sources on every pass.  Token totals below 2^26.
+__device__ void harmony_warp(const int32_t* meta, int G, int E, const int32_t* e2g, int eq_tokens, int32_t* S,
+                             long long* amt_wide, int32_t* Le, int32_t* amt) {
+  const int lane = threadIdx.x & 31;
+  const unsigned full = 0xffffffffu;
+  int part = 0;
+  for (int i = lane; i < G * E; i += 32) part += meta[i];
+  const unsigned total = __reduce_add_sync(full, (unsigned)part);
+  if (total >= (1u << 26)) {
+    harmony_warp_wide(meta, G, E, e2g, eq_tokens, S, amt_wide);
+    return;
+  }
+  for (int i = lane; i < G * E * G; i += 32) S[i] = 0;
+  for (int i = lane; i < E * G; i += 32) Le[i] = 0;
+  __syncwarp();
+  for (int i = lane; i < G * E; i += 32) {
+    const int src = i / E, e = i % E;
+    S[(src * E + e) * G + e2g[e]] = meta[i];
+  }
+  for (int e = lane; e < E; e += 32) {
+    int se = 0;
+    for (int src = 0; src < G; ++src) se += meta[src * E + e];
+    Le[e * G + e2g[e]] = se;
+  }
+  __syncwarp();
+  if (eq_tokens < 0) return;
+  const int avg = (int)(total / (unsigned)G);
+  if (lane < G) {
+    int a = 0;
+    for (int e = 0; e < E; ++e) a += Le[e * G + lane];
+    amt[lane] = a;
+  }
+  __syncwarp();
+  for (int guard = 0; guard < (1 << 20); ++guard) {
+    const int a = lane < G ? amt[lane] : 0;
+    if (!__any_sync(full, lane < G && a > avg)) break;
+    // most loaded GPU (lowest index on ties) and least loaded GPU (lowest index on ties)
+    const unsigned mk = __reduce_max_sync(full, lane < G ? ((unsigned)a << 5) | (31u - lane) : 0u);
+    const unsigned lk = __reduce_min_sync(full, lane < G ? ((unsigned)a << 5) | (unsigned)lane : 0xffffffffu);
+    const int over = 31 - (int)(mk & 31u), least = (int)(lk & 31u);
+    if (least == over || amt[least] + eq_tokens > avg) break;
+    // the expert with most tokens on the overloaded GPU (lowest id on ties)
+    unsigned ek = 0u;
+    for (int e = lane; e < E; e += 32) ek = max(ek, ((unsigned)Le[e * G + over] << 6) | (63u - e));
+    ek = __reduce_max_sync(full, ek);
+    const int e = 63 - (int)(ek & 63u);
+    if ((int)(ek >> 6) < eq_tokens) break;
+    int amount_over = amt[over] - avg;
+    int moved = 0;
+    while (amount_over > 0 && avg - amt[least] > 0) {
+      // the source rank with most tokens of expert e on `over` (lowest rank on ties)
+      const unsigned tk = __reduce_max_sync(
+          full, lane < G ? ((unsigned)S[(lane * E + e) * G + over] << 5) | (31u - lane) : 0u);
+      const int tv = (int)(tk >> 5), ti = 31 - (int)(tk & 31u);
+      if (tv <= 0) break;
+      const int room = avg - amt[least];
+      const int n = tv < room ? tv : room;
+      __syncwarp();
+      if (lane == 0) {
+        S[(ti * E + e) * G + over] -= n;
+        S[(ti * E + e) * G + least] += n;
+        Le[e * G + over] -= n;
+        Le[e * G + least] += n;
+        amt[over] -= n;
+        amt[least] += n;
+      }
+      __syncwarp();
+      amount_over -= n;
+      moved += n;
+    }
+    if (moved == 0) break;
+  }
+  __syncwarp();
+}
+
 // ------------------------------------------------------------------ plan kernel
 __global__ void __launch_bounds__(256) plan_kernel(Ctx* c, const int32_t* counts, uint64_t limit_ns, int32_t* err) {
   __shared__ int32_t meta_s[kMaxG * kMaxE];
   __shared__ int32_t S_s[kMaxG * kMaxE * kMaxG];
   __shared__ long long amt_s[kMaxG];
+  __shared__ int32_t amt32_s[kMaxG];
+  __shared__ int32_t le_s[kMaxE * kMaxG];
   __shared__ int32_t e2g_s[kMaxE];
   const int G = c->G, E = c->E, me = c->me, tid = threadIdx.x;
   const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(&c->epoch) + 1u;
@@ -133,7 +215,7 @@ __global__ void __launch_bounds__(256) plan_kernel(Ctx* c, const int32_t* counts
   for (int e = tid; e < E; e += blockDim.x) e2g_s[e] = c->expert_to_gpu[e];
   __syncthreads();
   // 3. the plan
-  if (tid < 32) harmony_warp(meta_s, G, E, e2g_s, c->eq_tokens, S_s, amt_s);
+  if (tid < 32) harmony_warp(meta_s, G, E, e2g_s, c->eq_tokens, S_s, amt_s, le_s, amt32_s);
   __syncthreads();
   auto Sv = [&](int src, int e, int dst) { return S_s[(src * E + e) * G + dst]; };
   for (int i = tid; i < G * E * G; i += blockDim.x) {
@@ -291,11 +373,13 @@ __global__ void plan_eval_kernel(const int32_t* meta, int G, int E, const int32_
   __shared__ int32_t meta_s[kMaxG * kMaxE];
   __shared__ int32_t S_s[kMaxG * kMaxE * kMaxG];
   __shared__ long long amt_s[kMaxG];
+  __shared__ int32_t amt32_s[kMaxG];
+  __shared__ int32_t le_s[kMaxE * kMaxG];
   __shared__ int32_t e2g_s[kMaxE];
   for (int i = threadIdx.x; i < G * E; i += 32) meta_s[i] = meta[i];
   for (int i = threadIdx.x; i < E; i += 32) e2g_s[i] = e2g[i];
   __syncwarp();
-  harmony_warp(meta_s, G, E, e2g_s, eq, S_s, amt_s);
+  harmony_warp(meta_s, G, E, e2g_s, eq, S_s, amt_s, le_s, amt32_s);
   for (int i = threadIdx.x; i < G * E * G; i += 32) S[i] = S_s[i];
 }
 
