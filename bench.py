@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="expert-parallel exchange: fused NVLink kernels (default) or the NCCL baseline")
     ap.add_argument("--ep-return", choices=["overlap", "fused"], default="overlap")
+    ap.add_argument("--ep-side-sms", type=int, default=0,
+                    help="SMs left to the dispatch / return copy kernels beside the shared-expert GEMMs")
     ap.add_argument("--tile-rows", type=int, choices=[0, 128, 256], default=0,
                     help="bf16 expert GEMM tiles: 0 = default per GEMM, 256 = CTA pairs (cta_group::2, "
                          "weights as M), 128 = one CTA per 128-token tile")
@@ -344,6 +346,7 @@ def main():
     eng.exchange = args.exchange
     eng.ep_return = args.ep_return
     eng.tile_rows = args.tile_rows
+    eng.ep_side_sms = args.ep_side_sms
     peaks = load_peaks()
     if args.once:
         eng.forward(x)

@@ -337,6 +337,9 @@ class MoEEngine:
         # "overlap": routed GEMM2 stores locally and a return kernel sends the rows on a side
         # stream beside the shared-expert GEMM2; "fused": GEMM2's epilogue stores them remotely
         self.ep_return = "overlap"
+        # SMs kept free of the shared-expert GEMMs while the side-stream copy kernels run beside
+        # them (0: the copy kernels' small CTAs fit next to the persistent GEMM CTAs)
+        self.ep_side_sms = 0
         # True: the router's last CTA computes counts / offsets / block bases (one launch);
         # False: the separate dsca_dispatch_scan launch does
         self.fuse_scan = True
@@ -449,7 +452,7 @@ class MoEEngine:
             self._ffn_call(x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, 3, ep_ctx)
 
     def _ffn_call(self, x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, phases, ep_ctx=None,
-                  segments=3):
+                  segments=3, num_ctas=None):
         pe = self.experts
         f = L.FfnArgs()
         f.dtype, f.act, f.d = (L.F8E4M3 if pe.fp8 else _dt(self.dtype)), pe.act, self.d
@@ -464,7 +467,7 @@ class MoEEngine:
         if pe.fp8:
             f.w1_scale, f.w2_scale = _ptr(pe.w1_scale), _ptr(pe.w2_scale)
             f.ws1_scale, f.ws2_scale = _ptr(pe.ws1_scale), _ptr(pe.ws2_scale)
-        f.err, f.num_ctas, f.phases = _ptr(self.err), self.num_ctas, phases
+        f.err, f.num_ctas, f.phases = _ptr(self.err), self.num_ctas if num_ctas is None else num_ctas, phases
         f.tile_rows = self.tile_rows
         f.ep_ctx = _ptr(ep_ctx)
         f.segments = segments
@@ -614,8 +617,9 @@ class MoEEngine:
             dispatched.record(side)
         args = (x, ws, ep["recv"], ep["h"], ep["y"], ep["recv_cap"], self.E, ep["group_offsets"], None)
         has_shared = self.experts.ws1 is not None
+        side_ctas = max(2, self.num_sms - self.ep_side_sms) if self.ep_side_sms > 0 else None
         if has_shared:
-            self._ffn_call(*args, 1, segments=2)
+            self._ffn_call(*args, 1, segments=2, num_ctas=side_ctas)
             self._mark("gemm1_shared")
         main.wait_event(dispatched)
         L.check(lib.dsca_ep_wait(ctx, 1, self.wait_limit_ns, err, _stream()), "dsca_ep_wait")
@@ -639,7 +643,7 @@ class MoEEngine:
                 returned = torch.cuda.Event()
                 returned.record(side)
             if has_shared:
-                self._ffn_call(*args, 2, segments=2)
+                self._ffn_call(*args, 2, segments=2, num_ctas=side_ctas)
                 self._mark("gemm2_shared")
             main.wait_event(returned)
         L.check(lib.dsca_ep_wait(ctx, 2, self.wait_limit_ns, err, _stream()), "dsca_ep_wait")
