@@ -131,7 +131,16 @@ __global__ void __launch_bounds__(256) permute_kernel(dsca_permute_args a) {
       if (xh != nullptr) xh[v] = o;
     }
   } else {
-    for (int v = lane; v < nvec; v += 32) dstp[v] = src[v];
+    // eight 16-byte loads in flight per lane before the stores (one memory latency per row)
+    int v = lane;
+    for (; v + 7 * 32 < nvec; v += 8 * 32) {
+      uint4 r[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) r[i] = src[v + 32 * i];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) dstp[v + 32 * i] = r[i];
+    }
+    for (; v < nvec; v += 32) dstp[v] = src[v];
   }
 }
 
@@ -153,6 +162,15 @@ template <typename T>
 struct Vec8;
 template <>
 struct Vec8<__nv_bfloat16> {
+  struct Raw {
+    uint4 u;
+  };
+  static __device__ Raw load_raw(const void* p) { return Raw{*reinterpret_cast<const uint4*>(p)}; }
+  static __device__ void convert(const Raw& r, float (&v)[8]) {
+    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&r.u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __bfloat162float(h[i]);
+  }
   static __device__ void load(const void* p, float (&v)[8]) {
     uint4 u = *reinterpret_cast<const uint4*>(p);
     const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
@@ -170,6 +188,16 @@ struct Vec8<__nv_bfloat16> {
 };
 template <>
 struct Vec8<float> {
+  struct Raw {
+    float4 a, b;
+  };
+  static __device__ Raw load_raw(const void* p) {
+    return Raw{reinterpret_cast<const float4*>(p)[0], reinterpret_cast<const float4*>(p)[1]};
+  }
+  static __device__ void convert(const Raw& r, float (&v)[8]) {
+    v[0] = r.a.x; v[1] = r.a.y; v[2] = r.a.z; v[3] = r.a.w;
+    v[4] = r.b.x; v[5] = r.b.y; v[6] = r.b.z; v[7] = r.b.w;
+  }
   static __device__ void load(const void* p, float (&v)[8]) {
     float4 a = reinterpret_cast<const float4*>(p)[0];
     float4 b = reinterpret_cast<const float4*>(p)[1];
@@ -182,40 +210,84 @@ struct Vec8<float> {
   }
 };
 
-template <typename T>
+// KC: the slot count as a compile-time constant (1, 2, 4, 8), or 0 for any count up to
+// DSCA_MAX_TOPK (registers sized for the maximum).
+template <typename T, int KC>
 __global__ void __launch_bounds__(256) combine_kernel(dsca_combine_args a) {
+  constexpr int KMAX = KC > 0 ? KC : DSCA_MAX_TOPK;
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = lane_id();
   if (t >= a.T) return;
-  int rows[DSCA_MAX_TOPK];
-  float w[DSCA_MAX_TOPK];
-  for (int j = 0; j < a.top_k; ++j) {
-    rows[j] = a.token_row[(size_t)t * a.top_k + j];
-    w[j] = a.topk_w[(size_t)t * a.top_k + j];
-    if (rows[j] < 0 || rows[j] >= a.rows) {
-      if (lane == 0) record_error(a.err, kErrIndex);
-      return;
+  int rows[KMAX];
+  float w[KMAX];
+  bool bad = false;
+#pragma unroll
+  for (int j = 0; j < KMAX; ++j) {
+    if (KC > 0 || j < a.top_k) {
+      rows[j] = a.token_row[(size_t)t * a.top_k + j];
+      w[j] = a.topk_w[(size_t)t * a.top_k + j];
+      bad |= rows[j] < 0 || rows[j] >= a.rows;
     }
+  }
+  if (bad) {
+    if (lane == 0) record_error(a.err, kErrIndex);
+    return;
   }
   const float sg = (a.ys != nullptr && a.shared_gate != nullptr) ? a.shared_gate[t] : 0.0f;
   const T* Y = reinterpret_cast<const T*>(a.y);
   const T* YS = reinterpret_cast<const T*>(a.ys);
   T* O = reinterpret_cast<T*>(a.out);
-  for (int c = lane * 8; c < a.d; c += 256) {
-    float acc[8], v[8];
+  // every slot's 16-byte piece (and the shared expert's) of two chunks is loaded before the first
+  // FMA, so two chunks cost one memory latency; the sums still run in slot order, then the
+  // shared term
+  using R = typename Vec8<T>::Raw;
+  constexpr int U = 2;  // chunks in flight per lane
+  for (int c0 = lane * 8; c0 < a.d; c0 += 256 * U) {
+    R raw[U][KMAX + 1];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-    for (int j = 0; j < a.top_k; ++j) {
-      Vec8<T>::load(Y + (size_t)rows[j] * a.d + c, v);
+    for (int h = 0; h < U; ++h) {
+      const int c = c0 + 256 * h;
+      if (c < a.d) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = __fmaf_rn(w[j], v[i], acc[i]);
+        for (int j = 0; j < KMAX; ++j)
+          if (KC > 0 || j < a.top_k) raw[h][j] = Vec8<T>::load_raw(Y + (size_t)rows[j] * a.d + c);
+        if (YS != nullptr) raw[h][KMAX] = Vec8<T>::load_raw(YS + (size_t)t * a.d + c);
+      }
     }
-    if (YS != nullptr) {
-      Vec8<T>::load(YS + (size_t)t * a.d + c, v);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = __fmaf_rn(sg, v[i], acc[i]);
+    for (int h = 0; h < U; ++h) {
+      const int c = c0 + 256 * h;
+      if (c >= a.d) break;
+      float acc[8], v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+#pragma unroll
+      for (int j = 0; j < KMAX; ++j) {
+        if (KC > 0 || j < a.top_k) {
+          Vec8<T>::convert(raw[h][j], v);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[i] = __fmaf_rn(w[j], v[i], acc[i]);
+        }
+      }
+      if (YS != nullptr) {
+        Vec8<T>::convert(raw[h][KMAX], v);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = __fmaf_rn(sg, v[i], acc[i]);
+      }
+      Vec8<T>::store(O + (size_t)t * a.d + c, acc);
     }
-    Vec8<T>::store(O + (size_t)t * a.d + c, acc);
+  }
+}
+
+
+template <typename T>
+static void launch_combine(const dsca_combine_args& a, int blocks, cudaStream_t stream) {
+  switch (a.top_k) {
+    case 1: combine_kernel<T, 1><<<blocks, 256, 0, stream>>>(a); break;
+    case 2: combine_kernel<T, 2><<<blocks, 256, 0, stream>>>(a); break;
+    case 4: combine_kernel<T, 4><<<blocks, 256, 0, stream>>>(a); break;
+    case 8: combine_kernel<T, 8><<<blocks, 256, 0, stream>>>(a); break;
+    default: combine_kernel<T, 0><<<blocks, 256, 0, stream>>>(a); break;
   }
 }
 
@@ -223,9 +295,9 @@ int launch_combine(const dsca_combine_args* a, cudaStream_t stream) {
   if (a->T == 0) return DSCA_OK;
   const int blocks = (int)(((long long)a->T * 32 + 255) / 256);
   if (a->dtype == DSCA_BF16)
-    combine_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>(*a);
+    launch_combine<__nv_bfloat16>(*a, blocks, stream);
   else
-    combine_kernel<float><<<blocks, 256, 0, stream>>>(*a);
+    launch_combine<float>(*a, blocks, stream);
   return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
 }
 
