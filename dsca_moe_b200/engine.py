@@ -588,8 +588,8 @@ class MoEEngine:
             bytes=total)
 
     def _forward_p2p(self, x, ws):
-        """Main stream: plan -> shared GEMM1 -> [dispatch done] routed GEMM1 -> routed GEMM2 ->
-        shared GEMM2 -> [return done] combine.  Side stream: dispatch (beside the shared GEMM1)
+        """Main stream: shared GEMM1 -> [dispatch done] routed GEMM1 -> routed GEMM2 -> shared
+        GEMM2 -> [return done] combine.  Side stream: plan and dispatch (beside the shared GEMM1)
         and the return kernel (beside the shared GEMM2).  ep_return = "fused" instead stores
         GEMM2's routed rows straight into the source ranks from its epilogue."""
         T = x.shape[0]
@@ -600,12 +600,15 @@ class MoEEngine:
             raise RuntimeError(f"{T} tokens exceed the reserved {ep['T_cap']} per rank (call reserve())")
         lib, ctx, err = L.load(), _ptr(ep["ctx"]), _ptr(self.err)
         main, side = torch.cuda.current_stream(), ep["side"]
-        L.check(lib.dsca_ep_plan(ctx, _ptr(ws["counts"]), self.wait_limit_ns, err, _stream()), "dsca_ep_plan")
-        self._mark("plan")
-        planned = torch.cuda.Event()
-        planned.record(main)
-        side.wait_event(planned)
+        # the plan (counts exchange + harmony) and the dispatch run on the side stream, beside the
+        # shared-expert GEMM1, which needs neither
+        routed = torch.cuda.Event()
+        routed.record(main)
+        side.wait_event(routed)
         with torch.cuda.stream(side):
+            t0 = self._side_mark()
+            L.check(lib.dsca_ep_plan(ctx, _ptr(ws["counts"]), self.wait_limit_ns, err, _stream()), "dsca_ep_plan")
+            self._side_mark("plan", t0)
             t0 = self._side_mark()
             a = L.EpDispatchArgs()
             a.x, a.T, a.d, a.top_k, a.dtype = _ptr(x), T, self.d, self.top_k, _dt(self.dtype)
