@@ -488,11 +488,29 @@ def main():
     tc_peak = peaks["tc"] if at_max else peaks["tc_sus"]
     tc_kind = ("bf16_tflops (burst; SM clock at max in the timed region)" if at_max
                else "bf16_tflops_sustained") + f", {peaks['src']}"
-    roof = {"bound": "tensor", "kernel": "dsca grouped_gemm_kernel (tcgen05, GEMM1+GEMM2 launches)",
-            "achieved": achieved, "peak": tc_peak, "unit": "TFLOP/s",
-            "frac": achieved / tc_peak, "traffic": traffic, "peak_kind": tc_kind,
-            "algorithmic_flops_per_launch": (f_g1 + f_g2) / 2, "gemm1_ms": t_g1, "gemm2_ms": t_g2,
-            "gemm1_tflops": f_g1 / (t_g1 / 1e3) / 1e12, "gemm2_tflops": f_g2 / (t_g2 / 1e3) / 1e12}
+    # algorithmic bytes of the two GEMM launches: expert weights touched + the activations they
+    # read and write (bf16); the GEMMs are tensor-bound when FLOPs / tensor peak is the longer
+    # time (Qwen block), HBM-bound otherwise (Switch layer at 1 GPU: ~64 rows per expert)
+    glu = w["act"] == "swiglu"
+    gemm_bytes = (2.0 * e_touched * (3 if glu else 2) * w["d"] * w["inter"]
+                  + (2.0 * 3 * w["d"] * w["shared"] if w["shared"] else 0.0)
+                  + 2.0 * rows * (w["d"] + w["inter"]) * 2            # routed: rows in + h out + h in + y out
+                  + (2.0 * T * (w["d"] + w["shared"]) * 2 if w["shared"] else 0.0))
+    t_tc = (f_g1 + f_g2) / (tc_peak * 1e12)
+    t_hbm = gemm_bytes / (peaks["hbm"] * 1e9)
+    t_gemm = (t_g1 + t_g2) / 1e3
+    if t_tc >= t_hbm:
+        roof = {"bound": "tensor", "achieved": achieved, "peak": tc_peak, "unit": "TFLOP/s",
+                "frac": achieved / tc_peak, "peak_kind": tc_kind}
+    else:
+        ach_bw = gemm_bytes / t_gemm / 1e9
+        roof = {"bound": "hbm", "achieved": ach_bw, "peak": peaks["hbm"], "unit": "GB/s",
+                "frac": ach_bw / peaks["hbm"], "peak_kind": f"hbm_gbs, {peaks['src']}",
+                "tensor_tflops": achieved}
+    roof.update({"kernel": "dsca grouped GEMM (tcgen05, GEMM1+GEMM2 launches)", "traffic": traffic,
+                 "algorithmic_flops_per_launch": (f_g1 + f_g2) / 2, "algorithmic_bytes_per_launch": gemm_bytes / 2,
+                 "gemm1_ms": t_g1, "gemm2_ms": t_g2,
+                 "gemm1_tflops": f_g1 / (t_g1 / 1e3) / 1e12, "gemm2_tflops": f_g2 / (t_g2 / 1e3) / 1e12})
     total_flops = f_router + f_g1 + f_g2
     t_roof = max(total_flops / (tc_peak * 1e12), hbm / (peaks["hbm"] * 1e9))
     layer_roof = {"flops": total_flops, "hbm_bytes": hbm, "t_roof_ms": t_roof * 1e3,
