@@ -11,6 +11,10 @@ router biased so top-1 expert loads follow Zipf s = 1.5.  Experts are placed con
 (60 on 8 GPUs = 4 x 8 + 4 x 7) and the harmony plan (eq_tokens 150) rebalances hot experts.
 `--workload switch`: one Switch-base-64 MoE layer (d 768, 64 ReLU experts of 3072, top-1,
 Zipf s = 1.0 router).
+`--workload switch-model | qwen-model` (one GPU): the whole random-init transformers model
+(Switch-base-64, 12 + 12 layers; Qwen1.5-MoE-A2.7B, 24 layers) on 16 x 256 random token ids,
+its MoE blocks swapped by replace_qosmoe_layer, timed against the same model with
+transformers' own MoE blocks.
 
 Timing: W untimed warm-up steps; then K steps, each bracketed by CUDA events on the launching
 stream, with a 256 MiB L2 flush (untimed) before each; barrier + synchronize before and after;
@@ -39,6 +43,19 @@ WORKLOADS = {
     "switch": dict(name="switch-base-64 MoE layer forward", d=768, E=64, inter=3072, shared=0, k=1,
                    act="relu", zipf=1.0, T=4096),
 }
+# whole models through the plugin (one GPU): the transformers model with every MoE block swapped
+# by replace_qosmoe_layer, against the same model with transformers' own MoE blocks
+MODELS = {
+    "switch-model": dict(name="switch-base-64 full forward (12 enc + 12 dec layers, 12 MoE layers)",
+                         hf="switch", d=768, E=64, batch=16, seq=256,
+                         plugin=dict(moe_parent_type="SwitchTransformersLayerFF",
+                                     moe_type="SwitchTransformersSparseMLP", name_experts="experts",
+                                     router_tensor_path="router.classifier")),
+    "qwen-model": dict(name="qwen1.5-moe-a2.7b prefill forward (24 layers)", hf="qwen", d=2048, E=60,
+                       batch=16, seq=256,
+                       plugin=dict(moe_parent_type="Qwen2MoeDecoderLayer", moe_type="Qwen2MoeSparseMoeBlock",
+                                   name_experts="experts", router_tensor_path="gate")),
+}
 FLUSH_BYTES = 256 << 20
 
 
@@ -48,7 +65,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=list(WORKLOADS), default="qwen")
+    ap.add_argument("--workload", choices=list(WORKLOADS) + list(MODELS), default="qwen")
     ap.add_argument("--tokens", type=int, default=None, help="tokens per GPU (default 4096 = 16 x 256)")
     ap.add_argument("--eq-tokens", type=int, default=150)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -318,8 +335,134 @@ def run_reference(args, w, T):
     print(json.dumps(line), flush=True)
 
 
+def build_hf_model(kind: str, dev):
+    """Random-init bf16 transformers model with the named architecture, built on the device."""
+    import torch
+
+    if kind == "switch":
+        from transformers import SwitchTransformersConfig as C, SwitchTransformersForConditionalGeneration as M
+
+        cfg = C(vocab_size=32128, d_model=768, d_kv=64, d_ff=3072, num_layers=12, num_decoder_layers=12,
+                num_heads=12, num_experts=64, encoder_sparse_step=2, decoder_sparse_step=2,
+                router_jitter_noise=0.0, dropout_rate=0.0)
+    else:
+        from transformers import Qwen2MoeConfig as C, Qwen2MoeForCausalLM as M
+
+        cfg = C(vocab_size=151936, hidden_size=2048, intermediate_size=5632, moe_intermediate_size=1408,
+                shared_expert_intermediate_size=5632, num_hidden_layers=24, num_attention_heads=16,
+                num_key_value_heads=16, num_experts=60, num_experts_per_tok=4, norm_topk_prob=False,
+                decoder_sparse_step=1, mlp_only_layers=[], max_position_embeddings=8192, rope_theta=1e6)
+    torch.manual_seed(0)
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        with torch.device(dev):
+            model = M(cfg)
+    finally:
+        torch.set_default_dtype(prev)
+    return model.eval()
+
+
+def run_model(args):
+    """Whole-model forward tokens/s on one GPU: transformers' own MoE blocks vs the swapped block."""
+    import torch
+
+    from dsca_moe_b200 import QoSMoEConfig, RequestStateTable, get_qosmoe_layers, replace_qosmoe_layer
+
+    m = MODELS[args.workload]
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps({"workload": m["name"], "unavailable": "whole-model runs use one GPU"}), flush=True)
+        return
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    model = build_hf_model(m["hf"], dev)
+    B, S = m["batch"], m["seq"]
+    T = B * S
+    gen = torch.Generator().manual_seed(1)
+    ids = torch.randint(0, model.config.vocab_size, (B, S), generator=gen).to(dev)
+    if m["hf"] == "switch":  # decoder ids = encoder ids (src/flexible_dataset.py:157-166)
+        fwd = lambda: model(input_ids=ids, decoder_input_ids=ids, use_cache=False).logits  # noqa: E731
+    else:
+        fwd = lambda: model(input_ids=ids, use_cache=False).logits  # noqa: E731
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+
+    def timed(steps, warmup):
+        with torch.no_grad():
+            for _ in range(warmup):
+                fwd()
+            torch.cuda.synchronize()
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+            for a, b in evs:
+                flush.zero_()
+                a.record()
+                fwd()
+                b.record()
+            torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in evs) / steps
+
+    ref_steps = max(1, min(args.steps, 5))
+    ref_ms = timed(ref_steps, min(args.warmup, 2))
+    with torch.no_grad():
+        ref_logits = fwd().float()
+    qcfg = QoSMoEConfig(rank=0, world_size=1, expert_cache_size=m["E"])
+    replace_qosmoe_layer(model, config=qcfg, **m["plugin"])
+    layers = get_qosmoe_layers(model)
+    ctx = RequestStateTable(qcfg).build_context({"attention_mask": torch.ones(B, S, dtype=torch.long)})
+    for layer in layers:
+        layer.set_runtime_context(ctx)
+    torch.cuda.empty_cache()
+    uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    try:
+        clocks = NvmlClockSampler(uuid)
+    except Exception:  # noqa: BLE001 - NVML missing: fall back to nvidia-smi
+        clocks = ClockSampler(uuid)
+    clocks.start()
+    ms = timed(args.steps, args.warmup)
+    clk = clocks.stop()
+    with torch.no_grad():
+        got = fwd().float()
+    for layer in layers:
+        layer.engine.check()
+    drift = float((got - ref_logits).norm() / ref_logits.norm())
+    # time spent inside the swapped blocks: events around each block in one more forward
+    marks = []
+
+    def mark(*_):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        marks.append(ev)
+
+    hooks = [h for layer in layers for h in (layer.register_forward_pre_hook(mark), layer.register_forward_hook(mark))]
+    with torch.no_grad():
+        flush.zero_()
+        fwd()
+    torch.cuda.synchronize()
+    for h in hooks:
+        h.remove()
+    moe_ms = sum(marks[i].elapsed_time(marks[i + 1]) for i in range(0, len(marks), 2))
+    line = {
+        "metric": "model forward tokens/sec", "value": T / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": m["name"], "batch_x_seq": f"{B}x{S}", "weights": "random init (transformers init)",
+                   "moe_layers_swapped": len(layers), "l2": "flushed (256 MiB write, untimed) before every timed step"},
+        "moe_blocks_ms_per_step": moe_ms, "rest_of_model_ms_per_step": ms - moe_ms,
+        "transformers_moe_blocks": {"value": T / (ref_ms / 1e3), "ms_per_step": ref_ms, "steps": ref_steps},
+        "logits_drift_vs_transformers": drift, "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
+    if args.workload in MODELS:
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "whole-model workloads time the transformers "
+                              "MoE blocks inside the ours arm (transformers_moe_blocks)"}), flush=True)
+            return
+        run_model(args)
+        return
     w = dict(WORKLOADS[args.workload])
     T = args.tokens or w["T"]
     if args.impl == "reference":

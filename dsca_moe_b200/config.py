@@ -64,3 +64,7 @@ class QoSMoEConfig:
     shared_expert_gate: object = None  # Linear(d, 1) or None
     process_group: object = None   # torch.distributed group for world_size > 1
     collect_stats: bool = False    # per-forward latency / token statistics (host syncs)
+    # forward returns (h, (router_logits, expert_index)) — the reference contract, which
+    # transformers-4.x SwitchTransformersLayerFF unpacks — or h alone (transformers-5.x callers);
+    # replace_qosmoe_layer sets it from the installed transformers
+    return_router_tuple: bool = True

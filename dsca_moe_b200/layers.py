@@ -11,6 +11,7 @@ ShardedQwenMoE   — constructor and forward contract of qwen_ep_adapter/qwen_ep
 """
 from __future__ import annotations
 
+import dataclasses
 import json
 
 import numpy as np
@@ -19,6 +20,19 @@ import torch.nn as nn
 
 from . import _lib as L
 from .engine import MoEEngine, default_expert_to_gpu, pack_relu, pack_swiglu
+
+
+def hf_callers_unpack_tuples() -> bool:
+    """Whether the installed transformers' decoder layers accept a tuple from their MoE child.
+    transformers 4.x (the reference's pins, 4.39 / 4.45) unpacks `(h, router_tuple)` in
+    SwitchTransformersLayerFF and `(h, router_logits)` in Qwen2MoeDecoderLayer; from 5.0 the
+    callers add the child's output to the residual directly, so a swapped block must return
+    the tensor alone.  No transformers installed: True (the reference contract)."""
+    try:
+        import transformers
+    except ImportError:
+        return True
+    return int(transformers.__version__.split(".")[0]) < 5
 
 
 def _sd(expert) -> dict:
@@ -103,6 +117,10 @@ class QoSMoELayer(nn.Module):
                                 shared_gate_weight=sg_w, rank=config.rank, world=config.world_size,
                                 group=getattr(config, "process_group", None), expert_to_gpu=e2g,
                                 eq_tokens=config.eq_tokens)
+        # the experts now live packed in the engine: drop this layer's references to the caller's
+        # expert modules / state dicts so that a swapped model does not hold both copies
+        if dataclasses.is_dataclass(config):
+            self.config = dataclasses.replace(config, experts=None, expert_example=None)
         self.tot_num_toks_send, self.tot_num_toks_recv = [], []
         self.latencies, self.expert_freqs, self.num_prefetch_launched = [], [], []
 
@@ -133,6 +151,7 @@ class QoSMoELayer(nn.Module):
         r = self.engine.forward(hidden_states.reshape(-1, self.d_model))
         out = r["out"].view(shape)
         self.runtime_context.last_hidden_states = r["out"]
+        tuple_out = getattr(self.config, "return_router_tuple", True)
         if stats:
             ev1.record()
             ev1.synchronize()
@@ -142,6 +161,8 @@ class QoSMoELayer(nn.Module):
             T = r["out"].shape[0] * self.engine.top_k
             self.tot_num_toks_send.append(int(lay.send_splits.sum()) if lay is not None else T)
             self.tot_num_toks_recv.append(int(lay.recv_splits.sum()) if lay is not None else T)
+        if not tuple_out:
+            return out
         return out, (r["logits"], r["expert_index"])
 
 
@@ -150,13 +171,19 @@ class ShardedQwenMoE(nn.Module):
     process group (or `group`).  Accepts a transformers-4.x block (experts ModuleList of
     Qwen2MoeMLP, gate Linear) or a transformers-5.x block (fused experts, Qwen2MoeTopKRouter).
     Placement: contiguous blocks (E % world need not be 0) or `expert_to_gpu`; `eq_tokens` >= 0
-    turns on harmony rebalancing (the reference block uses fixed ownership: eq_tokens = -1)."""
+    turns on harmony rebalancing (the reference block uses fixed ownership: eq_tokens = -1).
+    forward returns `(h, router_logits)` (the reference contract) or, with
+    `return_logits=False`, `h` alone for transformers-5.x decoder layers."""
 
-    def __init__(self, old, rank, world, policy="fifo", group=None, expert_to_gpu=None, eq_tokens=-1):
+    def __init__(self, old, rank, world, policy="fifo", group=None, expert_to_gpu=None, eq_tokens=-1,
+                 return_logits=True):
         super().__init__()
         self.rank, self.world, self.policy = rank, world, policy
-        self.num_experts, self.top_k = int(old.num_experts), int(old.top_k)
-        self.norm_topk_prob = bool(old.norm_topk_prob)
+        # transformers 4.x keeps num_experts / top_k / norm_topk_prob on the block, 5.x on its router
+        src = old if hasattr(old, "top_k") else old.gate
+        self.num_experts, self.top_k = int(src.num_experts), int(src.top_k)
+        self.norm_topk_prob = bool(src.norm_topk_prob)
+        self.return_logits = bool(return_logits)
         dev = torch.device("cuda", torch.cuda.current_device())
         experts = old.experts
         spec = experts_from_fused(experts) if hasattr(experts, "gate_up_proj") else experts_from_list(list(experts))
@@ -176,15 +203,19 @@ class ShardedQwenMoE(nn.Module):
         b, s, d = hidden_states.shape
         r = self.engine.forward(hidden_states.reshape(-1, d))
         self.route_calls += 1
+        if not self.return_logits:
+            return r["out"].view(b, s, d)
         return r["out"].view(b, s, d), r["logits"]
 
 
 def patch(model, rank, world, policy="fifo"):
-    """qwen_ep_adapter/qwen_ep.py:100-109: swap every Qwen2MoeSparseMoeBlock of model.model.layers."""
+    """qwen_ep_adapter/qwen_ep.py:100-109: swap every Qwen2MoeSparseMoeBlock of model.model.layers.
+    The swapped blocks return what the installed transformers' Qwen2MoeDecoderLayer expects."""
     changed = 0
+    tuple_out = hf_callers_unpack_tuples()
     for layer in model.model.layers:
         if layer.mlp.__class__.__name__ == "Qwen2MoeSparseMoeBlock":
-            layer.mlp = ShardedQwenMoE(layer.mlp, rank, world, policy)
+            layer.mlp = ShardedQwenMoE(layer.mlp, rank, world, policy, return_logits=tuple_out)
             changed += 1
     if not changed:
         raise RuntimeError("No Qwen2MoeSparseMoeBlock found: wrong checkpoint/model version")

@@ -9,7 +9,10 @@ experts) and router weight (`router_tensor_path` + ".weight").  layer_idx counts
 in traversal order.  Qwen blocks also carry shared_expert / shared_expert_gate / top_k /
 norm_topk_prob, which are picked up so the swapped block keeps top-k routing and the shared
 expert (the reference's QoSMoELayer drops both).  `placement` overrides
-config.expert_placement (exflow JSON path or [layer][gpu] -> experts list).
+config.expert_placement (exflow JSON path or [layer][gpu] -> experts list).  d_model and
+num_experts are taken from the router weight's shape; the swapped layers return the
+`(h, (logits, idx))` tuple when the installed transformers' callers unpack it (4.x) and `h`
+alone otherwise (5.x).
 """
 from __future__ import annotations
 
@@ -17,7 +20,7 @@ import dataclasses
 
 import torch.nn as nn
 
-from .layers import QoSMoELayer
+from .layers import QoSMoELayer, hf_callers_unpack_tuples
 
 
 def get_tensor_by_path(module, path):
@@ -29,10 +32,11 @@ def get_tensor_by_path(module, path):
 
 def replace_qosmoe_layer(model, moe_parent_type, moe_type, name_experts, router_tensor_path, config,
                          placement=None):
-    _replace(model, moe_parent_type, moe_type, [0], name_experts, router_tensor_path, config, placement)
+    _replace(model, moe_parent_type, moe_type, [0], name_experts, router_tensor_path, config, placement,
+             hf_callers_unpack_tuples())
 
 
-def _replace(model, parent_t, moe_t, layer_idx, name_experts, router_path, config, placement):
+def _replace(model, parent_t, moe_t, layer_idx, name_experts, router_path, config, placement, tuple_out):
     if type(model).__name__ == parent_t:
         for child_name, child in model.named_children():
             if type(child).__name__ != moe_t:
@@ -47,6 +51,8 @@ def _replace(model, parent_t, moe_t, layer_idx, name_experts, router_path, confi
             cfg.experts = experts
             cfg.expert_example = experts[0] if isinstance(experts, list) else experts
             cfg.router_weights = get_tensor_by_path(child, router_path).weight
+            cfg.num_experts, cfg.d_model = (int(v) for v in cfg.router_weights.shape)
+            cfg.return_router_tuple = tuple_out
             if placement is not None:
                 cfg.expert_placement = placement
             if getattr(child, "shared_expert", None) is not None and cfg.shared_expert is None:
@@ -63,7 +69,7 @@ def _replace(model, parent_t, moe_t, layer_idx, name_experts, router_path, confi
             setattr(model, child_name, new_layer)
     else:
         for child in model.children():
-            _replace(child, parent_t, moe_t, layer_idx, name_experts, router_path, config, placement)
+            _replace(child, parent_t, moe_t, layer_idx, name_experts, router_path, config, placement, tuple_out)
 
 
 def get_qosmoe_layers(model):
