@@ -342,9 +342,11 @@ def build_hf_model(kind: str, dev):
     if kind == "switch":
         from transformers import SwitchTransformersConfig as C, SwitchTransformersForConditionalGeneration as M
 
+        # router_dtype bf16: transformers then routes in the router weight's dtype, as the
+        # reference's Router does (src/harmonymoe/router.py:37-45), so the two model runs route alike
         cfg = C(vocab_size=32128, d_model=768, d_kv=64, d_ff=3072, num_layers=12, num_decoder_layers=12,
                 num_heads=12, num_experts=64, encoder_sparse_step=2, decoder_sparse_step=2,
-                router_jitter_noise=0.0, dropout_rate=0.0)
+                router_jitter_noise=0.0, dropout_rate=0.0, router_dtype="bfloat16")
     else:
         from transformers import Qwen2MoeConfig as C, Qwen2MoeForCausalLM as M
 
