@@ -78,6 +78,9 @@ def parse():
     ap.add_argument("--tile-rows", type=int, choices=[0, 128, 256], default=0,
                     help="bf16 expert GEMM tiles: 0 = default per GEMM, 256 = CTA pairs (cta_group::2, "
                          "weights as M), 128 = one CTA per 128-token tile")
+    ap.add_argument("--expert-cache", type=int, default=0,
+                    help="one GPU: keep only this many routed experts on the device (the reference's "
+                         "expert_cache_size); the rest stream in from pinned host memory per the QoS plan")
     ap.add_argument("--fp8", action="store_true",
                     help="fp8-e4m3 expert weights with per-output-channel scales (bf16 activations)")
     ap.add_argument("--router", choices=["zipf", "uniform"], default="zipf",
@@ -104,6 +107,12 @@ def flops_and_bytes(w, T, rows_routed, E_touched):
 
 def launches_per_step(world, exchange, eng):
     """This library's kernel launches in one forward (the timed step)."""
+    if eng.cache is not None:
+        # router, permute, shared GEMM1 + GEMM2, QoS scores (2), GEMM1 + GEMM2 per planned
+        # expert, combine
+        plan = eng.last_exec_plan
+        n = len(plan.expert_order) if plan is not None else eng.E
+        return 2 + (2 if eng.experts.ws1 is not None else 0) + 2 + 2 * n + 1 + (0 if eng.fuse_scan else 1)
     if world == 1:
         # router (+ fused scan), permute, GEMM1, GEMM2, combine
         return 5 + (0 if eng.fuse_scan else 1)
@@ -220,7 +229,7 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows), "power_w_max": max(pw) if pw else None}
 
 
-def build_block(w, T, rank, world, dev, eq_tokens, group=None, fp8=False):
+def build_block(w, T, rank, world, dev, eq_tokens, group=None, fp8=False, cache_slots=None):
     import torch
 
     from dsca_moe_b200 import _lib as L
@@ -247,14 +256,14 @@ def build_block(w, T, rank, world, dev, eq_tokens, group=None, fp8=False):
         eng = MoEEngine(torch.from_numpy(Wr).to(dev, torch.bfloat16), pe, top_k=w["k"],
                         route_mode=L.ROUTE_SOFTMAX_TOPK,
                         shared_gate_weight=torch.from_numpy(sgw).to(dev, torch.bfloat16),
-                        rank=rank, world=world, group=group, eq_tokens=eq_tokens)
+                        rank=rank, world=world, group=group, eq_tokens=eq_tokens, cache_slots=cache_slots)
     else:
         raw = dict(wi=n(E, I, d), wo=n(E, d, I))
         pe = pack_relu(raw["wi"], raw["wo"], device=dev)
         if fp8:
             pe = quantize_fp8(pe)
         eng = MoEEngine(torch.from_numpy(Wr).to(dev, torch.bfloat16), pe, top_k=1, route_mode=L.ROUTE_SWITCH_TOP1,
-                        rank=rank, world=world, group=group, eq_tokens=eq_tokens)
+                        rank=rank, world=world, group=group, eq_tokens=eq_tokens, cache_slots=cache_slots)
     x = torch.from_numpy(syn.hidden_states(T, d, 5000 + rank, "bf16")).to(dev, torch.bfloat16)
     return eng, x, Wr, raw, info
 
@@ -487,7 +496,10 @@ def main():
         group = dist.group.WORLD
     if args.router == "uniform":
         w["zipf"] = None
-    eng, x, Wr, raw, info = build_block(w, T, rank, world, dev, args.eq_tokens, group, fp8=args.fp8)
+    if args.expert_cache and world > 1:
+        raise SystemExit("--expert-cache runs on one GPU")
+    eng, x, Wr, raw, info = build_block(w, T, rank, world, dev, args.eq_tokens, group, fp8=args.fp8,
+                                        cache_slots=args.expert_cache or None)
     eng.exchange = args.exchange
     eng.ep_return = args.ep_return
     eng.tile_rows = args.tile_rows
@@ -526,6 +538,8 @@ def main():
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     barrier()
     torch.cuda._sleep(20_000_000)  # let the host queue ahead of the first timed step
+    loads0 = eng.cache.loads if eng.cache is not None else 0
+    bytes0 = eng.cache.bytes_loaded if eng.cache is not None else 0
     for i in range(args.steps):
         flush.zero_()
         evs[i][0].record()
@@ -533,6 +547,10 @@ def main():
         evs[i][1].record()
     barrier()
     step_ms = [a.elapsed_time(b) for a, b in evs]
+    cache_info = None
+    if eng.cache is not None:
+        cache_info = {"slots": eng.cache.slots, "loads_per_step": (eng.cache.loads - loads0) / args.steps,
+                      "h2d_bytes_per_step": (eng.cache.bytes_loaded - bytes0) / args.steps}
     tot = torch.tensor([sum(step_ms)], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(tot, op=dist.ReduceOp.MAX)
@@ -590,21 +608,26 @@ def main():
         dist.all_reduce(e_tot, op=dist.ReduceOp.MAX)
     e2e_serial = T * world / (float(e_tot.item()) / args.steps / 1e3)
 
-    from dsca_moe_b200.engine import HostPipeline
-    pipe = HostPipeline(eng, T)
-    xs = [x_host] * args.steps
-    outs = [outs_host[i & 1] for i in range(args.steps)]
-    pipe.run([x_host] * 2, outs_host)  # warm-up
-    barrier()
-    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    p0.record()
-    pipe.run(xs, outs)
-    p1.record()
-    barrier()
-    p_tot = torch.tensor([p0.elapsed_time(p1)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(p_tot, op=dist.ReduceOp.MAX)
-    e2e_value = T * world / (float(p_tot.item()) / args.steps / 1e3)
+    e2e_mode = "pipelined (HostPipeline: step i+1 H2D and step i-1 D2H overlap step i)"
+    if eng.cache is None:
+        from dsca_moe_b200.engine import HostPipeline
+        pipe = HostPipeline(eng, T)
+        xs = [x_host] * args.steps
+        outs = [outs_host[i & 1] for i in range(args.steps)]
+        pipe.run([x_host] * 2, outs_host)  # warm-up
+        barrier()
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p0.record()
+        pipe.run(xs, outs)
+        p1.record()
+        barrier()
+        p_tot = torch.tensor([p0.elapsed_time(p1)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(p_tot, op=dist.ReduceOp.MAX)
+        e2e_value = T * world / (float(p_tot.item()) / args.steps / 1e3)
+    else:
+        # the cache path reads the plan on the host every step: no pipelining across steps
+        e2e_value, e2e_mode = e2e_serial, "serial (expert-cache path: host plan per step)"
 
     # ---- roofline of the dominant kernel (grouped GEMM: GEMM1 + GEMM2 launches)
     if world == 1:
@@ -661,6 +684,25 @@ def main():
     layer_roof = {"flops": total_flops, "hbm_bytes": hbm, "t_roof_ms": t_roof * 1e3,
                   "frac": t_roof * 1e3 / ms_per_step,
                   "peaks": f"tensor {tc_peak} TFLOP/s ({tc_kind}), HBM {peaks['hbm']} GB/s ({peaks['src']})"}
+    if cache_info is not None:
+        # expert-cache path: bound by the expert weights crossing PCIe; the denominator is a
+        # pinned host -> device copy of 512 MiB measured here
+        src = torch.empty(256 << 20, dtype=torch.bfloat16).pin_memory()
+        dst = torch.empty_like(src, device=dev)
+        h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dst.copy_(src, non_blocking=True)
+        h0.record()
+        for _ in range(3):
+            dst.copy_(src, non_blocking=True)
+        h1.record()
+        torch.cuda.synchronize()
+        h2d_peak = 3 * src.numel() * 2 / (h0.elapsed_time(h1) / 1e3) / 1e9
+        ach = cache_info["h2d_bytes_per_step"] / (ms_per_step / 1e3) / 1e9
+        roof = {"bound": "pcie", "achieved": ach, "peak": h2d_peak, "unit": "GB/s", "frac": ach / h2d_peak,
+                "peak_kind": "pinned host -> device copy of 512 MiB, measured in this run",
+                "kernel": "expert weight loads (copy engine) of the expert-cache path", "traffic": None}
+        layer_roof["frac_pcie"] = cache_info["h2d_bytes_per_step"] / (h2d_peak * 1e9) * 1e3 / ms_per_step
+        del src, dst
 
     # ---- CPU baseline (rank 0, one GPU only)
     cpu = None
@@ -689,10 +731,9 @@ def main():
                                       256: "CTA-pair swap-AB tiles (256 channels x <=256 tokens)"}[args.tile_rows]},
             "roofline": roof, "layer_roofline": layer_roof, "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * w["d"] * 2,
-                    "d2h_bytes_per_step": T * w["d"] * 2,
-                    "mode": "pipelined (HostPipeline: step i+1 H2D and step i-1 D2H overlap step i)",
-                    "serial_value": e2e_serial},
+                    "d2h_bytes_per_step": T * w["d"] * 2, "mode": e2e_mode, "serial_value": e2e_serial},
             "gpu_launches": launches_per_step(world, args.exchange, eng) * args.steps, "clocks": clk,
+            "expert_cache": cache_info,
             "phases_ms": phase_ms,
         }
         print(json.dumps(line), flush=True)

@@ -4,6 +4,7 @@ Public surface (mirrors the reference's plugin):
   QoSMoEConfig, QoSMoELayer, replace_qosmoe_layer, get_qosmoe_layers, RequestStateTable
   ShardedQwenMoE, patch                          (qwen_ep_adapter drop-in)
   MoEEngine, pack_swiglu, pack_relu, plan_harmony, plan_layout   (engine level)
+  build_exec_plan, QoSInputs, ExpertCache        (expert cache / QoS planner path)
 The compute runs in libdsca_b200.so (include/dsca_b200.h); build it with
 ``python -m dsca_moe_b200.build``.
 """
@@ -23,4 +24,7 @@ def __getattr__(name):
                 "default_expert_to_gpu", "exchange_chunks"):
         from . import engine
         return getattr(engine, name)
+    if name in ("QoSExecPlan", "QoSInputs", "ExpertCache", "build_exec_plan"):
+        from . import qos
+        return getattr(qos, name)
     raise AttributeError(name)

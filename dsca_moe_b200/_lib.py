@@ -77,6 +77,14 @@ class CombineArgs(ctypes.Structure):
                 ("err", _vp)]
 
 
+class QosArgs(ctypes.Structure):
+    _fields_ = [("x", _vp), ("x_prev", _vp), ("logits", _vp), ("dtype", _i), ("topk_ids", _vp),
+                ("seq_priority", _vp), ("remaining", _vp), ("valid", _vp), ("T", _i), ("d", _i), ("E", _i),
+                ("top_k", _i), ("attention_mode", _i), ("alpha", ctypes.c_float), ("beta", ctypes.c_float),
+                ("delta", ctypes.c_float), ("target_batch", ctypes.c_float), ("epsilon", ctypes.c_float),
+                ("token_score", _vp), ("expert_priority", _vp), ("err", _vp)]
+
+
 # every symbol include/dsca_b200.h declares
 EXPORTED = ["dsca_version", "dsca_status_string", "dsca_device_info", "dsca_router_topk",
             "dsca_dispatch_scan", "dsca_permute", "dsca_grouped_ffn", "dsca_combine",
@@ -84,7 +92,7 @@ EXPORTED = ["dsca_version", "dsca_status_string", "dsca_device_info", "dsca_rout
             "dsca_grouped_ffn_static_scratch", "dsca_ep_ctx_bytes", "dsca_ep_init", "dsca_ep_group_offsets",
             "dsca_ep_plan", "dsca_ep_dispatch", "dsca_ep_wait", "dsca_ep_plan_eval", "dsca_ipc_export",
             "dsca_ipc_import", "dsca_ipc_close", "dsca_ep_read_plan", "dsca_ep_region_alloc",
-            "dsca_ep_region_free", "dsca_ep_return"]
+            "dsca_ep_region_free", "dsca_ep_return", "dsca_qos_priority"]
 STATIC_SCRATCH_BYTES = 16 << 20
 
 _LIB = None

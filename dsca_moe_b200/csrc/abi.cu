@@ -10,6 +10,7 @@ int launch_exp_eval(const float* x, float* y, int n, cudaStream_t stream);
 int launch_scan(const dsca_scan_args* a, cudaStream_t stream);
 int launch_permute(const dsca_permute_args* a, cudaStream_t stream);
 int launch_combine(const dsca_combine_args* a, cudaStream_t stream);
+int launch_qos(const dsca_qos_args* a, cudaStream_t stream);
 int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t stream);
 int launch_grouped_ffn_f32(const dsca_ffn_args* f, int num_sms, cudaStream_t stream);
 int launch_grouped_ffn_fp8(const dsca_ffn_args* f, int num_sms, cudaStream_t stream);
@@ -177,6 +178,17 @@ int dsca_combine(const dsca_combine_args* a, dsca_stream_t stream) {
     return DSCA_ERR_BAD_ARG;
   if ((a->ys == nullptr) != (a->shared_gate == nullptr)) return DSCA_ERR_BAD_ARG;
   return dsca::launch_combine(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int dsca_qos_priority(const dsca_qos_args* a, dsca_stream_t stream) {
+  if (a == nullptr || a->x == nullptr || a->logits == nullptr || a->topk_ids == nullptr ||
+      a->token_score == nullptr || a->expert_priority == nullptr || a->T < 0 || a->d <= 0 || a->E <= 0 ||
+      a->top_k <= 0 || a->top_k > DSCA_MAX_TOPK || a->top_k > a->E)
+    return DSCA_ERR_BAD_ARG;
+  if (a->dtype != DSCA_BF16 && a->dtype != DSCA_F32) return DSCA_ERR_BAD_ARG;
+  if (a->attention_mode != 0 && a->attention_mode != 1) return DSCA_ERR_BAD_ARG;
+  if (a->E > 4 * DSCA_MAX_EXPERTS) return DSCA_ERR_CAPACITY;
+  return dsca::launch_qos(a, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int dsca_check_error(int32_t* err_dev, dsca_stream_t stream) {

@@ -16,12 +16,13 @@ on the critical path.
 from __future__ import annotations
 
 import ctypes
-from dataclasses import dataclass
+from dataclasses import dataclass, replace
 
 import numpy as np
 import torch
 
 from . import _lib as L
+from .qos import ExpertCache, QoSInputs, build_exec_plan, match_token_length
 
 __all__ = ["PackedExperts", "pack_swiglu", "pack_relu", "MoEEngine", "plan_harmony", "plan_layout"]
 
@@ -296,22 +297,38 @@ class MoEEngine:
     def __init__(self, router_weight: torch.Tensor, experts: PackedExperts, top_k: int, route_mode: int,
                  norm_topk: bool = False, shared_gate_weight: torch.Tensor | None = None,
                  rank: int = 0, world: int = 1, group=None, expert_to_gpu=None, eq_tokens: int = 150,
-                 num_ctas: int = 0, exchange: str = "p2p", wait_limit_ns: int = 2_000_000_000):
+                 num_ctas: int = 0, exchange: str = "p2p", wait_limit_ns: int = 2_000_000_000,
+                 cache_slots: int | None = None, device=None, initial_cache=None):
         lib = L.load()
         n_sms, is_sm100 = ctypes.c_int(0), ctypes.c_int(0)
         L.check(lib.dsca_device_info(ctypes.byref(n_sms), ctypes.byref(is_sm100)), "dsca_device_info")
         if experts.dtype == torch.bfloat16 and not is_sm100.value:
             raise RuntimeError("the bf16 expert path needs an sm_100 (B200) GPU")
         self.num_sms = n_sms.value
-        self.experts = experts
+        n_experts = experts.E
         self.dtype = experts.dtype  # activation dtype (bf16 for fp8 weights)
         self.op_dtype = torch.float16 if experts.fp8 else self.dtype  # FFN operand dtype
         if experts.fp8 and world > 1:
             raise NotImplementedError("fp8 expert weights run on one GPU in this build")
-        self.device = experts.w1.device
+        self.device = torch.device(device) if device is not None else experts.w1.device
+        # expert cache (the reference's expert_cache_size < num_experts): the routed weights stay
+        # in pinned host memory and `cache_slots` device slots hold the ones being computed
+        self.cache = None
+        if cache_slots is not None:
+            if world != 1 or experts.fp8:
+                raise NotImplementedError("the expert cache runs on one GPU with bf16 / f32 weights")
+            self.cache = ExpertCache.create(experts.w1, experts.w2, int(cache_slots), self.device, initial_cache)
+            experts = replace(experts, w1=self.cache.w1, w2=self.cache.w2, E=int(cache_slots),
+                              ws1=None if experts.ws1 is None else experts.ws1.to(self.device),
+                              ws2=None if experts.ws2 is None else experts.ws2.to(self.device))
+        # QoS planner constants (src/qosmoe/config.py:30-43), used by the expert-cache path
+        self.qos_params = dict(alpha=1.0, beta=0.1, delta=0.5, target_batch=64.0, epsilon=1e-6, attention_mode=0)
+        self.last_exec_plan = None
+        self.last_loads = 0
+        self.experts = experts
         self.router_weight = router_weight.to(device=self.device, dtype=self.dtype).contiguous()
         self.E, self.d = self.router_weight.shape
-        if self.E != experts.E or self.d != experts.d:
+        if self.E != n_experts or self.d != experts.d:
             raise ValueError("router and experts disagree on E / d")
         self.route_mode = route_mode
         self.top_k = 1 if route_mode == L.ROUTE_SWITCH_TOP1 else int(top_k)
@@ -391,6 +408,8 @@ class MoEEngine:
             offsets=torch.empty(E + 1, dtype=torch.int32, device=dev),
             block_base=torch.empty(max(nb, 1), E, dtype=torch.int32, device=dev),
             token_row=torch.empty(T, k, dtype=torch.int32, device=dev),
+            token_score=torch.empty(T, dtype=torch.float32, device=dev) if self.cache is not None else None,
+            expert_priority=torch.empty(E, dtype=torch.float32, device=dev) if self.cache is not None else None,
             # fp8 weights: the FFN operands (rows, shared input, intermediates) are f16
             hs=torch.empty(T, pe.s_ip, dtype=self.op_dtype, device=dev) if pe.ws1 is not None else None,
             ys=torch.empty(T, d, dtype=dt, device=dev) if pe.ws1 is not None else None,
@@ -453,7 +472,7 @@ class MoEEngine:
 
     def _ffn_call(self, x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, phases, ep_ctx=None,
                   segments=3, num_ctas=None):
-        pe = self.experts
+        pe = self.experts  # with an expert cache: w1 / w2 are the device slots
         f = L.FfnArgs()
         f.dtype, f.act, f.d = (L.F8E4M3 if pe.fp8 else _dt(self.dtype)), pe.act, self.d
         f.n1p, f.ip, f.dp = pe.n1p, pe.ip, pe.dp
@@ -482,10 +501,12 @@ class MoEEngine:
         L.call("dsca_combine", ctypes.byref(c), _stream())
 
     # -------------------------------------------------------------- forward
-    def forward(self, x: torch.Tensor) -> dict:
+    def forward(self, x: torch.Tensor, qos: QoSInputs | None = None) -> dict:
         """x [T, d] (activation dtype, on this engine's device).  Returns a dict with the fresh
         results out [T, d], logits [T, E], topk_ids [T, k] and expert_index [T] (int64), plus
-        views of the reused scratch (topk_w, counts, token_row, ...) valid until the next call."""
+        views of the reused scratch (topk_w, counts, token_row, ...) valid until the next call.
+        `qos`: the planner's per-token inputs, read only with an expert cache (they order the
+        experts and choose the slots, never the result)."""
         if x.dim() != 2 or x.shape[1] != self.d:
             raise ValueError(f"expected [T, {self.d}] input, got {tuple(x.shape)}")
         x = x.to(dtype=self.dtype).contiguous()
@@ -502,6 +523,8 @@ class MoEEngine:
         self._mark("start")
         self._route(x, ws)
         self._mark("scan")
+        if self.world == 1 and self.cache is not None:
+            return self._forward_cached(x, ws, qos)
         if self.world == 1 and not self.ep_loopback:
             cap = ws["a"].shape[0]
             self._permute(x, ws, ws["a"], cap)
@@ -511,6 +534,68 @@ class MoEEngine:
             self._mark("combine")
             return ws
         return self._forward_ep(x, ws)
+
+    # -------------------------------------------------------------- expert cache path
+    def _qos(self, x, ws, qos: QoSInputs | None):
+        """dsca_qos_priority: token scores and expert priorities into the workspace."""
+        T = x.shape[0]
+        q = qos or QoSInputs()
+        dev = self.device
+
+        def vec(v):
+            v = match_token_length(v, T)
+            return None if v is None else v.to(device=dev, dtype=torch.float32).contiguous()
+
+        xp = q.x_prev
+        if xp is not None:
+            xp = xp.reshape(-1, xp.shape[-1]) if xp.dim() > 1 else xp
+            xp = xp.to(device=dev, dtype=self.dtype).contiguous() if tuple(xp.shape) == tuple(x.shape) else None
+        seq, rem, val = vec(q.seq_priority), vec(q.remaining), vec(q.valid)
+        a = L.QosArgs()
+        a.x, a.x_prev, a.logits, a.dtype = _ptr(x), _ptr(xp), _ptr(ws["logits"]), _dt(self.dtype)
+        a.topk_ids, a.seq_priority, a.remaining, a.valid = _ptr(ws["topk_ids"]), _ptr(seq), _ptr(rem), _ptr(val)
+        a.T, a.d, a.E, a.top_k = T, self.d, self.E, self.top_k
+        p = self.qos_params
+        a.attention_mode = int(p["attention_mode"])
+        a.alpha, a.beta, a.delta = p["alpha"], p["beta"], p["delta"]
+        a.target_batch, a.epsilon = p["target_batch"], p["epsilon"]
+        a.token_score, a.expert_priority, a.err = _ptr(ws["token_score"]), _ptr(ws["expert_priority"]), _ptr(self.err)
+        L.call("dsca_qos_priority", ctypes.byref(a), _stream())
+        # keep the per-token vectors alive until the kernel has read them
+        ws["_qos_keep"] = (xp, seq, rem, val)
+
+    def _forward_cached(self, x, ws, qos):
+        """One GPU, routed experts in `cache.slots` device slots: the shared expert first, then
+        the QoS plan's experts one grouped-GEMM launch each, every expert copied into its planned
+        slot (load stream) before its GEMM and a slot reused only after its last reader."""
+        cache = self.cache
+        cap = ws["a"].shape[0]
+        self._permute(x, ws, ws["a"], cap)
+        self._mark("permute")
+        if self.experts.ws1 is not None:
+            self._ffn_call(x, ws, ws["a"], ws["h"], ws["y"], cap, 1, ws["offsets"], None, 3, segments=2)
+        self._qos(x, ws, qos)
+        # the plan decides what crosses PCIe: the host reads counts and priorities (as the
+        # reference does with .item() per expert)
+        counts = ws["counts"].cpu().numpy()
+        prio = ws["expert_priority"].cpu().numpy()
+        plan = build_exec_plan(np.nonzero(counts > 0)[0], prio, cache.resident, cache.slots)
+        loads0 = cache.loads
+        cur = torch.cuda.current_stream(self.device)
+        need = set(plan.need_loading)
+        for e, s in zip(plan.expert_order, plan.slot_idxs):
+            if e in need:
+                cache.load(e, s)
+            cur.wait_event(cache.loaded[s])
+            self._ffn_call(x, ws, ws["a"], ws["h"], ws["y"], cap, 1, ws["offsets"][e:e + 2],
+                           cache.slot_ids[s:s + 1], 3, segments=1)
+            cache.free[s].record(cur)
+        self.last_exec_plan = plan
+        self.last_loads = cache.loads - loads0
+        self._mark("experts")
+        self._combine(ws, ws["y"], cap)
+        self._mark("combine")
+        return ws
 
     def _forward_ep(self, x, ws):
         if self.exchange == "p2p":

@@ -13,6 +13,7 @@ from __future__ import annotations
 
 import dataclasses
 import json
+import warnings
 
 import numpy as np
 import torch
@@ -20,6 +21,7 @@ import torch.nn as nn
 
 from . import _lib as L
 from .engine import MoEEngine, default_expert_to_gpu, pack_relu, pack_swiglu
+from .qos import QoSInputs
 
 
 def hf_callers_unpack_tuples() -> bool:
@@ -97,16 +99,28 @@ class QoSMoELayer(nn.Module):
         dtype = spec[1].dtype
         if dtype not in (torch.bfloat16, torch.float32):
             raise ValueError(f"expert dtype {dtype} not supported")
+        # expert_cache_size below the expert count: the reference's non-resident path (pinned host
+        # weights, cache slots, QoS-planned loads; src/qosmoe/moe_layer.py:129-131,296-330).
+        # Expert parallel keeps every local expert resident.
+        n_exp = int(spec[1].shape[0])
+        cache_slots = None
+        if int(config.expert_cache_size) < n_exp:
+            if config.world_size == 1:
+                cache_slots = max(1, int(config.expert_cache_size))
+            else:
+                warnings.warn("expert_cache_size < num_experts with world_size > 1: every local expert "
+                              "stays resident", stacklevel=2)
+        pack_dev = "cpu" if cache_slots is not None else dev
         shared = None
         sg_w = None
         if spec[0] == "relu":
-            packed = pack_relu(spec[1], spec[2], dtype=dtype, device=dev)
+            packed = pack_relu(spec[1], spec[2], dtype=dtype, device=pack_dev)
         else:
             if config.shared_expert is not None:
                 s = _sd(config.shared_expert)
                 shared = (s["gate_proj.weight"], s["up_proj.weight"], s["down_proj.weight"])
                 sg_w = _sd(config.shared_expert_gate)["weight"]
-            packed = pack_swiglu(spec[1], spec[2], spec[3], shared=shared, dtype=dtype, device=dev)
+            packed = pack_swiglu(spec[1], spec[2], spec[3], shared=shared, dtype=dtype, device=pack_dev)
         router_w = config.router_weights.detach()
         top_k = int(getattr(config, "top_k", 1) or 1)
         mode = L.ROUTE_SWITCH_TOP1 if top_k == 1 else L.ROUTE_SOFTMAX_TOPK
@@ -116,13 +130,17 @@ class QoSMoELayer(nn.Module):
                                 norm_topk=bool(getattr(config, "norm_topk_prob", False)),
                                 shared_gate_weight=sg_w, rank=config.rank, world=config.world_size,
                                 group=getattr(config, "process_group", None), expert_to_gpu=e2g,
-                                eq_tokens=config.eq_tokens)
+                                eq_tokens=config.eq_tokens, cache_slots=cache_slots, device=dev)
+        for k in ("alpha", "beta", "delta", "target_batch", "epsilon"):
+            self.engine.qos_params[k] = float(getattr(config, "qos_" + k, self.engine.qos_params[k]))
+        self.engine.qos_params["attention_mode"] = 0 if getattr(config, "qos_attention_mode", "router_var") == "router_var" else 1
         # the experts now live packed in the engine: drop this layer's references to the caller's
         # expert modules / state dicts so that a swapped model does not hold both copies
         if dataclasses.is_dataclass(config):
             self.config = dataclasses.replace(config, experts=None, expert_example=None)
         self.tot_num_toks_send, self.tot_num_toks_recv = [], []
         self.latencies, self.expert_freqs, self.num_prefetch_launched = [], [], []
+        self.expert_swaps = []
 
     def set_runtime_context(self, ctx):
         self.runtime_context = ctx
@@ -136,7 +154,7 @@ class QoSMoELayer(nn.Module):
                  "total number of tokens sent": self.tot_num_toks_send[i],
                  "total number of tokens recv": self.tot_num_toks_recv[i],
                  "expert distribution": self.expert_freqs[i],
-                 "num expert swaps": 0, "num prefetch launched": 0}
+                 "num expert swaps": self.expert_swaps[i], "num prefetch launched": 0}
                 for i in range(len(self.latencies))]
 
     @torch.no_grad()
@@ -148,7 +166,14 @@ class QoSMoELayer(nn.Module):
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             ev0.record()
         shape = hidden_states.shape
-        r = self.engine.forward(hidden_states.reshape(-1, self.d_model))
+        qos = None
+        if self.engine.cache is not None:
+            ctx = self.runtime_context
+            qos = QoSInputs(x_prev=getattr(ctx, "last_hidden_states", None),
+                            seq_priority=getattr(ctx, "flat_seq_priority", None),
+                            remaining=getattr(ctx, "flat_remaining_tokens", None),
+                            valid=getattr(ctx, "flat_valid_mask", None))
+        r = self.engine.forward(hidden_states.reshape(-1, self.d_model), qos=qos)
         out = r["out"].view(shape)
         self.runtime_context.last_hidden_states = r["out"]
         tuple_out = getattr(self.config, "return_router_tuple", True)
@@ -157,6 +182,7 @@ class QoSMoELayer(nn.Module):
             ev1.synchronize()
             self.latencies.append(ev0.elapsed_time(ev1))
             self.expert_freqs.append(r["counts"].tolist())
+            self.expert_swaps.append(self.engine.last_loads)
             lay = self.engine.last_layout
             T = r["out"].shape[0] * self.engine.top_k
             self.tot_num_toks_send.append(int(lay.send_splits.sum()) if lay is not None else T)

@@ -240,6 +240,37 @@ typedef struct {
 DSCA_API int dsca_combine(const dsca_combine_args* a, dsca_stream_t stream);
 
 /*
+ * QoS planner scores.  Replaces QoSPlanner.compute_token_scores and aggregate_expert_priority
+ * (src/qosmoe/planner.py:63-170).  They change no result: the expert-cache path orders its
+ * experts and chooses what to load by them (build_exec_plan, :172-237, on the host).  Per token:
+ *   gain    = |x - x_prev| (|x| when x_prev is NULL)
+ *   attn    = population variance of the token's logits row (0 when attention_mode = 1)
+ *   penalty = target_batch / (n(e0) + epsilon), e0 = the token's first choice, n(e) = how many
+ *             of the T tokens chose e first
+ *   score   = seq_priority (1 + gain (1 + attn) / (alpha d + beta remaining + delta penalty)),
+ *             -1e9 where valid == 0
+ * and per expert the sum of the scores of its (token, slot) assignments.  NULL per-token
+ * vectors read as seq_priority 1, remaining 0, valid 1.
+ */
+typedef struct {
+  const void* x;              /* [T, d] block input */
+  const void* x_prev;         /* [T, d] previous layer's hidden states, or NULL */
+  const void* logits;         /* [T, E] router logits */
+  int dtype;                  /* of x, x_prev and logits: DSCA_BF16 or DSCA_F32 */
+  const int32_t* topk_ids;    /* [T, top_k], first choice first */
+  const float* seq_priority;  /* [T] or NULL */
+  const float* remaining;     /* [T] or NULL */
+  const float* valid;         /* [T] or NULL */
+  int T, d, E, top_k;
+  int attention_mode;         /* 0 = router_var, 1 = none */
+  float alpha, beta, delta, target_batch, epsilon;
+  float* token_score;         /* [T] */
+  float* expert_priority;     /* [E] */
+  int32_t* err;
+} dsca_qos_args;
+DSCA_API int dsca_qos_priority(const dsca_qos_args* a, dsca_stream_t stream);
+
+/*
  * Harmony plan on the host (integer, deterministic, identical on every rank).
  * Restates Scheduler.schedule_harmony (src/harmonymoe/scheduler.py:324-372) over an arbitrary
  * expert -> GPU placement (the exflow [layer][gpu] -> experts format,

@@ -286,3 +286,64 @@ def max_rel_err(a, ref) -> float:
     ref = np.asarray(ref, np.float64)
     den = np.abs(ref).max()
     return float(np.abs(a - ref).max() / (den if den > 0 else 1.0))
+
+
+# ------------------------------------------------------------------------------ QoS planner
+def qos_token_scores(x, x_prev, logits, expert_index, seq_priority, remaining, valid, d_model,
+                     alpha=1.0, beta=0.1, delta=0.5, target_batch=64, eps=1e-6, mode="router_var"):
+    """QoSPlanner.compute_token_scores (src/qosmoe/planner.py:63-151) for per-token inputs of the
+    token count: info gain = |x - x_prev| (|x| when x_prev is missing or of another shape,
+    :100-110), attention factor = population variance of the logits row (:52-61), small-batch
+    penalty = target / (count of the token's expert + eps) (:117-123), priority = P (1 + gain
+    (1 + attn) / (alpha d + beta rem + delta penalty)), invalid tokens -1e9 (:135-151).
+    float64 arithmetic on the float32 inputs."""
+    x = np.asarray(x, np.float64)
+    if x_prev is not None and np.shape(x_prev) == x.shape:
+        gain = np.linalg.norm(x - np.asarray(x_prev, np.float64), axis=1)
+    else:
+        gain = np.linalg.norm(x, axis=1)
+    lg = np.asarray(logits, np.float64)
+    attn = lg.var(axis=1) if mode == "router_var" else np.zeros(len(x))
+    ei = np.asarray(expert_index, np.int64)
+    cnt = np.bincount(ei, minlength=lg.shape[1]).astype(np.float64)
+    penalty = target_batch / (cnt[ei] + eps)
+    denom = alpha * d_model + beta * np.asarray(remaining, np.float64) + delta * penalty
+    pri = np.asarray(seq_priority, np.float64) * (1.0 + gain * (1.0 + attn) / denom)
+    ok = np.asarray(valid) != 0
+    return np.where(ok, pri, -1e9)
+
+
+def qos_expert_priority(scores, topk_ids, E: int):
+    """QoSPlanner.aggregate_expert_priority (src/qosmoe/planner.py:153-170): per expert, the sum
+    of the scores of its tokens (every (token, slot) assignment with top-k routing)."""
+    ids = np.asarray(topk_ids).reshape(len(scores), -1)
+    out = np.zeros(E, np.float64)
+    for j in range(ids.shape[1]):
+        np.add.at(out, ids[:, j], np.asarray(scores, np.float64))
+    return out
+
+
+def qos_exec_plan(active, priority, cache: list, cache_size: int):
+    """QoSPlanner.build_exec_plan (src/qosmoe/planner.py:172-237): resident experts first, then
+    the others, each by priority descending (stable: expert id ascending on ties); the slots for
+    the experts to load cycle through the free slots, then the resident experts' slots from the
+    lowest priority up.  Returns (expert_order, slot_idxs, need_loading)."""
+    act = [e for e in range(len(priority)) if e in set(active)]
+    loaded = sorted([e for e in act if e in cache], key=lambda e: -priority[e])
+    unloaded = sorted([e for e in act if e not in cache], key=lambda e: -priority[e])
+    if not unloaded:
+        return loaded, [cache.index(e) for e in loaded], []
+    low_to_high = [cache.index(e) for e in sorted(loaded, key=lambda e: priority[e])]
+    used = set(low_to_high)
+    cand = [s for s in range(cache_size) if s not in used] + low_to_high
+    cand = cand or [0]
+    order, slots, need = loaded + unloaded, [], []
+    c = 0
+    for e in order:
+        if e in cache:
+            slots.append(cache.index(e))
+        else:
+            slots.append(cand[c % len(cand)])
+            c += 1
+            need.append(e)
+    return order, slots, need

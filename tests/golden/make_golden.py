@@ -424,6 +424,79 @@ def dispatch_fixture(name):
     print(f"{name}: {len(out)} cases")
 
 
+# ----------------------------------------------------------------------------- QoS planner
+def planner_fixture(name):
+    """Token scores, expert priorities and execution plans from the reference's QoSPlanner
+    (src/qosmoe/planner.py:63-237) on seeded inputs; the runtime context carries fixed
+    per-token vectors (the reference derives them from wall-clock deadlines)."""
+    from types import SimpleNamespace
+
+    from qosmoe.planner import QoSPlanner
+
+    g = syn.rng(5150)
+    out = {}
+    meta = []
+    score_cases = [
+        # (T, d, E, prev, mode, invalid fraction)
+        (96, 64, 8, "same", "router_var", 0.1),
+        (64, 32, 8, None, "router_var", 0.0),
+        (80, 48, 16, "other", "router_var", 0.25),
+        (50, 64, 8, "same", "none", 0.0),
+    ]
+    for ci, (T, d, E, prev, mode, inv) in enumerate(score_cases):
+        args = SimpleNamespace(qos_attention_mode=mode, qos_target_batch=64, qos_epsilon=1e-6,
+                               qos_alpha=1.0, qos_beta=0.1, qos_delta=0.5)
+        x = g.standard_normal((T, d)).astype(np.float32)
+        xp = None
+        if prev == "same":
+            xp = (x + 0.3 * g.standard_normal((T, d))).astype(np.float32)
+        elif prev == "other":
+            xp = g.standard_normal((T + 7, d)).astype(np.float32)
+        logits = (2.0 * g.standard_normal((T, E))).astype(np.float32)
+        eidx = np.argmax(logits, axis=1).astype(np.int64)
+        seq_pri = g.uniform(0.5, 2.0, T).astype(np.float32)
+        rem = g.integers(1, 300, T).astype(np.float32)
+        valid = (g.uniform(0, 1, T) >= inv).astype(np.float32)
+        ctx = SimpleNamespace(flat_remaining_tokens=torch.from_numpy(rem),
+                              flat_seq_priority=torch.from_numpy(seq_pri),
+                              flat_valid_mask=torch.from_numpy(valid))
+        pl = QoSPlanner(args, rank=0, num_experts=E, num_gpus=1, d_model=d)
+        with _CudaToCpu():
+            sc = pl.compute_token_scores(torch.from_numpy(x), None if xp is None else torch.from_numpy(xp),
+                                         torch.from_numpy(logits), torch.from_numpy(eidx), ctx)
+            lists = [torch.nonzero(torch.from_numpy(eidx) == e).flatten() for e in range(E)]
+            pri = pl.aggregate_expert_priority(lists, sc)
+        key = f"s{ci}"
+        out.update({key + "_x": x, key + "_logits": logits, key + "_eidx": eidx, key + "_seq": seq_pri,
+                    key + "_rem": rem, key + "_valid": valid, key + "_score": _np(sc), key + "_prio": _np(pri)})
+        if xp is not None:
+            out[key + "_xprev"] = xp
+        meta.append(dict(key=key, T=T, d=d, E=E, prev=prev, mode=mode))
+    plans = []
+    plan_cases = [
+        # (E, active experts, cache contents, cache_size)
+        (8, [0, 1, 2, 3, 4, 5, 6, 7], [], 2),
+        (8, [1, 3, 4, 6], [3, 6], 2),
+        (8, [0, 2, 5, 7], [2, 9, 5, 1], 4),
+        (16, list(range(16)), [4, 8, 12], 3),
+        (8, [2, 4], [2, 4, 6], 3),
+        (8, [1, 2, 3], [], 8),
+    ]
+    for E, active, cache, cs in plan_cases:
+        pr = g.standard_normal(E).astype(np.float32)
+        pr[2] = pr[3]  # a tie: the stable sort keeps expert id order
+        mask = [torch.zeros(3 if e in active else 0, dtype=torch.long) for e in range(E)]
+        pl = QoSPlanner(SimpleNamespace(), rank=0, num_experts=E, num_gpus=1, d_model=8)
+        plan = pl.build_exec_plan(mask, torch.from_numpy(pr), list(cache), cs)
+        plans.append(dict(E=E, active=active, cache=cache, cache_size=cs, priority=pr.tolist(),
+                          expert_order=[int(v) for v in plan.expert_order],
+                          slot_idxs=[int(v) for v in plan.slot_idxs],
+                          need_loading=[int(v) for v in plan.need_loading]))
+    out["meta"] = np.array(json.dumps(dict(score_cases=meta, plans=plans)))
+    np.savez_compressed(os.path.join(HERE, name), **out)
+    print("wrote", name)
+
+
 def main():
     install_shim()
     torch.manual_seed(0)
@@ -451,6 +524,8 @@ def main():
     # Scheduler plans and dispatch order
     scheduler_fixture("harmony_plans.json")
     dispatch_fixture("dispatch_order.json")
+    # QoS planner: token scores, expert priorities, execution plans
+    planner_fixture("qos_planner.npz")
 
 
 if __name__ == "__main__":

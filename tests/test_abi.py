@@ -42,7 +42,7 @@ def test_struct_layouts_match_header(lib):
             off = (off + sz - 1) // sz * sz + sz
         return (off + 7) // 8 * 8
 
-    for s in (_lib.RouterArgs, _lib.ScanArgs, _lib.PermuteArgs, _lib.FfnArgs, _lib.CombineArgs):
+    for s in (_lib.RouterArgs, _lib.ScanArgs, _lib.PermuteArgs, _lib.FfnArgs, _lib.CombineArgs, _lib.QosArgs):
         assert ctypes.sizeof(s) == c_size(s._fields_), s.__name__
 
 
