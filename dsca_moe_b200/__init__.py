@@ -5,6 +5,7 @@ Public surface (mirrors the reference's plugin):
   ShardedQwenMoE, patch                          (qwen_ep_adapter drop-in)
   MoEEngine, pack_swiglu, pack_relu, plan_harmony, plan_layout   (engine level)
   build_exec_plan, QoSInputs, ExpertCache        (expert cache / QoS planner path)
+  write_run_outputs, TokenTrace                  (the reference's run output files)
 The compute runs in libdsca_b200.so (include/dsca_b200.h); build it with
 ``python -m dsca_moe_b200.build``.
 """
@@ -24,6 +25,9 @@ def __getattr__(name):
                 "default_expert_to_gpu", "exchange_chunks"):
         from . import engine
         return getattr(engine, name)
+    if name in ("write_run_outputs", "TokenTrace"):
+        from . import reporting
+        return getattr(reporting, name)
     if name in ("QoSExecPlan", "QoSInputs", "ExpertCache", "build_exec_plan"):
         from . import qos
         return getattr(qos, name)

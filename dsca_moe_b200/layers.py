@@ -22,6 +22,7 @@ import torch.nn as nn
 from . import _lib as L
 from .engine import MoEEngine, default_expert_to_gpu, pack_relu, pack_swiglu
 from .qos import QoSInputs
+from .reporting import TRACE
 
 
 def hf_callers_unpack_tuples() -> bool:
@@ -173,7 +174,14 @@ class QoSMoELayer(nn.Module):
                             seq_priority=getattr(ctx, "flat_seq_priority", None),
                             remaining=getattr(ctx, "flat_remaining_tokens", None),
                             valid=getattr(ctx, "flat_valid_mask", None))
+        trace = TRACE.enabled()
+        if trace:  # the reference's token trace: host times around the block, device synchronised
+            torch.cuda.synchronize()
+            t0 = TRACE.now_ms()
         r = self.engine.forward(hidden_states.reshape(-1, self.d_model), qos=qos)
+        if trace:
+            torch.cuda.synchronize()
+            TRACE.record_block(self.layer_idx, r["topk_ids"].cpu().numpy(), t0, t0, TRACE.now_ms())
         out = r["out"].view(shape)
         self.runtime_context.last_hidden_states = r["out"]
         tuple_out = getattr(self.config, "return_router_tuple", True)
