@@ -30,7 +30,9 @@ class RouterArgs(ctypes.Structure):
                 ("norm_topk", _i), ("weight_round_bf16", _i),
                 ("logits", _vp), ("topk_ids", _vp), ("topk_w", _vp), ("expert_index", _vp),
                 ("shared_gate", _vp), ("block_hist", _vp), ("local_rank", _vp),
-                ("counts", _vp), ("offsets", _vp), ("block_base", _vp), ("done_counter", _vp)]
+                ("counts", _vp), ("offsets", _vp), ("block_base", _vp), ("done_counter", _vp),
+                ("w_slices", _vp), ("w_exp", _vp), ("x_slices", _vp), ("x_exp", _vp), ("logits_f32", _vp),
+                ("err", _vp)]
 
 
 class ScanArgs(ctypes.Structure):
@@ -92,7 +94,7 @@ EXPORTED = ["dsca_version", "dsca_status_string", "dsca_device_info", "dsca_rout
             "dsca_grouped_ffn_static_scratch", "dsca_ep_ctx_bytes", "dsca_ep_init", "dsca_ep_group_offsets",
             "dsca_ep_plan", "dsca_ep_dispatch", "dsca_ep_wait", "dsca_ep_plan_eval", "dsca_ipc_export",
             "dsca_ipc_import", "dsca_ipc_close", "dsca_ep_read_plan", "dsca_ep_region_alloc",
-            "dsca_ep_region_free", "dsca_ep_return", "dsca_qos_priority"]
+            "dsca_ep_region_free", "dsca_ep_return", "dsca_qos_priority", "dsca_router_pack_i8"]
 STATIC_SCRATCH_BYTES = 16 << 20
 
 _LIB = None

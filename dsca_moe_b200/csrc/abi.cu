@@ -5,7 +5,9 @@
 #include "common.cuh"
 
 namespace dsca {
-int launch_router(const dsca_router_args* p, cudaStream_t stream);
+int launch_router(const dsca_router_args* p, cudaStream_t stream, const float* logits_in = nullptr);
+int launch_router_tc(const dsca_router_args* a, cudaStream_t stream);
+int launch_router_pack_i8(const void* rows, int R, int d, void* slices, int32_t* exps, cudaStream_t stream);
 int launch_exp_eval(const float* x, float* y, int n, cudaStream_t stream);
 int launch_scan(const dsca_scan_args* a, cudaStream_t stream);
 int launch_permute(const dsca_permute_args* a, cudaStream_t stream);
@@ -93,8 +95,22 @@ int dsca_router_topk(const dsca_router_args* a, dsca_stream_t stream) {
   const int nscan = (a->counts != nullptr) + (a->offsets != nullptr) + (a->block_base != nullptr) +
                     (a->done_counter != nullptr);
   if (nscan != 0 && nscan != 4) return DSCA_ERR_BAD_ARG;
+  // the tensor-core logits take all five buffers or none, bf16 only
+  const int ntc = (a->w_slices != nullptr) + (a->w_exp != nullptr) + (a->x_slices != nullptr) +
+                  (a->x_exp != nullptr) + (a->logits_f32 != nullptr);
+  if (ntc != 0 && (ntc != 5 || a->dtype != DSCA_BF16 || !aligned16(a->w_slices) || !aligned16(a->x_slices) ||
+                   !aligned16(a->logits_f32) || a->d > 32768))
+    return DSCA_ERR_BAD_ARG;
   if (a->T == 0) return DSCA_OK;
+  if (ntc == 5) return dsca::launch_router_tc(a, reinterpret_cast<cudaStream_t>(stream));
   return dsca::launch_router(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int dsca_router_pack_i8(const void* rows, int R, int d, void* w_slices, int32_t* w_exp, dsca_stream_t stream) {
+  if (rows == nullptr || w_slices == nullptr || w_exp == nullptr || R <= 0 || R > DSCA_MAX_EXPERTS || d <= 0 ||
+      d % 8 != 0 || d > 32768 || !aligned16(rows) || !aligned16(w_slices))
+    return DSCA_ERR_BAD_ARG;
+  return dsca::launch_router_pack_i8(rows, R, d, w_slices, w_exp, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int dsca_dispatch_scan(const dsca_scan_args* a, dsca_stream_t stream) {

@@ -64,6 +64,9 @@ struct Args {
   int32_t* offsets;
   int32_t* block_base;
   uint32_t* done_counter;
+  // precomputed logits [T][64] (fp32 values already rounded to the router dtype, rows past E
+  // unused), or null: the kernel computes them (the chunked fp32 order below)
+  const float* logits_in;
 };
 
 __device__ __forceinline__ void group_sync(int q) {
@@ -277,6 +280,14 @@ __global__ void __launch_bounds__(kThreads, 1) router_kernel(Args a) {
   const bool tau_bf16 = sizeof(T) == 2;
   if (tid < kRows) emask[tid] = 0u;
 
+  if (a.logits_in != nullptr) {
+    // logits from the tensor-core pass (router_tc.cu)
+    for (int idx = tid; idx < kTokens * kRows; idx += kThreads) {
+      const int t = idx / kRows, r = idx % kRows;
+      lg_s[t * kLP + r] = (tok0 + t < a.T) ? a.logits_in[(size_t)(tok0 + t) * kRows + r] : 0.0f;
+    }
+    __syncthreads();
+  } else {
   // ---------------- chunk partial sums, two chunks per group
   const int C = 32 * ((a.d + 255) / 256);
   const int nq = (a.d + C - 1) / C;
@@ -339,6 +350,7 @@ __global__ void __launch_bounds__(kThreads, 1) router_kernel(Args a) {
     lg_s[t * kLP + r] = tau_bf16 ? round_bf16(tot) : tot;
   }
   __syncthreads();
+  }  // logits computed here
 
   // ---------------- softmax and selection: one warp per token
   const int warp = tid >> 5, lane = tid & 31;
@@ -441,9 +453,10 @@ __global__ void __launch_bounds__(kThreads, 1) router_kernel(Args a) {
 
 }  // namespace router
 
-int launch_router(const dsca_router_args* p, cudaStream_t stream) {
+int launch_router(const dsca_router_args* p, cudaStream_t stream, const float* logits_in) {
   static bool attr_done[2] = {false, false};
   router::Args a;
+  a.logits_in = logits_in;
   a.x = p->x;
   a.w_router = p->w_router;
   a.w_shared_gate = p->w_shared_gate;

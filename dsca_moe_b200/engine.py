@@ -337,6 +337,11 @@ class MoEEngine:
                                    shared_gate_weight.reshape(-1).to(device=self.device, dtype=self.dtype).contiguous())
         if (self.shared_gate_weight is None) != (experts.ws1 is None):
             raise ValueError("shared expert and shared gate must be given together")
+        # True (bf16 only): router logits on the tensor cores instead of the CUDA cores — exact
+        # fixed-point accumulation on int8 tcgen05 MMAs (router_tc.cu); off by default, the
+        # CUDA-core router is faster on the measured workloads
+        self.router_tensor_cores = False
+        self._w_slices = self._w_exp = None
         self.rank, self.world, self.group = rank, world, group
         if expert_to_gpu is None:
             expert_to_gpu = default_expert_to_gpu(self.E, world)
@@ -423,6 +428,28 @@ class MoEEngine:
         return ws
 
     # -------------------------------------------------------------- kernel steps
+    def _router_tc_buffers(self, T: int) -> dict:
+        """Tensor-core router: the sliced router rows (once) and the per-call scratch for T tokens."""
+        if self.dtype != torch.bfloat16:
+            raise ValueError("the tensor-core router takes bf16 inputs")
+        d16 = _ceil(self.d, 16) * 16
+        if self._w_slices is None:
+            rows = self.router_weight if self.shared_gate_weight is None else torch.cat(
+                [self.router_weight, self.shared_gate_weight[None]], 0)
+            self._w_rows = rows.contiguous()
+            self._w_slices = torch.empty(3, 64, d16, dtype=torch.int8, device=self.device)
+            self._w_exp = torch.empty(64, dtype=torch.int32, device=self.device)
+            L.call("dsca_router_pack_i8", _ptr(self._w_rows), self._w_rows.shape[0], self.d, _ptr(self._w_slices),
+                   _ptr(self._w_exp), _stream())
+        tc = getattr(self, "_tc_ws", None)
+        if tc is None or tc["x_exp"].shape[0] != T:
+            dev = self.device
+            tc = dict(x_slices=torch.empty(3, T, d16, dtype=torch.int8, device=dev),
+                      x_exp=torch.empty(T, dtype=torch.int32, device=dev),
+                      logits_f32=torch.empty(T, 64, dtype=torch.float32, device=dev))
+            self._tc_ws = tc
+        return tc
+
     def _route(self, x: torch.Tensor, ws: dict):
         T = x.shape[0]
         a = L.RouterArgs()
@@ -440,6 +467,11 @@ class MoEEngine:
         if self.fuse_scan:
             a.counts, a.offsets, a.block_base = _ptr(ws["counts"]), _ptr(ws["offsets"]), _ptr(ws["block_base"])
             a.done_counter = _ptr(self._done_counter)
+        if self.router_tensor_cores:
+            tc = self._router_tc_buffers(T)
+            a.w_slices, a.w_exp = _ptr(self._w_slices), _ptr(self._w_exp)
+            a.x_slices, a.x_exp, a.logits_f32 = _ptr(tc["x_slices"]), _ptr(tc["x_exp"]), _ptr(tc["logits_f32"])
+            a.err = _ptr(self.err)
         L.call("dsca_router_topk", ctypes.byref(a), _stream())
         self._mark("router")
         if self.fuse_scan:

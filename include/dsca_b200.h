@@ -74,8 +74,11 @@ DSCA_API int dsca_device_info(int* num_sms, int* is_sm100);
  * src/qosmoe/moe_layer.py:286-287, and the gate / softmax / topk of ShardedQwenMoE.forward
  * (qwen_ep_adapter/qwen_ep.py:48-53), plus the shared-expert gate sigmoid(x . g)
  * (qwen_ep_adapter/qwen_ep.py:94).
- * Arithmetic order is fixed: logit = round_dtype(fp32 fma over i = 0..d-1), softmax with a
- * deterministic exp (bit-identical to the C oracle).
+ * Arithmetic order is fixed (bit-identical to the C oracle): with the tensor-core fields below
+ * (bf16 only), logit = the exact fixed-point dot product of the bf16 rows (21 bits below each
+ * row's largest exponent, accumulated in integers on int8 tcgen05 MMAs), converted once to fp32
+ * and rounded to bf16; otherwise the fp32 fma chains of the kernel's chunked order, rounded to
+ * the dtype.  Softmax uses a deterministic exp.
  */
 typedef struct {
   const void* x;              /* [T, d], dtype */
@@ -99,8 +102,23 @@ typedef struct {
   int32_t* offsets;           /* [E + 1] */
   int32_t* block_base;        /* [ceil(T/32), E] */
   uint32_t* done_counter;
+  /* optional tensor-core logits (bf16): set all five or none; d16 = d rounded up to 16 */
+  const void* w_slices;       /* [3][64][d16] int8 from dsca_router_pack_i8 */
+  const int32_t* w_exp;       /* [64] from dsca_router_pack_i8 */
+  void* x_slices;             /* [3][T][d16] int8 scratch */
+  int32_t* x_exp;             /* [T] scratch */
+  float* logits_f32;          /* [T][64] scratch */
+  int32_t* err;               /* device error word for the tensor-core pass's bounded waits, or NULL */
 } dsca_router_args;
 DSCA_API int dsca_router_topk(const dsca_router_args* a, dsca_stream_t stream);
+
+/*
+ * Router rows for the tensor-core logits: `rows` [R][d] bf16 (R <= 64: the E router rows, then
+ * the shared-expert gate row) -> three int8 slice planes [3][64][d16] and the rows' exponents
+ * [64]; rows R..63 are zero.  Run once per router weight.
+ */
+DSCA_API int dsca_router_pack_i8(const void* rows, int R, int d, void* w_slices, int32_t* w_exp,
+                                 dsca_stream_t stream);
 
 /*
  * Dispatch scan: per-expert counts, expert-major row offsets and each block's base rank inside

@@ -52,6 +52,9 @@ def lib():
         _LIB.oracle_round_bf16.argtypes = [ctypes.c_float]
         _LIB.oracle_round_bf16.restype = ctypes.c_float
         _LIB.oracle_router_logits.argtypes = [f32p, f32p, c_int, c_int, c_int, c_int, f32p]
+        _LIB.oracle_router_logits_fixed.argtypes = [f32p, f32p, c_int, c_int, c_int, f32p]
+        _LIB.oracle_scale_pow2.argtypes = [ctypes.c_float, c_int]
+        _LIB.oracle_scale_pow2.restype = ctypes.c_float
         _LIB.oracle_route_top1.argtypes = [f32p, c_int, c_int, c_int, i32p, f32p]
         _LIB.oracle_route_topk.argtypes = [f32p, c_int, c_int, c_int, c_int, c_int, i32p, f32p]
         _LIB.oracle_softmax.argtypes = [f32p, c_int, c_int, f32p]
@@ -80,12 +83,23 @@ def exp_neg(x) -> np.ndarray:
 
 
 def router_logits(x, W, tau: str) -> np.ndarray:
-    """logits[T,E] in tau ('bf16' or 'f32'), fixed-order fp32 accumulation (routing.c)."""
+    """logits[T,E] in tau ('bf16' or 'f32') by the chunked fp32 fma order of the CUDA-core
+    router (routing.c: oracle_router_logits)."""
     x, W = _f32(x), _f32(W)
     T, d = x.shape
     E = W.shape[0]
     out = np.empty((T, E), np.float32)
     lib().oracle_router_logits(x, W, T, d, E, 1 if tau == "bf16" else 0, out)
+    return out
+
+
+def router_logits_fixed(x, W) -> np.ndarray:
+    """bf16 logits[T,E] of the tensor-core router: exact fixed-point accumulation of the bf16
+    inputs, one rounding to fp32, then to bf16 (routing.c: oracle_router_logits_fixed)."""
+    x, W = bf16_round(x), bf16_round(W)
+    T, d = x.shape
+    out = np.empty((T, W.shape[0]), np.float32)
+    lib().oracle_router_logits_fixed(x, W, T, d, W.shape[0], out)
     return out
 
 

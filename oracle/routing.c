@@ -19,7 +19,8 @@
  *     w      = w / sum(w)             only when norm_topk_prob
  *     w      = w.to(activation dtype)
  *
- * Fixed order used here and in the kernel (the reference leaves it to cuBLAS/ATen):
+ * Fixed order used here and in the kernels (the reference leaves it to cuBLAS/ATen); the
+ * optional tensor-core router follows oracle_router_logits_fixed instead:
  *   C          = 32 * ceil(d / 256)   (d splits into at most 8 chunks of C)
  *   S_q        = fma-accumulate over i in [qC, min(d, (q+1)C)) of x[t,i] * W[e,i], from 0.0f
  *   logit[t,e] = round_tau( partials summed left to right: ((S_0 + S_1) + S_2) + ... )
@@ -36,6 +37,7 @@
  * Build: oracle/Makefile (gcc -O2 -ffp-contract=off; fmaf is the correctly rounded libm fmaf).
  */
 #include <math.h>
+#include <stdlib.h>
 #include <stdint.h>
 #include <string.h>
 
@@ -102,6 +104,73 @@ void oracle_router_logits(const float* x, const float* W, int T, int d, int E, i
             logits[(size_t)t * E + e] = round_bf16 ? oracle_round_bf16(acc) : acc;
         }
     }
+}
+
+
+
+/*
+ * bf16 logits by exact fixed-point accumulation (the arithmetic of the tensor-core router).
+ * A bf16 value v (sign s, biased exponent b, 7-bit mantissa m) is s * M * 2^(e - 134) with
+ * M = 128 + m, e = b for normals and M = m, e = 1 for zero and subnormals.  With R the largest e
+ * over the row's nonzero entries (1 for an all-zero row), v is held as the 21-bit magnitude
+ *   F = M << (13 - (R - e))        when R - e <= 13  (exact: v = s F 2^(R - 147)),
+ *   F = M >> ((R - e) - 13)        otherwise          (low bits dropped; 0 from R - e = 21 on),
+ * and the logit of (x row, W row) is
+ *   P        = sum_i s_x s_w F_x F_w                 exact, in a 64-bit integer
+ *   logit32  = (float) P                             round to nearest even
+ *   logit32  = logit32 * 2^(R_x + R_w - 294)         IEEE multiplications by powers of two
+ *   logit    = round_bf16(logit32).
+ * The device splits each F into three signed 7-bit slices and accumulates the nine slice
+ * products in 32-bit integers on the tensor cores; the integer sum is the same P.
+ * Inputs are bf16 values carried in floats; non-finite inputs are not supported.
+ */
+static void fixed_row(const float* v, int d, int32_t* F, int* R) {
+    int rmax = 1;
+    for (int i = 0; i < d; ++i) {
+        const uint32_t u = f_to_bits(v[i]) >> 16;
+        const int b = (int)((u >> 7) & 0xffu);
+        const int m = (int)(u & 0x7fu);
+        if ((b != 0 || m != 0) && b > rmax) rmax = b;
+    }
+    for (int i = 0; i < d; ++i) {
+        const uint32_t u = f_to_bits(v[i]) >> 16;
+        const int b = (int)((u >> 7) & 0xffu);
+        const int m = (int)(u & 0x7fu);
+        const int M = b ? 128 + m : m;
+        const int e = b ? b : 1;
+        const int sh = rmax - e;
+        int32_t f = sh <= 13 ? (M << (13 - sh)) : (sh - 13 < 9 ? (M >> (sh - 13)) : 0);
+        F[i] = (u & 0x8000u) ? -f : f;
+    }
+    *R = rmax;
+}
+
+/* f * 2^k by IEEE single multiplications, each factor a normal power of two */
+float oracle_scale_pow2(float f, int k) {
+    while (k > 127) { f = f * bits_to_f(254u << 23); k -= 127; }
+    while (k < -126) { f = f * bits_to_f(1u << 23); k += 126; }
+    return f * bits_to_f((uint32_t)(k + 127) << 23);
+}
+
+void oracle_router_logits_fixed(const float* x, const float* W, int T, int d, int E, float* logits) {
+    int32_t* fw = (int32_t*)malloc(sizeof(int32_t) * (size_t)E * d);
+    int* rw = (int*)malloc(sizeof(int) * (size_t)E);
+    int32_t* fx = (int32_t*)malloc(sizeof(int32_t) * (size_t)d);
+    for (int e = 0; e < E; ++e) fixed_row(W + (size_t)e * d, d, fw + (size_t)e * d, rw + e);
+    for (int t = 0; t < T; ++t) {
+        int rx;
+        fixed_row(x + (size_t)t * d, d, fx, &rx);
+        for (int e = 0; e < E; ++e) {
+            const int32_t* w = fw + (size_t)e * d;
+            int64_t p = 0;
+            for (int i = 0; i < d; ++i) p += (int64_t)fx[i] * (int64_t)w[i];
+            const float l = oracle_scale_pow2((float)p, rx + rw[e] - 294);
+            logits[(size_t)t * E + e] = oracle_round_bf16(l);
+        }
+    }
+    free(fw);
+    free(rw);
+    free(fx);
 }
 
 /* softmax of one row in the kernel's order; probs[E] fp32 (not rounded) */

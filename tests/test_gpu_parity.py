@@ -421,3 +421,52 @@ def test_host_pipeline_matches_forward(cuda):
     for xh, oh in zip(xs, outs):
         ref = eng.forward(xh.to(cuda))["out"].cpu()
         assert torch.equal(oh, ref)
+
+
+@pytest.mark.parametrize("T,d,E", [(131, 72, 64), (300, 2048, 60), (5, 64, 8), (1, 128, 64)])
+def test_tensor_core_router_edge_values(cuda, T, d, E):
+    """The optional tensor-core router (bf16 logits by exact fixed-point accumulation on int8
+    tcgen05 MMAs) equals the oracle's fixed-point logits bit for bit on rows with zeros,
+    subnormals, negated rows and exponent spreads past the 13-bit window, a width that is not a
+    multiple of 16 and a token count that is not a multiple of 128."""
+    g = np.random.default_rng(9 + T)
+    x = g.standard_normal((T, d)) * np.exp2(g.integers(-24, 8, (T, d)))
+    x[0] = 0.0
+    if T > 3:
+        x[1, : d // 2] = 0.0
+        x[2] = 1e-40 * np.sign(x[2])  # bf16 subnormals
+        x[3] = -np.abs(x[3])
+    x = O.bf16_round(x.astype(np.float32))
+    W = O.bf16_round((g.standard_normal((E, d)) * np.exp2(g.integers(-16, 2, (E, d)))).astype(np.float32))
+    W[0] = 0.0
+    wi, wo = syn.switch_expert_weights(E, d, 256, 5, dtype="bf16")
+    eng = switch_engine(W, wi, wo, torch.bfloat16, cuda)
+    eng.router_tensor_cores = True
+    r = eng.forward(_t(x, torch.bfloat16, cuda))
+    torch.cuda.synchronize()
+    eng.check()
+    lg = O.router_logits_fixed(x, W)
+    assert np.array_equal(_np(r["logits"]).view(np.uint32), lg.view(np.uint32))
+    assert np.array_equal(r["expert_index"].cpu().numpy(), O.route_top1(lg, "bf16")[0])
+
+
+def test_tensor_core_router_qwen_block(cuda):
+    """Tensor-core router on the Qwen block shape (60 experts + the shared gate row): logits,
+    top-4 choices and weights and the shared gate follow the fixed-point oracle exactly, and the
+    block output stays within the bf16 tolerance of the oracle."""
+    T, d, E, k = 1000, 2048, 60, 4
+    x = syn.hidden_states(T, d, 401, "bf16")
+    Wg, _ = syn.router_weight(E, d, 402, zipf_s=1.5, dtype="bf16")
+    p = syn.qwen_expert_weights(E, d, 64, 128, 403, dtype="bf16")
+    eng = qwen_engine(Wg, p, k, False, torch.bfloat16, cuda)
+    eng.router_tensor_cores = True
+    r = eng.forward(_t(x, torch.bfloat16, cuda))
+    torch.cuda.synchronize()
+    eng.check()
+    lg = O.router_logits_fixed(x, Wg)
+    ids, w = O.route_topk(lg, k, False, "bf16")
+    assert np.array_equal(_np(r["logits"]).view(np.uint32), lg.view(np.uint32))
+    assert np.array_equal(r["topk_ids"].cpu().numpy(), ids)
+    assert np.array_equal(r["topk_w"].cpu().numpy().view(np.uint32), w.view(np.uint32))
+    z = O.router_logits_fixed(x, p["s_gate_w"])[:, 0].astype(np.float64)
+    assert np.abs(r["shared_gate"].cpu().numpy() - 1.0 / (1.0 + np.exp(-z))).max() < 1e-6
