@@ -78,6 +78,8 @@ def parse():
     ap.add_argument("--tile-rows", type=int, choices=[0, 128, 256], default=0,
                     help="bf16 expert GEMM tiles: 0 = default per GEMM, 256 = CTA pairs (cta_group::2, "
                          "weights as M), 128 = one CTA per 128-token tile")
+    ap.add_argument("--no-pdl", action="store_true",
+                    help="one GPU: launch GEMM1 after the permute has finished (no programmatic dependent launch)")
     ap.add_argument("--expert-cache", type=int, default=0,
                     help="one GPU: keep only this many routed experts on the device (the reference's "
                          "expert_cache_size); the rest stream in from pinned host memory per the QoS plan")
@@ -504,6 +506,7 @@ def main():
     eng.ep_return = args.ep_return
     eng.tile_rows = args.tile_rows
     eng.ep_side_sms = args.ep_side_sms
+    eng.pdl = not args.no_pdl
     peaks = load_peaks()
     if args.once:
         eng.forward(x)

@@ -55,7 +55,7 @@ class FfnArgs(ctypes.Structure):
                 ("xs", _vp), ("ws1", _vp), ("ws2", _vp), ("hs", _vp), ("ys", _vp), ("err", _vp),
                 ("num_ctas", _i), ("phases", _i), ("ep_ctx", _vp), ("segments", _i),
                 ("w1_scale", _vp), ("w2_scale", _vp), ("ws1_scale", _vp), ("ws2_scale", _vp),
-                ("tile_rows", _i)]
+                ("tile_rows", _i), ("pdl_after_permute", _i)]
 
 
 MAX_GPUS = 8
@@ -76,7 +76,7 @@ class EpDispatchArgs(ctypes.Structure):
 class CombineArgs(ctypes.Structure):
     _fields_ = [("T", _i), ("d", _i), ("top_k", _i), ("dtype", _i), ("y", _vp), ("token_row", _vp),
                 ("topk_w", _vp), ("ys", _vp), ("shared_gate", _vp), ("rows", _i), ("out", _vp),
-                ("err", _vp)]
+                ("err", _vp), ("pdl", _i)]
 
 
 class QosArgs(ctypes.Structure):

@@ -72,12 +72,11 @@ int launch_scan(const dsca_scan_args* a, cudaStream_t stream) {
 }
 
 // ------------------------------------------------------------------ permute
+// One warp per (token, slot) assignment, grid-stride over the assignments with a grid that is
+// resident at once (two CTAs per SM): every CTA starts immediately, so the programmatic
+// dependent launch below fires at the start and leaves room on each SM for the dependent GEMM.
 template <int ESZ>
-__global__ void __launch_bounds__(256) permute_kernel(dsca_permute_args a) {
-  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = lane_id();
-  const int total = a.T * a.top_k;
-  if (w >= total) return;
+__device__ __forceinline__ void permute_one(const dsca_permute_args& a, int w, int lane) {
   const int t = w / a.top_k;
   const int e = a.topk_ids[w];
   if (e < 0 || e >= a.E) {
@@ -118,12 +117,12 @@ __global__ void __launch_bounds__(256) permute_kernel(dsca_permute_args a) {
                     : nullptr;
     for (int v = lane; v < nvec; v += 32) {
       const uint4 u = src[v];
-      const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);
+      const __nv_bfloat162* bb = reinterpret_cast<const __nv_bfloat162*>(&u);
       uint4 o;
       uint32_t* op = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const float2 f = __bfloat1622float2(b[i]);
+        const float2 f = __bfloat1622float2(bb[i]);
         __half2 h = __floats2half2_rn(f.x, f.y);
         op[i] = *reinterpret_cast<uint32_t*>(&h);
       }
@@ -144,10 +143,39 @@ __global__ void __launch_bounds__(256) permute_kernel(dsca_permute_args a) {
   }
 }
 
+template <int ESZ>
+__global__ void __launch_bounds__(256) permute_kernel(dsca_permute_args a) {
+  // a GEMM1 launched as a programmatic dependent may start its shared-expert tiles now; it
+  // waits for this grid before reading the permuted rows
+  pdl_launch_dependents();
+  const int lane = lane_id();
+  const int total = a.T * a.top_k;
+  const int nwarps = (int)(gridDim.x * (blockDim.x >> 5));
+  for (int w = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); w < total; w += nwarps)
+    permute_one<ESZ>(a, w, lane);
+}
+
 int launch_permute(const dsca_permute_args* a, cudaStream_t stream) {
   const long long warps = (long long)a->T * a->top_k;
   if (warps == 0) return DSCA_OK;
-  const int blocks = (int)((warps * 32 + 255) / 256);
+  static int num_sms = 0;
+  if (num_sms == 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return DSCA_ERR_CUDA;
+    // the SMs keep their full shared-memory carveout while the permute runs, so that the
+    // dependent GEMM's CTAs can be placed next to it
+    cudaFuncSetAttribute(permute_kernel<2>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                         (int)cudaSharedmemCarveoutMaxShared);
+    cudaFuncSetAttribute(permute_kernel<4>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                         (int)cudaSharedmemCarveoutMaxShared);
+    cudaGetLastError();
+  }
+  // two 256-thread CTAs per SM (46 registers a thread): resident together, with room left on every
+  // SM for one CTA of the dependent GEMM (192 threads, 123 registers, 197 KB shared memory)
+  const long long need = (warps * 32 + 255) / 256;
+  const int blocks = (int)(need < 2LL * num_sms ? need : 2LL * num_sms);
   if (a->dtype == DSCA_BF16)
     permute_kernel<2><<<blocks, 256, 0, stream>>>(*a);
   else
@@ -215,6 +243,7 @@ struct Vec8<float> {
 template <typename T, int KC>
 __global__ void __launch_bounds__(256) combine_kernel(dsca_combine_args a) {
   constexpr int KMAX = KC > 0 ? KC : DSCA_MAX_TOPK;
+  pdl_wait();  // launched as a programmatic dependent of GEMM2: its outputs are complete past here
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = lane_id();
   if (t >= a.T) return;
@@ -280,14 +309,32 @@ __global__ void __launch_bounds__(256) combine_kernel(dsca_combine_args a) {
 }
 
 
+template <typename T, int KC>
+static void launch_combine_k(const dsca_combine_args& a, int blocks, cudaStream_t stream) {
+  if (!a.pdl) {
+    combine_kernel<T, KC><<<blocks, 256, 0, stream>>>(a);
+    return;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)blocks);
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, combine_kernel<T, KC>, a);
+}
+
 template <typename T>
 static void launch_combine(const dsca_combine_args& a, int blocks, cudaStream_t stream) {
   switch (a.top_k) {
-    case 1: combine_kernel<T, 1><<<blocks, 256, 0, stream>>>(a); break;
-    case 2: combine_kernel<T, 2><<<blocks, 256, 0, stream>>>(a); break;
-    case 4: combine_kernel<T, 4><<<blocks, 256, 0, stream>>>(a); break;
-    case 8: combine_kernel<T, 8><<<blocks, 256, 0, stream>>>(a); break;
-    default: combine_kernel<T, 0><<<blocks, 256, 0, stream>>>(a); break;
+    case 1: launch_combine_k<T, 1>(a, blocks, stream); break;
+    case 2: launch_combine_k<T, 2>(a, blocks, stream); break;
+    case 4: launch_combine_k<T, 4>(a, blocks, stream); break;
+    case 8: launch_combine_k<T, 8>(a, blocks, stream); break;
+    default: launch_combine_k<T, 0>(a, blocks, stream); break;
   }
 }
 

@@ -51,6 +51,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = warp_id(), lane = lane_id();
   volatile int* abort_flag = &ctl.abort_flag;
+  pdl_launch_dependents();  // a programmatic dependent (GEMM2) may be scheduled as SMs free up
 
   // ---- prologue: barriers, TMEM, group tile table
   if (threadIdx.x == 0) {
@@ -93,12 +94,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       int pending_phase[kStages];
       for (int i = 0; i < kStages; ++i) pending_phase[i] = -1;
       bool ok = true;
+      bool seg0_ready = !p.pdl_seg0_wait;
       for (int r = 0; ok; ++r) {
         const int tile = sched_tile(r, (int)blockIdx.x, (int)gridDim.x);
         if (tile >= total) break;
         const TileInfo ti = decode<BM>(p, ctl, tile);
         const CUtensorMap* ma = ti.seg == 0 ? &tmA0 : &tmA1;
         const CUtensorMap* mb = ti.seg == 0 ? &tmB0 : &tmB1;
+        if (ti.seg == 0 && !seg0_ready) {
+          pdl_wait();  // the preceding kernel (the permute) has written the rows
+          seg0_ready = true;
+        }
         const int kb_n = p.seg[ti.seg].k_blocks;
         for (int kb = 0; kb < kb_n; ++kb) {
           if (!mbar_wait(smem_u32(&ctl.empty[s]), ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
@@ -289,13 +295,28 @@ template <int EPI>
 static int launch_kernel(const CUtensorMap& a0, const CUtensorMap& b0, const CUtensorMap& a1, const CUtensorMap& b1,
                          const gemm::Params& p, int grid, cudaStream_t stream) {
   static bool attr_set = false;
+  auto kern = gemm::grouped_gemm_kernel<EPI>;
   if (!attr_set) {
-    if (cudaFuncSetAttribute(gemm::grouped_gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             gemm::kSmemBytes) != cudaSuccess)
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::kSmemBytes) != cudaSuccess)
       return DSCA_ERR_CUDA;
     attr_set = true;
   }
-  gemm::grouped_gemm_kernel<EPI><<<grid, gemm::kThreads, gemm::kSmemBytes, stream>>>(a0, b0, a1, b1, p);
+  if (!p.pdl_seg0_wait) {
+    kern<<<grid, gemm::kThreads, gemm::kSmemBytes, stream>>>(a0, b0, a1, b1, p);
+    return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
+  }
+  // programmatic dependent of the permute: may start while it runs (see Params::pdl_seg0_wait)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(gemm::kThreads);
+  cfg.dynamicSmemBytes = gemm::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, a0, b0, a1, b1, p) != cudaSuccess) return DSCA_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
 }
 
@@ -353,7 +374,10 @@ int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t st
     p.epi = epi;
     p.err = f->err;
     p.nseg = shared ? 2 : 1;
-    p.seg_first = 0;  // equal K (the model width) in both segments
+    // equal K (the model width) in both segments; after a permute launched just before, the
+    // shared-expert tiles go first so that they overlap it (programmatic dependent launch)
+    p.pdl_seg0_wait = (f->pdl_after_permute && routed) ? 1 : 0;
+    p.seg_first = (p.pdl_seg0_wait && shared) ? 1 : 0;
     gemm::Segment& s0 = p.seg[0];
     s0.group_offsets = f->group_offsets;
     s0.group_weight = f->group_weight;

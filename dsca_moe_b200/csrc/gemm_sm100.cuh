@@ -43,6 +43,12 @@ struct Params {
   int epi;
   int32_t* err;
   ep::Ctx* ep_signal;  // set: signal the return flag at every peer once the grid is done
+  // launched as a programmatic dependent of the kernel that writes segment 0's A rows: the
+  // producer runs griddepcontrol.wait before its first segment-0 load
+  int pdl_seg0_wait;
+  // launched as a programmatic dependent of the kernel that writes both segments' A rows (GEMM2
+  // after GEMM1): the producer runs griddepcontrol.wait before its first load
+  int pdl_wait_all;
 };
 
 // A tile: token rows [row0, row0 + rows_valid) of group `group`, weight rows [b_row0, b_row0 + 256)

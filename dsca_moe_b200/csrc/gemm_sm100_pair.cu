@@ -73,6 +73,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = warp_id(), lane = lane_id();
   volatile int* abort_flag = &ctl.abort_flag;
   const uint32_t rank = cluster_ctarank();  // 0 = the CTA that issues the MMAs
+  pdl_launch_dependents();  // a programmatic dependent (the combine) may be scheduled early
   const int unit = (int)(blockIdx.x >> 1), units = (int)(gridDim.x >> 1);
 
   // ---- prologue: barriers, TMEM, tile schedule
@@ -117,6 +118,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int pending_phase[S];
       for (int i = 0; i < S; ++i) pending_phase[i] = -1;
       bool ok = true;
+      if (p.pdl_wait_all) pdl_wait();  // GEMM1, which wrote the A rows, has completed
       for (int r = 0; ok; ++r) {
         const int tile = sched_tile(r, unit, units);
         if (tile >= total) break;
@@ -311,13 +313,17 @@ static int launch_pair(const CUtensorMap& w0, const CUtensorMap& t0, const CUten
   cfg.blockDim = dim3(gemm::kThreads);
   cfg.dynamicSmemBytes = smem_bytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  if (p.pdl_wait_all) {  // programmatic dependent of the preceding kernel (see Params::pdl_wait_all)
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = p.pdl_wait_all ? 2 : 1;
   if (cudaLaunchKernelEx(&cfg, kern, w0, t0, w1, t1, p) != cudaSuccess) return DSCA_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
 }
@@ -439,6 +445,7 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
     p.nseg = shared ? 2 : 1;
     p.seg_first = (shared && f->shared_ip > f->ip) ? 1 : 0;  // the longer K first
     p.ep_signal = routed ? static_cast<ep::Ctx*>(f->ep_ctx) : nullptr;
+    p.pdl_wait_all = (f->pdl_after_permute && f->ep_ctx == nullptr) ? 1 : 0;  // right after GEMM1
     gemm::Segment& s0 = p.seg[0];
     s0.ep = static_cast<const ep::Ctx*>(f->ep_ctx);
     s0.group_offsets = f->group_offsets;

@@ -368,6 +368,9 @@ class MoEEngine:
         # bf16 expert GEMM tile form (dsca_ffn_args.tile_rows): 0 = default per GEMM,
         # 128 = single-CTA tiles, 256 = CTA-pair swap-AB tiles
         self.tile_rows = 0
+        # one GPU: GEMM1 launched as a programmatic dependent of the permute (shared-expert tiles
+        # overlap it; the routed tiles wait for it on the device)
+        self.pdl = True
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._done_counter = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._ws = {}
@@ -492,18 +495,21 @@ class MoEEngine:
         p.x_f16 = _ptr(ws.get("x_f16"))
         L.call("dsca_permute", ctypes.byref(p), _stream())
 
-    def _ffn(self, x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, ep_ctx=None):
+    def _ffn(self, x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, ep_ctx=None,
+             after_permute=False):
         if self.markers is not None:
             # time GEMM1 and GEMM2 as separate launches
-            self._ffn_call(x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, 1, ep_ctx)
+            self._ffn_call(x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, 1, ep_ctx,
+                           after_permute=after_permute)
             self._mark("gemm1")
             self._ffn_call(x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, 2, ep_ctx)
             self._mark("gemm2")
         else:
-            self._ffn_call(x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, 3, ep_ctx)
+            self._ffn_call(x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, 3, ep_ctx,
+                           after_permute=after_permute)
 
     def _ffn_call(self, x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, phases, ep_ctx=None,
-                  segments=3, num_ctas=None):
+                  segments=3, num_ctas=None, after_permute=False):
         pe = self.experts  # with an expert cache: w1 / w2 are the device slots
         f = L.FfnArgs()
         f.dtype, f.act, f.d = (L.F8E4M3 if pe.fp8 else _dt(self.dtype)), pe.act, self.d
@@ -522,10 +528,14 @@ class MoEEngine:
         f.tile_rows = self.tile_rows
         f.ep_ctx = _ptr(ep_ctx)
         f.segments = segments
+        # GEMM1 directly after the permute: its shared-expert tiles overlap the permute
+        f.pdl_after_permute = int(after_permute and self.pdl)
         L.call("dsca_grouped_ffn", ctypes.byref(f), _stream())
 
-    def _combine(self, ws, y, rows):
+    def _combine(self, ws, y, rows, after_ffn=False):
         c = L.CombineArgs()
+        # directly after dsca_grouped_ffn on this stream: a programmatic dependent of GEMM2
+        c.pdl = int(after_ffn and self.pdl)
         c.T, c.d, c.top_k, c.dtype = ws["out"].shape[0], self.d, self.top_k, _dt(self.dtype)
         c.y, c.token_row, c.topk_w = _ptr(y), _ptr(ws["token_row"]), _ptr(ws["topk_w"])
         c.ys, c.shared_gate = _ptr(ws["ys"]), _ptr(ws["shared_gate"])
@@ -561,8 +571,8 @@ class MoEEngine:
             cap = ws["a"].shape[0]
             self._permute(x, ws, ws["a"], cap)
             self._mark("permute")
-            self._ffn(x, ws, ws["a"], ws["h"], ws["y"], cap, self.E, ws["offsets"], None)
-            self._combine(ws, ws["y"], cap)
+            self._ffn(x, ws, ws["a"], ws["h"], ws["y"], cap, self.E, ws["offsets"], None, after_permute=True)
+            self._combine(ws, ws["y"], cap, after_ffn=self.markers is None)
             self._mark("combine")
             return ws
         return self._forward_ep(x, ws)

@@ -220,6 +220,11 @@ typedef struct {
                                  tile; 256 = a CTA pair (tcgen05 cta_group::2) per 256-channel x
                                  <=256-token tile, tokens rounded up to 16 only; 0 = default
                                  (pair for GEMM2 and ReLU GEMM1, single CTA for SwiGLU GEMM1) */
+  int pdl_after_permute;      /* 1: the call directly follows dsca_permute on the same stream (one
+                                 GPU): GEMM1 is launched as the permute's programmatic dependent
+                                 (with a shared expert its tiles go first and overlap the permute;
+                                 the routed tiles wait on the device for the permute), and GEMM2 as
+                                 GEMM1's (it waits for GEMM1's outputs before its first load) */
 } dsca_ffn_args;
 DSCA_API int dsca_grouped_ffn(const dsca_ffn_args* a, dsca_stream_t stream);
 
@@ -254,6 +259,9 @@ typedef struct {
   int rows;                   /* rows of y (bounds check) */
   void* out;                  /* [T, d] */
   int32_t* err;
+  int pdl;                    /* 1: the call directly follows dsca_grouped_ffn on the same stream;
+                                 the combine is launched as its programmatic dependent (its blocks
+                                 start early and wait on the device for GEMM2's outputs) */
 } dsca_combine_args;
 DSCA_API int dsca_combine(const dsca_combine_args* a, dsca_stream_t stream);
 

@@ -470,3 +470,55 @@ def test_tensor_core_router_qwen_block(cuda):
     assert np.array_equal(r["topk_w"].cpu().numpy().view(np.uint32), w.view(np.uint32))
     z = O.router_logits_fixed(x, p["s_gate_w"])[:, 0].astype(np.float64)
     assert np.abs(r["shared_gate"].cpu().numpy() - 1.0 / (1.0 + np.exp(-z))).max() < 1e-6
+
+
+@pytest.mark.parametrize("T,d,E,I,Is", [(4096, 2048, 60, 1408, 5632), (300, 256, 16, 128, 384)])
+def test_gemm1_overlapping_permute_is_bit_identical(cuda, T, d, E, I, Is):
+    """GEMM1 launched as a programmatic dependent of the permute (shared-expert tiles first,
+    routed tiles after griddepcontrol.wait) gives the serialized launch's output bit for bit."""
+    from dsca_moe_b200 import _lib as L
+    from dsca_moe_b200.engine import MoEEngine, pack_swiglu
+
+    x = syn.hidden_states(T, d, 501, "bf16")
+    Wg, _ = syn.router_weight(E, d, 502, zipf_s=1.5, dtype="bf16")
+    sgw = syn.bf16_round(syn.rng(504).standard_normal((1, d)).astype(np.float32) / np.sqrt(d))
+    w = _device_qwen_weights(E, d, I, Is, 503, cuda)
+    pe = pack_swiglu(w["gate"], w["up"], w["down"], shared=(w["s_gate"], w["s_up"], w["s_down"]),
+                     dtype=torch.bfloat16, device=cuda)
+    eng = MoEEngine(_t(Wg, torch.bfloat16, cuda), pe, top_k=4, route_mode=L.ROUTE_SOFTMAX_TOPK,
+                    shared_gate_weight=_t(sgw, torch.bfloat16, cuda))
+    xd = _t(x, torch.bfloat16, cuda)
+    outs = []
+    for pdl in (False, True, True):
+        eng.pdl = pdl
+        r = eng.forward(xd)
+        torch.cuda.synchronize()
+        eng.check()
+        outs.append(r["out"].clone())
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
+
+
+def test_switch_block_programmatic_launches_are_bit_identical(cuda):
+    """Switch layer (no shared expert: GEMM1 on CTA pairs, GEMM2 and the combine launched as
+    programmatic dependents) gives the serialized launches' output bit for bit."""
+    T, d, E, F = 4096, 768, 64, 3072
+    x = syn.hidden_states(T, d, 601, "bf16")
+    Wr, _ = syn.router_weight(E, d, 602, zipf_s=1.0, dtype="bf16")
+    g = torch.Generator(device=cuda)
+    g.manual_seed(603)
+    wi = (torch.randn(E, F, d, generator=g, device=cuda) * 0.02).to(torch.bfloat16)
+    wo = (torch.randn(E, d, F, generator=g, device=cuda) * 0.02).to(torch.bfloat16)
+    from dsca_moe_b200 import _lib as L
+    from dsca_moe_b200.engine import MoEEngine, pack_relu
+
+    eng = MoEEngine(_t(Wr, torch.bfloat16, cuda), pack_relu(wi, wo, device=cuda), top_k=1,
+                    route_mode=L.ROUTE_SWITCH_TOP1)
+    xd = _t(x, torch.bfloat16, cuda)
+    outs = []
+    for pdl in (False, True, True):
+        eng.pdl = pdl
+        r = eng.forward(xd)
+        torch.cuda.synchronize()
+        eng.check()
+        outs.append(r["out"].clone())
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
