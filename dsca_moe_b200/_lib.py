@@ -143,6 +143,8 @@ def load():
     lib.dsca_ep_region_free.argtypes = [_vp]
     lib.dsca_ep_return.argtypes = [_vp, _vp, _i, _i, _i, _vp, _vp]
     lib.dsca_combine.argtypes = [p(CombineArgs), _vp]
+    lib.dsca_qos_priority.argtypes = [p(QosArgs), _vp]
+    lib.dsca_router_pack_i8.argtypes = [_vp, _i, _i, _vp, _vp, _vp]
     lib.dsca_plan_harmony.argtypes = [_vp, _i, _i, _vp, _i, _vp]
     lib.dsca_plan_layout.argtypes = [_vp, _i, _i, _i, p(_i), _vp, _vp, _vp, _vp, _vp, _vp, _vp]
     lib.dsca_check_error.argtypes = [_vp, _vp]

@@ -46,6 +46,21 @@ def test_struct_layouts_match_header(lib):
         assert ctypes.sizeof(s) == c_size(s._fields_), s.__name__
 
 
+def test_qos_bad_args_rejected_without_gpu(lib):
+    from dsca_moe_b200 import _lib
+
+    assert lib.dsca_qos_priority(None, None) == _lib.ERR_BAD_ARG
+    q = _lib.QosArgs()
+    q.x = q.logits = q.topk_ids = q.token_score = q.expert_priority = 4096
+    q.T, q.d, q.E, q.top_k, q.dtype = 16, 64, 8, 2, _lib.BF16
+    q.attention_mode = 2
+    assert lib.dsca_qos_priority(ctypes.byref(q), None) == _lib.ERR_BAD_ARG
+    q.attention_mode, q.top_k = 0, 9
+    assert lib.dsca_qos_priority(ctypes.byref(q), None) == _lib.ERR_BAD_ARG
+    q.top_k, q.E = 2, 257
+    assert lib.dsca_qos_priority(ctypes.byref(q), None) == _lib.ERR_CAPACITY
+
+
 def test_bad_args_rejected_without_gpu(lib):
     from dsca_moe_b200 import _lib
 
@@ -61,6 +76,18 @@ def test_bad_args_rejected_without_gpu(lib):
     a.T = 0  # a valid empty call with all four set returns OK without launching
     a.block_base = a.done_counter = 4096
     assert lib.dsca_router_topk(ctypes.byref(a), None) == _lib.OK
+    # tensor-core logits: all five buffers or none, bf16 only (checked before any device call)
+    a.T = 32
+    a.w_slices = a.w_exp = a.x_slices = 4096
+    assert lib.dsca_router_topk(ctypes.byref(a), None) == _lib.ERR_BAD_ARG
+    a.x_exp = a.logits_f32 = 4096
+    a.dtype = _lib.F32
+    assert lib.dsca_router_topk(ctypes.byref(a), None) == _lib.ERR_BAD_ARG
+    assert lib.dsca_router_pack_i8(None, 8, 64, None, None, None) == _lib.ERR_BAD_ARG
+    assert lib.dsca_router_pack_i8(ctypes.c_void_p(4096), 65, 64, ctypes.c_void_p(4096), ctypes.c_void_p(4096),
+                                   None) == _lib.ERR_BAD_ARG  # more than 64 router rows
+    assert lib.dsca_router_pack_i8(ctypes.c_void_p(4096), 8, 60, ctypes.c_void_p(4096), ctypes.c_void_p(4096),
+                                   None) == _lib.ERR_BAD_ARG  # width not a multiple of 8
     assert lib.dsca_grouped_ffn(None, None) == _lib.ERR_BAD_ARG
     assert lib.dsca_plan_harmony(None, 2, 8, None, 150, None) == _lib.ERR_BAD_ARG
 
