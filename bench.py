@@ -640,6 +640,23 @@ def main():
         S, rows = eng.read_plan()
         counts = S[:, :, rank].sum(axis=0)
     e_touched = int((counts > 0).sum())
+    a2a = None
+    if world > 1:
+        # all-to-all volume of this rank (one row of d bf16 per routed assignment that crosses to
+        # another GPU) over the device time of the side-stream dispatch / return kernels
+        row_b = w["d"] * 2
+        out_rows = int(S[rank].sum() - S[rank, :, rank].sum())
+        in_rows = int(S[:, :, rank].sum() - S[rank, :, rank].sum())
+        t_disp = phase_ms.get("side_dispatch")
+        t_ret = phase_ms.get("side_return")
+        a2a = {"dispatch_bytes_out": out_rows * row_b, "dispatch_bytes_in": in_rows * row_b,
+               "return_bytes_out": in_rows * row_b, "return_bytes_in": out_rows * row_b,
+               "dispatch_ms": t_disp, "return_ms": t_ret,
+               "dispatch_gbs": (out_rows * row_b / (t_disp / 1e3) / 1e9) if t_disp else None,
+               "return_gbs": (in_rows * row_b / (t_ret / 1e3) / 1e9) if t_ret else None,
+               "peak_gbs": 770.0,
+               "peak_kind": "peer copy per direction measured on this pool's B200s (900 nominal)",
+               "note": "rank 0; dispatch and return run on a side stream beside the shared-expert GEMMs"}
     f_router, f_g1, f_g2, hbm = flops_and_bytes(w, T, rows, e_touched)
     # GEMM launches per step: gemm1 / gemm2 (one GPU) or their routed / shared halves (expert
     # parallel; the fused variant names its GEMM2 gemm2_fused)
@@ -737,7 +754,7 @@ def main():
                     "d2h_bytes_per_step": T * w["d"] * 2, "mode": e2e_mode, "serial_value": e2e_serial},
             "gpu_launches": launches_per_step(world, args.exchange, eng) * args.steps, "clocks": clk,
             "expert_cache": cache_info,
-            "phases_ms": phase_ms,
+            "phases_ms": phase_ms, "all_to_all": a2a,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
