@@ -5,7 +5,6 @@ import os
 import re
 
 import numpy as np
-import pytest
 
 from golden_io import json_fixture
 from oracle import oracle as O

@@ -11,7 +11,6 @@ transformers, their MoE blocks swapped for the CUDA block by replace_qosmoe_laye
 """
 import copy
 
-import numpy as np
 import pytest
 import torch
 

@@ -12,7 +12,6 @@ already run every other test.
 """
 import ctypes
 
-import numpy as np
 import pytest
 import torch
 
