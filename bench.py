@@ -32,7 +32,14 @@ import subprocess
 import sys
 import time
 
-import numpy as np
+if "reference" in sys.argv[sys.argv.index("--impl") + 1:][:1] if "--impl" in sys.argv else "--impl=reference" in sys.argv:
+    # the CPU arm gets every host thread: torchrun exports OMP_NUM_THREADS=1 to each rank, which
+    # numpy's BLAS would otherwise read when it loads below
+    _n = str(len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1))
+    for _v in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+        os.environ[_v] = _n
+
+import numpy as np  # noqa: E402
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
@@ -42,6 +49,10 @@ WORKLOADS = {
                  act="swiglu", zipf=1.5, T=4096),
     "switch": dict(name="switch-base-64 MoE layer forward", d=768, E=64, inter=3072, shared=0, k=1,
                    act="relu", zipf=1.0, T=4096),
+    # skew stress: the Qwen-shaped block on 16384 tokens per GPU, Zipf s = 1.5 (the hottest expert
+    # takes ~40 % of the top-1 choices), harmony plan migrating the hot experts' tokens
+    "qwen-skew": dict(name="qwen-shaped MoE block skew stress (16384 tokens/GPU, zipf 1.5)", d=2048, E=60,
+                      inter=1408, shared=5632, k=4, act="swiglu", zipf=1.5, T=16384),
 }
 # whole models through the plugin (one GPU): the transformers model with every MoE block swapped
 # by replace_qosmoe_layer, against the same model with transformers' own MoE blocks
@@ -89,6 +100,10 @@ def parse():
                     help="zipf: rows scaled for the workload's Zipf top-1 loads; uniform: unscaled N(0,1/d) router")
     ap.add_argument("--once", action="store_true",
                     help="one untimed forward of the workload and exit (the case profiled under ncu)")
+    ap.add_argument("--no-graph", dest="graph", action="store_false",
+                    help="launch every kernel from the host each step instead of replaying a CUDA graph")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the untimed correctness check after the timing")
     return ap.parse_args()
 
 
@@ -119,9 +134,9 @@ def launches_per_step(world, exchange, eng):
         # router (+ fused scan), permute, GEMM1, GEMM2, combine
         return 5 + (0 if eng.fuse_scan else 1)
     if exchange == "p2p":
-        # router, plan, dispatch, shared GEMM1, wait, routed GEMM1, routed GEMM2 (+ return kernel),
-        # shared GEMM2, wait, combine
-        return 10 + (1 if eng.ep_return == "overlap" else 0) + (0 if eng.fuse_scan else 1)
+        # router, plan, dispatch, shared GEMM1, wait, routed GEMM1, GEMM2 (routed and shared in one
+        # launch with the fused return; or routed GEMM2, return kernel, shared GEMM2), wait, combine
+        return 9 + (2 if eng.ep_return == "overlap" else 0) + (0 if eng.fuse_scan else 1)
     # router, permute into the send buffer, GEMM1, GEMM2, combine (NCCL does the exchange)
     return 5 + (0 if eng.fuse_scan else 1)
 
@@ -270,25 +285,53 @@ def build_block(w, T, rank, world, dev, eq_tokens, group=None, fp8=False, cache_
     return eng, x, Wr, raw, info
 
 
-def cpu_oracle_rate(w, Wr, raw_host, seconds, sample_tokens=256):
-    """Oracle port (routing in C, FFN in numpy fp32 BLAS) on a sample of the workload's tokens;
-    returns (tokens/s, threads, description)."""
-    from dsca_moe_b200 import synthetic as syn
+def host_threads() -> int:
+    """Host cores this process may run on."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+def blas_threads() -> int | None:
+    """Threads numpy's BLAS will use (threadpoolctl's view), or None if it cannot tell."""
+    try:
+        from threadpoolctl import threadpool_info
+
+        n = [i["num_threads"] for i in threadpool_info() if i.get("user_api") == "blas"]
+        return max(n) if n else None
+    except Exception:  # noqa: BLE001
+        return None
+
+
+def cpu_forward_fn(w, Wr, raw_host, x):
+    """One block forward of the oracle port on the host (routing in C, FFN in numpy fp32 BLAS)."""
     from oracle import oracle as O
 
+    if w["act"] == "swiglu":
+        return lambda: O.qwen_forward(x, Wr, raw_host, w["k"], False, "bf16", compute=np.float32)
+    return lambda: O.switch_forward(x, Wr, raw_host["wi"], raw_host["wo"], "bf16", compute=np.float32)
+
+
+def cpu_oracle_rate(w, Wr, raw_host, seconds, sample_tokens=256):
+    """Oracle port on a bounded sample of the workload's tokens, with every host thread; returns
+    (tokens/s, threads, description)."""
+    from threadpoolctl import threadpool_limits
+
+    from dsca_moe_b200 import synthetic as syn
+
     x = syn.hidden_states(sample_tokens, w["d"], 777, "bf16")
-    run = (lambda: O.qwen_forward(x, Wr, raw_host, w["k"], False, "bf16", compute=np.float32)) \
-        if w["act"] == "swiglu" else (lambda: O.switch_forward(x, Wr, raw_host["wi"], raw_host["wo"], "bf16",
-                                                               compute=np.float32))
-    run()  # warm-up
-    n, t0 = 0, time.perf_counter()
-    while True:
-        run()
-        n += 1
-        el = time.perf_counter() - t0
-        if el >= seconds or n >= 200:
-            break
-    threads = os.cpu_count()
+    with threadpool_limits(limits=host_threads(), user_api="blas"):
+        threads = blas_threads() or host_threads()
+        run = cpu_forward_fn(w, Wr, raw_host, x)
+        run()  # warm-up
+        n, t0 = 0, time.perf_counter()
+        while True:
+            run()
+            n += 1
+            el = time.perf_counter() - t0
+            if el >= seconds or n >= 200:
+                break
     return sample_tokens * n / el, threads, f"{n} x {sample_tokens} tokens of the workload ({el:.1f} s)"
 
 
@@ -301,14 +344,33 @@ def host_weights(raw):
     return out
 
 
+def run_config(args, w, T, world) -> dict:
+    """The workload description, identical in both arms' JSON lines."""
+    return {"workload": w["name"], "tokens_per_gpu": T, "batch_x_seq": "16x256" if T == 4096 else str(T),
+            "d_model": w["d"], "experts": w["E"], "expert_inter": w["inter"], "shared_inter": w["shared"],
+            "top_k": w["k"],
+            "router": (f"zipf{w['zipf']} (calibrated top-1)" if w["zipf"] else "uniform (unscaled)"),
+            "expert_weights": "fp8-e4m3 + per-channel fp32 scales" if args.fp8 else "bf16",
+            "placement": "contiguous (60 on 8 = 4x8 + 4x7)" if w["E"] % max(world, 1) else "contiguous",
+            "plan": f"harmony eq_tokens={args.eq_tokens}" if world > 1 else "local",
+            "l2": "flushed (256 MiB write, untimed) before every timed step",
+            "parallelism": f"ep{world}"}
+
+
 def run_reference(args, w, T):
+    """The reference's CPU path on the host cores: the oracle port of the block (routing in C in the
+    kernel's order, FFN in numpy fp32 BLAS) on whole steps of the workload — every step is the full
+    T-token forward, timed on the host clock — with every host thread.  Rank 0 alone runs it."""
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
     import torch
+    from threadpoolctl import threadpool_limits
 
     from dsca_moe_b200 import synthetic as syn
 
+    torch.set_num_threads(host_threads())
     E, d, I, Is = w["E"], w["d"], w["inter"], w["shared"]
     Wr, _ = syn.router_weight(E, d, 1234, zipf_s=w["zipf"], dtype="bf16")
     g = torch.Generator()
@@ -323,25 +385,29 @@ def run_reference(args, w, T):
                                                             / np.sqrt(d)))
     else:
         raw = dict(wi=n(E, I, d), wo=n(E, d, I))
-    sample = 256
-    per_step = max(args.cpu_seconds / max(args.steps, 1), 0.5)
-    for _ in range(args.warmup):
-        cpu_oracle_rate(w, Wr, raw, 0.0, sample)
-    rates = []
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        r, threads, desc = cpu_oracle_rate(w, Wr, raw, per_step, sample)
-        rates.append(r)
-    el = time.perf_counter() - t0
-    value = statistics.mean(rates)
+    x = syn.hidden_states(T, d, 5000, "bf16")
+    with threadpool_limits(limits=host_threads(), user_api="blas"):
+        threads = blas_threads() or host_threads()
+        run = cpu_forward_fn(w, Wr, raw, x)
+        for _ in range(args.warmup):
+            run()
+        step_s = []
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            run()
+            step_s.append(time.perf_counter() - t0)
+    el = sum(step_s)
+    ms = 1e3 * el / len(step_s)
+    value = T / (ms / 1e3)
     line = {"impl": "reference", "metric": "MoE-layer tokens/sec (max over ranks)", "value": value,
             "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1e3 * T / value, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": w["name"], "tokens_per_gpu": T, "router": f"zipf{w['zipf']}",
-                       "path": "oracle port of the reference path (routing C, FFN numpy fp32 BLAS) on host cores"},
-            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-                             "sample": f"{args.steps} steps x {sample}-token samples ({el:.1f} s)"},
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic", "config": run_config(args, w, T, world),
+            "reference_path": ("oracle port of the reference's block forward on the host cores: routing in C "
+                               "(the kernel's fixed order), expert FFNs in numpy fp32 BLAS; one process (rank 0)"),
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                             "sample": f"{args.steps} whole {T}-token steps ({el:.1f} s), after {args.warmup} "
+                                       f"warm-up steps"},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -467,6 +533,120 @@ def run_model(args):
     print(json.dumps(line), flush=True)
 
 
+def torch_block_fp32(eng, x, topk_ids, topk_w):
+    """The block computed in fp32 with torch on the GPU from the same bf16 inputs and weights and
+    the kernel's routing (ids and weights; the routing itself is bit-exact against the oracle in
+    the tests): the tolerance reference for a full-size output, every token checked."""
+    import torch
+
+    from dsca_moe_b200 import _lib as L
+    from dsca_moe_b200.engine import unpack_swiglu
+
+    pe = eng.experts
+    xf = x.float()
+    T, d = xf.shape
+    y = torch.zeros(T, d, dtype=torch.float32, device=x.device)
+    ids = topk_ids.long()
+    w = topk_w.float()
+    if pe.act == L.ACT_SWIGLU:
+        gate, up, down, shared = unpack_swiglu(pe)
+    else:
+        F = pe.inter
+    for e in range(pe.E):
+        t, j = (ids == e).nonzero(as_tuple=True)
+        if t.numel() == 0:
+            continue
+        xe = xf[t]
+        if pe.act == L.ACT_SWIGLU:
+            h = torch.nn.functional.silu(xe @ gate[e].T) * (xe @ up[e].T)
+            ye = h @ down[e].T
+        else:
+            h = torch.relu(xe @ pe.w1[e, :F].float().T)
+            ye = h @ pe.w2[e, :d, :F].float().T
+        y.index_add_(0, t, ye * w[t, j, None])
+    if pe.act == L.ACT_SWIGLU and shared is not None:
+        sg_w, su_w, sd_w = shared
+        sg = torch.sigmoid(xf @ eng.shared_gate_weight.float())
+        y += ((torch.nn.functional.silu(xf @ sg_w.T) * (xf @ su_w.T)) @ sd_w.T) * sg[:, None]
+    return y
+
+
+def rel_err(a, ref) -> float:
+    a, ref = a.float(), ref.float()
+    return float((a - ref).abs().max() / ref.abs().max().clamp_min(1e-30))
+
+
+def parity_check(eng, x, w, rank, world, dev, eq_tokens, graph=None):
+    """Untimed correctness check of the measured configuration, after the timing.
+
+    Every rank runs one more forward of its bench tokens through the measured engine and compares:
+      * with more than one GPU: routing (expert ids), per-expert counts and the output against the
+        same tokens through a one-GPU engine on the same packed weights (the world=1 result is
+        the oracle for G > 1; outputs are expected bit-identical), and the device harmony plan
+        S[G, E, G] against the host planner (dsca_plan_harmony, pinned to the reference
+        Scheduler's plans by the tests) on the all-gathered counts;
+      * the output against the block computed in fp32 by torch on every token (max|d|/max|ref|);
+      * with a CUDA graph: the replayed output against the eager forward (bit-identical).
+    Returns a dict; `ok` is the AND over all ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from dsca_moe_b200.engine import MoEEngine, plan_harmony
+
+    tol = 2e-2
+    res = {"tol_max_rel": tol}
+    r = eng.forward(x)
+    out, ids, counts = r["out"].clone(), r["topk_ids"].clone(), r["counts"].clone()
+    topk_w = r["topk_w"].clone()
+    torch.cuda.synchronize(dev)
+    eng.check()
+    ok = True
+    if graph is not None:
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        res["graph_equals_eager"] = bool(torch.equal(graph.out, out))
+        ok &= res["graph_equals_eager"]
+    if world > 1:
+        S_dev, recv_rows = eng.read_plan()
+        meta = torch.empty(world, eng.E, dtype=torch.int32, device=dev)
+        dist.all_gather_into_tensor(meta, counts)
+        S_host = plan_harmony(meta.cpu().numpy(), eng.expert_to_gpu, eq_tokens)
+        res["plan_equal"] = bool(np.array_equal(S_dev, S_host))
+        owner = np.asarray(eng.expert_to_gpu)
+        migrated = sum(int(S_dev[s_, e, g_]) for s_ in range(world) for e in range(eng.E) for g_ in range(world)
+                       if g_ != owner[e])
+        res["tokens_migrated"] = migrated
+        res["rows_received_here"] = int(recv_rows)
+        local = MoEEngine(eng.router_weight, eng.experts, top_k=eng.top_k, route_mode=eng.route_mode,
+                          norm_topk=eng.norm_topk, shared_gate_weight=eng.shared_gate_weight, device=dev)
+        lr = local.forward(x)
+        torch.cuda.synchronize(dev)
+        local.check()
+        res["routing_equal"] = bool(torch.equal(lr["topk_ids"], ids))
+        res["counts_equal"] = bool(torch.equal(lr["counts"], counts))
+        res["out_bit_identical_to_1gpu"] = bool(torch.equal(lr["out"], out))
+        res["max_rel_err_vs_1gpu"] = rel_err(out, lr["out"])
+        ok &= res["plan_equal"] and res["routing_equal"] and res["counts_equal"] and res["max_rel_err_vs_1gpu"] < tol
+        del local, lr
+    ref = torch_block_fp32(eng, x, ids, topk_w)
+    res["max_rel_err_fp32"] = rel_err(out, ref)
+    res["rows_checked"] = int(x.shape[0])
+    ok &= res["max_rel_err_fp32"] < tol
+    del ref
+    torch.cuda.empty_cache()
+    if world > 1:
+        t = torch.tensor([1.0 if ok else 0.0, res["max_rel_err_fp32"], res.get("max_rel_err_vs_1gpu", 0.0)],
+                         dtype=torch.float64, device=dev)
+        t[0] = -t[0]
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ok = bool(-t[0] > 0.5)
+        res["max_rel_err_fp32_all_ranks"] = float(t[1])
+        res["max_rel_err_vs_1gpu_all_ranks"] = float(t[2])
+        res["ranks"] = world
+    res["ok"] = ok
+    return res
+
+
 def main():
     args = parse()
     if args.workload in MODELS:
@@ -477,11 +657,16 @@ def main():
         run_model(args)
         return
     w = dict(WORKLOADS[args.workload])
+    if args.router == "uniform":
+        w["zipf"] = None
     T = args.tokens or w["T"]
     if args.impl == "reference":
         run_reference(args, w, T)
         return
+    run_ours(args, w, T)
 
+
+def run_ours(args, w, T):
     import torch
     import torch.distributed as dist
 
@@ -496,8 +681,6 @@ def main():
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
         group = dist.group.WORLD
-    if args.router == "uniform":
-        w["zipf"] = None
     if args.expert_cache and world > 1:
         raise SystemExit("--expert-cache runs on one GPU")
     eng, x, Wr, raw, info = build_block(w, T, rank, world, dev, args.eq_tokens, group, fp8=args.fp8,
@@ -513,6 +696,7 @@ def main():
         torch.cuda.synchronize()
         eng.check()
         if world > 1:
+            eng.close()
             dist.destroy_process_group()
         return
 
@@ -521,9 +705,23 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
+    # one host call per step: the forward captured as a CUDA graph (collective; every rank)
+    graph = None
+    graph_note = None
+    use_graph = args.graph and eng.cache is None and (world == 1 or args.exchange == "p2p")
+    if use_graph:
+        graph = eng.capture(x)
+        graph_note = "cuda graph replay (one host call per step)"
+
+    def step():
+        if graph is not None:
+            graph.replay()
+        else:
+            eng.forward(x)
+
     flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
     for _ in range(args.warmup):
-        eng.forward(x)
+        step()
     barrier()
     uuid = None
     try:
@@ -546,7 +744,7 @@ def main():
     for i in range(args.steps):
         flush.zero_()
         evs[i][0].record()
-        eng.forward(x)
+        step()
         evs[i][1].record()
     barrier()
     step_ms = [a.elapsed_time(b) for a, b in evs]
@@ -561,7 +759,24 @@ def main():
     value = T * world / (ms_per_step / 1e3)
     clk = clocks.stop() if local == 0 else None
 
-    # ---- per-kernel phases (separate profiled steps with event markers between launches)
+    # ---- host cost of one forward: time to enqueue it (eager: one ctypes call per kernel; graph:
+    #      one replay), measured without waiting for the device
+    host = {}
+    n_host = 10
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(n_host):
+        eng.forward(x)
+    host["eager_us_per_forward"] = (time.perf_counter() - t0) / n_host * 1e6
+    barrier()
+    if graph is not None:
+        t0 = time.perf_counter()
+        for _ in range(n_host):
+            graph.replay()
+        host["graph_us_per_replay"] = (time.perf_counter() - t0) / n_host * 1e6
+        barrier()
+
+    # ---- per-kernel phases (separate eager steps with event markers between launches)
     eng.markers = []
     eng.side_markers = []
     phase_ms = {}
@@ -590,22 +805,30 @@ def main():
     # (b) pipelined (the reported e2e): HostPipeline overlaps step i's forward with step i+1's H2D
     #     and step i-1's D2H; each step still copies its input in and its output out.  No flush
     #     between steps: a step's working set (the expert weights) is larger than L2.
+    from dsca_moe_b200.engine import HostPipeline
+
     x_host = x.cpu().pin_memory()
     outs_host = [torch.empty(T, w["d"], dtype=torch.bfloat16).pin_memory() for _ in range(2)]
-    x_dev = torch.empty_like(x)
+    x_dev = graph.x if graph is not None else torch.empty_like(x)
     for _ in range(2):
         x_dev.copy_(x_host, non_blocking=True)
-        outs_host[0].copy_(eng.forward(x_dev)["out"], non_blocking=True)
+        step()
+        outs_host[0].copy_(graph.out if graph is not None else eng.forward(x_dev)["out"], non_blocking=True)
     barrier()
     e_evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     for i in range(args.steps):
         flush.zero_()
         e_evs[i][0].record()
         x_dev.copy_(x_host, non_blocking=True)
-        r = eng.forward(x_dev)
-        outs_host[0].copy_(r["out"], non_blocking=True)
+        if graph is not None:
+            graph.replay()
+            out_dev = graph.out
+        else:
+            out_dev = eng.forward(x_dev)["out"]
+        outs_host[0].copy_(out_dev, non_blocking=True)
         e_evs[i][1].record()
     barrier()
+    x_dev.copy_(x)  # the graph's input buffer holds the bench tokens again
     e_tot = torch.tensor([sum(a.elapsed_time(b) for a, b in e_evs)], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(e_tot, op=dist.ReduceOp.MAX)
@@ -613,8 +836,9 @@ def main():
 
     e2e_mode = "pipelined (HostPipeline: step i+1 H2D and step i-1 D2H overlap step i)"
     if eng.cache is None:
-        from dsca_moe_b200.engine import HostPipeline
-        pipe = HostPipeline(eng, T)
+        pipe = HostPipeline(eng, T, graphs=graph is not None)
+        if graph is not None:
+            e2e_mode += "; each step one CUDA graph replay"
         xs = [x_host] * args.steps
         outs = [outs_host[i & 1] for i in range(args.steps)]
         pipe.run([x_host] * 2, outs_host)  # warm-up
@@ -628,9 +852,13 @@ def main():
         if world > 1:
             dist.all_reduce(p_tot, op=dist.ReduceOp.MAX)
         e2e_value = T * world / (float(p_tot.item()) / args.steps / 1e3)
+        del pipe
     else:
         # the cache path reads the plan on the host every step: no pipelining across steps
         e2e_value, e2e_mode = e2e_serial, "serial (expert-cache path: host plan per step)"
+
+    # ---- correctness of the measured configuration (untimed)
+    parity = parity_check(eng, x, w, rank, world, dev, args.eq_tokens, graph) if not args.no_parity else None
 
     # ---- roofline of the dominant kernel (grouped GEMM: GEMM1 + GEMM2 launches)
     if world == 1:
@@ -735,29 +963,24 @@ def main():
             "metric": "MoE-layer tokens/sec (max over ranks)", "value": value, "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic",
-            "config": {"workload": w["name"], "tokens_per_gpu": T, "batch_x_seq": "16x256" if T == 4096 else str(T),
-                       "d_model": w["d"], "experts": w["E"], "expert_inter": w["inter"], "shared_inter": w["shared"],
-                       "top_k": w["k"],
-                       "router": (f"zipf{w['zipf']} (calibrated top-1)" if w["zipf"] else "uniform (unscaled)"),
-                       "expert_weights": "fp8-e4m3 + per-channel fp32 scales (f16 MMA operands)" if args.fp8 else "bf16",
-                       "placement": "contiguous (60 on 8 = 4x8 + 4x7)" if w["E"] % max(world, 1) else "contiguous",
-                       "plan": f"harmony eq_tokens={args.eq_tokens}" if world > 1 else "local",
-                       "l2": "flushed (256 MiB write, untimed) before every timed step",
-                       "parallelism": f"ep{world}",
-                       "exchange": (f"{args.exchange} (return {args.ep_return})" if world > 1 else "none"),
-                       "gemm_tiles": {0: "GEMM1 128-token single-CTA tiles, GEMM2 CTA-pair swap-AB tiles",
-                                      128: "128-token single-CTA tiles",
-                                      256: "CTA-pair swap-AB tiles (256 channels x <=256 tokens)"}[args.tile_rows]},
+            "data": "synthetic", "config": run_config(args, w, T, world),
+            "implementation": {
+                "launch": graph_note or "eager (one host call per kernel)",
+                "exchange": (f"{args.exchange} (return {args.ep_return})" if world > 1 else "none"),
+                "gemm_tiles": {0: "GEMM1 128-token single-CTA tiles, GEMM2 CTA-pair swap-AB tiles",
+                               128: "128-token single-CTA tiles",
+                               256: "CTA-pair swap-AB tiles (256 channels x <=256 tokens)"}[args.tile_rows]},
             "roofline": roof, "layer_roofline": layer_roof, "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * w["d"] * 2,
                     "d2h_bytes_per_step": T * w["d"] * 2, "mode": e2e_mode, "serial_value": e2e_serial},
             "gpu_launches": launches_per_step(world, args.exchange, eng) * args.steps, "clocks": clk,
+            "parity": parity, "host": host,
             "expert_cache": cache_info,
             "phases_ms": phase_ms, "all_to_all": a2a,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
+        del graph
         eng.close()
         dist.barrier()
         dist.destroy_process_group()

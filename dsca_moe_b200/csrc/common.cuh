@@ -25,6 +25,39 @@ enum : int32_t {
 // Wait limit for every spin in these kernels (nanoseconds on %globaltimer).
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
+// One-time set-up per device (host side).  Kernel attributes such as the dynamic shared-memory
+// limit belong to a device's context, so a process that drives several GPUs must set them on
+// each; a launcher keeps one of these per attribute it sets.  Two threads that race on the
+// first call both run `f`, which is harmless for idempotent set-up.
+constexpr int kMaxDevices = 64;
+struct PerDeviceOnce {
+  volatile int done[kMaxDevices];
+  template <class F>
+  cudaError_t run(F&& f) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return f();
+    if (__atomic_load_n(&done[dev], __ATOMIC_ACQUIRE)) return cudaSuccess;
+    e = f();
+    if (e == cudaSuccess) __atomic_store_n(&done[dev], 1, __ATOMIC_RELEASE);
+    return e;
+  }
+};
+
+// The SM count of the current device (cached per device).
+inline int current_device_sms() {
+  static volatile int sms[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
+  int n = __atomic_load_n(&sms[dev], __ATOMIC_ACQUIRE);
+  if (n == 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    __atomic_store_n(&sms[dev], n, __ATOMIC_RELEASE);
+  }
+  return n;
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));

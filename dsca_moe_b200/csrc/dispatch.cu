@@ -158,20 +158,19 @@ __global__ void __launch_bounds__(256) permute_kernel(dsca_permute_args a) {
 int launch_permute(const dsca_permute_args* a, cudaStream_t stream) {
   const long long warps = (long long)a->T * a->top_k;
   if (warps == 0) return DSCA_OK;
-  static int num_sms = 0;
-  if (num_sms == 0) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-      return DSCA_ERR_CUDA;
-    // the SMs keep their full shared-memory carveout while the permute runs, so that the
-    // dependent GEMM's CTAs can be placed next to it
+  const int num_sms = current_device_sms();
+  if (num_sms == 0) return DSCA_ERR_CUDA;
+  // the SMs keep their full shared-memory carveout while the permute runs, so that the
+  // dependent GEMM's CTAs can be placed next to it
+  static PerDeviceOnce carveout_once;
+  carveout_once.run([] {
     cudaFuncSetAttribute(permute_kernel<2>, cudaFuncAttributePreferredSharedMemoryCarveout,
                          (int)cudaSharedmemCarveoutMaxShared);
     cudaFuncSetAttribute(permute_kernel<4>, cudaFuncAttributePreferredSharedMemoryCarveout,
                          (int)cudaSharedmemCarveoutMaxShared);
     cudaGetLastError();
-  }
+    return cudaSuccess;
+  });
   // two 256-thread CTAs per SM (46 registers a thread): resident together, with room left on every
   // SM for one CTA of the dependent GEMM (192 threads, 123 registers, 197 KB shared memory)
   const long long need = (warps * 32 + 255) / 256;

@@ -14,6 +14,8 @@
 // plain stores or the source of plain loads: no TMA and no multicast touches it.
 #include <string.h>
 
+#include <algorithm>
+
 #include "ep.cuh"
 
 namespace dsca {
@@ -287,17 +289,22 @@ __global__ void __launch_bounds__(256) plan_kernel(Ctx* c, const int32_t* counts
 }
 
 // ------------------------------------------------------------------ dispatch kernel
+// A resident grid (a few CTAs per SM): warp w copies the routed rows w, w + W, ... (W warps in
+// the grid), each one row of d elements with eight 16-byte loads in flight per lane; the last
+// CTA to finish raises the dispatch flag at every peer.  Few CTAs keep the per-CTA completion
+// fence (system scope) rare.
 template <int ESZ>
 __global__ void __launch_bounds__(256) dispatch_kernel(dsca_ep_dispatch_args a, Ctx* c) {
-  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
+  const int nwarps = (int)(gridDim.x * blockDim.x) >> 5;
   const int total = a.T * a.top_k;
-  if (w < total) {
+  const int G = c->G;
+  const size_t row_bytes = (size_t)a.d * ESZ;
+  for (int w = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); w < total; w += nwarps) {
     const int t = w / a.top_k;
     const int e = a.topk_ids[w];
-    const int G = c->G;
     bool ok = e >= 0 && e < c->E;
-    int dst = 0, q = 0, before = 0;
+    int dst = 0, q = 0;
     if (ok) {
       q = a.block_base[(size_t)(t / DSCA_ROUTER_TOKENS) * c->E + e] + a.local_rank[w];
       while (dst < G && q >= c->cum_split[e][dst]) ++dst;
@@ -305,34 +312,34 @@ __global__ void __launch_bounds__(256) dispatch_kernel(dsca_ep_dispatch_args a, 
     }
     if (!ok) {
       if (lane == 0) record_error(a.err, kErrIndex);
-    } else {
-      before = dst > 0 ? c->cum_split[e][dst - 1] : 0;
-      const int rrow = c->remote_base[e][dst] + (q - before);
-      const int srow = c->send_base[e][dst] + (q - before);
-      if (rrow < 0 || rrow >= c->recv_capacity || srow < 0 || srow >= c->ret_capacity) {
-        if (lane == 0) record_error(a.err, kErrCapacity);
-      } else {
-        if (lane == 0) a.token_row[w] = srow;
-        const size_t row_bytes = (size_t)a.d * ESZ;
-        const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(a.x) + (size_t)t * row_bytes);
-        uint4* dp = reinterpret_cast<uint4*>(c->recv[dst] + (size_t)rrow * row_bytes);
-        warp_copy_row(dp, src, (int)(row_bytes / 16), lane);
-      }
+      continue;
     }
+    const int before = dst > 0 ? c->cum_split[e][dst - 1] : 0;
+    const int rrow = c->remote_base[e][dst] + (q - before);
+    const int srow = c->send_base[e][dst] + (q - before);
+    if (rrow < 0 || rrow >= c->recv_capacity || srow < 0 || srow >= c->ret_capacity) {
+      if (lane == 0) record_error(a.err, kErrCapacity);
+      continue;
+    }
+    if (lane == 0) a.token_row[w] = srow;
+    const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(a.x) + (size_t)t * row_bytes);
+    uint4* dp = reinterpret_cast<uint4*>(c->recv[dst] + (size_t)rrow * row_bytes);
+    warp_copy_row(dp, src, (int)(row_bytes / 16), lane);
   }
   signal_when_grid_done(c, &c->dispatch_done, kDispatch);
 }
 
 // ------------------------------------------------------------------ return kernel
 // Row r of this rank's receive layout (expert e, chunk of source src) goes to row
-// ret_start[e][src] + (r - chunk_start[e][src]) of src's return buffer; one warp per row, so each
-// NVLink store instruction writes 512 contiguous bytes.  The last CTA sets the return flags.
+// ret_start[e][src] + (r - chunk_start[e][src]) of src's return buffer.  A resident grid: warp w
+// takes rows w, w + W, ..., one row at a time (each NVLink store instruction writes 512
+// contiguous bytes); the row count is read on the device.  The last CTA sets the return flags.
 template <int ESZ>
 __global__ void __launch_bounds__(256) return_kernel(Ctx* c, const char* y, int d, int32_t* err) {
-  const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
+  const int nwarps = (int)(gridDim.x * blockDim.x) >> 5;
   const int total = c->recv_total;
-  if (r < total) {
+  for (int r = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); r < total; r += nwarps) {
     // expert: upper bound over group_offsets
     int lo = 0, hi = c->E;
     while (hi - lo > 1) {
@@ -350,11 +357,10 @@ __global__ void __launch_bounds__(256) return_kernel(Ctx* c, const char* y, int 
     }
     if (dst == nullptr) {
       if (lane == 0) record_error(err, kErrIndex);
-    } else {
-      const uint4* s = reinterpret_cast<const uint4*>(y + (size_t)r * d * ESZ);
-      uint4* t = reinterpret_cast<uint4*>(dst);
-      warp_copy_row(t, s, d * ESZ / 16, lane);
+      continue;
     }
+    const uint4* s = reinterpret_cast<const uint4*>(y + (size_t)r * d * ESZ);
+    warp_copy_row(reinterpret_cast<uint4*>(dst), s, d * ESZ / 16, lane);
   }
   signal_when_grid_done(c, &c->return_done, kReturn);
 }
@@ -458,7 +464,11 @@ int dsca_ep_dispatch(const dsca_ep_dispatch_args* a, dsca_stream_t stream) {
   const int esz = a->dtype == DSCA_BF16 ? 2 : 4;
   if (((size_t)a->d * esz) % 16 != 0 || (reinterpret_cast<uintptr_t>(a->x) & 15u)) return DSCA_ERR_BAD_ARG;
   const long long warps = (long long)a->T * a->top_k;
-  const int blocks = (int)(warps > 0 ? (warps * 32 + 255) / 256 : 1);  // >= 1 CTA so the flag is still set
+  // >= 1 CTA so the flag is still set; at most kCtasPerSm resident CTAs per SM (grid-stride)
+  const int sms = dsca::current_device_sms();
+  if (sms == 0) return DSCA_ERR_CUDA;
+  const long long need = warps > 0 ? (warps * 32 + 255) / 256 : 1;
+  const int blocks = (int)std::min<long long>(need, (long long)dsca::ep::kCtasPerSm * sms);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (esz == 2)
     dsca::ep::dispatch_kernel<2><<<blocks, 256, 0, st>>>(*a, static_cast<Ctx*>(a->ctx));
@@ -472,8 +482,12 @@ int dsca_ep_return(void* ctx_dev, const void* y, int d, int dtype, int max_rows,
   if (dtype != DSCA_BF16 && dtype != DSCA_F32) return DSCA_ERR_BAD_ARG;
   const int esz = dtype == DSCA_BF16 ? 2 : 4;
   if (((size_t)d * esz) % 16 != 0 || (reinterpret_cast<uintptr_t>(y) & 15u)) return DSCA_ERR_BAD_ARG;
-  // one warp per possible row (the actual count is on the device); >= 1 CTA so the flag is set
-  const int blocks = max(1, (int)(((long long)max_rows * 32 + 255) / 256));
+  // the row count is on the device: a resident grid (grid-stride over the rows) sized for at
+  // most max_rows rows; >= 1 CTA so the flag is set
+  const int sms = dsca::current_device_sms();
+  if (sms == 0) return DSCA_ERR_CUDA;
+  const long long need = std::max(1LL, ((long long)max_rows * 32 + 255) / 256);
+  const int blocks = (int)std::min<long long>(need, (long long)dsca::ep::kCtasPerSm * sms);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (esz == 2)
     dsca::ep::return_kernel<2><<<blocks, 256, 0, st>>>(static_cast<Ctx*>(ctx_dev), static_cast<const char*>(y), d, err);

@@ -14,6 +14,7 @@ namespace dsca {
 namespace ep {
 
 constexpr int kMaxG = DSCA_MAX_GPUS;      // 8
+constexpr int kCtasPerSm = 2;             // resident CTAs per SM of the dispatch / return copy kernels
 constexpr int kMaxE = DSCA_MAX_EXPERTS;   // 64
 enum FlagKind { kCounts = 0, kDispatch = 1, kReturn = 2 };
 

@@ -11,7 +11,12 @@
 //   * every GPU that loads this library holds DSCA_STATIC_SCRATCH_BYTES (16 MiB) of device
 //     memory for the array until the process exits;
 //   * the first call on a device looks up the array's device address (cudaGetSymbolAddress)
-//     with that device current; make that first call before any stream capture;
+//     with that device current; make that first call before any stream capture.  The address
+//     is cached per device and per CUDA context (its unique id), so after a cudaDeviceReset the
+//     next call looks it up again in the new context;
+//   * bf16 (tcgen05) and f32 (CUDA cores) only: fp8-e4m3 weights and, for f32, the fused
+//     expert-parallel return (ep_ctx) are refused with DSCA_ERR_UNSUPPORTED, as
+//     dsca_grouped_ffn does for f32;
 //   * all calls share the one array: two calls whose work overlaps on the GPU (different
 //     streams, or different host threads on the same device) race on it and produce garbage;
 //     calls that are ordered on one stream are safe.  The array keeps the previous call's
@@ -30,17 +35,44 @@ namespace {
 
 static __device__ __align__(256) unsigned char g_ffn_scratch[DSCA_STATIC_SCRATCH_BYTES];
 
-constexpr int kMaxDevices = 64;
-void* g_scratch_addr[kMaxDevices] = {};
-int g_num_sms[kMaxDevices] = {};
-int g_major[kMaxDevices] = {};
+void* g_scratch_addr[dsca::kMaxDevices] = {};
+unsigned long long g_ctx_id[dsca::kMaxDevices] = {};
+int g_num_sms[dsca::kMaxDevices] = {};
+int g_major[dsca::kMaxDevices] = {};
 std::mutex g_setup_mutex;
 
-// Once per device, with that device current: the array's device address and the SM count.
+// Unique id of the current CUDA context (0 when it cannot be read): a context created after a
+// device reset gets a new id even if its handle value is reused.
+unsigned long long current_context_id() {
+  typedef CUresult (*GetCurrent)(CUcontext*);
+  typedef CUresult (*GetId)(CUcontext, unsigned long long*);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  if (get_current == nullptr || get_id == nullptr) {
+    void* p = nullptr;
+    void* q = nullptr;
+    cudaDriverEntryPointQueryResult r1, r2;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &r1) != cudaSuccess ||
+        r1 != cudaDriverEntryPointSuccess ||
+        cudaGetDriverEntryPoint("cuCtxGetId", &q, cudaEnableDefault, &r2) != cudaSuccess ||
+        r2 != cudaDriverEntryPointSuccess)
+      return 0;
+    get_current = reinterpret_cast<GetCurrent>(p);
+    get_id = reinterpret_cast<GetId>(q);
+  }
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr || get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+// Once per device and context, with that device current: the array's device address and the
+// SM count.
 int scratch_setup(int dev, void** addr, int* num_sms, int* major) {
-  if (dev < 0 || dev >= kMaxDevices) return DSCA_ERR_CUDA;
+  if (dev < 0 || dev >= dsca::kMaxDevices) return DSCA_ERR_CUDA;
   std::lock_guard<std::mutex> lock(g_setup_mutex);
-  if (g_scratch_addr[dev] == nullptr) {
+  const unsigned long long ctx_id = current_context_id();
+  if (g_scratch_addr[dev] == nullptr || ctx_id != g_ctx_id[dev]) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_ffn_scratch) != cudaSuccess || p == nullptr) return DSCA_ERR_CUDA;
     cudaDeviceProp prop;
@@ -48,6 +80,7 @@ int scratch_setup(int dev, void** addr, int* num_sms, int* major) {
     g_num_sms[dev] = prop.multiProcessorCount;
     g_major[dev] = prop.major;
     g_scratch_addr[dev] = p;
+    g_ctx_id[dev] = current_context_id();  // read again: the lookup may have created the context
   }
   *addr = g_scratch_addr[dev];
   *num_sms = g_num_sms[dev];
@@ -75,7 +108,9 @@ extern "C" int dsca_grouped_ffn_static_scratch(const dsca_ffn_args* a, dsca_stre
       (a->xs == nullptr || a->ws1 == nullptr || a->ws2 == nullptr || a->ys == nullptr || a->shared_n1p <= 0 ||
        a->shared_n1p % 256 != 0 || a->shared_ip != (glu ? a->shared_n1p / 2 : a->shared_n1p)))
     return DSCA_ERR_BAD_ARG;
+  if (a->dtype == DSCA_F8E4M3) return DSCA_ERR_UNSUPPORTED;  // fp8 weights: dsca_grouped_ffn only
   if (a->dtype != DSCA_BF16 && a->dtype != DSCA_F32) return DSCA_ERR_BAD_ARG;
+  if (a->dtype == DSCA_F32 && a->ep_ctx != nullptr) return DSCA_ERR_UNSUPPORTED;  // as dsca_grouped_ffn
   if (a->phases != 0 && a->phases != 3) return DSCA_ERR_BAD_ARG;  // GEMM2 needs this call's GEMM1
   const void* vec_ptrs[] = {a->a, a->w1, a->w2, a->y, a->xs, a->ws1, a->ws2, a->ys};
   for (const void* p : vec_ptrs)

@@ -294,13 +294,12 @@ int make_map_bf16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols
 template <int EPI>
 static int launch_kernel(const CUtensorMap& a0, const CUtensorMap& b0, const CUtensorMap& a1, const CUtensorMap& b1,
                          const gemm::Params& p, int grid, cudaStream_t stream) {
-  static bool attr_set = false;
+  static PerDeviceOnce attr_once;
   auto kern = gemm::grouped_gemm_kernel<EPI>;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::kSmemBytes) != cudaSuccess)
-      return DSCA_ERR_CUDA;
-    attr_set = true;
-  }
+  if (attr_once.run([&] {
+        return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::kSmemBytes);
+      }) != cudaSuccess)
+    return DSCA_ERR_CUDA;
   if (!p.pdl_seg0_wait) {
     kern<<<grid, gemm::kThreads, gemm::kSmemBytes, stream>>>(a0, b0, a1, b1, p);
     return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
@@ -422,7 +421,9 @@ int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t st
     p.epi = gemm::kEpiStore;
     p.err = f->err;
     p.nseg = shared ? 2 : 1;
-    p.seg_first = (shared && f->shared_ip > f->ip) ? 1 : 0;  // the longer K first
+    // the longer K first; with the fused return (ep_ctx) the routed tiles first, so that their
+    // NVLink stores drain while the shared-expert tiles compute
+    p.seg_first = (shared && f->shared_ip > f->ip && f->ep_ctx == nullptr) ? 1 : 0;
     p.ep_signal = routed ? static_cast<ep::Ctx*>(f->ep_ctx) : nullptr;
     gemm::Segment& s0 = p.seg[0];
     s0.ep = static_cast<const ep::Ctx*>(f->ep_ctx);

@@ -445,13 +445,12 @@ static int make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t co
 template <int EPI>
 static int launch8(const CUtensorMap& a0, const CUtensorMap& b0, const CUtensorMap& a1, const CUtensorMap& b1,
                    const gemm8::Params& p, int grid, cudaStream_t stream) {
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(gemm8::grouped_gemm_fp8_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             gemm8::kSmemBytes) != cudaSuccess)
-      return DSCA_ERR_CUDA;
-    attr = true;
-  }
+  static PerDeviceOnce attr_once;
+  if (attr_once.run([] {
+        return cudaFuncSetAttribute(gemm8::grouped_gemm_fp8_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    gemm8::kSmemBytes);
+      }) != cudaSuccess)
+    return DSCA_ERR_CUDA;
   gemm8::grouped_gemm_fp8_kernel<EPI><<<grid, gemm8::kThreads, gemm8::kSmemBytes, stream>>>(a0, b0, a1, b1, p);
   return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
 }

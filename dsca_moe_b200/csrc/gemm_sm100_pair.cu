@@ -300,14 +300,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int EPI>
 static int launch_pair(const CUtensorMap& w0, const CUtensorMap& t0, const CUtensorMap& w1, const CUtensorMap& t1,
                        const gemm::Params& p, int grid, cudaStream_t stream) {
-  static bool attr_set = false;
+  static PerDeviceOnce attr_once;
   constexpr int smem_bytes = gemm::pair::Cfg<EPI>::kSmemBytes;
   auto kern = gemm::pair::pair_gemm_kernel<EPI>;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) != cudaSuccess)
-      return DSCA_ERR_CUDA;
-    attr_set = true;
-  }
+  if (attr_once.run([&] {
+        return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+      }) != cudaSuccess)
+    return DSCA_ERR_CUDA;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3(gemm::kThreads);
@@ -330,7 +329,10 @@ static int launch_pair(const CUtensorMap& w0, const CUtensorMap& t0, const CUten
 
 // CTA pairs that can be resident at once (a cluster of two needs two free SMs of one GPC).
 static int max_resident_pairs(int num_sms) {
-  static int cached = -1;
+  static volatile int cache[kMaxDevices];  // pairs + 1 per device (0 = not yet queried)
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) dev = -1;
+  int cached = dev >= 0 ? __atomic_load_n(&cache[dev], __ATOMIC_ACQUIRE) - 1 : -1;
   if (cached < 0) {
     auto kern = gemm::pair::pair_gemm_kernel<gemm::kEpiSwiGLU>;
     constexpr int smem_bytes = gemm::pair::Cfg<gemm::kEpiSwiGLU>::kSmemBytes;
@@ -351,6 +353,7 @@ static int max_resident_pairs(int num_sms) {
     }
     cudaGetLastError();
     cached = n > 0 ? std::min(n, num_sms / 2) : num_sms / 2;
+    if (dev >= 0) __atomic_store_n(&cache[dev], cached + 1, __ATOMIC_RELEASE);
   }
   return cached;
 }
@@ -443,7 +446,9 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
     p.epi = gemm::kEpiStore;
     p.err = f->err;
     p.nseg = shared ? 2 : 1;
-    p.seg_first = (shared && f->shared_ip > f->ip) ? 1 : 0;  // the longer K first
+    // the longer K first; with the fused return (ep_ctx) the routed tiles first, so that their
+    // NVLink stores drain while the shared-expert tiles compute
+    p.seg_first = (shared && f->shared_ip > f->ip && f->ep_ctx == nullptr) ? 1 : 0;
     p.ep_signal = routed ? static_cast<ep::Ctx*>(f->ep_ctx) : nullptr;
     p.pdl_wait_all = (f->pdl_after_permute && f->ep_ctx == nullptr) ? 1 : 0;  // right after GEMM1
     gemm::Segment& s0 = p.seg[0];

@@ -454,7 +454,7 @@ __global__ void __launch_bounds__(kThreads, 1) router_kernel(Args a) {
 }  // namespace router
 
 int launch_router(const dsca_router_args* p, cudaStream_t stream, const float* logits_in) {
-  static bool attr_done[2] = {false, false};
+  static PerDeviceOnce attr_once[2];
   router::Args a;
   a.logits_in = logits_in;
   a.x = p->x;
@@ -483,19 +483,17 @@ int launch_router(const dsca_router_args* p, cudaStream_t stream, const float* l
   const int nblocks = (p->T + router::kTokens - 1) / router::kTokens;
   cudaError_t e = cudaSuccess;
   if (p->dtype == DSCA_BF16) {
-    if (!attr_done[0]) {
-      e = cudaFuncSetAttribute(router::router_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)router::kSmemBytes);
-      attr_done[0] = e == cudaSuccess;
-    }
+    e = attr_once[0].run([] {
+      return cudaFuncSetAttribute(router::router_kernel<__nv_bfloat16>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)router::kSmemBytes);
+    });
     if (e == cudaSuccess)
       router::router_kernel<__nv_bfloat16><<<nblocks, router::kThreads, router::kSmemBytes, stream>>>(a);
   } else {
-    if (!attr_done[1]) {
-      e = cudaFuncSetAttribute(router::router_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)router::kSmemBytes);
-      attr_done[1] = e == cudaSuccess;
-    }
+    e = attr_once[1].run([] {
+      return cudaFuncSetAttribute(router::router_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)router::kSmemBytes);
+    });
     if (e == cudaSuccess) router::router_kernel<float><<<nblocks, router::kThreads, router::kSmemBytes, stream>>>(a);
   }
   if (e != cudaSuccess) return DSCA_ERR_CUDA;

@@ -440,7 +440,7 @@ int launch_router_pack_i8(const void* rows, int R, int d, void* slices, int32_t*
 }
 
 int launch_router_tc(const dsca_router_args* a, cudaStream_t stream) {
-  static bool attr_done = false;
+  static PerDeviceOnce attr_once;
   const int T = a->T, d16 = (a->d + 15) & ~15;
   router_tc::slice_rows_kernel<<<(T + 7) / 8, 256, 0, stream>>>(reinterpret_cast<const uint16_t*>(a->x), T, a->d,
                                                                  d16, T, reinterpret_cast<int8_t*>(a->x_slices),
@@ -453,11 +453,10 @@ int launch_router_tc(const dsca_router_args* a, cudaStream_t stream) {
   if ((rc = make_map_u8(&mw01, a->w_slices, wrows, (uint64_t)d16, 2 * router_tc::kRows))) return rc;
   if ((rc = make_map_u8(&mw2, a->w_slices, wrows, (uint64_t)d16, router_tc::kRows))) return rc;
   auto kern = router_tc::router_mma_kernel;
-  if (!attr_done) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, router_tc::kSmemBytes) != cudaSuccess)
-      return DSCA_ERR_CUDA;
-    attr_done = true;
-  }
+  if (attr_once.run([&] {
+        return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, router_tc::kSmemBytes);
+      }) != cudaSuccess)
+    return DSCA_ERR_CUDA;
   router_tc::MmaArgs p;
   p.T = T;
   p.d16 = d16;

@@ -1,11 +1,14 @@
 """MoE-block forward engine: packed expert weights, workspace, and the kernel sequence.
 
-One GPU:   router -> scan -> permute -> grouped FFN (routed + shared) -> combine, all on the
-           caller's current stream with device-side counts (no host sync).
-G GPUs:    router -> scan -> counts all-gather -> harmony plan (host C++, identical on every
-           rank) -> permute into the plan's send layout -> chunk exchange (NCCL grouped
-           send/recv, landing expert-major) -> grouped FFN on the received rows (+ the shared
-           expert on local tokens) -> return exchange -> combine.
+One GPU:   router (+ fused scan) -> permute -> grouped FFN (routed + shared) -> combine, all on
+           the caller's current stream with device-side counts (no host sync).
+G GPUs:    (exchange="p2p", the default) router -> counts pushed to every peer and the harmony
+           plan computed on the device -> rows stored straight into the owners' receive buffers
+           over NVLink -> grouped FFN on the received rows (+ the shared expert on local tokens,
+           overlapping the exchange on a side stream) -> rows stored back into the senders'
+           return buffers -> combine; no host sync, so a forward can be captured as a CUDA
+           graph (MoEEngine.capture).  exchange="nccl": counts all-gather -> host plan -> NCCL
+           grouped send/recv of the chunks, kept as the library-collective baseline.
 
 Reference hot path: QoSMoELayer.forward (src/qosmoe/moe_layer.py:271-459) and
 ShardedQwenMoE.forward (qwen_ep_adapter/qwen_ep.py:44-97).  Every expert's weights are
@@ -24,7 +27,8 @@ import torch
 from . import _lib as L
 from .qos import ExpertCache, QoSInputs, build_exec_plan, match_token_length
 
-__all__ = ["PackedExperts", "pack_swiglu", "pack_relu", "MoEEngine", "plan_harmony", "plan_layout"]
+__all__ = ["PackedExperts", "pack_swiglu", "pack_relu", "MoEEngine", "ForwardGraph", "HostPipeline", "plan_harmony",
+           "plan_layout"]
 
 
 def _ptr(t):
@@ -851,22 +855,70 @@ class MoEEngine:
         """Synchronise and raise if a kernel recorded an error."""
         L.check(L.load().dsca_check_error(_ptr(self.err), _stream()), "device error word")
 
+    # -------------------------------------------------------------- CUDA graphs
+    def capture(self, x: torch.Tensor) -> "ForwardGraph":
+        """Capture one forward on the static input `x` [T, d] as a CUDA graph.  Every launch of a
+        forward is stream-ordered with device-side counts and plans (no host synchronisation), so
+        a replay re-runs the whole block — router, permute or expert-parallel exchange, grouped
+        GEMMs, combine — for whatever `x` holds at replay time, for one host call.  One eager
+        forward runs first so that set-up (workspace, symmetric region, kernel attributes) happens
+        outside the capture; with more than one rank every rank must capture at the same point
+        (the eager forward takes part in the exchange).  The expert-cache path (host-side plan per
+        forward) and the NCCL exchange (host-side plan) cannot be captured."""
+        if self.cache is not None or (self.world > 1 and self.exchange != "p2p"):
+            raise NotImplementedError("only the resident and the fused-exchange paths can be captured")
+        if x.dim() != 2 or x.shape[1] != self.d or x.dtype != self.dtype or x.device != self.device \
+                or not x.is_contiguous():
+            raise ValueError("capture needs a contiguous [T, d] input of the engine's dtype and device")
+        self.forward(x)
+        torch.cuda.synchronize(self.device)
+        graph = torch.cuda.CUDAGraph()
+        markers, self.markers = self.markers, None
+        try:
+            with torch.cuda.graph(graph):
+                res = self.forward(x)
+        finally:
+            self.markers = markers
+        return ForwardGraph(graph, x, res)
+
+
+class ForwardGraph:
+    """A captured MoEEngine.forward: `x` is the static input buffer (write the next batch into it),
+    replay() runs the block on the current stream and leaves the results in `result` (out, logits,
+    topk_ids, expert_index; overwritten by the next replay)."""
+
+    def __init__(self, graph, x: torch.Tensor, result: dict):
+        self.graph, self.x, self.result = graph, x, result
+
+    @property
+    def out(self) -> torch.Tensor:
+        return self.result["out"]
+
+    def replay(self):
+        self.graph.replay()
+
 
 class HostPipeline:
     """MoEEngine.forward over batches that live in pinned host memory, with the PCIe copies
     overlapped: while batch i computes on the current stream, batch i + 1 is copied in on one copy
     stream and batch i - 1's output is copied out on another.  Every batch still crosses PCIe both
-    ways; only the waiting overlaps (two device input buffers, event-ordered reuse)."""
+    ways; only the waiting overlaps (two device input buffers, event-ordered reuse).
 
-    def __init__(self, engine: "MoEEngine", tokens: int):
+    graphs=True captures the forward once per input buffer (MoEEngine.capture) and replays it:
+    one host call per batch instead of one per kernel, so the host keeps ahead of the GPU even
+    when many ranks share the host's cores.  Capture is collective across ranks (see capture)."""
+
+    def __init__(self, engine: "MoEEngine", tokens: int, graphs: bool = False):
         self.eng = engine
         dev = engine.device
-        self.x_dev = [torch.empty(tokens, engine.d, dtype=engine.dtype, device=dev) for _ in range(2)]
+        self.x_dev = [torch.zeros(tokens, engine.d, dtype=engine.dtype, device=dev) for _ in range(2)]
         self.h2d = torch.cuda.Stream(device=dev)
         self.d2h = torch.cuda.Stream(device=dev)
         self._copied = [torch.cuda.Event() for _ in range(2)]
         self._consumed = [torch.cuda.Event() for _ in range(2)]
+        self._drained = [torch.cuda.Event() for _ in range(2)]
         self._used = [False, False]
+        self.graphs = [engine.capture(xb) for xb in self.x_dev] if graphs else None
 
     def _copy_in(self, i, x_host):
         b = i & 1
@@ -892,7 +944,13 @@ class HostPipeline:
             if i + 1 < n:
                 self._copy_in(i + 1, xs_host[i + 1])
             main.wait_event(self._copied[b])
-            out = self.eng.forward(self.x_dev[b])["out"]
+            if self.graphs is not None:
+                if self._used[b]:
+                    main.wait_event(self._drained[b])  # this graph's last output has been copied out
+                self.graphs[b].replay()
+                out = self.graphs[b].out
+            else:
+                out = self.eng.forward(self.x_dev[b])["out"]
             self._consumed[b].record(main)
             self._used[b] = True
             done = torch.cuda.Event()
@@ -900,7 +958,10 @@ class HostPipeline:
             self.d2h.wait_event(done)
             with torch.cuda.stream(self.d2h):
                 outs_host[i].copy_(out, non_blocking=True)
-            out.record_stream(self.d2h)
+            if self.graphs is not None:
+                self._drained[b].record(self.d2h)
+            else:
+                out.record_stream(self.d2h)
         end = torch.cuda.Event()
         end.record(self.d2h)
         main.wait_event(end)

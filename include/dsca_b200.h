@@ -230,15 +230,17 @@ DSCA_API int dsca_grouped_ffn(const dsca_ffn_args* a, dsca_stream_t stream);
 
 /*
  * Grouped expert FFN for callers that cannot allocate device memory (no counterpart in the
- * reference).  Same arguments and results as dsca_grouped_ffn, except that `h` and `hs` must be
- * NULL: the GEMM1 intermediate lives in a fixed array inside this library, so a caller that
- * runs where cudaMalloc is unavailable or forbidden (inside a graph replay or a callback, or
- * under a foreign, already-full allocator) only passes its inputs and outputs.
+ * reference).  Same arguments and results as dsca_grouped_ffn for bf16 and f32, except that `h`
+ * and `hs` must be NULL: the GEMM1 intermediate lives in a fixed array inside this library, so a
+ * caller that runs where cudaMalloc is unavailable or forbidden (inside a graph replay or a
+ * callback, or under a foreign, already-full allocator) only passes its inputs and outputs.
+ * dtype DSCA_F8E4M3, and ep_ctx with DSCA_F32, return DSCA_ERR_UNSUPPORTED.
  * Limit: capacity * ip + shared_rows * shared_ip elements (plus 256-byte alignment of the first
  * part) must fit in DSCA_STATIC_SCRATCH_BYTES, else DSCA_ERR_CAPACITY; `phases` must be 0 or 3.
  * Every GPU that loads the library holds that many bytes until exit.  The first call on a device
- * looks the array up with that device current; make it before any stream capture.  All calls
- * share the array: calls that overlap on the GPU race; calls ordered on one stream are safe.
+ * (and the first after a device reset) looks the array up with that device current; make it
+ * before any stream capture.  All calls share the array: calls that overlap on the GPU race;
+ * calls ordered on one stream are safe.
  */
 #define DSCA_STATIC_SCRATCH_BYTES (16u << 20)
 DSCA_API int dsca_grouped_ffn_static_scratch(const dsca_ffn_args* a, dsca_stream_t stream);

@@ -2,8 +2,9 @@
 """Generate the golden fixtures in this directory by running the reference's own code on CPU.
 
 The reference (acbling/DSCA-MoE) is pure Python/PyTorch and hard-codes CUDA streams, events and
-``device="cuda"`` literals.  This script imports it from REFERENCE_ROOT (default /root/reference)
-behind a small shim that
+``device="cuda"`` literals.  This script imports it from the directory named by the environment
+variable REFERENCE_ROOT (required: the root of an acbling/DSCA-MoE checkout) behind a small shim
+that
   * replaces torch.cuda.Event / Stream / stream / default_stream with host no-ops,
   * makes nn.Module.cuda, Tensor.cuda and Tensor.pin_memory identities,
   * rewrites ``device="cuda"`` keyword arguments to the CPU (TorchFunctionMode),
@@ -19,7 +20,7 @@ and then calls, unmodified:
 The fixtures are small; inputs that are not stored are regenerated from the seeds recorded in
 each file by ``dsca_moe_b200.synthetic``.  Run from the repository root:
 
-    python tests/golden/make_golden.py
+    REFERENCE_ROOT=<path to the DSCA-MoE checkout> python tests/golden/make_golden.py
 """
 from __future__ import annotations
 
@@ -34,7 +35,9 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REFERENCE_ROOT = os.environ.get("REFERENCE_ROOT", "/root/reference")
+REFERENCE_ROOT = os.environ.get("REFERENCE_ROOT", "")
+if not REFERENCE_ROOT or not os.path.isdir(REFERENCE_ROOT):
+    raise SystemExit("set REFERENCE_ROOT to the root of the DSCA-MoE checkout")
 sys.path.insert(0, REPO)
 
 os.environ["QOSMOE_REAL_TOKEN_TRACE"] = "0"

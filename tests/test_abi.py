@@ -28,21 +28,80 @@ def test_header_symbols_exported(lib):
     assert lib.dsca_status_string(3) == b"device wait timed out"
 
 
-def test_struct_layouts_match_header(lib):
-    """ctypes mirrors of the argument structs have the C sizes (checked against offsets that
-    the C compiler computes for the same declarations)."""
+# C struct name -> ctypes mirror in dsca_moe_b200._lib
+_STRUCTS = {"dsca_router_args": "RouterArgs", "dsca_scan_args": "ScanArgs", "dsca_permute_args": "PermuteArgs",
+            "dsca_ffn_args": "FfnArgs", "dsca_combine_args": "CombineArgs", "dsca_qos_args": "QosArgs",
+            "dsca_ep_setup": "EpSetup", "dsca_ep_dispatch_args": "EpDispatchArgs"}
+
+
+def test_struct_layouts_match_c_compiler(tmp_path):
+    """Every ctypes mirror has the size and field offsets that the C compiler gives the header's
+    declarations: a small C program prints sizeof / offsetof of every field of every argument
+    struct, compiled with gcc against include/dsca_b200.h."""
+    import json
+    import shutil
+    import subprocess
+
+    import pytest
+
     from dsca_moe_b200 import _lib
 
-    # every struct is pointers and ints; recompute the C layout rule independently
-    def c_size(fields):
-        off = 0
-        for f in fields:
-            sz = 8 if f[1] is ctypes.c_void_p else 4
-            off = (off + sz - 1) // sz * sz + sz
-        return (off + 7) // 8 * 8
+    if shutil.which("gcc") is None:
+        pytest.skip("gcc not available")
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "dsca_b200.h"', "int main(void) {",
+             '  printf("{");']
+    first = True
+    for cname, pyname in _STRUCTS.items():
+        cls = getattr(_lib, pyname)
+        sep = "" if first else ","
+        first = False
+        lines.append(f'  printf("{sep}\\"{cname}\\": {{\\"size\\": %zu", sizeof({cname}));')
+        for fname, _ in cls._fields_:
+            lines.append(f'  printf(", \\"{fname}\\": %zu", offsetof({cname}, {fname}));')
+        lines.append('  printf("}");')
+    lines += ['  printf("}\\n");', "  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c11", "-Wall", "-Werror", "-I", os.path.join(ROOT, "include"), str(src), "-o",
+                    str(exe)], check=True)
+    got = json.loads(subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout)
+    for cname, pyname in _STRUCTS.items():
+        cls = getattr(_lib, pyname)
+        assert got[cname]["size"] == ctypes.sizeof(cls), cname
+        for fname, _ in cls._fields_:
+            assert got[cname][fname] == getattr(cls, fname).offset, (cname, fname)
 
-    for s in (_lib.RouterArgs, _lib.ScanArgs, _lib.PermuteArgs, _lib.FfnArgs, _lib.CombineArgs, _lib.QosArgs):
-        assert ctypes.sizeof(s) == c_size(s._fields_), s.__name__
+
+def _header_struct_members():
+    """{struct name: [member names in declaration order]} parsed from include/dsca_b200.h."""
+    src = open(os.path.join(ROOT, "include", "dsca_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", " ", src, flags=re.S)
+    out = {}
+    for body, name in re.findall(r"typedef struct \{(.*?)\}\s*(dsca_[a-z0-9_]+)\s*;", src, flags=re.S):
+        members = []
+        for stmt in body.split(";"):
+            stmt = " ".join(stmt.split())
+            if not stmt:
+                continue
+            # "type a, b[8], *c" -> a, b, c (the first word(s) are the type)
+            decl = re.sub(r"^(const\s+)?(unsigned\s+)?[A-Za-z_][A-Za-z0-9_]*\s*\**", "", stmt)
+            for part in decl.split(","):
+                m = re.match(r"\s*\**\s*([A-Za-z_][A-Za-z0-9_]*)", part)
+                members.append(m.group(1))
+        out[name] = members
+    return out
+
+
+def test_every_argument_struct_is_mirrored():
+    """The header declares no argument struct without a ctypes mirror, and every mirror lists the
+    C members in the C order (their offsets are checked above)."""
+    from dsca_moe_b200 import _lib
+
+    members = _header_struct_members()
+    assert set(members) == set(_STRUCTS), set(members) ^ set(_STRUCTS)
+    for cname, pyname in _STRUCTS.items():
+        assert [f for f, _ in getattr(_lib, pyname)._fields_] == members[cname], cname
 
 
 def test_qos_bad_args_rejected_without_gpu(lib):

@@ -11,6 +11,7 @@ import numpy as np
 import pytest
 import torch
 
+import torch_ref
 from golden_io import assert_logits_close, load, qwen_weights, routing_near_ties, switch_weights
 from oracle import oracle as O
 from dsca_moe_b200 import synthetic as syn
@@ -282,7 +283,8 @@ def _device_qwen_weights(E, d, I, Is, seed, dev):
 
 def test_qwen_full_size_bf16(cuda):
     """Qwen1.5-MoE-A2.7B block, 4096 tokens: routing bit-exact on every token, permutation a
-    bijection, output within 2e-2 of the fp32 oracle on a token sample."""
+    bijection, output within 2e-2 of the fp32 oracle on a token sample and of the fp32 torch
+    restatement on every token."""
     from dsca_moe_b200 import _lib as L
     from dsca_moe_b200.engine import MoEEngine, pack_swiglu
 
@@ -319,6 +321,13 @@ def test_qwen_full_size_bf16(cuda):
     p["s_gate_w"] = sgw
     y, *_ = O.qwen_forward(x[sample], Wg, p, k, False, "bf16")
     assert O.max_rel_err(_np(r["out"])[sample], y) < BF16_TOL
+    # every token against the fp32 torch restatement (routing from the kernel, checked above)
+    ref = torch_ref.qwen_block_fp32(_t(x, torch.bfloat16, cuda), r["topk_ids"], r["topk_w"], w,
+                                    _t(sgw, torch.bfloat16, cuda))
+    assert torch_ref.max_rel_err(r["out"], ref) < BF16_TOL
+    # per-row diagnostic: no token's output norm is off by more than 2 %
+    rn = (r["out"].float() - ref).norm(dim=1) / ref.norm(dim=1).clamp_min(1e-30)
+    assert float(rn.max()) < BF16_TOL
     # Zipf s=1.5: the hottest expert takes about 42 % of the top-1 choices
     assert 0.35 < np.mean(ids[:, 0] == 0) < 0.5
 
@@ -346,6 +355,9 @@ def test_switch_full_size_bf16(cuda):
     wi_h, wo_h = wi.float().cpu().numpy(), wo.float().cpu().numpy()
     y, *_ = O.switch_forward(x[sample], Wr, wi_h, wo_h, "bf16")
     assert O.max_rel_err(_np(r["out"])[sample], y) < BF16_TOL
+    # every token against the fp32 torch restatement (routing from the kernel, checked above)
+    ref = torch_ref.switch_block_fp32(_t(x, torch.bfloat16, cuda), r["expert_index"], r["topk_w"], wi, wo)
+    assert torch_ref.max_rel_err(r["out"], ref) < BF16_TOL
 
 
 def test_repeat_calls_are_deterministic(cuda):
@@ -421,6 +433,52 @@ def test_host_pipeline_matches_forward(cuda):
     for xh, oh in zip(xs, outs):
         ref = eng.forward(xh.to(cuda))["out"].cpu()
         assert torch.equal(oh, ref)
+
+
+def test_host_pipeline_with_graphs_matches_forward(cuda):
+    """HostPipeline replaying CUDA graphs of the forward (one per input buffer) returns, for every
+    batch, exactly what forward() returns for it."""
+    from dsca_moe_b200.engine import HostPipeline
+    T, d, E, I, Is, k = 300, 128, 16, 64, 128, 4
+    Wg, _ = syn.router_weight(E, d, 1352, zipf_s=1.2, dtype="bf16")
+    eng = qwen_engine(Wg, syn.qwen_expert_weights(E, d, I, Is, 1353, dtype="bf16"), k, False, torch.bfloat16, cuda)
+    xs = [torch.from_numpy(syn.hidden_states(T, d, 1360 + i, "bf16")).to(torch.bfloat16).pin_memory() for i in range(7)]
+    outs = [torch.empty(T, d, dtype=torch.bfloat16).pin_memory() for _ in range(7)]
+    HostPipeline(eng, T, graphs=True).run(xs, outs)
+    torch.cuda.synchronize()
+    eng.check()
+    for xh, oh in zip(xs, outs):
+        ref = eng.forward(xh.to(cuda))["out"].cpu()
+        assert torch.equal(oh, ref)
+
+
+@pytest.mark.parametrize("kind", ["qwen", "switch"])
+def test_graph_replay_matches_eager(cuda, kind):
+    """A forward captured as a CUDA graph (MoEEngine.capture) and replayed on new contents of its
+    input buffer gives the eager forward's results bit for bit: routing, counts and output."""
+    if kind == "qwen":
+        T, d, E, I, Is, k = 1000, 2048, 60, 256, 512, 4
+        Wg, _ = syn.router_weight(E, d, 1402, zipf_s=1.5, dtype="bf16")
+        eng = qwen_engine(Wg, syn.qwen_expert_weights(E, d, I, Is, 1403, dtype="bf16"), k, False, torch.bfloat16,
+                          cuda)
+    else:
+        T, d, E = 4096, 768, 64
+        Wr, _ = syn.router_weight(E, d, 1412, zipf_s=1.0, dtype="bf16")
+        wi, wo = syn.switch_expert_weights(E, d, 3072, 1413, dtype="bf16")
+        eng = switch_engine(Wr, wi, wo, torch.bfloat16, cuda)
+    xbuf = _t(syn.hidden_states(T, d, 1420, "bf16"), torch.bfloat16, cuda)
+    graph = eng.capture(xbuf)
+    for seed in (1421, 1422, 1421):
+        xn = _t(syn.hidden_states(T, d, seed, "bf16"), torch.bfloat16, cuda)
+        xbuf.copy_(xn)
+        graph.replay()
+        torch.cuda.synchronize()
+        got = {key: graph.result[key].clone() for key in ("out", "topk_ids", "logits", "expert_index")}
+        ref = eng.forward(xn)
+        torch.cuda.synchronize()
+        eng.check()
+        for key, v in got.items():
+            assert torch.equal(v, ref[key]), key
 
 
 @pytest.mark.parametrize("T,d,E", [(131, 72, 64), (300, 2048, 60), (5, 64, 8), (1, 128, 64)])
