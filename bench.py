@@ -86,9 +86,10 @@ def parse():
     ap.add_argument("--ep-return", choices=["overlap", "fused"], default="overlap")
     ap.add_argument("--ep-side-sms", type=int, default=0,
                     help="SMs left to the dispatch / return copy kernels beside the shared-expert GEMMs")
-    ap.add_argument("--tile-rows", type=int, choices=[0, 128, 256], default=0,
+    ap.add_argument("--tile-rows", type=int, choices=[0, 128, 256, 512], default=0,
                     help="bf16 expert GEMM tiles: 0 = default per GEMM, 256 = CTA pairs (cta_group::2, "
-                         "weights as M), 128 = one CTA per 128-token tile")
+                         "weights as M), 128 = one CTA per 128-token tile, 512 = CTA pairs with whole "
+                         "256-token blocks of the SwiGLU GEMM1 non-swapped (tokens as M)")
     ap.add_argument("--no-pdl", action="store_true",
                     help="one GPU: launch GEMM1 after the permute has finished (no programmatic dependent launch)")
     ap.add_argument("--expert-cache", type=int, default=0,
@@ -134,9 +135,10 @@ def launches_per_step(world, exchange, eng):
         # router (+ fused scan), permute, GEMM1, GEMM2, combine
         return 5 + (0 if eng.fuse_scan else 1)
     if exchange == "p2p":
-        # router, plan, dispatch, shared GEMM1, wait, routed GEMM1, GEMM2 (routed and shared in one
-        # launch with the fused return; or routed GEMM2, return kernel, shared GEMM2), wait, combine
-        return 9 + (2 if eng.ep_return == "overlap" else 0) + (0 if eng.fuse_scan else 1)
+        # router, plan, dispatch, wait, routed GEMM1, routed GEMM2, wait, combine; + the return
+        # kernel ("overlap"); + shared-expert GEMM1 and GEMM2
+        return (8 + (1 if eng.ep_return == "overlap" else 0) + (2 if eng.experts.ws1 is not None else 0)
+                + (0 if eng.fuse_scan else 1))
     # router, permute into the send buffer, GEMM1, GEMM2, combine (NCCL does the exchange)
     return 5 + (0 if eng.fuse_scan else 1)
 
@@ -887,7 +889,7 @@ def run_ours(args, w, T):
                "note": "rank 0; dispatch and return run on a side stream beside the shared-expert GEMMs"}
     f_router, f_g1, f_g2, hbm = flops_and_bytes(w, T, rows, e_touched)
     # GEMM launches per step: gemm1 / gemm2 (one GPU) or their routed / shared halves (expert
-    # parallel; the fused variant names its GEMM2 gemm2_fused)
+    # parallel; the fused return names its routed GEMM2 gemm2_routed_fused)
     t_g1 = sum(v for k, v in phase_ms.items() if k.startswith("gemm1")) or float("nan")
     t_g2 = sum(v for k, v in phase_ms.items() if k.startswith("gemm2")) or float("nan")
     achieved = (f_g1 + f_g2) / ((t_g1 + t_g2) / 1e3) / 1e12
@@ -969,7 +971,9 @@ def run_ours(args, w, T):
                 "exchange": (f"{args.exchange} (return {args.ep_return})" if world > 1 else "none"),
                 "gemm_tiles": {0: "GEMM1 128-token single-CTA tiles, GEMM2 CTA-pair swap-AB tiles",
                                128: "128-token single-CTA tiles",
-                               256: "CTA-pair swap-AB tiles (256 channels x <=256 tokens)"}[args.tile_rows]},
+                               256: "CTA-pair swap-AB tiles (256 channels x <=256 tokens)",
+                               512: "CTA-pair tiles: SwiGLU GEMM1 whole 256-token blocks non-swapped "
+                                    "(256 tokens x 128 channels), the rest swap-AB"}[args.tile_rows]},
             "roofline": roof, "layer_roofline": layer_roof, "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * w["d"] * 2,
                     "d2h_bytes_per_step": T * w["d"] * 2, "mode": e2e_mode, "serial_value": e2e_serial},

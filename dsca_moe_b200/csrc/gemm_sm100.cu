@@ -330,7 +330,7 @@ static int launch_one(int epi, const CUtensorMap& a0, const CUtensorMap& b0, con
 
 int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t stream) {
   const int phases_all = f->phases == 0 ? 3 : f->phases;
-  if (f->tile_rows == 256) return launch_grouped_ffn_bf16_pair(f, num_sms, stream);
+  if (f->tile_rows == 256 || f->tile_rows == 512) return launch_grouped_ffn_bf16_pair(f, num_sms, stream);
   if (f->tile_rows == 0) {
     // default: the CTA-pair swap-AB kernel for GEMM2 (and a ReLU GEMM1); single-CTA tiles for
     // the SwiGLU GEMM1, whose gate and up halves then sit in the same accumulator row

@@ -25,6 +25,7 @@ struct Segment {
   int ngroups;
   int rows;
   int n_tiles;                   // 256-wide blocks of weight rows per group
+  int n_full;                    // hybrid tiles (Params::hybrid): 128-channel blocks per full tile
   int b_rows_per_group;
   int k_blocks;
   __nv_bfloat16* c;
@@ -49,13 +50,51 @@ struct Params {
   // launched as a programmatic dependent of the kernel that writes both segments' A rows (GEMM2
   // after GEMM1): the producer runs griddepcontrol.wait before its first load
   int pdl_wait_all;
+  // CTA-pair SwiGLU GEMM1 only: every whole 256-token block of a group is one non-swapped tile
+  // (tokens as M = 256 over the pair, 128 channels' gate and up rows as N = 256, Segment::n_full
+  // blocks), the remaining < 256 tokens swap-AB tiles as usual
+  int hybrid;
 };
 
 // A tile: token rows [row0, row0 + rows_valid) of group `group`, weight rows [b_row0, b_row0 + 256)
 // (weight block n_blk of the group).
 struct TileInfo {
   int seg, group, row0, rows_valid, b_row0, n_blk;
+  int full;  // hybrid: a non-swapped 256-token tile (b_row0 = its 256-row [gate | up] block)
 };
+
+// Tiles of a group of `rows` token rows: ceil(rows / TBM) row tiles x n_tiles weight blocks, or
+// with hybrid tiles floor(rows / 256) x n_full full tiles plus the remainder's row tiles.
+template <int TBM>
+__device__ __forceinline__ int group_tiles(int rows, const Segment& sg, int hybrid) {
+  if (!hybrid) return ((rows + TBM - 1) / TBM) * sg.n_tiles;
+  const int full = rows / 256, rest = rows - 256 * full;
+  return full * sg.n_full + ((rest + TBM - 1) / TBM) * sg.n_tiles;
+}
+
+// Tile `l` of a group (rows rows starting at row_base, weights starting at weight row w_base).
+template <int TBM>
+__device__ __forceinline__ void decode_in_group(TileInfo& ti, int l, int rows, int row_base, int w_base,
+                                                const Segment& sg, int hybrid) {
+  const int full = hybrid ? rows / 256 : 0;
+  const int nf = full * sg.n_full;
+  if (l < nf) {
+    const int m_blk = l / sg.n_full;
+    ti.n_blk = l - m_blk * sg.n_full;
+    ti.full = 1;
+    ti.row0 = row_base + 256 * m_blk;
+    ti.rows_valid = 256;
+    ti.b_row0 = w_base + ti.n_blk * BN;
+    return;
+  }
+  l -= nf;
+  const int m_blk = l / sg.n_tiles;
+  ti.n_blk = l - m_blk * sg.n_tiles;
+  ti.full = 0;
+  ti.row0 = row_base + 256 * full + m_blk * TBM;
+  ti.rows_valid = min(TBM, rows - 256 * full - m_blk * TBM);
+  ti.b_row0 = w_base + ti.n_blk * BN;
+}
 
 // Destination row pointer of a routed output row in the expert-parallel return path.
 __device__ __forceinline__ __nv_bfloat16* ep_return_row(const ep::Ctx* c, int e, int r, int ldc) {
@@ -107,7 +146,7 @@ __device__ __forceinline__ void build_group_table(const Params& p, SmemCtl& ctl,
       record_error(p.err, kErrCapacity);
       rows_g = 0;
     }
-    run += ((rows_g + TBM - 1) / TBM) * sg.n_tiles;
+    run += group_tiles<TBM>(rows_g, sg, p.hybrid);
   }
   int incl = run;
 #pragma unroll
@@ -120,14 +159,14 @@ __device__ __forceinline__ void build_group_table(const Params& p, SmemCtl& ctl,
     ctl.tile_start[g] = excl;
     int rows_g = max(0, ctl.goff[g + 1] - ctl.goff[g]);
     if (ctl.goff[g + 1] > sg.capacity) rows_g = 0;
-    excl += ((rows_g + TBM - 1) / TBM) * sg.n_tiles;
+    excl += group_tiles<TBM>(rows_g, sg, p.hybrid);
   }
   int total0 = __shfl_sync(0xffffffffu, incl, 31);
   if (lane == 0) {
     ctl.tile_start[ng] = total0;
     ctl.seg0_tiles = total0;
     int total1 = 0;
-    if (p.nseg > 1) total1 = ((p.seg[1].rows + TBM - 1) / TBM) * p.seg[1].n_tiles;
+    if (p.nseg > 1) total1 = group_tiles<TBM>(p.seg[1].rows, p.seg[1], p.hybrid);
     ctl.seg1_tiles = total1;
     ctl.total_tiles = total0 + total1;
   }
@@ -156,24 +195,14 @@ __device__ __forceinline__ TileInfo decode(const Params& p, const SmemCtl& s, in
       if (s.tile_start[mid] <= local) lo = mid; else hi = mid;
     }
     const int g = lo;
-    const int l = local - s.tile_start[g];
-    const int m_blk = l / sg.n_tiles;
-    ti.n_blk = l - m_blk * sg.n_tiles;
-    const int rows_g = s.goff[g + 1] - s.goff[g];
     ti.seg = 0;
     ti.group = g;
-    ti.row0 = s.goff[g] + m_blk * TBM;
-    ti.rows_valid = min(TBM, rows_g - m_blk * TBM);
-    ti.b_row0 = s.gw[g] * sg.b_rows_per_group + ti.n_blk * BN;
+    decode_in_group<TBM>(ti, local - s.tile_start[g], s.goff[g + 1] - s.goff[g], s.goff[g],
+                         s.gw[g] * sg.b_rows_per_group, sg, p.hybrid);
   } else {
-    const Segment& sg = p.seg[1];
-    const int m_blk = local / sg.n_tiles;
-    ti.n_blk = local - m_blk * sg.n_tiles;
     ti.seg = 1;
     ti.group = 0;
-    ti.row0 = m_blk * TBM;
-    ti.rows_valid = min(TBM, sg.rows - ti.row0);
-    ti.b_row0 = ti.n_blk * BN;
+    decode_in_group<TBM>(ti, local, p.seg[1].rows, 0, 0, p.seg[1], p.hybrid);
   }
   return ti;
 }

@@ -119,10 +119,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; i < S; ++i) pending_phase[i] = -1;
       bool ok = true;
       if (p.pdl_wait_all) pdl_wait();  // GEMM1, which wrote the A rows, has completed
+      bool seg0_ready = !p.pdl_seg0_wait;
       for (int r = 0; ok; ++r) {
         const int tile = sched_tile(r, unit, units);
         if (tile >= total) break;
         const TileInfo ti = decode<TBN>(p, ctl, tile);
+        if (ti.seg == 0 && !seg0_ready) {
+          pdl_wait();  // the preceding kernel (the permute) has written the routed rows
+          seg0_ready = true;
+        }
         const CUtensorMap* mw = ti.seg == 0 ? &tmW0 : &tmW1;
         const CUtensorMap* mt = ti.seg == 0 ? &tmT0 : &tmT1;
         const int half = tile_n(ti.rows_valid) / 2;
@@ -134,14 +139,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int w_row = C::kGlu ? ti.b_row0 + ti.n_blk * BN + 256 * (int)rank : ti.b_row0 + 128 * (int)rank;
         const int t_row = ti.row0 + half * (int)rank;
         const int kb_n = p.seg[ti.seg].k_blocks;
+        // hybrid full tile (SwiGLU): this CTA's 128 tokens (two 64-row token boxes into slot A)
+        // and the gate (even CTA) or up (odd CTA) rows of the tile's 128 channels (slot A2)
+        const bool full = C::kGlu && ti.full;
+        const int f_trow = ti.row0 + 128 * (int)rank, f_wrow = ti.b_row0 + 128 * (int)rank;
+        constexpr uint32_t tx_full = 2u * (uint32_t)(C::kABytes + C::kA2Bytes);
         for (int kb = 0; kb < kb_n; ++kb) {
           if (!mbar_wait(smem_u32(&ctl.empty[s]), ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
           const uint32_t fb = smem_u32(&ctl.full[s]);
           const uint32_t fb0 = mapa_shared(fb, 0);  // the even CTA's full barrier
-          if (rank == 0) mbar_arrive_expect_tx(fb, tx);
-          tma_load_2d_pair(smem_a + s * C::kABytes, mw, fb0, kb * BK, w_row);
-          if constexpr (C::kGlu) tma_load_2d_pair(smem_a2 + s * C::kA2Bytes, mw, fb0, kb * BK, w_row + 128);
-          tma_load_2d_pair(smem_t + s * C::kTBytes, mt, fb0, kb * BK, t_row);
+          if (full) {
+            if (rank == 0) mbar_arrive_expect_tx(fb, tx_full);
+            tma_load_2d_pair(smem_a + s * C::kABytes, mt, fb0, kb * BK, f_trow);
+            tma_load_2d_pair(smem_a + s * C::kABytes + C::kABytes / 2, mt, fb0, kb * BK, f_trow + 64);
+            tma_load_2d_pair(smem_a2 + s * C::kA2Bytes, mw, fb0, kb * BK, f_wrow);
+          } else {
+            if (rank == 0) mbar_arrive_expect_tx(fb, tx);
+            tma_load_2d_pair(smem_a + s * C::kABytes, mw, fb0, kb * BK, w_row);
+            if constexpr (C::kGlu) tma_load_2d_pair(smem_a2 + s * C::kA2Bytes, mw, fb0, kb * BK, w_row + 128);
+            tma_load_2d_pair(smem_t + s * C::kTBytes, mt, fb0, kb * BK, t_row);
+          }
           pending_phase[s] = (int)ph;
           if (++s == S) { s = 0; ph ^= 1u; }
         }
@@ -165,7 +182,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int tile = sched_tile(r, unit, units);
         if (tile >= total) break;
         const TileInfo ti = decode<TBN>(p, ctl, tile);
-        const uint32_t idesc = idesc_m | ((uint32_t)(tile_n(ti.rows_valid) >> 3) << 17);
+        const bool full = C::kGlu && ti.full;
+        const uint32_t idesc = full ? idesc_bf16_f32(256, 256)
+                                    : (idesc_m | ((uint32_t)(tile_n(ti.rows_valid) >> 3) << 17));
         const int acc = it & 1;
         const uint32_t acc_ph = (uint32_t)((it >> 1) & 1);
         if (!mbar_wait(smem_u32(&ctl.tmem_empty[acc]), acc_ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
@@ -177,13 +196,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint64_t adesc = sw128_kmajor_desc(smem_a + s * C::kABytes);
           const uint64_t tdesc = sw128_kmajor_desc(smem_t + s * C::kTBytes);
+          if (full) {
+            // tokens (slot A, M = 256 over the pair) x [gate | up] rows of 128 channels (slot
+            // A2, N = 256 over the pair): TMEM lane = token, columns 0-127 gate, 128-255 up
+            const uint64_t wdesc = sw128_kmajor_desc(smem_a2 + s * C::kA2Bytes);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
-            umma_f16_pair(d_tmem, adesc + (uint64_t)(2 * k), tdesc + (uint64_t)(2 * k), idesc, accum);
-            if constexpr (C::kGlu) {
-              const uint64_t udesc = sw128_kmajor_desc(smem_a2 + s * C::kA2Bytes);
-              umma_f16_pair(d_tmem + 128, udesc + (uint64_t)(2 * k), tdesc + (uint64_t)(2 * k), idesc, accum);
+            for (int k = 0; k < BK / 16; ++k)
+              umma_f16_pair(d_tmem, adesc + (uint64_t)(2 * k), wdesc + (uint64_t)(2 * k), idesc,
+                            (kb > 0 || k > 0) ? 1u : 0u);
+          } else {
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k) {
+              const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+              umma_f16_pair(d_tmem, adesc + (uint64_t)(2 * k), tdesc + (uint64_t)(2 * k), idesc, accum);
+              if constexpr (C::kGlu) {
+                const uint64_t udesc = sw128_kmajor_desc(smem_a2 + s * C::kA2Bytes);
+                umma_f16_pair(d_tmem + 128, udesc + (uint64_t)(2 * k), tdesc + (uint64_t)(2 * k), idesc, accum);
+              }
             }
           }
           const uint32_t eb = smem_u32(&ctl.empty[s]);
@@ -223,6 +252,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!w_ok) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * 256);
+      if (C::kGlu && ti.full) {
+        // hybrid full tile: TMEM lane = this CTA's token 32 q + lane, columns 0-127 gate and
+        // 128-255 up of channels 128 n_blk + [0, 128): each lane stores its row's 64-byte pieces
+        const size_t row = (size_t)(ti.row0 + 128 * (int)rank + q * 32 + lane);
+        __nv_bfloat16* crow = sg.c + row * (size_t)sg.ldc;
+        const int col0 = ti.n_blk * 128;
+#pragma unroll 1
+        for (int c = 0; c < 128; c += 32) {
+          uint32_t g[32], u[32];
+          tmem_ld32(taddr + c, g);
+          tmem_ld32(taddr + 128 + c, u);
+          tmem_wait_ld();
+          uint32_t packed[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            packed[i] = pack_bf16x2(silu(__uint_as_float(g[2 * i])) * __uint_as_float(u[2 * i]),
+                                    silu(__uint_as_float(g[2 * i + 1])) * __uint_as_float(u[2 * i + 1]));
+          const int col = col0 + c;
+          if (col < sg.n_store) {
+            uint4* dst = reinterpret_cast<uint4*>(crow + col);
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              if (col + v * 8 < sg.n_store)
+                dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(empty_bar[acc]);
+        continue;
+      }
       const int ntok = ti.rows_valid;
       const int ncol = tile_n(ntok);
       // this warp's 32 output channels: SwiGLU channel block n_blk (256 channels per pair);
@@ -317,12 +377,13 @@ static int launch_pair(const CUtensorMap& w0, const CUtensorMap& t0, const CUten
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  if (p.pdl_wait_all) {  // programmatic dependent of the preceding kernel (see Params::pdl_wait_all)
+  const bool pdl = p.pdl_wait_all || p.pdl_seg0_wait;
+  if (pdl) {  // programmatic dependent of the preceding kernel (see Params::pdl_wait_all / pdl_seg0_wait)
     attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[1].val.programmaticStreamSerializationAllowed = 1;
   }
   cfg.attrs = attr;
-  cfg.numAttrs = p.pdl_wait_all ? 2 : 1;
+  cfg.numAttrs = pdl ? 2 : 1;
   if (cudaLaunchKernelEx(&cfg, kern, w0, t0, w1, t1, p) != cudaSuccess) return DSCA_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
 }
@@ -398,7 +459,12 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
     p.epi = epi;
     p.err = f->err;
     p.nseg = shared ? 2 : 1;
-    p.seg_first = 0;  // equal K (the model width) in both segments
+    // tile_rows 512 (SwiGLU): whole 256-token blocks as non-swapped tiles, the rest swap-AB
+    p.hybrid = (glu && f->tile_rows == 512) ? 1 : 0;
+    // equal K (the model width) in both segments; right after the permute (one GPU, hybrid
+    // tiles) the shared-expert tiles go first and overlap it (programmatic dependent launch)
+    p.pdl_seg0_wait = (p.hybrid && f->pdl_after_permute && routed) ? 1 : 0;
+    p.seg_first = (p.pdl_seg0_wait && shared) ? 1 : 0;
     gemm::Segment& s0 = p.seg[0];
     s0.group_offsets = f->group_offsets;
     s0.group_weight = f->group_weight;
@@ -406,6 +472,7 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
     s0.rows = 0;
     // SwiGLU: a tile covers 256 output channels (gate and up rows of them); others 256 rows
     s0.n_tiles = glu ? (f->ip + gemm::BN - 1) / gemm::BN : f->n1p / gemm::BN;
+    s0.n_full = glu ? f->ip / 128 : 0;
     s0.b_rows_per_group = f->n1p;
     s0.k_blocks = (f->d + gemm::BK - 1) / gemm::BK;
     s0.c = reinterpret_cast<__nv_bfloat16*>(f->h);
@@ -419,6 +486,7 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
       s1.ngroups = 1;
       s1.rows = f->shared_rows;
       s1.n_tiles = glu ? (f->shared_ip + gemm::BN - 1) / gemm::BN : f->shared_n1p / gemm::BN;
+      s1.n_full = glu ? f->shared_ip / 128 : 0;
       s1.b_rows_per_group = f->shared_n1p;
       s1.k_blocks = (f->d + gemm::BK - 1) / gemm::BK;
       s1.c = reinterpret_cast<__nv_bfloat16*>(f->hs);
@@ -451,6 +519,7 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
     p.seg_first = (shared && f->shared_ip > f->ip && f->ep_ctx == nullptr) ? 1 : 0;
     p.ep_signal = routed ? static_cast<ep::Ctx*>(f->ep_ctx) : nullptr;
     p.pdl_wait_all = (f->pdl_after_permute && f->ep_ctx == nullptr) ? 1 : 0;  // right after GEMM1
+    p.hybrid = 0;
     gemm::Segment& s0 = p.seg[0];
     s0.ep = static_cast<const ep::Ctx*>(f->ep_ctx);
     s0.group_offsets = f->group_offsets;

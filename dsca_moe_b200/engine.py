@@ -719,10 +719,13 @@ class MoEEngine:
             bytes=total)
 
     def _forward_p2p(self, x, ws):
-        """Main stream: shared GEMM1 -> [dispatch done] routed GEMM1 -> routed GEMM2 -> shared
-        GEMM2 -> [return done] combine.  Side stream: plan and dispatch (beside the shared GEMM1)
-        and the return kernel (beside the shared GEMM2).  ep_return = "fused" instead stores
-        GEMM2's routed rows straight into the source ranks from its epilogue."""
+        """ep_return = "overlap": main stream shared GEMM1 -> [dispatch done] routed GEMM1 ->
+        routed GEMM2 -> shared GEMM2 -> [return done] combine; side stream: plan and dispatch
+        (beside the shared GEMM1) and the return kernel (beside the shared GEMM2).
+        ep_return = "fused": main stream shared GEMM1 -> shared GEMM2 -> [dispatch done] routed
+        GEMM1 -> routed GEMM2 whose epilogue stores every output row straight into the return
+        buffer of the rank that sent it (the return all-to-all fused into the GEMM, tile by tile)
+        -> [return done] combine; side stream: plan and dispatch beside both shared GEMMs."""
         T = x.shape[0]
         if self._ep is None:
             self._p2p_setup(T)
@@ -755,14 +758,17 @@ class MoEEngine:
         if has_shared:
             self._ffn_call(*args, 1, segments=2, num_ctas=side_ctas)
             self._mark("gemm1_shared")
+            if self.ep_return == "fused":
+                self._ffn_call(*args, 2, segments=2, num_ctas=side_ctas)
+                self._mark("gemm2_shared")
         main.wait_event(dispatched)
         L.check(lib.dsca_ep_wait(ctx, 1, self.wait_limit_ns, err, _stream()), "dsca_ep_wait")
         self._mark("wait_dispatch")
         self._ffn_call(*args, 1, segments=1)
         self._mark("gemm1_routed")
         if self.ep_return == "fused":
-            self._ffn_call(*args, 2, ep_ctx=ep["ctx"], segments=3)
-            self._mark("gemm2_fused")
+            self._ffn_call(*args, 2, ep_ctx=ep["ctx"], segments=1)
+            self._mark("gemm2_routed_fused")
         else:
             self._ffn_call(*args, 2, segments=1)
             self._mark("gemm2_routed")

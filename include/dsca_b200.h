@@ -218,8 +218,11 @@ typedef struct {
   const float* ws2_scale;
   int tile_rows;              /* bf16 path tile form: 128 = one CTA per 128-token x 256-channel
                                  tile; 256 = a CTA pair (tcgen05 cta_group::2) per 256-channel x
-                                 <=256-token tile, tokens rounded up to 16 only; 0 = default
-                                 (pair for GEMM2 and ReLU GEMM1, single CTA for SwiGLU GEMM1) */
+                                 <=256-token tile, tokens rounded up to 16 only; 512 = CTA pairs,
+                                 and in a SwiGLU GEMM1 every whole 256-token block of a group is
+                                 one non-swapped tile (256 tokens x the gate and up rows of 128
+                                 channels), the rest as in 256; 0 = default (pair for GEMM2 and
+                                 ReLU GEMM1, single CTA for SwiGLU GEMM1) */
   int pdl_after_permute;      /* 1: the call directly follows dsca_permute on the same stream (one
                                  GPU): GEMM1 is launched as the permute's programmatic dependent
                                  (with a shared expert its tiles go first and overlap the permute;

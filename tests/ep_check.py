@@ -22,7 +22,7 @@ sys.path.insert(0, ROOT)
 
 from dsca_moe_b200 import _lib as L  # noqa: E402
 from dsca_moe_b200 import synthetic as syn  # noqa: E402
-from dsca_moe_b200.engine import MoEEngine, pack_relu, pack_swiglu  # noqa: E402
+from dsca_moe_b200.engine import MoEEngine, pack_relu, pack_swiglu, plan_harmony  # noqa: E402
 
 
 def rel(a, b):
@@ -75,7 +75,7 @@ def main():
     results = []
     uneven60 = np.array([min(world - 1, (e * world * world) // (60 * (world + 1))) for e in range(60)], np.int32)
     cases = []
-    for exchange in ("p2p", "p2p-fused", "nccl"):
+    for exchange in ("p2p", "p2p-fused", "p2p-graph", "nccl"):
         cases += [
             (f"qwen contiguous, harmony, {exchange}", case_qwen, None, 150, exchange),
             (f"qwen contiguous, fixed, {exchange}", case_qwen, None, -1, exchange),
@@ -86,8 +86,20 @@ def main():
     for name, fn, e2g, eq, exchange in cases:
         ep, one, x = fn(rank, world, dev, group, e2g, eq, "nccl" if exchange == "nccl" else "p2p")
         ep.ep_return = "fused" if exchange == "p2p-fused" else "overlap"
+        graph = None
+        if exchange == "p2p-graph":
+            # the forward captured once (collective), replayed on new contents of its input buffer
+            xbuf = x.clone()
+            graph = ep.capture(xbuf)
         for it in range(3):
-            r_ep = ep.forward(x)
+            if graph is not None:
+                x = torch.from_numpy(syn.hidden_states(x.shape[0], x.shape[1], 900 + 10 * it + rank, "bf16")).to(
+                    dev, torch.bfloat16)
+                xbuf.copy_(x)
+                graph.replay()
+                r_ep = graph.result
+            else:
+                r_ep = ep.forward(x)
             r_one = one.forward(x)
             torch.cuda.synchronize()
             ep.check()
@@ -97,10 +109,16 @@ def main():
             exact = torch.equal(r_ep["out"], r_one["out"])
             S, _ = ep.read_plan()
             migrated = int(S.sum() - sum(S[:, e, ep.expert_to_gpu[e]].sum() for e in range(S.shape[1])))
-            good = same_route and err < 2e-2 and torch.isfinite(r_ep["out"].float()).all().item()
+            # the plan the devices computed equals the host planner's on the all-gathered counts
+            meta = torch.empty(world, ep.E, dtype=torch.int32, device=dev)
+            dist.all_gather_into_tensor(meta, r_one["counts"].contiguous())
+            plan_ok = bool(np.array_equal(S, plan_harmony(meta.cpu().numpy(), ep.expert_to_gpu, eq)))
+            good = same_route and plan_ok and err < 2e-2 and torch.isfinite(r_ep["out"].float()).all().item()
             ok &= bool(good)
             results.append({"case": name, "iter": it, "rank": rank, "routing_equal": bool(same_route),
-                            "max_rel_err": err, "bit_identical": bool(exact), "tokens_migrated": migrated})
+                            "plan_equal": plan_ok, "max_rel_err": err, "bit_identical": bool(exact),
+                            "tokens_migrated": migrated})
+        del graph
         ep.close()
     flag = torch.tensor([1 if ok else 0], device=dev)
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)

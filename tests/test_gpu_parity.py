@@ -395,18 +395,20 @@ def test_fused_scan_matches_separate_scan(cuda, T, k, E):
         assert torch.equal(got[1][kk], got[2][kk]), kk
 
 
-@pytest.mark.parametrize("T,d,E,I,Is,k", [(600, 256, 60, 128, 512, 4), (257, 128, 8, 64, 256, 2)])
+@pytest.mark.parametrize("T,d,E,I,Is,k", [(600, 256, 60, 128, 512, 4), (257, 128, 8, 64, 256, 2),
+                                           (1100, 512, 8, 384, 640, 2)])
 def test_single_cta_and_pair_tiles_agree(cuda, T, d, E, I, Is, k):
-    """The 128-row single-CTA tiles and the 256-row CTA-pair tiles give the same block output
-    (both accumulate each output element over K in the same order, so bf16 results match),
-    and both stay within the bf16 tolerance of the fp32 oracle."""
+    """The 128-row single-CTA tiles, the 256-row CTA-pair swap-AB tiles and the hybrid pair tiles
+    (whole 256-token blocks non-swapped, the rest swap-AB) give the same block output (every form
+    accumulates each output element over K in the same order, so bf16 results match), and all
+    stay within the bf16 tolerance of the fp32 oracle."""
     x = syn.hidden_states(T, d, 1201, "bf16")
     Wg, _ = syn.router_weight(E, d, 1202, zipf_s=1.5, dtype="bf16")
     p = syn.qwen_expert_weights(E, d, I, Is, 1203, dtype="bf16")
     eng = qwen_engine(Wg, p, k, False, torch.bfloat16, cuda)
     xd = _t(x, torch.bfloat16, cuda)
     outs = []
-    for rows in (128, 256):
+    for rows in (128, 256, 512):
         eng.tile_rows = rows
         r = eng.forward(xd)
         torch.cuda.synchronize()
@@ -416,6 +418,38 @@ def test_single_cta_and_pair_tiles_agree(cuda, T, d, E, I, Is, k):
     for o in outs:
         assert O.max_rel_err(o, y) < BF16_TOL
     assert np.abs(outs[0] - outs[1]).max() <= 1e-2 * max(1.0, np.abs(outs[1]).max())
+    assert np.abs(outs[0] - outs[2]).max() <= 1e-2 * max(1.0, np.abs(outs[2]).max())
+
+
+def test_hybrid_pair_tiles_full_size(cuda):
+    """Qwen1.5-MoE-A2.7B block, 4096 tokens (Zipf 1.5: the hot expert spans several whole
+    256-token blocks), hybrid CTA-pair GEMM1 tiles: every token within 2e-2 of the fp32 torch
+    restatement, and equal to the single-CTA tiles' output within bf16 rounding."""
+    from dsca_moe_b200 import _lib as L
+    from dsca_moe_b200.engine import MoEEngine, pack_swiglu
+
+    T, d, E, I, Is, k = 4096, 2048, 60, 1408, 5632, 4
+    x = syn.hidden_states(T, d, 811, "bf16")
+    Wg, _ = syn.router_weight(E, d, 812, zipf_s=1.5, dtype="bf16")
+    sgw = syn.bf16_round(syn.rng(814).standard_normal((1, d)).astype(np.float32) / np.sqrt(d))
+    w = _device_qwen_weights(E, d, I, Is, 813, cuda)
+    pe = pack_swiglu(w["gate"], w["up"], w["down"], shared=(w["s_gate"], w["s_up"], w["s_down"]),
+                     dtype=torch.bfloat16, device=cuda)
+    eng = MoEEngine(_t(Wg, torch.bfloat16, cuda), pe, top_k=k, route_mode=L.ROUTE_SOFTMAX_TOPK,
+                    shared_gate_weight=_t(sgw, torch.bfloat16, cuda))
+    xd = _t(x, torch.bfloat16, cuda)
+    outs = {}
+    for rows in (128, 512, 512):
+        eng.tile_rows = rows
+        r = eng.forward(xd)
+        torch.cuda.synchronize()
+        eng.check()
+        outs.setdefault(rows, []).append(r["out"].clone())
+    assert torch.equal(outs[512][0], outs[512][1])
+    ref = torch_ref.qwen_block_fp32(xd, r["topk_ids"], r["topk_w"], w, _t(sgw, torch.bfloat16, cuda))
+    assert torch_ref.max_rel_err(outs[512][0], ref) < BF16_TOL
+    assert torch_ref.max_rel_err(outs[512][0], outs[128][0]) < 1e-2
+    assert int(r["counts"].max()) >= 512  # the hot expert has whole 256-token blocks
 
 
 def test_host_pipeline_matches_forward(cuda):
