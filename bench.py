@@ -90,6 +90,9 @@ def parse():
                     help="bf16 expert GEMM tiles: 0 = default per GEMM, 256 = CTA pairs (cta_group::2, "
                          "weights as M), 128 = one CTA per 128-token tile, 512 = CTA pairs with whole "
                          "256-token blocks of the SwiGLU GEMM1 non-swapped (tokens as M)")
+    ap.add_argument("--tile-order", type=int, choices=[0, 1], default=0,
+                    help="routed and shared tiles of one GEMM launch: 0 = interleaved, 1 = one segment "
+                         "after the other")
     ap.add_argument("--no-pdl", action="store_true",
                     help="one GPU: launch GEMM1 after the permute has finished (no programmatic dependent launch)")
     ap.add_argument("--expert-cache", type=int, default=0,
@@ -690,6 +693,7 @@ def run_ours(args, w, T):
     eng.exchange = args.exchange
     eng.ep_return = args.ep_return
     eng.tile_rows = args.tile_rows
+    eng.tile_order = args.tile_order
     eng.ep_side_sms = args.ep_side_sms
     eng.pdl = not args.no_pdl
     peaks = load_peaks()
@@ -973,7 +977,8 @@ def run_ours(args, w, T):
                                128: "128-token single-CTA tiles",
                                256: "CTA-pair swap-AB tiles (256 channels x <=256 tokens)",
                                512: "CTA-pair tiles: SwiGLU GEMM1 whole 256-token blocks non-swapped "
-                                    "(256 tokens x 128 channels), the rest swap-AB"}[args.tile_rows]},
+                                    "(256 tokens x 128 channels), the rest swap-AB"}[args.tile_rows],
+                "tile_order": ["routed and shared tiles interleaved", "one segment after the other"][args.tile_order]},
             "roofline": roof, "layer_roofline": layer_roof, "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * w["d"] * 2,
                     "d2h_bytes_per_step": T * w["d"] * 2, "mode": e2e_mode, "serial_value": e2e_serial},

@@ -50,6 +50,11 @@ struct Params {
   // launched as a programmatic dependent of the kernel that writes both segments' A rows (GEMM2
   // after GEMM1): the producer runs griddepcontrol.wait before its first load
   int pdl_wait_all;
+  // two segments: -1 = all of seg_first's tiles, then the other segment's; >= 0 = this many of
+  // seg_first's tiles first, then the two segments' remaining tiles interleaved in proportion
+  // to their counts, so that at any time some SMs run the routed experts' tiles (which stream
+  // every expert's weights from HBM) while the others run the shared expert's (tensor bound)
+  int interleave_lead;
   // CTA-pair SwiGLU GEMM1 only: every whole 256-token block of a group is one non-swapped tile
   // (tokens as M = 256 over the pair, 128 channels' gate and up rows as N = 256, Segment::n_full
   // blocks), the remaining < 256 tokens swap-AB tiles as usual
@@ -179,13 +184,30 @@ template <int TBM>
 __device__ __forceinline__ TileInfo decode(const Params& p, const SmemCtl& s, int tile) {
   TileInfo ti;
   const int n_first = p.seg_first == 0 ? s.seg0_tiles : s.seg1_tiles;
+  const int n_second = s.seg0_tiles + s.seg1_tiles - n_first;
   int seg, local;
-  if (tile < n_first) {
-    seg = p.seg_first;
-    local = tile;
+  const int lead = min(p.interleave_lead, n_first);
+  if (p.interleave_lead < 0 || n_second == 0 || tile < lead) {
+    if (tile < n_first) {
+      seg = p.seg_first;
+      local = tile;
+    } else {
+      seg = 1 - p.seg_first;
+      local = tile - n_first;
+    }
   } else {
-    seg = 1 - p.seg_first;
-    local = tile - n_first;
+    // position i of the interleaved rest: c(i) = floor(i * n_second / rest) of the first i
+    // positions belong to the second segment; position i is the second segment's c(i)-th tile
+    // when c(i + 1) > c(i), else the first segment's (lead + i - c(i))-th
+    const long long i = tile - lead, rest = (long long)(n_first - lead) + n_second;
+    const int c0 = (int)(i * n_second / rest), c1 = (int)((i + 1) * n_second / rest);
+    if (c1 > c0) {
+      seg = 1 - p.seg_first;
+      local = c0;
+    } else {
+      seg = p.seg_first;
+      local = lead + (int)i - c0;
+    }
   }
   if (seg == 0) {
     const Segment& sg = p.seg[0];

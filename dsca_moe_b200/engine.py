@@ -370,8 +370,11 @@ class MoEEngine:
         # False: the separate dsca_dispatch_scan launch does
         self.fuse_scan = True
         # bf16 expert GEMM tile form (dsca_ffn_args.tile_rows): 0 = default per GEMM,
-        # 128 = single-CTA tiles, 256 = CTA-pair swap-AB tiles
+        # 128 = single-CTA tiles, 256 = CTA-pair swap-AB tiles, 512 = CTA pairs with whole
+        # 256-token blocks of the SwiGLU GEMM1 non-swapped
         self.tile_rows = 0
+        # routed and shared tiles of one launch: 0 = interleaved, 1 = one segment after the other
+        self.tile_order = 0
         # one GPU: GEMM1 launched as a programmatic dependent of the permute (shared-expert tiles
         # overlap it; the routed tiles wait for it on the device)
         self.pdl = True
@@ -530,6 +533,7 @@ class MoEEngine:
             f.ws1_scale, f.ws2_scale = _ptr(pe.ws1_scale), _ptr(pe.ws2_scale)
         f.err, f.num_ctas, f.phases = _ptr(self.err), self.num_ctas if num_ctas is None else num_ctas, phases
         f.tile_rows = self.tile_rows
+        f.tile_order = self.tile_order
         f.ep_ctx = _ptr(ep_ctx)
         f.segments = segments
         # GEMM1 directly after the permute: its shared-expert tiles overlap the permute

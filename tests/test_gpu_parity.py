@@ -410,10 +410,15 @@ def test_single_cta_and_pair_tiles_agree(cuda, T, d, E, I, Is, k):
     outs = []
     for rows in (128, 256, 512):
         eng.tile_rows = rows
-        r = eng.forward(xd)
-        torch.cuda.synchronize()
-        eng.check()
-        outs.append(r["out"].float().cpu().numpy())
+        got = []
+        for order in (0, 1):  # routed and shared tiles interleaved, or one segment after the other
+            eng.tile_order = order
+            r = eng.forward(xd)
+            torch.cuda.synchronize()
+            eng.check()
+            got.append(r["out"].clone())
+        assert torch.equal(got[0], got[1])
+        outs.append(got[0].float().cpu().numpy())
     y, *_ = O.qwen_forward(x, Wg, p, k, False, "bf16")
     for o in outs:
         assert O.max_rel_err(o, y) < BF16_TOL
