@@ -91,8 +91,8 @@ def parse():
                          "weights as M), 128 = one CTA per 128-token tile, 512 = CTA pairs with whole "
                          "256-token blocks of the SwiGLU GEMM1 non-swapped (tokens as M)")
     ap.add_argument("--tile-order", type=int, choices=[0, 1], default=0,
-                    help="routed and shared tiles of one GEMM launch: 0 = interleaved, 1 = one segment "
-                         "after the other")
+                    help="routed and shared tiles of one GEMM launch: 0 = one segment after the other, "
+                         "1 = interleaved")
     ap.add_argument("--no-pdl", action="store_true",
                     help="one GPU: launch GEMM1 after the permute has finished (no programmatic dependent launch)")
     ap.add_argument("--expert-cache", type=int, default=0,
@@ -978,7 +978,7 @@ def run_ours(args, w, T):
                                256: "CTA-pair swap-AB tiles (256 channels x <=256 tokens)",
                                512: "CTA-pair tiles: SwiGLU GEMM1 whole 256-token blocks non-swapped "
                                     "(256 tokens x 128 channels), the rest swap-AB"}[args.tile_rows],
-                "tile_order": ["routed and shared tiles interleaved", "one segment after the other"][args.tile_order]},
+                "tile_order": ["one segment after the other", "routed and shared tiles interleaved"][args.tile_order]},
             "roofline": roof, "layer_roofline": layer_roof, "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * w["d"] * 2,
                     "d2h_bytes_per_step": T * w["d"] * 2, "mode": e2e_mode, "serial_value": e2e_serial},

@@ -378,7 +378,7 @@ int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t st
     p.pdl_seg0_wait = (f->pdl_after_permute && routed) ? 1 : 0;
     p.seg_first = (p.pdl_seg0_wait && shared) ? 1 : 0;
     // interleaved segments: two rounds of shared tiles first when the permute is still running
-    p.interleave_lead = (shared && routed && f->tile_order == 0) ? (p.pdl_seg0_wait ? 2 * grid : 0) : -1;
+    p.interleave_lead = (shared && routed && f->tile_order == 1) ? (p.pdl_seg0_wait ? 2 * grid : 0) : -1;
     gemm::Segment& s0 = p.seg[0];
     s0.group_offsets = f->group_offsets;
     s0.group_weight = f->group_weight;
@@ -426,7 +426,7 @@ int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t st
     // the longer K first; with the fused return (ep_ctx) the routed tiles first, so that their
     // NVLink stores drain while the shared-expert tiles compute
     p.seg_first = (shared && f->shared_ip > f->ip && f->ep_ctx == nullptr) ? 1 : 0;
-    p.interleave_lead = (shared && routed && f->tile_order == 0) ? 0 : -1;
+    p.interleave_lead = (shared && routed && f->tile_order == 1) ? 0 : -1;
     p.ep_signal = routed ? static_cast<ep::Ctx*>(f->ep_ctx) : nullptr;
     gemm::Segment& s0 = p.seg[0];
     s0.ep = static_cast<const ep::Ctx*>(f->ep_ctx);

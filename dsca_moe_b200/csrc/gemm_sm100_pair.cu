@@ -466,7 +466,7 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
     p.pdl_seg0_wait = (p.hybrid && f->pdl_after_permute && routed) ? 1 : 0;
     p.seg_first = (p.pdl_seg0_wait && shared) ? 1 : 0;
     // interleaved segments: one round of shared tiles first when the permute is still running
-    p.interleave_lead = (shared && routed && f->tile_order == 0) ? (p.pdl_seg0_wait ? grid / 2 : 0) : -1;
+    p.interleave_lead = (shared && routed && f->tile_order == 1) ? (p.pdl_seg0_wait ? grid / 2 : 0) : -1;
     gemm::Segment& s0 = p.seg[0];
     s0.group_offsets = f->group_offsets;
     s0.group_weight = f->group_weight;
@@ -519,7 +519,7 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
     // the longer K first; with the fused return (ep_ctx) the routed tiles first, so that their
     // NVLink stores drain while the shared-expert tiles compute
     p.seg_first = (shared && f->shared_ip > f->ip && f->ep_ctx == nullptr) ? 1 : 0;
-    p.interleave_lead = (shared && routed && f->tile_order == 0) ? 0 : -1;
+    p.interleave_lead = (shared && routed && f->tile_order == 1) ? 0 : -1;
     p.ep_signal = routed ? static_cast<ep::Ctx*>(f->ep_ctx) : nullptr;
     p.pdl_wait_all = (f->pdl_after_permute && f->ep_ctx == nullptr) ? 1 : 0;  // right after GEMM1
     p.hybrid = 0;

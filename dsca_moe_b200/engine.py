@@ -373,7 +373,8 @@ class MoEEngine:
         # 128 = single-CTA tiles, 256 = CTA-pair swap-AB tiles, 512 = CTA pairs with whole
         # 256-token blocks of the SwiGLU GEMM1 non-swapped
         self.tile_rows = 0
-        # routed and shared tiles of one launch: 0 = interleaved, 1 = one segment after the other
+        # routed and shared tiles of one launch: 0 = one segment after the other, 1 = interleaved
+        # (measured slower)
         self.tile_order = 0
         # one GPU: GEMM1 launched as a programmatic dependent of the permute (shared-expert tiles
         # overlap it; the routed tiles wait for it on the device)
