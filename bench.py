@@ -141,7 +141,7 @@ def launches_per_step(world, exchange, eng):
         # router, plan, dispatch, wait, routed GEMM1, routed GEMM2, wait, combine; + the return
         # kernel ("overlap"); + shared-expert GEMM1 and GEMM2
         return (8 + (1 if eng.ep_return == "overlap" else 0) + (2 if eng.experts.ws1 is not None else 0)
-                + (0 if eng.fuse_scan else 1))
+                + (2 if eng.qos_order else 0) + (0 if eng.fuse_scan else 1))
     # router, permute into the send buffer, GEMM1, GEMM2, combine (NCCL does the exchange)
     return 5 + (0 if eng.fuse_scan else 1)
 

@@ -55,7 +55,7 @@ class FfnArgs(ctypes.Structure):
                 ("xs", _vp), ("ws1", _vp), ("ws2", _vp), ("hs", _vp), ("ys", _vp), ("err", _vp),
                 ("num_ctas", _i), ("phases", _i), ("ep_ctx", _vp), ("segments", _i),
                 ("w1_scale", _vp), ("w2_scale", _vp), ("ws1_scale", _vp), ("ws2_scale", _vp),
-                ("tile_rows", _i), ("pdl_after_permute", _i), ("tile_order", _i)]
+                ("tile_rows", _i), ("pdl_after_permute", _i), ("group_order", _vp), ("tile_order", _i)]
 
 
 MAX_GPUS = 8
@@ -92,7 +92,7 @@ EXPORTED = ["dsca_version", "dsca_status_string", "dsca_device_info", "dsca_rout
             "dsca_dispatch_scan", "dsca_permute", "dsca_grouped_ffn", "dsca_combine",
             "dsca_plan_harmony", "dsca_plan_layout", "dsca_check_error", "dsca_exp_neg_eval",
             "dsca_grouped_ffn_static_scratch", "dsca_ep_ctx_bytes", "dsca_ep_init", "dsca_ep_group_offsets",
-            "dsca_ep_plan", "dsca_ep_dispatch", "dsca_ep_wait", "dsca_ep_plan_eval", "dsca_ipc_export",
+            "dsca_ep_plan", "dsca_ep_group_order", "dsca_ep_dispatch", "dsca_ep_wait", "dsca_ep_plan_eval", "dsca_ipc_export",
             "dsca_ipc_import", "dsca_ipc_close", "dsca_ep_read_plan", "dsca_ep_region_alloc",
             "dsca_ep_region_free", "dsca_ep_return", "dsca_qos_priority", "dsca_router_pack_i8"]
 STATIC_SCRATCH_BYTES = 16 << 20
@@ -131,7 +131,9 @@ def load():
     lib.dsca_ep_init.argtypes = [_vp, p(EpSetup), _vp]
     lib.dsca_ep_group_offsets.restype = _vp
     lib.dsca_ep_group_offsets.argtypes = [_vp]
-    lib.dsca_ep_plan.argtypes = [_vp, _vp, u64, _vp, _vp]
+    lib.dsca_ep_group_order.restype = _vp
+    lib.dsca_ep_group_order.argtypes = [_vp]
+    lib.dsca_ep_plan.argtypes = [_vp, _vp, _vp, u64, _vp, _vp]
     lib.dsca_ep_dispatch.argtypes = [p(EpDispatchArgs), _vp]
     lib.dsca_ep_wait.argtypes = [_vp, _i, u64, _vp, _vp]
     lib.dsca_ep_plan_eval.argtypes = [_vp, _i, _i, _vp, _i, _vp, _vp]

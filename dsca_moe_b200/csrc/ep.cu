@@ -188,7 +188,8 @@ __device__ void harmony_warp(const int32_t* meta, int G, int E, const int32_t* e
 }
 
 // ------------------------------------------------------------------ plan kernel
-__global__ void __launch_bounds__(256) plan_kernel(Ctx* c, const int32_t* counts, uint64_t limit_ns, int32_t* err) {
+__global__ void __launch_bounds__(256) plan_kernel(Ctx* c, const int32_t* counts, const float* priority,
+                                                   uint64_t limit_ns, int32_t* err) {
   __shared__ int32_t meta_s[kMaxG * kMaxE];
   __shared__ int32_t S_s[kMaxG * kMaxE * kMaxG];
   __shared__ long long amt_s[kMaxG];
@@ -197,10 +198,11 @@ __global__ void __launch_bounds__(256) plan_kernel(Ctx* c, const int32_t* counts
   __shared__ int32_t e2g_s[kMaxE];
   const int G = c->G, E = c->E, me = c->me, tid = threadIdx.x;
   const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(&c->epoch) + 1u;
-  // 1. my counts into every rank's meta[me][*]
+  // 1. my counts (and QoS priorities) into every rank's meta[me][*]
   for (int i = tid; i < G * E; i += blockDim.x) {
     const int p = i / E, e = i % E;
     c->meta[p][me * kMaxE + e] = counts[e];
+    if (priority != nullptr) c->meta[p][kMaxG * kMaxE + me * kMaxE + e] = __float_as_int(priority[e]);
   }
   __syncthreads();
   if (tid == 0) {
@@ -215,6 +217,28 @@ __global__ void __launch_bounds__(256) plan_kernel(Ctx* c, const int32_t* counts
   const volatile int32_t* ml = c->meta[me];
   for (int i = tid; i < G * E; i += blockDim.x) meta_s[i] = ml[(i / E) * kMaxE + i % E];
   for (int e = tid; e < E; e += blockDim.x) e2g_s[e] = c->expert_to_gpu[e];
+  // QoS: the priorities summed over the ranks in rank order (the all-reduce of
+  // src/qosmoe/moe_layer.py:379-380, identical on every rank), and the execution order of the
+  // experts by it: descending, lowest expert id on ties (the stable sort of build_exec_plan,
+  // src/qosmoe/planner.py:189-198, with every expert resident)
+  __shared__ float prio_s[kMaxE];
+  if (tid < E) {
+    float sum = 0.0f;
+    if (priority != nullptr)
+      for (int src = 0; src < G; ++src) sum = __fadd_rn(sum, __int_as_float(ml[kMaxG * kMaxE + src * kMaxE + tid]));
+    prio_s[tid] = (sum == sum) ? sum : -INFINITY;  // a NaN orders last: the order stays a permutation
+  }
+  __syncthreads();
+  if (tid < E) {
+    const float pe = prio_s[tid];
+    int pos = 0;
+    for (int e2 = 0; e2 < E; ++e2) {
+      const float q = prio_s[e2];
+      pos += (q > pe || (q == pe && e2 < tid)) ? 1 : 0;
+    }
+    c->group_order[pos] = tid;
+    c->priority[tid] = pe;
+  }
   __syncthreads();
   // 3. the plan
   if (tid < 32) harmony_warp(meta_s, G, E, e2g_s, c->eq_tokens, S_s, amt_s, le_s, amt32_s);
@@ -449,10 +473,15 @@ int dsca_ep_init(void* ctx_dev, const dsca_ep_setup* s, dsca_stream_t stream) {
   return DSCA_OK;
 }
 
-int dsca_ep_plan(void* ctx_dev, const int32_t* counts, uint64_t limit_ns, int32_t* err, dsca_stream_t stream) {
+int32_t* dsca_ep_group_order(void* ctx_dev) {
+  return ctx_dev == nullptr ? nullptr : static_cast<Ctx*>(ctx_dev)->group_order;
+}
+
+int dsca_ep_plan(void* ctx_dev, const int32_t* counts, const float* priority, uint64_t limit_ns, int32_t* err,
+                 dsca_stream_t stream) {
   if (ctx_dev == nullptr || counts == nullptr) return DSCA_ERR_BAD_ARG;
   dsca::ep::plan_kernel<<<1, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(static_cast<Ctx*>(ctx_dev), counts,
-                                                                            limit_ns, err);
+                                                                            priority, limit_ns, err);
   return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
 }
 

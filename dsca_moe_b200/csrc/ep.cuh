@@ -27,7 +27,8 @@ struct Ctx {
   int32_t recv_total;
   int32_t expert_to_gpu[kMaxE];
   uint32_t* flags[kMaxG];  // flags[p]: peer p's flag array [3][kMaxG]
-  int32_t* meta[kMaxG];    // meta[p]:  peer p's counts table [kMaxG][kMaxE]
+  int32_t* meta[kMaxG];    // meta[p]:  peer p's counts table [kMaxG][kMaxE], then its priority
+                           //           table [kMaxG][kMaxE] (fp32 bits) right after it
   char* recv[kMaxG];       // recv[p]:  peer p's receive buffer
   char* ret[kMaxG];        // ret[p]:   peer p's return buffer
   // plan tables (written on the device by the plan kernel each forward)
@@ -39,6 +40,10 @@ struct Ctx {
   int32_t chunk_len[kMaxE][kMaxG];         // S[src][e][me]
   int32_t ret_start[kMaxE][kMaxG];         // where chunk (src, e) goes in src's return buffer
   int32_t S[kMaxG][kMaxE][kMaxG];          // the plan
+  // QoS execution order: experts by the priority summed over the ranks (descending, lowest id on
+  // ties); position -> expert.  The identity when the forward carries no priorities.
+  int32_t group_order[kMaxE];
+  float priority[kMaxE];                   // the summed priorities of the last forward
 };
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {

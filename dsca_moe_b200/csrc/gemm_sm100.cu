@@ -382,6 +382,7 @@ int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t st
     gemm::Segment& s0 = p.seg[0];
     s0.group_offsets = f->group_offsets;
     s0.group_weight = f->group_weight;
+    s0.group_order = f->group_order;
     s0.ngroups = routed ? f->num_groups : 0;
     s0.rows = 0;
     s0.n_tiles = f->n1p / gemm::BN;
@@ -432,6 +433,7 @@ int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t st
     s0.ep = static_cast<const ep::Ctx*>(f->ep_ctx);
     s0.group_offsets = f->group_offsets;
     s0.group_weight = f->group_weight;
+    s0.group_order = f->group_order;
     s0.ngroups = routed ? f->num_groups : 0;
     s0.rows = 0;
     s0.n_tiles = f->dp / gemm::BN;

@@ -22,6 +22,7 @@ enum Epi { kEpiSwiGLU = 0, kEpiReLU = 1, kEpiStore = 2 };
 struct Segment {
   const int32_t* group_offsets;  // device [ngroups + 1], or null = one group of `rows`
   const int32_t* group_weight;   // device [ngroups], or null = identity
+  const int32_t* group_order;    // device [ngroups]: execution position -> group, or null = identity
   int ngroups;
   int rows;
   int n_tiles;                   // 256-wide blocks of weight rows per group
@@ -122,9 +123,10 @@ struct SmemCtl {
   int total_tiles;
   int seg0_tiles;
   int seg1_tiles;
-  int tile_start[kMaxGroups + 1];  // segment 0: prefix of tiles per group
+  int tile_start[kMaxGroups + 1];  // segment 0: prefix of tiles per execution position
   int goff[kMaxGroups + 1];
   int gw[kMaxGroups];
+  int gord[kMaxGroups];            // execution position -> group
 };
 
 // Tile schedule.  The segment with the longer K (p.seg_first) comes first, then the other; inside
@@ -140,12 +142,21 @@ __device__ __forceinline__ void build_group_table(const Params& p, SmemCtl& ctl,
   for (int g = lane; g <= ng; g += 32)
     ctl.goff[g] = sg.group_offsets ? sg.group_offsets[g] : (g == 0 ? 0 : sg.rows);
   for (int g = lane; g < ng; g += 32) ctl.gw[g] = sg.group_weight ? sg.group_weight[g] : g;
+  for (int i = lane; i < ng; i += 32) {
+    int g = sg.group_order ? sg.group_order[i] : i;
+    if (g < 0 || g >= ng) {
+      record_error(p.err, kErrIndex);
+      g = i;
+    }
+    ctl.gord[i] = g;
+  }
   __syncwarp();
-  // each lane scans a contiguous run of groups, then a warp scan stitches the runs
+  // each lane scans a contiguous run of execution positions, then a warp scan stitches the runs
   const int per = (ng + 31) / 32;
   const int g0 = min(ng, lane * per), g1 = min(ng, g0 + per);
   int run = 0;
-  for (int g = g0; g < g1; ++g) {
+  for (int i = g0; i < g1; ++i) {
+    const int g = ctl.gord[i];
     int rows_g = ctl.goff[g + 1] - ctl.goff[g];
     if (rows_g < 0 || ctl.goff[g + 1] > sg.capacity) {
       record_error(p.err, kErrCapacity);
@@ -160,8 +171,9 @@ __device__ __forceinline__ void build_group_table(const Params& p, SmemCtl& ctl,
     if (lane >= off) incl += v;
   }
   int excl = incl - run;
-  for (int g = g0; g < g1; ++g) {
-    ctl.tile_start[g] = excl;
+  for (int i = g0; i < g1; ++i) {
+    const int g = ctl.gord[i];
+    ctl.tile_start[i] = excl;
     int rows_g = max(0, ctl.goff[g + 1] - ctl.goff[g]);
     if (ctl.goff[g + 1] > sg.capacity) rows_g = 0;
     excl += group_tiles<TBM>(rows_g, sg, p.hybrid);
@@ -216,10 +228,10 @@ __device__ __forceinline__ TileInfo decode(const Params& p, const SmemCtl& s, in
       const int mid = (lo + hi) >> 1;
       if (s.tile_start[mid] <= local) lo = mid; else hi = mid;
     }
-    const int g = lo;
+    const int g = s.gord[lo];
     ti.seg = 0;
     ti.group = g;
-    decode_in_group<TBM>(ti, local - s.tile_start[g], s.goff[g + 1] - s.goff[g], s.goff[g],
+    decode_in_group<TBM>(ti, local - s.tile_start[lo], s.goff[g + 1] - s.goff[g], s.goff[g],
                          s.gw[g] * sg.b_rows_per_group, sg, p.hybrid);
   } else {
     ti.seg = 1;

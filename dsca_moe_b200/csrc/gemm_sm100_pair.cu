@@ -470,6 +470,7 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
     gemm::Segment& s0 = p.seg[0];
     s0.group_offsets = f->group_offsets;
     s0.group_weight = f->group_weight;
+    s0.group_order = f->group_order;
     s0.ngroups = routed ? f->num_groups : 0;
     s0.rows = 0;
     // SwiGLU: a tile covers 256 output channels (gate and up rows of them); others 256 rows
@@ -527,6 +528,7 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
     s0.ep = static_cast<const ep::Ctx*>(f->ep_ctx);
     s0.group_offsets = f->group_offsets;
     s0.group_weight = f->group_weight;
+    s0.group_order = f->group_order;
     s0.ngroups = routed ? f->num_groups : 0;
     s0.rows = 0;
     s0.n_tiles = f->dp / gemm::BN;

@@ -319,8 +319,9 @@ class MoEEngine:
         # in pinned host memory and `cache_slots` device slots hold the ones being computed
         self.cache = None
         if cache_slots is not None:
-            if world != 1 or experts.fp8:
-                raise NotImplementedError("the expert cache runs on one GPU with bf16 / f32 weights")
+            if experts.fp8 or (world > 1 and exchange != "p2p"):
+                raise NotImplementedError("the expert cache takes bf16 / f32 weights and, with more than one "
+                                          "GPU, the fused exchange")
             self.cache = ExpertCache.create(experts.w1, experts.w2, int(cache_slots), self.device, initial_cache)
             experts = replace(experts, w1=self.cache.w1, w2=self.cache.w2, E=int(cache_slots),
                               ws1=None if experts.ws1 is None else experts.ws1.to(self.device),
@@ -329,6 +330,7 @@ class MoEEngine:
         self.qos_params = dict(alpha=1.0, beta=0.1, delta=0.5, target_batch=64.0, epsilon=1e-6, attention_mode=0)
         self.last_exec_plan = None
         self.last_loads = 0
+        self.last_priority = None  # host copy of the expert priorities of the last cache-path forward
         self.experts = experts
         self.router_weight = router_weight.to(device=self.device, dtype=self.dtype).contiguous()
         self.E, self.d = self.router_weight.shape
@@ -379,6 +381,10 @@ class MoEEngine:
         # one GPU: GEMM1 launched as a programmatic dependent of the permute (shared-expert tiles
         # overlap it; the routed tiles wait for it on the device)
         self.pdl = True
+        # expert parallel: the QoS planner's token scores and expert priorities are computed on
+        # every rank, summed over the ranks and order the routed experts' tiles (the reference's
+        # world > 1 path always runs them, src/qosmoe/moe_layer.py:306-316,379-380,422-427)
+        self.qos_order = True
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._done_counter = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._ws = {}
@@ -406,6 +412,10 @@ class MoEEngine:
             self.side_markers.append((name, start, ev))
         return ev
 
+    @property
+    def _uses_qos(self) -> bool:
+        return self.cache is not None or ((self.world > 1 or self.ep_loopback) and self.exchange == "p2p")
+
     # -------------------------------------------------------------- workspace
     def _workspace(self, T: int) -> dict:
         ws = self._ws.get(T)
@@ -424,8 +434,8 @@ class MoEEngine:
             offsets=torch.empty(E + 1, dtype=torch.int32, device=dev),
             block_base=torch.empty(max(nb, 1), E, dtype=torch.int32, device=dev),
             token_row=torch.empty(T, k, dtype=torch.int32, device=dev),
-            token_score=torch.empty(T, dtype=torch.float32, device=dev) if self.cache is not None else None,
-            expert_priority=torch.empty(E, dtype=torch.float32, device=dev) if self.cache is not None else None,
+            token_score=torch.empty(T, dtype=torch.float32, device=dev) if self._uses_qos else None,
+            expert_priority=torch.empty(E, dtype=torch.float32, device=dev) if self._uses_qos else None,
             # fp8 weights: the FFN operands (rows, shared input, intermediates) are f16
             hs=torch.empty(T, pe.s_ip, dtype=self.op_dtype, device=dev) if pe.ws1 is not None else None,
             ys=torch.empty(T, d, dtype=dt, device=dev) if pe.ws1 is not None else None,
@@ -517,7 +527,7 @@ class MoEEngine:
                            after_permute=after_permute)
 
     def _ffn_call(self, x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, phases, ep_ctx=None,
-                  segments=3, num_ctas=None, after_permute=False):
+                  segments=3, num_ctas=None, after_permute=False, group_order=None):
         pe = self.experts  # with an expert cache: w1 / w2 are the device slots
         f = L.FfnArgs()
         f.dtype, f.act, f.d = (L.F8E4M3 if pe.fp8 else _dt(self.dtype)), pe.act, self.d
@@ -535,6 +545,7 @@ class MoEEngine:
         f.err, f.num_ctas, f.phases = _ptr(self.err), self.num_ctas if num_ctas is None else num_ctas, phases
         f.tile_rows = self.tile_rows
         f.tile_order = self.tile_order
+        f.group_order = _ptr(group_order)
         f.ep_ctx = _ptr(ep_ctx)
         f.segments = segments
         # GEMM1 directly after the permute: its shared-expert tiles overlap the permute
@@ -584,7 +595,7 @@ class MoEEngine:
             self._combine(ws, ws["y"], cap, after_ffn=self.markers is None)
             self._mark("combine")
             return ws
-        return self._forward_ep(x, ws)
+        return self._forward_ep(x, ws, qos)
 
     # -------------------------------------------------------------- expert cache path
     def _qos(self, x, ws, qos: QoSInputs | None):
@@ -630,6 +641,7 @@ class MoEEngine:
         # reference does with .item() per expert)
         counts = ws["counts"].cpu().numpy()
         prio = ws["expert_priority"].cpu().numpy()
+        self.last_priority = prio
         plan = build_exec_plan(np.nonzero(counts > 0)[0], prio, cache.resident, cache.slots)
         loads0 = cache.loads
         cur = torch.cuda.current_stream(self.device)
@@ -648,10 +660,19 @@ class MoEEngine:
         self._mark("combine")
         return ws
 
-    def _forward_ep(self, x, ws):
+    def _forward_ep(self, x, ws, qos=None):
         if self.exchange == "p2p":
-            return self._forward_p2p(x, ws)
+            return self._forward_p2p(x, ws, qos)
         return self._forward_nccl(x, ws)
+
+    def last_priority_host(self):
+        """Expert priorities of the last forward on the host (the summed priorities with more than
+        one GPU), or None when that forward computed none.  Synchronises."""
+        if self.cache is not None and self.world == 1 and not self.ep_loopback:
+            return self.last_priority
+        if self._ep is not None and self.qos_order:
+            return self.read_qos_order()[1]
+        return None
 
     # -------------------------------------------------------------- fused NVLink path
     def reserve(self, tokens: int):
@@ -674,7 +695,7 @@ class MoEEngine:
         esz = 2 if self.dtype == torch.bfloat16 else 4
         recv_cap, ret_cap = G * T_cap * k, T_cap * k
         off_flags, off_meta = 0, 256
-        off_recv = 256 + 4 * L.MAX_GPUS * L.MAX_EXPERTS
+        off_recv = 256 + 2 * 4 * L.MAX_GPUS * L.MAX_EXPERTS  # counts, then priorities
         off_recv = _ceil(off_recv, 256) * 256
         off_ret = _ceil(off_recv + recv_cap * d * esz, 256) * 256
         total = off_ret + ret_cap * d * esz
@@ -721,9 +742,10 @@ class MoEEngine:
             y=torch.empty(recv_cap, d, dtype=dt, device=dev),
             side=torch.cuda.Stream(device=dev),
             group_offsets=int(lib.dsca_ep_group_offsets(_ptr(ctx)) or 0),
+            group_order=int(lib.dsca_ep_group_order(_ptr(ctx)) or 0),
             bytes=total)
 
-    def _forward_p2p(self, x, ws):
+    def _forward_p2p(self, x, ws, qos=None):
         """ep_return = "overlap": main stream shared GEMM1 -> [dispatch done] routed GEMM1 ->
         routed GEMM2 -> shared GEMM2 -> [return done] combine; side stream: plan and dispatch
         (beside the shared GEMM1) and the return kernel (beside the shared GEMM2).
@@ -745,8 +767,15 @@ class MoEEngine:
         routed.record(main)
         side.wait_event(routed)
         with torch.cuda.stream(side):
+            prio = None
+            if self.qos_order:
+                t0 = self._side_mark()
+                self._qos(x, ws, qos)
+                prio = ws["expert_priority"]
+                self._side_mark("qos", t0)
             t0 = self._side_mark()
-            L.check(lib.dsca_ep_plan(ctx, _ptr(ws["counts"]), self.wait_limit_ns, err, _stream()), "dsca_ep_plan")
+            L.check(lib.dsca_ep_plan(ctx, _ptr(ws["counts"]), _ptr(prio), self.wait_limit_ns, err, _stream()),
+                    "dsca_ep_plan")
             self._side_mark("plan", t0)
             t0 = self._side_mark()
             a = L.EpDispatchArgs()
@@ -769,13 +798,16 @@ class MoEEngine:
         main.wait_event(dispatched)
         L.check(lib.dsca_ep_wait(ctx, 1, self.wait_limit_ns, err, _stream()), "dsca_ep_wait")
         self._mark("wait_dispatch")
-        self._ffn_call(*args, 1, segments=1)
+        if self.cache is not None:
+            return self._forward_p2p_cached(x, ws, ep, args, has_shared, side_ctas)
+        order = ep["group_order"] if self.qos_order else None
+        self._ffn_call(*args, 1, segments=1, group_order=order)
         self._mark("gemm1_routed")
         if self.ep_return == "fused":
-            self._ffn_call(*args, 2, ep_ctx=ep["ctx"], segments=1)
+            self._ffn_call(*args, 2, ep_ctx=ep["ctx"], segments=1, group_order=order)
             self._mark("gemm2_routed_fused")
         else:
-            self._ffn_call(*args, 2, segments=1)
+            self._ffn_call(*args, 2, segments=1, group_order=order)
             self._mark("gemm2_routed")
             computed = torch.cuda.Event()
             computed.record(main)
@@ -796,6 +828,66 @@ class MoEEngine:
         self._combine(ws, ep["ret"], ep["ret_cap"])
         self._mark("combine")
         return ws
+
+    def _forward_p2p_cached(self, x, ws, ep, args, has_shared, side_ctas):
+        """Expert parallel with an expert cache (the reference runs its cache path on every rank,
+        src/qosmoe/async_cpu.py:98-256, execute_job :175): once the dispatched rows are here,
+        the host reads which experts received rows and the summed priorities (one
+        synchronisation, as the reference's .tolist() / .item() calls), plans the order and the
+        slots with build_exec_plan, and runs each expert's GEMMs from its slot, loading the
+        experts that are not cached on the load stream; then the return kernel, the return wait
+        and the combine.  Every expert is computed from its own weights, so the output equals the
+        resident path's."""
+        lib, ctx, err = L.load(), _ptr(ep["ctx"]), _ptr(self.err)
+        cache = self.cache
+        if has_shared and self.ep_return != "fused":
+            self._ffn_call(*args, 2, segments=2, num_ctas=side_ctas)
+            self._mark("gemm2_shared")
+        torch.cuda.current_stream(self.device).synchronize()
+        goff = _DevPtr.tensor(ep["group_offsets"], (self.E + 1,), torch.int32, self.device).cpu().numpy()
+        if self.qos_order:
+            prio = _DevPtr.tensor(ep["group_order"] + 4 * L.MAX_EXPERTS, (self.E,), torch.float32,
+                                  self.device).cpu().numpy()
+        else:
+            prio = np.zeros(self.E, np.float32)
+        self.last_priority = prio
+        active = np.nonzero(np.diff(goff) > 0)[0]
+        plan = build_exec_plan(active, prio, cache.resident, cache.slots)
+        loads0 = cache.loads
+        cur = torch.cuda.current_stream(self.device)
+        need = set(plan.need_loading)
+        rows = ep["recv_cap"]
+        for e, s in zip(plan.expert_order, plan.slot_idxs):
+            if e in need:
+                cache.load(e, s)
+            cur.wait_event(cache.loaded[s])
+            self._ffn_call(x, ws, ep["recv"], ep["h"], ep["y"], rows, 1, ep["group_offsets"] + 4 * int(e),
+                           cache.slot_ids[s:s + 1], 3, segments=1)
+            cache.free[s].record(cur)
+        self.last_exec_plan = plan
+        self.last_loads = cache.loads - loads0
+        self._mark("experts")
+        L.check(lib.dsca_ep_return(ctx, _ptr(ep["y"]), self.d, _dt(self.dtype), ep["recv_cap"], err, _stream()),
+                "dsca_ep_return")
+        self._mark("return")
+        L.check(lib.dsca_ep_wait(ctx, 2, self.wait_limit_ns, err, _stream()), "dsca_ep_wait")
+        self._mark("wait_return")
+        self._combine(ws, ep["ret"], ep["ret_cap"])
+        self._mark("combine")
+        return ws
+
+    def read_qos_order(self):
+        """(execution order [E], summed priorities [E]) of the last expert-parallel forward (host
+        copies; synchronises)."""
+        if self._ep is None:
+            return None, None
+        ctx = self._ep["ctx"]
+        torch.cuda.synchronize(self.device)
+        order = _DevPtr.tensor(self._ep["group_order"], (self.E,), torch.int32, self.device).cpu().numpy()
+        prio = _DevPtr.tensor(self._ep["group_order"] + 4 * L.MAX_EXPERTS, (self.E,), torch.float32,
+                              self.device).cpu().numpy()
+        del ctx
+        return order, prio
 
     def read_plan(self):
         """(S [G, E, G], rows received here) of the last forward (host copy; synchronises)."""

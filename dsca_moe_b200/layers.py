@@ -13,7 +13,6 @@ from __future__ import annotations
 
 import dataclasses
 import json
-import warnings
 
 import numpy as np
 import torch
@@ -106,11 +105,7 @@ class QoSMoELayer(nn.Module):
         n_exp = int(spec[1].shape[0])
         cache_slots = None
         if int(config.expert_cache_size) < n_exp:
-            if config.world_size == 1:
-                cache_slots = max(1, int(config.expert_cache_size))
-            else:
-                warnings.warn("expert_cache_size < num_experts with world_size > 1: every local expert "
-                              "stays resident", stacklevel=2)
+            cache_slots = max(1, int(config.expert_cache_size))
         pack_dev = "cpu" if cache_slots is not None else dev
         shared = None
         sg_w = None
@@ -151,12 +146,40 @@ class QoSMoELayer(nn.Module):
 
     def get_statistics(self):
         """Same keys as src/qosmoe/moe_layer.py:147-162 (filled when config.collect_stats)."""
+        prefetched = getattr(self, "num_prefetch_launched", [])
         return [{"latency (ms)": self.latencies[i],
                  "total number of tokens sent": self.tot_num_toks_send[i],
                  "total number of tokens recv": self.tot_num_toks_recv[i],
                  "expert distribution": self.expert_freqs[i],
-                 "num expert swaps": self.expert_swaps[i], "num prefetch launched": 0}
+                 "num expert swaps": self.expert_swaps[i],
+                 "num prefetch launched": prefetched[i] if i < len(prefetched) else 0}
                 for i in range(len(self.latencies))]
+
+    def _maybe_prefetch_next_layer(self, priority):
+        """src/qosmoe/moe_layer.py:164-194: with qos_enable_prefetch and a next layer, the top
+        qos_prefetch_topk (at most qos_prefetch_budget_experts) experts by this layer's priority
+        (clamped at 0, raised to qos_prefetch_score_power) are copied into the next layer's expert
+        cache ahead of its forward.  A next layer whose experts are all resident has no cache and
+        loads nothing, as in the reference, where every candidate is already cached."""
+        cfg = self.config
+        if not getattr(cfg, "qos_enable_prefetch", False) or self.next_layer is None or priority is None:
+            self.num_prefetch_launched.append(0)
+            return []
+        budget = int(getattr(cfg, "qos_prefetch_budget_experts", 0))
+        scores = torch.as_tensor(np.asarray(priority, np.float32)).clamp_min(0)
+        if budget <= 0 or scores.numel() == 0 or bool((scores <= 0).all()):
+            self.num_prefetch_launched.append(0)
+            return []
+        power = float(getattr(cfg, "qos_prefetch_score_power", 1.0))
+        if power != 1.0:
+            scores = scores.pow(power)
+        k = min(int(getattr(cfg, "qos_prefetch_topk", budget)), budget, scores.numel())
+        ids = torch.topk(scores, k=k).indices.tolist()
+        nxt = getattr(self.next_layer, "engine", None)
+        cache = getattr(nxt, "cache", None)
+        launched = cache.prefetch(ids) if cache is not None else []
+        self.num_prefetch_launched.append(len(launched))
+        return launched
 
     @torch.no_grad()
     def forward(self, hidden_states):
@@ -168,7 +191,7 @@ class QoSMoELayer(nn.Module):
             ev0.record()
         shape = hidden_states.shape
         qos = None
-        if self.engine.cache is not None:
+        if self.engine._uses_qos:
             ctx = self.runtime_context
             qos = QoSInputs(x_prev=getattr(ctx, "last_hidden_states", None),
                             seq_priority=getattr(ctx, "flat_seq_priority", None),
@@ -184,6 +207,8 @@ class QoSMoELayer(nn.Module):
             TRACE.record_block(self.layer_idx, r["topk_ids"].cpu().numpy(), t0, t0, TRACE.now_ms())
         out = r["out"].view(shape)
         self.runtime_context.last_hidden_states = r["out"]
+        if getattr(self.config, "qos_enable_prefetch", False):
+            self._maybe_prefetch_next_layer(self.engine.last_priority_host())
         tuple_out = getattr(self.config, "return_router_tuple", True)
         if stats:
             ev1.record()

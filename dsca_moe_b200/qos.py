@@ -102,6 +102,7 @@ class ExpertCache:
     free: list = field(default_factory=list)     # per slot: last GEMM that read it done
     loads: int = 0                   # experts copied in since creation
     bytes_loaded: int = 0
+    prefetch_cursor: int = 0         # next slot a prefetch overwrites (round robin)
 
     @property
     def slots(self) -> int:
@@ -137,3 +138,20 @@ class ExpertCache:
         self.loads += 1
         self.bytes_loaded += (self.host_w1[expert].numel() * self.host_w1.element_size()
                               + self.host_w2[expert].numel() * self.host_w2.element_size())
+
+    def prefetch(self, expert_ids) -> list:
+        """ExpertManager.prefetch_experts (src/qosmoe/expert_manager.py:94-128): every listed expert
+        that is not cached yet is copied into the next slot of a round-robin cursor (on the load
+        stream, after the last GEMM that read that slot); returns the (expert, slot) pairs."""
+        launched = []
+        cached = {e for e in self.resident if e >= 0}
+        for e in expert_ids:
+            e = int(e)
+            if e < 0 or e >= self.host_w1.shape[0] or e in cached:
+                continue
+            slot = self.prefetch_cursor % self.slots
+            self.prefetch_cursor = (self.prefetch_cursor + 1) % self.slots
+            self.load(e, slot)
+            launched.append((e, slot))
+            cached.add(e)
+        return launched

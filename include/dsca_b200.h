@@ -228,6 +228,11 @@ typedef struct {
                                  (with a shared expert its tiles go first and overlap the permute;
                                  the routed tiles wait on the device for the permute), and GEMM2 as
                                  GEMM1's (it waits for GEMM1's outputs before its first load) */
+  const int32_t* group_order; /* device [num_groups]: execution order of the routed groups
+                                 (position -> group; a permutation), or NULL = index order.  The
+                                 QoS planner's order (dsca_ep_group_order); bf16 only, other dtypes
+                                 run index order.  Only the order of the tiles changes, never a
+                                 result */
   int tile_order;             /* routed and shared expert in one launch (bf16): 0 = one segment's
                                  tiles after the other's (the default; measured faster); 1 = their
                                  tiles interleaved in proportion to their counts (after one round
@@ -333,7 +338,8 @@ DSCA_API int dsca_plan_layout(const int32_t* S, int G, int E, int rank, int* num
 
 /*
  * Fused expert-parallel exchange over NVLink (one process per GPU).  Each rank owns a symmetric
- * region: flags [3][DSCA_MAX_GPUS] u32, meta [DSCA_MAX_GPUS][DSCA_MAX_EXPERTS] i32, a receive
+ * region: flags [3][DSCA_MAX_GPUS] u32, meta [2][DSCA_MAX_GPUS][DSCA_MAX_EXPERTS] (i32 counts,
+ * then fp32 priorities), a receive
  * buffer [recv_capacity, d] and a return buffer [ret_capacity, d]; every rank maps every peer's
  * region (dsca_ipc_export / dsca_ipc_import) and passes the G pointers of each part.
  * Per forward, on one stream, with no host synchronisation:
@@ -365,11 +371,17 @@ DSCA_API size_t dsca_ep_ctx_bytes(void);
 DSCA_API int dsca_ep_init(void* ctx_dev, const dsca_ep_setup* s, dsca_stream_t stream);
 /* Device pointer of the plan's receive-side group offsets [E + 1] inside ctx_dev. */
 DSCA_API int32_t* dsca_ep_group_offsets(void* ctx_dev);
+/* Device pointer of the QoS execution order [E] inside ctx_dev (position -> expert), written by
+ * dsca_ep_plan: experts by their priority summed over the ranks, descending, lowest id on ties
+ * (the priority all-reduce and build_exec_plan order of src/qosmoe/moe_layer.py:379-380,422-427);
+ * the identity when dsca_ep_plan got no priorities.  Pass it as dsca_ffn_args.group_order. */
+DSCA_API int32_t* dsca_ep_group_order(void* ctx_dev);
 /* Copy the last plan S [DSCA_MAX_GPUS][DSCA_MAX_EXPERTS][DSCA_MAX_GPUS] and the rows this rank
  * received to the host (synchronises `stream`; for statistics, not the hot path). */
 DSCA_API int dsca_ep_read_plan(void* ctx_dev, int32_t* S_host, int32_t* recv_total_host, dsca_stream_t stream);
-DSCA_API int dsca_ep_plan(void* ctx_dev, const int32_t* counts, uint64_t limit_ns, int32_t* err,
-                          dsca_stream_t stream);
+/* priority: this rank's expert priorities [E] (dsca_qos_priority), or NULL (identity order) */
+DSCA_API int dsca_ep_plan(void* ctx_dev, const int32_t* counts, const float* priority, uint64_t limit_ns,
+                          int32_t* err, dsca_stream_t stream);
 typedef struct {
   const void* x;
   int T, d, top_k, dtype;

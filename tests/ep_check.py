@@ -65,6 +65,17 @@ def case_switch(rank, world, dev, group, e2g, eq_tokens, exchange, T=640):
     return ep, one, x
 
 
+def case_qwen_cache(rank, world, dev, group, e2g, eq_tokens, exchange, T=512):
+    """The Qwen case with an expert cache of 8 device slots per rank (the reference's
+    expert_cache_size < num_experts on every rank): experts are loaded into slots per the QoS
+    plan, and the output still equals the one-GPU result."""
+    ep, one, x = case_qwen(rank, world, dev, group, e2g, eq_tokens, exchange, T)
+    cached = MoEEngine(ep.router_weight, ep.experts, top_k=4, route_mode=L.ROUTE_SOFTMAX_TOPK,
+                       shared_gate_weight=ep.shared_gate_weight, rank=rank, world=world, group=group,
+                       expert_to_gpu=e2g, eq_tokens=eq_tokens, exchange=exchange, cache_slots=8)
+    return cached, one, x
+
+
 def main():
     world = int(os.environ["WORLD_SIZE"])
     rank = int(os.environ["RANK"])
@@ -82,6 +93,7 @@ def main():
             (f"qwen uneven placement, harmony, {exchange}", case_qwen, uneven60, 150, exchange),
             (f"switch top-1, harmony, {exchange}", case_switch, None, 150, exchange),
         ]
+    cases.append(("qwen contiguous, harmony, p2p, expert cache 8 slots", case_qwen_cache, None, 150, "p2p"))
     ok = True
     for name, fn, e2g, eq, exchange in cases:
         ep, one, x = fn(rank, world, dev, group, e2g, eq, "nccl" if exchange == "nccl" else "p2p")
@@ -105,6 +117,14 @@ def main():
             ep.check()
             one.check()
             same_route = torch.equal(r_ep["topk_ids"], r_one["topk_ids"]) and torch.equal(r_ep["logits"], r_one["logits"])
+            if exchange == "p2p" and ep.qos_order:
+                # the QoS order is the summed priorities' order, the same on every rank
+                order, prio = ep.read_qos_order()
+                mine = torch.from_numpy(prio.copy()).to(dev)
+                allp = [torch.empty_like(mine) for _ in range(world)]
+                dist.all_gather(allp, mine)
+                same_route = same_route and all(torch.equal(allp[0], t) for t in allp)
+                same_route = same_route and order.tolist() == sorted(range(ep.E), key=lambda e: (-float(prio[e]), e))
             err = rel(r_ep["out"], r_one["out"])
             exact = torch.equal(r_ep["out"], r_one["out"])
             S, _ = ep.read_plan()

@@ -84,6 +84,37 @@ def test_p2p_loopback_equals_local_path(lib, cuda, ret_mode):
         S, rows = loop.read_plan()
         assert rows == x.shape[0] * 4
         assert np.array_equal(S[0, :, 0], np.bincount(a["topk_ids"].cpu().numpy().reshape(-1), minlength=60))
+        # QoS execution order: experts by the planner's priority (summed over the ranks: here one),
+        # descending, lowest id on ties — a permutation, and the output above is unchanged by it
+        order, prio = loop.read_qos_order()
+        mine = loop._workspace(x.shape[0])["expert_priority"].cpu().numpy()
+        assert np.array_equal(prio.view(np.uint32), mine.view(np.uint32))
+        want = sorted(range(60), key=lambda e: (-float(mine[e]), e))
+        assert order.tolist() == want
+    finally:
+        loop.close()
+
+
+def test_qos_order_changes_no_result(lib, cuda):
+    """The routed GEMM tiles in any execution order (here reversed) give the same output bit for
+    bit: the QoS order only decides which experts run first."""
+    loop, local, x = _qwen_pair(cuda)
+    try:
+        a = loop.forward(x)["out"].clone()
+        ws = loop._workspace(x.shape[0])
+        rev = torch.arange(59, -1, -1, dtype=torch.int32, device=cuda)
+        b = local.forward(x)
+        torch.cuda.synchronize()
+        lws = local._workspace(x.shape[0])
+        y_ref = lws["y"].clone()
+        cap = lws["a"].shape[0]
+        local._ffn_call(x, lws, lws["a"], lws["h"], lws["y"], cap, local.E, lws["offsets"], None, 3,
+                        group_order=rev)
+        torch.cuda.synchronize()
+        local.check()
+        assert torch.equal(lws["y"], y_ref)
+        assert torch.equal(a, b["out"])
+        del ws
     finally:
         loop.close()
 
@@ -129,7 +160,7 @@ def test_wait_timeout_reports_and_context_survives(lib, cuda):
         s.expert_to_gpu = e2g.ctypes.data
         s.flags[0] = region.value
         s.meta[0] = region.value + 256
-        s.recv[0] = region.value + 4096
+        s.recv[0] = region.value + 8192
         s.ret[0] = region.value + 65536
         ctx = torch.empty(int(lib.dsca_ep_ctx_bytes()), dtype=torch.uint8, device=cuda)
         assert lib.dsca_ep_init(_p(ctx), ctypes.byref(s), _st()) == 0

@@ -138,3 +138,43 @@ def test_plugin_layer_default_cache_size_runs_cache_path(cuda):
     assert torch.equal(outs[0], outs[1])
     y_ref, *_ = O.switch_forward(x, Wr, wi, wo, "f32")
     assert O.max_rel_err(outs[0].reshape(T, d).cpu().numpy(), y_ref) < 1e-4
+
+
+def test_next_layer_prefetch_loads_top_priority_experts(cuda):
+    """qos_enable_prefetch (src/qosmoe/moe_layer.py:164-194): after a layer's forward, the top
+    qos_prefetch_topk experts by its priority (at most qos_prefetch_budget_experts) are copied
+    into the next layer's expert cache, round robin over its slots, skipping cached ones; the
+    next layer's output is unchanged by what was prefetched."""
+    from dsca_moe_b200 import QoSMoEConfig, QoSMoELayer, RequestStateTable
+
+    T, d, E, F = 128, 64, 8, 128
+    x = syn.hidden_states(T, d, 15, "f32")
+    Wr, _ = syn.router_weight(E, d, 16, zipf_s=1.0, dtype="f32")
+    wi, wo = syn.switch_expert_weights(E, d, F, 17, dtype="f32")
+    sds = [{"wi.weight": torch.from_numpy(wi[e]), "wo.weight": torch.from_numpy(wo[e])} for e in range(E)]
+
+    def layer(idx, prefetch):
+        cfg = QoSMoEConfig(rank=0, world_size=1, experts=sds, router_weights=torch.from_numpy(Wr), d_model=d,
+                           num_experts=E, expert_cache_size=3, layer_idx=idx, collect_stats=True,
+                           qos_enable_prefetch=prefetch, qos_prefetch_topk=2, qos_prefetch_budget_experts=2)
+        lay = QoSMoELayer(cfg)
+        lay.set_runtime_context(RequestStateTable(cfg).build_context({"attention_mask": torch.ones(2, 64)}))
+        return lay
+
+    a, b = layer(0, True), layer(1, False)
+    a.set_next_layer(b)
+    before = list(b.engine.cache.resident)
+    xd = _t(x, torch.float32, cuda).view(2, 64, d)
+    ya, _ = a(xd)
+    torch.cuda.synchronize()
+    prio = a.engine.last_priority
+    top = [int(e) for e in torch.topk(torch.as_tensor(prio).clamp_min(0), k=2).indices]
+    want = [e for e in top if e not in before]
+    assert a.get_statistics()[0]["num prefetch launched"] == len(want)
+    for e in top:
+        assert e in b.engine.cache.resident
+    yb, _ = b(ya)
+    ref = layer(2, False)
+    yr, _ = ref(ya)
+    torch.cuda.synchronize()
+    assert torch.equal(yb, yr)
