@@ -448,22 +448,44 @@ def build_hf_model(kind: str, dev):
 
 
 def run_model(args):
-    """Whole-model forward tokens/s on one GPU: transformers' own MoE blocks vs the swapped block."""
+    """Whole-model forward tokens/s: the transformers model with every MoE block swapped by
+    replace_qosmoe_layer against the same model with transformers' own MoE blocks.  With N ranks
+    (torchrun) every rank builds the same random-init model, feeds its own 16 x 256 token ids and
+    the swapped blocks run expert parallel over the N GPUs (experts placed contiguously: 60 on 8
+    = 4 x 8 + 4 x 7; Switch 64 / N each); time = max over ranks."""
     import torch
+    import torch.distributed as dist
 
     from dsca_moe_b200 import QoSMoEConfig, RequestStateTable, get_qosmoe_layers, replace_qosmoe_layer
 
     m = MODELS[args.workload]
-    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
-        if int(os.environ.get("RANK", "0")) == 0:
-            print(json.dumps({"workload": m["name"], "unavailable": "whole-model runs use one GPU"}), flush=True)
-        return
-    dev = torch.device("cuda", 0)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    group = None
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+        group = dist.group.WORLD
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
     model = build_hf_model(m["hf"], dev)
     B, S = m["batch"], m["seq"]
     T = B * S
-    gen = torch.Generator().manual_seed(1)
+    gen = torch.Generator().manual_seed(1 + rank)
     ids = torch.randint(0, model.config.vocab_size, (B, S), generator=gen).to(dev)
     if m["hf"] == "switch":  # decoder ids = encoder ids (src/flexible_dataset.py:157-166)
         fwd = lambda: model(input_ids=ids, decoder_input_ids=ids, use_cache=False).logits  # noqa: E731
@@ -475,40 +497,44 @@ def run_model(args):
         with torch.no_grad():
             for _ in range(warmup):
                 fwd()
-            torch.cuda.synchronize()
+            barrier()
             evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
             for a, b in evs:
                 flush.zero_()
                 a.record()
                 fwd()
                 b.record()
-            torch.cuda.synchronize()
-        return sum(a.elapsed_time(b) for a, b in evs) / steps
+            barrier()
+        return max_over_ranks(sum(a.elapsed_time(b) for a, b in evs) / steps)
 
     ref_steps = max(1, min(args.steps, 5))
     ref_ms = timed(ref_steps, min(args.warmup, 2))
     with torch.no_grad():
         ref_logits = fwd().float()
-    qcfg = QoSMoEConfig(rank=0, world_size=1, expert_cache_size=m["E"])
+    qcfg = QoSMoEConfig(rank=rank, world_size=world, expert_cache_size=m["E"], process_group=group,
+                        eq_tokens=args.eq_tokens)
     replace_qosmoe_layer(model, config=qcfg, **m["plugin"])
     layers = get_qosmoe_layers(model)
     ctx = RequestStateTable(qcfg).build_context({"attention_mask": torch.ones(B, S, dtype=torch.long)})
-    for layer in layers:
+    for i, layer in enumerate(layers):  # the driver's chaining, src/start_qosmoe.py:184-188
         layer.set_runtime_context(ctx)
+        layer.set_next_layer(layers[i + 1] if i + 1 < len(layers) else None)
+        layer.engine.ep_return = args.ep_return
     torch.cuda.empty_cache()
     uuid = str(torch.cuda.get_device_properties(dev).uuid)
     try:
         clocks = NvmlClockSampler(uuid)
     except Exception:  # noqa: BLE001 - NVML missing: fall back to nvidia-smi
         clocks = ClockSampler(uuid)
-    clocks.start()
+    if local == 0:
+        clocks.start()
     ms = timed(args.steps, args.warmup)
-    clk = clocks.stop()
+    clk = clocks.stop() if local == 0 else None
     with torch.no_grad():
         got = fwd().float()
     for layer in layers:
         layer.engine.check()
-    drift = float((got - ref_logits).norm() / ref_logits.norm())
+    drift = max_over_ranks(float((got - ref_logits).norm() / ref_logits.norm()))
     # time spent inside the swapped blocks: events around each block in one more forward
     marks = []
 
@@ -521,21 +547,30 @@ def run_model(args):
     with torch.no_grad():
         flush.zero_()
         fwd()
-    torch.cuda.synchronize()
+    barrier()
     for h in hooks:
         h.remove()
-    moe_ms = sum(marks[i].elapsed_time(marks[i + 1]) for i in range(0, len(marks), 2))
-    line = {
-        "metric": "model forward tokens/sec", "value": T / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": m["name"], "batch_x_seq": f"{B}x{S}", "weights": "random init (transformers init)",
-                   "moe_layers_swapped": len(layers), "l2": "flushed (256 MiB write, untimed) before every timed step"},
-        "moe_blocks_ms_per_step": moe_ms, "rest_of_model_ms_per_step": ms - moe_ms,
-        "transformers_moe_blocks": {"value": T / (ref_ms / 1e3), "ms_per_step": ref_ms, "steps": ref_steps},
-        "logits_drift_vs_transformers": drift, "clocks": clk,
-    }
-    print(json.dumps(line), flush=True)
+    moe_ms = max_over_ranks(sum(marks[i].elapsed_time(marks[i + 1]) for i in range(0, len(marks), 2)))
+    if rank == 0:
+        line = {
+            "metric": "model forward tokens/sec", "value": T * world / (ms / 1e3), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": m["name"], "batch_x_seq": f"{B}x{S}", "weights": "random init (transformers init)",
+                       "moe_layers_swapped": len(layers), "parallelism": f"ep{world}",
+                       "placement": "contiguous" + (" (60 on 8 = 4x8 + 4x7)" if m["E"] % max(world, 1) else ""),
+                       "l2": "flushed (256 MiB write, untimed) before every timed step"},
+            "moe_blocks_ms_per_step": moe_ms, "rest_of_model_ms_per_step": ms - moe_ms,
+            "transformers_moe_blocks": {"value": T * world / (ref_ms / 1e3), "ms_per_step": ref_ms, "steps": ref_steps,
+                                        "note": "each rank runs its own unswapped model (no expert parallelism)"},
+            "logits_drift_vs_transformers_max_over_ranks": drift, "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        for layer in layers:
+            layer.engine.close()
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def torch_block_fp32(eng, x, topk_ids, topk_w):

@@ -70,7 +70,8 @@ class EpSetup(ctypes.Structure):
 
 class EpDispatchArgs(ctypes.Structure):
     _fields_ = [("x", _vp), ("T", _i), ("d", _i), ("top_k", _i), ("dtype", _i), ("topk_ids", _vp),
-                ("local_rank", _vp), ("block_base", _vp), ("ctx", _vp), ("token_row", _vp), ("err", _vp)]
+                ("local_rank", _vp), ("block_base", _vp), ("ctx", _vp), ("token_row", _vp), ("err", _vp),
+                ("out_f16", _i), ("x_f16", _vp)]
 
 
 class CombineArgs(ctypes.Structure):

@@ -3,6 +3,7 @@
 
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -309,6 +310,20 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
          | (1u << 10)                    // B format bf16
          | ((uint32_t)(N >> 3) << 17)    // N / 8
          | ((uint32_t)(M >> 4) << 24);   // M / 16
+}
+
+// Eight bf16 values -> the same eight values as f16 (round to nearest), 16-byte vectors.
+__device__ __forceinline__ uint4 bf16x8_to_f16x8(uint4 u) {
+  const __nv_bfloat162* bb = reinterpret_cast<const __nv_bfloat162*>(&u);
+  uint4 o;
+  uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(bb[i]);
+    __half2 h = __floats2half2_rn(f.x, f.y);
+    op[i] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  return o;
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

@@ -348,7 +348,20 @@ __global__ void __launch_bounds__(256) dispatch_kernel(dsca_ep_dispatch_args a, 
     if (lane == 0) a.token_row[w] = srow;
     const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(a.x) + (size_t)t * row_bytes);
     uint4* dp = reinterpret_cast<uint4*>(c->recv[dst] + (size_t)rrow * row_bytes);
-    warp_copy_row(dp, src, (int)(row_bytes / 16), lane);
+    if (ESZ == 2 && a.out_f16) {
+      // bf16 -> f16 on the way (the operand of the fp8-weight FFN); the token's slot-0 warp also
+      // writes the local f16 copy of x for the shared expert
+      uint4* xh = (a.x_f16 != nullptr && (w % a.top_k) == 0)
+                      ? reinterpret_cast<uint4*>(reinterpret_cast<char*>(a.x_f16) + (size_t)t * row_bytes)
+                      : nullptr;
+      for (int v = lane; v < (int)(row_bytes / 16); v += 32) {
+        const uint4 o = bf16x8_to_f16x8(src[v]);
+        dp[v] = o;
+        if (xh != nullptr) xh[v] = o;
+      }
+    } else {
+      warp_copy_row(dp, src, (int)(row_bytes / 16), lane);
+    }
   }
   signal_when_grid_done(c, &c->dispatch_done, kDispatch);
 }
@@ -492,6 +505,7 @@ int dsca_ep_dispatch(const dsca_ep_dispatch_args* a, dsca_stream_t stream) {
   if (a->dtype != DSCA_BF16 && a->dtype != DSCA_F32) return DSCA_ERR_BAD_ARG;
   const int esz = a->dtype == DSCA_BF16 ? 2 : 4;
   if (((size_t)a->d * esz) % 16 != 0 || (reinterpret_cast<uintptr_t>(a->x) & 15u)) return DSCA_ERR_BAD_ARG;
+  if (a->out_f16 && (a->dtype != DSCA_BF16 || (reinterpret_cast<uintptr_t>(a->x_f16) & 15u))) return DSCA_ERR_BAD_ARG;
   const long long warps = (long long)a->T * a->top_k;
   // >= 1 CTA so the flag is still set; at most kCtasPerSm resident CTAs per SM (grid-stride)
   const int sms = dsca::current_device_sms();

@@ -312,8 +312,8 @@ class MoEEngine:
         n_experts = experts.E
         self.dtype = experts.dtype  # activation dtype (bf16 for fp8 weights)
         self.op_dtype = torch.float16 if experts.fp8 else self.dtype  # FFN operand dtype
-        if experts.fp8 and world > 1:
-            raise NotImplementedError("fp8 expert weights run on one GPU in this build")
+        if experts.fp8 and world > 1 and exchange != "p2p":
+            raise NotImplementedError("fp8 expert weights with more than one GPU need the fused exchange")
         self.device = torch.device(device) if device is not None else experts.w1.device
         # expert cache (the reference's expert_cache_size < num_experts): the routed weights stay
         # in pinned host memory and `cache_slots` device slots hold the ones being computed
@@ -738,7 +738,7 @@ class MoEEngine:
             region=region.value, imported=imported, ctx=ctx, T_cap=T_cap, recv_cap=recv_cap, ret_cap=ret_cap,
             recv=_DevPtr.tensor(region.value + off_recv, (recv_cap, d), dt, dev),
             ret=_DevPtr.tensor(region.value + off_ret, (ret_cap, d), dt, dev),
-            h=torch.empty(recv_cap, self.experts.ip, dtype=dt, device=dev),
+            h=torch.empty(recv_cap, self.experts.ip, dtype=self.op_dtype, device=dev),
             y=torch.empty(recv_cap, d, dtype=dt, device=dev),
             side=torch.cuda.Stream(device=dev),
             group_offsets=int(lib.dsca_ep_group_offsets(_ptr(ctx)) or 0),
@@ -782,17 +782,20 @@ class MoEEngine:
             a.x, a.T, a.d, a.top_k, a.dtype = _ptr(x), T, self.d, self.top_k, _dt(self.dtype)
             a.topk_ids, a.local_rank = _ptr(ws["topk_ids"]), _ptr(ws["local_rank"])
             a.block_base, a.ctx, a.token_row, a.err = _ptr(ws["block_base"]), ctx, _ptr(ws["token_row"]), err
+            a.out_f16, a.x_f16 = int(self.experts.fp8), _ptr(ws.get("x_f16"))
             L.call("dsca_ep_dispatch", ctypes.byref(a), _stream())
             self._side_mark("dispatch", t0)
             dispatched = torch.cuda.Event()
             dispatched.record(side)
         args = (x, ws, ep["recv"], ep["h"], ep["y"], ep["recv_cap"], self.E, ep["group_offsets"], None)
         has_shared = self.experts.ws1 is not None
+        # the fp8-weight GEMM has no remote-store epilogue: its routed rows go back by the return kernel
+        fused = self.ep_return == "fused" and not self.experts.fp8
         side_ctas = max(2, self.num_sms - self.ep_side_sms) if self.ep_side_sms > 0 else None
         if has_shared:
             self._ffn_call(*args, 1, segments=2, num_ctas=side_ctas)
             self._mark("gemm1_shared")
-            if self.ep_return == "fused":
+            if fused:
                 self._ffn_call(*args, 2, segments=2, num_ctas=side_ctas)
                 self._mark("gemm2_shared")
         main.wait_event(dispatched)
@@ -803,7 +806,7 @@ class MoEEngine:
         order = ep["group_order"] if self.qos_order else None
         self._ffn_call(*args, 1, segments=1, group_order=order)
         self._mark("gemm1_routed")
-        if self.ep_return == "fused":
+        if fused:
             self._ffn_call(*args, 2, ep_ctx=ep["ctx"], segments=1, group_order=order)
             self._mark("gemm2_routed_fused")
         else:
@@ -840,7 +843,7 @@ class MoEEngine:
         resident path's."""
         lib, ctx, err = L.load(), _ptr(ep["ctx"]), _ptr(self.err)
         cache = self.cache
-        if has_shared and self.ep_return != "fused":
+        if has_shared and not (self.ep_return == "fused" and not self.experts.fp8):
             self._ffn_call(*args, 2, segments=2, num_ctas=side_ctas)
             self._mark("gemm2_shared")
         torch.cuda.current_stream(self.device).synchronize()

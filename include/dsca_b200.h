@@ -391,6 +391,8 @@ typedef struct {
   void* ctx;                  /* device context */
   int32_t* token_row;         /* [T, k] out: row of (t, j) in this rank's return buffer */
   int32_t* err;
+  int out_f16;                /* bf16 input: store the rows as f16 (the fp8-weight FFN operand) */
+  void* x_f16;                /* [T, d] f16 copy of x written here (shared-expert operand), or NULL */
 } dsca_ep_dispatch_args;
 DSCA_API int dsca_ep_dispatch(const dsca_ep_dispatch_args* a, dsca_stream_t stream);
 DSCA_API int dsca_ep_wait(void* ctx_dev, int kind, uint64_t limit_ns, int32_t* err, dsca_stream_t stream);

@@ -177,3 +177,31 @@ def test_wait_timeout_reports_and_context_survives(lib, cuda):
     finally:
         torch.cuda.synchronize()
         lib.dsca_ep_region_free(region)
+
+
+def test_p2p_loopback_fp8_weights(lib, cuda):
+    """fp8-e4m3 expert weights through the fused exchange in loopback: the dispatch writes the
+    rows as f16 (and the f16 copy of x for the shared expert), the rows go back by the return
+    kernel; the output equals the one-GPU fp8 path bit for bit."""
+    from dsca_moe_b200 import _lib as L
+    from dsca_moe_b200.engine import MoEEngine, quantize_fp8
+
+    loop, local, x = _qwen_pair(cuda, d=512, I=256, Is=512)
+    pe8 = quantize_fp8(local.experts)
+    loop8 = MoEEngine(local.router_weight, pe8, top_k=4, route_mode=L.ROUTE_SOFTMAX_TOPK,
+                      shared_gate_weight=local.shared_gate_weight, exchange="p2p")
+    loop8.ep_loopback = True
+    local8 = MoEEngine(local.router_weight, pe8, top_k=4, route_mode=L.ROUTE_SOFTMAX_TOPK,
+                       shared_gate_weight=local.shared_gate_weight)
+    try:
+        for mode in ("overlap", "fused"):  # "fused" falls back to the return kernel for fp8
+            loop8.ep_return = mode
+            a = loop8.forward(x)
+            b = local8.forward(x)
+            torch.cuda.synchronize()
+            loop8.check()
+            local8.check()
+            assert torch.equal(a["out"], b["out"]), mode
+    finally:
+        loop8.close()
+        loop.close()

@@ -119,3 +119,31 @@ def test_qwen_model_bf16_blocks(cuda):
     got = _block_checks(model, "Qwen2MoeSparseMoeBlock", QWEN_PLUGIN, lambda: model(input_ids=ids).logits,
                         4, 64, 4)
     assert torch.isfinite(got).all() and _norm_rel(got, ref) < 0.25
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_qwen_model_expert_parallel_matches_single_gpu(world):
+    """A small Qwen2-MoE model swapped at world_size 2 / 4 through replace_qosmoe_layer (one rank
+    per GPU, tests/model_ep_check.py): every rank's logits equal the same model's at world_size 1
+    and stay within 1e-4 of the unswapped transformers model.  Skipped with fewer GPUs."""
+    import json
+    import os
+    import socket
+    import subprocess
+    import sys
+
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={world}", "--master-addr", "127.0.0.1", "--master-port", str(port),
+           os.path.join(root, "tests", "model_ep_check.py")]
+    p = subprocess.run(cmd, cwd=root, env=env, capture_output=True, text=True, timeout=700)
+    assert p.returncode == 0, p.stdout[-3000:] + p.stderr[-3000:]
+    res = json.loads([line for line in p.stdout.splitlines() if line.startswith("{")][-1])
+    assert res["ok"], res
