@@ -76,6 +76,21 @@ def case_qwen_cache(rank, world, dev, group, e2g, eq_tokens, exchange, T=512):
     return cached, one, x
 
 
+def case_qwen_fp8(rank, world, dev, group, e2g, eq_tokens, exchange, T=512):
+    """The Qwen case with fp8-e4m3 expert weights (per-channel scales): the dispatch stores f16
+    rows, the return kernel brings the bf16 outputs back; equal to the one-GPU fp8 result."""
+    from dsca_moe_b200.engine import quantize_fp8
+
+    ep, one, x = case_qwen(rank, world, dev, group, e2g, eq_tokens, exchange, T)
+    pe8 = quantize_fp8(ep.experts)
+    ep8 = MoEEngine(ep.router_weight, pe8, top_k=4, route_mode=L.ROUTE_SOFTMAX_TOPK,
+                    shared_gate_weight=ep.shared_gate_weight, rank=rank, world=world, group=group,
+                    expert_to_gpu=e2g, eq_tokens=eq_tokens, exchange=exchange)
+    one8 = MoEEngine(ep.router_weight, pe8, top_k=4, route_mode=L.ROUTE_SOFTMAX_TOPK,
+                     shared_gate_weight=ep.shared_gate_weight)
+    return ep8, one8, x
+
+
 def main():
     world = int(os.environ["WORLD_SIZE"])
     rank = int(os.environ["RANK"])
@@ -94,6 +109,7 @@ def main():
             (f"switch top-1, harmony, {exchange}", case_switch, None, 150, exchange),
         ]
     cases.append(("qwen contiguous, harmony, p2p, expert cache 8 slots", case_qwen_cache, None, 150, "p2p"))
+    cases.append(("qwen contiguous, harmony, p2p, fp8-e4m3 weights", case_qwen_fp8, None, 150, "p2p"))
     ok = True
     for name, fn, e2g, eq, exchange in cases:
         ep, one, x = fn(rank, world, dev, group, e2g, eq, "nccl" if exchange == "nccl" else "p2p")
