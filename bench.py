@@ -93,10 +93,12 @@ def parse():
     ap.add_argument("--tile-order", type=int, choices=[0, 1], default=0,
                     help="routed and shared tiles of one GEMM launch: 0 = one segment after the other, "
                          "1 = interleaved")
+    ap.add_argument("--cache-hints", type=int, choices=[0, 1], default=0,
+                    help="L2 policies of the GEMM loads: 1 = routed weights evict-first, the rest evict-last")
     ap.add_argument("--no-pdl", action="store_true",
                     help="one GPU: launch GEMM1 after the permute has finished (no programmatic dependent launch)")
     ap.add_argument("--expert-cache", type=int, default=0,
-                    help="one GPU: keep only this many routed experts on the device (the reference's "
+                    help="keep only this many routed experts on each device (the reference's "
                          "expert_cache_size); the rest stream in from pinned host memory per the QoS plan")
     ap.add_argument("--fp8", action="store_true",
                     help="fp8-e4m3 expert weights with per-output-channel scales (bf16 activations)")
@@ -580,9 +582,11 @@ def torch_block_fp32(eng, x, topk_ids, topk_w):
     import torch
 
     from dsca_moe_b200 import _lib as L
-    from dsca_moe_b200.engine import unpack_swiglu
+    from dsca_moe_b200.engine import dequantize_fp8, unpack_swiglu
 
     pe = eng.experts
+    if pe.fp8:  # the weights an fp8 block computes with: q * per-channel scale
+        pe = dequantize_fp8(pe)
     xf = x.float()
     T, d = xf.shape
     y = torch.zeros(T, d, dtype=torch.float32, device=x.device)
@@ -721,14 +725,13 @@ def run_ours(args, w, T):
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
         group = dist.group.WORLD
-    if args.expert_cache and world > 1:
-        raise SystemExit("--expert-cache runs on one GPU")
     eng, x, Wr, raw, info = build_block(w, T, rank, world, dev, args.eq_tokens, group, fp8=args.fp8,
                                         cache_slots=args.expert_cache or None)
     eng.exchange = args.exchange
     eng.ep_return = args.ep_return
     eng.tile_rows = args.tile_rows
     eng.tile_order = args.tile_order
+    eng.cache_hints = args.cache_hints
     eng.ep_side_sms = args.ep_side_sms
     eng.pdl = not args.no_pdl
     peaks = load_peaks()
@@ -1013,7 +1016,8 @@ def run_ours(args, w, T):
                                256: "CTA-pair swap-AB tiles (256 channels x <=256 tokens)",
                                512: "CTA-pair tiles: SwiGLU GEMM1 whole 256-token blocks non-swapped "
                                     "(256 tokens x 128 channels), the rest swap-AB"}[args.tile_rows],
-                "tile_order": ["one segment after the other", "routed and shared tiles interleaved"][args.tile_order]},
+                "tile_order": ["one segment after the other", "routed and shared tiles interleaved"][args.tile_order],
+                "l2_hints": ["default", "routed weights evict-first, the rest evict-last"][args.cache_hints]},
             "roofline": roof, "layer_roofline": layer_roof, "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * w["d"] * 2,
                     "d2h_bytes_per_step": T * w["d"] * 2, "mode": e2e_mode, "serial_value": e2e_serial},

@@ -55,7 +55,7 @@ class FfnArgs(ctypes.Structure):
                 ("xs", _vp), ("ws1", _vp), ("ws2", _vp), ("hs", _vp), ("ys", _vp), ("err", _vp),
                 ("num_ctas", _i), ("phases", _i), ("ep_ctx", _vp), ("segments", _i),
                 ("w1_scale", _vp), ("w2_scale", _vp), ("ws1_scale", _vp), ("ws2_scale", _vp),
-                ("tile_rows", _i), ("pdl_after_permute", _i), ("group_order", _vp), ("tile_order", _i)]
+                ("tile_rows", _i), ("pdl_after_permute", _i), ("group_order", _vp), ("cache_hints", _i), ("tile_order", _i)]
 
 
 MAX_GPUS = 8

@@ -95,6 +95,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; i < kStages; ++i) pending_phase[i] = -1;
       bool ok = true;
       bool seg0_ready = !p.pdl_seg0_wait;
+      const uint64_t pol_first = l2_policy_evict_first(), pol_last = l2_policy_evict_last();
       for (int r = 0; ok; ++r) {
         const int tile = sched_tile(r, (int)blockIdx.x, (int)gridDim.x);
         if (tile >= total) break;
@@ -110,8 +111,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!mbar_wait(smem_u32(&ctl.empty[s]), ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
           const uint32_t fb = smem_u32(&ctl.full[s]);
           mbar_arrive_expect_tx(fb, kStageBytes);
-          tma_load_2d(smem_a + s * kABytes, ma, fb, kb * BK, ti.row0);
-          tma_load_2d(smem_b + s * kBBytes, mb, fb, kb * BK, ti.b_row0);
+          if (p.l2_hints) {
+            tma_load_2d_hint(smem_a + s * kABytes, ma, fb, kb * BK, ti.row0, pol_last);
+            tma_load_2d_hint(smem_b + s * kBBytes, mb, fb, kb * BK, ti.b_row0, ti.seg == 0 ? pol_first : pol_last);
+          } else {
+            tma_load_2d(smem_a + s * kABytes, ma, fb, kb * BK, ti.row0);
+            tma_load_2d(smem_b + s * kBBytes, mb, fb, kb * BK, ti.b_row0);
+          }
           pending_phase[s] = (int)ph;
           if (++s == kStages) { s = 0; ph ^= 1u; }
         }
@@ -378,6 +384,7 @@ int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t st
     p.pdl_seg0_wait = (f->pdl_after_permute && routed) ? 1 : 0;
     p.seg_first = (p.pdl_seg0_wait && shared) ? 1 : 0;
     // interleaved segments: two rounds of shared tiles first when the permute is still running
+    p.l2_hints = f->cache_hints;
     p.interleave_lead = (shared && routed && f->tile_order == 1) ? (p.pdl_seg0_wait ? 2 * grid : 0) : -1;
     gemm::Segment& s0 = p.seg[0];
     s0.group_offsets = f->group_offsets;
@@ -427,6 +434,7 @@ int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t st
     // the longer K first; with the fused return (ep_ctx) the routed tiles first, so that their
     // NVLink stores drain while the shared-expert tiles compute
     p.seg_first = (shared && f->shared_ip > f->ip && f->ep_ctx == nullptr) ? 1 : 0;
+    p.l2_hints = f->cache_hints;
     p.interleave_lead = (shared && routed && f->tile_order == 1) ? 0 : -1;
     p.ep_signal = routed ? static_cast<ep::Ctx*>(f->ep_ctx) : nullptr;
     gemm::Segment& s0 = p.seg[0];

@@ -56,6 +56,9 @@ struct Params {
   // to their counts, so that at any time some SMs run the routed experts' tiles (which stream
   // every expert's weights from HBM) while the others run the shared expert's (tensor bound)
   int interleave_lead;
+  // L2 policies of the loads: 0 = default; 1 = routed experts' weights (segment 0, streamed from
+  // DRAM and mostly read once) evict-first, shared-expert weights and token rows evict-last
+  int l2_hints;
   // CTA-pair SwiGLU GEMM1 only: every whole 256-token block of a group is one non-swapped tile
   // (tokens as M = 256 over the pair, 128 channels' gate and up rows as N = 256, Segment::n_full
   // blocks), the remaining < 256 tokens swap-AB tiles as usual

@@ -120,6 +120,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       if (p.pdl_wait_all) pdl_wait();  // GEMM1, which wrote the A rows, has completed
       bool seg0_ready = !p.pdl_seg0_wait;
+      const uint64_t pol_first = l2_policy_evict_first(), pol_last = l2_policy_evict_last();
       for (int r = 0; ok; ++r) {
         const int tile = sched_tile(r, unit, units);
         if (tile >= total) break;
@@ -148,16 +149,31 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!mbar_wait(smem_u32(&ctl.empty[s]), ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
           const uint32_t fb = smem_u32(&ctl.full[s]);
           const uint32_t fb0 = mapa_shared(fb, 0);  // the even CTA's full barrier
+          // L2 policies (Params::l2_hints): routed weights evict-first, the rest evict-last
+          const uint64_t wpol = ti.seg == 0 ? pol_first : pol_last;
           if (full) {
             if (rank == 0) mbar_arrive_expect_tx(fb, tx_full);
-            tma_load_2d_pair(smem_a + s * C::kABytes, mt, fb0, kb * BK, f_trow);
-            tma_load_2d_pair(smem_a + s * C::kABytes + C::kABytes / 2, mt, fb0, kb * BK, f_trow + 64);
-            tma_load_2d_pair(smem_a2 + s * C::kA2Bytes, mw, fb0, kb * BK, f_wrow);
+            if (p.l2_hints) {
+              tma_load_2d_pair_hint(smem_a + s * C::kABytes, mt, fb0, kb * BK, f_trow, pol_last);
+              tma_load_2d_pair_hint(smem_a + s * C::kABytes + C::kABytes / 2, mt, fb0, kb * BK, f_trow + 64, pol_last);
+              tma_load_2d_pair_hint(smem_a2 + s * C::kA2Bytes, mw, fb0, kb * BK, f_wrow, wpol);
+            } else {
+              tma_load_2d_pair(smem_a + s * C::kABytes, mt, fb0, kb * BK, f_trow);
+              tma_load_2d_pair(smem_a + s * C::kABytes + C::kABytes / 2, mt, fb0, kb * BK, f_trow + 64);
+              tma_load_2d_pair(smem_a2 + s * C::kA2Bytes, mw, fb0, kb * BK, f_wrow);
+            }
           } else {
             if (rank == 0) mbar_arrive_expect_tx(fb, tx);
-            tma_load_2d_pair(smem_a + s * C::kABytes, mw, fb0, kb * BK, w_row);
-            if constexpr (C::kGlu) tma_load_2d_pair(smem_a2 + s * C::kA2Bytes, mw, fb0, kb * BK, w_row + 128);
-            tma_load_2d_pair(smem_t + s * C::kTBytes, mt, fb0, kb * BK, t_row);
+            if (p.l2_hints) {
+              tma_load_2d_pair_hint(smem_a + s * C::kABytes, mw, fb0, kb * BK, w_row, wpol);
+              if constexpr (C::kGlu)
+                tma_load_2d_pair_hint(smem_a2 + s * C::kA2Bytes, mw, fb0, kb * BK, w_row + 128, wpol);
+              tma_load_2d_pair_hint(smem_t + s * C::kTBytes, mt, fb0, kb * BK, t_row, pol_last);
+            } else {
+              tma_load_2d_pair(smem_a + s * C::kABytes, mw, fb0, kb * BK, w_row);
+              if constexpr (C::kGlu) tma_load_2d_pair(smem_a2 + s * C::kA2Bytes, mw, fb0, kb * BK, w_row + 128);
+              tma_load_2d_pair(smem_t + s * C::kTBytes, mt, fb0, kb * BK, t_row);
+            }
           }
           pending_phase[s] = (int)ph;
           if (++s == S) { s = 0; ph ^= 1u; }
@@ -466,6 +482,7 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
     p.pdl_seg0_wait = (p.hybrid && f->pdl_after_permute && routed) ? 1 : 0;
     p.seg_first = (p.pdl_seg0_wait && shared) ? 1 : 0;
     // interleaved segments: one round of shared tiles first when the permute is still running
+    p.l2_hints = f->cache_hints;
     p.interleave_lead = (shared && routed && f->tile_order == 1) ? (p.pdl_seg0_wait ? grid / 2 : 0) : -1;
     gemm::Segment& s0 = p.seg[0];
     s0.group_offsets = f->group_offsets;
@@ -520,6 +537,7 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
     // the longer K first; with the fused return (ep_ctx) the routed tiles first, so that their
     // NVLink stores drain while the shared-expert tiles compute
     p.seg_first = (shared && f->shared_ip > f->ip && f->ep_ctx == nullptr) ? 1 : 0;
+    p.l2_hints = f->cache_hints;
     p.interleave_lead = (shared && routed && f->tile_order == 1) ? 0 : -1;
     p.ep_signal = routed ? static_cast<ep::Ctx*>(f->ep_ctx) : nullptr;
     p.pdl_wait_all = (f->pdl_after_permute && f->ep_ctx == nullptr) ? 1 : 0;  // right after GEMM1

@@ -2,10 +2,10 @@
 // (src/qosmoe/planner.py:63-170) on the device.  They change no result: the expert-cache path
 // orders its experts (and picks which ones to load) by these priorities.
 //
-//   token kernel:  one warp per token.  gain = |x - x_prev| (|x| without x_prev), attention
-//                  factor = population variance of the token's logits row, penalty = target /
-//                  (n(e0) + eps) with e0 the token's first choice and n the first-choice count
-//                  over all T tokens (each CTA counts them into shared memory), score =
+//   count kernel:  n(e) = how many of the T tokens chose e first (one CTA).
+//   token kernel:  one warp per token, 16-byte loads.  gain = |x - x_prev| (|x| without x_prev),
+//                  attention factor = population variance of the token's logits row, penalty =
+//                  target / (n(e0) + eps) with e0 the token's first choice, score =
 //                  P (1 + gain (1 + attn) / (alpha d + beta rem + delta penalty)), -1e9 where
 //                  the token is not valid.
 //   expert kernel: one CTA per expert sums the scores of its (token, slot) assignments; each
@@ -17,7 +17,6 @@ namespace dsca {
 namespace qos {
 
 constexpr int kWarps = 8;
-constexpr int kTokensPerWarp = 8;
 constexpr int kMaxE = 4 * DSCA_MAX_EXPERTS;
 
 template <typename T>
@@ -29,80 +28,153 @@ __device__ __forceinline__ float ld<__nv_bfloat16>(const void* p, size_t i) {
   return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
 }
 
+// 16 bytes of T as floats
 template <typename T>
-__global__ void __launch_bounds__(kWarps * 32) token_kernel(dsca_qos_args a) {
-  __shared__ int first_count[kMaxE];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  for (int e = tid; e < a.E; e += blockDim.x) first_count[e] = 0;
+struct V16;
+template <>
+struct V16<__nv_bfloat16> {
+  static constexpr int n = 8;
+  static __device__ __forceinline__ void get(uint4 u, float* f) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[2 * i] = __uint_as_float(w[i] << 16);
+      f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  }
+};
+template <>
+struct V16<float> {
+  static constexpr int n = 4;
+  static __device__ __forceinline__ void get(uint4 u, float* f) {
+    f[0] = __uint_as_float(u.x);
+    f[1] = __uint_as_float(u.y);
+    f[2] = __uint_as_float(u.z);
+    f[3] = __uint_as_float(u.w);
+  }
+};
+
+// first-choice counts n(e) over all T tokens (one CTA; into first_count [E])
+__global__ void __launch_bounds__(1024) count_kernel(dsca_qos_args a, int32_t* first_count) {
+  __shared__ int cnt[kMaxE];
+  for (int e = threadIdx.x; e < a.E; e += blockDim.x) cnt[e] = 0;
   __syncthreads();
-  for (int t = tid; t < a.T; t += blockDim.x) {
+  for (int t = threadIdx.x; t < a.T; t += blockDim.x) {
     const int e = a.topk_ids[(size_t)t * a.top_k];
-    if (e >= 0 && e < a.E) atomicAdd(&first_count[e], 1);
+    if (e >= 0 && e < a.E) atomicAdd(&cnt[e], 1);
   }
   __syncthreads();
-  const float hidden_cost = (float)a.d;
-  for (int i = 0; i < kTokensPerWarp; ++i) {
-    const int t = (blockIdx.x * kWarps + warp) * kTokensPerWarp + i;
-    if (t >= a.T) break;
-    // information gain: |x - x_prev| over the row, lane partials in index order, then the
-    // xor butterfly
-    float ss = 0.0f;
-    const size_t row = (size_t)t * a.d;
+  for (int e = threadIdx.x; e < a.E; e += blockDim.x) first_count[e] = cnt[e];
+}
+
+// One warp per token.  The row sums run in a fixed order: lane l takes the 16-byte vectors
+// l, l + 32, ... of the row (all loads issued before the arithmetic), each vector's elements in
+// index order into the lane's partial, then the xor butterfly.
+template <typename T>
+__global__ void __launch_bounds__(kWarps * 32) token_kernel(dsca_qos_args a, const int32_t* first_count) {
+  const int lane = threadIdx.x & 31;
+  const int t = (int)(blockIdx.x * kWarps + (threadIdx.x >> 5));
+  if (t >= a.T) return;
+  const size_t row = (size_t)t * a.d;
+  float ss = 0.0f;
+  constexpr int kE = V16<T>::n;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(a.x) | reinterpret_cast<uintptr_t>(a.x_prev)) & 15u) == 0;
+  if ((a.d % kE) == 0 && aligned) {
+    const uint4* xv = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.x) + row);
+    const uint4* pv = a.x_prev != nullptr ? reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.x_prev) + row)
+                                          : nullptr;
+    const int nv = a.d / kE;
+    constexpr int kU = 8;
+    for (int v0 = lane; v0 < nv; v0 += 32 * kU) {
+      uint4 xu[kU], pu[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int v = v0 + 32 * u;
+        xu[u] = v < nv ? xv[v] : make_uint4(0u, 0u, 0u, 0u);
+        pu[u] = (pv != nullptr && v < nv) ? pv[v] : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        if (v0 + 32 * u >= nv) break;
+        float xf[kE], pf[kE];
+        V16<T>::get(xu[u], xf);
+        V16<T>::get(pu[u], pf);
+#pragma unroll
+        for (int i = 0; i < kE; ++i) {
+          const float v = pv != nullptr ? __fsub_rn(xf[i], pf[i]) : xf[i];
+          ss = __fmaf_rn(v, v, ss);
+        }
+      }
+    }
+  } else {
     for (int c = lane; c < a.d; c += 32) {
       float v = ld<T>(a.x, row + c);
       if (a.x_prev != nullptr) v = __fsub_rn(v, ld<T>(a.x_prev, row + c));
       ss = __fmaf_rn(v, v, ss);
     }
+  }
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
-    const float gain = sqrtf(ss);
-    // attention factor: population variance of the logits row (two passes)
-    float attn = 0.0f;
-    if (a.attention_mode == 0) {
-      const size_t lrow = (size_t)t * a.E;
-      float s = 0.0f;
-      for (int e = lane; e < a.E; e += 32) s = __fadd_rn(s, ld<T>(a.logits, lrow + e));
+  for (int off = 16; off >= 1; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
+  const float gain = sqrtf(ss);
+  // attention factor: population variance of the logits row (two passes)
+  float attn = 0.0f;
+  if (a.attention_mode == 0) {
+    const size_t lrow = (size_t)t * a.E;
+    float s = 0.0f;
+    for (int e = lane; e < a.E; e += 32) s = __fadd_rn(s, ld<T>(a.logits, lrow + e));
 #pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
-      const float mean = __fdiv_rn(s, (float)a.E);
-      float q = 0.0f;
-      for (int e = lane; e < a.E; e += 32) {
-        const float dv = __fsub_rn(ld<T>(a.logits, lrow + e), mean);
-        q = __fmaf_rn(dv, dv, q);
-      }
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) q = __fadd_rn(q, __shfl_xor_sync(0xffffffffu, q, off));
-      attn = __fdiv_rn(q, (float)a.E);
+    for (int off = 16; off >= 1; off >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
+    const float mean = __fdiv_rn(s, (float)a.E);
+    float q = 0.0f;
+    for (int e = lane; e < a.E; e += 32) {
+      const float dv = __fsub_rn(ld<T>(a.logits, lrow + e), mean);
+      q = __fmaf_rn(dv, dv, q);
     }
-    if (lane == 0) {
-      const int e0 = a.topk_ids[(size_t)t * a.top_k];
-      float score = -1e9f;
-      if (e0 < 0 || e0 >= a.E) {
-        record_error(a.err, kErrIndex);
-      } else {
-        const float valid = a.valid != nullptr ? a.valid[t] : 1.0f;
-        if (valid != 0.0f) {
-          const float pri = a.seq_priority != nullptr ? a.seq_priority[t] : 1.0f;
-          const float rem = a.remaining != nullptr ? a.remaining[t] : 0.0f;
-          const float penalty = __fdiv_rn(a.target_batch, __fadd_rn((float)first_count[e0], a.epsilon));
-          const float denom = __fadd_rn(__fadd_rn(__fmul_rn(a.alpha, hidden_cost), __fmul_rn(a.beta, rem)),
-                                        __fmul_rn(a.delta, penalty));
-          const float value = __fdiv_rn(__fmul_rn(gain, __fadd_rn(1.0f, attn)), denom);
-          score = __fmul_rn(pri, __fadd_rn(1.0f, value));
-        }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) q = __fadd_rn(q, __shfl_xor_sync(0xffffffffu, q, off));
+    attn = __fdiv_rn(q, (float)a.E);
+  }
+  if (lane == 0) {
+    const int e0 = a.topk_ids[(size_t)t * a.top_k];
+    float score = -1e9f;
+    if (e0 < 0 || e0 >= a.E) {
+      record_error(a.err, kErrIndex);
+    } else {
+      const float valid = a.valid != nullptr ? a.valid[t] : 1.0f;
+      if (valid != 0.0f) {
+        const float pri = a.seq_priority != nullptr ? a.seq_priority[t] : 1.0f;
+        const float rem = a.remaining != nullptr ? a.remaining[t] : 0.0f;
+        const float penalty = __fdiv_rn(a.target_batch, __fadd_rn((float)first_count[e0], a.epsilon));
+        const float denom = __fadd_rn(__fadd_rn(__fmul_rn(a.alpha, (float)a.d), __fmul_rn(a.beta, rem)),
+                                      __fmul_rn(a.delta, penalty));
+        const float value = __fdiv_rn(__fmul_rn(gain, __fadd_rn(1.0f, attn)), denom);
+        score = __fmul_rn(pri, __fadd_rn(1.0f, value));
       }
-      a.token_score[t] = score;
     }
+    a.token_score[t] = score;
   }
 }
 
+// One CTA per expert sums the scores of its (token, slot) assignments; each thread walks a fixed
+// stride of the assignments in order and the block reduces in a fixed tree, so the result does
+// not depend on scheduling.  Eight loads in flight per thread.
 __global__ void __launch_bounds__(256) expert_kernel(dsca_qos_args a) {
   __shared__ float part[256];
   const int e = blockIdx.x, tid = threadIdx.x;
   const int n = a.T * a.top_k;
   float s = 0.0f;
-  for (int w = tid; w < n; w += 256)
-    if (a.topk_ids[w] == e) s = __fadd_rn(s, a.token_score[w / a.top_k]);
+  constexpr int kU = 8;
+  for (int w0 = tid; w0 < n; w0 += 256 * kU) {
+    int ids[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int w = w0 + 256 * u;
+      ids[u] = w < n ? a.topk_ids[w] : -1;
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u)
+      if (ids[u] == e) s = __fadd_rn(s, a.token_score[(w0 + 256 * u) / a.top_k]);
+  }
   part[tid] = s;
   __syncthreads();
   for (int h = 128; h >= 1; h >>= 1) {
@@ -115,13 +187,16 @@ __global__ void __launch_bounds__(256) expert_kernel(dsca_qos_args a) {
 }  // namespace qos
 
 int launch_qos(const dsca_qos_args* a, cudaStream_t stream) {
-  constexpr int per_block = qos::kWarps * qos::kTokensPerWarp;
-  const int blocks = (a->T + per_block - 1) / per_block;
+  // the first-choice counts go to the expert_priority array first (it is E floats long and is
+  // overwritten by the expert kernel below, after the token kernel has read the counts)
+  int32_t* first_count = reinterpret_cast<int32_t*>(a->expert_priority);
+  qos::count_kernel<<<1, 1024, 0, stream>>>(*a, first_count);
+  const int blocks = (a->T + qos::kWarps - 1) / qos::kWarps;
   if (blocks > 0) {
     if (a->dtype == DSCA_BF16)
-      qos::token_kernel<__nv_bfloat16><<<blocks, qos::kWarps * 32, 0, stream>>>(*a);
+      qos::token_kernel<__nv_bfloat16><<<blocks, qos::kWarps * 32, 0, stream>>>(*a, first_count);
     else
-      qos::token_kernel<float><<<blocks, qos::kWarps * 32, 0, stream>>>(*a);
+      qos::token_kernel<float><<<blocks, qos::kWarps * 32, 0, stream>>>(*a, first_count);
   }
   qos::expert_kernel<<<a->E, 256, 0, stream>>>(*a);
   return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;

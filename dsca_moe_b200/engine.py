@@ -378,6 +378,9 @@ class MoEEngine:
         # routed and shared tiles of one launch: 0 = one segment after the other, 1 = interleaved
         # (measured slower)
         self.tile_order = 0
+        # L2 policies of the GEMM loads (dsca_ffn_args.cache_hints): 0 = default, 1 = routed
+        # weights evict-first, shared weights and token rows evict-last
+        self.cache_hints = 0
         # one GPU: GEMM1 launched as a programmatic dependent of the permute (shared-expert tiles
         # overlap it; the routed tiles wait for it on the device)
         self.pdl = True
@@ -545,6 +548,7 @@ class MoEEngine:
         f.err, f.num_ctas, f.phases = _ptr(self.err), self.num_ctas if num_ctas is None else num_ctas, phases
         f.tile_rows = self.tile_rows
         f.tile_order = self.tile_order
+        f.cache_hints = self.cache_hints
         f.group_order = _ptr(group_order)
         f.ep_ctx = _ptr(ep_ctx)
         f.segments = segments

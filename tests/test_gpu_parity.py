@@ -411,13 +411,17 @@ def test_single_cta_and_pair_tiles_agree(cuda, T, d, E, I, Is, k):
     for rows in (128, 256, 512):
         eng.tile_rows = rows
         got = []
-        for order in (0, 1):  # routed and shared tiles interleaved, or one segment after the other
-            eng.tile_order = order
+        # one segment after the other / routed and shared tiles interleaved, with and without the
+        # L2 eviction policies on the loads: the order of the tiles never changes a result
+        for order, hints in ((0, 0), (1, 0), (0, 1), (1, 1)):
+            eng.tile_order, eng.cache_hints = order, hints
             r = eng.forward(xd)
             torch.cuda.synchronize()
             eng.check()
             got.append(r["out"].clone())
-        assert torch.equal(got[0], got[1])
+        eng.tile_order, eng.cache_hints = 0, 0
+        for g in got[1:]:
+            assert torch.equal(got[0], g)
         outs.append(got[0].float().cpu().numpy())
     y, *_ = O.qwen_forward(x, Wg, p, k, False, "bf16")
     for o in outs:
