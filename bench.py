@@ -95,6 +95,9 @@ def parse():
                          "1 = interleaved")
     ap.add_argument("--cache-hints", type=int, choices=[0, 1], default=0,
                     help="L2 policies of the GEMM loads: 1 = routed weights evict-first, the rest evict-last")
+    ap.add_argument("--no-qos-order", action="store_true",
+                    help="expert parallel: skip the QoS planner (scores, priority sum) and run the routed "
+                         "tiles in expert order")
     ap.add_argument("--no-pdl", action="store_true",
                     help="one GPU: launch GEMM1 after the permute has finished (no programmatic dependent launch)")
     ap.add_argument("--expert-cache", type=int, default=0,
@@ -732,6 +735,7 @@ def run_ours(args, w, T):
     eng.tile_rows = args.tile_rows
     eng.tile_order = args.tile_order
     eng.cache_hints = args.cache_hints
+    eng.qos_order = not args.no_qos_order
     eng.ep_side_sms = args.ep_side_sms
     eng.pdl = not args.no_pdl
     peaks = load_peaks()
@@ -1017,7 +1021,8 @@ def run_ours(args, w, T):
                                512: "CTA-pair tiles: SwiGLU GEMM1 whole 256-token blocks non-swapped "
                                     "(256 tokens x 128 channels), the rest swap-AB"}[args.tile_rows],
                 "tile_order": ["one segment after the other", "routed and shared tiles interleaved"][args.tile_order],
-                "l2_hints": ["default", "routed weights evict-first, the rest evict-last"][args.cache_hints]},
+                "l2_hints": ["default", "routed weights evict-first, the rest evict-last"][args.cache_hints],
+                "qos_order": (eng.qos_order if world > 1 else None)},
             "roofline": roof, "layer_roofline": layer_roof, "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * w["d"] * 2,
                     "d2h_bytes_per_step": T * w["d"] * 2, "mode": e2e_mode, "serial_value": e2e_serial},
