@@ -25,7 +25,7 @@ NVCC = shutil.which("nvcc") or os.path.join(CUDA_HOME, "bin", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
               "--expt-relaxed-constexpr", "-I" + INCLUDE] + ARCH
-CU_SOURCES = ["router.cu", "router_tc.cu", "dispatch.cu", "gemm_sm100.cu", "gemm_sm100_pair.cu", "gemm_sm100_fp8.cu", "gemm_simt.cu", "abi.cu",
+CU_SOURCES = ["router.cu", "router_tc.cu", "dispatch.cu", "gemm_sm100.cu", "gemm_sm100_pair.cu", "gemm_sm100_fp8.cu", "gemm_sm100_fp8t.cu", "gemm_simt.cu", "abi.cu",
               "ffn_static_scratch.cu", "ep.cu", "qos.cu"]
 CXX_SOURCES = ["plan.cpp"]
 

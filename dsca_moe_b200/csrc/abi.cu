@@ -16,6 +16,7 @@ int launch_qos(const dsca_qos_args* a, cudaStream_t stream);
 int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t stream);
 int launch_grouped_ffn_f32(const dsca_ffn_args* f, int num_sms, cudaStream_t stream);
 int launch_grouped_ffn_fp8(const dsca_ffn_args* f, int num_sms, cudaStream_t stream);
+int launch_grouped_ffn_fp8_tmem(const dsca_ffn_args* f, int num_sms, cudaStream_t stream);
 }  // namespace dsca
 
 namespace {
@@ -176,6 +177,8 @@ int dsca_grouped_ffn(const dsca_ffn_args* f, dsca_stream_t stream) {
     const void* ptrs[] = {f->a, f->w1, f->w2, f->h, f->y};
     for (const void* p : ptrs)
       if (!aligned16(p)) return DSCA_ERR_BAD_ARG;
+    // tile_rows 256: weights converted into tensor memory (swap-AB); otherwise through shared memory
+    if (f->tile_rows == 256) return dsca::launch_grouped_ffn_fp8_tmem(f, num_sms, st);
     return dsca::launch_grouped_ffn_fp8(f, num_sms, st);
   }
   if (f->dtype == DSCA_F32) {

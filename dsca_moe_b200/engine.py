@@ -373,7 +373,8 @@ class MoEEngine:
         self.fuse_scan = True
         # bf16 expert GEMM tile form (dsca_ffn_args.tile_rows): 0 = default per GEMM,
         # 128 = single-CTA tiles, 256 = CTA-pair swap-AB tiles, 512 = CTA pairs with whole
-        # 256-token blocks of the SwiGLU GEMM1 non-swapped
+        # 256-token blocks of the SwiGLU GEMM1 non-swapped; fp8 weights: 256 = converted into
+        # tensor memory, else into shared memory
         self.tile_rows = 0
         # routed and shared tiles of one launch: 0 = one segment after the other, 1 = interleaved
         # (measured slower)

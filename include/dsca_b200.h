@@ -222,7 +222,11 @@ typedef struct {
                                  and in a SwiGLU GEMM1 every whole 256-token block of a group is
                                  one non-swapped tile (256 tokens x the gate and up rows of 128
                                  channels), the rest as in 256; 0 = default (pair for GEMM2 and
-                                 ReLU GEMM1, single CTA for SwiGLU GEMM1) */
+                                 ReLU GEMM1, single CTA for SwiGLU GEMM1).
+                                 dtype DSCA_F8E4M3: 256 = the weights converted into tensor memory
+                                 (e4m3 -> f16 by converter warps, the MMA's A operand read from
+                                 TMEM, tokens as the MMA N); anything else = the weights converted
+                                 into shared memory */
   int pdl_after_permute;      /* 1: the call directly follows dsca_permute on the same stream (one
                                  GPU): GEMM1 is launched as the permute's programmatic dependent
                                  (with a shared expert its tiles go first and overlap the permute;

@@ -1,7 +1,8 @@
 """fp8-e4m3 expert weights with per-output-channel fp32 scales: the block (f16 operands, fp32
 accumulation, scales in the epilogue) against the fp32 oracle run on the dequantised weights
 (q * scale) and the same inputs — 2e-2 max relative error.  Routing is unchanged by the weight
-format and stays bit-exact."""
+format and stays bit-exact.  Both kernel forms run: tile_rows 0 (weights converted into shared
+memory) and 256 (weights converted into tensor memory, the MMA's A operand read from TMEM)."""
 import numpy as np
 import pytest
 import torch
@@ -36,9 +37,15 @@ def _qwen(dev, T, d, E, I, Is, seed):
     return eng, Wg, p
 
 
-@pytest.mark.parametrize("T,d,E,I,Is", [(200, 256, 60, 128, 256), (77, 128, 8, 64, 128), (1, 64, 8, 32, 64)])
-def test_qwen_fp8_vs_oracle(cuda, T, d, E, I, Is):
+FORMS = [0, 256]
+
+
+@pytest.mark.parametrize("tile_rows", FORMS)
+@pytest.mark.parametrize("T,d,E,I,Is", [(200, 256, 60, 128, 256), (77, 128, 8, 64, 128), (1, 64, 8, 32, 64),
+                                        (300, 192, 8, 320, 384)])
+def test_qwen_fp8_vs_oracle(cuda, T, d, E, I, Is, tile_rows):
     eng, Wg, p = _qwen(cuda, T, d, E, I, Is, 41)
+    eng.tile_rows = tile_rows
     x = syn.hidden_states(T, d, 42, "bf16")
     r = eng.forward(torch.from_numpy(x).to(cuda, torch.bfloat16))
     torch.cuda.synchronize()
@@ -48,7 +55,8 @@ def test_qwen_fp8_vs_oracle(cuda, T, d, E, I, Is):
     assert O.max_rel_err(r["out"].float().cpu().numpy(), y) < TOL
 
 
-def test_switch_fp8_vs_oracle(cuda):
+@pytest.mark.parametrize("tile_rows", FORMS)
+def test_switch_fp8_vs_oracle(cuda, tile_rows):
     from dsca_moe_b200 import _lib as L
     from dsca_moe_b200.engine import MoEEngine, dequantize_fp8, pack_relu, quantize_fp8
 
@@ -60,6 +68,7 @@ def test_switch_fp8_vs_oracle(cuda):
     q = quantize_fp8(pack_relu(wi, wo, device=cuda))
     Wr, _ = syn.router_weight(E, d, 52, zipf_s=1.0, dtype="bf16")
     eng = MoEEngine(torch.from_numpy(Wr).to(cuda, torch.bfloat16), q, top_k=1, route_mode=L.ROUTE_SWITCH_TOP1)
+    eng.tile_rows = tile_rows
     x = syn.hidden_states(T, d, 53, "bf16")
     r = eng.forward(torch.from_numpy(x).to(cuda, torch.bfloat16))
     torch.cuda.synchronize()
@@ -72,11 +81,12 @@ def test_switch_fp8_vs_oracle(cuda):
     assert O.max_rel_err(r["out"].float().cpu().numpy(), y) < TOL
 
 
-def test_qwen_fp8_full_size(cuda):
-    """Qwen1.5-MoE-A2.7B shape, 4096 tokens: fp8 output vs the oracle on a token sample, and its
-    distance from the unquantised bf16 block (the quantisation error itself)."""
+@pytest.mark.parametrize("tile_rows", FORMS)
+def test_qwen_fp8_full_size(cuda, tile_rows):
+    """Qwen1.5-MoE-A2.7B shape, 4096 tokens: fp8 output vs the oracle on a token sample."""
     T, d, E, I, Is = 4096, 2048, 60, 1408, 5632
     eng, Wg, p = _qwen(cuda, T, d, E, I, Is, 61)
+    eng.tile_rows = tile_rows
     x = syn.hidden_states(T, d, 62, "bf16")
     r = eng.forward(torch.from_numpy(x).to(cuda, torch.bfloat16))
     torch.cuda.synchronize()
@@ -84,3 +94,20 @@ def test_qwen_fp8_full_size(cuda):
     sample = syn.rng(63).choice(T, 48, replace=False)
     y, *_ = O.qwen_forward(x[sample], Wg, p, 4, False, "bf16")
     assert O.max_rel_err(r["out"].float().cpu().numpy()[sample], y) < TOL
+
+
+def test_fp8_forms_agree(cuda):
+    """The two kernel forms on the same fp8 block: both accumulate exact f16 products in fp32, so
+    they differ only by summation order and the f16 rounding of the intermediate (1e-2)."""
+    T, d, E, I, Is = 1000, 512, 60, 384, 768
+    eng, Wg, p = _qwen(cuda, T, d, E, I, Is, 71)
+    x = torch.from_numpy(syn.hidden_states(T, d, 72, "bf16")).to(cuda, torch.bfloat16)
+    outs = []
+    for tr in FORMS:
+        eng.tile_rows = tr
+        outs.append(eng.forward(x)["out"].float().clone())
+        torch.cuda.synchronize()
+        eng.check()
+    a, b = outs
+    assert torch.isfinite(b).all()
+    assert ((a - b).abs().max() / a.abs().max()).item() < 1e-2
