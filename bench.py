@@ -95,6 +95,9 @@ def parse():
                          "1 = interleaved")
     ap.add_argument("--cache-hints", type=int, choices=[0, 1], default=0,
                     help="L2 policies of the GEMM loads: 1 = routed weights evict-first, the rest evict-last")
+    ap.add_argument("--router-tc", type=int, choices=[0, 1], default=0,
+                    help="router logits: 1 = tensor cores (exact int8 fixed-point products, correctly "
+                         "rounded bf16 logits), 0 = CUDA-core fp32 fma chains in the fixed chunk order")
     ap.add_argument("--no-qos-order", action="store_true",
                     help="expert parallel: skip the QoS planner (scores, priority sum) and run the routed "
                          "tiles in expert order")
@@ -666,6 +669,7 @@ def parity_check(eng, x, w, rank, world, dev, eq_tokens, graph=None):
         res["rows_received_here"] = int(recv_rows)
         local = MoEEngine(eng.router_weight, eng.experts, top_k=eng.top_k, route_mode=eng.route_mode,
                           norm_topk=eng.norm_topk, shared_gate_weight=eng.shared_gate_weight, device=dev)
+        local.router_tensor_cores = eng.router_tensor_cores
         lr = local.forward(x)
         torch.cuda.synchronize(dev)
         local.check()
@@ -736,6 +740,7 @@ def run_ours(args, w, T):
     eng.tile_order = args.tile_order
     eng.cache_hints = args.cache_hints
     eng.qos_order = not args.no_qos_order
+    eng.router_tensor_cores = bool(args.router_tc)
     eng.ep_side_sms = args.ep_side_sms
     eng.pdl = not args.no_pdl
     peaks = load_peaks()
@@ -1022,7 +1027,9 @@ def run_ours(args, w, T):
                                     "(256 tokens x 128 channels), the rest swap-AB"}[args.tile_rows],
                 "tile_order": ["one segment after the other", "routed and shared tiles interleaved"][args.tile_order],
                 "l2_hints": ["default", "routed weights evict-first, the rest evict-last"][args.cache_hints],
-                "qos_order": (eng.qos_order if world > 1 else None)},
+                "qos_order": (eng.qos_order if world > 1 else None),
+                "router": ("tensor cores: exact int8 fixed-point products, one fused kernel"
+                           if eng.router_tensor_cores else "CUDA cores: fp32 fma chains in the fixed chunk order")},
             "roofline": roof, "layer_roofline": layer_roof, "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * w["d"] * 2,
                     "d2h_bytes_per_step": T * w["d"] * 2, "mode": e2e_mode, "serial_value": e2e_serial},

@@ -8,6 +8,7 @@ namespace dsca {
 int launch_router(const dsca_router_args* p, cudaStream_t stream, const float* logits_in = nullptr);
 int launch_router_tc(const dsca_router_args* a, cudaStream_t stream);
 int launch_router_pack_i8(const void* rows, int R, int d, void* slices, int32_t* exps, cudaStream_t stream);
+bool router_tc_fused_supported(int d);
 int launch_exp_eval(const float* x, float* y, int n, cudaStream_t stream);
 int launch_scan(const dsca_scan_args* a, cudaStream_t stream);
 int launch_permute(const dsca_permute_args* a, cudaStream_t stream);
@@ -96,14 +97,20 @@ int dsca_router_topk(const dsca_router_args* a, dsca_stream_t stream) {
   const int nscan = (a->counts != nullptr) + (a->offsets != nullptr) + (a->block_base != nullptr) +
                     (a->done_counter != nullptr);
   if (nscan != 0 && nscan != 4) return DSCA_ERR_BAD_ARG;
-  // the tensor-core logits take all five buffers or none, bf16 only
-  const int ntc = (a->w_slices != nullptr) + (a->w_exp != nullptr) + (a->x_slices != nullptr) +
-                  (a->x_exp != nullptr) + (a->logits_f32 != nullptr);
-  if (ntc != 0 && (ntc != 5 || a->dtype != DSCA_BF16 || !aligned16(a->w_slices) || !aligned16(a->x_slices) ||
-                   !aligned16(a->logits_f32) || a->d > 32768))
-    return DSCA_ERR_BAD_ARG;
+  // the tensor-core logits: w_slices and w_exp, bf16 only; the scratch buffers (all three) only
+  // for d > 2048
+  const bool tc = a->w_slices != nullptr || a->w_exp != nullptr;
+  if (tc) {
+    if (a->w_slices == nullptr || a->w_exp == nullptr || a->dtype != DSCA_BF16 || !aligned16(a->w_slices) ||
+        a->d > 32768)
+      return DSCA_ERR_BAD_ARG;
+    if (!dsca::router_tc_fused_supported(a->d) &&
+        (a->x_slices == nullptr || a->x_exp == nullptr || a->logits_f32 == nullptr || !aligned16(a->x_slices) ||
+         !aligned16(a->logits_f32)))
+      return DSCA_ERR_BAD_ARG;
+  }
   if (a->T == 0) return DSCA_OK;
-  if (ntc == 5) return dsca::launch_router_tc(a, reinterpret_cast<cudaStream_t>(stream));
+  if (tc) return dsca::launch_router_tc(a, reinterpret_cast<cudaStream_t>(stream));
   return dsca::launch_router(a, reinterpret_cast<cudaStream_t>(stream));
 }
 

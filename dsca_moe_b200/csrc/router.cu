@@ -30,44 +30,21 @@
 // 32-bit token masks per expert.  With the fused scan, the last CTA to finish turns every
 // block's histogram into the per-expert counts, offsets and block bases (stable: block order,
 // then token order).
-#include "common.cuh"
+#include "router_select.cuh"
 
 namespace dsca {
 namespace router {
 
-constexpr int kTokens = DSCA_ROUTER_TOKENS;  // 32
-constexpr int kRows = 64;                    // router rows (E + shared gate <= 64)
 constexpr int kGroups = 4;                   // chunk pairs
 constexpr int kGroupThreads = 128;
-constexpr int kThreads = kGroups * kGroupThreads;  // 512
+static_assert(kGroups * kGroupThreads == kThreads, "512 threads per router CTA");
 constexpr int kKS = 16;                      // k slice (per chunk)
 constexpr int kXP = 2 * kKS + 4;             // floats per token row of the interleaved x slice
 constexpr int kWP = 2 * kKS + 4;             // floats per router row of the interleaved W slice
 constexpr int kStageFloats = kTokens * kXP + kRows * kWP;
-constexpr int kLP = kRows + 1;               // logit tile pitch
 constexpr size_t kSmemBytes = sizeof(float) * (size_t)(kGroups * 2 * kStageFloats);
 static_assert(kSmemBytes >= sizeof(float) * 8 * kTokens * kRows, "partials fit the staging area");
 
-struct Args {
-  const void* x;
-  const void* w_router;
-  const void* w_shared_gate;
-  int T, d, E, top_k, mode, norm_topk, weight_round_bf16;
-  void* logits;
-  int32_t* topk_ids;
-  float* topk_w;
-  int64_t* expert_index;
-  float* shared_gate;
-  int32_t* block_hist;
-  int32_t* local_rank;
-  int32_t* counts;
-  int32_t* offsets;
-  int32_t* block_base;
-  uint32_t* done_counter;
-  // precomputed logits [T][64] (fp32 values already rounded to the router dtype, rows past E
-  // unused), or null: the kernel computes them (the chunked fp32 order below)
-  const float* logits_in;
-};
 
 __device__ __forceinline__ void group_sync(int q) {
   asm volatile("bar.sync %0, %1;" ::"r"(q + 1), "r"(kGroupThreads) : "memory");
@@ -149,26 +126,6 @@ struct Slice {
 };
 static_assert(kXP == kWP, "one pitch for the x and W rows of a slice");
 
-template <typename T>
-__device__ __forceinline__ void store_logit(void* logits, size_t i, float v);
-template <>
-__device__ __forceinline__ void store_logit<__nv_bfloat16>(void* logits, size_t i, float v) {
-  reinterpret_cast<__nv_bfloat16*>(logits)[i] = __float2bfloat16_rn(v);
-}
-template <>
-__device__ __forceinline__ void store_logit<float>(void* logits, size_t i, float v) {
-  reinterpret_cast<float*>(logits)[i] = v;
-}
-
-// Order-preserving map of a (non-NaN) float onto uint32, and back.
-__device__ __forceinline__ uint32_t ord_key(float f) {
-  const uint32_t u = __float_as_uint(f);
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-__device__ __forceinline__ float ord_val(uint32_t k) {
-  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
-}
-
 // Two k of the slice for both chunks of the pair: 4 tokens x 4 rows of packed pairs.
 __device__ __forceinline__ void mma_k2(float2 (&acc)[4][4], const float* xb, const float* wb, int kk) {
   float4 xv[4], wv[4];
@@ -189,77 +146,6 @@ __device__ __forceinline__ void mma_k2(float2 (&acc)[4][4], const float* xb, con
       acc[i][j] = __ffma2_rn(make_float2(xv[i].z, xv[i].w), make_float2(wv[j].z, wv[j].w), acc[i][j]);
 }
 
-// Per-expert counts, offsets and block bases from all blocks' histograms (the last CTA).
-// The histograms pass through shared memory in chunks of rows.  Thread (c, e) (e = tid % 64,
-// c = tid / 64) sums a contiguous run of rows of column e (a warp reads 32 consecutive columns
-// of one row: no bank conflicts), the 8 run sums of a column give each run its base, and the
-// bases go back through shared memory to coalesced stores.
-__device__ void scan_blocks(const Args& a, int nb, int* sbuf, int cap_ints, int* run_s, int (*seg)[kRows]) {
-  constexpr int kSegs = kThreads / kRows;  // 8
-  const int E = a.E, tid = threadIdx.x;
-  const int e = tid % kRows, c = tid / kRows;
-  const int rows = max(1, min(nb, cap_ints / E));
-  if (tid < kRows) run_s[tid] = 0;
-  for (int b0 = 0; b0 < nb; b0 += rows) {
-    const int nr = min(rows, nb - b0), n = nr * E;
-    const int32_t* src = a.block_hist + (size_t)b0 * E;
-    constexpr int kBatch = 8;  // loads in flight per thread
-    for (int i0 = 0; i0 < n; i0 += kBatch * kThreads) {
-      int v[kBatch];
-#pragma unroll
-      for (int u = 0; u < kBatch; ++u) {
-        const int i = i0 + u * kThreads + tid;
-        v[u] = i < n ? __ldcg(src + i) : 0;
-      }
-#pragma unroll
-      for (int u = 0; u < kBatch; ++u) {
-        const int i = i0 + u * kThreads + tid;
-        if (i < n) sbuf[i] = v[u];
-      }
-    }
-    __syncthreads();
-    const int per = (nr + kSegs - 1) / kSegs;
-    const int r0 = min(nr, c * per), r1 = min(nr, r0 + per);
-    int sum = 0;
-    if (e < E)
-      for (int r = r0; r < r1; ++r) sum += sbuf[r * E + e];
-    seg[c][e] = sum;
-    __syncthreads();
-    if (e < E) {
-      int base = run_s[e];
-      for (int cc = 0; cc < c; ++cc) base += seg[cc][e];
-      for (int r = r0; r < r1; ++r) {
-        const int v = sbuf[r * E + e];
-        sbuf[r * E + e] = base;
-        base += v;
-      }
-    }
-    __syncthreads();
-    if (c == 0 && e < E) {
-      int tot = run_s[e];
-      for (int cc = 0; cc < kSegs; ++cc) tot += seg[cc][e];
-      run_s[e] = tot;
-    }
-    int32_t* dst = a.block_base + (size_t)b0 * E;
-    for (int i = tid; i < n; i += kThreads) dst[i] = sbuf[i];
-    __syncthreads();
-  }
-  // counts, and offsets by a warp-wide scan (lane L holds experts L and L + 32)
-  if (tid < 32) {
-    const int L = tid;
-    const int v0 = L < E ? run_s[L] : 0, v1 = L + 32 < E ? run_s[L + 32] : 0;
-    int i0 = v0, i1 = v1;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const int u0 = __shfl_up_sync(0xffffffffu, i0, off), u1 = __shfl_up_sync(0xffffffffu, i1, off);
-      if (L >= off) { i0 += u0; i1 += u1; }
-    }
-    const int tot0 = __shfl_sync(0xffffffffu, i0, 31), tot1 = __shfl_sync(0xffffffffu, i1, 31);
-    if (L < E) { a.counts[L] = v0; a.offsets[L] = i0 - v0; }
-    if (L + 32 < E) { a.counts[L + 32] = v1; a.offsets[L + 32] = tot0 + i1 - v1; }
-    if (L == 0) a.offsets[E] = tot0 + tot1;
-  }
-}
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) router_kernel(Args a) {
@@ -275,8 +161,6 @@ __global__ void __launch_bounds__(kThreads, 1) router_kernel(Args a) {
   const int q = tid / kGroupThreads;  // chunk group
   const int g = tid % kGroupThreads;
   const int tok0 = blockIdx.x * kTokens;
-  const int E = a.E;
-  const bool has_sg = a.w_shared_gate != nullptr;
   const bool tau_bf16 = sizeof(T) == 2;
   if (tid < kRows) emask[tid] = 0u;
 
@@ -352,103 +236,8 @@ __global__ void __launch_bounds__(kThreads, 1) router_kernel(Args a) {
   __syncthreads();
   }  // logits computed here
 
-  // ---------------- softmax and selection: one warp per token
-  const int warp = tid >> 5, lane = tid & 31;
-  const int e0 = lane, e1 = lane + 32;
-  const int k = (a.mode == DSCA_ROUTE_SWITCH_TOP1) ? 1 : a.top_k;
-  for (int tl = warp; tl < kTokens; tl += kThreads / 32) {
-    const int t = tok0 + tl;
-    const bool valid = t < a.T;
-    const float l0 = lg_s[tl * kLP + e0];
-    const float l1 = lg_s[tl * kLP + e1];
-    if (valid) {
-      if (e0 < E) store_logit<T>(a.logits, (size_t)t * E + e0, l0);
-      if (e1 < E) store_logit<T>(a.logits, (size_t)t * E + e1, l1);
-      if (has_sg && a.shared_gate != nullptr && (e0 == E || e1 == E)) {
-        const float z = (e0 == E) ? l0 : l1;
-        a.shared_gate[t] = 1.0f / (1.0f + expf(-z));
-      }
-    }
-    // row max through an order-preserving integer key (one warp reduction)
-    const uint32_t mkey = __reduce_max_sync(0xffffffffu, max((e0 < E) ? ord_key(l0) : 0u, (e1 < E) ? ord_key(l1) : 0u));
-    const float m = ord_val(mkey);
-    const float x0 = (e0 < E) ? exp_neg(__fsub_rn(l0, m)) : 0.0f;
-    const float x1 = (e1 < E) ? exp_neg(__fsub_rn(l1, m)) : 0.0f;
-    float ps = (e0 < E) ? __fadd_rn(0.0f, x0) : 0.0f;
-    if (e1 < E) ps = __fadd_rn(ps, x1);
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) ps = __fadd_rn(ps, __shfl_xor_sync(0xffffffffu, ps, off));
-    float p0 = (e0 < E) ? __fdiv_rn(x0, ps) : 0.0f;
-    float p1 = (e1 < E) ? __fdiv_rn(x1, ps) : 0.0f;
-    if (a.mode == DSCA_ROUTE_SWITCH_TOP1 && tau_bf16) {
-      p0 = round_bf16(p0);
-      p1 = round_bf16(p1);
-    }
-
-    // k rounds of (probability desc, expert id asc): probabilities are >= +0, so their bits
-    // order like the values; key = bits + 1, 0 = no candidate.  Lane j keeps the j-th choice;
-    // every lane sums the choices in rank order.
-    float my_p = 0.0f, sum = 0.0f;
-    int my_id = -1;
-    bool taken0 = !(e0 < E), taken1 = !(e1 < E);
-    for (int j = 0; j < k; ++j) {
-      const uint32_t k0 = taken0 ? 0u : __float_as_uint(p0) + 1u;
-      const uint32_t k1 = taken1 ? 0u : __float_as_uint(p1) + 1u;
-      const uint32_t best = __reduce_max_sync(0xffffffffu, max(k0, k1));
-      const uint32_t cand = (k0 == best) ? (uint32_t)e0 : ((k1 == best) ? (uint32_t)e1 : 0xffffffffu);
-      const int bi = (int)__reduce_min_sync(0xffffffffu, cand);
-      const float bv = __uint_as_float(best - 1u);
-      if (bi == e0) taken0 = true;
-      if (bi == e1) taken1 = true;
-      if (lane == j) { my_p = bv; my_id = bi; }
-      sum = __fadd_rn(sum, bv);
-    }
-    if (lane < k) {
-      ids_s[tl][lane] = valid ? my_id : -1;
-      if (valid) {
-        float w = my_p;
-        if (a.mode != DSCA_ROUTE_SWITCH_TOP1) {
-          if (a.norm_topk) w = __fdiv_rn(my_p, sum);
-          if (a.weight_round_bf16) w = round_bf16(w);
-        }
-        a.topk_ids[(size_t)t * k + lane] = my_id;
-        a.topk_w[(size_t)t * k + lane] = w;
-        if (lane == 0 && a.expert_index != nullptr) a.expert_index[t] = my_id;
-        atomicOr(&emask[my_id], 1u << tl);
-      }
-    }
-  }
-  __syncthreads();
-
-  // ---------------- per-block histogram and stable in-block ranks (token, then slot order):
-  // an expert appears at most once per token, so the rank of (t, j) is the number of earlier
-  // tokens of the block routed to the same expert
-  for (int e = tid; e < E; e += kThreads) {
-    a.block_hist[(size_t)blockIdx.x * E + e] = __popc(emask[e]);
-    if (a.done_counter != nullptr) __threadfence();  // the histogram before this CTA's arrival
-  }
-  for (int idx = tid; idx < kTokens * k; idx += kThreads) {
-    const int tl = idx / k, j = idx % k;
-    const int t = tok0 + tl;
-    const int e = ids_s[tl][j];
-    if (t >= a.T || e < 0) continue;
-    a.local_rank[(size_t)t * k + j] = __popc(emask[e] & ((1u << tl) - 1u));
-  }
-
-  // ---------------- fused scan: the last CTA to finish
-  if (a.done_counter != nullptr) {
-    __syncthreads();
-    if (tid == 0) {
-      const uint32_t prev = atomicAdd(a.done_counter, 1u);
-      is_last = prev == gridDim.x - 1;
-      __threadfence();
-    }
-    __syncthreads();
-    if (is_last) {
-      scan_blocks(a, gridDim.x, reinterpret_cast<int*>(smem), (int)(kSmemBytes / sizeof(int)), run_s, seg_s);
-      if (tid == 0) *a.done_counter = 0u;  // ready for the next launch (stream ordered)
-    }
-  }
+  select_block<T>(a, lg_s, ids_s, emask, run_s, seg_s, &is_last, reinterpret_cast<int*>(smem),
+                  (int)(kSmemBytes / sizeof(int)), (int)blockIdx.x, (int)gridDim.x, (int)gridDim.x);
 }
 
 }  // namespace router
@@ -456,30 +245,8 @@ __global__ void __launch_bounds__(kThreads, 1) router_kernel(Args a) {
 int launch_router(const dsca_router_args* p, cudaStream_t stream, const float* logits_in) {
   static PerDeviceOnce attr_once[2];
   router::Args a;
+  router::fill_args(p, &a);
   a.logits_in = logits_in;
-  a.x = p->x;
-  a.w_router = p->w_router;
-  a.w_shared_gate = p->w_shared_gate;
-  a.T = p->T;
-  a.d = p->d;
-  a.E = p->E;
-  a.top_k = p->mode == DSCA_ROUTE_SWITCH_TOP1 ? 1 : p->top_k;
-  a.mode = p->mode;
-  a.norm_topk = p->norm_topk;
-  a.weight_round_bf16 = p->weight_round_bf16;
-  a.logits = p->logits;
-  a.topk_ids = p->topk_ids;
-  a.topk_w = p->topk_w;
-  a.expert_index = p->expert_index;
-  a.shared_gate = p->shared_gate;
-  a.block_hist = p->block_hist;
-  a.local_rank = p->local_rank;
-  const bool fused = p->done_counter != nullptr && p->counts != nullptr && p->offsets != nullptr &&
-                     p->block_base != nullptr;
-  a.counts = fused ? p->counts : nullptr;
-  a.offsets = fused ? p->offsets : nullptr;
-  a.block_base = fused ? p->block_base : nullptr;
-  a.done_counter = fused ? p->done_counter : nullptr;
   const int nblocks = (p->T + router::kTokens - 1) / router::kTokens;
   cudaError_t e = cudaSuccess;
   if (p->dtype == DSCA_BF16) {

@@ -19,7 +19,7 @@
 //                      TMEM accumulators (5 x 64 columns); four epilogue warps combine them and
 //                      write fp32 logits [T][64] rounded to bf16.  No multicast.  Every wait is
 //                      bounded (2 s): a timeout records DSCA_ERR_WAIT_TIMEOUT, drains and frees TMEM.
-#include "common.cuh"
+#include "router_select.cuh"
 
 namespace dsca {
 
@@ -401,6 +401,357 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------ fused form (d <= 2048)
+//
+// One kernel from the bf16 rows to the routing outputs.  A cluster of kSplit CTAs takes a
+// 128-token tile; CTA r of the cluster owns K steps [r q, (r + 1) q) (q = ceil(ceil(d/128) / 4),
+// at most 4 steps of 128) and tokens [32 r, 32 r + 32) of the tile for the selection.
+//   1. The W slice planes of the CTA's K steps go to shared memory by TMA (no multicast).  Every
+//      thread loads its share of the tile's x rows for those K steps into registers (thread:
+//      rows (tid >> 4) + 32 u, u < 4, 16-byte chunk tid & 15 of each step) and reduces the
+//      rows' largest exponents over its 16-lane row group; the four CTAs exchange their partial
+//      maxima through distributed shared memory, giving every row its exponent R.
+//   2. Per K step the threads slice their registers into the three int8 planes: the magnitude
+//      F = floor(|v| 2^(147 - R)) is one fma rounded down (|v| 2^(147 - R) + 2^23, the integer
+//      part landing in the low mantissa bits; rows with R < 20 pre-scale by 2^64), byte
+//      permutes pack the 7-bit slices of four values per word, and negative values negate their
+//      bytes ((0x80 - b) ^ 0x80 per byte, selected by the sign mask).  The planes land in the
+//      128-byte-swizzled K-major layout of the MMA's A operand (two buffers); one thread issues
+//      the six int8 MMAs per 32-byte K step into the five TMEM accumulators of the three-kernel
+//      form above, overlapping the slicing of the next step.
+//   3. Each CTA combines its accumulators into one exact 64-bit partial per (token, router row)
+//      in shared memory; CTA r adds the four partials of its 32 tokens over distributed shared
+//      memory, forms the bf16 logits, and runs the selection of router_select.cuh (softmax,
+//      top-k, histogram, ranks, fused scan) on them.
+// F = floor(|v| 2^(147 - R)) equals the integer form of the C oracle's fixed_row (M << (13 - sh)
+// for sh <= 13, M >> (sh - 13) above), so the logits are the same bits as the three-kernel form.
+namespace fused {
+constexpr int kThreads = router::kThreads;      // 512
+constexpr int BM = 128;                         // tokens per tile = TMEM lanes
+constexpr int kSplit = 4;                       // CTAs per tile (K ranges)
+constexpr int kKStep = 128;                     // K per MMA stage (bytes of each slice plane)
+constexpr int kMaxSteps = 4;                    // K steps per CTA
+constexpr int kMaxD = kSplit * kMaxSteps * kKStep;  // 2048
+constexpr int kWPlane = kRows * kKStep;         // 8 KB: one W plane of one K step
+constexpr int kWStage = kSlices * kWPlane;      // 24 KB
+constexpr int kXPlane = BM * kKStep;            // 16 KB: one x plane of one K step
+constexpr int kXStage = kSlices * kXPlane;      // 48 KB
+constexpr int kPartPitch = kRows + 2;           // int64 per staged partial row (bank spread)
+constexpr int kSmemBytes = kMaxSteps * kWStage + 2 * kXStage + 1024;
+static_assert(BM * kPartPitch * 8 <= 2 * kXStage, "partials fit the x slice buffers");
+static_assert(kThreads == 16 * 32 && BM * (kKStep / 8) == 4 * kThreads, "four row chunks per thread and step");
+}  // namespace fused
+
+__device__ __forceinline__ int ld_dsmem_s32(uint32_t addr, uint32_t rank) {
+  int v;
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(mapa_shared(addr, rank)) : "memory");
+  return v;
+}
+__device__ __forceinline__ void ld_dsmem_2x64(uint32_t addr, uint32_t rank, long long& a, long long& b) {
+  asm volatile("ld.shared::cluster.v2.s64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "r"(mapa_shared(addr, rank)) : "memory");
+}
+__device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+// per byte: the sign of the selected byte replicated (selector nibble bit 3)
+__device__ __forceinline__ uint32_t prmt_sign(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+
+// Magnitude bits of one bf16 (bits in the high half of `f32bits`): 2^23 + floor(|v| 2^s) as an
+// fp32 bit pattern, so bits [0, 21) hold F.  pre = 2^64 when s > 127 (then scale = 2^(s - 64)).
+__device__ __forceinline__ uint32_t fixed_bits(uint32_t f32bits, float pre, float scale) {
+  const float v = fabsf(__uint_as_float(f32bits)) * pre;  // exact: a power of two, normal result
+  return __float_as_uint(__fmaf_rd(v, scale, 8388608.0f));
+}
+
+// Three slice words (plane 0 = F >> 14, plane 1 = (F >> 7) & 127, plane 2 = F & 127, signed)
+// of four values with magnitude bits t0..t3 and bf16 words w0 (values 0, 1) and w1 (values 2, 3).
+__device__ __forceinline__ void slice4(uint32_t t0, uint32_t t1, uint32_t t2, uint32_t t3, uint32_t w0, uint32_t w1,
+                                       uint32_t& p0, uint32_t& p1, uint32_t& p2) {
+  const uint32_t lo01 = __byte_perm(t0, t1, 0x5410), lo23 = __byte_perm(t2, t3, 0x5410);  // bits 0..15 of each
+  const uint32_t mi01 = __byte_perm(t0, t1, 0x6521), mi23 = __byte_perm(t2, t3, 0x6521);  // bits 8..23 of each
+  const uint32_t a2 = __byte_perm(lo01, lo23, 0x6420) & 0x7f7f7f7fu;
+  const uint32_t a1 = __byte_perm(lo01 >> 7, lo23 >> 7, 0x6420) & 0x7f7f7f7fu;
+  const uint32_t a0 = __byte_perm(mi01 >> 6, mi23 >> 6, 0x6420);  // bits 14..21 (bit 21 is 0)
+  const uint32_t m = prmt_sign(w0, w1, 0xFDB9u);                   // 0xff for negative values
+  const uint32_t n0 = (0x80808080u - a0) ^ 0x80808080u, n1 = (0x80808080u - a1) ^ 0x80808080u,
+                 n2 = (0x80808080u - a2) ^ 0x80808080u;
+  p0 = (a0 & ~m) | (n0 & m);
+  p1 = (a1 & ~m) | (n1 & m);
+  p2 = (a2 & ~m) | (n2 & m);
+}
+
+__global__ void __launch_bounds__(fused::kThreads, 1)
+    router_fused_kernel(const __grid_constant__ CUtensorMap tmW, const router::Args a, const int32_t* __restrict__ w_exp,
+                        int32_t* err) {
+  constexpr int BM = fused::BM, kSplit = fused::kSplit, kKStep = fused::kKStep, kMaxSteps = fused::kMaxSteps;
+  constexpr int kWPlane = fused::kWPlane, kWStage = fused::kWStage, kXPlane = fused::kXPlane;
+  constexpr int kXStage = fused::kXStage, kPartPitch = fused::kPartPitch, kSmemBytes = fused::kSmemBytes;
+  constexpr int kThreads = fused::kThreads;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  __shared__ uint64_t wfull[kMaxSteps], sfree[2], acc_full, mma_done;
+  __shared__ uint32_t tmem_base_s;
+  __shared__ int abort_s;
+  __shared__ int rpart[BM], rfin[BM], rw_s[kRows];
+  __shared__ float lg_s[router::kTokens * router::kLP];
+  __shared__ int ids_s[router::kTokens][DSCA_MAX_TOPK];
+  __shared__ uint32_t emask[kRows];
+  __shared__ int run_s[kRows];
+  __shared__ int seg_s[kThreads / kRows][kRows];
+  __shared__ int is_last;
+
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t w_base = smem_u32(smem);                             // [kMaxSteps][3][64][128]
+  uint8_t* xs = smem + kMaxSteps * kWStage;                           // [2][3][128][128]
+  const uint32_t x_base = smem_u32(xs);
+  const int tid = (int)threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  volatile int* abort_flag = &abort_s;
+  const uint32_t rank = cluster_ctarank();
+  const int row0 = (int)(blockIdx.x / kSplit) * BM;
+  const int T = a.T, d = a.d;
+  const int nks_total = (d + kKStep - 1) / kKStep;
+  const int q = (nks_total + kSplit - 1) / kSplit;
+  const int ks0 = min(nks_total, (int)rank * q);
+  const int nks = min(nks_total, ks0 + q) - ks0;
+
+  if (tid == 0) {
+    for (int s = 0; s < kMaxSteps; ++s) mbar_init(smem_u32(&wfull[s]), 1);
+    mbar_init(smem_u32(&sfree[0]), 1);
+    mbar_init(smem_u32(&sfree[1]), 1);
+    mbar_init(smem_u32(&acc_full), 1);
+    mbar_init(smem_u32(&mma_done), 1);
+    abort_s = 0;
+    fence_mbar_init();
+  }
+  if (tid < kRows) {
+    emask[tid] = 0u;
+    rw_s[tid] = w_exp[tid];
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&tmem_base_s), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_s;
+
+  if (tid == 0) {
+    prefetch_tmap(&tmW);
+    for (int s = 0; s < nks; ++s) {
+      const uint32_t bar = smem_u32(&wfull[s]);
+      mbar_arrive_expect_tx(bar, (uint32_t)kWStage);
+      const uint32_t dst = w_base + (uint32_t)(s * kWStage);
+      for (int j = 0; j < kSlices; ++j)
+        tma_load_2d(dst + (uint32_t)(j * kWPlane), &tmW, bar, (ks0 + s) * kKStep, j * kRows);
+    }
+  }
+
+  // ---------------- 1. x rows into registers, the rows' exponents
+  const int c16 = tid & 15;
+  uint4 xv[kMaxSteps][4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int t = row0 + (tid >> 4) + 32 * u;
+#pragma unroll
+    for (int s = 0; s < kMaxSteps; ++s) {
+      const int k = (ks0 + s) * kKStep + 8 * c16;
+      xv[s][u] = (s < nks && t < T && k < d)
+                     ? ldg_nc_v4(reinterpret_cast<const uint16_t*>(a.x) + (size_t)t * d + k)
+                     : make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    uint32_t m2 = 0u;
+#pragma unroll
+    for (int s = 0; s < kMaxSteps; ++s) {
+      m2 = __vmaxu2(m2, (xv[s][u].x >> 7) & 0x00ff00ffu);
+      m2 = __vmaxu2(m2, (xv[s][u].y >> 7) & 0x00ff00ffu);
+      m2 = __vmaxu2(m2, (xv[s][u].z >> 7) & 0x00ff00ffu);
+      m2 = __vmaxu2(m2, (xv[s][u].w >> 7) & 0x00ff00ffu);
+    }
+    int r = (int)max(m2 & 0xffffu, m2 >> 16);
+    r = max(r, __shfl_xor_sync(0xffffffffu, r, 8));
+    r = max(r, __shfl_xor_sync(0xffffffffu, r, 4));
+    r = max(r, __shfl_xor_sync(0xffffffffu, r, 2));
+    r = max(r, __shfl_xor_sync(0xffffffffu, r, 1));
+    if (c16 == 0) rpart[(tid >> 4) + 32 * u] = max(r, 1);
+  }
+  cluster_sync_all();  // every CTA's partial exponents
+  if (tid < BM) {
+    const uint32_t addr = smem_u32(&rpart[tid]);
+    int r = 1;
+    for (uint32_t src = 0; src < (uint32_t)kSplit; ++src) r = max(r, ld_dsmem_s32(addr, src));
+    rfin[tid] = r;
+  }
+  __syncthreads();
+
+  // ---------------- 2. slice each K step into the x planes; one thread issues the MMAs
+  float pre[4], scl[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int sh = 147 - rfin[(tid >> 4) + 32 * u];  // -107 .. 146
+    const bool big = sh > 127;
+    pre[u] = big ? __uint_as_float((uint32_t)(64 + 127) << 23) : 1.0f;
+    scl[u] = __uint_as_float((uint32_t)((big ? sh - 64 : sh) + 127) << 23);
+  }
+  bool issued = false;
+#pragma unroll
+  for (int s = 0; s < kMaxSteps; ++s) {
+    if (s >= nks) break;
+    const int b = s & 1;
+    if (s >= 2 && tid == 0) mbar_wait(smem_u32(&sfree[b]), (uint32_t)(((s - 2) >> 1) & 1), abort_flag, err);
+    __syncthreads();
+    if (abort_s) break;
+    uint8_t* xb = xs + b * kXStage;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int r = (tid >> 4) + 32 * u;
+      const uint4 v = xv[s][u];
+      const uint32_t t0 = fixed_bits(v.x << 16, pre[u], scl[u]), t1 = fixed_bits(v.x & 0xffff0000u, pre[u], scl[u]);
+      const uint32_t t2 = fixed_bits(v.y << 16, pre[u], scl[u]), t3 = fixed_bits(v.y & 0xffff0000u, pre[u], scl[u]);
+      const uint32_t t4 = fixed_bits(v.z << 16, pre[u], scl[u]), t5 = fixed_bits(v.z & 0xffff0000u, pre[u], scl[u]);
+      const uint32_t t6 = fixed_bits(v.w << 16, pre[u], scl[u]), t7 = fixed_bits(v.w & 0xffff0000u, pre[u], scl[u]);
+      uint32_t p0a, p1a, p2a, p0b, p1b, p2b;
+      slice4(t0, t1, t2, t3, v.x, v.y, p0a, p1a, p2a);
+      slice4(t4, t5, t6, t7, v.z, v.w, p0b, p1b, p2b);
+      // 8 bytes of K at offset 8 c16 of the row, 128-byte swizzle
+      const int off = r * kKStep + ((((c16 >> 1) ^ (r & 7))) << 4) + ((c16 & 1) << 3);
+      *reinterpret_cast<uint2*>(xb + off) = make_uint2(p0a, p0b);
+      *reinterpret_cast<uint2*>(xb + kXPlane + off) = make_uint2(p1a, p1b);
+      *reinterpret_cast<uint2*>(xb + 2 * kXPlane + off) = make_uint2(p2a, p2b);
+    }
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (tid == 32 && mbar_wait(smem_u32(&wfull[s]), 0u, abort_flag, err)) {
+      tc_fence_after();
+      constexpr uint32_t id128 = idesc_s8_s32(BM, 2 * kRows);
+      constexpr uint32_t id64 = idesc_s8_s32(BM, kRows);
+      const uint32_t xa = x_base + (uint32_t)(b * kXStage), wa = w_base + (uint32_t)(s * kWStage);
+      const uint64_t x0 = sw128_kmajor_desc(xa), x1 = sw128_kmajor_desc(xa + kXPlane),
+                     x2 = sw128_kmajor_desc(xa + 2 * kXPlane);
+      const uint64_t w01 = sw128_kmajor_desc(wa), w2 = sw128_kmajor_desc(wa + 2 * kWPlane);
+#pragma unroll
+      for (int k = 0; k < kKStep / 32; ++k) {
+        const uint64_t o = (uint64_t)(2 * k);  // 32 bytes of K
+        const uint32_t acc = (s > 0 || k > 0) ? 1u : 0u;
+        umma_i8(tmem_base + kColD01, x0 + o, w01 + o, id128, acc);       // X_0 W_0 | X_0 W_1
+        umma_i8(tmem_base + kColD23, x2 + o, w01 + o, id128, acc);       // X_2 W_0 | X_2 W_1
+        umma_i8(tmem_base + kColE12, x1 + o, w01 + o, id128, acc);       // X_1 W_0 | X_1 W_1
+        umma_i8(tmem_base + kColD4, x2 + o, w2 + o, id64, acc);          // X_2 W_2
+        umma_i8(tmem_base + kColD23, x0 + o, w2 + o, id64, 1u);          // + X_0 W_2 into D_2
+        umma_i8(tmem_base + kColD23 + kRows, x1 + o, w2 + o, id64, 1u);  // + X_1 W_2 into D_3
+      }
+      umma_commit(smem_u32(&sfree[b]));
+      if (s == nks - 1) umma_commit(smem_u32(&acc_full));
+      issued = true;
+    }
+  }
+  __syncthreads();
+  const bool aborted = abort_s != 0;
+  if (aborted) {
+    // let issued MMAs and TMA loads finish before the shared memory and TMEM go away
+    if (tid == 32 && issued) {
+      umma_commit(smem_u32(&mma_done));
+      drain(smem_u32(&mma_done), 0);
+    }
+    if (tid == 0)
+      for (int s = 0; s < nks; ++s) drain(smem_u32(&wfull[s]), 0);
+    __syncthreads();
+  }
+
+  // ---------------- 3. exact 64-bit partials of this CTA's K range
+  long long* part = reinterpret_cast<long long*>(xs);
+  {
+    const int lq = warp & 3, cg = warp >> 2;  // TMEM lane quarter; 16 router rows
+    const int tr = 32 * lq + lane;            // tile row held by this lane
+    bool have = nks > 0 && !aborted;
+    if (have) {
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait(smem_u32(&acc_full), 0u, abort_flag, err) ? 1 : 0;
+      have = __shfl_sync(0xffffffffu, ok, 0) != 0;
+    }
+    if (have) tc_fence_after();
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int e = 16 * cg + 8 * h;
+      long long pv[8];
+      if (have) {
+        const uint32_t ta = tmem_base + ((uint32_t)(32 * lq) << 16) + (uint32_t)e;
+        uint32_t d0[8], d1a[8], d1b[8], d2a[8], d2b[8], d3[8], d4[8];
+        tmem_ld8(ta + kColD01, d0);
+        tmem_ld8(ta + kColD01 + kRows, d1a);
+        tmem_ld8(ta + kColE12, d1b);
+        tmem_ld8(ta + kColD23, d2a);
+        tmem_ld8(ta + kColE12 + kRows, d2b);
+        tmem_ld8(ta + kColD23 + kRows, d3);
+        tmem_ld8(ta + kColD4, d4);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const long long D1 = (long long)(int)d1a[i] + (long long)(int)d1b[i];
+          const long long D2 = (long long)(int)d2a[i] + (long long)(int)d2b[i];
+          pv[i] = (long long)(int)d0[i] * (1ll << 28) + D1 * (1ll << 21) + D2 * (1ll << 14) +
+                  (long long)(int)d3[i] * (1ll << 7) + (long long)(int)d4[i];
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) pv[i] = 0;
+      }
+      long long* dst = part + (size_t)tr * kPartPitch + e;
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) *reinterpret_cast<longlong2*>(dst + i) = make_longlong2(pv[i], pv[i + 1]);
+    }
+  }
+  tc_fence_before();
+  cluster_sync_all();  // every CTA's partials staged
+  {
+    // tokens [32 rank, 32 rank + 32) of the tile: 4 router rows per thread
+    const int rl = tid >> 4, eg = 4 * (tid & 15);
+    const int tr = 32 * (int)rank + rl;
+    long long acc[4] = {0, 0, 0, 0};
+    const uint32_t addr = smem_u32(part + (size_t)tr * kPartPitch + eg);
+#pragma unroll
+    for (uint32_t src = 0; src < (uint32_t)kSplit; ++src) {
+      long long v0, v1, v2, v3;
+      ld_dsmem_2x64(addr, src, v0, v1);
+      ld_dsmem_2x64(addr + 16u, src, v2, v3);
+      acc[0] += v0;
+      acc[1] += v1;
+      acc[2] += v2;
+      acc[3] += v3;
+    }
+    const int rx = rfin[tr];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      lg_s[rl * router::kLP + eg + i] = round_bf16(scale_pow2(__ll2float_rn(acc[i]), rx + rw_s[eg + i] - 294));
+  }
+  cluster_sync_all();  // the peers have read this CTA's partials; lg_s complete
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+  const int nblocks = (T + router::kTokens - 1) / router::kTokens;
+  router::select_block<__nv_bfloat16>(a, lg_s, ids_s, emask, run_s, seg_s, &is_last, reinterpret_cast<int*>(smem),
+                                      kSmemBytes / (int)sizeof(int) - 256, (int)blockIdx.x, nblocks, (int)gridDim.x);
+}
+
 }  // namespace router_tc
 
 int launch_router(const dsca_router_args* p, cudaStream_t stream, const float* logits_in);
@@ -439,7 +790,43 @@ int launch_router_pack_i8(const void* rows, int R, int d, void* slices, int32_t*
   return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
 }
 
+// The fused form: d <= 2048.
+static int launch_router_fused(const dsca_router_args* a, cudaStream_t stream) {
+  static PerDeviceOnce attr_once;
+  const int T = a->T, d16 = (a->d + 15) & ~15;
+  CUtensorMap mw;
+  int rc;
+  if ((rc = make_map_u8(&mw, a->w_slices, (uint64_t)router_tc::kSlices * router_tc::kRows, (uint64_t)d16,
+                        router_tc::kRows)))
+    return rc;
+  auto kern = router_tc::router_fused_kernel;
+  if (attr_once.run([&] {
+        return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    router_tc::fused::kSmemBytes);
+      }) != cudaSuccess)
+    return DSCA_ERR_CUDA;
+  router::Args args;
+  router::fill_args(a, &args);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(((T + router_tc::fused::BM - 1) / router_tc::fused::BM) * router_tc::fused::kSplit));
+  cfg.blockDim = dim3(router_tc::fused::kThreads);
+  cfg.dynamicSmemBytes = router_tc::fused::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = router_tc::fused::kSplit;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, mw, args, a->w_exp, a->err) != cudaSuccess) return DSCA_ERR_CUDA;
+  return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
+}
+
+bool router_tc_fused_supported(int d) { return d <= router_tc::fused::kMaxD; }
+
 int launch_router_tc(const dsca_router_args* a, cudaStream_t stream) {
+  if (a->d <= router_tc::fused::kMaxD) return launch_router_fused(a, stream);
   static PerDeviceOnce attr_once;
   const int T = a->T, d16 = (a->d + 15) & ~15;
   router_tc::slice_rows_kernel<<<(T + 7) / 8, 256, 0, stream>>>(reinterpret_cast<const uint16_t*>(a->x), T, a->d,

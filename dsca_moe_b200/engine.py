@@ -454,7 +454,8 @@ class MoEEngine:
 
     # -------------------------------------------------------------- kernel steps
     def _router_tc_buffers(self, T: int) -> dict:
-        """Tensor-core router: the sliced router rows (once) and the per-call scratch for T tokens."""
+        """Tensor-core router: the sliced router rows (once), and for d > 2048 the per-call scratch for
+        T tokens."""
         if self.dtype != torch.bfloat16:
             raise ValueError("the tensor-core router takes bf16 inputs")
         d16 = _ceil(self.d, 16) * 16
@@ -466,6 +467,8 @@ class MoEEngine:
             self._w_exp = torch.empty(64, dtype=torch.int32, device=self.device)
             L.call("dsca_router_pack_i8", _ptr(self._w_rows), self._w_rows.shape[0], self.d, _ptr(self._w_slices),
                    _ptr(self._w_exp), _stream())
+        if self.d <= 2048:  # the fused kernel: no scratch
+            return {}
         tc = getattr(self, "_tc_ws", None)
         if tc is None or tc["x_exp"].shape[0] != T:
             dev = self.device
@@ -495,7 +498,8 @@ class MoEEngine:
         if self.router_tensor_cores:
             tc = self._router_tc_buffers(T)
             a.w_slices, a.w_exp = _ptr(self._w_slices), _ptr(self._w_exp)
-            a.x_slices, a.x_exp, a.logits_f32 = _ptr(tc["x_slices"]), _ptr(tc["x_exp"]), _ptr(tc["logits_f32"])
+            if tc:
+                a.x_slices, a.x_exp, a.logits_f32 = _ptr(tc["x_slices"]), _ptr(tc["x_exp"]), _ptr(tc["logits_f32"])
             a.err = _ptr(self.err)
         L.call("dsca_router_topk", ctypes.byref(a), _stream())
         self._mark("router")

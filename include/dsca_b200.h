@@ -102,12 +102,14 @@ typedef struct {
   int32_t* offsets;           /* [E + 1] */
   int32_t* block_base;        /* [ceil(T/32), E] */
   uint32_t* done_counter;
-  /* optional tensor-core logits (bf16): set all five or none; d16 = d rounded up to 16 */
+  /* optional tensor-core logits (bf16): w_slices and w_exp select them; d16 = d rounded up to 16.
+     d <= 2048 runs one fused kernel (clusters of four CTAs per 128 tokens) and needs no scratch;
+     a larger d needs the three scratch buffers as well (NULL otherwise) */
   const void* w_slices;       /* [3][64][d16] int8 from dsca_router_pack_i8 */
   const int32_t* w_exp;       /* [64] from dsca_router_pack_i8 */
-  void* x_slices;             /* [3][T][d16] int8 scratch */
-  int32_t* x_exp;             /* [T] scratch */
-  float* logits_f32;          /* [T][64] scratch */
+  void* x_slices;             /* [3][T][d16] int8 scratch (d > 2048) */
+  int32_t* x_exp;             /* [T] scratch (d > 2048) */
+  float* logits_f32;          /* [T][64] scratch (d > 2048) */
   int32_t* err;               /* device error word for the tensor-core pass's bounded waits, or NULL */
 } dsca_router_args;
 DSCA_API int dsca_router_topk(const dsca_router_args* a, dsca_stream_t stream);

@@ -134,11 +134,17 @@ def test_bad_args_rejected_without_gpu(lib):
     a.T = 0  # a valid empty call with all four set returns OK without launching
     a.block_base = a.done_counter = 4096
     assert lib.dsca_router_topk(ctypes.byref(a), None) == _lib.OK
-    # tensor-core logits: all five buffers or none, bf16 only (checked before any device call)
+    # tensor-core logits (checked before any device call): w_slices and w_exp together, bf16
+    # only, and above d = 2048 the three scratch buffers as well
     a.T = 32
-    a.w_slices = a.w_exp = a.x_slices = 4096
+    a.w_slices = 4096
     assert lib.dsca_router_topk(ctypes.byref(a), None) == _lib.ERR_BAD_ARG
-    a.x_exp = a.logits_f32 = 4096
+    a.w_exp = 4096
+    a.d = 2304
+    a.x_slices = a.x_exp = 4096
+    assert lib.dsca_router_topk(ctypes.byref(a), None) == _lib.ERR_BAD_ARG
+    a.d = 64
+    a.logits_f32 = 4096
     a.dtype = _lib.F32
     assert lib.dsca_router_topk(ctypes.byref(a), None) == _lib.ERR_BAD_ARG
     assert lib.dsca_router_pack_i8(None, 8, 64, None, None, None) == _lib.ERR_BAD_ARG

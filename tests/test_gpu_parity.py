@@ -524,7 +524,7 @@ def test_graph_replay_matches_eager(cuda, kind):
             assert torch.equal(v, ref[key]), key
 
 
-@pytest.mark.parametrize("T,d,E", [(131, 72, 64), (300, 2048, 60), (5, 64, 8), (1, 128, 64)])
+@pytest.mark.parametrize("T,d,E", [(131, 72, 64), (300, 2048, 60), (5, 64, 8), (1, 128, 64), (40, 2304, 16)])
 def test_tensor_core_router_edge_values(cuda, T, d, E):
     """The optional tensor-core router (bf16 logits by exact fixed-point accumulation on int8
     tcgen05 MMAs) equals the oracle's fixed-point logits bit for bit on rows with zeros,
@@ -571,6 +571,42 @@ def test_tensor_core_router_qwen_block(cuda):
     assert np.array_equal(r["topk_w"].cpu().numpy().view(np.uint32), w.view(np.uint32))
     z = O.router_logits_fixed(x, p["s_gate_w"])[:, 0].astype(np.float64)
     assert np.abs(r["shared_gate"].cpu().numpy() - 1.0 / (1.0 + np.exp(-z))).max() < 1e-6
+
+
+@pytest.mark.parametrize("T,d,E,k", [(4096, 2048, 60, 4), (4100, 2048, 60, 4), (20000, 768, 63, 8),
+                                     (70, 2304, 60, 4)])
+def test_tensor_core_router_scan_and_exactness(cuda, T, d, E, k):
+    """Tensor-core router (the fused one-kernel form for d <= 2048, the three-kernel form above
+    it): logits and top-k choices equal the fixed-point oracle bit for bit, the fused last-CTA
+    scan equals the separate scan launch and leaves its counter at zero, the permutation offsets
+    follow the choices, and token counts that are not a multiple of the 128-token tile leave no
+    stray histogram rows (the block output agrees across the three calls)."""
+    x = syn.hidden_states(T, d, 1201, "bf16")
+    Wg, _ = syn.router_weight(E, d, 1202, zipf_s=1.2, dtype="bf16")
+    eng = qwen_engine(Wg, syn.qwen_expert_weights(E, d, 64, 128, 1203, dtype="bf16"), k, False,
+                      torch.bfloat16, cuda)
+    eng.router_tensor_cores = True
+    keys = ("counts", "offsets", "block_base", "token_row", "out")
+    ws = eng._workspace(T)
+    xd = _t(x, torch.bfloat16, cuda)
+    got = []
+    for fused in (True, True, False):
+        eng.fuse_scan = fused
+        r = eng.forward(xd)
+        torch.cuda.synchronize()
+        eng.check()
+        got.append({kk: (ws[kk] if kk in ws else r[kk]).clone() for kk in keys})
+        assert int(eng._done_counter.item()) == 0
+    for kk in keys:
+        assert torch.equal(got[0][kk], got[2][kk]), kk
+        assert torch.equal(got[1][kk], got[2][kk]), kk
+    sample = np.arange(T) if T <= 4100 else syn.rng(1204).choice(T, 2000, replace=False)
+    lg = O.router_logits_fixed(x[sample], Wg)
+    ids, _ = O.route_topk(lg, k, False, "bf16")
+    assert np.array_equal(_np(r["logits"])[sample].view(np.uint32), lg.view(np.uint32))
+    assert np.array_equal(r["topk_ids"].cpu().numpy()[sample], ids)
+    _, _, offs = O.permutation_world1(r["topk_ids"].cpu().numpy(), E)
+    assert np.array_equal(got[0]["offsets"].cpu().numpy(), offs)
 
 
 @pytest.mark.parametrize("T,d,E,I,Is", [(4096, 2048, 60, 1408, 5632), (300, 256, 16, 128, 384)])
