@@ -10,14 +10,14 @@
 // Tile: 128 weight rows (TMEM lanes; SwiGLU: the gate and the up rows of 128 channels, two
 // slabs) x up to TBN tokens (the MMA N, rounded up to 16) x 64 K per stage.
 //   warp 0      TMA producer: the e4m3 weight rows (64-byte rows, 64-byte swizzle) and the f16
-//               token rows (128-byte swizzle) of each K step, 6-stage ring.  No multicast.
+//               token rows (128-byte swizzle) of each K step, 8-stage ring.  No multicast.
 //   warp 1      TMEM allocator; one thread issues tcgen05.mma kind::f16 with A in tensor memory
 //               (M128 N<=TBN K16, four per slab per stage).
 //   warps 2-5   epilogue: TMEM lane = weight row, column = token; x the row's scale, SiLU(g) * u
 //               (GEMM1) or ReLU or store; each warp stages its 32 x 32 block in shared memory
 //               and writes 16-byte pieces of token rows.
 //   warps 6-9   converters: thread = weight row; the row's 64 e4m3 bytes of the stage ->
-//               cvt.rn.f16x2.e4m3x2 -> tcgen05.st of 32 columns into one of two TMEM slabs.
+//               cvt.rn.f16x2.e4m3x2 -> tcgen05.st of 32 columns into one of four TMEM slab sets.
 // Every wait is bounded (2 s); a timeout records DSCA_ERR_WAIT_TIMEOUT, the producer and the MMA
 // thread drain what they issued, TMEM is freed and the kernel returns.
 #include <algorithm>
@@ -29,8 +29,8 @@ namespace gemm8t {
 
 constexpr int BM = 128;         // weight rows per tile = TMEM lanes
 constexpr int BK = 64;          // K per stage
-constexpr int kStages = 6;
-constexpr int kAStages = 2;     // converted weight slab sets in TMEM
+constexpr int kStages = 8;
+constexpr int kAStages = 4;     // converted weight slab sets in TMEM
 constexpr int kThreads = 320;
 constexpr int kTmemCols = 512;
 constexpr int kMaxGroups = 256;
