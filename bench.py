@@ -114,23 +114,28 @@ def parse():
                     help="one untimed forward of the workload and exit (the case profiled under ncu)")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="launch every kernel from the host each step instead of replaying a CUDA graph")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the skew-stress and fp8 batch-sweep configurations that the default "
+                         "block workload measures after the headline")
     ap.add_argument("--no-parity", action="store_true",
                     help="skip the untimed correctness check after the timing")
     return ap.parse_args()
 
 
-def flops_and_bytes(w, T, rows_routed, E_touched):
-    """Algorithmic work of one block forward on one GPU (no padding)."""
+def flops_and_bytes(w, T, rows_routed, E_touched, wbytes=2):
+    """Algorithmic work of one block forward on one GPU (no padding); `wbytes` per expert weight
+    (2 bf16, 1 fp8-e4m3 plus a 4-byte scale per output channel)."""
     d, I, Is, E = w["d"], w["inter"], w["shared"], w["E"]
     glu = w["act"] == "swiglu"
     m = 3 if glu else 2
     router = 2.0 * T * d * E
     g1 = 2.0 * rows_routed * d * (2 * I if glu else I) + (2.0 * T * d * 2 * Is if Is else 0.0)
     g2 = 2.0 * rows_routed * I * d + (2.0 * T * Is * d if Is else 0.0)
+    scales = 4.0 * ((2 * I if glu else I) + d) if wbytes == 1 else 0.0
     hbm = (2.0 * T * d * 2                       # x read, out write (bf16)
            + 2.0 * E * d                         # router weight
-           + 2.0 * E_touched * m * d * I         # experts touched at least once
-           + (2.0 * 3 * d * Is + 2.0 * d if Is else 0.0))
+           + E_touched * (wbytes * m * d * I + scales)   # experts touched at least once
+           + (wbytes * 3 * d * Is + 2.0 * d + (4.0 * (2 * Is + d) if wbytes == 1 else 0.0) if Is else 0.0))
     return router, g1, g2, hbm
 
 
@@ -581,6 +586,167 @@ def run_model(args):
         dist.destroy_process_group()
 
 
+SWEEP_TOKENS = (512, 2048, 8192, 32768, 65536)
+
+
+def max_over_ranks_pair(a, b, world, dev):
+    """(max over ranks of a, max over ranks of b)."""
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([a, b], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t[0]), float(t[1])
+
+
+def sub_config(label, w, T, router_w, experts, sgw, world, rank, dev, group, eq_tokens, flush, peaks, tc_peak,
+               steps, warmup, fp8):
+    """One more configuration of the block measured in the same run as the headline: a fresh
+    engine on the given packed weights and router, T tokens per GPU of N(0,1) hidden states,
+    the forward captured as a CUDA graph, `steps` device-timed replays (L2 flushed before each,
+    max over ranks), per-kernel phases from two eager marker steps, and an untimed check: the
+    output against the block in fp32 (torch, every token) and, with more than one GPU, against
+    the same tokens through a one-GPU engine (bit-identical expected).  Collective: every rank
+    calls it with the same arguments."""
+    import torch
+    import torch.distributed as dist
+
+    from dsca_moe_b200 import _lib as L
+    from dsca_moe_b200 import synthetic as syn
+    from dsca_moe_b200.engine import MoEEngine
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(vals):
+        t = torch.tensor(vals, dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.tolist()
+
+    kw = dict(top_k=w["k"], route_mode=L.ROUTE_SOFTMAX_TOPK if w["act"] == "swiglu" else L.ROUTE_SWITCH_TOP1,
+              shared_gate_weight=sgw)
+    eng = MoEEngine(router_w, experts, rank=rank, world=world, group=group, eq_tokens=eq_tokens, **kw)
+    x = torch.from_numpy(syn.hidden_states(T, w["d"], 7000 + T + rank, "bf16")).to(dev, torch.bfloat16)
+    graph = eng.capture(x)
+    for _ in range(warmup):
+        graph.replay()
+    barrier()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for a, b in evs:
+        flush.zero_()
+        a.record()
+        graph.replay()
+        b.record()
+    barrier()
+    ms = max_over_ranks([sum(a.elapsed_time(b) for a, b in evs) / steps])[0]
+    # phases (eager, with event markers between the launches)
+    eng.markers, eng.side_markers = [], []
+    for _ in range(2):
+        flush.zero_()
+        eng.forward(x)
+    torch.cuda.synchronize()
+    marks, eng.markers = eng.markers, None
+    ph = {}
+    for i in range(1, len(marks)):
+        if marks[i][0] != "start":
+            ph.setdefault(marks[i][0], []).append(marks[i - 1][1].elapsed_time(marks[i][1]))
+    for name, a, b in eng.side_markers:
+        ph.setdefault("side_" + name, []).append(a.elapsed_time(b))
+    ph = {k: statistics.mean(v) for k, v in ph.items()}
+    # routed rows computed on this rank and experts touched
+    r = eng.forward(x)
+    out, ids, tw = r["out"].clone(), r["topk_ids"].clone(), r["topk_w"].clone()
+    torch.cuda.synchronize()
+    eng.check()
+    if world == 1:
+        rows = T * w["k"]
+        counts = r["counts"].cpu().numpy()
+        migrated, a2a = None, None
+    else:
+        S, rows = eng.read_plan()
+        counts = S[:, :, rank].sum(axis=0)
+        owner = np.asarray(eng.expert_to_gpu)
+        migrated = int(sum(int(S[s_, e, g_]) for s_ in range(world) for e in range(eng.E) for g_ in range(world)
+                           if g_ != owner[e]))
+        row_b = w["d"] * 2
+        out_rows = int(S[rank].sum() - S[rank, :, rank].sum())
+        in_rows = int(S[:, :, rank].sum() - S[rank, :, rank].sum())
+        td, tr = ph.get("side_dispatch"), ph.get("side_return")
+        a2a = {"dispatch_bytes_out": out_rows * row_b, "return_bytes_out": in_rows * row_b,
+               "dispatch_gbs": (out_rows * row_b / (td / 1e3) / 1e9) if td else None,
+               "return_gbs": (in_rows * row_b / (tr / 1e3) / 1e9) if tr else None}
+    e_touched = int((np.asarray(counts) > 0).sum())
+    f_router, f_g1, f_g2, hbm = flops_and_bytes(w, T, rows, e_touched, wbytes=1 if fp8 else 2)
+    t_roof = max((f_router + f_g1 + f_g2) / (tc_peak * 1e12), hbm / (peaks["hbm"] * 1e9))
+    t_g = sum(v for k, v in ph.items() if k.startswith("gemm"))
+    res = {"config": label, "tokens_per_gpu": T, "expert_weights": "fp8-e4m3 + per-channel fp32 scales" if fp8
+           else "bf16", "value": T * world / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
+           "warmup": warmup, "layer_roofline_frac": t_roof * 1e3 / ms,
+           "layer_bound": "tensor" if (f_router + f_g1 + f_g2) / (tc_peak * 1e12) >= hbm / (peaks["hbm"] * 1e9)
+           else "hbm",
+           "gemm_tflops": ((f_g1 + f_g2) / (t_g / 1e3) / 1e12) if t_g else None,
+           "phases_ms": {k: round(v, 4) for k, v in ph.items()}, "tokens_migrated": migrated, "all_to_all": a2a}
+    # untimed check
+    ref = torch_block_fp32(eng, x, ids, tw)
+    err = rel_err(out, ref)
+    del ref
+    ok = err < 2e-2
+    eq1 = 1.0
+    if world > 1:
+        local = MoEEngine(router_w, experts, device=dev, **kw)
+        lr = local.forward(x)
+        torch.cuda.synchronize()
+        local.check()
+        eq1 = 1.0 if (torch.equal(lr["out"], out) and torch.equal(lr["topk_ids"], ids)) else 0.0
+        del local, lr
+    e_all, neq = max_over_ranks([err, -eq1])
+    same = bool(neq < -0.5)  # every rank's -eq1 is -1
+    res["parity"] = {"max_rel_err_fp32_all_ranks": e_all, "tol_max_rel": 2e-2,
+                     "routing_and_out_bit_identical_to_1gpu": same if world > 1 else None,
+                     "ok": bool(e_all < 2e-2 and ok and (world == 1 or same))}
+    del graph
+    eng.close()
+    del eng, x, out
+    torch.cuda.empty_cache()
+    barrier()
+    return res
+
+
+def extra_configs(args, w, eng, world, rank, dev, group, flush, peaks, tc_peak):
+    """The skew stress (16384 tokens per GPU, the headline's Zipf 1.5 router and weights) and the
+    fp8 batch sweep (fp8-e4m3 expert weights with per-channel scales, uniform router, 512 ... 65536
+    tokens per GPU; each point beside the same point with bf16 weights), at this run's GPU count."""
+    import torch
+
+    from dsca_moe_b200 import synthetic as syn
+    from dsca_moe_b200.engine import quantize_fp8
+
+    out = {}
+    sgw = eng.shared_gate_weight
+    out["skew_stress"] = sub_config("qwen-shaped block skew stress (zipf 1.5, harmony plan)", w, 16384,
+                                    eng.router_weight, eng.experts, sgw, world, rank, dev, group, args.eq_tokens,
+                                    flush, peaks, tc_peak, steps=10, warmup=3, fp8=False)
+    Wu, _ = syn.router_weight(w["E"], w["d"], 1234, zipf_s=None, dtype="bf16")
+    Wu = torch.from_numpy(Wu).to(dev, torch.bfloat16)
+    pe8 = quantize_fp8(eng.experts)
+    sweep = []
+    for T in SWEEP_TOKENS:
+        steps = 10 if T <= 8192 else 5
+        p8 = sub_config("fp8 batch sweep (uniform router)", w, T, Wu, pe8, sgw, world, rank, dev, group,
+                        args.eq_tokens, flush, peaks, tc_peak, steps=steps, warmup=3, fp8=True)
+        pb = sub_config("bf16 weights, same point", w, T, Wu, eng.experts, sgw, world, rank, dev, group,
+                        args.eq_tokens, flush, peaks, tc_peak, steps=steps, warmup=3, fp8=False)
+        sweep.append({"tokens_per_gpu": T, "fp8": p8, "bf16": pb, "fp8_over_bf16": p8["value"] / pb["value"]})
+    del pe8
+    torch.cuda.empty_cache()
+    out["fp8_sweep"] = sweep
+    return out
+
+
 def torch_block_fp32(eng, x, topk_ids, topk_w):
     """The block computed in fp32 with torch on the GPU from the same bf16 inputs and weights and
     the kernel's routing (ids and weights; the routing itself is bit-exact against the oracle in
@@ -910,6 +1076,35 @@ def run_ours(args, w, T):
         # the cache path reads the plan on the host every step: no pipelining across steps
         e2e_value, e2e_mode = e2e_serial, "serial (expert-cache path: host plan per step)"
 
+    # ---- the host link alone: this step's input in and output out (the same pinned buffers and
+    #      sizes), H2D and D2H on two streams at once on every rank together, no compute.  With
+    #      the device time this bounds the pipelined e2e: T / max(step, H2D, D2H) per rank.
+    link = None
+    if eng.cache is None:
+        s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+        n_link = max(args.steps, 10)
+        barrier()
+        a_in, b_in = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a_out, b_out = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a_in.record(s_in)
+        a_out.record(s_out)
+        for i in range(n_link):
+            with torch.cuda.stream(s_in):
+                x_dev.copy_(x_host, non_blocking=True)
+            with torch.cuda.stream(s_out):
+                outs_host[i & 1].copy_(x, non_blocking=True)
+        b_in.record(s_in)
+        b_out.record(s_out)
+        barrier()
+        x_dev.copy_(x)
+        t_in, t_out = max_over_ranks_pair(a_in.elapsed_time(b_in) / n_link, a_out.elapsed_time(b_out) / n_link,
+                                          world, dev)
+        nb = T * w["d"] * 2
+        link = {"h2d_gbs_per_rank": nb / (t_in / 1e3) / 1e9, "d2h_gbs_per_rank": nb / (t_out / 1e3) / 1e9,
+                "h2d_ms": t_in, "d2h_ms": t_out,
+                "e2e_bound_tokens_per_s": T * world / (max(ms_per_step, t_in, t_out) / 1e3),
+                "note": "every rank copies at once (slowest rank); both directions concurrently"}
+
     # ---- correctness of the measured configuration (untimed)
     parity = parity_check(eng, x, w, rank, world, dev, args.eq_tokens, graph) if not args.no_parity else None
 
@@ -938,7 +1133,8 @@ def run_ours(args, w, T):
                "peak_gbs": 770.0,
                "peak_kind": "peer copy per direction measured on this pool's B200s (900 nominal)",
                "note": "rank 0; dispatch and return run on a side stream beside the shared-expert GEMMs"}
-    f_router, f_g1, f_g2, hbm = flops_and_bytes(w, T, rows, e_touched)
+    wb = 1 if args.fp8 else 2  # bytes per expert weight
+    f_router, f_g1, f_g2, hbm = flops_and_bytes(w, T, rows, e_touched, wbytes=wb)
     # GEMM launches per step: gemm1 / gemm2 (one GPU) or their routed / shared halves (expert
     # parallel; the fused return names its routed GEMM2 gemm2_routed_fused)
     t_g1 = sum(v for k, v in phase_ms.items() if k.startswith("gemm1")) or float("nan")
@@ -961,8 +1157,8 @@ def run_ours(args, w, T):
     # read and write (bf16); the GEMMs are tensor-bound when FLOPs / tensor peak is the longer
     # time (Qwen block), HBM-bound otherwise (Switch layer at 1 GPU: ~64 rows per expert)
     glu = w["act"] == "swiglu"
-    gemm_bytes = (2.0 * e_touched * (3 if glu else 2) * w["d"] * w["inter"]
-                  + (2.0 * 3 * w["d"] * w["shared"] if w["shared"] else 0.0)
+    gemm_bytes = (wb * e_touched * (3 if glu else 2) * w["d"] * w["inter"]
+                  + (wb * 3 * w["d"] * w["shared"] if w["shared"] else 0.0)
                   + 2.0 * rows * (w["d"] + w["inter"]) * 2            # routed: rows in + h out + h in + y out
                   + (2.0 * T * (w["d"] + w["shared"]) * 2 if w["shared"] else 0.0))
     t_tc = (f_g1 + f_g2) / (tc_peak * 1e12)
@@ -1005,6 +1201,13 @@ def run_ours(args, w, T):
         layer_roof["frac_pcie"] = cache_info["h2d_bytes_per_step"] / (h2d_peak * 1e9) * 1e3 / ms_per_step
         del src, dst
 
+    # ---- the skew stress and the fp8 batch sweep at this GPU count (untimed for the headline;
+    #      each configuration timed on its own), after the headline configuration
+    extra = None
+    if (args.workload == "qwen" and args.tokens is None and not args.fp8 and w["zipf"] and eng.cache is None
+            and args.exchange == "p2p" and not args.no_extra):
+        extra = extra_configs(args, w, eng, world, rank, dev, group, flush, peaks, tc_peak)
+
     # ---- CPU baseline (rank 0, one GPU only)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -1032,11 +1235,12 @@ def run_ours(args, w, T):
                            if eng.router_tensor_cores else "CUDA cores: fp32 fma chains in the fixed chunk order")},
             "roofline": roof, "layer_roofline": layer_roof, "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * w["d"] * 2,
-                    "d2h_bytes_per_step": T * w["d"] * 2, "mode": e2e_mode, "serial_value": e2e_serial},
+                    "d2h_bytes_per_step": T * w["d"] * 2, "mode": e2e_mode, "serial_value": e2e_serial,
+                    "host_link": link},
             "gpu_launches": launches_per_step(world, args.exchange, eng) * args.steps, "clocks": clk,
             "parity": parity, "host": host,
             "expert_cache": cache_info,
-            "phases_ms": phase_ms, "all_to_all": a2a,
+            "phases_ms": phase_ms, "all_to_all": a2a, "other_configs": extra,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
