@@ -90,9 +90,9 @@ def parse():
                     help="bf16 expert GEMM tiles: 0 = default per GEMM, 256 = CTA pairs (cta_group::2, "
                          "weights as M), 128 = one CTA per 128-token tile, 512 = CTA pairs with whole "
                          "256-token blocks of the SwiGLU GEMM1 non-swapped (tokens as M)")
-    ap.add_argument("--tile-order", type=int, choices=[0, 1], default=0,
+    ap.add_argument("--tile-order", type=int, choices=[0, 1], default=None,
                     help="routed and shared tiles of one GEMM launch: 0 = one segment after the other, "
-                         "1 = interleaved")
+                         "1 = interleaved (default: the engine's)")
     ap.add_argument("--cache-hints", type=int, choices=[0, 1], default=0,
                     help="L2 policies of the GEMM loads: 1 = routed weights evict-first, the rest evict-last")
     ap.add_argument("--router-tc", type=int, choices=[0, 1], default=0,
@@ -114,6 +114,9 @@ def parse():
                     help="one untimed forward of the workload and exit (the case profiled under ncu)")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="launch every kernel from the host each step instead of replaying a CUDA graph")
+    ap.add_argument("--fp8-form", choices=["split", "smem", "tmem"], default="split",
+                    help="fp8 weights: split = e4m3 weights unconverted on kind::f8f6f4 MMAs against two-term "
+                         "e4m3 tokens; smem / tmem = weights converted to f16 in shared / tensor memory")
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the skew-stress and fp8 batch-sweep configurations that the default "
                          "block workload measures after the headline")
@@ -903,7 +906,12 @@ def run_ours(args, w, T):
     eng.exchange = args.exchange
     eng.ep_return = args.ep_return
     eng.tile_rows = args.tile_rows
-    eng.tile_order = args.tile_order
+    if args.fp8:
+        eng.fp8_split = args.fp8_form == "split"
+        if args.fp8_form == "tmem":
+            eng.tile_rows = 256
+    if args.tile_order is not None:
+        eng.tile_order = args.tile_order
     eng.cache_hints = args.cache_hints
     eng.qos_order = not args.no_qos_order
     eng.router_tensor_cores = bool(args.router_tc)
@@ -1228,7 +1236,10 @@ def run_ours(args, w, T):
                                256: "CTA-pair swap-AB tiles (256 channels x <=256 tokens)",
                                512: "CTA-pair tiles: SwiGLU GEMM1 whole 256-token blocks non-swapped "
                                     "(256 tokens x 128 channels), the rest swap-AB"}[args.tile_rows],
-                "tile_order": ["one segment after the other", "routed and shared tiles interleaved"][args.tile_order],
+                "tile_order": ["one segment after the other", "routed and shared tiles interleaved"][eng.tile_order],
+                "fp8_form": ({"split": "e4m3 weights unconverted (kind::f8f6f4) x two-term e4m3 tokens",
+                              "smem": "weights converted to f16 in shared memory",
+                              "tmem": "weights converted to f16 in tensor memory"}[args.fp8_form] if args.fp8 else None),
                 "l2_hints": ["default", "routed weights evict-first, the rest evict-last"][args.cache_hints],
                 "qos_order": (eng.qos_order if world > 1 else None),
                 "router": ("tensor cores: exact int8 fixed-point products, one fused kernel"

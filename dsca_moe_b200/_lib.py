@@ -44,7 +44,13 @@ class PermuteArgs(ctypes.Structure):
     _fields_ = [("x", _vp), ("T", _i), ("d", _i), ("E", _i), ("top_k", _i), ("dtype", _i),
                 ("topk_ids", _vp), ("local_rank", _vp), ("block_base", _vp), ("offsets", _vp),
                 ("G", _i), ("cum_split", _vp), ("dest_base", _vp), ("capacity", _i), ("out", _vp),
-                ("token_row", _vp), ("err", _vp), ("out_f16", _i), ("x_f16", _vp)]
+                ("token_row", _vp), ("err", _vp), ("out_f16", _i), ("x_f16", _vp),
+                ("out_e4m3", _i), ("out_scale", _vp), ("x_q", _vp), ("x_scale", _vp)]
+
+
+class SplitArgs(ctypes.Structure):
+    _fields_ = [("src", _vp), ("ld", _i), ("rows", _i), ("K", _i), ("rows_dev", _vp), ("dst", _vp),
+                ("inv_scale", _vp)]
 
 
 class FfnArgs(ctypes.Structure):
@@ -55,7 +61,9 @@ class FfnArgs(ctypes.Structure):
                 ("xs", _vp), ("ws1", _vp), ("ws2", _vp), ("hs", _vp), ("ys", _vp), ("err", _vp),
                 ("num_ctas", _i), ("phases", _i), ("ep_ctx", _vp), ("segments", _i),
                 ("w1_scale", _vp), ("w2_scale", _vp), ("ws1_scale", _vp), ("ws2_scale", _vp),
-                ("tile_rows", _i), ("pdl_after_permute", _i), ("group_order", _vp), ("cache_hints", _i), ("tile_order", _i)]
+                ("tile_rows", _i), ("pdl_after_permute", _i), ("group_order", _vp), ("cache_hints", _i), ("tile_order", _i),
+                ("f8_split", _i), ("a_scale", _vp), ("xs_scale", _vp), ("hq", _vp), ("hsq", _vp), ("h_scale", _vp),
+                ("hs_scale", _vp)]
 
 
 MAX_GPUS = 8
@@ -95,7 +103,7 @@ EXPORTED = ["dsca_version", "dsca_status_string", "dsca_device_info", "dsca_rout
             "dsca_grouped_ffn_static_scratch", "dsca_ep_ctx_bytes", "dsca_ep_init", "dsca_ep_group_offsets",
             "dsca_ep_plan", "dsca_ep_group_order", "dsca_ep_dispatch", "dsca_ep_wait", "dsca_ep_plan_eval", "dsca_ipc_export",
             "dsca_ipc_import", "dsca_ipc_close", "dsca_ep_read_plan", "dsca_ep_region_alloc",
-            "dsca_ep_region_free", "dsca_ep_return", "dsca_qos_priority", "dsca_router_pack_i8"]
+            "dsca_ep_region_free", "dsca_ep_return", "dsca_qos_priority", "dsca_router_pack_i8", "dsca_split_rows"]
 STATIC_SCRATCH_BYTES = 16 << 20
 
 _LIB = None
@@ -124,6 +132,7 @@ def load():
     lib.dsca_router_topk.argtypes = [p(RouterArgs), _vp]
     lib.dsca_dispatch_scan.argtypes = [p(ScanArgs), _vp]
     lib.dsca_permute.argtypes = [p(PermuteArgs), _vp]
+    lib.dsca_split_rows.argtypes = [p(SplitArgs), _vp]
     lib.dsca_grouped_ffn.argtypes = [p(FfnArgs), _vp]
     lib.dsca_grouped_ffn_static_scratch.argtypes = [p(FfnArgs), _vp]
     u64 = ctypes.c_uint64

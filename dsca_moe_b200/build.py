@@ -40,7 +40,9 @@ def _newer(src_list, target):
 def build(verbose: bool = False, ptxas_verbose: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
     os.makedirs(LIBDIR, exist_ok=True)
-    headers = [os.path.join(CSRC, "common.cuh"), os.path.join(CSRC, "router_select.cuh"), os.path.join(CSRC, "ep.cuh"), os.path.join(CSRC, "gemm_sm100.cuh"), os.path.join(INCLUDE, "dsca_b200.h")]
+    # every header of the package (a change to any of them rebuilds every object)
+    headers = sorted(os.path.join(CSRC, h) for h in os.listdir(CSRC) if h.endswith((".cuh", ".h")))
+    headers.append(os.path.join(INCLUDE, "dsca_b200.h"))
     objs = []
     for src in CU_SOURCES:
         s = os.path.join(CSRC, src)

@@ -18,6 +18,9 @@ int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t st
 int launch_grouped_ffn_f32(const dsca_ffn_args* f, int num_sms, cudaStream_t stream);
 int launch_grouped_ffn_fp8(const dsca_ffn_args* f, int num_sms, cudaStream_t stream);
 int launch_grouped_ffn_fp8_tmem(const dsca_ffn_args* f, int num_sms, cudaStream_t stream);
+int launch_grouped_ffn_f8_split(const dsca_ffn_args* f, int num_sms, cudaStream_t stream);
+int launch_split_rows(const void* src, int ld, int rows, const int32_t* rows_dev, int K, void* dst, float* inv_scale,
+                      cudaStream_t stream);
 }  // namespace dsca
 
 namespace {
@@ -142,7 +145,20 @@ int dsca_permute(const dsca_permute_args* a, dsca_stream_t stream) {
   } else {
     if (a->dest_base == nullptr || a->G <= 0 || a->G > DSCA_MAX_GPUS) return DSCA_ERR_BAD_ARG;
   }
+  if (a->out_e4m3) {
+    if (a->dtype != DSCA_BF16 || a->out_f16 || a->out_scale == nullptr || a->d % 8 != 0) return DSCA_ERR_BAD_ARG;
+    if (a->x_q != nullptr && (a->x_scale == nullptr || !aligned16(a->x_q))) return DSCA_ERR_BAD_ARG;
+  }
   return dsca::launch_permute(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int dsca_split_rows(const dsca_split_args* a, dsca_stream_t stream) {
+  if (a == nullptr || a->rows < 0 || a->K <= 0 || a->K % 8 != 0 || a->ld < a->K || a->ld % 8 != 0) return DSCA_ERR_BAD_ARG;
+  if (a->rows == 0) return DSCA_OK;
+  if (a->src == nullptr || a->dst == nullptr || a->inv_scale == nullptr || !aligned16(a->src) || !aligned16(a->dst))
+    return DSCA_ERR_BAD_ARG;
+  return dsca::launch_split_rows(a->src, a->ld, a->rows, a->rows_dev, a->K, a->dst, a->inv_scale,
+                                 reinterpret_cast<cudaStream_t>(stream));
 }
 
 int dsca_grouped_ffn(const dsca_ffn_args* f, dsca_stream_t stream) {
@@ -184,6 +200,15 @@ int dsca_grouped_ffn(const dsca_ffn_args* f, dsca_stream_t stream) {
     const void* ptrs[] = {f->a, f->w1, f->w2, f->h, f->y};
     for (const void* p : ptrs)
       if (!aligned16(p)) return DSCA_ERR_BAD_ARG;
+    if (f->f8_split) {
+      // e4m3 weights as they are, tokens as two e4m3 terms (CTA-pair kind::f8f6f4 tiles)
+      if (f->a_scale == nullptr || f->hq == nullptr || f->h_scale == nullptr || !aligned16(f->hq))
+        return DSCA_ERR_BAD_ARG;
+      if (f->shared_rows > 0 && (f->xs_scale == nullptr || f->hsq == nullptr || f->hs_scale == nullptr ||
+                                 !aligned16(f->xs) || !aligned16(f->hsq) || !aligned16(f->hs)))
+        return DSCA_ERR_BAD_ARG;
+      return dsca::launch_grouped_ffn_f8_split(f, num_sms, st);
+    }
     // tile_rows 256: weights converted into tensor memory (swap-AB); otherwise through shared memory
     if (f->tile_rows == 256) return dsca::launch_grouped_ffn_fp8_tmem(f, num_sms, st);
     return dsca::launch_grouped_ffn_fp8(f, num_sms, st);

@@ -10,6 +10,7 @@
 // Combine: deterministic gather-reduce (replaces router_probs * h at moe_layer.py:255-258 and
 // index_add_ + shared add at qwen_ep.py:92-94).
 #include "common.cuh"
+#include "fp8_split.cuh"
 
 namespace dsca {
 
@@ -105,6 +106,22 @@ __device__ __forceinline__ void permute_one(const dsca_permute_args& a, int w, i
     return;
   }
   if (lane == 0) a.token_row[w] = row;
+  if (ESZ == 2 && a.out_e4m3) {
+    // two e4m3 terms per value (fp8_split.cuh); the copy of x for the shared expert is written
+    // once per token, by its slot-0 warp
+    const int Kp = (a.d + 127) & ~127;
+    const uint16_t* xr = reinterpret_cast<const uint16_t*>(a.x) + (size_t)t * a.d;
+    uint8_t* dst = reinterpret_cast<uint8_t*>(a.out) + (size_t)row * 2 * Kp;
+    uint8_t* dq = (a.x_q != nullptr && (w % a.top_k) == 0)
+                      ? reinterpret_cast<uint8_t*>(a.x_q) + (size_t)t * 2 * Kp
+                      : nullptr;
+    const float inv = f8s::split_row(xr, a.d, Kp, dst, dq, lane);
+    if (lane == 0) {
+      a.out_scale[row] = inv;
+      if (dq != nullptr) a.x_scale[t] = inv;
+    }
+    return;
+  }
   const size_t row_bytes = (size_t)a.d * ESZ;
   const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(a.x) + (size_t)t * row_bytes);
   uint4* dstp = reinterpret_cast<uint4*>(reinterpret_cast<char*>(a.out) + (size_t)row * row_bytes);
@@ -153,6 +170,40 @@ __global__ void __launch_bounds__(256) permute_kernel(dsca_permute_args a) {
   const int nwarps = (int)(gridDim.x * (blockDim.x >> 5));
   for (int w = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); w < total; w += nwarps)
     permute_one<ESZ>(a, w, lane);
+}
+
+// dsca_split_rows: one warp per row, grid-stride over the rows.
+__global__ void __launch_bounds__(256) split_rows_kernel(dsca_split_args a) {
+  const int lane = lane_id();
+  int rows = a.rows;
+  if (a.rows_dev != nullptr) rows = min(rows, max(0, *a.rows_dev));
+  const int Kp = (a.K + 127) & ~127;
+  const int nwarps = (int)(gridDim.x * (blockDim.x >> 5));
+  for (int r = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); r < rows; r += nwarps) {
+    const uint16_t* src = reinterpret_cast<const uint16_t*>(a.src) + (size_t)r * a.ld;
+    uint8_t* dst = reinterpret_cast<uint8_t*>(a.dst) + (size_t)r * 2 * Kp;
+    const float inv = f8s::split_row(src, a.K, Kp, dst, nullptr, lane);
+    if (lane == 0) a.inv_scale[r] = inv;
+  }
+}
+
+int launch_split_rows(const void* src, int ld, int rows, const int32_t* rows_dev, int K, void* dst, float* inv_scale,
+                      cudaStream_t stream) {
+  if (rows <= 0) return DSCA_OK;
+  const int num_sms = current_device_sms();
+  if (num_sms == 0) return DSCA_ERR_CUDA;
+  dsca_split_args a;
+  a.src = src;
+  a.ld = ld;
+  a.rows = rows;
+  a.K = K;
+  a.rows_dev = rows_dev;
+  a.dst = dst;
+  a.inv_scale = inv_scale;
+  const long long need = ((long long)rows * 32 + 255) / 256;
+  const int blocks = (int)(need < 4LL * num_sms ? need : 4LL * num_sms);
+  split_rows_kernel<<<blocks, 256, 0, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
 }
 
 int launch_permute(const dsca_permute_args* a, cudaStream_t stream) {

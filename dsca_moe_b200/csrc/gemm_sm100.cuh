@@ -36,6 +36,11 @@ struct Segment {
   // expert parallel: when set, output row r of group e belongs to chunk (src, e) of the
   // receive buffer and is stored straight into rank src's return buffer (peer memory)
   const ep::Ctx* ep;
+  // fp8-e4m3 weights with two-term e4m3 tokens (pair kernel, F8): the lo plane's first byte
+  // column in a token row, 1 / s per token row, and the scale per packed weight row
+  int t_lo;
+  const float* t_scale;
+  const float* w_scale;
 };
 
 struct Params {
@@ -261,5 +266,10 @@ __device__ __forceinline__ float silu(float g) { return __fdividef(g, 1.0f + __e
 int make_map_bf16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows);
 // The CTA-pair swap-AB path of dsca_grouped_ffn (bf16).
 int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream_t stream);
+// dsca_grouped_ffn with fp8-e4m3 weights and two-term e4m3 tokens (f8_split = 1).
+int launch_grouped_ffn_f8_split(const dsca_ffn_args* f, int num_sms, cudaStream_t stream);
+// One warp per row: bf16 rows -> two-term e4m3 rows and 1 / s (fp8_split.cuh).
+int launch_split_rows(const void* src, int ld, int rows, const int32_t* rows_dev, int K, void* dst, float* inv_scale,
+                      cudaStream_t stream);
 
 }  // namespace dsca

@@ -35,16 +35,28 @@ namespace pair {
 // Per-epilogue configuration.  SwiGLU: a CTA's 128 channels need 128 gate rows (slot A) and the
 // 128 matching up rows (slot A2), two MMAs per K step into a gate and an up accumulator of N <=
 // 128 columns each.  Others: 128 weight rows (slot A), N <= 256.
-template <int EPI>
+//
+// F8 (fp8-e4m3 weights): a stage is 128 bytes of K per row as in bf16 — 128 e4m3 weights instead
+// of 64 bf16 — and the tokens come as two e4m3 planes (hi, lo; fp8_split.cuh), so each 32-byte K
+// step runs two tcgen05.mma.kind::f8f6f4 (W . hi, W . lo) into the same accumulator: the tensor
+// time per K element of the bf16 MMA, half its weight bytes, and no conversion of the weights.
+// The epilogue multiplies by the weight row's scale and the token row's 1 / s.
+// F8 SwiGLU takes up to 256 tokens a tile (an expert's rows in one tile up to 256, so each weight
+// block is streamed once): its gate and up accumulators fill the 512 TMEM columns, one buffer.
+template <int EPI, bool F8 = false>
 struct Cfg {
   static constexpr bool kGlu = EPI == kEpiSwiGLU;
-  static constexpr int S = kGlu ? 5 : 6;                  // stages
-  static constexpr int TBN = kGlu ? 128 : 256;            // token rows per tile (MMA N)
+  static constexpr int TBN = (kGlu && !F8) ? 128 : 256;  // token rows per tile (MMA N)
+  static constexpr int kAccBufs = (kGlu && F8) ? 1 : 2;  // accumulator buffers (256 columns each)
+  static constexpr int kUpCol = kGlu ? TBN : 0;          // SwiGLU: the up accumulator's column
+  static constexpr int S = F8 ? (kGlu ? 3 : 4) : (kGlu ? 5 : 6);  // stages
   static constexpr int kWBox = 128;                       // weight rows per TMA box
   static constexpr int kTBox = TBN / 2;                   // token rows per TMA box (one per stage)
-  static constexpr int kABytes = 128 * BK * 2;            // 16 KB
-  static constexpr int kA2Bytes = kGlu ? 128 * BK * 2 : 0;
-  static constexpr int kTBytes = (TBN / 2) * BK * 2;      // this CTA's token rows
+  static constexpr int kKE = F8 ? 128 : BK;               // K elements per stage (128 bytes a row)
+  static constexpr int kABytes = 128 * 128;               // 16 KB
+  static constexpr int kA2Bytes = kGlu ? 128 * 128 : 0;
+  static constexpr int kTPlane = (TBN / 2) * 128;         // this CTA's token rows, one plane
+  static constexpr int kTBytes = (F8 ? 2 : 1) * kTPlane;
   static constexpr int kStageBytes = kABytes + kA2Bytes + kTBytes;
   static constexpr int kStageElems = 32 * 32;             // epilogue staging per warp, bf16
   static constexpr int kSmemBytes = S * kStageBytes + 4 * kStageElems * 2 + 1024;
@@ -54,12 +66,28 @@ struct Cfg {
 // number of 8-row swizzle atoms).
 __device__ __forceinline__ int tile_n(int ntok) { return max(16, (ntok + 15) & ~15); }
 
-template <int EPI>
+// D(tmem) (+)= A(smem desc) * B(smem desc), e4m3 x e4m3, fp32 accumulate, CTA pair
+__device__ __forceinline__ void umma_f8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Instruction descriptor, kind::f8f6f4: A = B = e4m3 (format 0), D = f32, both K-major.
+__host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N) {
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+template <int EPI, bool F8>
 __global__ void __launch_bounds__(kThreads, 1)
     pair_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__ CUtensorMap tmT0,
                      const __grid_constant__ CUtensorMap tmW1, const __grid_constant__ CUtensorMap tmT1,
                      const Params p) {
-  using C = Cfg<EPI>;
+  using C = Cfg<EPI, F8>;
   constexpr int S = C::S;
   constexpr int TBN = C::TBN;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -142,7 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int kb_n = p.seg[ti.seg].k_blocks;
         // hybrid full tile (SwiGLU): this CTA's 128 tokens (two 64-row token boxes into slot A)
         // and the gate (even CTA) or up (odd CTA) rows of the tile's 128 channels (slot A2)
-        const bool full = C::kGlu && ti.full;
+        const bool full = !F8 && C::kGlu && ti.full;
         const int f_trow = ti.row0 + 128 * (int)rank, f_wrow = ti.b_row0 + 128 * (int)rank;
         constexpr uint32_t tx_full = 2u * (uint32_t)(C::kABytes + C::kA2Bytes);
         for (int kb = 0; kb < kb_n; ++kb) {
@@ -154,25 +182,31 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (full) {
             if (rank == 0) mbar_arrive_expect_tx(fb, tx_full);
             if (p.l2_hints) {
-              tma_load_2d_pair_hint(smem_a + s * C::kABytes, mt, fb0, kb * BK, f_trow, pol_last);
-              tma_load_2d_pair_hint(smem_a + s * C::kABytes + C::kABytes / 2, mt, fb0, kb * BK, f_trow + 64, pol_last);
-              tma_load_2d_pair_hint(smem_a2 + s * C::kA2Bytes, mw, fb0, kb * BK, f_wrow, wpol);
+              tma_load_2d_pair_hint(smem_a + s * C::kABytes, mt, fb0, kb * C::kKE, f_trow, pol_last);
+              tma_load_2d_pair_hint(smem_a + s * C::kABytes + C::kABytes / 2, mt, fb0, kb * C::kKE, f_trow + 64, pol_last);
+              tma_load_2d_pair_hint(smem_a2 + s * C::kA2Bytes, mw, fb0, kb * C::kKE, f_wrow, wpol);
             } else {
-              tma_load_2d_pair(smem_a + s * C::kABytes, mt, fb0, kb * BK, f_trow);
-              tma_load_2d_pair(smem_a + s * C::kABytes + C::kABytes / 2, mt, fb0, kb * BK, f_trow + 64);
-              tma_load_2d_pair(smem_a2 + s * C::kA2Bytes, mw, fb0, kb * BK, f_wrow);
+              tma_load_2d_pair(smem_a + s * C::kABytes, mt, fb0, kb * C::kKE, f_trow);
+              tma_load_2d_pair(smem_a + s * C::kABytes + C::kABytes / 2, mt, fb0, kb * C::kKE, f_trow + 64);
+              tma_load_2d_pair(smem_a2 + s * C::kA2Bytes, mw, fb0, kb * C::kKE, f_wrow);
             }
           } else {
             if (rank == 0) mbar_arrive_expect_tx(fb, tx);
             if (p.l2_hints) {
-              tma_load_2d_pair_hint(smem_a + s * C::kABytes, mw, fb0, kb * BK, w_row, wpol);
+              tma_load_2d_pair_hint(smem_a + s * C::kABytes, mw, fb0, kb * C::kKE, w_row, wpol);
               if constexpr (C::kGlu)
-                tma_load_2d_pair_hint(smem_a2 + s * C::kA2Bytes, mw, fb0, kb * BK, w_row + 128, wpol);
-              tma_load_2d_pair_hint(smem_t + s * C::kTBytes, mt, fb0, kb * BK, t_row, pol_last);
+                tma_load_2d_pair_hint(smem_a2 + s * C::kA2Bytes, mw, fb0, kb * C::kKE, w_row + 128, wpol);
+              tma_load_2d_pair_hint(smem_t + s * C::kTBytes, mt, fb0, kb * C::kKE, t_row, pol_last);
+              if constexpr (F8)  // the lo plane of the same token rows
+                tma_load_2d_pair_hint(smem_t + s * C::kTBytes + C::kTPlane, mt, fb0,
+                                      p.seg[ti.seg].t_lo + kb * C::kKE, t_row, pol_last);
             } else {
-              tma_load_2d_pair(smem_a + s * C::kABytes, mw, fb0, kb * BK, w_row);
-              if constexpr (C::kGlu) tma_load_2d_pair(smem_a2 + s * C::kA2Bytes, mw, fb0, kb * BK, w_row + 128);
-              tma_load_2d_pair(smem_t + s * C::kTBytes, mt, fb0, kb * BK, t_row);
+              tma_load_2d_pair(smem_a + s * C::kABytes, mw, fb0, kb * C::kKE, w_row);
+              if constexpr (C::kGlu) tma_load_2d_pair(smem_a2 + s * C::kA2Bytes, mw, fb0, kb * C::kKE, w_row + 128);
+              tma_load_2d_pair(smem_t + s * C::kTBytes, mt, fb0, kb * C::kKE, t_row);
+              if constexpr (F8)
+                tma_load_2d_pair(smem_t + s * C::kTBytes + C::kTPlane, mt, fb0, p.seg[ti.seg].t_lo + kb * C::kKE,
+                                 t_row);
             }
           }
           pending_phase[s] = (int)ph;
@@ -189,7 +223,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer (even CTA)
     if (lane == 0 && rank == 0) {
-      constexpr uint32_t idesc_m = idesc_bf16_f32(256, 0);
+      constexpr uint32_t idesc_m = F8 ? idesc_e4m3_f32(256, 0) : idesc_bf16_f32(256, 0);
       int s = 0;
       uint32_t ph = 0;
       int it = 0;
@@ -198,11 +232,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int tile = sched_tile(r, unit, units);
         if (tile >= total) break;
         const TileInfo ti = decode<TBN>(p, ctl, tile);
-        const bool full = C::kGlu && ti.full;
+        const bool full = !F8 && C::kGlu && ti.full;
         const uint32_t idesc = full ? idesc_bf16_f32(256, 256)
                                     : (idesc_m | ((uint32_t)(tile_n(ti.rows_valid) >> 3) << 17));
-        const int acc = it & 1;
-        const uint32_t acc_ph = (uint32_t)((it >> 1) & 1);
+        const int acc = it % C::kAccBufs;
+        const uint32_t acc_ph = (uint32_t)((it / C::kAccBufs) & 1);
         if (!mbar_wait(smem_u32(&ctl.tmem_empty[acc]), acc_ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * 256);
@@ -220,6 +254,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int k = 0; k < BK / 16; ++k)
               umma_f16_pair(d_tmem, adesc + (uint64_t)(2 * k), wdesc + (uint64_t)(2 * k), idesc,
                             (kb > 0 || k > 0) ? 1u : 0u);
+          } else if constexpr (F8) {
+            // two e4m3 MMAs per 32-byte K step: the weights times the hi and the lo token plane
+            const uint64_t ldesc = sw128_kmajor_desc(smem_t + s * C::kTBytes + C::kTPlane);
+#pragma unroll
+            for (int k = 0; k < C::kKE / 32; ++k) {
+              const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+              const uint64_t ko = (uint64_t)(2 * k);
+              umma_f8_pair(d_tmem, adesc + ko, tdesc + ko, idesc, accum);
+              umma_f8_pair(d_tmem, adesc + ko, ldesc + ko, idesc, 1u);
+              if constexpr (C::kGlu) {
+                const uint64_t udesc = sw128_kmajor_desc(smem_a2 + s * C::kA2Bytes);
+                umma_f8_pair(d_tmem + C::kUpCol, udesc + ko, tdesc + ko, idesc, accum);
+                umma_f8_pair(d_tmem + C::kUpCol, udesc + ko, ldesc + ko, idesc, 1u);
+              }
+            }
           } else {
 #pragma unroll
             for (int k = 0; k < BK / 16; ++k) {
@@ -259,8 +308,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (tile >= total) break;
       const TileInfo ti = decode<TBN>(p, ctl, tile);
       const Segment& sg = p.seg[ti.seg];
-      const int acc = it & 1;
-      const uint32_t acc_ph = (uint32_t)((it >> 1) & 1);
+      const int acc = it % C::kAccBufs;
+      const uint32_t acc_ph = (uint32_t)((it / C::kAccBufs) & 1);
       // one lane polls, the warp follows its verdict (tcgen05.ld below must not diverge)
       int w_ok = 1;
       if (lane == 0) w_ok = mbar_wait(smem_u32(&ctl.tmem_full[acc]), acc_ph, abort_flag, p.err) ? 1 : 0;
@@ -268,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!w_ok) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * 256);
-      if (C::kGlu && ti.full) {
+      if (!F8 && C::kGlu && ti.full) {
         // hybrid full tile: TMEM lane = this CTA's token 32 q + lane, columns 0-127 gate and
         // 128-255 up of channels 128 n_blk + [0, 128): each lane stores its row's 64-byte pieces
         const size_t row = (size_t)(ti.row0 + 128 * (int)rank + q * 32 + lane);
@@ -304,24 +353,47 @@ __global__ void __launch_bounds__(kThreads, 1)
       // this warp's 32 output channels: SwiGLU channel block n_blk (256 channels per pair);
       // otherwise weight rows of the 256-row block
       const int ch0 = ti.n_blk * 256 + 128 * (int)rank + 32 * q;
+      // F8: this lane's weight row scale(s) (gate and up for SwiGLU)
+      float wsc0 = 1.0f, wsc1 = 1.0f;
+      if constexpr (F8) {
+        const int wr = C::kGlu ? ti.b_row0 + ti.n_blk * BN + 256 * (int)rank + 32 * q + lane
+                               : ti.b_row0 + 128 * (int)rank + 32 * q + lane;
+        // SwiGLU: the odd CTA of a group's last tile holds no channels when ip % 256 == 128 (its
+        // weight rows lie past the group's); only channels below n_store read a scale
+        if (!C::kGlu || ch0 + lane < sg.n_store) {
+          wsc0 = __ldg(sg.w_scale + wr);
+          if constexpr (C::kGlu) wsc1 = __ldg(sg.w_scale + wr + 128);
+        }
+      }
       // staged output: each lane writes its channel for 32 tokens, then the warp stores whole
       // 64-byte token-row pieces with 16-byte stores
 #pragma unroll 1
       for (int c = 0; c < ncol; c += 32) {
+        // F8: the 1 / s of token c + lane, broadcast per token below
+        float tsv = 1.0f;
+        if constexpr (F8) tsv = (c + lane < ntok) ? __ldg(sg.t_scale + ti.row0 + c + lane) : 0.0f;
         uint32_t v[32];
         tmem_ld32(taddr + c, v);
         if constexpr (C::kGlu) {
           uint32_t u[32];
-          tmem_ld32(taddr + 128 + c, u);
+          tmem_ld32(taddr + C::kUpCol + c, u);
           tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            stg[j * 32 + lane] = __float2bfloat16_rn(silu(__uint_as_float(v[j])) * __uint_as_float(u[j]));
+          for (int j = 0; j < 32; ++j) {
+            float g = __uint_as_float(v[j]), up = __uint_as_float(u[j]);
+            if constexpr (F8) {
+              const float ts = __shfl_sync(0xffffffffu, tsv, j);
+              g = g * wsc0 * ts;
+              up = up * wsc1 * ts;
+            }
+            stg[j * 32 + lane] = __float2bfloat16_rn(silu(g) * up);
+          }
         } else {
           tmem_wait_ld();
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             float a = __uint_as_float(v[j]);
+            if constexpr (F8) a = a * wsc0 * __shfl_sync(0xffffffffu, tsv, j);
             if constexpr (EPI == kEpiReLU) a = fmaxf(a, 0.0f);
             stg[j * 32 + lane] = __float2bfloat16_rn(a);
           }
@@ -373,12 +445,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace pair
 }  // namespace gemm
 
-template <int EPI>
+template <int EPI, bool F8 = false>
 static int launch_pair(const CUtensorMap& w0, const CUtensorMap& t0, const CUtensorMap& w1, const CUtensorMap& t1,
                        const gemm::Params& p, int grid, cudaStream_t stream) {
   static PerDeviceOnce attr_once;
-  constexpr int smem_bytes = gemm::pair::Cfg<EPI>::kSmemBytes;
-  auto kern = gemm::pair::pair_gemm_kernel<EPI>;
+  constexpr int smem_bytes = gemm::pair::Cfg<EPI, F8>::kSmemBytes;
+  auto kern = gemm::pair::pair_gemm_kernel<EPI, F8>;
   if (attr_once.run([&] {
         return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
       }) != cudaSuccess)
@@ -411,7 +483,7 @@ static int max_resident_pairs(int num_sms) {
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) dev = -1;
   int cached = dev >= 0 ? __atomic_load_n(&cache[dev], __ATOMIC_ACQUIRE) - 1 : -1;
   if (cached < 0) {
-    auto kern = gemm::pair::pair_gemm_kernel<gemm::kEpiSwiGLU>;
+    auto kern = gemm::pair::pair_gemm_kernel<gemm::kEpiSwiGLU, false>;
     constexpr int smem_bytes = gemm::pair::Cfg<gemm::kEpiSwiGLU>::kSmemBytes;
     int n = 0;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) == cudaSuccess) {
@@ -571,6 +643,178 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
       s1.capacity = f->shared_rows;
     }
     if ((rc = launch_pair_one(gemm::kEpiStore, w0, t0, w1, t1, p, grid, stream))) return rc;
+  }
+  return DSCA_OK;
+}
+
+}  // namespace dsca
+
+// ------------------------------------------------------------------ fp8 weights, two-term tokens
+namespace dsca {
+
+// 2-D byte tensor map over a row-major [rows, cols] matrix (e4m3 weights or two-term token rows),
+// box = box_rows x 128 bytes, 128-byte swizzle.
+static int make_map_e4m3(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  typedef CUresult (*Encode)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                             const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                             CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  static Encode enc = nullptr;
+  if (enc == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return DSCA_ERR_CUDA;
+    enc = reinterpret_cast<Encode>(fn);
+  }
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || cols % 16 != 0) return DSCA_ERR_BAD_ARG;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols};
+  cuuint32_t box[2] = {128, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? DSCA_OK : DSCA_ERR_CUDA;
+}
+
+static int launch_pair_f8(int epi, const CUtensorMap& w0, const CUtensorMap& t0, const CUtensorMap& w1,
+                          const CUtensorMap& t1, const gemm::Params& p, int grid, cudaStream_t stream) {
+  switch (epi) {
+    case gemm::kEpiSwiGLU: return launch_pair<gemm::kEpiSwiGLU, true>(w0, t0, w1, t1, p, grid, stream);
+    case gemm::kEpiReLU: return launch_pair<gemm::kEpiReLU, true>(w0, t0, w1, t1, p, grid, stream);
+    default: return launch_pair<gemm::kEpiStore, true>(w0, t0, w1, t1, p, grid, stream);
+  }
+}
+
+// GEMM1 (e4m3 weights x two-term tokens) -> h, hs in bf16 -> split into hq, hsq -> GEMM2.
+int launch_grouped_ffn_f8_split(const dsca_ffn_args* f, int num_sms, cudaStream_t stream) {
+  const int want = f->num_ctas > 0 ? f->num_ctas : num_sms;
+  const int grid = 2 * std::max(1, std::min(want / 2, max_resident_pairs(num_sms)));
+  const int segs = f->segments == 0 ? 3 : f->segments;
+  const bool shared = f->shared_rows > 0 && (segs & 2);
+  const bool routed = (segs & 1) != 0;
+  const int phases = f->phases == 0 ? 3 : f->phases;
+  if (!routed && !shared) return DSCA_OK;
+  if (f->ep_ctx != nullptr) return DSCA_ERR_UNSUPPORTED;
+  if (f->n1p % 256 != 0 || f->dp % 256 != 0 || (shared && f->shared_n1p % 256 != 0)) return DSCA_ERR_BAD_ARG;
+  if (f->ip % 128 != 0 || (shared && f->shared_ip % 128 != 0) || f->d % 16 != 0) return DSCA_ERR_BAD_ARG;
+  const bool glu = f->act == DSCA_ACT_SWIGLU;
+  const int Kd = (f->d + 127) & ~127;  // token row: [hi: Kd | lo: Kd] bytes
+  int rc;
+  if (phases & 1) {
+    using CG = gemm::pair::Cfg<gemm::kEpiSwiGLU, true>;
+    using CR = gemm::pair::Cfg<gemm::kEpiReLU, true>;
+    const uint32_t tbox = glu ? CG::kTBox : CR::kTBox;
+    CUtensorMap w0, t0, w1, t1;
+    if ((rc = make_map_e4m3(&w0, f->w1, (uint64_t)f->num_experts_w * f->n1p, (uint64_t)f->d, CG::kWBox))) return rc;
+    if ((rc = make_map_e4m3(&t0, f->a, (uint64_t)std::max(f->capacity, 1), (uint64_t)2 * Kd, tbox))) return rc;
+    if (shared) {
+      if ((rc = make_map_e4m3(&w1, f->ws1, (uint64_t)f->shared_n1p, (uint64_t)f->d, CG::kWBox))) return rc;
+      if ((rc = make_map_e4m3(&t1, f->xs, (uint64_t)f->shared_rows, (uint64_t)2 * Kd, tbox))) return rc;
+    } else {
+      w1 = w0;
+      t1 = t0;
+    }
+    gemm::Params p{};
+    const int epi = glu ? gemm::kEpiSwiGLU : gemm::kEpiReLU;
+    p.epi = epi;
+    p.err = f->err;
+    p.nseg = shared ? 2 : 1;
+    p.seg_first = 0;
+    p.interleave_lead = -1;
+    p.l2_hints = f->cache_hints;
+    gemm::Segment& s0 = p.seg[0];
+    s0.group_offsets = f->group_offsets;
+    s0.group_weight = f->group_weight;
+    s0.group_order = f->group_order;
+    s0.ngroups = routed ? f->num_groups : 0;
+    s0.n_tiles = glu ? (f->ip + gemm::BN - 1) / gemm::BN : f->n1p / gemm::BN;
+    s0.b_rows_per_group = f->n1p;
+    s0.k_blocks = (f->d + 127) / 128;
+    s0.c = reinterpret_cast<__nv_bfloat16*>(f->h);
+    s0.ldc = f->ip;
+    s0.n_store = f->ip;
+    s0.capacity = f->capacity;
+    s0.t_lo = Kd;
+    s0.t_scale = f->a_scale;
+    s0.w_scale = f->w1_scale;
+    if (shared) {
+      gemm::Segment& s1 = p.seg[1];
+      s1.ngroups = 1;
+      s1.rows = f->shared_rows;
+      s1.n_tiles = glu ? (f->shared_ip + gemm::BN - 1) / gemm::BN : f->shared_n1p / gemm::BN;
+      s1.b_rows_per_group = f->shared_n1p;
+      s1.k_blocks = (f->d + 127) / 128;
+      s1.c = reinterpret_cast<__nv_bfloat16*>(f->hs);
+      s1.ldc = f->shared_ip;
+      s1.n_store = f->shared_ip;
+      s1.capacity = f->shared_rows;
+      s1.t_lo = Kd;
+      s1.t_scale = f->xs_scale;
+      s1.w_scale = f->ws1_scale;
+    }
+    if ((rc = launch_pair_f8(epi, w0, t0, w1, t1, p, grid, stream))) return rc;
+    // the intermediates as two-term rows for GEMM2 (routed rows: as many as the groups hold)
+    if (routed && (rc = launch_split_rows(f->h, f->ip, f->capacity, f->group_offsets + f->num_groups, f->ip, f->hq,
+                                          f->h_scale, stream)))
+      return rc;
+    if (shared && (rc = launch_split_rows(f->hs, f->shared_ip, f->shared_rows, nullptr, f->shared_ip, f->hsq,
+                                          f->hs_scale, stream)))
+      return rc;
+  }
+  if (phases & 2) {
+    using CS = gemm::pair::Cfg<gemm::kEpiStore, true>;
+    CUtensorMap w0, t0, w1, t1;
+    if ((rc = make_map_e4m3(&w0, f->w2, (uint64_t)f->num_experts_w * f->dp, (uint64_t)f->ip, CS::kWBox))) return rc;
+    if ((rc = make_map_e4m3(&t0, f->hq, (uint64_t)std::max(f->capacity, 1), (uint64_t)2 * f->ip, CS::kTBox)))
+      return rc;
+    if (shared) {
+      if ((rc = make_map_e4m3(&w1, f->ws2, (uint64_t)f->dp, (uint64_t)f->shared_ip, CS::kWBox))) return rc;
+      if ((rc = make_map_e4m3(&t1, f->hsq, (uint64_t)f->shared_rows, (uint64_t)2 * f->shared_ip, CS::kTBox)))
+        return rc;
+    } else {
+      w1 = w0;
+      t1 = t0;
+    }
+    gemm::Params p{};
+    p.epi = gemm::kEpiStore;
+    p.err = f->err;
+    p.nseg = shared ? 2 : 1;
+    p.seg_first = (shared && f->shared_ip > f->ip) ? 1 : 0;  // the longer K first
+    p.interleave_lead = -1;
+    p.l2_hints = f->cache_hints;
+    gemm::Segment& s0 = p.seg[0];
+    s0.group_offsets = f->group_offsets;
+    s0.group_weight = f->group_weight;
+    s0.group_order = f->group_order;
+    s0.ngroups = routed ? f->num_groups : 0;
+    s0.n_tiles = f->dp / gemm::BN;
+    s0.b_rows_per_group = f->dp;
+    s0.k_blocks = f->ip / 128;
+    s0.c = reinterpret_cast<__nv_bfloat16*>(f->y);
+    s0.ldc = f->d;
+    s0.n_store = f->d;
+    s0.capacity = f->capacity;
+    s0.t_lo = f->ip;
+    s0.t_scale = f->h_scale;
+    s0.w_scale = f->w2_scale;
+    if (shared) {
+      gemm::Segment& s1 = p.seg[1];
+      s1.ngroups = 1;
+      s1.rows = f->shared_rows;
+      s1.n_tiles = f->dp / gemm::BN;
+      s1.b_rows_per_group = f->dp;
+      s1.k_blocks = f->shared_ip / 128;
+      s1.c = reinterpret_cast<__nv_bfloat16*>(f->ys);
+      s1.ldc = f->d;
+      s1.n_store = f->d;
+      s1.capacity = f->shared_rows;
+      s1.t_lo = f->shared_ip;
+      s1.t_scale = f->hs_scale;
+      s1.w_scale = f->ws2_scale;
+    }
+    if ((rc = launch_pair_f8(gemm::kEpiStore, w0, t0, w1, t1, p, grid, stream))) return rc;
   }
   return DSCA_OK;
 }

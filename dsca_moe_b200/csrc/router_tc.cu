@@ -417,8 +417,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 //      permutes pack the 7-bit slices of four values per word, and negative values negate their
 //      bytes ((0x80 - b) ^ 0x80 per byte, selected by the sign mask).  The planes land in the
 //      128-byte-swizzled K-major layout of the MMA's A operand (two buffers); one thread issues
-//      the six int8 MMAs per 32-byte K step into the five TMEM accumulators of the three-kernel
-//      form above, overlapping the slicing of the next step.
+//      three int8 MMAs per 32-byte K step, X_j against the stacked planes [W_0; W_1; W_2]
+//      (N = 192) into the column window of D_j .. D_j+2 of five zeroed TMEM accumulators,
+//      overlapping the slicing of the next step.
 //   3. Each CTA combines its accumulators into one exact 64-bit partial per (token, router row)
 //      in shared memory; CTA r adds the four partials of its 32 tokens over distributed shared
 //      memory, forms the bf16 logits, and runs the selection of router_select.cuh (softmax,
@@ -466,6 +467,15 @@ __device__ __forceinline__ uint32_t prmt_sign(uint32_t a, uint32_t b, uint32_t s
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+// 32 lanes x 32 consecutive 32-bit columns of zeros (thread i of the warp writes lane base + i)
+__device__ __forceinline__ void tmem_st32_zero(uint32_t taddr) {
+  const uint32_t z = 0u;
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
+      "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
@@ -593,7 +603,16 @@ __global__ void __launch_bounds__(fused::kThreads, 1)
     r = max(r, __shfl_xor_sync(0xffffffffu, r, 1));
     if (c16 == 0) rpart[(tid >> 4) + 32 * u] = max(r, 1);
   }
-  cluster_sync_all();  // every CTA's partial exponents
+  if (warp < 4) {
+    // the five accumulators start at zero (the MMAs below all accumulate): columns [0, 320) of
+    // lane quarter `warp`
+    const uint32_t z = tmem_base + ((uint32_t)(32 * warp) << 16);
+#pragma unroll 1
+    for (int c = 0; c < kAcc * kRows; c += 32) tmem_st32_zero(z + (uint32_t)c);
+    tmem_wait_st();
+    tc_fence_before();
+  }
+  cluster_sync_all();  // every CTA's partial exponents; the accumulators are zeroed
   if (tid < BM) {
     const uint32_t addr = smem_u32(&rpart[tid]);
     int r = 1;
@@ -641,22 +660,20 @@ __global__ void __launch_bounds__(fused::kThreads, 1)
     __syncthreads();
     if (tid == 32 && mbar_wait(smem_u32(&wfull[s]), 0u, abort_flag, err)) {
       tc_fence_after();
-      constexpr uint32_t id128 = idesc_s8_s32(BM, 2 * kRows);
-      constexpr uint32_t id64 = idesc_s8_s32(BM, kRows);
+      // X_j times the three stacked router slice planes [W_0; W_1; W_2] (N = 192) lands on the
+      // accumulators D_j | D_j+1 | D_j+2: the three MMAs write overlapping 192-column windows of
+      // the 320 zeroed columns D_0 .. D_4 (64 each), so D_s = sum_{j+k=s} X_j W_k
+      constexpr uint32_t id192 = idesc_s8_s32(BM, 3 * kRows);
       const uint32_t xa = x_base + (uint32_t)(b * kXStage), wa = w_base + (uint32_t)(s * kWStage);
       const uint64_t x0 = sw128_kmajor_desc(xa), x1 = sw128_kmajor_desc(xa + kXPlane),
                      x2 = sw128_kmajor_desc(xa + 2 * kXPlane);
-      const uint64_t w01 = sw128_kmajor_desc(wa), w2 = sw128_kmajor_desc(wa + 2 * kWPlane);
+      const uint64_t w012 = sw128_kmajor_desc(wa);
 #pragma unroll
       for (int k = 0; k < kKStep / 32; ++k) {
         const uint64_t o = (uint64_t)(2 * k);  // 32 bytes of K
-        const uint32_t acc = (s > 0 || k > 0) ? 1u : 0u;
-        umma_i8(tmem_base + kColD01, x0 + o, w01 + o, id128, acc);       // X_0 W_0 | X_0 W_1
-        umma_i8(tmem_base + kColD23, x2 + o, w01 + o, id128, acc);       // X_2 W_0 | X_2 W_1
-        umma_i8(tmem_base + kColE12, x1 + o, w01 + o, id128, acc);       // X_1 W_0 | X_1 W_1
-        umma_i8(tmem_base + kColD4, x2 + o, w2 + o, id64, acc);          // X_2 W_2
-        umma_i8(tmem_base + kColD23, x0 + o, w2 + o, id64, 1u);          // + X_0 W_2 into D_2
-        umma_i8(tmem_base + kColD23 + kRows, x1 + o, w2 + o, id64, 1u);  // + X_1 W_2 into D_3
+        umma_i8(tmem_base, x0 + o, w012 + o, id192, 1u);              // D_0 | D_1 | D_2 += X_0 W
+        umma_i8(tmem_base + kRows, x1 + o, w012 + o, id192, 1u);      // D_1 | D_2 | D_3 += X_1 W
+        umma_i8(tmem_base + 2 * kRows, x2 + o, w012 + o, id192, 1u);  // D_2 | D_3 | D_4 += X_2 W
       }
       umma_commit(smem_u32(&sfree[b]));
       if (s == nks - 1) umma_commit(smem_u32(&acc_full));
@@ -694,22 +711,17 @@ __global__ void __launch_bounds__(fused::kThreads, 1)
       long long pv[8];
       if (have) {
         const uint32_t ta = tmem_base + ((uint32_t)(32 * lq) << 16) + (uint32_t)e;
-        uint32_t d0[8], d1a[8], d1b[8], d2a[8], d2b[8], d3[8], d4[8];
-        tmem_ld8(ta + kColD01, d0);
-        tmem_ld8(ta + kColD01 + kRows, d1a);
-        tmem_ld8(ta + kColE12, d1b);
-        tmem_ld8(ta + kColD23, d2a);
-        tmem_ld8(ta + kColE12 + kRows, d2b);
-        tmem_ld8(ta + kColD23 + kRows, d3);
-        tmem_ld8(ta + kColD4, d4);
+        uint32_t d0[8], d1[8], d2[8], d3[8], d4[8];
+        tmem_ld8(ta, d0);
+        tmem_ld8(ta + kRows, d1);
+        tmem_ld8(ta + 2 * kRows, d2);
+        tmem_ld8(ta + 3 * kRows, d3);
+        tmem_ld8(ta + 4 * kRows, d4);
         tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const long long D1 = (long long)(int)d1a[i] + (long long)(int)d1b[i];
-          const long long D2 = (long long)(int)d2a[i] + (long long)(int)d2b[i];
-          pv[i] = (long long)(int)d0[i] * (1ll << 28) + D1 * (1ll << 21) + D2 * (1ll << 14) +
-                  (long long)(int)d3[i] * (1ll << 7) + (long long)(int)d4[i];
-        }
+        for (int i = 0; i < 8; ++i)
+          pv[i] = (long long)(int)d0[i] * (1ll << 28) + (long long)(int)d1[i] * (1ll << 21) +
+                  (long long)(int)d2[i] * (1ll << 14) + (long long)(int)d3[i] * (1ll << 7) + (long long)(int)d4[i];
       } else {
 #pragma unroll
         for (int i = 0; i < 8; ++i) pv[i] = 0;

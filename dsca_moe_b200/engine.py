@@ -326,6 +326,10 @@ class MoEEngine:
             experts = replace(experts, w1=self.cache.w1, w2=self.cache.w2, E=int(cache_slots),
                               ws1=None if experts.ws1 is None else experts.ws1.to(self.device),
                               ws2=None if experts.ws2 is None else experts.ws2.to(self.device))
+        # fp8 weights: True = the e4m3 weights go to the tensor cores unconverted (kind::f8f6f4)
+        # against the tokens held as two e4m3 terms (dsca_split_rows); False = the weights are
+        # converted to f16 inside the GEMM (tile_rows picks shared or tensor memory)
+        self.fp8_split = bool(experts.fp8)
         # QoS planner constants (src/qosmoe/config.py:30-43), used by the expert-cache path
         self.qos_params = dict(alpha=1.0, beta=0.1, delta=0.5, target_batch=64.0, epsilon=1e-6, attention_mode=0)
         self.last_exec_plan = None
@@ -421,8 +425,12 @@ class MoEEngine:
         return self.cache is not None or ((self.world > 1 or self.ep_loopback) and self.exchange == "p2p")
 
     # -------------------------------------------------------------- workspace
+    @property
+    def _split(self) -> bool:
+        return bool(self.experts.fp8 and self.fp8_split)
+
     def _workspace(self, T: int) -> dict:
-        ws = self._ws.get(T)
+        ws = self._ws.get((T, self._split))
         if ws is not None:
             return ws
         dev, dt, k, E, d = self.device, self.dtype, self.top_k, self.E, self.d
@@ -445,11 +453,29 @@ class MoEEngine:
             ys=torch.empty(T, d, dtype=dt, device=dev) if pe.ws1 is not None else None,
             x_f16=torch.empty(T, d, dtype=torch.float16, device=dev) if (pe.fp8 and pe.ws1 is not None) else None,
         )
-        if self.world == 1:
+        if self._split:
+            # two-term e4m3 token rows ([hi | lo], kd bytes each) with 1 / s per row; bf16
+            # intermediates, split again for GEMM2
+            kd = _ceil(d, 128) * 128
+            ws["x_f16"] = None
+            if pe.ws1 is not None:
+                ws.update(hs=torch.empty(T, pe.s_ip, dtype=torch.bfloat16, device=dev),
+                          x_q=torch.empty(T, 2 * kd, dtype=torch.uint8, device=dev),
+                          x_scale=torch.empty(T, dtype=torch.float32, device=dev),
+                          hsq=torch.empty(T, 2 * pe.s_ip, dtype=torch.uint8, device=dev),
+                          hs_scale=torch.empty(T, dtype=torch.float32, device=dev))
+            if self.world == 1:
+                ws.update(a=torch.empty(cap, 2 * kd, dtype=torch.uint8, device=dev),
+                          a_scale=torch.empty(cap, dtype=torch.float32, device=dev),
+                          h=torch.empty(cap, pe.ip, dtype=torch.bfloat16, device=dev),
+                          hq=torch.empty(cap, 2 * pe.ip, dtype=torch.uint8, device=dev),
+                          h_scale=torch.empty(cap, dtype=torch.float32, device=dev),
+                          y=torch.empty(cap, d, dtype=dt, device=dev))
+        elif self.world == 1:
             ws.update(a=torch.empty(cap, d, dtype=self.op_dtype, device=dev),
                       h=torch.empty(cap, pe.ip, dtype=self.op_dtype, device=dev),
                       y=torch.empty(cap, d, dtype=dt, device=dev))
-        self._ws = {T: ws}  # keep one shape resident
+        self._ws = {(T, self._split): ws}  # keep one shape resident
         return ws
 
     # -------------------------------------------------------------- kernel steps
@@ -517,9 +543,20 @@ class MoEEngine:
         p.offsets = _ptr(ws["offsets"])
         p.G, p.cum_split, p.dest_base = G, _ptr(cum_split), _ptr(dest_base)
         p.capacity, p.out, p.token_row, p.err = capacity, _ptr(out), _ptr(ws["token_row"]), _ptr(self.err)
-        p.out_f16 = int(self.experts.fp8)
-        p.x_f16 = _ptr(ws.get("x_f16"))
+        if self._split:
+            p.out_e4m3, p.out_scale = 1, _ptr(ws["a_scale"])
+            p.x_q, p.x_scale = _ptr(ws.get("x_q")), _ptr(ws.get("x_scale"))
+        else:
+            p.out_f16 = int(self.experts.fp8)
+            p.x_f16 = _ptr(ws.get("x_f16"))
         L.call("dsca_permute", ctypes.byref(p), _stream())
+
+    def _split_rows(self, src, rows, K, dst, inv_scale, rows_dev=0):
+        """dsca_split_rows: bf16 rows [rows, K] -> two-term e4m3 rows and 1 / s."""
+        a = L.SplitArgs()
+        a.src, a.ld, a.rows, a.K = _ptr(src), src.shape[1], rows, K
+        a.rows_dev, a.dst, a.inv_scale = rows_dev, _ptr(dst), _ptr(inv_scale)
+        L.call("dsca_split_rows", ctypes.byref(a), _stream())
 
     def _ffn(self, x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, ep_ctx=None,
              after_permute=False):
@@ -535,7 +572,9 @@ class MoEEngine:
                            after_permute=after_permute)
 
     def _ffn_call(self, x, ws, a, h, y, capacity, num_groups, group_offsets, group_weight, phases, ep_ctx=None,
-                  segments=3, num_ctas=None, after_permute=False, group_order=None):
+                  segments=3, num_ctas=None, after_permute=False, group_order=None, split=None):
+        """`split` (two-term fp8 path): the routed rows' (a_scale, hq, h_scale); default the one-GPU
+        workspace's."""
         pe = self.experts  # with an expert cache: w1 / w2 are the device slots
         f = L.FfnArgs()
         f.dtype, f.act, f.d = (L.F8E4M3 if pe.fp8 else _dt(self.dtype)), pe.act, self.d
@@ -544,12 +583,17 @@ class MoEEngine:
         f.num_experts_w, f.capacity = pe.E, capacity
         f.a, f.w1, f.w2, f.h, f.y = _ptr(a), _ptr(pe.w1), _ptr(pe.w2), _ptr(h), _ptr(y)
         if pe.ws1 is not None:
-            xs = ws["x_f16"] if pe.fp8 else x
+            xs = (ws["x_q"] if self._split else ws["x_f16"]) if pe.fp8 else x
             f.shared_rows, f.shared_n1p, f.shared_ip = x.shape[0], pe.s_n1p, pe.s_ip
             f.xs, f.ws1, f.ws2, f.hs, f.ys = _ptr(xs), _ptr(pe.ws1), _ptr(pe.ws2), _ptr(ws["hs"]), _ptr(ws["ys"])
         if pe.fp8:
             f.w1_scale, f.w2_scale = _ptr(pe.w1_scale), _ptr(pe.w2_scale)
             f.ws1_scale, f.ws2_scale = _ptr(pe.ws1_scale), _ptr(pe.ws2_scale)
+        if self._split:
+            a_scale, hq, h_scale = split if split is not None else (ws["a_scale"], ws["hq"], ws["h_scale"])
+            f.f8_split, f.a_scale, f.hq, f.h_scale = 1, _ptr(a_scale), _ptr(hq), _ptr(h_scale)
+            if pe.ws1 is not None:
+                f.xs_scale, f.hsq, f.hs_scale = _ptr(ws["x_scale"]), _ptr(ws["hsq"]), _ptr(ws["hs_scale"])
         f.err, f.num_ctas, f.phases = _ptr(self.err), self.num_ctas if num_ctas is None else num_ctas, phases
         f.tile_rows = self.tile_rows
         f.tile_order = self.tile_order
@@ -743,16 +787,25 @@ class MoEEngine:
         if G > 1:
             dist.barrier(group=self.group)  # every region is zeroed and mapped before anyone stores
         dt = self.dtype
+        split = {}
+        if self._split:
+            # the received bf16 rows and the intermediates as two-term e4m3 rows (dsca_split_rows)
+            kd, ip = _ceil(d, 128) * 128, self.experts.ip
+            split = dict(aq=torch.empty(recv_cap, 2 * kd, dtype=torch.uint8, device=dev),
+                         a_scale=torch.empty(recv_cap, dtype=torch.float32, device=dev),
+                         hq=torch.empty(recv_cap, 2 * ip, dtype=torch.uint8, device=dev),
+                         h_scale=torch.empty(recv_cap, dtype=torch.float32, device=dev))
         self._ep = dict(
             region=region.value, imported=imported, ctx=ctx, T_cap=T_cap, recv_cap=recv_cap, ret_cap=ret_cap,
             recv=_DevPtr.tensor(region.value + off_recv, (recv_cap, d), dt, dev),
             ret=_DevPtr.tensor(region.value + off_ret, (ret_cap, d), dt, dev),
-            h=torch.empty(recv_cap, self.experts.ip, dtype=self.op_dtype, device=dev),
+            h=torch.empty(recv_cap, self.experts.ip, dtype=torch.bfloat16 if self._split else self.op_dtype,
+                          device=dev),
             y=torch.empty(recv_cap, d, dtype=dt, device=dev),
             side=torch.cuda.Stream(device=dev),
             group_offsets=int(lib.dsca_ep_group_offsets(_ptr(ctx)) or 0),
             group_order=int(lib.dsca_ep_group_order(_ptr(ctx)) or 0),
-            bytes=total)
+            bytes=total, split_fp8=self._split, **split)
 
     def _forward_p2p(self, x, ws, qos=None):
         """ep_return = "overlap": main stream shared GEMM1 -> [dispatch done] routed GEMM1 ->
@@ -791,35 +844,47 @@ class MoEEngine:
             a.x, a.T, a.d, a.top_k, a.dtype = _ptr(x), T, self.d, self.top_k, _dt(self.dtype)
             a.topk_ids, a.local_rank = _ptr(ws["topk_ids"]), _ptr(ws["local_rank"])
             a.block_base, a.ctx, a.token_row, a.err = _ptr(ws["block_base"]), ctx, _ptr(ws["token_row"]), err
-            a.out_f16, a.x_f16 = int(self.experts.fp8), _ptr(ws.get("x_f16"))
+            if not self._split:  # the two-term fp8 path sends bf16 rows and splits them on arrival
+                a.out_f16, a.x_f16 = int(self.experts.fp8), _ptr(ws.get("x_f16"))
             L.call("dsca_ep_dispatch", ctypes.byref(a), _stream())
             self._side_mark("dispatch", t0)
             dispatched = torch.cuda.Event()
             dispatched.record(side)
-        args = (x, ws, ep["recv"], ep["h"], ep["y"], ep["recv_cap"], self.E, ep["group_offsets"], None)
         has_shared = self.experts.ws1 is not None
+        kw = {}
+        if self._split:
+            kw = dict(split=(ep["a_scale"], ep["hq"], ep["h_scale"]))
+            if has_shared:
+                self._split_rows(x, T, self.d, ws["x_q"], ws["x_scale"])
+        args = (x, ws, ep["aq"] if self._split else ep["recv"], ep["h"], ep["y"], ep["recv_cap"], self.E,
+                ep["group_offsets"], None)
         # the fp8-weight GEMM has no remote-store epilogue: its routed rows go back by the return kernel
         fused = self.ep_return == "fused" and not self.experts.fp8
         side_ctas = max(2, self.num_sms - self.ep_side_sms) if self.ep_side_sms > 0 else None
         if has_shared:
-            self._ffn_call(*args, 1, segments=2, num_ctas=side_ctas)
+            self._ffn_call(*args, 1, segments=2, num_ctas=side_ctas, **kw)
             self._mark("gemm1_shared")
             if fused:
-                self._ffn_call(*args, 2, segments=2, num_ctas=side_ctas)
+                self._ffn_call(*args, 2, segments=2, num_ctas=side_ctas, **kw)
                 self._mark("gemm2_shared")
         main.wait_event(dispatched)
         L.check(lib.dsca_ep_wait(ctx, 1, self.wait_limit_ns, err, _stream()), "dsca_ep_wait")
         self._mark("wait_dispatch")
+        if self._split:
+            # the received rows (as many as the plan's receive offsets hold) as two-term rows
+            self._split_rows(ep["recv"], ep["recv_cap"], self.d, ep["aq"], ep["a_scale"],
+                             rows_dev=ep["group_offsets"] + 4 * self.E)
+            self._mark("split_received")
         if self.cache is not None:
             return self._forward_p2p_cached(x, ws, ep, args, has_shared, side_ctas)
         order = ep["group_order"] if self.qos_order else None
-        self._ffn_call(*args, 1, segments=1, group_order=order)
+        self._ffn_call(*args, 1, segments=1, group_order=order, **kw)
         self._mark("gemm1_routed")
         if fused:
             self._ffn_call(*args, 2, ep_ctx=ep["ctx"], segments=1, group_order=order)
             self._mark("gemm2_routed_fused")
         else:
-            self._ffn_call(*args, 2, segments=1, group_order=order)
+            self._ffn_call(*args, 2, segments=1, group_order=order, **kw)
             self._mark("gemm2_routed")
             computed = torch.cuda.Event()
             computed.record(main)
@@ -832,7 +897,7 @@ class MoEEngine:
                 returned = torch.cuda.Event()
                 returned.record(side)
             if has_shared:
-                self._ffn_call(*args, 2, segments=2, num_ctas=side_ctas)
+                self._ffn_call(*args, 2, segments=2, num_ctas=side_ctas, **kw)
                 self._mark("gemm2_shared")
             main.wait_event(returned)
         L.check(lib.dsca_ep_wait(ctx, 2, self.wait_limit_ns, err, _stream()), "dsca_ep_wait")

@@ -161,6 +161,12 @@ typedef struct {
   int32_t* err;               /* device error word */
   int out_f16;                /* bf16 input: write the rows as f16 (fp8-weight FFN operand) */
   void* x_f16;                /* [T, d] f16 copy of x (shared-expert operand), or NULL */
+  int out_e4m3;               /* bf16 input: write each row as two e4m3 terms (dsca_split_rows;
+                                 2 * Kd bytes a row, Kd = d rounded up to 128) with its 1 / s in
+                                 out_scale[row] (operand of the f8_split FFN) */
+  float* out_scale;           /* [capacity] */
+  void* x_q;                  /* [T, 2 * Kd] two-term copy of x (shared-expert operand), or NULL */
+  float* x_scale;             /* [T] */
 } dsca_permute_args;
 DSCA_API int dsca_permute(const dsca_permute_args* a, dsca_stream_t stream);
 
@@ -247,8 +253,39 @@ typedef struct {
                                  tiles interleaved in proportion to their counts (after one round
                                  of shared tiles when GEMM1 overlaps the permute), HBM-bound routed
                                  tiles beside tensor-bound shared tiles */
+  /* dtype DSCA_F8E4M3 with f8_split = 1: the e4m3 weights go to the tensor cores as they are
+     (tcgen05 kind::f8f6f4, CTA-pair tiles with the tokens as the MMA N), multiplied by tokens held
+     as two e4m3 terms per value (dsca_split_rows): a [capacity, 2 * Kd] and xs [shared_rows,
+     2 * Kd] bytes (Kd = d rounded up to 128) with 1 / s per row in a_scale and xs_scale.  GEMM1
+     writes h and hs in bf16; the call splits them into hq [capacity, 2 * ip] and hsq
+     [shared_rows, 2 * shared_ip] with h_scale and hs_scale, which GEMM2 reads; y and ys bf16.
+     ep_ctx must be NULL. */
+  int f8_split;
+  const float* a_scale;
+  const float* xs_scale;
+  void* hq;
+  void* hsq;
+  float* h_scale;
+  float* hs_scale;
 } dsca_ffn_args;
 DSCA_API int dsca_grouped_ffn(const dsca_ffn_args* a, dsca_stream_t stream);
+
+/*
+ * Two-term e4m3 rows (the token operand of the f8_split FFN; no counterpart in the reference,
+ * whose experts run in the weights' dtype).  Each bf16 row x of src [rows, ld] is scaled by a
+ * power of two s (its largest magnitude to [128, 256)) and written as hi = RN_e4m3(s x) and
+ * lo = RN_e4m3(s x - hi): dst row = [hi: Kp bytes | lo: Kp bytes], Kp = K rounded up to 128,
+ * zero past K; inv_scale[row] = 1 / s.  hi + lo = s x exactly for |s x| >= 1/4.  One warp a row;
+ * rows_dev (device int, or NULL) bounds the rows processed.
+ */
+typedef struct {
+  const void* src;            /* bf16 [rows, ld] */
+  int ld, rows, K;            /* K % 8 == 0, K <= ld, ld % 8 == 0 */
+  const int32_t* rows_dev;    /* device row count (min with rows), or NULL */
+  void* dst;                  /* [rows, 2 * Kp] bytes */
+  float* inv_scale;           /* [rows] */
+} dsca_split_args;
+DSCA_API int dsca_split_rows(const dsca_split_args* a, dsca_stream_t stream);
 
 /*
  * Grouped expert FFN for callers that cannot allocate device memory (no counterpart in the

@@ -294,6 +294,54 @@ def qwen_forward(x, Wg, p: dict, k: int, norm_topk: bool, act: str, compute=np.f
     return y, logits, ids, w, sg[:, 0]
 
 
+def e4m3_rn(v) -> np.ndarray:
+    """float32 values (|v| < 464) -> e4m3 bytes, round to nearest even (the sign of zero kept)."""
+    v = np.asarray(v, np.float32).astype(np.float64)
+    a = np.abs(v)
+    _, ex = np.frexp(np.where(a > 0, a, 1.0))
+    e = np.maximum(ex.astype(np.float64) - 1.0, -6.0)  # subnormals: quantum 2^-9
+    q = np.exp2(e - 3.0)
+    r = np.rint(a / q) * q
+    _, ex2 = np.frexp(np.where(r > 0, r, 1.0))
+    e2 = ex2.astype(np.int64) - 1
+    normal = (r > 0) & (e2 >= -6)
+    expf = np.where(normal, e2 + 7, 0)
+    mant = np.where(normal, np.rint((r / np.exp2(e2.astype(np.float64)) - 1.0) * 8.0), np.rint(r / 2.0 ** -9))
+    bits = (expf.astype(np.int64) << 3) | mant.astype(np.int64)
+    bits = np.where(r > 0, bits, 0) | np.where(np.signbit(v), 0x80, 0)
+    return bits.astype(np.uint8)
+
+
+def e4m3_value(b) -> np.ndarray:
+    """e4m3 bytes -> float32 values."""
+    b = np.asarray(b, np.int64)
+    expf, mant = (b >> 3) & 15, b & 7
+    mag = np.where(expf > 0, np.exp2(expf - 7.0) * (1.0 + mant / 8.0), np.exp2(-9.0) * mant)
+    return np.where(b & 0x80, -mag, mag).astype(np.float32)
+
+
+def split_e4m3(x) -> tuple[np.ndarray, np.ndarray]:
+    """Two-term e4m3 rows of bf16 rows x [rows, K] (values given as float32), the restatement of
+    dsca_split_rows: per row s = 2^(134 - E) with E the bf16 exponent field of max|x| clamped to
+    [8, 254]; v = x s, hi = RN(v), lo = RN(v - hi) in float32 arithmetic.  Returns (bytes
+    [rows, 2 Kp] = [hi | lo], Kp = K rounded up to 128, zero padded; 1 / s [rows] float32)."""
+    x = np.asarray(x, np.float32)
+    rows, K = x.shape
+    kp = (K + 127) // 128 * 128
+    mx = np.abs(x).max(axis=1) if K else np.zeros(rows, np.float32)
+    E = (mx.view(np.uint32) >> 23).astype(np.int64) & 0xFF
+    E = np.clip(E, 8, 254)
+    s = ((261 - E).astype(np.uint32) << 23).view(np.float32)
+    inv = ((E - 7).astype(np.uint32) << 23).view(np.float32)
+    v = (x * s[:, None]).astype(np.float32)
+    hi = e4m3_rn(v)
+    lo = e4m3_rn((v - e4m3_value(hi)).astype(np.float32))
+    out = np.zeros((rows, 2 * kp), np.uint8)
+    out[:, :K] = hi
+    out[:, kp:kp + K] = lo
+    return out, inv
+
+
 def max_rel_err(a, ref) -> float:
     """max|a - ref| / max|ref| over the tensor."""
     a = np.asarray(a, np.float64)

@@ -31,7 +31,7 @@ def test_header_symbols_exported(lib):
 # C struct name -> ctypes mirror in dsca_moe_b200._lib
 _STRUCTS = {"dsca_router_args": "RouterArgs", "dsca_scan_args": "ScanArgs", "dsca_permute_args": "PermuteArgs",
             "dsca_ffn_args": "FfnArgs", "dsca_combine_args": "CombineArgs", "dsca_qos_args": "QosArgs",
-            "dsca_ep_setup": "EpSetup", "dsca_ep_dispatch_args": "EpDispatchArgs"}
+            "dsca_ep_setup": "EpSetup", "dsca_ep_dispatch_args": "EpDispatchArgs", "dsca_split_args": "SplitArgs"}
 
 
 def test_struct_layouts_match_c_compiler(tmp_path):

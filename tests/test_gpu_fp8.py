@@ -1,8 +1,10 @@
 """fp8-e4m3 expert weights with per-output-channel fp32 scales: the block (f16 operands, fp32
 accumulation, scales in the epilogue) against the fp32 oracle run on the dequantised weights
 (q * scale) and the same inputs — 2e-2 max relative error.  Routing is unchanged by the weight
-format and stays bit-exact.  Both kernel forms run: tile_rows 0 (weights converted into shared
-memory) and 256 (weights converted into tensor memory, the MMA's A operand read from TMEM)."""
+format and stays bit-exact.  Three kernel forms run: "split" (the e4m3 weights unconverted on
+kind::f8f6f4 MMAs against two-term e4m3 tokens, the default), "smem" (weights converted to f16
+in shared memory) and "tmem" (converted into tensor memory, the MMA's A operand read from TMEM).
+dsca_split_rows is bit-exact against the oracle's restatement."""
 import numpy as np
 import pytest
 import torch
@@ -37,7 +39,12 @@ def _qwen(dev, T, d, E, I, Is, seed):
     return eng, Wg, p
 
 
-FORMS = [0, 256]
+FORMS = ["split", "smem", "tmem"]
+
+
+def _form(eng, form):
+    eng.fp8_split = form == "split"
+    eng.tile_rows = 256 if form == "tmem" else 0
 
 
 @pytest.mark.parametrize("tile_rows", FORMS)
@@ -45,7 +52,7 @@ FORMS = [0, 256]
                                         (300, 192, 8, 320, 384)])
 def test_qwen_fp8_vs_oracle(cuda, T, d, E, I, Is, tile_rows):
     eng, Wg, p = _qwen(cuda, T, d, E, I, Is, 41)
-    eng.tile_rows = tile_rows
+    _form(eng, tile_rows)
     x = syn.hidden_states(T, d, 42, "bf16")
     r = eng.forward(torch.from_numpy(x).to(cuda, torch.bfloat16))
     torch.cuda.synchronize()
@@ -68,7 +75,7 @@ def test_switch_fp8_vs_oracle(cuda, tile_rows):
     q = quantize_fp8(pack_relu(wi, wo, device=cuda))
     Wr, _ = syn.router_weight(E, d, 52, zipf_s=1.0, dtype="bf16")
     eng = MoEEngine(torch.from_numpy(Wr).to(cuda, torch.bfloat16), q, top_k=1, route_mode=L.ROUTE_SWITCH_TOP1)
-    eng.tile_rows = tile_rows
+    _form(eng, tile_rows)
     x = syn.hidden_states(T, d, 53, "bf16")
     r = eng.forward(torch.from_numpy(x).to(cuda, torch.bfloat16))
     torch.cuda.synchronize()
@@ -86,7 +93,7 @@ def test_qwen_fp8_full_size(cuda, tile_rows):
     """Qwen1.5-MoE-A2.7B shape, 4096 tokens: fp8 output vs the oracle on a token sample."""
     T, d, E, I, Is = 4096, 2048, 60, 1408, 5632
     eng, Wg, p = _qwen(cuda, T, d, E, I, Is, 61)
-    eng.tile_rows = tile_rows
+    _form(eng, tile_rows)
     x = syn.hidden_states(T, d, 62, "bf16")
     r = eng.forward(torch.from_numpy(x).to(cuda, torch.bfloat16))
     torch.cuda.synchronize()
@@ -103,11 +110,49 @@ def test_fp8_forms_agree(cuda):
     eng, Wg, p = _qwen(cuda, T, d, E, I, Is, 71)
     x = torch.from_numpy(syn.hidden_states(T, d, 72, "bf16")).to(cuda, torch.bfloat16)
     outs = []
-    for tr in FORMS:
-        eng.tile_rows = tr
+    for form in FORMS:
+        _form(eng, form)
         outs.append(eng.forward(x)["out"].float().clone())
         torch.cuda.synchronize()
         eng.check()
-    a, b = outs
-    assert torch.isfinite(b).all()
-    assert ((a - b).abs().max() / a.abs().max()).item() < 1e-2
+    a = outs[0]
+    for b in outs[1:]:
+        assert torch.isfinite(b).all()
+        assert ((a - b).abs().max() / a.abs().max()).item() < 1e-2
+
+
+@pytest.mark.parametrize("rows,K,ld,bound", [(300, 2048, 2048, None), (77, 200, 208, None), (1000, 1408, 1408, 613),
+                                             (5, 8, 8, None)])
+def test_split_rows_bit_exact(cuda, lib, rows, K, ld, bound):
+    """dsca_split_rows through the C-ABI against the oracle's restatement: the hi / lo bytes and
+    1 / s bit for bit, rows of mixed magnitudes (zero, subnormal-scale, large) included; a
+    device row count bounds the rows written."""
+    import ctypes
+
+    from dsca_moe_b200 import _lib as L
+
+    g = np.random.default_rng(rows + K)
+    x = g.standard_normal((rows, ld)).astype(np.float32) * np.exp2(g.integers(-30, 30, (rows, 1))).astype(np.float32)
+    x[0] = 0.0
+    if rows > 2:
+        x[1, : K // 2] *= np.float32(2.0 ** -40)
+        x[2] *= np.float32(2.0 ** 60)
+    x = syn.bf16_round(x)
+    kp = (K + 127) // 128 * 128
+    src = torch.from_numpy(x).to(cuda, torch.bfloat16)
+    dst = torch.full((rows, 2 * kp), 0xAB, dtype=torch.uint8, device=cuda)
+    inv = torch.full((rows,), -1.0, dtype=torch.float32, device=cuda)
+    nrow = torch.tensor([bound if bound is not None else rows], dtype=torch.int32, device=cuda)
+    a = L.SplitArgs()
+    a.src, a.ld, a.rows, a.K = src.data_ptr(), ld, rows, K
+    a.rows_dev = nrow.data_ptr() if bound is not None else None
+    a.dst, a.inv_scale = dst.data_ptr(), inv.data_ptr()
+    L.check(lib.dsca_split_rows(ctypes.byref(a), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)),
+            "dsca_split_rows")
+    torch.cuda.synchronize()
+    q, iv = O.split_e4m3(x[:, :K])
+    n = bound if bound is not None else rows
+    assert np.array_equal(dst.cpu().numpy()[:n], q[:n])
+    assert np.array_equal(inv.cpu().numpy()[:n].view(np.uint32), iv[:n].view(np.uint32))
+    if n < rows:  # rows past the device count untouched
+        assert (dst[n:] == 0xAB).all() and (inv[n:] == -1.0).all()
