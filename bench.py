@@ -93,11 +93,13 @@ def parse():
     ap.add_argument("--tile-order", type=int, choices=[0, 1], default=None,
                     help="routed and shared tiles of one GEMM launch: 0 = one segment after the other, "
                          "1 = interleaved (default: the engine's)")
-    ap.add_argument("--cache-hints", type=int, choices=[0, 1], default=0,
-                    help="L2 policies of the GEMM loads: 1 = routed weights evict-first, the rest evict-last")
-    ap.add_argument("--router-tc", type=int, choices=[0, 1], default=0,
+    ap.add_argument("--cache-hints", type=int, choices=[0, 1, 2, 3], default=0,
+                    help="GEMM loads: bit 0 = routed weights evict-first, the rest evict-last; bit 1 = each CTA "
+                         "prefetches its next tile's weights into L2")
+    ap.add_argument("--router-tc", type=int, choices=[0, 1], default=None,
                     help="router logits: 1 = tensor cores (exact int8 fixed-point products, correctly "
-                         "rounded bf16 logits), 0 = CUDA-core fp32 fma chains in the fixed chunk order")
+                         "rounded bf16 logits), 0 = CUDA-core fp32 fma chains in the fixed chunk order "
+                         "(default: the engine's, tensor cores where they apply)")
     ap.add_argument("--no-qos-order", action="store_true",
                     help="expert parallel: skip the QoS planner (scores, priority sum) and run the routed "
                          "tiles in expert order")
@@ -914,7 +916,8 @@ def run_ours(args, w, T):
         eng.tile_order = args.tile_order
     eng.cache_hints = args.cache_hints
     eng.qos_order = not args.no_qos_order
-    eng.router_tensor_cores = bool(args.router_tc)
+    if args.router_tc is not None:
+        eng.router_tensor_cores = bool(args.router_tc)
     eng.ep_side_sms = args.ep_side_sms
     eng.pdl = not args.no_pdl
     peaks = load_peaks()
@@ -1240,7 +1243,9 @@ def run_ours(args, w, T):
                 "fp8_form": ({"split": "e4m3 weights unconverted (kind::f8f6f4) x two-term e4m3 tokens",
                               "smem": "weights converted to f16 in shared memory",
                               "tmem": "weights converted to f16 in tensor memory"}[args.fp8_form] if args.fp8 else None),
-                "l2_hints": ["default", "routed weights evict-first, the rest evict-last"][args.cache_hints],
+                "l2_hints": ["default", "routed weights evict-first, the rest evict-last",
+                             "next tile's weights prefetched into L2",
+                             "evict-first / evict-last, next tile's weights prefetched"][args.cache_hints],
                 "qos_order": (eng.qos_order if world > 1 else None),
                 "router": ("tensor cores: exact int8 fixed-point products, one fused kernel"
                            if eng.router_tensor_cores else "CUDA cores: fp32 fma chains in the fixed chunk order")},

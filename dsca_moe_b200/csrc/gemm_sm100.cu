@@ -32,17 +32,40 @@ namespace dsca {
 namespace gemm {
 
 constexpr int BM = 128;
-constexpr int kStages = 4;
-constexpr int kABytes = BM * BK * 2;
-constexpr int kBBytes = BN * BK * 2;
-constexpr int kStageBytes = kABytes + kBBytes;
-constexpr int kSmemBytes = kStages * kStageBytes + 1024;  // + alignment slack
 
-template <int EPI>
+// Stage layout.  bf16: A 128 x 64 and B 256 x 64, 4 stages.  F8 (fp8-e4m3 weights, the tokens as
+// two e4m3 planes, fp8_split.cuh): 128 bytes of K per row as in bf16 — 128 elements — with the
+// A tile's hi and lo planes, two tcgen05.mma.kind::f8f6f4 per 32-byte K step into the same
+// accumulator (the bf16 MMA's tensor time per K element, half its weight bytes), 3 stages.
+template <bool F8>
+struct SCfg {
+  static constexpr int kStages = F8 ? 3 : 4;
+  static constexpr int kKE = F8 ? 128 : BK;         // K elements per stage
+  static constexpr int kAPlane = BM * 128;          // 16 KB
+  static constexpr int kABytes = (F8 ? 2 : 1) * kAPlane;
+  static constexpr int kBBytes = BN * 128;          // 32 KB
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024;  // + alignment slack
+};
+
+// D(tmem) (+)= A(smem desc) * B(smem desc), e4m3 x e4m3, fp32 accumulate
+__device__ __forceinline__ void umma_f8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+template <int EPI, bool F8>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmB0,
                         const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmB1,
                         const Params p) {
+  using C = SCfg<F8>;
+  constexpr int kStages = C::kStages, kABytes = C::kABytes, kBBytes = C::kBBytes, kStageBytes = C::kStageBytes;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ SmemCtl ctl;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -107,16 +130,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           seg0_ready = true;
         }
         const int kb_n = p.seg[ti.seg].k_blocks;
+        // l2_hints bit 1: the next tile's weights are prefetched into L2 alongside this tile's loads
+        const int next = (p.l2_hints & 2) ? sched_tile(r + 1, (int)blockIdx.x, (int)gridDim.x) : total;
+        TileInfo tn{};
+        if (next < total) tn = decode<BM>(p, ctl, next);
+        const CUtensorMap* mbn = tn.seg == 0 ? &tmB0 : &tmB1;
+        const int kb_pf = next < total ? p.seg[tn.seg].k_blocks : 0;
         for (int kb = 0; kb < kb_n; ++kb) {
           if (!mbar_wait(smem_u32(&ctl.empty[s]), ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
           const uint32_t fb = smem_u32(&ctl.full[s]);
           mbar_arrive_expect_tx(fb, kStageBytes);
-          if (p.l2_hints) {
-            tma_load_2d_hint(smem_a + s * kABytes, ma, fb, kb * BK, ti.row0, pol_last);
-            tma_load_2d_hint(smem_b + s * kBBytes, mb, fb, kb * BK, ti.b_row0, ti.seg == 0 ? pol_first : pol_last);
+          const int kx = kb * C::kKE;
+          if (kb < kb_pf) tma_prefetch_2d(mbn, kx, tn.b_row0);
+          if (p.l2_hints & 1) {
+            tma_load_2d_hint(smem_a + s * kABytes, ma, fb, kx, ti.row0, pol_last);
+            if constexpr (F8)  // the lo plane of the same token rows
+              tma_load_2d_hint(smem_a + s * kABytes + C::kAPlane, ma, fb, p.seg[ti.seg].t_lo + kx, ti.row0, pol_last);
+            tma_load_2d_hint(smem_b + s * kBBytes, mb, fb, kx, ti.b_row0, ti.seg == 0 ? pol_first : pol_last);
           } else {
-            tma_load_2d(smem_a + s * kABytes, ma, fb, kb * BK, ti.row0);
-            tma_load_2d(smem_b + s * kBBytes, mb, fb, kb * BK, ti.b_row0);
+            tma_load_2d(smem_a + s * kABytes, ma, fb, kx, ti.row0);
+            if constexpr (F8) tma_load_2d(smem_a + s * kABytes + C::kAPlane, ma, fb, p.seg[ti.seg].t_lo + kx, ti.row0);
+            tma_load_2d(smem_b + s * kBBytes, mb, fb, kx, ti.b_row0);
           }
           pending_phase[s] = (int)ph;
           if (++s == kStages) { s = 0; ph ^= 1u; }
@@ -131,7 +165,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+      constexpr uint32_t idesc = F8 ? idesc_e4m3_f32(BM, BN) : idesc_bf16_f32(BM, BN);
       int s = 0;
       uint32_t ph = 0;
       int it = 0;
@@ -151,10 +185,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint64_t adesc = sw128_kmajor_desc(smem_a + s * kABytes);
           const uint64_t bdesc = sw128_kmajor_desc(smem_b + s * kBBytes);
+          if constexpr (F8) {
+            const uint64_t ldesc = sw128_kmajor_desc(smem_a + s * kABytes + C::kAPlane);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            umma_f16(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), idesc,
-                     (kb > 0 || k > 0) ? 1u : 0u);
+            for (int k = 0; k < C::kKE / 32; ++k) {
+              const uint64_t ko = (uint64_t)(2 * k);
+              umma_f8(d_tmem, adesc + ko, bdesc + ko, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+              umma_f8(d_tmem, ldesc + ko, bdesc + ko, idesc, 1u);
+            }
+          } else {
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k)
+              umma_f16(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), idesc,
+                       (kb > 0 || k > 0) ? 1u : 0u);
+          }
           umma_commit(smem_u32(&ctl.empty[s]));
           if (++s == kStages) { s = 0; ph ^= 1u; }
         }
@@ -197,6 +241,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           valid = false;
         }
       }
+      // F8: this row's 1 / s (the token scale); the weight row scales are per column below
+      const float ts = (F8 && valid) ? __ldg(sg.t_scale + row) : 0.0f;
       if constexpr (EPI == kEpiSwiGLU) {
         const int col0 = ti.n_blk * (BN / 2);
 #pragma unroll 1
@@ -206,6 +252,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld32(taddr + c, g);
           tmem_ld32(taddr + BN / 2 + c, u);
           tmem_wait_ld();
+          if constexpr (F8) {
+            // weight rows b_row0 + c + i (gate) and b_row0 + 128 + c + i (up) (packed rows past a
+            // group's channels are zero)
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              g[i] = __float_as_uint(__uint_as_float(g[i]) * __ldg(sg.w_scale + ti.b_row0 + c + i) * ts);
+              u[i] = __float_as_uint(__uint_as_float(u[i]) * __ldg(sg.w_scale + ti.b_row0 + BN / 2 + c + i) * ts);
+            }
+          }
           uint32_t packed[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
@@ -229,6 +284,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t v32[32];
           tmem_ld32(taddr + c, v32);
           tmem_wait_ld();
+          if constexpr (F8) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              v32[i] = __float_as_uint(__uint_as_float(v32[i]) * __ldg(sg.w_scale + ti.b_row0 + c + i) * ts);
+          }
           uint32_t packed[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
@@ -297,24 +357,25 @@ int make_map_bf16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols
   return r == CUDA_SUCCESS ? DSCA_OK : DSCA_ERR_CUDA;
 }
 
-template <int EPI>
+template <int EPI, bool F8 = false>
 static int launch_kernel(const CUtensorMap& a0, const CUtensorMap& b0, const CUtensorMap& a1, const CUtensorMap& b1,
                          const gemm::Params& p, int grid, cudaStream_t stream) {
   static PerDeviceOnce attr_once;
-  auto kern = gemm::grouped_gemm_kernel<EPI>;
+  auto kern = gemm::grouped_gemm_kernel<EPI, F8>;
+  constexpr int smem_bytes = gemm::SCfg<F8>::kSmemBytes;
   if (attr_once.run([&] {
-        return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::kSmemBytes);
+        return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
       }) != cudaSuccess)
     return DSCA_ERR_CUDA;
   if (!p.pdl_seg0_wait) {
-    kern<<<grid, gemm::kThreads, gemm::kSmemBytes, stream>>>(a0, b0, a1, b1, p);
+    kern<<<grid, gemm::kThreads, smem_bytes, stream>>>(a0, b0, a1, b1, p);
     return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
   }
   // programmatic dependent of the permute: may start while it runs (see Params::pdl_seg0_wait)
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3(gemm::kThreads);
-  cfg.dynamicSmemBytes = gemm::kSmemBytes;
+  cfg.dynamicSmemBytes = smem_bytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -468,6 +529,84 @@ int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t st
     if ((rc = launch_one(gemm::kEpiStore, a0, b0, a1, b1, p, grid, stream))) return rc;
   }
   return DSCA_OK;
+}
+
+// 2-D byte tensor map over a row-major [rows, cols] matrix (e4m3 weights or two-term token rows),
+// box = box_rows x 128 bytes, 128-byte swizzle.
+int make_map_e4m3(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  PFN_encodeTiled enc = get_encode_fn();
+  if (enc == nullptr) return DSCA_ERR_CUDA;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || cols % 16 != 0) return DSCA_ERR_BAD_ARG;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols};
+  cuuint32_t box[2] = {128, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? DSCA_OK : DSCA_ERR_CUDA;
+}
+
+// GEMM1 of the f8_split FFN on single-CTA tiles (128 tokens x 256 weight rows): h = act(a . w1^T),
+// hs = act(xs . ws1^T) in bf16, the tokens as two-term e4m3 rows.
+int launch_gemm1_f8_single(const dsca_ffn_args* f, int num_sms, cudaStream_t stream) {
+  const int grid = f->num_ctas > 0 ? f->num_ctas : num_sms;
+  const int segs = f->segments == 0 ? 3 : f->segments;
+  const bool shared = f->shared_rows > 0 && (segs & 2);
+  const bool routed = (segs & 1) != 0;
+  if (!routed && !shared) return DSCA_OK;
+  const int Kd = (f->d + 127) & ~127;
+  int rc;
+  CUtensorMap a0, b0, a1, b1;
+  if ((rc = make_map_e4m3(&a0, f->a, (uint64_t)std::max(f->capacity, 1), (uint64_t)2 * Kd, gemm::BM))) return rc;
+  if ((rc = make_map_e4m3(&b0, f->w1, (uint64_t)f->num_experts_w * f->n1p, (uint64_t)f->d, gemm::BN))) return rc;
+  if (shared) {
+    if ((rc = make_map_e4m3(&a1, f->xs, (uint64_t)f->shared_rows, (uint64_t)2 * Kd, gemm::BM))) return rc;
+    if ((rc = make_map_e4m3(&b1, f->ws1, (uint64_t)f->shared_n1p, (uint64_t)f->d, gemm::BN))) return rc;
+  } else {
+    a1 = a0;
+    b1 = b0;
+  }
+  gemm::Params p{};
+  const int epi = f->act == DSCA_ACT_SWIGLU ? gemm::kEpiSwiGLU : gemm::kEpiReLU;
+  p.epi = epi;
+  p.err = f->err;
+  p.nseg = shared ? 2 : 1;
+  p.seg_first = 0;
+  p.interleave_lead = -1;
+  p.l2_hints = f->cache_hints;
+  gemm::Segment& s0 = p.seg[0];
+  s0.group_offsets = f->group_offsets;
+  s0.group_weight = f->group_weight;
+  s0.group_order = f->group_order;
+  s0.ngroups = routed ? f->num_groups : 0;
+  s0.n_tiles = f->n1p / gemm::BN;
+  s0.b_rows_per_group = f->n1p;
+  s0.k_blocks = (f->d + 127) / 128;
+  s0.c = reinterpret_cast<__nv_bfloat16*>(f->h);
+  s0.ldc = f->ip;
+  s0.n_store = f->ip;
+  s0.capacity = f->capacity;
+  s0.t_lo = Kd;
+  s0.t_scale = f->a_scale;
+  s0.w_scale = f->w1_scale;
+  if (shared) {
+    gemm::Segment& s1 = p.seg[1];
+    s1.ngroups = 1;
+    s1.rows = f->shared_rows;
+    s1.n_tiles = f->shared_n1p / gemm::BN;
+    s1.b_rows_per_group = f->shared_n1p;
+    s1.k_blocks = (f->d + 127) / 128;
+    s1.c = reinterpret_cast<__nv_bfloat16*>(f->hs);
+    s1.ldc = f->shared_ip;
+    s1.n_store = f->shared_ip;
+    s1.capacity = f->shared_rows;
+    s1.t_lo = Kd;
+    s1.t_scale = f->xs_scale;
+    s1.w_scale = f->ws1_scale;
+  }
+  return epi == gemm::kEpiSwiGLU ? launch_kernel<gemm::kEpiSwiGLU, true>(a0, b0, a1, b1, p, grid, stream)
+                                 : launch_kernel<gemm::kEpiReLU, true>(a0, b0, a1, b1, p, grid, stream);
 }
 
 }  // namespace dsca

@@ -61,8 +61,10 @@ struct Params {
   // to their counts, so that at any time some SMs run the routed experts' tiles (which stream
   // every expert's weights from HBM) while the others run the shared expert's (tensor bound)
   int interleave_lead;
-  // L2 policies of the loads: 0 = default; 1 = routed experts' weights (segment 0, streamed from
-  // DRAM and mostly read once) evict-first, shared-expert weights and token rows evict-last
+  // L2 policies of the loads (bit 0): routed experts' weights (segment 0, streamed from DRAM and
+  // mostly read once) evict-first, shared-expert weights and token rows evict-last.  Bit 1: while
+  // loading K step kb of a tile, the producer prefetches K step kb of its next tile's weights into
+  // L2, so that a tile starting on an expert's weights finds them on the way from DRAM
   int l2_hints;
   // CTA-pair SwiGLU GEMM1 only: every whole 256-token block of a group is one non-swapped tile
   // (tokens as M = 256 over the pair, 128 channels' gate and up rows as N = 256, Segment::n_full
@@ -266,6 +268,10 @@ __device__ __forceinline__ float silu(float g) { return __fdividef(g, 1.0f + __e
 int make_map_bf16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows);
 // The CTA-pair swap-AB path of dsca_grouped_ffn (bf16).
 int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream_t stream);
+// 2-D byte tensor map (e4m3 weights or two-term token rows), box = box_rows x 128, 128B swizzle.
+int make_map_e4m3(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows);
+// GEMM1 of the f8_split FFN on single-CTA tiles (gemm_sm100.cu).
+int launch_gemm1_f8_single(const dsca_ffn_args* f, int num_sms, cudaStream_t stream);
 // dsca_grouped_ffn with fp8-e4m3 weights and two-term e4m3 tokens (f8_split = 1).
 int launch_grouped_ffn_f8_split(const dsca_ffn_args* f, int num_sms, cudaStream_t stream);
 // One warp per row: bf16 rows -> two-term e4m3 rows and 1 / s (fp8_split.cuh).

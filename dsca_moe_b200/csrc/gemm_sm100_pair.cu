@@ -77,11 +77,6 @@ __device__ __forceinline__ void umma_f8_pair(uint32_t d_tmem, uint64_t adesc, ui
       : "memory");
 }
 
-// Instruction descriptor, kind::f8f6f4: A = B = e4m3 (format 0), D = f32, both K-major.
-__host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N) {
-  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
-}
-
 template <int EPI, bool F8>
 __global__ void __launch_bounds__(kThreads, 1)
     pair_gemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__ CUtensorMap tmT0,
@@ -168,6 +163,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int w_row = C::kGlu ? ti.b_row0 + ti.n_blk * BN + 256 * (int)rank : ti.b_row0 + 128 * (int)rank;
         const int t_row = ti.row0 + half * (int)rank;
         const int kb_n = p.seg[ti.seg].k_blocks;
+        // l2_hints bit 1: this CTA's weight rows of its next tile are prefetched into L2 alongside
+        // this tile's loads
+        const int next = (p.l2_hints & 2) ? sched_tile(r + 1, unit, units) : total;
+        TileInfo tn{};
+        if (next < total) tn = decode<TBN>(p, ctl, next);
+        const CUtensorMap* mwn = tn.seg == 0 ? &tmW0 : &tmW1;
+        const int kb_pf = (next < total && !(C::kGlu && tn.full)) ? p.seg[tn.seg].k_blocks : 0;
+        const int w_row_n = C::kGlu ? tn.b_row0 + tn.n_blk * BN + 256 * (int)rank : tn.b_row0 + 128 * (int)rank;
         // hybrid full tile (SwiGLU): this CTA's 128 tokens (two 64-row token boxes into slot A)
         // and the gate (even CTA) or up (odd CTA) rows of the tile's 128 channels (slot A2)
         const bool full = !F8 && C::kGlu && ti.full;
@@ -179,9 +182,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t fb0 = mapa_shared(fb, 0);  // the even CTA's full barrier
           // L2 policies (Params::l2_hints): routed weights evict-first, the rest evict-last
           const uint64_t wpol = ti.seg == 0 ? pol_first : pol_last;
+          if (kb < kb_pf) {
+            tma_prefetch_2d(mwn, kb * C::kKE, w_row_n);
+            if constexpr (C::kGlu) tma_prefetch_2d(mwn, kb * C::kKE, w_row_n + 128);
+          }
           if (full) {
             if (rank == 0) mbar_arrive_expect_tx(fb, tx_full);
-            if (p.l2_hints) {
+            if (p.l2_hints & 1) {
               tma_load_2d_pair_hint(smem_a + s * C::kABytes, mt, fb0, kb * C::kKE, f_trow, pol_last);
               tma_load_2d_pair_hint(smem_a + s * C::kABytes + C::kABytes / 2, mt, fb0, kb * C::kKE, f_trow + 64, pol_last);
               tma_load_2d_pair_hint(smem_a2 + s * C::kA2Bytes, mw, fb0, kb * C::kKE, f_wrow, wpol);
@@ -192,7 +199,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           } else {
             if (rank == 0) mbar_arrive_expect_tx(fb, tx);
-            if (p.l2_hints) {
+            if (p.l2_hints & 1) {
               tma_load_2d_pair_hint(smem_a + s * C::kABytes, mw, fb0, kb * C::kKE, w_row, wpol);
               if constexpr (C::kGlu)
                 tma_load_2d_pair_hint(smem_a2 + s * C::kA2Bytes, mw, fb0, kb * C::kKE, w_row + 128, wpol);
@@ -652,32 +659,6 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
 // ------------------------------------------------------------------ fp8 weights, two-term tokens
 namespace dsca {
 
-// 2-D byte tensor map over a row-major [rows, cols] matrix (e4m3 weights or two-term token rows),
-// box = box_rows x 128 bytes, 128-byte swizzle.
-static int make_map_e4m3(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
-  typedef CUresult (*Encode)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                             const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                             CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-  static Encode enc = nullptr;
-  if (enc == nullptr) {
-    void* fn = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      return DSCA_ERR_CUDA;
-    enc = reinterpret_cast<Encode>(fn);
-  }
-  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || cols % 16 != 0) return DSCA_ERR_BAD_ARG;
-  cuuint64_t dims[2] = {cols, rows};
-  cuuint64_t strides[1] = {cols};
-  cuuint32_t box[2] = {128, box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? DSCA_OK : DSCA_ERR_CUDA;
-}
-
 static int launch_pair_f8(int epi, const CUtensorMap& w0, const CUtensorMap& t0, const CUtensorMap& w1,
                           const CUtensorMap& t1, const gemm::Params& p, int grid, cudaStream_t stream) {
   switch (epi) {
@@ -702,7 +683,10 @@ int launch_grouped_ffn_f8_split(const dsca_ffn_args* f, int num_sms, cudaStream_
   const bool glu = f->act == DSCA_ACT_SWIGLU;
   const int Kd = (f->d + 127) & ~127;  // token row: [hi: Kd | lo: Kd] bytes
   int rc;
-  if (phases & 1) {
+  if ((phases & 1) && f->tile_rows != 256) {
+    // GEMM1 on single-CTA tiles (as the bf16 default), then the intermediates' split below
+    if ((rc = launch_gemm1_f8_single(f, num_sms, stream))) return rc;
+  } else if (phases & 1) {
     using CG = gemm::pair::Cfg<gemm::kEpiSwiGLU, true>;
     using CR = gemm::pair::Cfg<gemm::kEpiReLU, true>;
     const uint32_t tbox = glu ? CG::kTBox : CR::kTBox;
@@ -755,6 +739,8 @@ int launch_grouped_ffn_f8_split(const dsca_ffn_args* f, int num_sms, cudaStream_
       s1.w_scale = f->ws1_scale;
     }
     if ((rc = launch_pair_f8(epi, w0, t0, w1, t1, p, grid, stream))) return rc;
+  }
+  if (phases & 1) {
     // the intermediates as two-term rows for GEMM2 (routed rows: as many as the groups hold)
     if (routed && (rc = launch_split_rows(f->h, f->ip, f->capacity, f->group_offsets + f->num_groups, f->ip, f->hq,
                                           f->h_scale, stream)))

@@ -514,7 +514,7 @@ __global__ void __launch_bounds__(fused::kThreads, 1)
   constexpr int kXStage = fused::kXStage, kPartPitch = fused::kPartPitch, kSmemBytes = fused::kSmemBytes;
   constexpr int kThreads = fused::kThreads;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  __shared__ uint64_t wfull[kMaxSteps], sfree[2], acc_full, mma_done;
+  __shared__ uint64_t wfull[kMaxSteps], sfree[2], sliced[2], acc_full, mma_done;
   __shared__ uint32_t tmem_base_s;
   __shared__ int abort_s;
   __shared__ int rpart[BM], rfin[BM], rw_s[kRows];
@@ -539,10 +539,27 @@ __global__ void __launch_bounds__(fused::kThreads, 1)
   const int ks0 = min(nks_total, (int)rank * q);
   const int nks = min(nks_total, ks0 + q) - ks0;
 
+  // ---------------- 1. x rows into registers (issued first: the set-up below runs while they
+  //                     are in flight), then the rows' exponents
+  const int c16 = tid & 15;
+  uint4 xv[kMaxSteps][4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int t = row0 + (tid >> 4) + 32 * u;
+#pragma unroll
+    for (int s = 0; s < kMaxSteps; ++s) {
+      const int k = (ks0 + s) * kKStep + 8 * c16;
+      xv[s][u] = (s < nks && t < T && k < d)
+                     ? ldg_nc_v4(reinterpret_cast<const uint16_t*>(a.x) + (size_t)t * d + k)
+                     : make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
   if (tid == 0) {
     for (int s = 0; s < kMaxSteps; ++s) mbar_init(smem_u32(&wfull[s]), 1);
     mbar_init(smem_u32(&sfree[0]), 1);
     mbar_init(smem_u32(&sfree[1]), 1);
+    mbar_init(smem_u32(&sliced[0]), kThreads);
+    mbar_init(smem_u32(&sliced[1]), kThreads);
     mbar_init(smem_u32(&acc_full), 1);
     mbar_init(smem_u32(&mma_done), 1);
     abort_s = 0;
@@ -572,20 +589,6 @@ __global__ void __launch_bounds__(fused::kThreads, 1)
     }
   }
 
-  // ---------------- 1. x rows into registers, the rows' exponents
-  const int c16 = tid & 15;
-  uint4 xv[kMaxSteps][4];
-#pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    const int t = row0 + (tid >> 4) + 32 * u;
-#pragma unroll
-    for (int s = 0; s < kMaxSteps; ++s) {
-      const int k = (ks0 + s) * kKStep + 8 * c16;
-      xv[s][u] = (s < nks && t < T && k < d)
-                     ? ldg_nc_v4(reinterpret_cast<const uint16_t*>(a.x) + (size_t)t * d + k)
-                     : make_uint4(0u, 0u, 0u, 0u);
-    }
-  }
 #pragma unroll
   for (int u = 0; u < 4; ++u) {
     uint32_t m2 = 0u;
@@ -630,14 +633,15 @@ __global__ void __launch_bounds__(fused::kThreads, 1)
     pre[u] = big ? __uint_as_float((uint32_t)(64 + 127) << 23) : 1.0f;
     scl[u] = __uint_as_float((uint32_t)((big ? sh - 64 : sh) + 127) << 23);
   }
+  // every thread slices its share of step s into buffer s & 1 (after the MMAs of step s - 2 have
+  // released it) and arrives on sliced[s & 1]; thread 32 waits for the 512 arrivals and the W
+  // planes, then issues the step's MMAs (no CTA-wide barrier per step)
   bool issued = false;
 #pragma unroll
   for (int s = 0; s < kMaxSteps; ++s) {
     if (s >= nks) break;
     const int b = s & 1;
-    if (s >= 2 && tid == 0) mbar_wait(smem_u32(&sfree[b]), (uint32_t)(((s - 2) >> 1) & 1), abort_flag, err);
-    __syncthreads();
-    if (abort_s) break;
+    if (s >= 2 && !mbar_wait(smem_u32(&sfree[b]), (uint32_t)(((s - 2) >> 1) & 1), abort_flag, err)) break;
     uint8_t* xb = xs + b * kXStage;
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
@@ -657,8 +661,9 @@ __global__ void __launch_bounds__(fused::kThreads, 1)
       *reinterpret_cast<uint2*>(xb + 2 * kXPlane + off) = make_uint2(p2a, p2b);
     }
     fence_proxy_async_smem();
-    __syncthreads();
-    if (tid == 32 && mbar_wait(smem_u32(&wfull[s]), 0u, abort_flag, err)) {
+    mbar_arrive(smem_u32(&sliced[b]));
+    if (tid == 32 && mbar_wait(smem_u32(&sliced[b]), (uint32_t)((s >> 1) & 1), abort_flag, err) &&
+        mbar_wait(smem_u32(&wfull[s]), 0u, abort_flag, err)) {
       tc_fence_after();
       // X_j times the three stacked router slice planes [W_0; W_1; W_2] (N = 192) lands on the
       // accumulators D_j | D_j+1 | D_j+2: the three MMAs write overlapping 192-column windows of
@@ -739,16 +744,16 @@ __global__ void __launch_bounds__(fused::kThreads, 1)
     const int tr = 32 * (int)rank + rl;
     long long acc[4] = {0, 0, 0, 0};
     const uint32_t addr = smem_u32(part + (size_t)tr * kPartPitch + eg);
+    long long v[kSplit][4];  // every peer's partials requested before the first is used
 #pragma unroll
     for (uint32_t src = 0; src < (uint32_t)kSplit; ++src) {
-      long long v0, v1, v2, v3;
-      ld_dsmem_2x64(addr, src, v0, v1);
-      ld_dsmem_2x64(addr + 16u, src, v2, v3);
-      acc[0] += v0;
-      acc[1] += v1;
-      acc[2] += v2;
-      acc[3] += v3;
+      ld_dsmem_2x64(addr, src, v[src][0], v[src][1]);
+      ld_dsmem_2x64(addr + 16u, src, v[src][2], v[src][3]);
     }
+#pragma unroll
+    for (int src = 0; src < kSplit; ++src)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[i] += v[src][i];
     const int rx = rfin[tr];
 #pragma unroll
     for (int i = 0; i < 4; ++i)

@@ -348,9 +348,11 @@ class MoEEngine:
         if (self.shared_gate_weight is None) != (experts.ws1 is None):
             raise ValueError("shared expert and shared gate must be given together")
         # True (bf16 only): router logits on the tensor cores instead of the CUDA cores — exact
-        # fixed-point accumulation on int8 tcgen05 MMAs (router_tc.cu); off by default, the
-        # CUDA-core router is faster on the measured workloads
-        self.router_tensor_cores = False
+        # fixed-point accumulation on int8 tcgen05 MMAs (router_tc.cu).  On by default where the
+        # one-kernel form applies (d <= 2048, at most 64 router rows), which measured faster than
+        # the CUDA-core router (its fixed fp32 chunk order, the form for f32 and wider models)
+        n_rows = self.E + (0 if self.shared_gate_weight is None else 1)
+        self.router_tensor_cores = bool(self.dtype == torch.bfloat16 and self.d <= 2048 and n_rows <= 64)
         self._w_slices = self._w_exp = None
         self.rank, self.world, self.group = rank, world, group
         if expert_to_gpu is None:

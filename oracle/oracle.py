@@ -103,6 +103,24 @@ def router_logits_fixed(x, W) -> np.ndarray:
     return out
 
 
+def tensor_core_router_default(tau: str, d: int, rows: int) -> bool:
+    """The engine's default router form: the tensor-core router for bf16 with d <= 2048 and at most
+    64 router rows (experts plus the shared-expert gate), the CUDA-core router otherwise."""
+    return tau == "bf16" and d <= 2048 and rows <= 64
+
+
+def router_logits_for(x, W, tau: str, tensor_cores: bool | None = None, rows: int | None = None) -> np.ndarray:
+    """The logits of the router form an engine ran: ``router_logits_fixed`` (exact fixed-point
+    products, the tensor-core router) for bf16 with ``tensor_cores``, else ``router_logits`` (the
+    CUDA-core router's fixed fp32 chunk order).  ``tensor_cores=None``: the engine's default for
+    `rows` router rows (default: W's rows)."""
+    if tensor_cores is None:
+        tensor_cores = tensor_core_router_default(tau, np.shape(x)[1], np.shape(W)[0] if rows is None else rows)
+    if tensor_cores and tau == "bf16":
+        return router_logits_fixed(x, W)
+    return router_logits(x, W, tau)
+
+
 def softmax(logits) -> np.ndarray:
     lg = _f32(logits)
     out = np.empty_like(lg)
@@ -252,13 +270,14 @@ def _silu(v):
     return v / (1.0 + np.exp(-v))
 
 
-def switch_forward(x, Wr, wi, wo, tau: str, compute=np.float64):
+def switch_forward(x, Wr, wi, wo, tau: str, compute=np.float64, tensor_cores=None):
     """Switch top-1 block (src/qosmoe/moe_layer.py:196-269 with router.py:52-63):
     y[t] = g[t] * wo[e] ReLU(wi[e] x[t]).  Returns (y, logits, idx, gate).  `compute` is the
-    FFN arithmetic type: float64 for checking, float32 for the timed CPU baseline."""
+    FFN arithmetic type: float64 for checking, float32 for the timed CPU baseline;
+    `tensor_cores` the router form (None: the engine's default, router_logits_for)."""
     c = compute
     xc = np.asarray(x, c)
-    logits = router_logits(x, Wr, tau)
+    logits = router_logits_for(x, Wr, tau, tensor_cores)
     idx, gate = route_top1(logits, tau)
     E = wi.shape[0]
     y = np.zeros_like(xc)
@@ -271,13 +290,14 @@ def switch_forward(x, Wr, wi, wo, tau: str, compute=np.float64):
     return y, logits, idx, gate
 
 
-def qwen_forward(x, Wg, p: dict, k: int, norm_topk: bool, act: str, compute=np.float64):
+def qwen_forward(x, Wg, p: dict, k: int, norm_topk: bool, act: str, compute=np.float64, tensor_cores=None):
     """Qwen top-k + shared-expert block (qwen_ep_adapter/qwen_ep.py:44-97):
     y[t] = sum_j w[t,j] D_c(SiLU(G_c x) * U_c x) + sigmoid(g . x) * D_s(SiLU(G_s x) * U_s x).
-    Returns (y, logits, ids, w, shared_gate_sigmoid).  `compute` as in switch_forward."""
+    Returns (y, logits, ids, w, shared_gate_sigmoid).  `compute` and `tensor_cores` as in
+    switch_forward (the router rows count the shared-expert gate)."""
     c = compute
     xc = np.asarray(x, c)
-    logits = router_logits(x, Wg, "bf16" if act == "bf16" else "f32")
+    logits = router_logits_for(x, Wg, "bf16" if act == "bf16" else "f32", tensor_cores, rows=np.shape(Wg)[0] + 1)
     ids, w = route_topk(logits, k, norm_topk, act)
     E = p["gate"].shape[0]
     y = np.zeros_like(xc)

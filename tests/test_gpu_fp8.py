@@ -1,9 +1,10 @@
 """fp8-e4m3 expert weights with per-output-channel fp32 scales: the block (f16 operands, fp32
 accumulation, scales in the epilogue) against the fp32 oracle run on the dequantised weights
 (q * scale) and the same inputs — 2e-2 max relative error.  Routing is unchanged by the weight
-format and stays bit-exact.  Three kernel forms run: "split" (the e4m3 weights unconverted on
-kind::f8f6f4 MMAs against two-term e4m3 tokens, the default), "smem" (weights converted to f16
-in shared memory) and "tmem" (converted into tensor memory, the MMA's A operand read from TMEM).
+format and stays bit-exact.  Four kernel forms run: "split" (the e4m3 weights unconverted on
+kind::f8f6f4 MMAs against two-term e4m3 tokens, the default: GEMM1 single-CTA tiles, GEMM2
+CTA-pair tiles), "split-pair" (both GEMMs on CTA pairs), "smem" (weights converted to f16 in
+shared memory) and "tmem" (converted into tensor memory, the MMA's A operand read from TMEM).
 dsca_split_rows is bit-exact against the oracle's restatement."""
 import numpy as np
 import pytest
@@ -39,12 +40,13 @@ def _qwen(dev, T, d, E, I, Is, seed):
     return eng, Wg, p
 
 
-FORMS = ["split", "smem", "tmem"]
+FORMS = ["split", "split-pair", "smem", "tmem"]
 
 
 def _form(eng, form):
-    eng.fp8_split = form == "split"
-    eng.tile_rows = 256 if form == "tmem" else 0
+    """split: GEMM1 on single-CTA tiles, GEMM2 on CTA pairs; split-pair: both GEMMs on CTA pairs."""
+    eng.fp8_split = form.startswith("split")
+    eng.tile_rows = 256 if form in ("tmem", "split-pair") else 0
 
 
 @pytest.mark.parametrize("tile_rows", FORMS)

@@ -84,7 +84,7 @@ def test_router_switch_bit_exact(cuda, dtype, T, d, E):
     r = eng.forward(_t(x, tdt, cuda))
     torch.cuda.synchronize()
     eng.check()
-    lg = O.router_logits(x, Wr, dtype)
+    lg = O.router_logits_for(x, Wr, dtype, eng.router_tensor_cores)
     idx, gate = O.route_top1(lg, dtype)
     assert np.array_equal(_np(r["logits"]).view(np.uint32), lg.view(np.uint32))
     assert np.array_equal(r["expert_index"].cpu().numpy(), idx)
@@ -103,13 +103,13 @@ def test_router_topk_bit_exact(cuda, T, d, E, k, norm):
     r = eng.forward(_t(x, torch.bfloat16, cuda))
     torch.cuda.synchronize()
     eng.check()
-    lg = O.router_logits(x, Wg, "bf16")
+    lg = O.router_logits_for(x, Wg, "bf16", eng.router_tensor_cores)
     ids, w = O.route_topk(lg, k, norm, "bf16")
     assert np.array_equal(_np(r["logits"]).view(np.uint32), lg.view(np.uint32))
     assert np.array_equal(r["topk_ids"].cpu().numpy(), ids)
     assert np.array_equal(r["topk_w"].cpu().numpy().view(np.uint32), w.view(np.uint32))
     # shared-expert gate: sigmoid of the bf16-rounded gate logit
-    z = O.router_logits(x, p["s_gate_w"], "bf16")[:, 0].astype(np.float64)
+    z = O.router_logits_for(x, p["s_gate_w"], "bf16", eng.router_tensor_cores)[:, 0].astype(np.float64)
     sg = 1.0 / (1.0 + np.exp(-z))
     assert np.abs(r["shared_gate"].cpu().numpy() - sg).max() < 1e-6
 
@@ -229,7 +229,8 @@ def test_switch_golden_through_plugin_layer(cuda, name):
     got = idx.cpu().numpy()
     assert np.array_equal(got[~near], z["expert_index"][~near])
     # exact against the oracle on every token
-    assert np.array_equal(got, O.route_top1(O.router_logits(z["x"], z["Wr"], m["dtype"]), m["dtype"])[0])
+    tc = layer.engine.router_tensor_cores
+    assert np.array_equal(got, O.route_top1(O.router_logits_for(z["x"], z["Wr"], m["dtype"], tc), m["dtype"])[0])
     tol = F32_TOL if m["dtype"] == "f32" else BF16_TOL
     same = got == z["expert_index"]
     assert O.max_rel_err(_np(y).reshape(-1, m["d"])[same], z["y"][same]) < tol
@@ -249,7 +250,8 @@ def test_qwen_golden(cuda, name):
         eng.check()
         lg = _np(res["logits"])
         assert_logits_close(lg, z["logits"][r], m["dtype"])
-        assert np.array_equal(lg.view(np.uint32), O.router_logits(z["x"][r], z["Wg"], m["dtype"]).view(np.uint32))
+        assert np.array_equal(lg.view(np.uint32), O.router_logits_for(z["x"][r], z["Wg"], m["dtype"],
+                                                                       eng.router_tensor_cores).view(np.uint32))
         pr = O.softmax(lg)
         s = -np.sort(-pr, axis=1)
         keep = (s[:, m["top_k"] - 1] != s[:, m["top_k"]]) & ~routing_near_ties(lg, m["top_k"], m["dtype"])
@@ -300,7 +302,7 @@ def test_qwen_full_size_bf16(cuda):
     r = eng.forward(_t(x, torch.bfloat16, cuda))
     torch.cuda.synchronize()
     eng.check()
-    lg = O.router_logits(x, Wg, "bf16")
+    lg = O.router_logits_for(x, Wg, "bf16", eng.router_tensor_cores)
     ids, wts = O.route_topk(lg, k, False, "bf16")
     assert np.array_equal(_np(r["logits"]).view(np.uint32), lg.view(np.uint32))
     assert np.array_equal(r["topk_ids"].cpu().numpy(), ids)
@@ -348,7 +350,7 @@ def test_switch_full_size_bf16(cuda):
     r = eng.forward(_t(x, torch.bfloat16, cuda))
     torch.cuda.synchronize()
     eng.check()
-    lg = O.router_logits(x, Wr, "bf16")
+    lg = O.router_logits_for(x, Wr, "bf16", eng.router_tensor_cores)
     idx, gate = O.route_top1(lg, "bf16")
     assert np.array_equal(r["expert_index"].cpu().numpy(), idx)
     sample = syn.rng(904).choice(T, 64, replace=False)
