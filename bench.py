@@ -93,13 +93,14 @@ def parse():
     ap.add_argument("--tile-order", type=int, choices=[0, 1], default=None,
                     help="routed and shared tiles of one GEMM launch: 0 = one segment after the other, "
                          "1 = interleaved (default: the engine's)")
-    ap.add_argument("--cache-hints", type=int, choices=[0, 1, 2, 3], default=0,
-                    help="GEMM loads: bit 0 = routed weights evict-first, the rest evict-last; bit 1 = each CTA "
-                         "prefetches its next tile's weights into L2")
+    ap.add_argument("--cache-hints", type=int, choices=[0, 1], default=0,
+                    help="L2 policies of the GEMM loads: 1 = routed weights evict-first, the rest evict-last")
     ap.add_argument("--router-tc", type=int, choices=[0, 1], default=None,
                     help="router logits: 1 = tensor cores (exact int8 fixed-point products, correctly "
                          "rounded bf16 logits), 0 = CUDA-core fp32 fma chains in the fixed chunk order "
                          "(default: the engine's, tensor cores where they apply)")
+    ap.add_argument("--qos-stream", choices=["side", "main"], default=None,
+                    help="expert parallel: where the QoS scores run (default: the engine's)")
     ap.add_argument("--no-qos-order", action="store_true",
                     help="expert parallel: skip the QoS planner (scores, priority sum) and run the routed "
                          "tiles in expert order")
@@ -147,19 +148,24 @@ def flops_and_bytes(w, T, rows_routed, E_touched, wbytes=2):
 def launches_per_step(world, exchange, eng):
     """This library's kernel launches in one forward (the timed step)."""
     if eng.cache is not None:
-        # router, permute, shared GEMM1 + GEMM2, QoS scores (2), GEMM1 + GEMM2 per planned
+        # router, permute, shared GEMM1 + GEMM2, QoS scores (3), GEMM1 + GEMM2 per planned
         # expert, combine
         plan = eng.last_exec_plan
         n = len(plan.expert_order) if plan is not None else eng.E
-        return 2 + (2 if eng.experts.ws1 is not None else 0) + 2 + 2 * n + 1 + (0 if eng.fuse_scan else 1)
+        return 2 + (2 if eng.experts.ws1 is not None else 0) + 3 + 2 * n + 1 + (0 if eng.fuse_scan else 1)
+    shared = eng.experts.ws1 is not None
+    # fp8 weights with two-term tokens: the GEMM1 intermediates are split before GEMM2
+    split = (1 + (1 if shared else 0)) if (eng.experts.fp8 and eng.fp8_split) else 0
     if world == 1:
         # router (+ fused scan), permute, GEMM1, GEMM2, combine
-        return 5 + (0 if eng.fuse_scan else 1)
+        return 5 + (0 if eng.fuse_scan else 1) + split
     if exchange == "p2p":
         # router, plan, dispatch, wait, routed GEMM1, routed GEMM2, wait, combine; + the return
-        # kernel ("overlap"); + shared-expert GEMM1 and GEMM2
-        return (8 + (1 if eng.ep_return == "overlap" else 0) + (2 if eng.experts.ws1 is not None else 0)
-                + (2 if eng.qos_order else 0) + (0 if eng.fuse_scan else 1))
+        # kernel ("overlap"); + shared-expert GEMM1 and GEMM2; + the QoS scores (three kernels);
+        # fp8 two-term tokens: + the split of x (shared expert) and of the received rows
+        return (8 + (1 if eng.ep_return == "overlap" else 0) + (2 if shared else 0)
+                + (3 if eng.qos_order else 0) + (0 if eng.fuse_scan else 1)
+                + (split + 1 + (1 if shared else 0) if split else 0))
     # router, permute into the send buffer, GEMM1, GEMM2, combine (NCCL does the exchange)
     return 5 + (0 if eng.fuse_scan else 1)
 
@@ -916,6 +922,8 @@ def run_ours(args, w, T):
         eng.tile_order = args.tile_order
     eng.cache_hints = args.cache_hints
     eng.qos_order = not args.no_qos_order
+    if args.qos_stream is not None:
+        eng.qos_stream = args.qos_stream
     if args.router_tc is not None:
         eng.router_tensor_cores = bool(args.router_tc)
     eng.ep_side_sms = args.ep_side_sms
@@ -988,6 +996,32 @@ def run_ours(args, w, T):
     ms_per_step = float(tot.item()) / args.steps
     value = T * world / (ms_per_step / 1e3)
     clk = clocks.stop() if local == 0 else None
+
+    # ---- the same step back to back for ~150 ms (no L2 flush: the expert weights exceed L2),
+    #      with the clocks sampled throughout: which bf16 peak (burst or sustained) the GEMMs see
+    #      once the power and clock settle; reported beside the headline, not in it
+    sustained = None
+    n_long = max(50, int(150.0 / max(ms_per_step, 1e-3)))
+    try:
+        clocks2 = NvmlClockSampler(uuid)
+    except Exception:  # noqa: BLE001
+        clocks2 = ClockSampler(uuid)
+    barrier()
+    if local == 0:
+        clocks2.start()
+    l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0.record()
+    for _ in range(n_long):
+        step()
+    l1.record()
+    barrier()
+    clk2 = clocks2.stop() if local == 0 else None
+    l_ms = torch.tensor([l0.elapsed_time(l1) / n_long], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(l_ms, op=dist.ReduceOp.MAX)
+    sustained = {"steps": n_long, "ms_per_step": float(l_ms.item()),
+                 "value": T * world / (float(l_ms.item()) / 1e3), "clocks": clk2,
+                 "note": "back-to-back steps without the L2 flush, clocks sampled throughout"}
 
     # ---- host cost of one forward: time to enqueue it (eager: one ctypes call per kernel; graph:
     #      one replay), measured without waiting for the device
@@ -1243,9 +1277,7 @@ def run_ours(args, w, T):
                 "fp8_form": ({"split": "e4m3 weights unconverted (kind::f8f6f4) x two-term e4m3 tokens",
                               "smem": "weights converted to f16 in shared memory",
                               "tmem": "weights converted to f16 in tensor memory"}[args.fp8_form] if args.fp8 else None),
-                "l2_hints": ["default", "routed weights evict-first, the rest evict-last",
-                             "next tile's weights prefetched into L2",
-                             "evict-first / evict-last, next tile's weights prefetched"][args.cache_hints],
+                "l2_hints": ["default", "routed weights evict-first, the rest evict-last"][args.cache_hints],
                 "qos_order": (eng.qos_order if world > 1 else None),
                 "router": ("tensor cores: exact int8 fixed-point products, one fused kernel"
                            if eng.router_tensor_cores else "CUDA cores: fp32 fma chains in the fixed chunk order")},
@@ -1254,7 +1286,7 @@ def run_ours(args, w, T):
                     "d2h_bytes_per_step": T * w["d"] * 2, "mode": e2e_mode, "serial_value": e2e_serial,
                     "host_link": link},
             "gpu_launches": launches_per_step(world, args.exchange, eng) * args.steps, "clocks": clk,
-            "parity": parity, "host": host,
+            "parity": parity, "host": host, "sustained": sustained,
             "expert_cache": cache_info,
             "phases_ms": phase_ms, "all_to_all": a2a, "other_configs": extra,
         }

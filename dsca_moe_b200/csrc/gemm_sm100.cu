@@ -130,19 +130,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           seg0_ready = true;
         }
         const int kb_n = p.seg[ti.seg].k_blocks;
-        // l2_hints bit 1: the next tile's weights are prefetched into L2 alongside this tile's loads
-        const int next = (p.l2_hints & 2) ? sched_tile(r + 1, (int)blockIdx.x, (int)gridDim.x) : total;
-        TileInfo tn{};
-        if (next < total) tn = decode<BM>(p, ctl, next);
-        const CUtensorMap* mbn = tn.seg == 0 ? &tmB0 : &tmB1;
-        const int kb_pf = next < total ? p.seg[tn.seg].k_blocks : 0;
         for (int kb = 0; kb < kb_n; ++kb) {
           if (!mbar_wait(smem_u32(&ctl.empty[s]), ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
           const uint32_t fb = smem_u32(&ctl.full[s]);
           mbar_arrive_expect_tx(fb, kStageBytes);
           const int kx = kb * C::kKE;
-          if (kb < kb_pf) tma_prefetch_2d(mbn, kx, tn.b_row0);
-          if (p.l2_hints & 1) {
+          if (p.l2_hints) {
             tma_load_2d_hint(smem_a + s * kABytes, ma, fb, kx, ti.row0, pol_last);
             if constexpr (F8)  // the lo plane of the same token rows
               tma_load_2d_hint(smem_a + s * kABytes + C::kAPlane, ma, fb, p.seg[ti.seg].t_lo + kx, ti.row0, pol_last);

@@ -61,10 +61,8 @@ struct Params {
   // to their counts, so that at any time some SMs run the routed experts' tiles (which stream
   // every expert's weights from HBM) while the others run the shared expert's (tensor bound)
   int interleave_lead;
-  // L2 policies of the loads (bit 0): routed experts' weights (segment 0, streamed from DRAM and
-  // mostly read once) evict-first, shared-expert weights and token rows evict-last.  Bit 1: while
-  // loading K step kb of a tile, the producer prefetches K step kb of its next tile's weights into
-  // L2, so that a tile starting on an expert's weights finds them on the way from DRAM
+  // L2 policies of the loads: 0 = default; 1 = routed experts' weights (segment 0, streamed from
+  // DRAM and mostly read once) evict-first, shared-expert weights and token rows evict-last
   int l2_hints;
   // CTA-pair SwiGLU GEMM1 only: every whole 256-token block of a group is one non-swapped tile
   // (tokens as M = 256 over the pair, 128 channels' gate and up rows as N = 256, Segment::n_full

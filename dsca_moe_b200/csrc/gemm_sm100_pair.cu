@@ -163,14 +163,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int w_row = C::kGlu ? ti.b_row0 + ti.n_blk * BN + 256 * (int)rank : ti.b_row0 + 128 * (int)rank;
         const int t_row = ti.row0 + half * (int)rank;
         const int kb_n = p.seg[ti.seg].k_blocks;
-        // l2_hints bit 1: this CTA's weight rows of its next tile are prefetched into L2 alongside
-        // this tile's loads
-        const int next = (p.l2_hints & 2) ? sched_tile(r + 1, unit, units) : total;
-        TileInfo tn{};
-        if (next < total) tn = decode<TBN>(p, ctl, next);
-        const CUtensorMap* mwn = tn.seg == 0 ? &tmW0 : &tmW1;
-        const int kb_pf = (next < total && !(C::kGlu && tn.full)) ? p.seg[tn.seg].k_blocks : 0;
-        const int w_row_n = C::kGlu ? tn.b_row0 + tn.n_blk * BN + 256 * (int)rank : tn.b_row0 + 128 * (int)rank;
         // hybrid full tile (SwiGLU): this CTA's 128 tokens (two 64-row token boxes into slot A)
         // and the gate (even CTA) or up (odd CTA) rows of the tile's 128 channels (slot A2)
         const bool full = !F8 && C::kGlu && ti.full;
@@ -182,13 +174,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t fb0 = mapa_shared(fb, 0);  // the even CTA's full barrier
           // L2 policies (Params::l2_hints): routed weights evict-first, the rest evict-last
           const uint64_t wpol = ti.seg == 0 ? pol_first : pol_last;
-          if (kb < kb_pf) {
-            tma_prefetch_2d(mwn, kb * C::kKE, w_row_n);
-            if constexpr (C::kGlu) tma_prefetch_2d(mwn, kb * C::kKE, w_row_n + 128);
-          }
           if (full) {
             if (rank == 0) mbar_arrive_expect_tx(fb, tx_full);
-            if (p.l2_hints & 1) {
+            if (p.l2_hints) {
               tma_load_2d_pair_hint(smem_a + s * C::kABytes, mt, fb0, kb * C::kKE, f_trow, pol_last);
               tma_load_2d_pair_hint(smem_a + s * C::kABytes + C::kABytes / 2, mt, fb0, kb * C::kKE, f_trow + 64, pol_last);
               tma_load_2d_pair_hint(smem_a2 + s * C::kA2Bytes, mw, fb0, kb * C::kKE, f_wrow, wpol);
@@ -199,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           } else {
             if (rank == 0) mbar_arrive_expect_tx(fb, tx);
-            if (p.l2_hints & 1) {
+            if (p.l2_hints) {
               tma_load_2d_pair_hint(smem_a + s * C::kABytes, mw, fb0, kb * C::kKE, w_row, wpol);
               if constexpr (C::kGlu)
                 tma_load_2d_pair_hint(smem_a2 + s * C::kA2Bytes, mw, fb0, kb * C::kKE, w_row + 128, wpol);

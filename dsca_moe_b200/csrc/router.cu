@@ -236,8 +236,7 @@ __global__ void __launch_bounds__(kThreads, 1) router_kernel(Args a) {
   __syncthreads();
   }  // logits computed here
 
-  select_block<T>(a, lg_s, ids_s, emask, run_s, seg_s, &is_last, reinterpret_cast<int*>(smem),
-                  (int)(kSmemBytes / sizeof(int)), (int)blockIdx.x, (int)gridDim.x, (int)gridDim.x);
+  select_block<T>(a, lg_s, ids_s, emask, run_s, seg_s, &is_last, (int)blockIdx.x, (int)gridDim.x, (int)gridDim.x);
 }
 
 }  // namespace router

@@ -63,49 +63,39 @@ __device__ __forceinline__ float ord_val(uint32_t k) {
 
 
 // Per-expert counts, offsets and block bases from all blocks' histograms (the last CTA).
-// The histograms pass through shared memory in chunks of rows.  Thread (c, e) (e = tid % 64,
-// c = tid / 64) sums a contiguous run of rows of column e (a warp reads 32 consecutive columns
-// of one row: no bank conflicts), the 8 run sums of a column give each run its base, and the
-// bases go back through shared memory to coalesced stores.
-__device__ __forceinline__ void scan_blocks(const Args& a, int nb, int* sbuf, int cap_ints, int* run_s,
-                                            int (*seg)[kRows]) {
+// Thread (c, e) (e = tid % 64, c = tid / 64) takes a run of kR consecutive rows of column e per
+// round of 8 kR rows: its kR loads go out together into registers (a warp reads 32 consecutive
+// columns of one row per load), the 8 run sums of a column give each run its base, and each
+// thread writes its rows' block bases from its registers.  Integer sums: the result does not
+// depend on the order.
+__device__ __forceinline__ void scan_blocks(const Args& a, int nb, int* run_s, int (*seg)[kRows]) {
   constexpr int kSegs = kThreads / kRows;  // 8
+  constexpr int kR = 16;                   // rows per thread per round
   const int E = a.E, tid = threadIdx.x;
   const int e = tid % kRows, c = tid / kRows;
-  const int rows = max(1, min(nb, cap_ints / E));
   if (tid < kRows) run_s[tid] = 0;
-  for (int b0 = 0; b0 < nb; b0 += rows) {
-    const int nr = min(rows, nb - b0), n = nr * E;
-    const int32_t* src = a.block_hist + (size_t)b0 * E;
-    constexpr int kBatch = 8;  // loads in flight per thread
-    for (int i0 = 0; i0 < n; i0 += kBatch * kThreads) {
-      int v[kBatch];
+  __syncthreads();
+  for (int b0 = 0; b0 < nb; b0 += kSegs * kR) {
+    const int r0 = b0 + c * kR;
+    int v[kR];
 #pragma unroll
-      for (int u = 0; u < kBatch; ++u) {
-        const int i = i0 + u * kThreads + tid;
-        v[u] = i < n ? __ldcg(src + i) : 0;
-      }
-#pragma unroll
-      for (int u = 0; u < kBatch; ++u) {
-        const int i = i0 + u * kThreads + tid;
-        if (i < n) sbuf[i] = v[u];
-      }
+    for (int i = 0; i < kR; ++i) {
+      const int r = r0 + i;
+      v[i] = (e < E && r < nb) ? __ldcg(a.block_hist + (size_t)r * E + e) : 0;
     }
-    __syncthreads();
-    const int per = (nr + kSegs - 1) / kSegs;
-    const int r0 = min(nr, c * per), r1 = min(nr, r0 + per);
     int sum = 0;
-    if (e < E)
-      for (int r = r0; r < r1; ++r) sum += sbuf[r * E + e];
+#pragma unroll
+    for (int i = 0; i < kR; ++i) sum += v[i];
     seg[c][e] = sum;
     __syncthreads();
     if (e < E) {
       int base = run_s[e];
       for (int cc = 0; cc < c; ++cc) base += seg[cc][e];
-      for (int r = r0; r < r1; ++r) {
-        const int v = sbuf[r * E + e];
-        sbuf[r * E + e] = base;
-        base += v;
+#pragma unroll
+      for (int i = 0; i < kR; ++i) {
+        const int r = r0 + i;
+        if (r < nb) a.block_base[(size_t)r * E + e] = base;
+        base += v[i];
       }
     }
     __syncthreads();
@@ -114,8 +104,6 @@ __device__ __forceinline__ void scan_blocks(const Args& a, int nb, int* sbuf, in
       for (int cc = 0; cc < kSegs; ++cc) tot += seg[cc][e];
       run_s[e] = tot;
     }
-    int32_t* dst = a.block_base + (size_t)b0 * E;
-    for (int i = tid; i < n; i += kThreads) dst[i] = sbuf[i];
     __syncthreads();
   }
   // counts, and offsets by a warp-wide scan (lane L holds experts L and L + 32)
@@ -138,12 +126,12 @@ __device__ __forceinline__ void scan_blocks(const Args& a, int nb, int* sbuf, in
 // Selection, histogram, ranks and the fused scan for block `block` (tokens [32 block, +32)).
 // lg_s holds the block's logits [32][kLP] already rounded to the router dtype T; emask is zeroed
 // and a __syncthreads() has passed since.  nblocks = ceil(T / 32) (blocks from nblocks on write
-// no histogram row); the fused scan runs in the last of the grid's `ncta` CTAs to arrive.
-// scan_buf / scan_cap_ints: shared-memory scratch for that scan.  Every thread of the CTA calls it.
+// no histogram row); the fused scan runs in the last of the grid's `ncta` CTAs to arrive.  Every
+// thread of the CTA calls it.
 template <typename T>
 __device__ __forceinline__ void select_block(const Args& a, const float* lg_s, int (*ids_s)[DSCA_MAX_TOPK],
                                              uint32_t* emask, int* run_s, int (*seg_s)[kRows], int* is_last,
-                                             int* scan_buf, int scan_cap_ints, int block, int nblocks, int ncta) {
+                                             int block, int nblocks, int ncta) {
   const int tid = threadIdx.x;
   const int tok0 = block * kTokens;
   const int E = a.E;
@@ -242,7 +230,7 @@ __device__ __forceinline__ void select_block(const Args& a, const float* lg_s, i
     }
     __syncthreads();
     if (*is_last) {
-      scan_blocks(a, nblocks, scan_buf, scan_cap_ints, run_s, seg_s);
+      scan_blocks(a, nblocks, run_s, seg_s);
       if (tid == 0) *a.done_counter = 0u;  // ready for the next launch (stream ordered)
     }
   }

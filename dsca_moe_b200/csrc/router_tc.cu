@@ -439,7 +439,7 @@ constexpr int kXPlane = BM * kKStep;            // 16 KB: one x plane of one K s
 constexpr int kXStage = kSlices * kXPlane;      // 48 KB
 constexpr int kPartPitch = kRows + 2;           // int64 per staged partial row (bank spread)
 constexpr int kSmemBytes = kMaxSteps * kWStage + 2 * kXStage + 1024;
-static_assert(BM * kPartPitch * 8 <= 2 * kXStage, "partials fit the x slice buffers");
+static_assert(kSplit * 32 * kPartPitch * 8 <= 2 * kXStage, "the partial inboxes fit the x slice buffers");
 static_assert(kThreads == 16 * 32 && BM * (kKStep / 8) == 4 * kThreads, "four row chunks per thread and step");
 }  // namespace fused
 
@@ -448,8 +448,8 @@ __device__ __forceinline__ int ld_dsmem_s32(uint32_t addr, uint32_t rank) {
   asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(mapa_shared(addr, rank)) : "memory");
   return v;
 }
-__device__ __forceinline__ void ld_dsmem_2x64(uint32_t addr, uint32_t rank, long long& a, long long& b) {
-  asm volatile("ld.shared::cluster.v2.s64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "r"(mapa_shared(addr, rank)) : "memory");
+__device__ __forceinline__ void st_dsmem_2x64(uint32_t addr, uint32_t rank, long long a, long long b) {
+  asm volatile("st.shared::cluster.v2.s64 [%0], {%1, %2};" ::"r"(mapa_shared(addr, rank)), "l"(a), "l"(b) : "memory");
 }
 __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
   uint4 v;
@@ -511,7 +511,7 @@ __global__ void __launch_bounds__(fused::kThreads, 1)
                         int32_t* err) {
   constexpr int BM = fused::BM, kSplit = fused::kSplit, kKStep = fused::kKStep, kMaxSteps = fused::kMaxSteps;
   constexpr int kWPlane = fused::kWPlane, kWStage = fused::kWStage, kXPlane = fused::kXPlane;
-  constexpr int kXStage = fused::kXStage, kPartPitch = fused::kPartPitch, kSmemBytes = fused::kSmemBytes;
+  constexpr int kXStage = fused::kXStage, kPartPitch = fused::kPartPitch;
   constexpr int kThreads = fused::kThreads;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ uint64_t wfull[kMaxSteps], sfree[2], sliced[2], acc_full, mma_done;
@@ -698,11 +698,14 @@ __global__ void __launch_bounds__(fused::kThreads, 1)
     __syncthreads();
   }
 
-  // ---------------- 3. exact 64-bit partials of this CTA's K range
-  long long* part = reinterpret_cast<long long*>(xs);
+  // ---------------- 3. exact 64-bit partials of this CTA's K range, pushed to their owners: the
+  // partials of tile rows [32 o, 32 o + 32) go to CTA o's inbox slot [this CTA] (remote stores
+  // into its x slice buffers, free once every CTA's MMAs have completed), then each CTA adds the
+  // four slots of its own rows from local shared memory
+  long long* inbox = reinterpret_cast<long long*>(xs);  // [kSplit][32 rows][kPartPitch]
+  long long pvs[2][8];
   {
-    const int lq = warp & 3, cg = warp >> 2;  // TMEM lane quarter; 16 router rows
-    const int tr = 32 * lq + lane;            // tile row held by this lane
+    const int lq = warp & 3, cg = warp >> 2;  // TMEM lane quarter (tile rows 32 lq + lane); 16 router rows
     bool have = nks > 0 && !aborted;
     if (have) {
       int ok = 1;
@@ -731,42 +734,51 @@ __global__ void __launch_bounds__(fused::kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 8; ++i) pv[i] = 0;
       }
-      long long* dst = part + (size_t)tr * kPartPitch + e;
 #pragma unroll
-      for (int i = 0; i < 8; i += 2) *reinterpret_cast<longlong2*>(dst + i) = make_longlong2(pv[i], pv[i + 1]);
+      for (int i = 0; i < 8; ++i) pvs[h][i] = pv[i];
     }
   }
   tc_fence_before();
-  cluster_sync_all();  // every CTA's partials staged
+  cluster_sync_all();  // every CTA's MMAs are complete: the inboxes are free
   {
-    // tokens [32 rank, 32 rank + 32) of the tile: 4 router rows per thread
+    const int lq = warp & 3, cg = warp >> 2;
+    // rows 32 lq + lane belong to CTA lq: slot [rank], row lane
+    const uint32_t slot = smem_u32(inbox + ((size_t)rank * 32 + lane) * kPartPitch);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t dst = slot + (uint32_t)(16 * cg + 8 * h) * 8u;
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) st_dsmem_2x64(dst + 8u * (uint32_t)i, (uint32_t)lq, pvs[h][i], pvs[h][i + 1]);
+    }
+  }
+  cluster_sync_all();  // every CTA's pushes have landed
+  {
+    // tokens [32 rank, 32 rank + 32) of the tile: 4 router rows per thread, local reads
     const int rl = tid >> 4, eg = 4 * (tid & 15);
     const int tr = 32 * (int)rank + rl;
     long long acc[4] = {0, 0, 0, 0};
-    const uint32_t addr = smem_u32(part + (size_t)tr * kPartPitch + eg);
-    long long v[kSplit][4];  // every peer's partials requested before the first is used
 #pragma unroll
-    for (uint32_t src = 0; src < (uint32_t)kSplit; ++src) {
-      ld_dsmem_2x64(addr, src, v[src][0], v[src][1]);
-      ld_dsmem_2x64(addr + 16u, src, v[src][2], v[src][3]);
+    for (int src = 0; src < kSplit; ++src) {
+      const long long* q = inbox + ((size_t)src * 32 + rl) * kPartPitch + eg;
+      const longlong2 a01 = *reinterpret_cast<const longlong2*>(q), a23 = *reinterpret_cast<const longlong2*>(q + 2);
+      acc[0] += a01.x;
+      acc[1] += a01.y;
+      acc[2] += a23.x;
+      acc[3] += a23.y;
     }
-#pragma unroll
-    for (int src = 0; src < kSplit; ++src)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) acc[i] += v[src][i];
     const int rx = rfin[tr];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
       lg_s[rl * router::kLP + eg + i] = round_bf16(scale_pow2(__ll2float_rn(acc[i]), rx + rw_s[eg + i] - 294));
   }
-  cluster_sync_all();  // the peers have read this CTA's partials; lg_s complete
+  __syncthreads();  // lg_s complete (no CTA touches another's shared memory from here on)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
   const int nblocks = (T + router::kTokens - 1) / router::kTokens;
-  router::select_block<__nv_bfloat16>(a, lg_s, ids_s, emask, run_s, seg_s, &is_last, reinterpret_cast<int*>(smem),
-                                      kSmemBytes / (int)sizeof(int) - 256, (int)blockIdx.x, nblocks, (int)gridDim.x);
+  router::select_block<__nv_bfloat16>(a, lg_s, ids_s, emask, run_s, seg_s, &is_last, (int)blockIdx.x, nblocks,
+                                      (int)gridDim.x);
 }
 
 }  // namespace router_tc

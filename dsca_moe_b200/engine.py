@@ -395,6 +395,9 @@ class MoEEngine:
         # every rank, summed over the ranks and order the routed experts' tiles (the reference's
         # world > 1 path always runs them, src/qosmoe/moe_layer.py:306-316,379-380,422-427)
         self.qos_order = True
+        # where the QoS scores run at world > 1: "side" = on the side stream ahead of the plan,
+        # beside the shared-expert GEMM1; "main" = on the main stream before it
+        self.qos_stream = "side"
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._done_counter = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._ws = {}
@@ -827,12 +830,18 @@ class MoEEngine:
         main, side = torch.cuda.current_stream(), ep["side"]
         # the plan (counts exchange + harmony) and the dispatch run on the side stream, beside the
         # shared-expert GEMM1, which needs neither
+        prio = None
+        if self.qos_order and self.qos_stream == "main":
+            # the QoS scores alone on the GPU, before the shared-expert GEMM1 fills it (beside it
+            # they share its SMs and lengthen the side stream's chain to the dispatch)
+            self._qos(x, ws, qos)
+            prio = ws["expert_priority"]
+            self._mark("qos")
         routed = torch.cuda.Event()
         routed.record(main)
         side.wait_event(routed)
         with torch.cuda.stream(side):
-            prio = None
-            if self.qos_order:
+            if self.qos_order and self.qos_stream != "main":
                 t0 = self._side_mark()
                 self._qos(x, ws, qos)
                 prio = ws["expert_priority"]

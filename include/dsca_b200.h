@@ -245,11 +245,10 @@ typedef struct {
                                  QoS planner's order (dsca_ep_group_order); bf16 only, other dtypes
                                  run index order.  Only the order of the tiles changes, never a
                                  result */
-  int cache_hints;            /* bf16 and f8_split: bit 0 (1): the routed experts' weights (streamed
-                                 from DRAM, mostly read once) loaded evict-first, the shared
-                                 expert's weights and the token rows evict-last (else the default
-                                 L2 policy); bit 1 (2): each CTA prefetches the weights of its next
-                                 tile into L2 while it loads the current one */
+  int cache_hints;            /* bf16 and f8_split: 0 = default L2 policy for every load; 1 = the
+                                 routed experts' weights (streamed from DRAM, mostly read once)
+                                 loaded evict-first, the shared expert's weights and the token rows
+                                 evict-last */
   int tile_order;             /* routed and shared expert in one launch (bf16): 0 = one segment's
                                  tiles after the other's (the default; measured faster); 1 = their
                                  tiles interleaved in proportion to their counts (after one round
