@@ -32,7 +32,7 @@ class RouterArgs(ctypes.Structure):
                 ("shared_gate", _vp), ("block_hist", _vp), ("local_rank", _vp),
                 ("counts", _vp), ("offsets", _vp), ("block_base", _vp), ("done_counter", _vp),
                 ("w_slices", _vp), ("w_exp", _vp), ("x_slices", _vp), ("x_exp", _vp), ("logits_f32", _vp),
-                ("err", _vp)]
+                ("err", _vp), ("first_counts", _vp)]
 
 
 class ScanArgs(ctypes.Structure):
@@ -93,7 +93,8 @@ class QosArgs(ctypes.Structure):
                 ("seq_priority", _vp), ("remaining", _vp), ("valid", _vp), ("T", _i), ("d", _i), ("E", _i),
                 ("top_k", _i), ("attention_mode", _i), ("alpha", ctypes.c_float), ("beta", ctypes.c_float),
                 ("delta", ctypes.c_float), ("target_batch", ctypes.c_float), ("epsilon", ctypes.c_float),
-                ("token_score", _vp), ("expert_priority", _vp), ("err", _vp)]
+                ("token_score", _vp), ("expert_priority", _vp), ("err", _vp),
+                ("first_counts", _vp), ("partial", _vp), ("done_counter", _vp)]
 
 
 # every symbol include/dsca_b200.h declares

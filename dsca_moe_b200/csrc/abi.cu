@@ -239,6 +239,8 @@ int dsca_qos_priority(const dsca_qos_args* a, dsca_stream_t stream) {
   if (a->dtype != DSCA_BF16 && a->dtype != DSCA_F32) return DSCA_ERR_BAD_ARG;
   if (a->attention_mode != 0 && a->attention_mode != 1) return DSCA_ERR_BAD_ARG;
   if (a->E > 4 * DSCA_MAX_EXPERTS) return DSCA_ERR_CAPACITY;
+  if ((a->partial == nullptr) != (a->done_counter == nullptr)) return DSCA_ERR_BAD_ARG;
+  if (a->top_k > DSCA_MAX_TOPK) return DSCA_ERR_BAD_ARG;
   return dsca::launch_qos(a, reinterpret_cast<cudaStream_t>(stream));
 }
 

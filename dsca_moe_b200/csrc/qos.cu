@@ -67,14 +67,12 @@ __global__ void __launch_bounds__(1024) count_kernel(dsca_qos_args a, int32_t* f
   for (int e = threadIdx.x; e < a.E; e += blockDim.x) first_count[e] = cnt[e];
 }
 
-// One warp per token.  The row sums run in a fixed order: lane l takes the 16-byte vectors
-// l, l + 32, ... of the row (all loads issued before the arithmetic), each vector's elements in
-// index order into the lane's partial, then the xor butterfly.
+// One warp scores token t (every lane returns the score; lane 0 stores it).  The row sums run in
+// a fixed order: lane l takes the 16-byte vectors l, l + 32, ... of the row (all loads issued
+// before the arithmetic), each vector's elements in index order into the lane's partial, then
+// the xor butterfly.
 template <typename T>
-__global__ void __launch_bounds__(kWarps * 32) token_kernel(dsca_qos_args a, const int32_t* first_count) {
-  const int lane = threadIdx.x & 31;
-  const int t = (int)(blockIdx.x * kWarps + (threadIdx.x >> 5));
-  if (t >= a.T) return;
+__device__ __forceinline__ float score_token(const dsca_qos_args& a, int t, const int32_t* first_count, int lane) {
   const size_t row = (size_t)t * a.d;
   float ss = 0.0f;
   constexpr int kE = V16<T>::n;
@@ -134,9 +132,9 @@ __global__ void __launch_bounds__(kWarps * 32) token_kernel(dsca_qos_args a, con
     for (int off = 16; off >= 1; off >>= 1) q = __fadd_rn(q, __shfl_xor_sync(0xffffffffu, q, off));
     attn = __fdiv_rn(q, (float)a.E);
   }
+  float score = -1e9f;
   if (lane == 0) {
     const int e0 = a.topk_ids[(size_t)t * a.top_k];
-    float score = -1e9f;
     if (e0 < 0 || e0 >= a.E) {
       record_error(a.err, kErrIndex);
     } else {
@@ -153,6 +151,78 @@ __global__ void __launch_bounds__(kWarps * 32) token_kernel(dsca_qos_args a, con
     }
     a.token_score[t] = score;
   }
+  return __shfl_sync(0xffffffffu, score, 0);
+}
+
+// One warp per token.
+template <typename T>
+__global__ void __launch_bounds__(kWarps * 32) token_kernel(dsca_qos_args a, const int32_t* first_count) {
+  const int t = (int)(blockIdx.x * kWarps + (threadIdx.x >> 5));
+  if (t >= a.T) return;
+  score_token<T>(a, t, first_count, (int)(threadIdx.x & 31));
+}
+
+// The one-kernel form: CTA b scores tokens [32 b, 32 b + 32) (one warp per token), sums the scores
+// of its own (token, slot) assignments per expert in token-then-slot order into partial[b], and
+// the last CTA to finish adds the partials in CTA order (four runs of CTAs, eight loads in flight
+// each, then the four run sums in order).  first_count is read by every CTA before it arrives;
+// the last CTA zeroes it (when the router accumulated it) and the done counter.
+constexpr int kFusedTokens = 32;
+template <typename T>
+__global__ void __launch_bounds__(kWarps * 32) fused_kernel(dsca_qos_args a, const int32_t* first_count,
+                                                            int zero_first_count) {
+  __shared__ float sc[kFusedTokens];
+  __shared__ int ids_s[kFusedTokens * DSCA_MAX_TOPK];
+  __shared__ float run[4][kMaxE];
+  __shared__ int is_last;
+  const int warp = (int)(threadIdx.x >> 5), lane = (int)(threadIdx.x & 31), tid = (int)threadIdx.x;
+  const int t0 = (int)blockIdx.x * kFusedTokens, k = a.top_k, E = a.E;
+  for (int tl = warp; tl < kFusedTokens; tl += kWarps) {
+    const int t = t0 + tl;
+    const float s = t < a.T ? score_token<T>(a, t, first_count, lane) : 0.0f;
+    if (lane == 0) sc[tl] = s;
+  }
+  for (int i = tid; i < kFusedTokens * k; i += kWarps * 32) {
+    const int t = t0 + i / k;
+    ids_s[i] = t < a.T ? a.topk_ids[(size_t)t0 * k + i] : -1;
+  }
+  __syncthreads();
+  for (int e = tid; e < E; e += kWarps * 32) {
+    float p = 0.0f;
+    for (int i = 0; i < kFusedTokens * k; ++i)
+      if (ids_s[i] == e) p = __fadd_rn(p, sc[i / k]);
+    a.partial[(size_t)blockIdx.x * E + e] = p;
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const uint32_t prev = atomicAdd(a.done_counter, 1u);
+    is_last = prev == gridDim.x - 1u;
+    __threadfence();
+  }
+  __syncthreads();
+  if (!is_last) return;
+  const int nb = (int)gridDim.x, per = (nb + 3) / 4;
+  for (int idx = tid; idx < 4 * E; idx += kWarps * 32) {
+    const int e = idx % E, c = idx / E;
+    const int b0 = min(nb, c * per), b1 = min(nb, b0 + per);
+    float p = 0.0f;
+    for (int b = b0; b < b1; b += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = b + u < b1 ? __ldcg(a.partial + (size_t)(b + u) * E + e) : 0.0f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (b + u < b1) p = __fadd_rn(p, v[u]);
+    }
+    run[c][e] = p;
+  }
+  __syncthreads();
+  for (int e = tid; e < E; e += kWarps * 32) {
+    a.expert_priority[e] = __fadd_rn(__fadd_rn(__fadd_rn(run[0][e], run[1][e]), run[2][e]), run[3][e]);
+    if (zero_first_count) a.first_counts[e] = 0;
+  }
+  if (tid == 0) *a.done_counter = 0u;
 }
 
 // One CTA per expert sums the scores of its (token, slot) assignments; each thread walks a fixed
@@ -187,10 +257,22 @@ __global__ void __launch_bounds__(256) expert_kernel(dsca_qos_args a) {
 }  // namespace qos
 
 int launch_qos(const dsca_qos_args* a, cudaStream_t stream) {
-  // the first-choice counts go to the expert_priority array first (it is E floats long and is
-  // overwritten by the expert kernel below, after the token kernel has read the counts)
-  int32_t* first_count = reinterpret_cast<int32_t*>(a->expert_priority);
-  qos::count_kernel<<<1, 1024, 0, stream>>>(*a, first_count);
+  // the first-choice counts: from the router (first_counts), else counted here into the
+  // expert_priority array (E floats long, overwritten with the priorities once every token has
+  // read the counts)
+  const bool from_router = a->first_counts != nullptr;
+  int32_t* first_count = from_router ? a->first_counts : reinterpret_cast<int32_t*>(a->expert_priority);
+  if (!from_router) qos::count_kernel<<<1, 1024, 0, stream>>>(*a, first_count);
+  if (a->partial != nullptr && a->done_counter != nullptr) {
+    const int blocks = (a->T + qos::kFusedTokens - 1) / qos::kFusedTokens;
+    if (blocks > 0) {
+      if (a->dtype == DSCA_BF16)
+        qos::fused_kernel<__nv_bfloat16><<<blocks, qos::kWarps * 32, 0, stream>>>(*a, first_count, from_router);
+      else
+        qos::fused_kernel<float><<<blocks, qos::kWarps * 32, 0, stream>>>(*a, first_count, from_router);
+    }
+    return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
+  }
   const int blocks = (a->T + qos::kWarps - 1) / qos::kWarps;
   if (blocks > 0) {
     if (a->dtype == DSCA_BF16)

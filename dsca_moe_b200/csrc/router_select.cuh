@@ -39,6 +39,7 @@ struct Args {
   // precomputed logits [T][64] (fp32 values already rounded to the router dtype, rows past E
   // unused), or null: the kernel computes them (the chunked fp32 order below)
   const float* logits_in;
+  int32_t* first_counts;  // += first-choice counts of the block's tokens, or null
 };
 
 template <typename T>
@@ -212,6 +213,13 @@ __device__ __forceinline__ void select_block(const Args& a, const float* lg_s, i
     a.block_hist[(size_t)block * E + e] = __popc(emask[e]);
     if (a.done_counter != nullptr) __threadfence();  // the histogram before this CTA's arrival
   }
+  // first-choice counts (the QoS planner's n(e)): integer atomics, one per expert of the block
+  if (a.first_counts != nullptr)
+    for (int e = tid; e < E && block < nblocks; e += kThreads) {
+      int n = 0;
+      for (int tl = 0; tl < kTokens; ++tl) n += ids_s[tl][0] == e ? 1 : 0;
+      if (n) atomicAdd(&a.first_counts[e], n);
+    }
   for (int idx = tid; idx < kTokens * k; idx += kThreads) {
     const int tl = idx / k, j = idx % k;
     const int t = tok0 + tl;
@@ -263,6 +271,7 @@ inline void fill_args(const dsca_router_args* p, Args* a) {
   a->offsets = fused ? p->offsets : nullptr;
   a->block_base = fused ? p->block_base : nullptr;
   a->done_counter = fused ? p->done_counter : nullptr;
+  a->first_counts = p->first_counts;
 }
 
 }  // namespace router

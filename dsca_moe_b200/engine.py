@@ -400,6 +400,10 @@ class MoEEngine:
         self.qos_stream = "side"
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._done_counter = torch.zeros(1, dtype=torch.int32, device=self.device)
+        # the QoS scores: first-choice counts accumulated by the router (zeroed again by the QoS
+        # kernel) and the QoS kernel's own done counter
+        self._first_counts = torch.zeros(self.E, dtype=torch.int32, device=self.device)
+        self._qos_done = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._ws = {}
         self.last_plan = None
         self.last_layout = None
@@ -424,6 +428,14 @@ class MoEEngine:
         if name is not None and start is not None:
             self.side_markers.append((name, start, ev))
         return ev
+
+    @property
+    def _qos_in_forward(self) -> bool:
+        """Whether forward() runs the QoS scores (so the router accumulates their first-choice
+        counts): the one-GPU expert-cache path, and the fused exchange with the QoS order."""
+        if self.world == 1 and not self.ep_loopback:
+            return self.cache is not None
+        return self.exchange == "p2p" and self.qos_order
 
     @property
     def _uses_qos(self) -> bool:
@@ -452,6 +464,8 @@ class MoEEngine:
             block_base=torch.empty(max(nb, 1), E, dtype=torch.int32, device=dev),
             token_row=torch.empty(T, k, dtype=torch.int32, device=dev),
             token_score=torch.empty(T, dtype=torch.float32, device=dev) if self._uses_qos else None,
+            qos_partial=(torch.empty(max(_ceil(T, 32), 1), E, dtype=torch.float32, device=dev)
+                         if self._uses_qos else None),
             expert_priority=torch.empty(E, dtype=torch.float32, device=dev) if self._uses_qos else None,
             # fp8 weights: the FFN operands (rows, shared input, intermediates) are f16
             hs=torch.empty(T, pe.s_ip, dtype=self.op_dtype, device=dev) if pe.ws1 is not None else None,
@@ -523,6 +537,8 @@ class MoEEngine:
         a.expert_index = _ptr(ws["expert_index"])
         a.shared_gate = _ptr(ws["shared_gate"])
         a.block_hist, a.local_rank = _ptr(ws["block_hist"]), _ptr(ws["local_rank"])
+        if self._qos_in_forward:
+            a.first_counts = _ptr(self._first_counts)
         if self.fuse_scan:
             a.counts, a.offsets, a.block_base = _ptr(ws["counts"]), _ptr(ws["offsets"]), _ptr(ws["block_base"])
             a.done_counter = _ptr(self._done_counter)
@@ -680,6 +696,9 @@ class MoEEngine:
         a.alpha, a.beta, a.delta = p["alpha"], p["beta"], p["delta"]
         a.target_batch, a.epsilon = p["target_batch"], p["epsilon"]
         a.token_score, a.expert_priority, a.err = _ptr(ws["token_score"]), _ptr(ws["expert_priority"]), _ptr(self.err)
+        # one kernel; n(e) from the router of this forward (see _route)
+        a.first_counts = _ptr(self._first_counts) if self._qos_in_forward else None
+        a.partial, a.done_counter = _ptr(ws["qos_partial"]), _ptr(self._qos_done)
         L.call("dsca_qos_priority", ctypes.byref(a), _stream())
         # keep the per-token vectors alive until the kernel has read them
         ws["_qos_keep"] = (xp, seq, rem, val)

@@ -111,6 +111,9 @@ typedef struct {
   int32_t* x_exp;             /* [T] scratch (d > 2048) */
   float* logits_f32;          /* [T][64] scratch (d > 2048) */
   int32_t* err;               /* device error word for the tensor-core pass's bounded waits, or NULL */
+  /* optional: first_counts[e] += how many of the tokens chose e first (integer atomics; the
+     QoS planner's n(e), dsca_qos_args.first_counts, which zeroes it again), or NULL */
+  int32_t* first_counts;
 } dsca_router_args;
 DSCA_API int dsca_router_topk(const dsca_router_args* a, dsca_stream_t stream);
 
@@ -355,6 +358,14 @@ typedef struct {
   float* token_score;         /* [T] */
   float* expert_priority;     /* [E] */
   int32_t* err;
+  /* optional one-kernel form (set partial and done_counter): every 32-token CTA scores its tokens
+     and sums its own assignments per expert into partial; the last CTA to finish adds the
+     partials in CTA order into expert_priority (the same result whatever the schedule).
+     first_counts: n(e) accumulated by dsca_router_topk in the same forward, read here and left
+     zeroed for the next forward; NULL = counted here from topk_ids */
+  int32_t* first_counts;      /* [E] or NULL */
+  float* partial;             /* [ceil(T / 32), E] scratch, or NULL */
+  uint32_t* done_counter;     /* zeroed uint32 that the kernel leaves at zero, or NULL */
 } dsca_qos_args;
 DSCA_API int dsca_qos_priority(const dsca_qos_args* a, dsca_stream_t stream);
 
