@@ -120,6 +120,8 @@ def parse():
     ap.add_argument("--fp8-form", choices=["split", "smem", "tmem"], default="split",
                     help="fp8 weights: split = e4m3 weights unconverted on kind::f8f6f4 MMAs against two-term "
                          "e4m3 tokens; smem / tmem = weights converted to f16 in shared / tensor memory")
+    ap.add_argument("--static-tiles", action="store_true",
+                    help="grouped GEMM tiles by the static schedule instead of atomic tickets")
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the skew-stress and fp8 batch-sweep configurations that the default "
                          "block workload measures after the headline")
@@ -928,6 +930,8 @@ def run_ours(args, w, T):
         eng.router_tensor_cores = bool(args.router_tc)
     eng.ep_side_sms = args.ep_side_sms
     eng.pdl = not args.no_pdl
+    if args.static_tiles:
+        eng.dynamic_tiles = False
     peaks = load_peaks()
     if args.once:
         eng.forward(x)

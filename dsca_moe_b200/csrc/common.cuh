@@ -135,15 +135,31 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with cluster-scope acquire: for a barrier that a peer CTA of the cluster arrives on
+// (mbarrier.arrive.release.cluster) after storing data this CTA then reads.
+__device__ __forceinline__ bool mbar_try_wait_cl(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait for the phase with the given parity.  Returns false (after recording
 // kErrWaitTimeout and raising the CTA's abort flag) when the limit passes or another role of
 // the CTA has already aborted.
+template <bool kClusterScope = false>
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                           int32_t* err) {
-  if (mbar_try_wait(bar, parity)) return true;
+  auto tw = [](uint32_t b, uint32_t q) { return kClusterScope ? mbar_try_wait_cl(b, q) : mbar_try_wait(b, q); };
+  if (tw(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (tw(bar, parity)) return true;
     if ((it & 63u) == 0u) {
       if (*abort_flag) return false;
       if (globaltimer_ns() - t0 > kWaitLimitNs) {
@@ -223,6 +239,9 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
   return r;
+}
+__device__ __forceinline__ void st_shared_cluster_s32(uint32_t addr_cluster, int v) {
+  asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(addr_cluster), "r"(v) : "memory");
 }
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");

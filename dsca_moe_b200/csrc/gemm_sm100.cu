@@ -86,6 +86,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(smem_u32(&ctl.tmem_full[a]), 1);
       mbar_init(smem_u32(&ctl.tmem_empty[a]), 128);
     }
+    for (int i = 0; i < kTQ; ++i) {
+      mbar_init(smem_u32(&ctl.tq_full[i]), 1);
+      mbar_init(smem_u32(&ctl.tq_empty[i]), 5);  // the MMA thread and the four epilogue warps
+    }
     mbar_init(smem_u32(&ctl.mma_done), 1);
     ctl.abort_flag = 0;
     fence_mbar_init();
@@ -120,8 +124,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool seg0_ready = !p.pdl_seg0_wait;
       const uint64_t pol_first = l2_policy_evict_first(), pol_last = l2_policy_evict_last();
       for (int r = 0; ok; ++r) {
-        const int tile = sched_tile(r, (int)blockIdx.x, (int)gridDim.x);
-        if (tile >= total) break;
+        // the tile of round r: drawn (static or ticket) and published to the MMA and epilogue
+        const int slot = r % kTQ;
+        if (!mbar_wait(smem_u32(&ctl.tq_empty[slot]), (uint32_t)(((r / kTQ) & 1) ^ 1), abort_flag, p.err)) {
+          ok = false;
+          break;
+        }
+        int tile = ticket_tile(p, r, (int)blockIdx.x, (int)gridDim.x);
+        if (tile >= total) tile = -1;
+        *reinterpret_cast<volatile int*>(&ctl.tq[slot]) = tile;
+        mbar_arrive(smem_u32(&ctl.tq_full[slot]));
+        if (tile < 0) break;
         const TileInfo ti = decode<BM>(p, ctl, tile);
         const CUtensorMap* ma = ti.seg == 0 ? &tmA0 : &tmA1;
         const CUtensorMap* mb = ti.seg == 0 ? &tmB0 : &tmB1;
@@ -164,8 +177,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       int it = 0;
       bool ok = true;
       for (int r = 0; ok; ++r, ++it) {
-        const int tile = sched_tile(r, (int)blockIdx.x, (int)gridDim.x);
-        if (tile >= total) break;
+        const int tile = tq_take<false>(ctl, r, abort_flag, p.err, nullptr);
+        if (tile < 0) {
+          ok = *abort_flag == 0;
+          break;
+        }
         const TileInfo ti = decode<BM>(p, ctl, tile);
         const int acc = it & 1;
         const uint32_t acc_ph = (uint32_t)((it >> 1) & 1);
@@ -210,8 +226,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r_in_tile = q * 32 + lane;
     int it = 0;
     for (int r = 0;; ++r, ++it) {
-      const int tile = sched_tile(r, (int)blockIdx.x, (int)gridDim.x);
-      if (tile >= total) break;
+      int tile = 0;
+      if (lane == 0) tile = tq_take<false>(ctl, r, abort_flag, p.err, nullptr);
+      tile = __shfl_sync(0xffffffffu, tile, 0);
+      if (tile < 0) break;
       const TileInfo ti = decode<BM>(p, ctl, tile);
       const Segment& sg = p.seg[ti.seg];
       const int acc = it & 1;
@@ -312,6 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
+  if (threadIdx.x == 0) tile_counter_exit(p);
   if (p.ep_signal != nullptr) ep::signal_when_grid_done(p.ep_signal, &p.ep_signal->return_done, ep::kReturn);
 }
 
@@ -431,6 +450,7 @@ int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t st
     gemm::Params p{};
     const int epi = f->act == DSCA_ACT_SWIGLU ? gemm::kEpiSwiGLU : gemm::kEpiReLU;
     p.epi = epi;
+    p.tile_counter = f->tile_counters;  // GEMM1: [0, 2)
     p.err = f->err;
     p.nseg = shared ? 2 : 1;
     // equal K (the model width) in both segments; after a permute launched just before, the
@@ -483,6 +503,7 @@ int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t st
     }
     gemm::Params p{};
     p.epi = gemm::kEpiStore;
+    p.tile_counter = f->tile_counters != nullptr ? f->tile_counters + 2 : nullptr;  // GEMM2: [2, 4)
     p.err = f->err;
     p.nseg = shared ? 2 : 1;
     // the longer K first; with the fused return (ep_ctx) the routed tiles first, so that their
@@ -563,6 +584,7 @@ int launch_gemm1_f8_single(const dsca_ffn_args* f, int num_sms, cudaStream_t str
   gemm::Params p{};
   const int epi = f->act == DSCA_ACT_SWIGLU ? gemm::kEpiSwiGLU : gemm::kEpiReLU;
   p.epi = epi;
+  p.tile_counter = f->tile_counters;  // GEMM1: [0, 2)
   p.err = f->err;
   p.nseg = shared ? 2 : 1;
   p.seg_first = 0;

@@ -68,6 +68,9 @@ struct Params {
   // (tokens as M = 256 over the pair, 128 channels' gate and up rows as N = 256, Segment::n_full
   // blocks), the remaining < 256 tokens swap-AB tiles as usual
   int hybrid;
+  // dynamic tile schedule: [0] the launch's tile ticket counter, [1] its exit counter (both zero
+  // at launch; the last CTA to exit zeroes them), or null = the static boustrophedon schedule
+  uint32_t* tile_counter;
 };
 
 // A tile: token rows [row0, row0 + rows_valid) of group `group`, weight rows [b_row0, b_row0 + 256)
@@ -120,7 +123,12 @@ __device__ __forceinline__ __nv_bfloat16* ep_return_row(const ep::Ctx* c, int e,
   return nullptr;
 }
 
+constexpr int kTQ = 4;  // tile queue depth (tiles the producer may run ahead of the consumers)
+
 struct SmemCtl {
+  uint64_t tq_full[kTQ];   // tile id of round r published (1 arrival: the tile source)
+  uint64_t tq_empty[kTQ];  // read by every consumer of the CTA (count set by the kernel)
+  int tq[kTQ];
   uint64_t full[kMaxStages];
   uint64_t empty[kMaxStages];
   uint64_t tmem_full[2];
@@ -199,6 +207,39 @@ __device__ __forceinline__ void build_group_table(const Params& p, SmemCtl& ctl,
 
 // Tile index of round r for unit u of U (boustrophedon order).
 __device__ __forceinline__ int sched_tile(int r, int u, int U) { return r * U + ((r & 1) ? U - 1 - u : u); }
+
+// The tile of round r, from the launch's ticket counter (Params::tile_counter: every unit takes
+// the next tile when it is ready for one, so long and short tiles spread by their actual
+// durations) or the static schedule; `total` or more past the last tile.
+__device__ __forceinline__ int ticket_tile(const Params& p, int r, int u, int U) {
+  return p.tile_counter != nullptr ? (int)atomicAdd(p.tile_counter, 1u) : sched_tile(r, u, U);
+}
+
+// Tile queue, consumer side (one thread): the tile of round r, or -1 past the last tile or when
+// the wait ran out (the abort flag is then set).  Arrives on tq_empty[slot] once the id is read:
+// this CTA's barrier, or with kCluster the barrier at shared::cluster address empty_bars[slot]
+// (the even CTA's of a pair).
+template <bool kCluster>
+__device__ __forceinline__ int tq_take(SmemCtl& ctl, int r, volatile int* abort_flag, int32_t* err,
+                                       const uint32_t* empty_bars) {
+  const int slot = r % kTQ;
+  if (!mbar_wait<kCluster>(smem_u32(&ctl.tq_full[slot]), (uint32_t)((r / kTQ) & 1), abort_flag, err)) return -1;
+  const int tile = *reinterpret_cast<volatile int*>(&ctl.tq[slot]);
+  if constexpr (kCluster) mbar_arrive_cluster(empty_bars[slot]);
+  else mbar_arrive(smem_u32(&ctl.tq_empty[slot]));
+  return tile;
+}
+
+// The last CTA to exit zeroes the launch's counters (every other CTA has drawn its last ticket).
+__device__ __forceinline__ void tile_counter_exit(const Params& p) {
+  if (p.tile_counter == nullptr) return;
+  __threadfence();
+  if (atomicAdd(p.tile_counter + 1, 1u) == gridDim.x - 1u) {
+    p.tile_counter[0] = 0u;
+    p.tile_counter[1] = 0u;
+    __threadfence();
+  }
+}
 
 template <int TBM>
 __device__ __forceinline__ TileInfo decode(const Params& p, const SmemCtl& s, int tile) {

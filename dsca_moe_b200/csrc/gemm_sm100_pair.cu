@@ -109,6 +109,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(smem_u32(&ctl.tmem_full[a]), 1);
       mbar_init(smem_u32(&ctl.tmem_empty[a]), 8);  // 4 epilogue warps x 2 CTAs
     }
+    // the tile queue: the even CTA's producer publishes each tile id into both CTAs' queues;
+    // its readers (the even CTA's MMA thread and epilogue warps, the odd CTA's producer and
+    // epilogue warps) release a slot on the even CTA's tq_empty
+    for (int i = 0; i < kTQ; ++i) {
+      mbar_init(smem_u32(&ctl.tq_full[i]), 1);
+      mbar_init(smem_u32(&ctl.tq_empty[i]), 10);
+    }
     mbar_init(smem_u32(&ctl.mma_done), 1);
     ctl.abort_flag = 0;
     fence_mbar_init();
@@ -144,9 +151,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (p.pdl_wait_all) pdl_wait();  // GEMM1, which wrote the A rows, has completed
       bool seg0_ready = !p.pdl_seg0_wait;
       const uint64_t pol_first = l2_policy_evict_first(), pol_last = l2_policy_evict_last();
+      uint32_t tq_empty0[kTQ];
+      for (int i = 0; i < kTQ; ++i) tq_empty0[i] = mapa_shared(smem_u32(&ctl.tq_empty[i]), 0);
       for (int r = 0; ok; ++r) {
-        const int tile = sched_tile(r, unit, units);
-        if (tile >= total) break;
+        // the tile of round r: the even CTA draws it and publishes it to both CTAs' queues (the
+        // id into the odd CTA's queue by a remote store, ordered before the remote arrive)
+        int tile;
+        if (rank == 0) {
+          const int slot = r % kTQ;
+          if (!mbar_wait<true>(smem_u32(&ctl.tq_empty[slot]), (uint32_t)(((r / kTQ) & 1) ^ 1), abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          tile = ticket_tile(p, r, unit, units);
+          if (tile >= total) tile = -1;
+          *reinterpret_cast<volatile int*>(&ctl.tq[slot]) = tile;
+          st_shared_cluster_s32(mapa_shared(smem_u32(&ctl.tq[slot]), 1), tile);
+          mbar_arrive(smem_u32(&ctl.tq_full[slot]));
+          mbar_arrive_cluster(mapa_shared(smem_u32(&ctl.tq_full[slot]), 1));
+        } else {
+          tile = tq_take<true>(ctl, r, abort_flag, p.err, tq_empty0);
+          if (tile < 0 && *abort_flag) ok = false;
+        }
+        if (tile < 0) break;
         const TileInfo ti = decode<TBN>(p, ctl, tile);
         if (ti.seg == 0 && !seg0_ready) {
           pdl_wait();  // the preceding kernel (the permute) has written the routed rows
@@ -223,9 +250,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t ph = 0;
       int it = 0;
       bool ok = true;
+      uint32_t tq_empty0[kTQ];
+      for (int i = 0; i < kTQ; ++i) tq_empty0[i] = smem_u32(&ctl.tq_empty[i]);  // own CTA (rank 0)
       for (int r = 0; ok; ++r, ++it) {
-        const int tile = sched_tile(r, unit, units);
-        if (tile >= total) break;
+        const int tile = tq_take<true>(ctl, r, abort_flag, p.err, tq_empty0);
+        if (tile < 0) {
+          ok = *abort_flag == 0;
+          break;
+        }
         const TileInfo ti = decode<TBN>(p, ctl, tile);
         const bool full = !F8 && C::kGlu && ti.full;
         const uint32_t idesc = full ? idesc_bf16_f32(256, 256)
@@ -297,10 +329,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t empty_bar[2] = {mapa_shared(smem_u32(&ctl.tmem_empty[0]), 0),
                                    mapa_shared(smem_u32(&ctl.tmem_empty[1]), 0)};
     __nv_bfloat16* stg = stage_all + (warp - 2) * C::kStageElems;
+    uint32_t tq_empty0[kTQ];
+    for (int i = 0; i < kTQ; ++i) tq_empty0[i] = mapa_shared(smem_u32(&ctl.tq_empty[i]), 0);
     int it = 0;
     for (int r = 0;; ++r, ++it) {
-      const int tile = sched_tile(r, unit, units);
-      if (tile >= total) break;
+      int tile = 0;
+      if (lane == 0) tile = tq_take<true>(ctl, r, abort_flag, p.err, tq_empty0);
+      tile = __shfl_sync(0xffffffffu, tile, 0);
+      if (tile < 0) break;
       const TileInfo ti = decode<TBN>(p, ctl, tile);
       const Segment& sg = p.seg[ti.seg];
       const int acc = it % C::kAccBufs;
@@ -434,6 +470,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, kTmemCols);
   }
+  if (threadIdx.x == 0) tile_counter_exit(p);
   if (p.ep_signal != nullptr) ep::signal_when_grid_done(p.ep_signal, &p.ep_signal->return_done, ep::kReturn);
 }
 
@@ -540,6 +577,7 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
     gemm::Params p{};
     const int epi = f->act == DSCA_ACT_SWIGLU ? gemm::kEpiSwiGLU : gemm::kEpiReLU;
     p.epi = epi;
+    p.tile_counter = f->tile_counters;  // GEMM1: [0, 2)
     p.err = f->err;
     p.nseg = shared ? 2 : 1;
     // tile_rows 512 (SwiGLU): whole 256-token blocks as non-swapped tiles, the rest swap-AB
@@ -599,6 +637,7 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
     }
     gemm::Params p{};
     p.epi = gemm::kEpiStore;
+    p.tile_counter = f->tile_counters != nullptr ? f->tile_counters + 2 : nullptr;  // GEMM2: [2, 4)
     p.err = f->err;
     p.nseg = shared ? 2 : 1;
     // the longer K first; with the fused return (ep_ctx) the routed tiles first, so that their
@@ -691,6 +730,7 @@ int launch_grouped_ffn_f8_split(const dsca_ffn_args* f, int num_sms, cudaStream_
     gemm::Params p{};
     const int epi = glu ? gemm::kEpiSwiGLU : gemm::kEpiReLU;
     p.epi = epi;
+    p.tile_counter = f->tile_counters;  // GEMM1: [0, 2)
     p.err = f->err;
     p.nseg = shared ? 2 : 1;
     p.seg_first = 0;
@@ -753,6 +793,7 @@ int launch_grouped_ffn_f8_split(const dsca_ffn_args* f, int num_sms, cudaStream_
     }
     gemm::Params p{};
     p.epi = gemm::kEpiStore;
+    p.tile_counter = f->tile_counters != nullptr ? f->tile_counters + 2 : nullptr;  // GEMM2: [2, 4)
     p.err = f->err;
     p.nseg = shared ? 2 : 1;
     p.seg_first = (shared && f->shared_ip > f->ip) ? 1 : 0;  // the longer K first

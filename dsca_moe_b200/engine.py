@@ -403,6 +403,10 @@ class MoEEngine:
         # the QoS scores: first-choice counts accumulated by the router (zeroed again by the QoS
         # kernel) and the QoS kernel's own done counter
         self._first_counts = torch.zeros(self.E, dtype=torch.int32, device=self.device)
+        # grouped GEMM tiles handed out by atomic tickets (dsca_ffn_args.tile_counters; every
+        # launch leaves the four counters zeroed) instead of the static schedule
+        self.dynamic_tiles = True
+        self._tile_ctr = torch.zeros(4, dtype=torch.int32, device=self.device)
         self._qos_done = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._ws = {}
         self.last_plan = None
@@ -624,6 +628,7 @@ class MoEEngine:
         f.segments = segments
         # GEMM1 directly after the permute: its shared-expert tiles overlap the permute
         f.pdl_after_permute = int(after_permute and self.pdl)
+        f.tile_counters = _ptr(self._tile_ctr) if self.dynamic_tiles else None
         L.call("dsca_grouped_ffn", ctypes.byref(f), _stream())
 
     def _combine(self, ws, y, rows, after_ffn=False):

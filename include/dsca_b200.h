@@ -271,6 +271,11 @@ typedef struct {
   void* hsq;
   float* h_scale;
   float* hs_scale;
+  /* optional dynamic tile schedule: 4 zeroed uint32 (GEMM1 uses [0, 2), GEMM2 [2, 4)), left
+     zeroed by every launch.  Each CTA (pair) then takes its next tile from an atomic ticket when
+     it is ready for one, so tiles of different lengths spread by their actual durations; NULL =
+     the static schedule.  Calls that overlap on the GPU must not share them. */
+  uint32_t* tile_counters;
 } dsca_ffn_args;
 DSCA_API int dsca_grouped_ffn(const dsca_ffn_args* a, dsca_stream_t stream);
 
