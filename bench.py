@@ -90,9 +90,10 @@ def parse():
                     help="bf16 expert GEMM tiles: 0 = default per GEMM, 256 = CTA pairs (cta_group::2, "
                          "weights as M), 128 = one CTA per 128-token tile, 512 = CTA pairs with whole "
                          "256-token blocks of the SwiGLU GEMM1 non-swapped (tokens as M)")
-    ap.add_argument("--tile-order", type=int, choices=[0, 1], default=None,
-                    help="routed and shared tiles of one GEMM launch: 0 = one segment after the other, "
-                         "1 = interleaved (default: the engine's)")
+    ap.add_argument("--tile-order", type=int, choices=list(range(8)), default=None,
+                    help="bit 0: routed and shared tiles of one GEMM launch interleaved (else one segment "
+                         "after the other); bits 1 / 2: shared / routed tiles weight-block major "
+                         "(default: the engine's)")
     ap.add_argument("--cache-hints", type=int, choices=[0, 1], default=0,
                     help="L2 policies of the GEMM loads: 1 = routed weights evict-first, the rest evict-last")
     ap.add_argument("--router-tc", type=int, choices=[0, 1], default=None,
@@ -120,6 +121,8 @@ def parse():
     ap.add_argument("--fp8-form", choices=["split", "smem", "tmem"], default="split",
                     help="fp8 weights: split = e4m3 weights unconverted on kind::f8f6f4 MMAs against two-term "
                          "e4m3 tokens; smem / tmem = weights converted to f16 in shared / tensor memory")
+    ap.add_argument("--l2-ahead", type=int, default=None,
+                    help="routed GEMM tiles: L2 prefetch distance in K blocks (0 = off; default: the engine's)")
     ap.add_argument("--static-tiles", action="store_true",
                     help="grouped GEMM tiles by the static schedule instead of atomic tickets")
     ap.add_argument("--no-extra", action="store_true",
@@ -932,6 +935,8 @@ def run_ours(args, w, T):
     eng.pdl = not args.no_pdl
     if args.static_tiles:
         eng.dynamic_tiles = False
+    if args.l2_ahead is not None:
+        eng.l2_ahead = args.l2_ahead
     peaks = load_peaks()
     if args.once:
         eng.forward(x)
@@ -1277,11 +1282,14 @@ def run_ours(args, w, T):
                                256: "CTA-pair swap-AB tiles (256 channels x <=256 tokens)",
                                512: "CTA-pair tiles: SwiGLU GEMM1 whole 256-token blocks non-swapped "
                                     "(256 tokens x 128 channels), the rest swap-AB"}[args.tile_rows],
-                "tile_order": ["one segment after the other", "routed and shared tiles interleaved"][eng.tile_order],
+                "tile_order": (["one segment after the other", "routed and shared tiles interleaved"][eng.tile_order & 1]
+                               + ("; shared tiles weight-block major" if eng.tile_order & 2 else "")
+                               + ("; routed tiles weight-block major" if eng.tile_order & 4 else "")),
                 "fp8_form": ({"split": "e4m3 weights unconverted (kind::f8f6f4) x two-term e4m3 tokens",
                               "smem": "weights converted to f16 in shared memory",
                               "tmem": "weights converted to f16 in tensor memory"}[args.fp8_form] if args.fp8 else None),
                 "l2_hints": ["default", "routed weights evict-first, the rest evict-last"][args.cache_hints],
+                "l2_prefetch_k_blocks": eng.l2_ahead,
                 "qos_order": (eng.qos_order if world > 1 else None),
                 "router": ("tensor cores: exact int8 fixed-point products, one fused kernel"
                            if eng.router_tensor_cores else "CUDA cores: fp32 fma chains in the fixed chunk order")},

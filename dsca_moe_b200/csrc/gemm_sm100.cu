@@ -143,11 +143,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           seg0_ready = true;
         }
         const int kb_n = p.seg[ti.seg].k_blocks;
+        // routed tile: L2 prefetch of the boxes beyond the shared-memory stages, then one box
+        // l2_ahead K blocks ahead of every load
+        const int pf = ti.seg == 0 ? p.l2_ahead : 0;
+        for (int kb = kStages; kb < min(pf, kb_n); ++kb) {
+          tma_prefetch_l2_2d(mb, kb * C::kKE, ti.b_row0);
+          tma_prefetch_l2_2d(ma, kb * C::kKE, ti.row0);
+        }
         for (int kb = 0; kb < kb_n; ++kb) {
           if (!mbar_wait(smem_u32(&ctl.empty[s]), ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
           const uint32_t fb = smem_u32(&ctl.full[s]);
           mbar_arrive_expect_tx(fb, kStageBytes);
           const int kx = kb * C::kKE;
+          if (pf > 0 && kb + pf < kb_n && kb + pf >= kStages) {
+            tma_prefetch_l2_2d(mb, (kb + pf) * C::kKE, ti.b_row0);
+            tma_prefetch_l2_2d(ma, (kb + pf) * C::kKE, ti.row0);
+          }
           if (p.l2_hints) {
             tma_load_2d_hint(smem_a + s * kABytes, ma, fb, kx, ti.row0, pol_last);
             if constexpr (F8)  // the lo plane of the same token rows
@@ -458,8 +469,10 @@ int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t st
     p.pdl_seg0_wait = (f->pdl_after_permute && routed) ? 1 : 0;
     p.seg_first = (p.pdl_seg0_wait && shared) ? 1 : 0;
     // interleaved segments: two rounds of shared tiles first when the permute is still running
-    p.l2_hints = f->cache_hints;
-    p.interleave_lead = (shared && routed && f->tile_order == 1) ? (p.pdl_seg0_wait ? 2 * grid : 0) : -1;
+    p.l2_hints = f->cache_hints & 1;
+    p.l2_ahead = (f->cache_hints >> 8) & 0xff;
+    p.interleave_lead = (shared && routed && (f->tile_order & 1)) ? (p.pdl_seg0_wait ? 2 * grid : 0) : -1;
+    gemm::set_weight_major(p, f->tile_order);
     gemm::Segment& s0 = p.seg[0];
     s0.group_offsets = f->group_offsets;
     s0.group_weight = f->group_weight;
@@ -509,8 +522,10 @@ int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t st
     // the longer K first; with the fused return (ep_ctx) the routed tiles first, so that their
     // NVLink stores drain while the shared-expert tiles compute
     p.seg_first = (shared && f->shared_ip > f->ip && f->ep_ctx == nullptr) ? 1 : 0;
-    p.l2_hints = f->cache_hints;
-    p.interleave_lead = (shared && routed && f->tile_order == 1) ? 0 : -1;
+    p.l2_hints = f->cache_hints & 1;
+    p.l2_ahead = (f->cache_hints >> 8) & 0xff;
+    p.interleave_lead = (shared && routed && (f->tile_order & 1)) ? 0 : -1;
+    gemm::set_weight_major(p, f->tile_order);
     p.ep_signal = routed ? static_cast<ep::Ctx*>(f->ep_ctx) : nullptr;
     gemm::Segment& s0 = p.seg[0];
     s0.ep = static_cast<const ep::Ctx*>(f->ep_ctx);
@@ -589,7 +604,9 @@ int launch_gemm1_f8_single(const dsca_ffn_args* f, int num_sms, cudaStream_t str
   p.nseg = shared ? 2 : 1;
   p.seg_first = 0;
   p.interleave_lead = -1;
-  p.l2_hints = f->cache_hints;
+  gemm::set_weight_major(p, f->tile_order);
+  p.l2_hints = f->cache_hints & 1;
+    p.l2_ahead = (f->cache_hints >> 8) & 0xff;
   gemm::Segment& s0 = p.seg[0];
   s0.group_offsets = f->group_offsets;
   s0.group_weight = f->group_weight;

@@ -41,6 +41,10 @@ struct Segment {
   int t_lo;
   const float* t_scale;
   const float* w_scale;
+  // tile order inside a group: 0 = the weight blocks of one token block after another (token
+  // block major); 1 = the token blocks of one weight block after another (weight block major:
+  // a weight block is read by all its token blocks back to back, while it is in L2)
+  int wmajor;
 };
 
 struct Params {
@@ -64,6 +68,10 @@ struct Params {
   // L2 policies of the loads: 0 = default; 1 = routed experts' weights (segment 0, streamed from
   // DRAM and mostly read once) evict-first, shared-expert weights and token rows evict-last
   int l2_hints;
+  // routed tiles (segment 0): the producer prefetches into L2 the operand boxes this many K
+  // blocks ahead of its shared-memory loads (0 = off), so that a tile whose expert weights are
+  // not yet in L2 has more DRAM reads in flight than its shared-memory stages hold
+  int l2_ahead;
   // CTA-pair SwiGLU GEMM1 only: every whole 256-token block of a group is one non-swapped tile
   // (tokens as M = 256 over the pair, 128 channels' gate and up rows as N = 256, Segment::n_full
   // blocks), the remaining < 256 tokens swap-AB tiles as usual
@@ -105,8 +113,15 @@ __device__ __forceinline__ void decode_in_group(TileInfo& ti, int l, int rows, i
     return;
   }
   l -= nf;
-  const int m_blk = l / sg.n_tiles;
-  ti.n_blk = l - m_blk * sg.n_tiles;
+  int m_blk;
+  if (sg.wmajor) {
+    const int nm = max(1, (rows - 256 * full + TBM - 1) / TBM);
+    ti.n_blk = l / nm;
+    m_blk = l - ti.n_blk * nm;
+  } else {
+    m_blk = l / sg.n_tiles;
+    ti.n_blk = l - m_blk * sg.n_tiles;
+  }
   ti.full = 0;
   ti.row0 = row_base + 256 * full + m_blk * TBM;
   ti.rows_valid = min(TBM, rows - 256 * full - m_blk * TBM);
@@ -121,6 +136,13 @@ __device__ __forceinline__ __nv_bfloat16* ep_return_row(const ep::Ctx* c, int e,
       return reinterpret_cast<__nv_bfloat16*>(c->ret[src]) + (size_t)(c->ret_start[e][src] + r - cs) * ldc;
   }
   return nullptr;
+}
+
+// dsca_ffn_args::tile_order bits 1 and 2: weight-block-major order for the shared expert's
+// segment (1) and the routed groups (0)
+inline void set_weight_major(Params& p, int tile_order) {
+  p.seg[0].wmajor = (tile_order >> 2) & 1;
+  p.seg[1].wmajor = (tile_order >> 1) & 1;
 }
 
 constexpr int kTQ = 4;  // tile queue depth (tiles the producer may run ahead of the consumers)

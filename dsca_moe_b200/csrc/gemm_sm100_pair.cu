@@ -195,10 +195,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool full = !F8 && C::kGlu && ti.full;
         const int f_trow = ti.row0 + 128 * (int)rank, f_wrow = ti.b_row0 + 128 * (int)rank;
         constexpr uint32_t tx_full = 2u * (uint32_t)(C::kABytes + C::kA2Bytes);
+        // routed swap-AB tile: L2 prefetch of this CTA's boxes beyond the shared-memory stages,
+        // then one K block l2_ahead ahead of every load
+        const int pf = (ti.seg == 0 && !full) ? p.l2_ahead : 0;
+        auto prefetch_kb = [&](int k) {
+          tma_prefetch_l2_2d(mw, k * C::kKE, w_row);
+          if constexpr (C::kGlu) tma_prefetch_l2_2d(mw, k * C::kKE, w_row + 128);
+          tma_prefetch_l2_2d(mt, k * C::kKE, t_row);
+        };
+        for (int kb = S; kb < min(pf, kb_n); ++kb) prefetch_kb(kb);
         for (int kb = 0; kb < kb_n; ++kb) {
           if (!mbar_wait(smem_u32(&ctl.empty[s]), ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
           const uint32_t fb = smem_u32(&ctl.full[s]);
           const uint32_t fb0 = mapa_shared(fb, 0);  // the even CTA's full barrier
+          if (pf > 0 && kb + pf < kb_n && kb + pf >= S) prefetch_kb(kb + pf);
           // L2 policies (Params::l2_hints): routed weights evict-first, the rest evict-last
           const uint64_t wpol = ti.seg == 0 ? pol_first : pol_last;
           if (full) {
@@ -587,8 +597,10 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
     p.pdl_seg0_wait = (p.hybrid && f->pdl_after_permute && routed) ? 1 : 0;
     p.seg_first = (p.pdl_seg0_wait && shared) ? 1 : 0;
     // interleaved segments: one round of shared tiles first when the permute is still running
-    p.l2_hints = f->cache_hints;
-    p.interleave_lead = (shared && routed && f->tile_order == 1) ? (p.pdl_seg0_wait ? grid / 2 : 0) : -1;
+    p.l2_hints = f->cache_hints & 1;
+    p.l2_ahead = (f->cache_hints >> 8) & 0xff;
+    p.interleave_lead = (shared && routed && (f->tile_order & 1)) ? (p.pdl_seg0_wait ? grid / 2 : 0) : -1;
+    gemm::set_weight_major(p, f->tile_order);
     gemm::Segment& s0 = p.seg[0];
     s0.group_offsets = f->group_offsets;
     s0.group_weight = f->group_weight;
@@ -643,8 +655,10 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
     // the longer K first; with the fused return (ep_ctx) the routed tiles first, so that their
     // NVLink stores drain while the shared-expert tiles compute
     p.seg_first = (shared && f->shared_ip > f->ip && f->ep_ctx == nullptr) ? 1 : 0;
-    p.l2_hints = f->cache_hints;
-    p.interleave_lead = (shared && routed && f->tile_order == 1) ? 0 : -1;
+    p.l2_hints = f->cache_hints & 1;
+    p.l2_ahead = (f->cache_hints >> 8) & 0xff;
+    p.interleave_lead = (shared && routed && (f->tile_order & 1)) ? 0 : -1;
+    gemm::set_weight_major(p, f->tile_order);
     p.ep_signal = routed ? static_cast<ep::Ctx*>(f->ep_ctx) : nullptr;
     p.pdl_wait_all = (f->pdl_after_permute && f->ep_ctx == nullptr) ? 1 : 0;  // right after GEMM1
     p.hybrid = 0;
@@ -735,7 +749,9 @@ int launch_grouped_ffn_f8_split(const dsca_ffn_args* f, int num_sms, cudaStream_
     p.nseg = shared ? 2 : 1;
     p.seg_first = 0;
     p.interleave_lead = -1;
-    p.l2_hints = f->cache_hints;
+    gemm::set_weight_major(p, f->tile_order);
+    p.l2_hints = f->cache_hints & 1;
+    p.l2_ahead = (f->cache_hints >> 8) & 0xff;
     gemm::Segment& s0 = p.seg[0];
     s0.group_offsets = f->group_offsets;
     s0.group_weight = f->group_weight;
@@ -798,7 +814,9 @@ int launch_grouped_ffn_f8_split(const dsca_ffn_args* f, int num_sms, cudaStream_
     p.nseg = shared ? 2 : 1;
     p.seg_first = (shared && f->shared_ip > f->ip) ? 1 : 0;  // the longer K first
     p.interleave_lead = -1;
-    p.l2_hints = f->cache_hints;
+    gemm::set_weight_major(p, f->tile_order);
+    p.l2_hints = f->cache_hints & 1;
+    p.l2_ahead = (f->cache_hints >> 8) & 0xff;
     gemm::Segment& s0 = p.seg[0];
     s0.group_offsets = f->group_offsets;
     s0.group_weight = f->group_weight;

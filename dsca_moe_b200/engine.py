@@ -382,12 +382,15 @@ class MoEEngine:
         # 256-token blocks of the SwiGLU GEMM1 non-swapped; fp8 weights: 256 = converted into
         # tensor memory, else into shared memory
         self.tile_rows = 0
-        # routed and shared tiles of one launch: 0 = one segment after the other, 1 = interleaved
-        # (measured slower)
+        # dsca_ffn_args.tile_order: bit 0 = routed and shared tiles of one launch interleaved
+        # (else one segment after the other), bits 1 / 2 = shared / routed tiles weight-block major
         self.tile_order = 0
         # L2 policies of the GEMM loads (dsca_ffn_args.cache_hints): 0 = default, 1 = routed
         # weights evict-first, shared weights and token rows evict-last
         self.cache_hints = 0
+        # routed GEMM tiles: L2 prefetch of the operand boxes this many K blocks ahead of the
+        # shared-memory loads (dsca_ffn_args.cache_hints bits 8-15; 0 = off)
+        self.l2_ahead = 0
         # one GPU: GEMM1 launched as a programmatic dependent of the permute (shared-expert tiles
         # overlap it; the routed tiles wait for it on the device)
         self.pdl = True
@@ -622,7 +625,7 @@ class MoEEngine:
         f.err, f.num_ctas, f.phases = _ptr(self.err), self.num_ctas if num_ctas is None else num_ctas, phases
         f.tile_rows = self.tile_rows
         f.tile_order = self.tile_order
-        f.cache_hints = self.cache_hints
+        f.cache_hints = self.cache_hints | (self.l2_ahead << 8)
         f.group_order = _ptr(group_order)
         f.ep_ctx = _ptr(ep_ctx)
         f.segments = segments

@@ -248,15 +248,19 @@ typedef struct {
                                  QoS planner's order (dsca_ep_group_order); bf16 only, other dtypes
                                  run index order.  Only the order of the tiles changes, never a
                                  result */
-  int cache_hints;            /* bf16 and f8_split: 0 = default L2 policy for every load; 1 = the
-                                 routed experts' weights (streamed from DRAM, mostly read once)
-                                 loaded evict-first, the shared expert's weights and the token rows
-                                 evict-last */
-  int tile_order;             /* routed and shared expert in one launch (bf16): 0 = one segment's
-                                 tiles after the other's (the default; measured faster); 1 = their
-                                 tiles interleaved in proportion to their counts (after one round
-                                 of shared tiles when GEMM1 overlaps the permute), HBM-bound routed
-                                 tiles beside tensor-bound shared tiles */
+  int cache_hints;            /* bf16 and f8_split.  Bit 0: 0 = default L2 policy for every load;
+                                 1 = the routed experts' weights (streamed from DRAM, mostly read
+                                 once) loaded evict-first, the shared expert's weights and the
+                                 token rows evict-last.  Bits 8-15: L2 prefetch distance in K
+                                 blocks for the routed tiles' operands (0 = off) */
+  int tile_order;             /* bit 0, routed and shared expert in one launch (bf16): 0 = one
+                                 segment's tiles after the other's (the default); 1 = their tiles
+                                 interleaved in proportion to their counts (after one round of
+                                 shared tiles when GEMM1 overlaps the permute), HBM-bound routed
+                                 tiles beside tensor-bound shared tiles.  Bits 1 / 2: the shared
+                                 expert's / the routed groups' tiles weight-block major (every
+                                 token block of one weight block, then the next weight block)
+                                 instead of token-block major.  No bit changes a result. */
   /* dtype DSCA_F8E4M3 with f8_split = 1: the e4m3 weights go to the tensor cores as they are
      (tcgen05 kind::f8f6f4, CTA-pair tiles with the tokens as the MMA N), multiplied by tokens held
      as two e4m3 terms per value (dsca_split_rows): a [capacity, 2 * Kd] and xs [shared_rows,

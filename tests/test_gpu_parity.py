@@ -413,15 +413,17 @@ def test_single_cta_and_pair_tiles_agree(cuda, T, d, E, I, Is, k):
     for rows in (128, 256, 512):
         eng.tile_rows = rows
         got = []
-        # one segment after the other / routed and shared tiles interleaved, with and without the
-        # L2 eviction policies on the loads: the order of the tiles never changes a result
-        for order, hints in ((0, 0), (1, 0), (0, 1), (1, 1)):
-            eng.tile_order, eng.cache_hints = order, hints
+        # one segment after the other / routed and shared tiles interleaved, token- or
+        # weight-block-major inside a group, with and without the L2 eviction policies and L2
+        # prefetches: neither the order of the tiles nor the cache use changes a result
+        for order, hints, ahead in ((0, 0, 0), (1, 0, 0), (0, 1, 0), (1, 1, 0), (2, 0, 0), (3, 0, 8),
+                                    (6, 0, 12), (7, 1, 16)):
+            eng.tile_order, eng.cache_hints, eng.l2_ahead = order, hints, ahead
             r = eng.forward(xd)
             torch.cuda.synchronize()
             eng.check()
             got.append(r["out"].clone())
-        eng.tile_order, eng.cache_hints = 0, 0
+        eng.tile_order, eng.cache_hints, eng.l2_ahead = 0, 0, 0
         for g in got[1:]:
             assert torch.equal(got[0], g)
         outs.append(got[0].float().cpu().numpy())
