@@ -1279,7 +1279,8 @@ def run_ours(args, w, T):
                 "exchange": (f"{args.exchange} (return {args.ep_return})" if world > 1 else "none"),
                 "gemm_tiles": {0: "GEMM1 128-token single-CTA tiles, GEMM2 CTA-pair swap-AB tiles",
                                128: "128-token single-CTA tiles",
-                               256: "CTA-pair swap-AB tiles (256 channels x <=256 tokens)",
+                               256: "CTA-pair swap-AB tiles (SwiGLU GEMM1: 128 channels, gate and up halves per CTA, "
+                                    "x <=256 tokens; otherwise 256 weight rows x <=256 tokens)",
                                512: "CTA-pair tiles: SwiGLU GEMM1 whole 256-token blocks non-swapped "
                                     "(256 tokens x 128 channels), the rest swap-AB"}[args.tile_rows],
                 "tile_order": (["one segment after the other", "routed and shared tiles interleaved"][eng.tile_order & 1]

@@ -15,7 +15,9 @@ constexpr int kTmemCols = 512;
 constexpr int kMaxGroups = 256;
 constexpr int kMaxStages = 6;
 
-enum Epi { kEpiSwiGLU = 0, kEpiReLU = 1, kEpiStore = 2 };
+// kEpiSwiGLU2: SwiGLU on CTA pairs with the gate and the up rows of a CTA's 64 channels as one
+// 128-row M operand (one accumulator; the gate and up halves meet in shared memory)
+enum Epi { kEpiSwiGLU = 0, kEpiReLU = 1, kEpiStore = 2, kEpiSwiGLU2 = 3 };
 
 // One GEMM segment: the routed experts (row groups with device-side offsets) or the shared
 // expert (one group over all tokens).  "b" is the weight operand: [groups * b_rows_per_group, K].
@@ -156,6 +158,8 @@ struct SmemCtl {
   uint64_t tmem_full[2];
   uint64_t tmem_empty[2];
   uint64_t mma_done;
+  uint64_t xfull[2][2][2];   // kEpiSwiGLU2: exchange half [warp pair][buffer][sender] written
+  uint64_t xempty[2][2][2];  // ... and read by the other warp
   uint32_t tmem_base;
   int abort_flag;
   int total_tiles;

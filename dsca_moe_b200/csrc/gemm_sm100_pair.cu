@@ -43,14 +43,25 @@ namespace pair {
 // The epilogue multiplies by the weight row's scale and the token row's 1 / s.
 // F8 SwiGLU takes up to 256 tokens a tile (an expert's rows in one tile up to 256, so each weight
 // block is streamed once): its gate and up accumulators fill the 512 TMEM columns, one buffer.
+//
+// kEpiSwiGLU2 (bf16): a tile is the 128 channels of one packed 256-row block [128 gate | 128 up]
+// times up to 256 tokens.  CTA r loads gate rows 64 r + [0, 64) and the matching up rows as one
+// 128-row operand (two 64-row boxes), so one M256 MMA per K16 step fills a single accumulator
+// whose TMEM lanes 0-63 are gate and 64-127 up values of the same 64 channels: an SM streams 32
+// KB per K step (16 KB weights + 16 KB tokens) for the tensor work a 128 x 256 single-CTA tile
+// does with 48 KB.  The epilogue warps of lane quarters q and q + 2 hold the gate and the up
+// values of 32 channels; per chunk of 32 tokens each sends the other the values of the 16
+// tokens the other forms SiLU(g) * u for (16 x 32 fp32 each way, two buffers per warp pair,
+// mbarrier-paced), so both warps compute and store at once.
 template <int EPI, bool F8 = false>
 struct Cfg {
   static constexpr bool kGlu = EPI == kEpiSwiGLU;
+  static constexpr bool kG2 = EPI == kEpiSwiGLU2;
   static constexpr int TBN = (kGlu && !F8) ? 128 : 256;  // token rows per tile (MMA N)
   static constexpr int kAccBufs = (kGlu && F8) ? 1 : 2;  // accumulator buffers (256 columns each)
   static constexpr int kUpCol = kGlu ? TBN : 0;          // SwiGLU: the up accumulator's column
   static constexpr int S = F8 ? (kGlu ? 3 : 4) : (kGlu ? 5 : 6);  // stages
-  static constexpr int kWBox = 128;                       // weight rows per TMA box
+  static constexpr int kWBox = kG2 ? 64 : 128;            // weight rows per TMA box
   static constexpr int kTBox = TBN / 2;                   // token rows per TMA box (one per stage)
   static constexpr int kKE = F8 ? 128 : BK;               // K elements per stage (128 bytes a row)
   static constexpr int kABytes = 128 * 128;               // 16 KB
@@ -59,7 +70,8 @@ struct Cfg {
   static constexpr int kTBytes = (F8 ? 2 : 1) * kTPlane;
   static constexpr int kStageBytes = kABytes + kA2Bytes + kTBytes;
   static constexpr int kStageElems = 32 * 32;             // epilogue staging per warp, bf16
-  static constexpr int kSmemBytes = S * kStageBytes + 4 * kStageElems * 2 + 1024;
+  static constexpr int kXBytes = kG2 ? 2 * 2 * 32 * 32 * 4 : 0;  // gate / up exchange, fp32
+  static constexpr int kSmemBytes = S * kStageBytes + 4 * kStageElems * 2 + kXBytes + 1024;
 };
 
 // MMA N for a tile of `ntok` token rows: a multiple of 16 (each CTA holds N / 2 rows, a whole
@@ -92,6 +104,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t smem_a2 = smem_a + S * C::kABytes;
   const uint32_t smem_t = smem_a2 + S * C::kA2Bytes;
   __nv_bfloat16* stage_all = reinterpret_cast<__nv_bfloat16*>(smem + S * C::kStageBytes);
+  float* xbuf = reinterpret_cast<float*>(smem + S * C::kStageBytes + 4 * C::kStageElems * 2);
 
   const int warp = warp_id(), lane = lane_id();
   volatile int* abort_flag = &ctl.abort_flag;
@@ -117,6 +130,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(smem_u32(&ctl.tq_empty[i]), 10);
     }
     mbar_init(smem_u32(&ctl.mma_done), 1);
+    for (int i = 0; i < 2; ++i)
+      for (int b = 0; b < 2; ++b)
+        for (int d = 0; d < 2; ++d) {
+          mbar_init(smem_u32(&ctl.xfull[i][b][d]), 1);
+          mbar_init(smem_u32(&ctl.xempty[i][b][d]), 1);
+        }
     ctl.abort_flag = 0;
     fence_mbar_init();
   }
@@ -187,7 +206,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr uint32_t tx = 2u * (uint32_t)C::kStageBytes;
         // weight rows: SwiGLU packs 256-row blocks [128 gate | 128 up]; this CTA's 128 channels
         // are packed block 2 n_blk + rank
-        const int w_row = C::kGlu ? ti.b_row0 + ti.n_blk * BN + 256 * (int)rank : ti.b_row0 + 128 * (int)rank;
+        // kEpiSwiGLU2: gate rows 64 rank + [0, 64) of the tile's 256-row block (the up rows 128 further)
+        const int w_row = C::kGlu ? ti.b_row0 + ti.n_blk * BN + 256 * (int)rank
+                                  : ti.b_row0 + (C::kG2 ? 64 : 128) * (int)rank;
         const int t_row = ti.row0 + half * (int)rank;
         const int kb_n = p.seg[ti.seg].k_blocks;
         // hybrid full tile (SwiGLU): this CTA's 128 tokens (two 64-row token boxes into slot A)
@@ -200,7 +221,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int pf = (ti.seg == 0 && !full) ? p.l2_ahead : 0;
         auto prefetch_kb = [&](int k) {
           tma_prefetch_l2_2d(mw, k * C::kKE, w_row);
-          if constexpr (C::kGlu) tma_prefetch_l2_2d(mw, k * C::kKE, w_row + 128);
+          if constexpr (C::kGlu || C::kG2) tma_prefetch_l2_2d(mw, k * C::kKE, w_row + 128);
           tma_prefetch_l2_2d(mt, k * C::kKE, t_row);
         };
         for (int kb = S; kb < min(pf, kb_n); ++kb) prefetch_kb(kb);
@@ -228,6 +249,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_load_2d_pair_hint(smem_a + s * C::kABytes, mw, fb0, kb * C::kKE, w_row, wpol);
               if constexpr (C::kGlu)
                 tma_load_2d_pair_hint(smem_a2 + s * C::kA2Bytes, mw, fb0, kb * C::kKE, w_row + 128, wpol);
+              if constexpr (C::kG2)  // the up rows as the operand's rows 64-127
+                tma_load_2d_pair_hint(smem_a + s * C::kABytes + C::kABytes / 2, mw, fb0, kb * C::kKE, w_row + 128,
+                                      wpol);
               tma_load_2d_pair_hint(smem_t + s * C::kTBytes, mt, fb0, kb * C::kKE, t_row, pol_last);
               if constexpr (F8)  // the lo plane of the same token rows
                 tma_load_2d_pair_hint(smem_t + s * C::kTBytes + C::kTPlane, mt, fb0,
@@ -235,6 +259,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
               tma_load_2d_pair(smem_a + s * C::kABytes, mw, fb0, kb * C::kKE, w_row);
               if constexpr (C::kGlu) tma_load_2d_pair(smem_a2 + s * C::kA2Bytes, mw, fb0, kb * C::kKE, w_row + 128);
+              if constexpr (C::kG2)
+                tma_load_2d_pair(smem_a + s * C::kABytes + C::kABytes / 2, mw, fb0, kb * C::kKE, w_row + 128);
               tma_load_2d_pair(smem_t + s * C::kTBytes, mt, fb0, kb * C::kKE, t_row);
               if constexpr (F8)
                 tma_load_2d_pair(smem_t + s * C::kTBytes + C::kTPlane, mt, fb0, p.seg[ti.seg].t_lo + kb * C::kKE,
@@ -342,6 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t tq_empty0[kTQ];
     for (int i = 0; i < kTQ; ++i) tq_empty0[i] = mapa_shared(smem_u32(&ctl.tq_empty[i]), 0);
     int it = 0;
+    uint32_t xg = 0;  // kEpiSwiGLU2: exchange chunks so far (the same sequence in both warps of a pair)
     for (int r = 0;; ++r, ++it) {
       int tile = 0;
       if (lane == 0) tile = tq_take<true>(ctl, r, abort_flag, p.err, tq_empty0);
@@ -358,6 +385,63 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!w_ok) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * 256);
+      if constexpr (C::kG2) {
+        // lane quarters 0 / 1: gate values of channels 32 pr + lane (pr = q & 1) of this CTA's 64;
+        // quarters 2 / 3: their up values.  Chunk of 32 tokens: the gate warp forms SiLU(g) * u
+        // for tokens 0-15 and the up warp for tokens 16-31, each sending the other the 16 values
+        // it lacks, then stores its 16 tokens' 64-byte row pieces.
+        const int ntok = ti.rows_valid;
+        const int ncol = tile_n(ntok);
+        const int pr = q & 1;
+        const int me = q >> 1, other = me ^ 1;  // 0 = gate warp, 1 = up warp
+        const int keep = me * 16;  // this warp's tokens: chunk columns keep + [0, 16)
+        const int ch0 = ti.n_blk * 128 + 64 * (int)rank + 32 * pr;
+        bool x_ok = true;
+#pragma unroll 1
+        for (int c = 0; c < ncol; c += 32, ++xg) {
+          const uint32_t b = xg & 1u, use = xg >> 1;
+          float* xs = xbuf + ((pr * 2 + (int)b) * 2 + me) * 512;     // this warp's sent half
+          float* xr = xbuf + ((pr * 2 + (int)b) * 2 + other) * 512;  // the other warp's
+          uint32_t v[32];
+          tmem_ld32(taddr + c, v);
+          tmem_wait_ld();
+          // every lane waits: the other warp has read this buffer's previous use of our half
+          bool w = use == 0 || mbar_wait(smem_u32(&ctl.xempty[pr][b][me]), (use - 1u) & 1u, abort_flag, p.err);
+          if (!__all_sync(0xffffffffu, w)) { x_ok = false; break; }
+#pragma unroll
+          for (int j = 0; j < 16; ++j) xs[j * 32 + lane] = __uint_as_float(me ? v[j] : v[16 + j]);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&ctl.xfull[pr][b][me]));
+          w = mbar_wait(smem_u32(&ctl.xfull[pr][b][other]), use & 1u, abort_flag, p.err);
+          if (!__all_sync(0xffffffffu, w)) { x_ok = false; break; }
+          float o[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) o[j] = xr[j * 32 + lane];
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&ctl.xempty[pr][b][other]));
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float mine = __uint_as_float(me ? v[16 + j] : v[j]);
+            const float g = me ? o[j] : mine, up = me ? mine : o[j];
+            stg[j * 32 + lane] = __float2bfloat16_rn(silu(g) * up);
+          }
+          __syncwarp();
+#pragma unroll
+          for (int rr = 0; rr < 2; ++rr) {
+            const int jj = rr * 8 + (lane >> 2), piece = lane & 3;
+            const int t = c + keep + jj, col = ch0 + piece * 8;
+            if (t < ntok && col < sg.n_store)
+              *reinterpret_cast<uint4*>(sg.c + (size_t)(ti.row0 + t) * sg.ldc + col) =
+                  *reinterpret_cast<const uint4*>(stg + jj * 32 + piece * 8);
+          }
+          __syncwarp();
+        }
+        if (!x_ok) break;
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(empty_bar[acc]);
+        continue;
+      }
       if (!F8 && C::kGlu && ti.full) {
         // hybrid full tile: TMEM lane = this CTA's token 32 q + lane, columns 0-127 gate and
         // 128-255 up of channels 128 n_blk + [0, 128): each lane stores its row's 64-byte pieces
@@ -553,6 +637,7 @@ static int launch_pair_one(int epi, const CUtensorMap& w0, const CUtensorMap& t0
                            const CUtensorMap& t1, const gemm::Params& p, int grid, cudaStream_t stream) {
   switch (epi) {
     case gemm::kEpiSwiGLU: return launch_pair<gemm::kEpiSwiGLU>(w0, t0, w1, t1, p, grid, stream);
+    case gemm::kEpiSwiGLU2: return launch_pair<gemm::kEpiSwiGLU2>(w0, t0, w1, t1, p, grid, stream);
     case gemm::kEpiReLU: return launch_pair<gemm::kEpiReLU>(w0, t0, w1, t1, p, grid, stream);
     default: return launch_pair<gemm::kEpiStore>(w0, t0, w1, t1, p, grid, stream);
   }
@@ -573,8 +658,12 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
   if (phases & 1) {
     CUtensorMap w0, t0, w1, t1;
     const bool glu = f->act == DSCA_ACT_SWIGLU;
-    const uint32_t wbox = gemm::pair::Cfg<gemm::kEpiSwiGLU>::kWBox;
-    const uint32_t tbox = glu ? gemm::pair::Cfg<gemm::kEpiSwiGLU>::kTBox : gemm::pair::Cfg<gemm::kEpiReLU>::kTBox;
+    // tile_rows 256 (SwiGLU): 128 channels x <= 256 tokens, gate and up halves per CTA
+    // (kEpiSwiGLU2); 512: hybrid tiles on the two-accumulator form
+    const bool g2 = glu && f->tile_rows != 512;
+    const uint32_t wbox = g2 ? gemm::pair::Cfg<gemm::kEpiSwiGLU2>::kWBox : gemm::pair::Cfg<gemm::kEpiSwiGLU>::kWBox;
+    const uint32_t tbox = g2 ? gemm::pair::Cfg<gemm::kEpiSwiGLU2>::kTBox
+                             : glu ? gemm::pair::Cfg<gemm::kEpiSwiGLU>::kTBox : gemm::pair::Cfg<gemm::kEpiReLU>::kTBox;
     if ((rc = make_map_bf16(&w0, f->w1, (uint64_t)f->num_experts_w * f->n1p, (uint64_t)f->d, wbox))) return rc;
     if ((rc = make_map_bf16(&t0, f->a, (uint64_t)f->capacity, (uint64_t)f->d, tbox))) return rc;
     if (shared) {
@@ -585,16 +674,16 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
       t1 = t0;
     }
     gemm::Params p{};
-    const int epi = f->act == DSCA_ACT_SWIGLU ? gemm::kEpiSwiGLU : gemm::kEpiReLU;
+    const int epi = g2 ? gemm::kEpiSwiGLU2 : glu ? gemm::kEpiSwiGLU : gemm::kEpiReLU;
     p.epi = epi;
     p.tile_counter = f->tile_counters;  // GEMM1: [0, 2)
     p.err = f->err;
     p.nseg = shared ? 2 : 1;
     // tile_rows 512 (SwiGLU): whole 256-token blocks as non-swapped tiles, the rest swap-AB
     p.hybrid = (glu && f->tile_rows == 512) ? 1 : 0;
-    // equal K (the model width) in both segments; right after the permute (one GPU, hybrid
-    // tiles) the shared-expert tiles go first and overlap it (programmatic dependent launch)
-    p.pdl_seg0_wait = (p.hybrid && f->pdl_after_permute && routed) ? 1 : 0;
+    // equal K (the model width) in both segments; right after the permute (SwiGLU) the
+    // shared-expert tiles go first and overlap it (programmatic dependent launch)
+    p.pdl_seg0_wait = ((p.hybrid || g2) && f->pdl_after_permute && routed) ? 1 : 0;
     p.seg_first = (p.pdl_seg0_wait && shared) ? 1 : 0;
     // interleaved segments: one round of shared tiles first when the permute is still running
     p.l2_hints = f->cache_hints & 1;
@@ -607,8 +696,9 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
     s0.group_order = f->group_order;
     s0.ngroups = routed ? f->num_groups : 0;
     s0.rows = 0;
-    // SwiGLU: a tile covers 256 output channels (gate and up rows of them); others 256 rows
-    s0.n_tiles = glu ? (f->ip + gemm::BN - 1) / gemm::BN : f->n1p / gemm::BN;
+    // SwiGLU: a tile covers 256 output channels (gate and up rows of them; kEpiSwiGLU2: 128,
+    // one packed 256-row block); others 256 rows
+    s0.n_tiles = (glu && !g2) ? (f->ip + gemm::BN - 1) / gemm::BN : f->n1p / gemm::BN;
     s0.n_full = glu ? f->ip / 128 : 0;
     s0.b_rows_per_group = f->n1p;
     s0.k_blocks = (f->d + gemm::BK - 1) / gemm::BK;
@@ -622,7 +712,7 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
       s1.group_weight = nullptr;
       s1.ngroups = 1;
       s1.rows = f->shared_rows;
-      s1.n_tiles = glu ? (f->shared_ip + gemm::BN - 1) / gemm::BN : f->shared_n1p / gemm::BN;
+      s1.n_tiles = (glu && !g2) ? (f->shared_ip + gemm::BN - 1) / gemm::BN : f->shared_n1p / gemm::BN;
       s1.n_full = glu ? f->shared_ip / 128 : 0;
       s1.b_rows_per_group = f->shared_n1p;
       s1.k_blocks = (f->d + gemm::BK - 1) / gemm::BK;

@@ -437,7 +437,9 @@ def test_single_cta_and_pair_tiles_agree(cuda, T, d, E, I, Is, k):
 def test_hybrid_pair_tiles_full_size(cuda):
     """Qwen1.5-MoE-A2.7B block, 4096 tokens (Zipf 1.5: the hot expert spans several whole
     256-token blocks), hybrid CTA-pair GEMM1 tiles: every token within 2e-2 of the fp32 torch
-    restatement, and equal to the single-CTA tiles' output within bf16 rounding."""
+    restatement, and equal to the single-CTA tiles' output within bf16 rounding; the CTA-pair
+    swap-AB tiles with gate and up halves per CTA (tile_rows 256) equal the single-CTA tiles'
+    output exactly."""
     from dsca_moe_b200 import _lib as L
     from dsca_moe_b200.engine import MoEEngine, pack_swiglu
 
@@ -452,13 +454,14 @@ def test_hybrid_pair_tiles_full_size(cuda):
                     shared_gate_weight=_t(sgw, torch.bfloat16, cuda))
     xd = _t(x, torch.bfloat16, cuda)
     outs = {}
-    for rows in (128, 512, 512):
+    for rows in (128, 256, 512, 512):
         eng.tile_rows = rows
         r = eng.forward(xd)
         torch.cuda.synchronize()
         eng.check()
         outs.setdefault(rows, []).append(r["out"].clone())
     assert torch.equal(outs[512][0], outs[512][1])
+    assert torch.equal(outs[256][0], outs[128][0])
     ref = torch_ref.qwen_block_fp32(xd, r["topk_ids"], r["topk_w"], w, _t(sgw, torch.bfloat16, cuda))
     assert torch_ref.max_rel_err(outs[512][0], ref) < BF16_TOL
     assert torch_ref.max_rel_err(outs[512][0], outs[128][0]) < 1e-2
