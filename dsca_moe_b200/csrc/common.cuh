@@ -248,6 +248,25 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
 __device__ __forceinline__ void st_shared_cluster_s32(uint32_t addr_cluster, int v) {
   asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(addr_cluster), "r"(v) : "memory");
 }
+// Arrive on a barrier by its shared::cluster address (a peer CTA's, or this CTA's) with the
+// default semantics (release at CTA scope): a consumer handing back a buffer it has finished
+// reading.  The .release.cluster form, issued by a thread with asynchronous tensor-core or bulk
+// copies in flight, stalled that thread for about a microsecond per arrive.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+// Arrive on a peer CTA's barrier expecting `bytes` of asynchronous stores (st_async_s32).
+__device__ __forceinline__ void mbar_arrive_expect_tx_remote(uint32_t bar_cluster, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cluster.b64 _, [%0], %1;" ::"r"(bar_cluster), "r"(bytes)
+               : "memory");
+}
+// 4-byte store into a peer CTA's shared memory that completes its bytes on the peer's barrier:
+// a reader that waits for the barrier's phase sees the value.
+__device__ __forceinline__ void st_async_s32(uint32_t addr_cluster, int v, uint32_t bar_cluster) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.s32 [%0], %1, [%2];" ::"r"(addr_cluster),
+               "r"(v), "r"(bar_cluster)
+               : "memory");
+}
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
 }

@@ -123,18 +123,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       bool seg0_ready = !p.pdl_seg0_wait;
       const uint64_t pol_first = l2_policy_evict_first(), pol_last = l2_policy_evict_last();
-      for (int r = 0; ok; ++r) {
-        // the tile of round r: drawn (static or ticket) and published to the MMA and epilogue
+      // the tile of round r: drawn (static or ticket) and published to the MMA and epilogue
+      // warps; -1 past the last tile, -2 when the wait for a free queue slot gave up
+      auto publish = [&](int r) -> int {
         const int slot = r % kTQ;
-        if (!mbar_wait(smem_u32(&ctl.tq_empty[slot]), (uint32_t)(((r / kTQ) & 1) ^ 1), abort_flag, p.err)) {
-          ok = false;
-          break;
-        }
+        if (!mbar_wait(smem_u32(&ctl.tq_empty[slot]), (uint32_t)(((r / kTQ) & 1) ^ 1), abort_flag, p.err))
+          return -2;
         int tile = ticket_tile(p, r, (int)blockIdx.x, (int)gridDim.x);
         if (tile >= total) tile = -1;
         *reinterpret_cast<volatile int*>(&ctl.tq[slot]) = tile;
         mbar_arrive(smem_u32(&ctl.tq_full[slot]));
+        return tile;
+      };
+      int next = publish(0);
+      for (int r = 0; ok; ++r) {
+        if (next == -2) {
+          ok = false;
+          break;
+        }
+        const int tile = next;
         if (tile < 0) break;
+        // the next round's tile is drawn one tile ahead: the ticket's latency overlaps this
+        // tile's loads instead of delaying the next tile's first stage
+        next = publish(r + 1);
         const TileInfo ti = decode<BM>(p, ctl, tile);
         const CUtensorMap* ma = ti.seg == 0 ? &tmA0 : &tmA1;
         const CUtensorMap* mb = ti.seg == 0 ? &tmB0 : &tmB1;

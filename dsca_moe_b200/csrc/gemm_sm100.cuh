@@ -251,7 +251,7 @@ __device__ __forceinline__ int tq_take(SmemCtl& ctl, int r, volatile int* abort_
   const int slot = r % kTQ;
   if (!mbar_wait<kCluster>(smem_u32(&ctl.tq_full[slot]), (uint32_t)((r / kTQ) & 1), abort_flag, err)) return -1;
   const int tile = *reinterpret_cast<volatile int*>(&ctl.tq[slot]);
-  if constexpr (kCluster) mbar_arrive_cluster(empty_bars[slot]);
+  if constexpr (kCluster) mbar_arrive_remote(empty_bars[slot]);
   else mbar_arrive(smem_u32(&ctl.tq_empty[slot]));
   return tile;
 }

@@ -172,22 +172,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t pol_first = l2_policy_evict_first(), pol_last = l2_policy_evict_last();
       uint32_t tq_empty0[kTQ];
       for (int i = 0; i < kTQ; ++i) tq_empty0[i] = mapa_shared(smem_u32(&ctl.tq_empty[i]), 0);
+      // the tile of round r: the even CTA draws it and publishes it to both CTAs' queues (the id
+      // into the odd CTA's queue by an asynchronous store that completes on its barrier); -1
+      // past the last tile, -2 when the wait for a free queue slot gave up
+      auto publish = [&](int r) -> int {
+        const int slot = r % kTQ;
+        if (!mbar_wait<true>(smem_u32(&ctl.tq_empty[slot]), (uint32_t)(((r / kTQ) & 1) ^ 1), abort_flag, p.err))
+          return -2;
+        int tile = ticket_tile(p, r, unit, units);
+        if (tile >= total) tile = -1;
+        *reinterpret_cast<volatile int*>(&ctl.tq[slot]) = tile;
+        mbar_arrive(smem_u32(&ctl.tq_full[slot]));
+        const uint32_t rbar = mapa_shared(smem_u32(&ctl.tq_full[slot]), 1);
+        mbar_arrive_expect_tx_remote(rbar, 4u);
+        st_async_s32(mapa_shared(smem_u32(&ctl.tq[slot]), 1), tile, rbar);
+        return tile;
+      };
+      int next = rank == 0 ? publish(0) : 0;
       for (int r = 0; ok; ++r) {
-        // the tile of round r: the even CTA draws it and publishes it to both CTAs' queues (the
-        // id into the odd CTA's queue by a remote store, ordered before the remote arrive)
         int tile;
         if (rank == 0) {
-          const int slot = r % kTQ;
-          if (!mbar_wait<true>(smem_u32(&ctl.tq_empty[slot]), (uint32_t)(((r / kTQ) & 1) ^ 1), abort_flag, p.err)) {
+          if (next == -2) {
             ok = false;
             break;
           }
-          tile = ticket_tile(p, r, unit, units);
-          if (tile >= total) tile = -1;
-          *reinterpret_cast<volatile int*>(&ctl.tq[slot]) = tile;
-          st_shared_cluster_s32(mapa_shared(smem_u32(&ctl.tq[slot]), 1), tile);
-          mbar_arrive(smem_u32(&ctl.tq_full[slot]));
-          mbar_arrive_cluster(mapa_shared(smem_u32(&ctl.tq_full[slot]), 1));
+          tile = next;
+          // the next round's tile is drawn one tile ahead (its ticket latency overlaps this
+          // tile's loads)
+          if (tile >= 0) next = publish(r + 1);
         } else {
           tile = tq_take<true>(ctl, r, abort_flag, p.err, tq_empty0);
           if (tile < 0 && *abort_flag) ok = false;
@@ -286,10 +298,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t ph = 0;
       int it = 0;
       bool ok = true;
-      uint32_t tq_empty0[kTQ];
-      for (int i = 0; i < kTQ; ++i) tq_empty0[i] = smem_u32(&ctl.tq_empty[i]);  // own CTA (rank 0)
       for (int r = 0; ok; ++r, ++it) {
-        const int tile = tq_take<true>(ctl, r, abort_flag, p.err, tq_empty0);
+        const int tile = tq_take<false>(ctl, r, abort_flag, p.err, nullptr);
         if (tile < 0) {
           ok = *abort_flag == 0;
           break;
@@ -371,7 +381,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t xg = 0;  // kEpiSwiGLU2: exchange chunks so far (the same sequence in both warps of a pair)
     for (int r = 0;; ++r, ++it) {
       int tile = 0;
-      if (lane == 0) tile = tq_take<true>(ctl, r, abort_flag, p.err, tq_empty0);
+      if (lane == 0)
+        tile = rank == 0 ? tq_take<false>(ctl, r, abort_flag, p.err, nullptr)
+                         : tq_take<true>(ctl, r, abort_flag, p.err, tq_empty0);
       tile = __shfl_sync(0xffffffffu, tile, 0);
       if (tile < 0) break;
       const TileInfo ti = decode<TBN>(p, ctl, tile);
@@ -439,7 +451,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!x_ok) break;
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(empty_bar[acc]);
+        if (lane == 0) mbar_arrive_remote(empty_bar[acc]);
         continue;
       }
       if (!F8 && C::kGlu && ti.full) {
@@ -470,7 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(empty_bar[acc]);
+        if (lane == 0) mbar_arrive_remote(empty_bar[acc]);
         continue;
       }
       const int ntok = ti.rows_valid;
@@ -548,7 +560,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // every lane's TMEM reads are complete: the warp releases the accumulator once
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(empty_bar[acc]);
+      if (lane == 0) mbar_arrive_remote(empty_bar[acc]);
     }
   }
 
