@@ -345,6 +345,15 @@ __device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t adesc, u
 }
 // arrive on the mbarrier at shared::cluster address `bar_cluster` (either CTA of the pair)
 // once every previously issued tcgen05 op of this thread completes
+// One commit of the pair's tensor-core work arriving on the barrier at this shared offset in
+// both CTAs of the pair (CTA mask 0b11): the empty / accumulator-full barriers of a K stage or
+// tile, one instruction instead of one commit per CTA.
+__device__ __forceinline__ void umma_commit_pair_both(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"((unsigned short)3)
+      : "memory");
+}
 __device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                    bar_cluster)

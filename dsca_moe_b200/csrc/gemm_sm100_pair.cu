@@ -354,14 +354,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           const uint32_t eb = smem_u32(&ctl.empty[s]);
-          umma_commit_pair(mapa_shared(eb, 0));
-          umma_commit_pair(mapa_shared(eb, 1));
+          umma_commit_pair_both(eb);
           if (++s == S) { s = 0; ph ^= 1u; }
         }
         if (!ok) break;
         const uint32_t fb = smem_u32(&ctl.tmem_full[acc]);
-        umma_commit_pair(mapa_shared(fb, 0));
-        umma_commit_pair(mapa_shared(fb, 1));
+        umma_commit_pair_both(fb);
       }
       if (!ok) {
         // aborting: wait until every MMA this thread issued has completed before TMEM is freed
