@@ -123,6 +123,8 @@ def parse():
                          "e4m3 tokens; smem / tmem = weights converted to f16 in shared / tensor memory")
     ap.add_argument("--l2-ahead", type=int, default=None,
                     help="routed GEMM tiles: L2 prefetch distance in K blocks (0 = off; default: the engine's)")
+    ap.add_argument("--no-handoff", action="store_true",
+                    help="GEMM2's shared-expert tiles wait for all of GEMM1 (no shared-expert handoff)")
     ap.add_argument("--static-tiles", action="store_true",
                     help="grouped GEMM tiles by the static schedule instead of atomic tickets")
     ap.add_argument("--no-extra", action="store_true",
@@ -935,6 +937,8 @@ def run_ours(args, w, T):
     eng.pdl = not args.no_pdl
     if args.static_tiles:
         eng.dynamic_tiles = False
+    if args.no_handoff:
+        eng.shared_handoff = False
     if args.l2_ahead is not None:
         eng.l2_ahead = args.l2_ahead
     peaks = load_peaks()

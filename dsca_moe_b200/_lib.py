@@ -63,7 +63,7 @@ class FfnArgs(ctypes.Structure):
                 ("w1_scale", _vp), ("w2_scale", _vp), ("ws1_scale", _vp), ("ws2_scale", _vp),
                 ("tile_rows", _i), ("pdl_after_permute", _i), ("group_order", _vp), ("cache_hints", _i), ("tile_order", _i),
                 ("f8_split", _i), ("a_scale", _vp), ("xs_scale", _vp), ("hq", _vp), ("hsq", _vp), ("h_scale", _vp),
-                ("hs_scale", _vp), ("tile_counters", _vp)]
+                ("hs_scale", _vp), ("tile_counters", _vp), ("shared_handoff", _i)]
 
 
 MAX_GPUS = 8

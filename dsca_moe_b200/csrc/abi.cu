@@ -162,6 +162,7 @@ int dsca_split_rows(const dsca_split_args* a, dsca_stream_t stream) {
 }
 
 int dsca_grouped_ffn(const dsca_ffn_args* f, dsca_stream_t stream) {
+  if (f != nullptr && f->shared_handoff != 0 && f->shared_handoff != 1) return DSCA_ERR_BAD_ARG;
   if (f == nullptr || f->a == nullptr || f->w1 == nullptr || f->w2 == nullptr || f->h == nullptr ||
       f->y == nullptr || f->group_offsets == nullptr)
     return DSCA_ERR_BAD_ARG;

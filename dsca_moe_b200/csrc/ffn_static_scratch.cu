@@ -97,6 +97,7 @@ extern "C" int dsca_grouped_ffn_static_scratch(const dsca_ffn_args* a, dsca_stre
       a->group_offsets == nullptr)
     return DSCA_ERR_BAD_ARG;
   if (a->h != nullptr || a->hs != nullptr) return DSCA_ERR_BAD_ARG;  // the scratch is internal
+  if (a->shared_handoff != 0 && a->shared_handoff != 1) return DSCA_ERR_BAD_ARG;
   if (a->num_groups <= 0 || a->num_groups > 256 || a->capacity < 0 || a->d <= 0 || a->num_experts_w <= 0)
     return a->num_groups > 256 ? DSCA_ERR_CAPACITY : DSCA_ERR_BAD_ARG;
   if (a->act != DSCA_ACT_RELU && a->act != DSCA_ACT_SWIGLU) return DSCA_ERR_BAD_ARG;

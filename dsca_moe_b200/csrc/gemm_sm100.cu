@@ -344,6 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(smem_u32(&ctl.tmem_empty[acc]));
+      if (p.seg1_done != nullptr && ti.seg == 1) seg1_tile_stored(p, ctl, lane, 4u);
     }
   }
 
@@ -438,6 +439,12 @@ int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t st
     const bool glu = f->act == DSCA_ACT_SWIGLU;
     dsca_ffn_args g = *f;
     int rc;
+    // shared-expert handoff between the two launches (see dsca_ffn_args::shared_handoff); 2
+    // marks it as arranged here for the two launches below
+    const int segs = f->segments == 0 ? 3 : f->segments;
+    const bool handoff = f->shared_handoff == 1 && glu && phases_all == 3 && f->tile_counters != nullptr &&
+                         f->pdl_after_permute && f->ep_ctx == nullptr && f->shared_rows > 0 && segs == 3;
+    g.shared_handoff = handoff ? 2 : 0;
     if (phases_all & 1) {
       g.phases = 1;
       g.tile_rows = glu ? 128 : 256;
@@ -473,6 +480,7 @@ int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t st
     const int epi = f->act == DSCA_ACT_SWIGLU ? gemm::kEpiSwiGLU : gemm::kEpiReLU;
     p.epi = epi;
     p.tile_counter = f->tile_counters;  // GEMM1: [0, 2)
+    p.seg1_done = (f->shared_handoff == 2 && shared) ? f->tile_counters + 4 : nullptr;  // [4, 6)
     p.err = f->err;
     p.nseg = shared ? 2 : 1;
     // equal K (the model width) in both segments; after a permute launched just before, the

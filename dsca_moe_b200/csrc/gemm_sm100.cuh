@@ -81,6 +81,12 @@ struct Params {
   // dynamic tile schedule: [0] the launch's tile ticket counter, [1] its exit counter (both zero
   // at launch; the last CTA to exit zeroes them), or null = the static boustrophedon schedule
   uint32_t* tile_counter;
+  // shared-expert handoff (dsca_ffn_args::shared_handoff): GEMM1 counts its epilogue warps'
+  // finished shared-expert tiles in seg1_done[0] and sets seg1_done[1] when all are stored;
+  // GEMM2 starts its shared-expert tiles once seg1_flag[0] is set (and zeroes both words when
+  // its last CTA exits).  Null = off.
+  uint32_t* seg1_done;
+  uint32_t* seg1_flag;
 };
 
 // A tile: token rows [row0, row0 + rows_valid) of group `group`, weight rows [b_row0, b_row0 + 256)
@@ -256,15 +262,57 @@ __device__ __forceinline__ int tq_take(SmemCtl& ctl, int r, volatile int* abort_
   return tile;
 }
 
-// The last CTA to exit zeroes the launch's counters (every other CTA has drawn its last ticket).
+// The last CTA to exit zeroes the launch's counters (every other CTA has drawn its last ticket),
+// and, in GEMM2, the shared-expert handoff words (every GEMM2 CTA waited for GEMM1's completion
+// before exiting, and GEMM1 touches them no more once the flag is set).
 __device__ __forceinline__ void tile_counter_exit(const Params& p) {
   if (p.tile_counter == nullptr) return;
   __threadfence();
   if (atomicAdd(p.tile_counter + 1, 1u) == gridDim.x - 1u) {
     p.tile_counter[0] = 0u;
     p.tile_counter[1] = 0u;
+    if (p.seg1_flag != nullptr) {
+      p.seg1_flag[-1] = 0u;
+      p.seg1_flag[0] = 0u;
+    }
     __threadfence();
   }
+}
+
+// GEMM1 epilogue warp, after storing its part of a shared-expert tile: count it; the warp that
+// completes the count (warps_per_tile x the segment's tiles) raises the flag.  Every lane fences
+// its own stores before the warp's count.
+__device__ __forceinline__ void seg1_tile_stored(const Params& p, const SmemCtl& s, int lane,
+                                                 unsigned warps_per_tile) {
+  __threadfence();
+  __syncwarp();
+  if (lane == 0) {
+    const unsigned old = atomicAdd(p.seg1_done, 1u);
+    if (old + 1u == warps_per_tile * (unsigned)s.seg1_tiles) {
+      __threadfence();
+      atomicExch(p.seg1_done + 1, 1u);
+    }
+  }
+}
+
+// GEMM2 producer: bounded wait for the shared-expert handoff flag, then make GEMM1's stores
+// visible to this thread's bulk-tensor (async proxy) loads.
+__device__ __forceinline__ bool wait_seg1_flag(const Params& p, volatile int* abort_flag) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 0;; ++it) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p.seg1_flag) : "memory");
+    if (v != 0u) break;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      record_error(p.err, kErrWaitTimeout);
+      *abort_flag = 1;
+      return false;
+    }
+    __nanosleep(200);
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
 }
 
 template <int TBM>

@@ -167,7 +167,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       int pending_phase[S];
       for (int i = 0; i < S; ++i) pending_phase[i] = -1;
       bool ok = true;
-      if (p.pdl_wait_all) pdl_wait();  // GEMM1, which wrote the A rows, has completed
+      // GEMM2 after GEMM1: griddepcontrol.wait (GEMM1 has completed) before the first load, or,
+      // with the shared-expert handoff, before the first routed tile's load and the handoff
+      // flag before the first shared-expert tile's
+      bool all_ready = !p.pdl_wait_all;
+      if (!all_ready && p.seg1_flag == nullptr) {
+        pdl_wait();
+        all_ready = true;
+      }
+      bool seg1_ready = all_ready;
       bool seg0_ready = !p.pdl_seg0_wait;
       const uint64_t pol_first = l2_policy_evict_first(), pol_last = l2_policy_evict_last();
       uint32_t tq_empty0[kTQ];
@@ -209,6 +217,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ti.seg == 0 && !seg0_ready) {
           pdl_wait();  // the preceding kernel (the permute) has written the routed rows
           seg0_ready = true;
+        }
+        if (!all_ready && ti.seg == 0) {
+          pdl_wait();  // GEMM1 has completed
+          all_ready = seg1_ready = true;
+        }
+        if (!seg1_ready && ti.seg == 1) {
+          if (!wait_seg1_flag(p, abort_flag)) {
+            ok = false;
+            break;
+          }
+          seg1_ready = true;
         }
         const CUtensorMap* mw = ti.seg == 0 ? &tmW0 : &tmW1;
         const CUtensorMap* mt = ti.seg == 0 ? &tmT0 : &tmT1;
@@ -283,6 +302,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (++s == S) { s = 0; ph ^= 1u; }
         }
       }
+      // every CTA completes only after GEMM1 (a CTA that ran only shared-expert tiles under the
+      // handoff has not waited for it yet), so later work ordered after GEMM2 is after GEMM1 too
+      if (!all_ready) pdl_wait();
       if (!ok && rank == 0) {
         // drain: the last armed phase of every stage must complete before the CTA exits (this
         // also covers the odd CTA's loads, which complete on these barriers)
@@ -761,6 +783,7 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
     gemm::set_weight_major(p, f->tile_order);
     p.ep_signal = routed ? static_cast<ep::Ctx*>(f->ep_ctx) : nullptr;
     p.pdl_wait_all = (f->pdl_after_permute && f->ep_ctx == nullptr) ? 1 : 0;  // right after GEMM1
+    p.seg1_flag = (p.pdl_wait_all && f->shared_handoff == 2 && shared) ? f->tile_counters + 5 : nullptr;
     p.hybrid = 0;
     gemm::Segment& s0 = p.seg[0];
     s0.ep = static_cast<const ep::Ctx*>(f->ep_ctx);

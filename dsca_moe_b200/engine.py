@@ -406,10 +406,13 @@ class MoEEngine:
         # the QoS scores: first-choice counts accumulated by the router (zeroed again by the QoS
         # kernel) and the QoS kernel's own done counter
         self._first_counts = torch.zeros(self.E, dtype=torch.int32, device=self.device)
-        # grouped GEMM tiles handed out by atomic tickets (dsca_ffn_args.tile_counters; every
-        # launch leaves the four counters zeroed) instead of the static schedule
+        # grouped GEMM tiles handed out by atomic tickets (dsca_ffn_args.tile_counters, 8 words;
+        # every call leaves them zeroed) instead of the static schedule
         self.dynamic_tiles = True
-        self._tile_ctr = torch.zeros(4, dtype=torch.int32, device=self.device)
+        self._tile_ctr = torch.zeros(8, dtype=torch.int32, device=self.device)
+        # GEMM2's shared-expert tiles start when GEMM1's are stored (dsca_ffn_args.shared_handoff;
+        # one GPU, dynamic tiles)
+        self.shared_handoff = True
         self._qos_done = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._ws = {}
         self.last_plan = None
@@ -632,6 +635,7 @@ class MoEEngine:
         # GEMM1 directly after the permute: its shared-expert tiles overlap the permute
         f.pdl_after_permute = int(after_permute and self.pdl)
         f.tile_counters = _ptr(self._tile_ctr) if self.dynamic_tiles else None
+        f.shared_handoff = int(self.shared_handoff and self.dynamic_tiles)
         L.call("dsca_grouped_ffn", ctypes.byref(f), _stream())
 
     def _combine(self, ws, y, rows, after_ffn=False):

@@ -275,11 +275,17 @@ typedef struct {
   void* hsq;
   float* h_scale;
   float* hs_scale;
-  /* optional dynamic tile schedule: 4 zeroed uint32 (GEMM1 uses [0, 2), GEMM2 [2, 4)), left
-     zeroed by every launch.  Each CTA (pair) then takes its next tile from an atomic ticket when
-     it is ready for one, so tiles of different lengths spread by their actual durations; NULL =
-     the static schedule.  Calls that overlap on the GPU must not share them. */
+  /* optional dynamic tile schedule: 8 zeroed uint32 (GEMM1 uses [0, 2), GEMM2 [2, 4), the
+     shared-expert handoff [4, 6)), left zeroed by every call.  Each CTA (pair) then takes its next
+     tile from an atomic ticket when it is ready for one, so tiles of different lengths spread by
+     their actual durations; NULL = the static schedule.  Calls that overlap on the GPU must not
+     share them. */
   uint32_t* tile_counters;
+  /* 1: with tile_counters, both phases in this call, pdl_after_permute, bf16 SwiGLU in the
+     default tile form and a shared expert, GEMM1 raises a flag once its shared-expert tiles are
+     stored and GEMM2's shared-expert tiles start on it instead of after all of GEMM1 (GEMM2's
+     CTAs take the SMs GEMM1's CTAs leave); otherwise ignored.  0 = off. */
+  int shared_handoff;
 } dsca_ffn_args;
 DSCA_API int dsca_grouped_ffn(const dsca_ffn_args* a, dsca_stream_t stream);
 

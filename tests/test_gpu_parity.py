@@ -468,6 +468,39 @@ def test_hybrid_pair_tiles_full_size(cuda):
     assert int(r["counts"].max()) >= 512  # the hot expert has whole 256-token blocks
 
 
+@pytest.mark.parametrize("T", [300, 4096])
+def test_shared_handoff_changes_no_result(cuda, T):
+    """Qwen1.5-MoE-A2.7B block shapes: GEMM2's shared-expert tiles starting on GEMM1's handoff
+    flag (dsca_ffn_args.shared_handoff) instead of after all of GEMM1 give the same output bits
+    as without the handoff and as the static tile schedule, over repeated forwards (every call
+    leaves the ticket and handoff words zeroed)."""
+    from dsca_moe_b200 import _lib as L
+    from dsca_moe_b200.engine import MoEEngine, pack_swiglu
+
+    d, E, I, Is, k = 2048, 60, 1408, 5632, 4
+    x = syn.hidden_states(T, d, 821, "bf16")
+    Wg, _ = syn.router_weight(E, d, 822, zipf_s=1.5, dtype="bf16")
+    sgw = syn.bf16_round(syn.rng(824).standard_normal((1, d)).astype(np.float32) / np.sqrt(d))
+    w = _device_qwen_weights(E, d, I, Is, 823, cuda)
+    pe = pack_swiglu(w["gate"], w["up"], w["down"], shared=(w["s_gate"], w["s_up"], w["s_down"]),
+                     dtype=torch.bfloat16, device=cuda)
+    eng = MoEEngine(_t(Wg, torch.bfloat16, cuda), pe, top_k=k, route_mode=L.ROUTE_SOFTMAX_TOPK,
+                    shared_gate_weight=_t(sgw, torch.bfloat16, cuda))
+    xd = _t(x, torch.bfloat16, cuda)
+    outs = []
+    for handoff, dynamic in ((False, True), (True, True), (True, True), (True, True), (False, False)):
+        eng.shared_handoff, eng.dynamic_tiles = handoff, dynamic
+        r = eng.forward(xd)
+        torch.cuda.synchronize()
+        eng.check()
+        outs.append(r["out"].clone())
+    assert int(eng._tile_ctr.abs().sum()) == 0
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    ref = torch_ref.qwen_block_fp32(xd, r["topk_ids"], r["topk_w"], w, _t(sgw, torch.bfloat16, cuda))
+    assert torch_ref.max_rel_err(outs[0], ref) < BF16_TOL
+
+
 def test_host_pipeline_matches_forward(cuda):
     """HostPipeline (overlapped H2D / forward / D2H over pinned host batches) returns, for every
     batch, exactly what forward() returns for it."""
