@@ -100,7 +100,7 @@ def parse():
                     help="router logits: 1 = tensor cores (exact int8 fixed-point products, correctly "
                          "rounded bf16 logits), 0 = CUDA-core fp32 fma chains in the fixed chunk order "
                          "(default: the engine's, tensor cores where they apply)")
-    ap.add_argument("--qos-stream", choices=["side", "main"], default=None,
+    ap.add_argument("--qos-stream", choices=["parallel", "side", "main"], default=None,
                     help="expert parallel: where the QoS scores run (default: the engine's)")
     ap.add_argument("--no-qos-order", action="store_true",
                     help="expert parallel: skip the QoS planner (scores, priority sum) and run the routed "

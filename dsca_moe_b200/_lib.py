@@ -102,7 +102,7 @@ EXPORTED = ["dsca_version", "dsca_status_string", "dsca_device_info", "dsca_rout
             "dsca_dispatch_scan", "dsca_permute", "dsca_grouped_ffn", "dsca_combine",
             "dsca_plan_harmony", "dsca_plan_layout", "dsca_check_error", "dsca_exp_neg_eval",
             "dsca_grouped_ffn_static_scratch", "dsca_ep_ctx_bytes", "dsca_ep_init", "dsca_ep_group_offsets",
-            "dsca_ep_plan", "dsca_ep_group_order", "dsca_ep_dispatch", "dsca_ep_wait", "dsca_ep_plan_eval", "dsca_ipc_export",
+            "dsca_ep_plan", "dsca_ep_plan_counts", "dsca_ep_priority", "dsca_ep_group_order", "dsca_ep_dispatch", "dsca_ep_wait", "dsca_ep_plan_eval", "dsca_ipc_export",
             "dsca_ipc_import", "dsca_ipc_close", "dsca_ep_read_plan", "dsca_ep_region_alloc",
             "dsca_ep_region_free", "dsca_ep_return", "dsca_qos_priority", "dsca_router_pack_i8", "dsca_split_rows"]
 STATIC_SCRATCH_BYTES = 16 << 20
@@ -145,6 +145,8 @@ def load():
     lib.dsca_ep_group_order.restype = _vp
     lib.dsca_ep_group_order.argtypes = [_vp]
     lib.dsca_ep_plan.argtypes = [_vp, _vp, _vp, u64, _vp, _vp]
+    lib.dsca_ep_plan_counts.argtypes = [_vp, _vp, u64, _vp, _vp]
+    lib.dsca_ep_priority.argtypes = [_vp, _vp, u64, _vp, _vp]
     lib.dsca_ep_dispatch.argtypes = [p(EpDispatchArgs), _vp]
     lib.dsca_ep_wait.argtypes = [_vp, _i, u64, _vp, _vp]
     lib.dsca_ep_plan_eval.argtypes = [_vp, _i, _i, _vp, _i, _vp, _vp]

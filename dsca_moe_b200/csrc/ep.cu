@@ -187,44 +187,17 @@ __device__ void harmony_warp(const int32_t* meta, int G, int E, const int32_t* e
   __syncwarp();
 }
 
-// ------------------------------------------------------------------ plan kernel
-__global__ void __launch_bounds__(256) plan_kernel(Ctx* c, const int32_t* counts, const float* priority,
-                                                   uint64_t limit_ns, int32_t* err) {
-  __shared__ int32_t meta_s[kMaxG * kMaxE];
-  __shared__ int32_t S_s[kMaxG * kMaxE * kMaxG];
-  __shared__ long long amt_s[kMaxG];
-  __shared__ int32_t amt32_s[kMaxG];
-  __shared__ int32_t le_s[kMaxE * kMaxG];
-  __shared__ int32_t e2g_s[kMaxE];
-  const int G = c->G, E = c->E, me = c->me, tid = threadIdx.x;
-  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(&c->epoch) + 1u;
-  // 1. my counts (and QoS priorities) into every rank's meta[me][*]
-  for (int i = tid; i < G * E; i += blockDim.x) {
-    const int p = i / E, e = i % E;
-    c->meta[p][me * kMaxE + e] = counts[e];
-    if (priority != nullptr) c->meta[p][kMaxG * kMaxE + me * kMaxE + e] = __float_as_int(priority[e]);
-  }
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence_system();
-    for (int p = 0; p < G; ++p) st_release_sys(c->flags[p] + kCounts * kMaxG + me, epoch);
-  }
-  // 2. every rank's counts
-  if (tid < G) {
-    if (!wait_flag(c->flags[me] + kCounts * kMaxG + tid, epoch, limit_ns)) record_error(err, kErrWaitTimeout);
-  }
-  __syncthreads();
-  const volatile int32_t* ml = c->meta[me];
-  for (int i = tid; i < G * E; i += blockDim.x) meta_s[i] = ml[(i / E) * kMaxE + i % E];
-  for (int e = tid; e < E; e += blockDim.x) e2g_s[e] = c->expert_to_gpu[e];
-  // QoS: the priorities summed over the ranks in rank order (the all-reduce of
-  // src/qosmoe/moe_layer.py:379-380, identical on every rank), and the execution order of the
-  // experts by it: descending, lowest expert id on ties (the stable sort of build_exec_plan,
-  // src/qosmoe/planner.py:189-198, with every expert resident)
-  __shared__ float prio_s[kMaxE];
+// QoS execution order from the priority tables every rank pushed into meta[me] (summed over
+// the ranks in rank order: the all-reduce of src/qosmoe/moe_layer.py:379-380, identical on
+// every rank), descending, lowest expert id on ties (the stable sort of build_exec_plan,
+// src/qosmoe/planner.py:189-198, with every expert resident).  Threads < E; ends with a
+// __syncthreads.
+__device__ __forceinline__ void qos_order(Ctx* c, bool have_priority, float* prio_s) {
+  const int E = c->E, G = c->G, tid = threadIdx.x;
+  const volatile int32_t* ml = c->meta[c->me];
   if (tid < E) {
     float sum = 0.0f;
-    if (priority != nullptr)
+    if (have_priority)
       for (int src = 0; src < G; ++src) sum = __fadd_rn(sum, __int_as_float(ml[kMaxG * kMaxE + src * kMaxE + tid]));
     prio_s[tid] = (sum == sum) ? sum : -INFINITY;  // a NaN orders last: the order stays a permutation
   }
@@ -240,6 +213,74 @@ __global__ void __launch_bounds__(256) plan_kernel(Ctx* c, const int32_t* counts
     c->priority[tid] = pe;
   }
   __syncthreads();
+}
+
+// ------------------------------------------------------------------ priority kernel
+// dsca_ep_priority: this rank's [E] priorities into every rank's priority table, the kPrio flag,
+// a bounded wait for every rank's, then the execution order.  Its own epoch, so it may run beside
+// the counts-only plan of the same forward on another stream.
+__global__ void __launch_bounds__(256) priority_kernel(Ctx* c, const float* priority, uint64_t limit_ns,
+                                                       int32_t* err) {
+  __shared__ float prio_s[kMaxE];
+  const int G = c->G, E = c->E, me = c->me, tid = threadIdx.x;
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(&c->prio_epoch) + 1u;
+  for (int i = tid; i < G * E; i += blockDim.x) {
+    const int p = i / E, e = i % E;
+    c->meta[p][kMaxG * kMaxE + me * kMaxE + e] = __float_as_int(priority[e]);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence_system();
+    for (int p = 0; p < G; ++p) st_release_sys(c->flags[p] + kPrio * kMaxG + me, epoch);
+  }
+  if (tid < G) {
+    if (!wait_flag(c->flags[me] + kPrio * kMaxG + tid, epoch, limit_ns)) record_error(err, kErrWaitTimeout);
+  }
+  __syncthreads();
+  qos_order(c, true, prio_s);
+  if (tid == 0) {
+    __threadfence();
+    *reinterpret_cast<volatile uint32_t*>(&c->prio_epoch) = epoch;
+  }
+}
+
+// ------------------------------------------------------------------ plan kernel
+// kOrder = false (dsca_ep_plan_counts): counts only; the QoS order and the priority tables are
+// left to dsca_ep_priority.
+template <bool kOrder>
+__global__ void __launch_bounds__(256) plan_kernel(Ctx* c, const int32_t* counts, const float* priority,
+                                                   uint64_t limit_ns, int32_t* err) {
+  __shared__ int32_t meta_s[kMaxG * kMaxE];
+  __shared__ int32_t S_s[kMaxG * kMaxE * kMaxG];
+  __shared__ long long amt_s[kMaxG];
+  __shared__ int32_t amt32_s[kMaxG];
+  __shared__ int32_t le_s[kMaxE * kMaxG];
+  __shared__ int32_t e2g_s[kMaxE];
+  const int G = c->G, E = c->E, me = c->me, tid = threadIdx.x;
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(&c->epoch) + 1u;
+  // 1. my counts (and QoS priorities) into every rank's meta[me][*]
+  for (int i = tid; i < G * E; i += blockDim.x) {
+    const int p = i / E, e = i % E;
+    c->meta[p][me * kMaxE + e] = counts[e];
+    if (kOrder && priority != nullptr) c->meta[p][kMaxG * kMaxE + me * kMaxE + e] = __float_as_int(priority[e]);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence_system();
+    for (int p = 0; p < G; ++p) st_release_sys(c->flags[p] + kCounts * kMaxG + me, epoch);
+  }
+  // 2. every rank's counts
+  if (tid < G) {
+    if (!wait_flag(c->flags[me] + kCounts * kMaxG + tid, epoch, limit_ns)) record_error(err, kErrWaitTimeout);
+  }
+  __syncthreads();
+  const volatile int32_t* ml = c->meta[me];
+  for (int i = tid; i < G * E; i += blockDim.x) meta_s[i] = ml[(i / E) * kMaxE + i % E];
+  for (int e = tid; e < E; e += blockDim.x) e2g_s[e] = c->expert_to_gpu[e];
+  // QoS: the execution order of the experts by their summed priorities (identity without them)
+  __shared__ float prio_s[kMaxE];
+  if (kOrder) qos_order(c, priority != nullptr, prio_s);
+  else __syncthreads();
   // 3. the plan
   if (tid < 32) harmony_warp(meta_s, G, E, e2g_s, c->eq_tokens, S_s, amt_s, le_s, amt32_s);
   __syncthreads();
@@ -468,6 +509,7 @@ int dsca_ep_init(void* ctx_dev, const dsca_ep_setup* s, dsca_stream_t stream) {
   host.eq_tokens = s->eq_tokens;
   host.elem_bytes = s->elem_bytes;
   host.epoch = s->start_epoch;
+  host.prio_epoch = s->start_epoch;
   for (int e = 0; e < s->E; ++e) {
     if (s->expert_to_gpu[e] < 0 || s->expert_to_gpu[e] >= s->G) return DSCA_ERR_BAD_ARG;
     host.expert_to_gpu[e] = s->expert_to_gpu[e];
@@ -493,8 +535,22 @@ int32_t* dsca_ep_group_order(void* ctx_dev) {
 int dsca_ep_plan(void* ctx_dev, const int32_t* counts, const float* priority, uint64_t limit_ns, int32_t* err,
                  dsca_stream_t stream) {
   if (ctx_dev == nullptr || counts == nullptr) return DSCA_ERR_BAD_ARG;
-  dsca::ep::plan_kernel<<<1, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(static_cast<Ctx*>(ctx_dev), counts,
-                                                                            priority, limit_ns, err);
+  dsca::ep::plan_kernel<true><<<1, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<Ctx*>(ctx_dev), counts, priority, limit_ns, err);
+  return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
+}
+
+int dsca_ep_plan_counts(void* ctx_dev, const int32_t* counts, uint64_t limit_ns, int32_t* err, dsca_stream_t stream) {
+  if (ctx_dev == nullptr || counts == nullptr) return DSCA_ERR_BAD_ARG;
+  dsca::ep::plan_kernel<false><<<1, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<Ctx*>(ctx_dev), counts, nullptr, limit_ns, err);
+  return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
+}
+
+int dsca_ep_priority(void* ctx_dev, const float* priority, uint64_t limit_ns, int32_t* err, dsca_stream_t stream) {
+  if (ctx_dev == nullptr || priority == nullptr) return DSCA_ERR_BAD_ARG;
+  dsca::ep::priority_kernel<<<1, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(static_cast<Ctx*>(ctx_dev),
+                                                                                priority, limit_ns, err);
   return cudaGetLastError() == cudaSuccess ? DSCA_OK : DSCA_ERR_CUDA;
 }
 

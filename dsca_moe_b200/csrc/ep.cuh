@@ -2,8 +2,8 @@
 // grouped GEMM's return epilogue (gemm_sm100.cu).
 //
 // Every rank owns one symmetric region (same layout on every rank, mapped into every peer
-// through CUDA IPC): flags [3][kMaxG] u32 (counts / dispatch / return, written by the source
-// rank with release semantics, value = the forward's epoch), meta [kMaxG][kMaxE] i32 (each
+// through CUDA IPC): flags [4][kMaxG] u32 (counts / dispatch / return / priorities, written by
+// the source rank with release semantics, value = the forward's epoch), meta [kMaxG][kMaxE] i32 (each
 // source's per-expert counts), the receive buffer (rows dispatched to this rank, expert-major)
 // and the return buffer (this rank's expert outputs coming back, in its send layout).
 #pragma once
@@ -16,7 +16,7 @@ namespace ep {
 constexpr int kMaxG = DSCA_MAX_GPUS;      // 8
 constexpr int kCtasPerSm = 2;             // resident CTAs per SM of the dispatch / return copy kernels
 constexpr int kMaxE = DSCA_MAX_EXPERTS;   // 64
-enum FlagKind { kCounts = 0, kDispatch = 1, kReturn = 2 };
+enum FlagKind { kCounts = 0, kDispatch = 1, kReturn = 2, kPrio = 3 };
 
 struct Ctx {
   int G, E, me, d;
@@ -44,6 +44,7 @@ struct Ctx {
   // ties); position -> expert.  The identity when the forward carries no priorities.
   int32_t group_order[kMaxE];
   float priority[kMaxE];                   // the summed priorities of the last forward
+  uint32_t prio_epoch;  // epoch of the last priority exchange (dsca_ep_priority advances it)
 };
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {

@@ -399,7 +399,10 @@ class MoEEngine:
         # world > 1 path always runs them, src/qosmoe/moe_layer.py:306-316,379-380,422-427)
         self.qos_order = True
         # where the QoS scores run at world > 1: "side" = on the side stream ahead of the plan,
-        # beside the shared-expert GEMM1; "main" = on the main stream before it
+        # which carries the priorities (the default); "parallel" = on a stream of their own, with
+        # the priority exchange (dsca_ep_priority), beside the counts-only plan and the dispatch on
+        # the side stream (the routed GEMM1 waits for both); "main" = on the main stream before
+        # the shared GEMM1
         self.qos_stream = "side"
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._done_counter = torch.zeros(1, dtype=torch.int32, device=self.device)
@@ -839,6 +842,7 @@ class MoEEngine:
                           device=dev),
             y=torch.empty(recv_cap, d, dtype=dt, device=dev),
             side=torch.cuda.Stream(device=dev),
+            qos_side=torch.cuda.Stream(device=dev),
             group_offsets=int(lib.dsca_ep_group_offsets(_ptr(ctx)) or 0),
             group_order=int(lib.dsca_ep_group_order(_ptr(ctx)) or 0),
             bytes=total, split_fp8=self._split, **split)
@@ -862,6 +866,8 @@ class MoEEngine:
         # the plan (counts exchange + harmony) and the dispatch run on the side stream, beside the
         # shared-expert GEMM1, which needs neither
         prio = None
+        parallel = self.qos_order and self.qos_stream == "parallel" and self.cache is None
+        prio_done = None
         if self.qos_order and self.qos_stream == "main":
             # the QoS scores alone on the GPU, before the shared-expert GEMM1 fills it (beside it
             # they share its SMs and lengthen the side stream's chain to the dispatch)
@@ -871,15 +877,34 @@ class MoEEngine:
         routed = torch.cuda.Event()
         routed.record(main)
         side.wait_event(routed)
+        if parallel:
+            # the QoS scores and the priority exchange on their own stream: the plan and the
+            # dispatch need only the counts
+            qs = ep["qos_side"]
+            qs.wait_event(routed)
+            with torch.cuda.stream(qs):
+                t0 = self._side_mark()
+                self._qos(x, ws, qos)
+                self._side_mark("qos", t0)
+                t0 = self._side_mark()
+                L.check(lib.dsca_ep_priority(ctx, _ptr(ws["expert_priority"]), self.wait_limit_ns, err, _stream()),
+                        "dsca_ep_priority")
+                self._side_mark("priority", t0)
+                prio_done = torch.cuda.Event()
+                prio_done.record(qs)
         with torch.cuda.stream(side):
-            if self.qos_order and self.qos_stream != "main":
+            if self.qos_order and not parallel and self.qos_stream != "main":
                 t0 = self._side_mark()
                 self._qos(x, ws, qos)
                 prio = ws["expert_priority"]
                 self._side_mark("qos", t0)
             t0 = self._side_mark()
-            L.check(lib.dsca_ep_plan(ctx, _ptr(ws["counts"]), _ptr(prio), self.wait_limit_ns, err, _stream()),
-                    "dsca_ep_plan")
+            if parallel:
+                L.check(lib.dsca_ep_plan_counts(ctx, _ptr(ws["counts"]), self.wait_limit_ns, err, _stream()),
+                        "dsca_ep_plan_counts")
+            else:
+                L.check(lib.dsca_ep_plan(ctx, _ptr(ws["counts"]), _ptr(prio), self.wait_limit_ns, err, _stream()),
+                        "dsca_ep_plan")
             self._side_mark("plan", t0)
             t0 = self._side_mark()
             a = L.EpDispatchArgs()
@@ -920,6 +945,8 @@ class MoEEngine:
         if self.cache is not None:
             return self._forward_p2p_cached(x, ws, ep, args, has_shared, side_ctas)
         order = ep["group_order"] if self.qos_order else None
+        if prio_done is not None:
+            main.wait_event(prio_done)
         self._ffn_call(*args, 1, segments=1, group_order=order, **kw)
         self._mark("gemm1_routed")
         if fused:

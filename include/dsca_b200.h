@@ -445,9 +445,10 @@ DSCA_API int dsca_ep_init(void* ctx_dev, const dsca_ep_setup* s, dsca_stream_t s
 /* Device pointer of the plan's receive-side group offsets [E + 1] inside ctx_dev. */
 DSCA_API int32_t* dsca_ep_group_offsets(void* ctx_dev);
 /* Device pointer of the QoS execution order [E] inside ctx_dev (position -> expert), written by
- * dsca_ep_plan: experts by their priority summed over the ranks, descending, lowest id on ties
- * (the priority all-reduce and build_exec_plan order of src/qosmoe/moe_layer.py:379-380,422-427);
- * the identity when dsca_ep_plan got no priorities.  Pass it as dsca_ffn_args.group_order. */
+ * dsca_ep_plan or dsca_ep_priority: experts by their priority summed over the ranks, descending,
+ * lowest id on ties (the priority all-reduce and build_exec_plan order of
+ * src/qosmoe/moe_layer.py:379-380,422-427); the identity after a dsca_ep_plan without
+ * priorities.  Pass it as dsca_ffn_args.group_order. */
 DSCA_API int32_t* dsca_ep_group_order(void* ctx_dev);
 /* Copy the last plan S [DSCA_MAX_GPUS][DSCA_MAX_EXPERTS][DSCA_MAX_GPUS] and the rows this rank
  * received to the host (synchronises `stream`; for statistics, not the hot path). */
@@ -455,6 +456,17 @@ DSCA_API int dsca_ep_read_plan(void* ctx_dev, int32_t* S_host, int32_t* recv_tot
 /* priority: this rank's expert priorities [E] (dsca_qos_priority), or NULL (identity order) */
 DSCA_API int dsca_ep_plan(void* ctx_dev, const int32_t* counts, const float* priority, uint64_t limit_ns,
                           int32_t* err, dsca_stream_t stream);
+/* dsca_ep_plan split in two for a forward whose dispatch should not wait for the QoS scores
+ * (the harmony plan and the layouts need only the counts; the priorities only order the routed
+ * tiles): dsca_ep_plan_counts is dsca_ep_plan without the execution order (left as it is), and
+ * dsca_ep_priority exchanges this rank's priorities [E] with every peer (bounded wait), sums them
+ * in rank order and writes the execution order (dsca_ep_group_order).  Once each per forward on
+ * every rank, in any order or concurrently on different streams; the GEMM that reads the order
+ * must come after dsca_ep_priority.  Same reference lines as dsca_ep_plan. */
+DSCA_API int dsca_ep_plan_counts(void* ctx_dev, const int32_t* counts, uint64_t limit_ns, int32_t* err,
+                                 dsca_stream_t stream);
+DSCA_API int dsca_ep_priority(void* ctx_dev, const float* priority, uint64_t limit_ns, int32_t* err,
+                              dsca_stream_t stream);
 typedef struct {
   const void* x;
   int T, d, top_k, dtype;

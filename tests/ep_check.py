@@ -111,12 +111,16 @@ def main():
     cases.append(("qwen contiguous, harmony, p2p, expert cache 8 slots", case_qwen_cache, None, 150, "p2p"))
     cases.append(("qwen contiguous, harmony, p2p, fp8-e4m3 weights", case_qwen_fp8, None, 150, "p2p"))
     cases.append(("qwen contiguous, harmony, p2p, QoS scores on the main stream", case_qwen, None, 150, "p2p-qosmain"))
+    cases.append(("qwen contiguous, harmony, p2p, QoS scores and priority exchange on their own stream", case_qwen,
+                  None, 150, "p2p-qospar"))
     ok = True
     for name, fn, e2g, eq, exchange in cases:
         ep, one, x = fn(rank, world, dev, group, e2g, eq, "nccl" if exchange == "nccl" else "p2p")
         ep.ep_return = "fused" if exchange == "p2p-fused" else "overlap"
         if exchange == "p2p-qosmain":
             ep.qos_stream = "main"
+        if exchange == "p2p-qospar":
+            ep.qos_stream = "parallel"
         graph = None
         if exchange == "p2p-graph":
             # the forward captured once (collective), replayed on new contents of its input buffer
@@ -136,7 +140,7 @@ def main():
             ep.check()
             one.check()
             same_route = torch.equal(r_ep["topk_ids"], r_one["topk_ids"]) and torch.equal(r_ep["logits"], r_one["logits"])
-            if exchange in ("p2p", "p2p-qosmain") and ep.qos_order:
+            if exchange in ("p2p", "p2p-qosmain", "p2p-qospar") and ep.qos_order:
                 # the QoS order is the summed priorities' order, the same on every rank
                 order, prio = ep.read_qos_order()
                 mine = torch.from_numpy(prio.copy()).to(dev)
