@@ -28,6 +28,10 @@
 
 #include "gemm_sm100.cuh"
 
+#ifndef DSCA_GEMM2_WIDE_STAGES
+#define DSCA_GEMM2_WIDE_STAGES 1
+#endif
+
 namespace dsca {
 namespace gemm {
 namespace pair {
@@ -53,20 +57,26 @@ namespace pair {
 // values of 32 channels; per chunk of 32 tokens each sends the other the values of the 16
 // tokens the other forms SiLU(g) * u for (16 x 32 fp32 each way, two buffers per warp pair,
 // mbarrier-paced), so both warps compute and store at once.
+//
+// kWide (bf16 store epilogue, GEMM2): a stage holds two 64-wide K blocks of each operand (two
+// TMA boxes each, 64 KB per CTA, 3 stages), eight MMAs per full-barrier wait and commit.
 template <int EPI, bool F8 = false>
 struct Cfg {
   static constexpr bool kGlu = EPI == kEpiSwiGLU;
   static constexpr bool kG2 = EPI == kEpiSwiGLU2;
+  static constexpr bool kWide = EPI == kEpiStore && !F8 && DSCA_GEMM2_WIDE_STAGES;
+  static constexpr int kSub = kWide ? 2 : 1;              // 128-byte K boxes per operand and stage
   static constexpr int TBN = (kGlu && !F8) ? 128 : 256;  // token rows per tile (MMA N)
   static constexpr int kAccBufs = (kGlu && F8) ? 1 : 2;  // accumulator buffers (256 columns each)
   static constexpr int kUpCol = kGlu ? TBN : 0;          // SwiGLU: the up accumulator's column
-  static constexpr int S = F8 ? (kGlu ? 3 : 4) : (kGlu ? 5 : 6);  // stages
+  static constexpr int S = F8 ? (kGlu ? 3 : 4) : (kGlu ? 5 : (kWide ? 3 : 6));  // stages
   static constexpr int kWBox = kG2 ? 64 : 128;            // weight rows per TMA box
-  static constexpr int kTBox = TBN / 2;                   // token rows per TMA box (one per stage)
-  static constexpr int kKE = F8 ? 128 : BK;               // K elements per stage (128 bytes a row)
-  static constexpr int kABytes = 128 * 128;               // 16 KB
+  static constexpr int kTBox = TBN / 2;                   // token rows per TMA box
+  static constexpr int kKE = F8 ? 128 : BK;               // K elements per box (128 bytes a row)
+  static constexpr int kKS = kKE * kSub;                  // K elements per stage
+  static constexpr int kABytes = 128 * 128 * kSub;        // 16 KB per box
   static constexpr int kA2Bytes = kGlu ? 128 * 128 : 0;
-  static constexpr int kTPlane = (TBN / 2) * 128;         // this CTA's token rows, one plane
+  static constexpr int kTPlane = (TBN / 2) * 128 * kSub;  // this CTA's token rows, one plane
   static constexpr int kTBytes = (F8 ? 2 : 1) * kTPlane;
   static constexpr int kStageBytes = kABytes + kA2Bytes + kTBytes;
   static constexpr int kStageElems = 32 * 32;             // epilogue staging per warp, bf16
@@ -251,9 +261,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         // then one K block l2_ahead ahead of every load
         const int pf = (ti.seg == 0 && !full) ? p.l2_ahead : 0;
         auto prefetch_kb = [&](int k) {
-          tma_prefetch_l2_2d(mw, k * C::kKE, w_row);
-          if constexpr (C::kGlu || C::kG2) tma_prefetch_l2_2d(mw, k * C::kKE, w_row + 128);
-          tma_prefetch_l2_2d(mt, k * C::kKE, t_row);
+          for (int h = 0; h < C::kSub; ++h) {
+            const int kx = k * C::kKS + h * C::kKE;
+            tma_prefetch_l2_2d(mw, kx, w_row);
+            if constexpr (C::kGlu || C::kG2) tma_prefetch_l2_2d(mw, kx, w_row + 128);
+            tma_prefetch_l2_2d(mt, kx, t_row);
+          }
         };
         for (int kb = S; kb < min(pf, kb_n); ++kb) prefetch_kb(kb);
         for (int kb = 0; kb < kb_n; ++kb) {
@@ -273,6 +286,22 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_load_2d_pair(smem_a + s * C::kABytes, mt, fb0, kb * C::kKE, f_trow);
               tma_load_2d_pair(smem_a + s * C::kABytes + C::kABytes / 2, mt, fb0, kb * C::kKE, f_trow + 64);
               tma_load_2d_pair(smem_a2 + s * C::kA2Bytes, mw, fb0, kb * C::kKE, f_wrow);
+            }
+          } else if constexpr (C::kWide) {
+            if (rank == 0) mbar_arrive_expect_tx(fb, tx);
+            // two 64-wide K boxes of weights and tokens; a box past K reads zeros
+#pragma unroll
+            for (int h = 0; h < C::kSub; ++h) {
+              const int kx = kb * C::kKS + h * C::kKE;
+              const uint32_t wdst = smem_a + s * C::kABytes + h * (C::kABytes / C::kSub);
+              const uint32_t tdst = smem_t + s * C::kTBytes + h * (C::kTPlane / C::kSub);
+              if (p.l2_hints) {
+                tma_load_2d_pair_hint(wdst, mw, fb0, kx, w_row, wpol);
+                tma_load_2d_pair_hint(tdst, mt, fb0, kx, t_row, pol_last);
+              } else {
+                tma_load_2d_pair(wdst, mw, fb0, kx, w_row);
+                tma_load_2d_pair(tdst, mt, fb0, kx, t_row);
+              }
             }
           } else {
             if (rank == 0) mbar_arrive_expect_tx(fb, tx);
@@ -363,6 +392,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 umma_f8_pair(d_tmem + C::kUpCol, udesc + ko, tdesc + ko, idesc, accum);
                 umma_f8_pair(d_tmem + C::kUpCol, udesc + ko, ldesc + ko, idesc, 1u);
               }
+            }
+          } else if constexpr (C::kWide) {
+#pragma unroll
+            for (int h = 0; h < C::kSub; ++h) {
+              const uint64_t ah = sw128_kmajor_desc(smem_a + s * C::kABytes + h * (C::kABytes / C::kSub));
+              const uint64_t th = sw128_kmajor_desc(smem_t + s * C::kTBytes + h * (C::kTPlane / C::kSub));
+#pragma unroll
+              for (int k = 0; k < BK / 16; ++k)
+                umma_f16_pair(d_tmem, ah + (uint64_t)(2 * k), th + (uint64_t)(2 * k), idesc,
+                              (kb > 0 || h > 0 || k > 0) ? 1u : 0u);
             }
           } else {
 #pragma unroll
@@ -794,7 +833,8 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
     s0.rows = 0;
     s0.n_tiles = f->dp / gemm::BN;
     s0.b_rows_per_group = f->dp;
-    s0.k_blocks = (f->ip + gemm::BK - 1) / gemm::BK;
+    constexpr int kks = gemm::pair::Cfg<gemm::kEpiStore>::kKS;  // K elements per stage
+    s0.k_blocks = (f->ip + kks - 1) / kks;
     s0.c = reinterpret_cast<__nv_bfloat16*>(f->y);
     s0.ldc = f->d;
     s0.n_store = f->d;
@@ -807,7 +847,7 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
       s1.rows = f->shared_rows;
       s1.n_tiles = f->dp / gemm::BN;
       s1.b_rows_per_group = f->dp;
-      s1.k_blocks = (f->shared_ip + gemm::BK - 1) / gemm::BK;
+      s1.k_blocks = (f->shared_ip + kks - 1) / kks;
       s1.c = reinterpret_cast<__nv_bfloat16*>(f->ys);
       s1.ldc = f->d;
       s1.n_store = f->d;
