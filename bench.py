@@ -1281,7 +1281,9 @@ def run_ours(args, w, T):
             "implementation": {
                 "launch": graph_note or "eager (one host call per kernel)",
                 "exchange": (f"{args.exchange} (return {args.ep_return})" if world > 1 else "none"),
-                "gemm_tiles": {0: "GEMM1 128-token single-CTA tiles, GEMM2 CTA-pair swap-AB tiles",
+                "gemm_tiles": {0: "CTA-pair swap-AB tiles for GEMM2; SwiGLU GEMM1 on CTA pairs (128 channels x <=256 "
+                                  "tokens, gate and up halves per CTA) from 4096 tokens in one launch, else "
+                                  "128-token single-CTA tiles",
                                128: "128-token single-CTA tiles",
                                256: "CTA-pair swap-AB tiles (SwiGLU GEMM1: 128 channels, gate and up halves per CTA, "
                                     "x <=256 tokens; otherwise 256 weight rows x <=256 tokens)",

@@ -434,8 +434,10 @@ int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t st
   const int phases_all = f->phases == 0 ? 3 : f->phases;
   if (f->tile_rows == 256 || f->tile_rows == 512) return launch_grouped_ffn_bf16_pair(f, num_sms, stream);
   if (f->tile_rows == 0) {
-    // default: the CTA-pair swap-AB kernel for GEMM2 (and a ReLU GEMM1); single-CTA tiles for
-    // the SwiGLU GEMM1, whose gate and up halves then sit in the same accumulator row
+    // default: the CTA-pair swap-AB kernel for GEMM2 and a ReLU GEMM1.  A SwiGLU GEMM1 with both
+    // segments in this call and 4096 or more tokens takes the pair kernel too (the gate and up
+    // rows of a CTA's 64 channels as one operand: measured faster there), otherwise single-CTA
+    // 128-token tiles (more tiles for fewer tokens: faster at 1024 tokens)
     const bool glu = f->act == DSCA_ACT_SWIGLU;
     dsca_ffn_args g = *f;
     int rc;
@@ -445,9 +447,11 @@ int launch_grouped_ffn_bf16(const dsca_ffn_args* f, int num_sms, cudaStream_t st
     const bool handoff = f->shared_handoff == 1 && glu && phases_all == 3 && f->tile_counters != nullptr &&
                          f->pdl_after_permute && f->ep_ctx == nullptr && f->shared_rows > 0 && segs == 3;
     g.shared_handoff = handoff ? 2 : 0;
+    const int rows1 = f->shared_rows > 0 ? f->shared_rows : f->capacity;
+    const bool pair1 = glu && segs == 3 && rows1 >= 4096;
     if (phases_all & 1) {
       g.phases = 1;
-      g.tile_rows = glu ? 128 : 256;
+      g.tile_rows = (pair1 || !glu) ? 256 : 128;
       if ((rc = launch_grouped_ffn_bf16(&g, num_sms, stream))) return rc;
     }
     if (phases_all & 2) {

@@ -64,12 +64,14 @@ template <int EPI, bool F8 = false>
 struct Cfg {
   static constexpr bool kGlu = EPI == kEpiSwiGLU;
   static constexpr bool kG2 = EPI == kEpiSwiGLU2;
-  static constexpr bool kWide = EPI == kEpiStore && !F8 && DSCA_GEMM2_WIDE_STAGES;
+  static constexpr bool kWide = (EPI == kEpiStore || EPI == kEpiSwiGLU2) && !F8 && DSCA_GEMM2_WIDE_STAGES;
   static constexpr int kSub = kWide ? 2 : 1;              // 128-byte K boxes per operand and stage
   static constexpr int TBN = (kGlu && !F8) ? 128 : 256;  // token rows per tile (MMA N)
   static constexpr int kAccBufs = (kGlu && F8) ? 1 : 2;  // accumulator buffers (256 columns each)
   static constexpr int kUpCol = kGlu ? TBN : 0;          // SwiGLU: the up accumulator's column
   static constexpr int S = F8 ? (kGlu ? 3 : 4) : (kGlu ? 5 : (kWide ? 3 : 6));  // stages
+  static_assert(!kWide || S * (128 * 128 * 2 * 2) + 4 * 32 * 32 * 2 + (kG2 ? 16384 : 0) + 1024 <= 227 * 1024,
+                "two-box stages exceed the shared memory of a CTA");
   static constexpr int kWBox = kG2 ? 64 : 128;            // weight rows per TMA box
   static constexpr int kTBox = TBN / 2;                   // token rows per TMA box
   static constexpr int kKE = F8 ? 128 : BK;               // K elements per box (128 bytes a row)
@@ -295,11 +297,15 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int kx = kb * C::kKS + h * C::kKE;
               const uint32_t wdst = smem_a + s * C::kABytes + h * (C::kABytes / C::kSub);
               const uint32_t tdst = smem_t + s * C::kTBytes + h * (C::kTPlane / C::kSub);
+              // kEpiSwiGLU2: the gate rows, then the up rows 128 further, as the box's rows 64-127
+              constexpr uint32_t up_off = C::kABytes / C::kSub / 2;
               if (p.l2_hints) {
                 tma_load_2d_pair_hint(wdst, mw, fb0, kx, w_row, wpol);
+                if constexpr (C::kG2) tma_load_2d_pair_hint(wdst + up_off, mw, fb0, kx, w_row + 128, wpol);
                 tma_load_2d_pair_hint(tdst, mt, fb0, kx, t_row, pol_last);
               } else {
                 tma_load_2d_pair(wdst, mw, fb0, kx, w_row);
+                if constexpr (C::kG2) tma_load_2d_pair(wdst + up_off, mw, fb0, kx, w_row + 128);
                 tma_load_2d_pair(tdst, mt, fb0, kx, t_row);
               }
             }
@@ -511,6 +517,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_remote(empty_bar[acc]);
+        // shared-expert handoff: the 8 epilogue warps of the pair count each stored tile
+        if (p.seg1_done != nullptr && ti.seg == 1) seg1_tile_stored(p, ctl, lane, 8u);
         continue;
       }
       if (!F8 && C::kGlu && ti.full) {
@@ -748,6 +756,7 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
     const int epi = g2 ? gemm::kEpiSwiGLU2 : glu ? gemm::kEpiSwiGLU : gemm::kEpiReLU;
     p.epi = epi;
     p.tile_counter = f->tile_counters;  // GEMM1: [0, 2)
+    p.seg1_done = (f->shared_handoff == 2 && shared && g2) ? f->tile_counters + 4 : nullptr;  // [4, 6)
     p.err = f->err;
     p.nseg = shared ? 2 : 1;
     // tile_rows 512 (SwiGLU): whole 256-token blocks as non-swapped tiles, the rest swap-AB
@@ -772,7 +781,8 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
     s0.n_tiles = (glu && !g2) ? (f->ip + gemm::BN - 1) / gemm::BN : f->n1p / gemm::BN;
     s0.n_full = glu ? f->ip / 128 : 0;
     s0.b_rows_per_group = f->n1p;
-    s0.k_blocks = (f->d + gemm::BK - 1) / gemm::BK;
+    const int kks1 = g2 ? gemm::pair::Cfg<gemm::kEpiSwiGLU2>::kKS : gemm::BK;  // K elements per stage
+    s0.k_blocks = (f->d + kks1 - 1) / kks1;
     s0.c = reinterpret_cast<__nv_bfloat16*>(f->h);
     s0.ldc = f->ip;
     s0.n_store = f->ip;
@@ -786,7 +796,7 @@ int launch_grouped_ffn_bf16_pair(const dsca_ffn_args* f, int num_sms, cudaStream
       s1.n_tiles = (glu && !g2) ? (f->shared_ip + gemm::BN - 1) / gemm::BN : f->shared_n1p / gemm::BN;
       s1.n_full = glu ? f->shared_ip / 128 : 0;
       s1.b_rows_per_group = f->shared_n1p;
-      s1.k_blocks = (f->d + gemm::BK - 1) / gemm::BK;
+      s1.k_blocks = (f->d + kks1 - 1) / kks1;
       s1.c = reinterpret_cast<__nv_bfloat16*>(f->hs);
       s1.ldc = f->shared_ip;
       s1.n_store = f->shared_ip;
